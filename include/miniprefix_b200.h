@@ -1,0 +1,151 @@
+/*
+ * miniprefix_b200.h -- C ABI of the B200 (sm_100a) MiniPrefix forward over paged KV.
+ *
+ * This is the drop-in boundary for the device half of TinyInfer MiniPrefix's
+ * CudaRunner (TinyInfer v0.3.0, miniprefix/src/backend/cuda/llama_runner.cu). The
+ * reference's host bookkeeping (KVManager, ExactPrefixCache, Engine) keeps owning
+ * metadata; it calls these functions where CudaRunner called cudaMalloc, cuBLAS,
+ * its seven kernels and cudaMemcpy*. Plain C types only; every pointer is
+ * caller-owned unless stated. One context per GPU, single-threaded per context
+ * (the reference's ModelRunner contract, miniprefix/include/miniprefix/kv_manager.h:18-19).
+ *
+ * Return codes: MP_OK or one of MP_ERR_*; mp_last_error() gives the message of
+ * the last failure on the calling thread.
+ */
+#ifndef MINIPREFIX_B200_H
+#define MINIPREFIX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MP_OK 0
+#define MP_ERR_INVALID 1     /* rejected argument; no state changed */
+#define MP_ERR_CUDA 2        /* CUDA runtime failure */
+#define MP_ERR_NONFINITE 3   /* a logit of the step was NaN/Inf */
+#define MP_ERR_BOUNDS 4      /* device bounds check tripped (page id, token, region) */
+#define MP_ERR_TIMEOUT 5     /* bounded wait expired (host sync or in-kernel copy wait) */
+#define MP_ERR_NOMEM 6       /* device allocation failed */
+#define MP_ERR_UNSUPPORTED 7 /* model geometry outside the specialised kernels */
+
+typedef struct mp_context mp_context;
+
+/* Mirrors miniprefix::ModelConfig (miniprefix/include/miniprefix/model.h:9-16). */
+typedef struct {
+    int32_t layers, hidden, intermediate, heads, kv_heads, vocabulary, context, eos;
+    float rms_epsilon, rope_theta;
+    int32_t tied;
+} mp_model_config;
+
+/* Paged KV pool and step capacities. block_tokens / max_blocks are
+ * KvCacheConfig's (miniprefix/include/miniprefix/paged_kv.h:13-17); each of the K
+ * and V pools holds max_blocks * layers * block_tokens * kv_width floats in the
+ * reference layout [block][layer][slot][kv_width] (paged_kv.h:25-27). */
+typedef struct {
+    int32_t block_tokens;
+    int32_t max_blocks;
+    int32_t max_sequences;      /* device block-table slots */
+    int32_t table_stride;       /* entries per slot: >= ceil(context / block_tokens) */
+    int32_t max_step_tokens;    /* most tokens one forward may carry (sum over sequences) */
+    int32_t max_step_sequences; /* most sequences one forward may carry */
+} mp_runtime_config;
+
+/* One sequence of a forward: `count` new tokens appended at positions
+ * start .. start+count-1 of the sequence whose block table lives in `slot`. The
+ * table must already map every page that covers start+count tokens. */
+typedef struct {
+    int32_t slot, start, count;
+} mp_sequence_desc;
+
+/* KVManager::TailCopyRegion (miniprefix/include/miniprefix/kv_manager.h:38): float
+ * element offsets into ONE pool; the copy is applied to both the K and V pools. */
+typedef struct {
+    uint64_t destination, source, pitch, width, rows;
+} mp_tail_copy_region;
+
+const char* mp_last_error(void);
+
+/* Replaces CudaRunner's constructor (llama_runner.cu:78-87): selects `device`,
+ * creates the stream, allocates weights, both pools (zeroed), tables and the
+ * step workspace. */
+int mp_create(int device, const mp_model_config* model, const mp_runtime_config* runtime, mp_context** out);
+void mp_destroy(mp_context* ctx);
+
+/* Replaces upload_parameter (llama_runner.cu:72-76): one MPFX0001 tensor by name,
+ * [in, out] orientation as stored by the reference (miniprefix/src/model/model.cpp:28-38).
+ * The tied head is read from the embedding; no transposed copy is made (:84). */
+int mp_set_weight(mp_context* ctx, const char* name, const float* host, size_t elements);
+/* Checks every tensor arrived and packs the device copies. Required before forward. */
+int mp_finalize_weights(mp_context* ctx);
+
+/* Replaces the incremental block-table upload (llama_runner.cu:139-143, :113):
+ * entries [first, first+count) of `slot` := blocks. Queued on the context stream. */
+int mp_table_write(mp_context* ctx, int32_t slot, int32_t first, const int32_t* blocks, int32_t count);
+
+/* Replaces the COW cudaMemcpy2DAsync pair (llama_runner.cu:130-137), batched:
+ * every region copies rows x width floats at pitch in both pools. */
+int mp_cow_copy(mp_context* ctx, const mp_tail_copy_region* regions, int32_t count);
+
+/* Replaces the append body (llama_runner.cu:144-170) for a BATCH of sequences:
+ * uploads tokens and descriptors, runs the 30-layer forward, and downloads per
+ * sequence the greedy token (first index of the maximum, engine.cpp:99), a
+ * finiteness flag (:94-95) and, when out_logits is not NULL, the full last-row
+ * logits (sequences x vocabulary floats, the reference's append() result).
+ * Blocks until the step completed or timeout_ms elapsed (MP_ERR_TIMEOUT).
+ * Returns MP_ERR_NONFINITE when any sequence had a nonfinite logit (outputs are
+ * still written) and MP_ERR_BOUNDS when a device bounds check tripped. */
+int mp_forward(mp_context* ctx, const mp_sequence_desc* sequences, int32_t count, const int32_t* tokens,
+               int32_t* out_tokens, int32_t* out_finite, float* out_logits, int32_t timeout_ms);
+
+/* The same step split in three, for callers that keep inputs resident and time
+ * the device work alone: prepare uploads, launch only enqueues kernels that read
+ * device memory, collect downloads and waits. */
+int mp_forward_prepare(mp_context* ctx, const mp_sequence_desc* sequences, int32_t count, const int32_t* tokens);
+int mp_forward_launch(mp_context* ctx);
+int mp_forward_collect(mp_context* ctx, int32_t* out_tokens, int32_t* out_finite, float* out_logits,
+                       int32_t timeout_ms);
+
+/* Waits for all queued work with a bounded host wait (event polling). */
+int mp_sync(mp_context* ctx, int32_t timeout_ms);
+
+/* Device pointers of the K and V pools and their element count (tests, tools). */
+int mp_kv_pools(mp_context* ctx, float** keys, float** values, uint64_t* elements);
+/* Synchronous host copies of pool payload (0 = K pool, 1 = V pool), element
+ * offsets; for tests and tools that inspect or seed pages. */
+int mp_kv_read(mp_context* ctx, int32_t pool, uint64_t offset, uint64_t count, float* host);
+int mp_kv_write(mp_context* ctx, int32_t pool, uint64_t offset, uint64_t count, const float* host);
+/* The context stream as a cudaStream_t (void* here to keep the ABI CUDA-free). */
+void* mp_stream(mp_context* ctx);
+
+/* Device event timing on the context stream: mp_timer_mark records a mark;
+ * mp_timer_elapsed gives milliseconds between the last two marks. */
+int mp_timer_mark(mp_context* ctx);
+int mp_timer_elapsed(mp_context* ctx, float* milliseconds);
+/* When enabled, forward launches bracket every attention launch with events;
+ * mp_profile_read returns the summed attention milliseconds and launch count
+ * since the last read (and resets them). */
+int mp_profile_enable(mp_context* ctx, int32_t enabled);
+int mp_profile_read(mp_context* ctx, float* attention_ms, int32_t* attention_launches, double* attention_bytes);
+
+/* The paged-attention decode OPERATOR alone (one query row per sequence), on
+ * caller device buffers: q [count][9*64] roped queries, pools in the reference
+ * layout with `layers` layers, tables [count][table_stride] (device), out
+ * [count][9*64]. `lengths` is a HOST array (tokens to attend per sequence);
+ * pages_per_split 0 picks a split for the 148 SMs. Runs on `stream`
+ * (cudaStream_t, NULL = legacy default) and does not synchronise. Uses an
+ * internal scratch buffer that grows on demand. */
+int mp_paged_attention_decode(const float* q, const float* keys, const float* values, int32_t layers, int32_t layer,
+                              int32_t block_tokens, int32_t max_blocks, const int32_t* tables, int32_t table_stride,
+                              const int32_t* lengths, int32_t count, float* out, int32_t pages_per_split, void* stream);
+/* Synchronises `stream`, then reads and clears the operator's device error word on
+ * the current device: MP_OK, MP_ERR_BOUNDS (a page id outside [0, max_blocks)) or
+ * MP_ERR_TIMEOUT (an in-kernel copy wait expired). */
+int mp_paged_attention_status(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,88 @@
+"""Build the in-tree shared libraries for sm_100a.
+
+  libmpb200.so       -- the device layer: CUDA kernels + the C ABI of
+                        include/miniprefix_b200.h
+  libmpb200_host.so  -- the C++ host layer (page pool, prefix cache, KV manager,
+                        scheduler, engine, runner) + the C ABI of
+                        include/miniprefix_b200_host.h; links libmpb200.so
+
+nvcc cross-compiles without a GPU. Outputs stay next to this file so they travel
+with the repository snapshot; nothing is installed.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+INCLUDE = os.path.join(ROOT, "include")
+DEVICE_LIB = os.path.join(HERE, "libmpb200.so")
+HOST_LIB = os.path.join(HERE, "libmpb200_host.so")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", f"-I{CSRC}"]
+
+DEVICE_SOURCES = ["attention.cu", "gemm_simt.cu", "fused_ops.cu", "context.cu", "operator.cu"]
+HOST_SOURCES = []  # filled in by host/ when present
+
+
+def _stale(target: str, sources: list[str]) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    deps = list(sources)
+    for d in (CSRC, os.path.join(CSRC, "host"), INCLUDE):
+        if os.path.isdir(d):
+            deps += [os.path.join(d, f) for f in os.listdir(d) if f.endswith((".h", ".cuh", ".hpp"))]
+    return any(os.path.getmtime(s) > t for s in deps)
+
+
+def _run(cmd: list[str]) -> None:
+    print(" ".join(cmd), file=sys.stderr)
+    subprocess.run(cmd, check=True)
+
+
+def build_device(force: bool = False) -> str:
+    sources = [os.path.join(CSRC, s) for s in DEVICE_SOURCES]
+    if not force and not _stale(DEVICE_LIB, sources):
+        return DEVICE_LIB
+    objdir = os.path.join(HERE, "_build")
+    os.makedirs(objdir, exist_ok=True)
+    objects = []
+    for s in sources:
+        o = os.path.join(objdir, os.path.basename(s) + ".o")
+        _run([NVCC, *ARCH, *COMMON, "-c", s, "-o", o])
+        objects.append(o)
+    _run([NVCC, *ARCH, "-shared", "-o", DEVICE_LIB, *objects])
+    return DEVICE_LIB
+
+
+def host_sources() -> list[str]:
+    d = os.path.join(CSRC, "host")
+    if not os.path.isdir(d):
+        return []
+    return sorted(os.path.join(d, f) for f in os.listdir(d) if f.endswith(".cpp"))
+
+
+def build_host(force: bool = False) -> str | None:
+    sources = host_sources()
+    if not sources:
+        return None
+    if not force and not _stale(HOST_LIB, sources + [DEVICE_LIB]):
+        return HOST_LIB
+    _run(["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-Wextra", f"-I{INCLUDE}",
+          f"-I{os.path.join(CSRC, 'host')}", *sources, "-o", HOST_LIB, f"-L{HERE}", "-lmpb200",
+          "-Wl,-rpath,$ORIGIN", "-Wl,--no-undefined"])
+    return HOST_LIB
+
+
+def build(force: bool = False) -> None:
+    build_device(force)
+    build_host(force)
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv)

@@ -1,0 +1,270 @@
+// Paged attention over the MiniPrefix K/V page pools (sm_100a).
+//
+// Replaces the reference's attention_kernel (miniprefix/src/backend/cuda/
+// llama_runner.cu:33-48: one block per (row, q head), one token per iteration,
+// eight __syncthreads per token, each K/V row fetched once per q head) and
+// computes the CPU runner's attention (miniprefix/src/backend/cpu/
+// llama_runner.cpp:85-93): causal GQA, kv head = h / 3, scale 1/sqrt(64), softmax.
+//
+// Design (one query row, all 9 heads, per CTA; split-K over pages):
+//  * A CTA owns one slice [page_begin, page_end) of one query row's context. A row
+//    with more than one slice is merged by the last slice to finish (arrival
+//    counter per row), so one launch produces the final output.
+//  * K and V of 32 consecutive tokens form one stage. Runs of tokens that are
+//    contiguous inside a page (a page is [slot][192] floats for one layer) are
+//    moved by the bulk-copy engine (cp.async.bulk) into shared memory and
+//    complete on a per-stage mbarrier, so 2 stages stay in flight while one is
+//    consumed. Each K/V byte is read from HBM once for all 3 q heads of its group.
+//  * Scores: 96 (token, kv head) pairs x 4 lanes; each lane keeps its 3 heads'
+//    16 query values in registers and dots one 64-byte quarter of the key row,
+//    quarters rotated by pair parity so the 8 lanes of a 128-bit phase hit
+//    distinct banks. Softmax: one warp per head, online (running max / sum).
+//    P.V: 2 token halves x 192 (kv head, dim) columns, 3 heads per thread.
+//  * Tokens past the row length are masked by select (never by multiplying), so
+//    stale or uninitialised shared memory cannot leak NaN into the result.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mpb {
+namespace {
+
+constexpr int kStageTokens = 32;
+constexpr int kThreads = 384;
+constexpr int kStages = 3;
+constexpr int kStageFloats = kStageTokens * kKvWidth;  // per pool
+constexpr size_t kAttnSmem = size_t(kStages) * 2 * kStageFloats * sizeof(float) +
+                             2 * kHeads * kStageTokens * sizeof(float) + 4 * kHeads * sizeof(float) +
+                             kStages * sizeof(uint64_t) + 16;
+
+struct Shared {
+    float* stages;  // stage i: K at stages + 2*i*kStageFloats, V right after
+    float* scores;  // [9][32]
+    float* probs;   // [9][32]
+    float* alpha;   // [9]
+    float* m;       // [9]
+    float* l;       // [9]
+    int* flag;      // [1] error / last-arriver broadcast
+    uint64_t* bar;  // [kStages]
+};
+
+// Issue the copies for context tokens [a, b) into stage buffers (warp 0 only).
+__device__ __forceinline__ void issue_stage(const AttnParams& p, const int32_t* table, int a, int b, float* kdst,
+                                            float* vdst, uint64_t* bar, int lane) {
+    const int bt = p.block_tokens;
+    const int first_page = a / bt;
+    const int run_begin = max(a, (first_page + lane) * bt);
+    const int run_end = min(b, (first_page + lane + 1) * bt);
+    if (lane == 0) mbar_arrive_expect_tx(bar, uint32_t(b - a) * 2u * kKvWidth * sizeof(float));
+    __syncwarp();
+    if (run_begin < run_end) {
+        const int page = first_page + lane;
+        int block = page < p.table_stride ? table[page] : -1;
+        if (block < 0 || block >= p.max_blocks) {
+            raise_error(p.error, kErrBounds);
+            block = 0;  // stay in bounds; the error word fails the step
+        }
+        const size_t src = ((size_t(block) * p.layers + p.layer) * bt + (run_begin - page * bt)) * kKvWidth;
+        const uint32_t bytes = uint32_t(run_end - run_begin) * kKvWidth * sizeof(float);
+        bulk_copy_g2s(kdst + (run_begin - a) * kKvWidth, p.keys + src, bytes, bar);
+        bulk_copy_g2s(vdst + (run_begin - a) * kKvWidth, p.values + src, bytes, bar);
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) paged_attention_kernel(const AttnParams p) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    Shared s;
+    {
+        float* f = reinterpret_cast<float*>(smem_raw);
+        s.stages = f;
+        f += 2 * kStages * kStageFloats;
+        s.scores = f; f += kHeads * kStageTokens;
+        s.probs = f; f += kHeads * kStageTokens;
+        s.alpha = f; f += kHeads;
+        s.m = f; f += kHeads;
+        s.l = f; f += kHeads;
+        s.flag = reinterpret_cast<int*>(f); f += kHeads;
+        s.bar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(f) + 7) & ~uintptr_t(7));
+    }
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const AttnWork w = p.work[blockIdx.x];
+    const int row = w.row;
+    const int len = p.row_len[row];
+    const int32_t* table = p.tables + size_t(p.row_slot[row]) * p.table_stride;
+    const int tok_begin = w.page_begin * p.block_tokens;
+    const int tok_end = min(w.page_end * p.block_tokens, len);
+    const int n_stages = tok_end > tok_begin ? (tok_end - tok_begin + kStageTokens - 1) / kStageTokens : 0;
+
+    if (tid == 0) {
+        for (int i = 0; i < kStages; ++i) mbar_init(&s.bar[i], 1);
+        s.flag[0] = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (warp == 0)
+        for (int i = 0; i < kStages && i < n_stages; ++i) {
+            const int a = tok_begin + i * kStageTokens;
+            issue_stage(p, table, a, min(a + kStageTokens, tok_end), s.stages + 2 * i * kStageFloats,
+                        s.stages + (2 * i + 1) * kStageFloats, &s.bar[i], lane);
+        }
+
+    // Score-phase identity: pair = (token t, kv head kh), 4 lanes per pair.
+    const int pair = tid >> 2, sub = tid & 3;
+    const int st = pair / kKvHeads, skh = pair % kKvHeads, rot = pair & 1;
+    float4 qr[kGroup][4];
+    {
+        const float* qrow = p.q + size_t(row) * p.q_stride;
+#pragma unroll
+        for (int hh = 0; hh < kGroup; ++hh)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int chunk = sub + 4 * ((j + rot) & 3);
+                qr[hh][j] = *reinterpret_cast<const float4*>(qrow + (skh * kGroup + hh) * kHeadDim + 4 * chunk);
+            }
+    }
+    // P.V identity: token half, column (kv head, dim).
+    const int half = tid / kKvWidth, col = tid % kKvWidth, pkh = col / kHeadDim;
+    float acc[kGroup] = {0.f, 0.f, 0.f};
+    float m_run = -INFINITY, l_run = 0.f;  // meaningful in warps 0..8 (head = warp)
+
+    for (int i = 0; i < n_stages; ++i) {
+        const int stage = i % kStages;
+        const int a = tok_begin + i * kStageTokens;
+        const int n_valid = min(kStageTokens, tok_end - a);
+        if (!mbar_wait_bounded(&s.bar[stage], (i / kStages) & 1)) s.flag[0] = 1;
+        // scores
+        {
+            const float* krow = s.stages + 2 * stage * kStageFloats + st * kKvWidth + skh * kHeadDim;
+            float part[kGroup] = {0.f, 0.f, 0.f};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int chunk = sub + 4 * ((j + rot) & 3);
+                const float4 kv = *reinterpret_cast<const float4*>(krow + 4 * chunk);
+#pragma unroll
+                for (int hh = 0; hh < kGroup; ++hh) {
+                    part[hh] = fmaf(qr[hh][j].x, kv.x, part[hh]);
+                    part[hh] = fmaf(qr[hh][j].y, kv.y, part[hh]);
+                    part[hh] = fmaf(qr[hh][j].z, kv.z, part[hh]);
+                    part[hh] = fmaf(qr[hh][j].w, kv.w, part[hh]);
+                }
+            }
+#pragma unroll
+            for (int hh = 0; hh < kGroup; ++hh) {
+                part[hh] += __shfl_xor_sync(0xffffffffu, part[hh], 1);
+                part[hh] += __shfl_xor_sync(0xffffffffu, part[hh], 2);
+            }
+            if (sub < kGroup) {
+                const float sc = sub == 0 ? part[0] : (sub == 1 ? part[1] : part[2]);
+                s.scores[(skh * kGroup + sub) * kStageTokens + st] = st < n_valid ? sc * 0.125f : -INFINITY;
+            }
+        }
+        __syncthreads();
+        if (s.flag[0]) break;
+        // online softmax, one warp per head
+        if (warp < kHeads) {
+            const float sc = s.scores[warp * kStageTokens + lane];
+            const float m_new = fmaxf(m_run, warp_max(sc));
+            const float alpha = expf(m_run - m_new);
+            const float pr = expf(sc - m_new);
+            l_run = l_run * alpha + warp_sum(pr);
+            m_run = m_new;
+            s.probs[warp * kStageTokens + lane] = pr;
+            if (lane == 0) s.alpha[warp] = alpha;
+        }
+        __syncthreads();
+        // P.V
+        {
+            const float* vbase = s.stages + (2 * stage + 1) * kStageFloats + col;
+            const float* pb = s.probs + (pkh * kGroup) * kStageTokens + half * 16;
+#pragma unroll
+            for (int hh = 0; hh < kGroup; ++hh) acc[hh] *= s.alpha[pkh * kGroup + hh];
+#pragma unroll
+            for (int tt = 0; tt < 16; ++tt) {
+                const int t = half * 16 + tt;
+                const float v = t < n_valid ? vbase[t * kKvWidth] : 0.f;
+#pragma unroll
+                for (int hh = 0; hh < kGroup; ++hh) acc[hh] = fmaf(pb[hh * kStageTokens + tt], v, acc[hh]);
+            }
+        }
+        __syncthreads();
+        if (warp == 0 && i + kStages < n_stages) {
+            fence_proxy_async_shared();
+            const int a2 = tok_begin + (i + kStages) * kStageTokens;
+            issue_stage(p, table, a2, min(a2 + kStageTokens, tok_end), s.stages + 2 * stage * kStageFloats,
+                        s.stages + (2 * stage + 1) * kStageFloats, &s.bar[stage], lane);
+        }
+    }
+    if (s.flag[0]) {
+        if (tid == 0) raise_error(p.error, kErrTimeout);
+        return;
+    }
+    // Merge the two token halves; head statistics to shared memory.
+    float* red = s.stages;  // all copies have landed: stage 0 is free
+    if (half == 1) {
+#pragma unroll
+        for (int hh = 0; hh < kGroup; ++hh) red[hh * kKvWidth + col] = acc[hh];
+    }
+    if (warp < kHeads && lane == 0) {
+        s.m[warp] = m_run;
+        s.l[warp] = l_run;
+    }
+    __syncthreads();
+    const int splits = p.row_splits[row];
+    if (half == 0) {
+#pragma unroll
+        for (int hh = 0; hh < kGroup; ++hh) {
+            const float total = acc[hh] + red[hh * kKvWidth + col];
+            const int h = pkh * kGroup + hh, d = col % kHeadDim;
+            if (splits == 1) {
+                p.out[size_t(row) * p.out_stride + h * kHeadDim + d] = total / s.l[h];
+            } else {
+                float* part = p.partial + (size_t(blockIdx.x) * kHeads + h) * (kHeadDim + 2);
+                part[2 + d] = total;
+                if (d == 0) {
+                    part[0] = s.m[h];
+                    part[1] = s.l[h];
+                }
+            }
+        }
+    }
+    if (splits == 1) return;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned prev = atomicAdd(&p.counters[row], 1u);
+        s.flag[0] = prev == unsigned(splits - 1) ? 2 : 0;
+    }
+    __syncthreads();
+    if (s.flag[0] != 2) return;
+    __threadfence();
+    // Last slice of this row: merge all slices' (m, l, acc) in slice order.
+    const int w0 = p.row_work0[row];
+    for (int o = tid; o < kHeads * kHeadDim; o += kThreads) {
+        const int h = o / kHeadDim, d = o % kHeadDim;
+        float mx = -INFINITY;
+        for (int k = 0; k < splits; ++k)
+            mx = fmaxf(mx, __ldcg(p.partial + (size_t(w0 + k) * kHeads + h) * (kHeadDim + 2)));
+        float num = 0.f, den = 0.f;
+        for (int k = 0; k < splits; ++k) {
+            const float* part = p.partial + (size_t(w0 + k) * kHeads + h) * (kHeadDim + 2);
+            const float sc = expf(__ldcg(part) - mx);
+            den = fmaf(__ldcg(part + 1), sc, den);
+            num = fmaf(__ldcg(part + 2 + d), sc, num);
+        }
+        p.out[size_t(row) * p.out_stride + o] = num / den;
+    }
+    if (tid == 0) p.counters[row] = 0u;  // ready for the next launch
+}
+
+}  // namespace
+
+cudaError_t configure_attention() {
+    return cudaFuncSetAttribute(paged_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kAttnSmem));
+}
+
+cudaError_t launch_paged_attention(const AttnParams& p, cudaStream_t stream) {
+    if (p.work_count <= 0) return cudaSuccess;
+    paged_attention_kernel<<<p.work_count, kThreads, kAttnSmem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace mpb

@@ -1,0 +1,770 @@
+// C ABI of the device layer (include/miniprefix_b200.h): context, weights, pools,
+// block tables, COW, the batched forward and the paged-attention operator.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "kernels.h"
+#include "miniprefix_b200.h"
+
+namespace {
+
+thread_local std::string g_error;
+
+struct Failure {
+    int code;
+    std::string message;
+};
+
+void fail(int code, const std::string& message) { throw Failure{code, message}; }
+
+void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) fail(e == cudaErrorMemoryAllocation ? MP_ERR_NOMEM : MP_ERR_CUDA,
+                               std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+template <class F>
+int guarded(F&& body) {
+    try {
+        body();
+        return MP_OK;
+    } catch (const Failure& f) {
+        g_error = f.message;
+        return f.code;
+    } catch (const std::bad_alloc&) {
+        g_error = "host allocation failed";
+        return MP_ERR_NOMEM;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return MP_ERR_INVALID;
+    }
+}
+
+template <class T>
+T* device_alloc(size_t count, const char* what) {
+    void* p = nullptr;
+    if (count == 0) count = 1;
+    cuda_check(cudaMalloc(&p, count * sizeof(T)), what);
+    return static_cast<T*>(p);
+}
+
+template <class T>
+T* host_alloc(size_t count, const char* what) {
+    void* p = nullptr;
+    if (count == 0) count = 1;
+    cuda_check(cudaMallocHost(&p, count * sizeof(T)), what);
+    return static_cast<T*>(p);
+}
+
+// Work decomposition of paged attention: each query row's context pages are cut
+// into slices of `pages_per_split` pages. With pages_per_split == 0 the slice
+// length targets about eight CTAs per SM over the whole launch (148 SMs), never
+// below 64 tokens per slice.
+struct AttnPlan {
+    std::vector<int32_t> splits, work0;
+    std::vector<mpb::AttnWork> work;
+    double bytes = 0;  // algorithmic K/V bytes one layer reads
+};
+
+void plan_attention(const int32_t* lengths, int rows, int block_tokens, int pages_per_split, AttnPlan& plan) {
+    plan.splits.assign(rows, 0);
+    plan.work0.assign(rows, 0);
+    plan.work.clear();
+    plan.bytes = 0;
+    long long total_tokens = 0;
+    for (int r = 0; r < rows; ++r) total_tokens += lengths[r];
+    int pps = pages_per_split;
+    if (pps <= 0) {
+        const long long target = 148LL * 8;
+        long long slice_tokens = std::max<long long>(64, (total_tokens + target - 1) / target);
+        slice_tokens = (slice_tokens + 31) / 32 * 32;
+        pps = int(std::max<long long>(1, slice_tokens / block_tokens));
+    }
+    for (int r = 0; r < rows; ++r) {
+        const int pages = (lengths[r] + block_tokens - 1) / block_tokens;
+        const int n = std::max(1, (pages + pps - 1) / pps);
+        plan.splits[r] = n;
+        plan.work0[r] = int(plan.work.size());
+        for (int s = 0; s < n; ++s)
+            plan.work.push_back({r, s * pps, std::min(pages, (s + 1) * pps), s});
+        // K and V rows, the query row and output row, the table entries.
+        plan.bytes += double(lengths[r]) * 2 * mpb::kKvWidth * sizeof(float) +
+                      2.0 * mpb::kQWidth * sizeof(float) + double(pages) * sizeof(int32_t);
+    }
+}
+
+}  // namespace
+
+namespace mpb {
+void set_last_error(const char* message) { g_error = message; }
+}  // namespace mpb
+
+struct mp_context {
+    int device = 0;
+    mp_model_config model{};
+    mp_runtime_config rt{};
+    int dim = 64, kvw = 192, qkvw = 960;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t done = nullptr, mark[2] = {nullptr, nullptr};
+    int mark_count = 0;
+    // weights, packed [N][K] (K contiguous)
+    float *embed = nullptr, *final_norm = nullptr, *head = nullptr, *in_norm = nullptr, *post_norm = nullptr;
+    float *wqkv = nullptr, *wo = nullptr, *wgate = nullptr, *wup = nullptr, *wdown = nullptr;
+    std::set<std::string> received;
+    bool finalized = false;
+    // pools and tables
+    float *keys = nullptr, *values = nullptr;
+    uint64_t pool_elements = 0;
+    int32_t* tables = nullptr;
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+    // workspace
+    float *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr;
+    float *xl = nullptr, *logits = nullptr, *partial = nullptr;
+    unsigned *counters = nullptr, *error = nullptr;
+    int32_t *meta = nullptr, *out_tokens = nullptr, *out_finite = nullptr, *cow = nullptr, *patch = nullptr;
+    size_t meta_capacity = 0, work_capacity = 0;
+    // pinned host staging
+    int32_t* h_meta = nullptr;
+    int32_t *h_tokens = nullptr, *h_finite = nullptr;
+    unsigned* h_error = nullptr;
+    int32_t* h_patch = nullptr;
+    size_t patch_capacity = 0;
+    uint64_t* h_cow = nullptr;
+    size_t cow_capacity = 0;
+    // current step
+    int rows = 0, seqs = 0, work_count = 0;
+    size_t off_tokens = 0, off_pos = 0, off_slot = 0, off_len = 0, off_splits = 0, off_work0 = 0, off_last = 0,
+           off_work = 0;
+    bool prepared = false;
+    AttnPlan plan;
+    std::vector<int32_t> lengths;
+    // attention profiling
+    bool profile = false;
+    std::vector<cudaEvent_t> prof_events;
+    int prof_used = 0;
+    float prof_ms = 0.f;
+    int prof_launches = 0;
+    double prof_bytes = 0;
+};
+
+namespace {
+
+size_t max_work(const mp_runtime_config& rt) { return size_t(rt.max_step_tokens) + 2048; }
+
+void free_context(mp_context* c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    for (void* p : {(void*)c->embed, (void*)c->final_norm, (void*)c->in_norm, (void*)c->post_norm, (void*)c->wqkv,
+                    (void*)c->wo, (void*)c->wgate, (void*)c->wup, (void*)c->wdown, (void*)c->keys, (void*)c->values,
+                    (void*)c->tables, (void*)c->rope_cos, (void*)c->rope_sin, (void*)c->x, (void*)c->xn,
+                    (void*)c->qkv, (void*)c->q, (void*)c->attn, (void*)c->h, (void*)c->xl, (void*)c->logits,
+                    (void*)c->partial, (void*)c->counters, (void*)c->error, (void*)c->meta, (void*)c->out_tokens,
+                    (void*)c->out_finite, (void*)c->cow, (void*)c->patch})
+        if (p) cudaFree(p);
+    if (c->head && c->head != c->embed) cudaFree(c->head);
+    for (void* p : {(void*)c->h_meta, (void*)c->h_tokens, (void*)c->h_finite, (void*)c->h_error, (void*)c->h_patch,
+                    (void*)c->h_cow})
+        if (p) cudaFreeHost(p);
+    for (auto e : c->prof_events) cudaEventDestroy(e);
+    if (c->done) cudaEventDestroy(c->done);
+    for (auto e : c->mark)
+        if (e) cudaEventDestroy(e);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+void wait_event(cudaEvent_t e, int timeout_ms) {
+    const auto start = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t s = cudaEventQuery(e);
+        if (s == cudaSuccess) return;
+        if (s != cudaErrorNotReady) cuda_check(s, "step completion");
+        if (timeout_ms >= 0 &&
+            std::chrono::steady_clock::now() - start > std::chrono::milliseconds(timeout_ms))
+            fail(MP_ERR_TIMEOUT, "device work did not complete within the timeout");
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+void validate_geometry(const mp_model_config& m, const mp_runtime_config& r) {
+    const bool valid = m.layers >= 1 && m.layers <= 128 && m.hidden >= 2 && m.hidden <= 8192 && m.intermediate >= 1 &&
+                       m.intermediate <= 65536 && m.heads >= 1 && m.kv_heads >= 1 && m.hidden % m.heads == 0 &&
+                       m.heads % m.kv_heads == 0 && (m.hidden / m.heads) % 2 == 0 && m.hidden / m.heads <= 256 &&
+                       m.vocabulary >= 2 && m.vocabulary <= 262144 && m.context >= 1 && m.context <= 131072 &&
+                       m.eos >= 0 && m.eos < m.vocabulary && std::isfinite(m.rms_epsilon) && m.rms_epsilon > 0 &&
+                       std::isfinite(m.rope_theta) && m.rope_theta > 1;
+    if (!valid) fail(MP_ERR_INVALID, "unsupported/invalid Llama configuration");
+    if (m.heads != mpb::kHeads || m.kv_heads != mpb::kKvHeads || m.hidden != mpb::kQWidth)
+        fail(MP_ERR_UNSUPPORTED, "kernels are specialised for 9 query heads, 3 kv heads, head_dim 64");
+    if (m.intermediate % 64 || m.vocabulary % 64)
+        fail(MP_ERR_UNSUPPORTED, "intermediate and vocabulary must be multiples of 64");
+    if (r.block_tokens < 1 || r.max_blocks < 1 || r.max_sequences < 1 || r.max_step_tokens < 1 ||
+        r.max_step_sequences < 1 || r.max_step_sequences > r.max_step_tokens || r.table_stride < 1 ||
+        int64_t(r.table_stride) * r.block_tokens < m.context)
+        fail(MP_ERR_INVALID, "invalid runtime configuration");
+}
+
+struct WeightSlot {
+    float* base;
+    int rows_n;  // N of the packed [N][K] matrix slice
+    int k;       // K
+    bool transpose;
+    size_t elements;
+};
+
+// Resolve an MPFX0001 tensor name to its packed destination.
+WeightSlot resolve(mp_context* c, const std::string& name) {
+    const auto& m = c->model;
+    const int H = m.hidden, I = m.intermediate, kvw = c->kvw, V = m.vocabulary;
+    if (name == "model.embed_tokens.weight") return {c->embed, V, H, false, size_t(V) * H};
+    if (name == "model.norm.weight") return {c->final_norm, 1, H, false, size_t(H)};
+    if (name == "lm_head.weight") {
+        if (m.tied) fail(MP_ERR_INVALID, "tied model has no lm_head.weight");
+        return {c->head, V, H, true, size_t(V) * H};
+    }
+    const std::string prefix = "model.layers.";
+    if (name.compare(0, prefix.size(), prefix) != 0) fail(MP_ERR_INVALID, "unknown tensor: " + name);
+    size_t dot = name.find('.', prefix.size());
+    if (dot == std::string::npos) fail(MP_ERR_INVALID, "unknown tensor: " + name);
+    int layer = -1;
+    try {
+        layer = std::stoi(name.substr(prefix.size(), dot - prefix.size()));
+    } catch (...) {
+        fail(MP_ERR_INVALID, "unknown tensor: " + name);
+    }
+    if (layer < 0 || layer >= m.layers) fail(MP_ERR_INVALID, "unknown tensor: " + name);
+    const std::string s = name.substr(dot + 1);
+    const size_t L = size_t(layer);
+    if (s == "input_layernorm.weight") return {c->in_norm + L * H, 1, H, false, size_t(H)};
+    if (s == "post_attention_layernorm.weight") return {c->post_norm + L * H, 1, H, false, size_t(H)};
+    float* qkv = c->wqkv + L * size_t(c->qkvw) * H;
+    if (s == "self_attn.q_proj.weight") return {qkv, H, H, true, size_t(H) * H};
+    if (s == "self_attn.k_proj.weight") return {qkv + size_t(H) * H, kvw, H, true, size_t(H) * kvw};
+    if (s == "self_attn.v_proj.weight") return {qkv + size_t(H + kvw) * H, kvw, H, true, size_t(H) * kvw};
+    if (s == "self_attn.o_proj.weight") return {c->wo + L * size_t(H) * H, H, H, true, size_t(H) * H};
+    if (s == "mlp.gate_proj.weight") return {c->wgate + L * size_t(I) * H, I, H, true, size_t(H) * I};
+    if (s == "mlp.up_proj.weight") return {c->wup + L * size_t(I) * H, I, H, true, size_t(H) * I};
+    if (s == "mlp.down_proj.weight") return {c->wdown + L * size_t(H) * I, H, I, true, size_t(I) * H};
+    fail(MP_ERR_INVALID, "unknown tensor: " + name);
+    return {};
+}
+
+size_t expected_tensors(const mp_model_config& m) { return size_t(m.layers) * 9 + 2 + (m.tied ? 0 : 1); }
+
+void ensure_patch(mp_context* c, size_t pairs) {
+    if (pairs <= c->patch_capacity) return;
+    cuda_check(cudaStreamSynchronize(c->stream), "patch staging reuse");
+    if (c->h_patch) cudaFreeHost(c->h_patch);
+    if (c->patch) cudaFree(c->patch);
+    c->h_patch = nullptr;
+    c->patch = nullptr;
+    c->patch_capacity = 0;
+    c->h_patch = host_alloc<int32_t>(2 * pairs, "table patch staging");
+    c->patch = device_alloc<int32_t>(2 * pairs, "table patch buffer");
+    c->patch_capacity = pairs;
+}
+
+void record_attention_event(mp_context* c) {
+    if (size_t(c->prof_used) == c->prof_events.size()) {
+        cudaEvent_t e;
+        cuda_check(cudaEventCreate(&e), "profile event");
+        c->prof_events.push_back(e);
+    }
+    cuda_check(cudaEventRecord(c->prof_events[c->prof_used++], c->stream), "profile event record");
+}
+
+void harvest_profile(mp_context* c) {
+    for (int i = 0; i + 1 < c->prof_used; i += 2) {
+        float ms = 0.f;
+        cuda_check(cudaEventElapsedTime(&ms, c->prof_events[i], c->prof_events[i + 1]), "profile elapsed");
+        c->prof_ms += ms;
+        c->prof_launches += 1;
+    }
+    c->prof_used = 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mp_last_error(void) { return g_error.c_str(); }
+
+int mp_create(int device, const mp_model_config* model, const mp_runtime_config* runtime, mp_context** out) {
+    if (!model || !runtime || !out) {
+        g_error = "null argument";
+        return MP_ERR_INVALID;
+    }
+    *out = nullptr;
+    mp_context* c = new (std::nothrow) mp_context;
+    if (!c) return MP_ERR_NOMEM;
+    const int rc = guarded([&] {
+        validate_geometry(*model, *runtime);
+        c->device = device;
+        c->model = *model;
+        c->rt = *runtime;
+        const auto& m = c->model;
+        const auto& r = c->rt;
+        c->dim = m.hidden / m.heads;
+        c->kvw = m.kv_heads * c->dim;
+        c->qkvw = m.hidden + 2 * c->kvw;
+        cuda_check(cudaSetDevice(device), "select device");
+        cuda_check(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "create stream");
+        cuda_check(cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming), "create event");
+        for (auto& e : c->mark) cuda_check(cudaEventCreate(&e), "create timer event");
+        cuda_check(mpb::configure_attention(), "configure attention kernel");
+        const size_t H = m.hidden, I = m.intermediate, L = m.layers, V = m.vocabulary;
+        c->embed = device_alloc<float>(V * H, "embedding");
+        c->final_norm = device_alloc<float>(H, "final norm");
+        c->head = m.tied ? c->embed : device_alloc<float>(V * H, "lm head");
+        c->in_norm = device_alloc<float>(L * H, "input norms");
+        c->post_norm = device_alloc<float>(L * H, "post-attention norms");
+        c->wqkv = device_alloc<float>(L * c->qkvw * H, "qkv projections");
+        c->wo = device_alloc<float>(L * H * H, "o projections");
+        c->wgate = device_alloc<float>(L * I * H, "gate projections");
+        c->wup = device_alloc<float>(L * I * H, "up projections");
+        c->wdown = device_alloc<float>(L * H * I, "down projections");
+        c->pool_elements = uint64_t(r.max_blocks) * L * r.block_tokens * c->kvw;
+        c->keys = device_alloc<float>(c->pool_elements, "K pool");
+        c->values = device_alloc<float>(c->pool_elements, "V pool");
+        cuda_check(cudaMemsetAsync(c->keys, 0, c->pool_elements * sizeof(float), c->stream), "zero K pool");
+        cuda_check(cudaMemsetAsync(c->values, 0, c->pool_elements * sizeof(float), c->stream), "zero V pool");
+        const size_t table_elements = size_t(r.max_sequences) * r.table_stride;
+        c->tables = device_alloc<int32_t>(table_elements, "block tables");
+        cuda_check(cudaMemsetAsync(c->tables, 0xff, table_elements * sizeof(int32_t), c->stream), "clear tables");
+        // RoPE tables, computed exactly as the CPU runner computes each angle
+        // (miniprefix/src/backend/cpu/llama_runner.cpp:19-20).
+        {
+            const int half = c->dim / 2;
+            std::vector<float> cs(size_t(m.context) * half), sn(size_t(m.context) * half);
+            for (int p = 0; p < m.context; ++p)
+                for (int d = 0; d < half; ++d) {
+                    const float angle = float(p) / std::pow(m.rope_theta, float(2 * d) / float(c->dim));
+                    cs[size_t(p) * half + d] = std::cos(angle);
+                    sn[size_t(p) * half + d] = std::sin(angle);
+                }
+            c->rope_cos = device_alloc<float>(cs.size(), "rope cos");
+            c->rope_sin = device_alloc<float>(sn.size(), "rope sin");
+            cuda_check(cudaMemcpy(c->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "upload rope cos");
+            cuda_check(cudaMemcpy(c->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "upload rope sin");
+        }
+        const size_t T = r.max_step_tokens, S = r.max_step_sequences;
+        c->x = device_alloc<float>(T * H, "residual stream");
+        c->xn = device_alloc<float>(T * H, "normed activations");
+        c->qkv = device_alloc<float>(T * c->qkvw, "qkv activations");
+        c->q = device_alloc<float>(T * H, "roped queries");
+        c->attn = device_alloc<float>(T * H, "attention output");
+        c->h = device_alloc<float>(T * I, "mlp activations");
+        c->xl = device_alloc<float>(S * H, "last-row activations");
+        c->logits = device_alloc<float>(S * V, "logits");
+        c->work_capacity = max_work(r);
+        c->partial = device_alloc<float>(c->work_capacity * mpb::kHeads * (mpb::kHeadDim + 2), "attention partials");
+        c->counters = device_alloc<unsigned>(T, "attention counters");
+        cuda_check(cudaMemsetAsync(c->counters, 0, T * sizeof(unsigned), c->stream), "zero counters");
+        c->error = device_alloc<unsigned>(1, "error word");
+        cuda_check(cudaMemsetAsync(c->error, 0, sizeof(unsigned), c->stream), "zero error word");
+        c->meta_capacity = 6 * T + S + 4 * c->work_capacity;
+        c->meta = device_alloc<int32_t>(c->meta_capacity, "step metadata");
+        c->h_meta = host_alloc<int32_t>(c->meta_capacity, "step metadata staging");
+        c->out_tokens = device_alloc<int32_t>(S, "greedy tokens");
+        c->out_finite = device_alloc<int32_t>(S, "finite flags");
+        c->h_tokens = host_alloc<int32_t>(S, "token staging");
+        c->h_finite = host_alloc<int32_t>(S, "finite staging");
+        c->h_error = host_alloc<unsigned>(1, "error staging");
+        cuda_check(cudaStreamSynchronize(c->stream), "context initialisation");
+    });
+    if (rc != MP_OK) {
+        free_context(c);
+        return rc;
+    }
+    *out = c;
+    return MP_OK;
+}
+
+void mp_destroy(mp_context* c) { free_context(c); }
+
+int mp_set_weight(mp_context* c, const char* name, const float* host, size_t elements) {
+    return guarded([&] {
+        if (!c || !name || !host) fail(MP_ERR_INVALID, "null argument");
+        cuda_check(cudaSetDevice(c->device), "select device");
+        const WeightSlot slot = resolve(c, name);
+        if (elements != slot.elements) fail(MP_ERR_INVALID, std::string("tensor shape mismatch: ") + name);
+        if (!slot.transpose) {
+            cuda_check(cudaMemcpy(slot.base, host, elements * 4, cudaMemcpyHostToDevice), "upload weight");
+        } else {
+            // MPFX stores [K][N] ([in][out]); the kernels read [N][K].
+            const int N = slot.rows_n, K = slot.k;
+            std::vector<float> t(elements);
+            for (int k = 0; k < K; ++k)
+                for (int n = 0; n < N; ++n) t[size_t(n) * K + k] = host[size_t(k) * N + n];
+            cuda_check(cudaMemcpy(slot.base, t.data(), elements * 4, cudaMemcpyHostToDevice), "upload weight");
+        }
+        c->received.insert(name);
+        c->finalized = false;
+    });
+}
+
+int mp_finalize_weights(mp_context* c) {
+    return guarded([&] {
+        if (!c) fail(MP_ERR_INVALID, "null context");
+        if (c->received.size() != expected_tensors(c->model)) fail(MP_ERR_INVALID, "model tensor count mismatch");
+        c->finalized = true;
+    });
+}
+
+int mp_table_write(mp_context* c, int32_t slot, int32_t first, const int32_t* blocks, int32_t count) {
+    return guarded([&] {
+        if (!c || (count > 0 && !blocks)) fail(MP_ERR_INVALID, "null argument");
+        if (slot < 0 || slot >= c->rt.max_sequences || first < 0 || count < 0 ||
+            int64_t(first) + count > c->rt.table_stride)
+            fail(MP_ERR_INVALID, "block table write out of range");
+        if (count == 0) return;
+        for (int i = 0; i < count; ++i)
+            if (blocks[i] < 0 || blocks[i] >= c->rt.max_blocks) fail(MP_ERR_INVALID, "invalid physical page id");
+        cuda_check(cudaSetDevice(c->device), "select device");
+        ensure_patch(c, size_t(count));
+        // The staging buffer may still feed the previous patch: wait for it.
+        cuda_check(cudaStreamSynchronize(c->stream), "table staging reuse");
+        for (int i = 0; i < count; ++i) {
+            c->h_patch[2 * i] = slot * c->rt.table_stride + first + i;
+            c->h_patch[2 * i + 1] = blocks[i];
+        }
+        cuda_check(cudaMemcpyAsync(c->patch, c->h_patch, size_t(count) * 8, cudaMemcpyHostToDevice, c->stream),
+                   "upload block table entries");
+        cuda_check(mpb::launch_table_patch(c->patch, count, c->tables,
+                                           int64_t(c->rt.max_sequences) * c->rt.table_stride, c->error, c->stream),
+                   "table patch launch");
+    });
+}
+
+int mp_cow_copy(mp_context* c, const mp_tail_copy_region* regions, int32_t count) {
+    return guarded([&] {
+        if (!c || (count > 0 && !regions)) fail(MP_ERR_INVALID, "null argument");
+        if (count <= 0) return;
+        uint64_t max_rows = 0;
+        for (int i = 0; i < count; ++i) {
+            const auto& r = regions[i];
+            if (r.width % 4 || r.destination % 4 || r.source % 4 || r.pitch % 4 || r.width > r.pitch ||
+                r.destination + (r.rows ? (r.rows - 1) * r.pitch + r.width : 0) > c->pool_elements ||
+                r.source + (r.rows ? (r.rows - 1) * r.pitch + r.width : 0) > c->pool_elements)
+                fail(MP_ERR_INVALID, "COW region outside the pools");
+            max_rows = std::max(max_rows, r.rows);
+        }
+        cuda_check(cudaSetDevice(c->device), "select device");
+        if (size_t(count) > c->cow_capacity) {
+            cuda_check(cudaStreamSynchronize(c->stream), "cow staging reuse");
+            if (c->h_cow) cudaFreeHost(c->h_cow);
+            if (c->cow) cudaFree(c->cow);
+            c->h_cow = nullptr;
+            c->cow = nullptr;
+            c->cow_capacity = 0;
+            c->h_cow = host_alloc<uint64_t>(size_t(count) * 5, "cow staging");
+            c->cow = device_alloc<int32_t>(size_t(count) * 10, "cow regions");
+            c->cow_capacity = count;
+        }
+        cuda_check(cudaStreamSynchronize(c->stream), "cow staging reuse");
+        std::memcpy(c->h_cow, regions, size_t(count) * sizeof(mp_tail_copy_region));
+        cuda_check(cudaMemcpyAsync(c->cow, c->h_cow, size_t(count) * sizeof(mp_tail_copy_region),
+                                   cudaMemcpyHostToDevice, c->stream),
+                   "upload cow regions");
+        cuda_check(mpb::launch_cow_copy(reinterpret_cast<const mpb::CowRegion*>(c->cow), count, int(max_rows), c->keys,
+                                        c->values, c->pool_elements, c->error, c->stream),
+                   "cow launch");
+    });
+}
+
+int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t count, const int32_t* tokens) {
+    return guarded([&] {
+        if (!c || !seqs || !tokens) fail(MP_ERR_INVALID, "null argument");
+        if (!c->finalized) fail(MP_ERR_INVALID, "weights not finalized");
+        const auto& r = c->rt;
+        if (count < 1 || count > r.max_step_sequences) fail(MP_ERR_INVALID, "invalid sequence count");
+        int64_t total = 0;
+        for (int i = 0; i < count; ++i) {
+            const auto& s = seqs[i];
+            if (s.slot < 0 || s.slot >= r.max_sequences || s.start < 0 || s.count < 1 ||
+                int64_t(s.start) + s.count > c->model.context ||
+                int64_t(s.start) + s.count > int64_t(r.table_stride) * r.block_tokens)
+                fail(MP_ERR_INVALID, "invalid sequence descriptor");
+            total += s.count;
+        }
+        if (total > r.max_step_tokens) fail(MP_ERR_INVALID, "step exceeds max_step_tokens");
+        const int T = int(total);
+        for (int i = 0; i < T; ++i)
+            if (tokens[i] < 0 || tokens[i] >= c->model.vocabulary) fail(MP_ERR_INVALID, "invalid token");
+        c->lengths.resize(T);
+        int row = 0;
+        for (int i = 0; i < count; ++i)
+            for (int j = 0; j < seqs[i].count; ++j) c->lengths[row++] = seqs[i].start + j + 1;
+        plan_attention(c->lengths.data(), T, r.block_tokens, 0, c->plan);
+        const size_t W = c->plan.work.size();
+        if (W > c->work_capacity) fail(MP_ERR_INVALID, "attention work list exceeds capacity");
+        // layout: tokens | pos | slot | len | splits | work0 | last | work
+        cuda_check(cudaSetDevice(c->device), "select device");
+        cuda_check(cudaStreamSynchronize(c->stream), "metadata staging reuse");
+        int32_t* h = c->h_meta;
+        c->off_tokens = 0;
+        c->off_pos = c->off_tokens + T;
+        c->off_slot = c->off_pos + T;
+        c->off_len = c->off_slot + T;
+        c->off_splits = c->off_len + T;
+        c->off_work0 = c->off_splits + T;
+        c->off_last = c->off_work0 + T;
+        c->off_work = c->off_last + count;
+        std::memcpy(h + c->off_tokens, tokens, size_t(T) * 4);
+        row = 0;
+        for (int i = 0; i < count; ++i) {
+            for (int j = 0; j < seqs[i].count; ++j, ++row) {
+                h[c->off_pos + row] = seqs[i].start + j;
+                h[c->off_slot + row] = seqs[i].slot;
+                h[c->off_len + row] = seqs[i].start + j + 1;
+            }
+            h[c->off_last + i] = row - 1;
+        }
+        std::memcpy(h + c->off_splits, c->plan.splits.data(), size_t(T) * 4);
+        std::memcpy(h + c->off_work0, c->plan.work0.data(), size_t(T) * 4);
+        std::memcpy(h + c->off_work, c->plan.work.data(), W * sizeof(mpb::AttnWork));
+        const size_t bytes = (c->off_work + 4 * W) * 4;
+        cuda_check(cudaMemcpyAsync(c->meta, h, bytes, cudaMemcpyHostToDevice, c->stream), "upload step metadata");
+        c->rows = T;
+        c->seqs = count;
+        c->work_count = int(W);
+        c->prepared = true;
+    });
+}
+
+int mp_forward_launch(mp_context* c) {
+    return guarded([&] {
+        if (!c || !c->prepared) fail(MP_ERR_INVALID, "no prepared step");
+        cuda_check(cudaSetDevice(c->device), "select device");
+        const auto& m = c->model;
+        const auto& r = c->rt;
+        const int T = c->rows, S = c->seqs, H = m.hidden, I = m.intermediate;
+        cudaStream_t st = c->stream;
+        const int32_t* meta = c->meta;
+        cuda_check(cudaMemsetAsync(c->error, 0, sizeof(unsigned), st), "reset error word");
+        cuda_check(mpb::launch_embed_rmsnorm(meta + c->off_tokens, c->embed, m.vocabulary, c->in_norm, m.rms_epsilon,
+                                             c->x, c->xn, T, H, c->error, st),
+                   "embed launch");
+        mpb::AttnParams ap{};
+        ap.q = c->q;
+        ap.q_stride = H;
+        ap.keys = c->keys;
+        ap.values = c->values;
+        ap.layers = m.layers;
+        ap.block_tokens = r.block_tokens;
+        ap.max_blocks = r.max_blocks;
+        ap.tables = c->tables;
+        ap.table_stride = r.table_stride;
+        ap.row_slot = meta + c->off_slot;
+        ap.row_len = meta + c->off_len;
+        ap.row_splits = meta + c->off_splits;
+        ap.row_work0 = meta + c->off_work0;
+        ap.work = reinterpret_cast<const mpb::AttnWork*>(meta + c->off_work);
+        ap.work_count = c->work_count;
+        ap.partial = c->partial;
+        ap.counters = c->counters;
+        ap.out = c->attn;
+        ap.out_stride = H;
+        ap.error = c->error;
+        mpb::RopeAppendArgs ra{};
+        ra.qkv = c->qkv;
+        ra.qkv_stride = c->qkvw;
+        ra.row_pos = meta + c->off_pos;
+        ra.row_slot = meta + c->off_slot;
+        ra.rope_cos = c->rope_cos;
+        ra.rope_sin = c->rope_sin;
+        ra.max_position = m.context;
+        ra.q_out = c->q;
+        ra.q_stride = H;
+        ra.keys = c->keys;
+        ra.values = c->values;
+        ra.tables = c->tables;
+        ra.table_stride = r.table_stride;
+        ra.layers = m.layers;
+        ra.block_tokens = r.block_tokens;
+        ra.max_blocks = r.max_blocks;
+        ra.rows = T;
+        ra.error = c->error;
+        for (int l = 0; l < m.layers; ++l) {
+            const size_t L = size_t(l);
+            if (l > 0)
+                cuda_check(mpb::launch_rmsnorm(c->x, nullptr, c->in_norm + L * H, m.rms_epsilon, c->xn, T, H, st),
+                           "rmsnorm launch");
+            cuda_check(mpb::launch_gemm_simt({c->xn, H, c->wqkv + L * c->qkvw * H, H, c->qkv, c->qkvw, T, c->qkvw, H,
+                                              mpb::Epilogue::Store},
+                                             st),
+                       "qkv gemm");
+            ra.layer = l;
+            cuda_check(mpb::launch_rope_append(ra, st), "rope/append launch");
+            ap.layer = l;
+            if (c->profile) record_attention_event(c);
+            cuda_check(mpb::launch_paged_attention(ap, st), "attention launch");
+            if (c->profile) record_attention_event(c);
+            cuda_check(mpb::launch_gemm_simt({c->attn, H, c->wo + L * H * H, H, c->x, H, T, H, H, mpb::Epilogue::AddTo},
+                                             st),
+                       "o gemm");
+            cuda_check(mpb::launch_rmsnorm(c->x, nullptr, c->post_norm + L * H, m.rms_epsilon, c->xn, T, H, st),
+                       "rmsnorm launch");
+            cuda_check(mpb::launch_gemm_simt({c->xn, H, c->wgate + L * size_t(I) * H, H, c->h, I, T, I, H,
+                                              mpb::Epilogue::Store},
+                                             st),
+                       "gate gemm");
+            cuda_check(mpb::launch_gemm_simt({c->xn, H, c->wup + L * size_t(I) * H, H, c->h, I, T, I, H,
+                                              mpb::Epilogue::SiluMul},
+                                             st),
+                       "up gemm");
+            cuda_check(mpb::launch_gemm_simt({c->h, I, c->wdown + L * size_t(H) * I, I, c->x, H, T, H, I,
+                                              mpb::Epilogue::AddTo},
+                                             st),
+                       "down gemm");
+        }
+        cuda_check(mpb::launch_rmsnorm(c->x, meta + c->off_last, c->final_norm, m.rms_epsilon, c->xl, S, H, st),
+                   "final norm launch");
+        cuda_check(mpb::launch_gemm_simt({c->xl, H, c->head, H, c->logits, m.vocabulary, S, m.vocabulary, H,
+                                          mpb::Epilogue::Store},
+                                         st),
+                   "lm head gemm");
+        cuda_check(mpb::launch_argmax(c->logits, S, m.vocabulary, c->out_tokens, c->out_finite, st), "argmax launch");
+        if (c->profile) c->prof_bytes += c->plan.bytes * m.layers;
+    });
+}
+
+int mp_forward_collect(mp_context* c, int32_t* out_tokens, int32_t* out_finite, float* out_logits,
+                       int32_t timeout_ms) {
+    int finite_all = 1;
+    int rc = guarded([&] {
+        if (!c || !c->prepared) fail(MP_ERR_INVALID, "no prepared step");
+        cuda_check(cudaSetDevice(c->device), "select device");
+        const int S = c->seqs;
+        cudaStream_t st = c->stream;
+        cuda_check(cudaMemcpyAsync(c->h_tokens, c->out_tokens, size_t(S) * 4, cudaMemcpyDeviceToHost, st),
+                   "download tokens");
+        cuda_check(cudaMemcpyAsync(c->h_finite, c->out_finite, size_t(S) * 4, cudaMemcpyDeviceToHost, st),
+                   "download finite flags");
+        cuda_check(cudaMemcpyAsync(c->h_error, c->error, sizeof(unsigned), cudaMemcpyDeviceToHost, st),
+                   "download error word");
+        if (out_logits)
+            cuda_check(cudaMemcpyAsync(out_logits, c->logits, size_t(S) * c->model.vocabulary * 4,
+                                       cudaMemcpyDeviceToHost, st),
+                       "download logits");
+        cuda_check(cudaEventRecord(c->done, st), "record completion");
+        wait_event(c->done, timeout_ms);
+        if (c->profile) harvest_profile(c);
+        if (out_tokens) std::memcpy(out_tokens, c->h_tokens, size_t(S) * 4);
+        if (out_finite) std::memcpy(out_finite, c->h_finite, size_t(S) * 4);
+        for (int i = 0; i < S; ++i) finite_all &= c->h_finite[i] != 0;
+        c->prepared = false;
+        const unsigned err = *c->h_error;
+        if (err & mpb::kErrTimeout) fail(MP_ERR_TIMEOUT, "an in-kernel copy wait expired");
+        if (err & mpb::kErrBounds) fail(MP_ERR_BOUNDS, "device bounds check failed (page id, token or region)");
+    });
+    if (rc == MP_OK && !finite_all) {
+        g_error = "nonfinite logits";
+        rc = MP_ERR_NONFINITE;
+    }
+    return rc;
+}
+
+int mp_forward(mp_context* c, const mp_sequence_desc* seqs, int32_t count, const int32_t* tokens, int32_t* out_tokens,
+               int32_t* out_finite, float* out_logits, int32_t timeout_ms) {
+    int rc = mp_forward_prepare(c, seqs, count, tokens);
+    if (rc != MP_OK) return rc;
+    rc = mp_forward_launch(c);
+    if (rc != MP_OK) {
+        if (c && c->stream) cudaStreamSynchronize(c->stream);
+        if (c) c->prepared = false;
+        return rc;
+    }
+    return mp_forward_collect(c, out_tokens, out_finite, out_logits, timeout_ms);
+}
+
+int mp_sync(mp_context* c, int32_t timeout_ms) {
+    return guarded([&] {
+        if (!c) fail(MP_ERR_INVALID, "null context");
+        cuda_check(cudaSetDevice(c->device), "select device");
+        cuda_check(cudaEventRecord(c->done, c->stream), "record completion");
+        wait_event(c->done, timeout_ms);
+        cuda_check(cudaMemcpy(c->h_error, c->error, sizeof(unsigned), cudaMemcpyDeviceToHost), "read error word");
+        const unsigned err = *c->h_error;
+        if (err) {
+            cuda_check(cudaMemsetAsync(c->error, 0, sizeof(unsigned), c->stream), "reset error word");
+            if (err & mpb::kErrTimeout) fail(MP_ERR_TIMEOUT, "an in-kernel copy wait expired");
+            fail(MP_ERR_BOUNDS, "device bounds check failed (page id, token or region)");
+        }
+    });
+}
+
+int mp_kv_pools(mp_context* c, float** keys, float** values, uint64_t* elements) {
+    if (!c) return MP_ERR_INVALID;
+    if (keys) *keys = c->keys;
+    if (values) *values = c->values;
+    if (elements) *elements = c->pool_elements;
+    return MP_OK;
+}
+
+static int kv_copy(mp_context* c, int32_t pool, uint64_t offset, uint64_t count, void* host, bool to_device) {
+    return guarded([&] {
+        if (!c || !host || (pool != 0 && pool != 1)) fail(MP_ERR_INVALID, "invalid argument");
+        if (offset > c->pool_elements || count > c->pool_elements - offset) fail(MP_ERR_INVALID, "range outside the pool");
+        cuda_check(cudaSetDevice(c->device), "select device");
+        cuda_check(cudaStreamSynchronize(c->stream), "pool copy ordering");
+        float* base = (pool == 0 ? c->keys : c->values) + offset;
+        cuda_check(to_device ? cudaMemcpy(base, host, count * 4, cudaMemcpyHostToDevice)
+                             : cudaMemcpy(host, base, count * 4, cudaMemcpyDeviceToHost),
+                   "pool copy");
+    });
+}
+
+int mp_kv_read(mp_context* c, int32_t pool, uint64_t offset, uint64_t count, float* host) {
+    return kv_copy(c, pool, offset, count, host, false);
+}
+
+int mp_kv_write(mp_context* c, int32_t pool, uint64_t offset, uint64_t count, const float* host) {
+    return kv_copy(c, pool, offset, count, const_cast<float*>(host), true);
+}
+
+void* mp_stream(mp_context* c) { return c ? static_cast<void*>(c->stream) : nullptr; }
+
+int mp_timer_mark(mp_context* c) {
+    return guarded([&] {
+        if (!c) fail(MP_ERR_INVALID, "null context");
+        cuda_check(cudaEventRecord(c->mark[c->mark_count & 1], c->stream), "timer mark");
+        ++c->mark_count;
+    });
+}
+
+int mp_timer_elapsed(mp_context* c, float* ms) {
+    return guarded([&] {
+        if (!c || !ms || c->mark_count < 2) fail(MP_ERR_INVALID, "need two timer marks");
+        cudaEvent_t a = c->mark[(c->mark_count - 2) & 1], b = c->mark[(c->mark_count - 1) & 1];
+        cuda_check(cudaEventSynchronize(b), "timer wait");
+        cuda_check(cudaEventElapsedTime(ms, a, b), "timer elapsed");
+    });
+}
+
+int mp_profile_enable(mp_context* c, int32_t enabled) {
+    if (!c) return MP_ERR_INVALID;
+    c->profile = enabled != 0;
+    return MP_OK;
+}
+
+int mp_profile_read(mp_context* c, float* attention_ms, int32_t* launches, double* bytes) {
+    if (!c) return MP_ERR_INVALID;
+    if (attention_ms) *attention_ms = c->prof_ms;
+    if (launches) *launches = c->prof_launches;
+    if (bytes) *bytes = c->prof_bytes;
+    c->prof_ms = 0.f;
+    c->prof_launches = 0;
+    c->prof_bytes = 0;
+    return MP_OK;
+}
+
+}  // extern "C"

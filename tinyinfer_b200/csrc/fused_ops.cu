@@ -1,0 +1,252 @@
+// Bandwidth-bound fused ops of the forward (sm_100a).
+//
+//  embed_rmsnorm : reference embedding_kernel + first rms_kernel
+//                  (miniprefix/src/backend/cuda/llama_runner.cu:15-22, launches :146,148)
+//  rmsnorm       : rms_kernel (:17-22); final norm only on each sequence's last row (:166)
+//  rope_append   : rope_kernel x2 + append_kernel (:23-32, launches :151-155)
+//  argmax        : greedy sampling of Engine::step (miniprefix/src/engine/engine.cpp:99)
+//                  + the nonfinite check (:94-95; runner :173), on device
+//  cow_copy      : the 2 cudaMemcpy2DAsync of a COW tail region (:130-137)
+//  table_patch   : block-table delta upload (:139-143) applied as (index, value) pairs
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mpb {
+namespace {
+
+// One warp per row. Sum of squares by per-lane partials and a butterfly; the
+// normalisation order matches the CPU runner: (x * scale) * w
+// (miniprefix/src/backend/cpu/llama_runner.cpp:10-16).
+__device__ __forceinline__ void rms_row(const float* x, const float* w, float eps, float* out, int hidden, int lane) {
+    float sum = 0.f;
+    for (int d = lane * 4; d < hidden; d += 128) {
+        const float4 v = *reinterpret_cast<const float4*>(x + d);
+        sum = fmaf(v.x, v.x, sum);
+        sum = fmaf(v.y, v.y, sum);
+        sum = fmaf(v.z, v.z, sum);
+        sum = fmaf(v.w, v.w, sum);
+    }
+    sum = warp_sum(sum);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, float(hidden)), eps)));
+    for (int d = lane * 4; d < hidden; d += 128) {
+        const float4 v = *reinterpret_cast<const float4*>(x + d);
+        const float4 g = *reinterpret_cast<const float4*>(w + d);
+        float4 r;
+        r.x = __fmul_rn(__fmul_rn(v.x, scale), g.x);
+        r.y = __fmul_rn(__fmul_rn(v.y, scale), g.y);
+        r.z = __fmul_rn(__fmul_rn(v.z, scale), g.z);
+        r.w = __fmul_rn(__fmul_rn(v.w, scale), g.w);
+        *reinterpret_cast<float4*>(out + d) = r;
+    }
+}
+
+__global__ void embed_rmsnorm_kernel(const int32_t* tokens, const float* embed, int vocabulary, const float* w,
+                                     float eps, float* x, float* normed, int rows, int hidden, unsigned* error) {
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    int tok = tokens[row];
+    if (tok < 0 || tok >= vocabulary) {
+        if (lane == 0) raise_error(error, kErrBounds);
+        tok = 0;
+    }
+    const float* src = embed + size_t(tok) * hidden;
+    float* xr = x + size_t(row) * hidden;
+    for (int d = lane * 4; d < hidden; d += 128)
+        *reinterpret_cast<float4*>(xr + d) = *reinterpret_cast<const float4*>(src + d);
+    __syncwarp();
+    rms_row(xr, w, eps, normed + size_t(row) * hidden, hidden, lane);
+}
+
+__global__ void rmsnorm_kernel(const float* x, const int32_t* rows, const float* w, float eps, float* out, int count,
+                               int hidden) {
+    const int i = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
+    if (i >= count) return;
+    const int r = rows ? rows[i] : i;
+    rms_row(x + size_t(r) * hidden, w, eps, out + size_t(i) * hidden, hidden, lane);
+}
+
+// One CTA of 384 threads per row: threads 0..287 rotate the 9 q heads' 32 pairs,
+// 288..383 the 3 k heads'; threads 0..191 also move the v row. The rotation is
+// a' = a*cos - b*sin, b' = b*cos + a*sin with separately rounded products, as
+// the CPU runner (llama_runner.cpp:17-22) computes it; cos/sin come from tables
+// the host filled with the same libm calls as the CPU runner.
+__global__ void __launch_bounds__(384) rope_append_kernel(const RopeAppendArgs a) {
+    const int row = blockIdx.x, t = threadIdx.x;
+    const int pos = a.row_pos[row];
+    const float* src = a.qkv + size_t(row) * a.qkv_stride;
+    __shared__ size_t dst_off;
+    if (t == 0) {
+        const int page = pos / a.block_tokens;
+        int block = -1;
+        if (page < a.table_stride && pos < a.max_position)
+            block = a.tables[size_t(a.row_slot[row]) * a.table_stride + page];
+        if (block < 0 || block >= a.max_blocks) {
+            raise_error(a.error, kErrBounds);
+            dst_off = ~size_t(0);
+        } else {
+            dst_off = ((size_t(block) * a.layers + a.layer) * a.block_tokens + pos % a.block_tokens) * kKvWidth;
+        }
+    }
+    __syncthreads();
+    const size_t off = dst_off;
+    const int p = min(pos, a.max_position - 1);
+    if (t < 288 + 96) {
+        const bool is_q = t < 288;
+        const int idx = is_q ? t : t - 288;
+        const int head = idx / 32, d = idx % 32;
+        const float cs = a.rope_cos[size_t(p) * 32 + d], sn = a.rope_sin[size_t(p) * 32 + d];
+        const float* base = src + (is_q ? 0 : kQWidth) + head * kHeadDim;
+        const float x0 = base[d], x1 = base[d + 32];
+        const float r0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+        const float r1 = __fadd_rn(__fmul_rn(x1, cs), __fmul_rn(x0, sn));
+        if (is_q) {
+            float* q = a.q_out + size_t(row) * a.q_stride + head * kHeadDim;
+            q[d] = r0;
+            q[d + 32] = r1;
+        } else if (off != ~size_t(0)) {
+            float* k = a.keys + off + head * kHeadDim;
+            k[d] = r0;
+            k[d + 32] = r1;
+        }
+    }
+    if (t < kKvWidth && off != ~size_t(0)) a.values[off + t] = src[kQWidth + kKvWidth + t];
+}
+
+// One CTA of 1024 threads per logits row. First maximum wins (std::max_element):
+// candidates compare by value, then by lower index.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int vocabulary, int32_t* tokens,
+                                                      int32_t* finite) {
+    const int row = blockIdx.x, t = threadIdx.x;
+    const float* x = logits + size_t(row) * vocabulary;
+    float best = -INFINITY;
+    int index = vocabulary;
+    bool ok = true;
+    for (int i = t; i < vocabulary; i += 1024) {
+        const float v = x[i];
+        ok &= isfinite(v);
+        if (v > best || (index == vocabulary && !(v < best))) {
+            best = v;
+            index = i;
+        }
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    __shared__ int sok[32];
+    const int lane = t & 31, warp = t >> 5;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, index, o);
+        if (ov > best || (ov == best && oi < index)) {
+            best = ov;
+            index = oi;
+        }
+    }
+    const int all_ok = __all_sync(0xffffffffu, ok);
+    if (lane == 0) {
+        sv[warp] = best;
+        si[warp] = index;
+        sok[warp] = all_ok;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        best = sv[lane];
+        index = si[lane];
+        ok = sok[lane];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, index, o);
+            if (ov > best || (ov == best && oi < index)) {
+                best = ov;
+                index = oi;
+            }
+        }
+        const int fin = __all_sync(0xffffffffu, ok);
+        if (lane == 0) {
+            tokens[row] = index < vocabulary ? index : 0;
+            finite[row] = fin;
+        }
+    }
+}
+
+// grid (count, max_rows): one CTA per (region, layer row), float4 copies of
+// `width` floats in both pools. Offsets are validated against the pool size.
+__global__ void cow_copy_kernel(const CowRegion* regions, float* keys, float* values, uint64_t pool_elements,
+                                unsigned* error) {
+    const CowRegion r = regions[blockIdx.x];
+    const uint64_t row = blockIdx.y;
+    if (row >= r.rows) return;
+    const uint64_t dst = r.destination + row * r.pitch, src = r.source + row * r.pitch;
+    if (dst + r.width > pool_elements || src + r.width > pool_elements || (r.width | dst | src) & 3) {
+        if (threadIdx.x == 0) raise_error(error, kErrBounds);
+        return;
+    }
+    const float4* ks = reinterpret_cast<const float4*>(keys + src);
+    const float4* vs = reinterpret_cast<const float4*>(values + src);
+    float4* kd = reinterpret_cast<float4*>(keys + dst);
+    float4* vd = reinterpret_cast<float4*>(values + dst);
+    for (uint64_t i = threadIdx.x; i < r.width / 4; i += blockDim.x) {
+        kd[i] = ks[i];
+        vd[i] = vs[i];
+    }
+}
+
+__global__ void table_patch_kernel(const int32_t* pairs, int count, int32_t* tables, int64_t elements,
+                                   unsigned* error) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    const int64_t index = pairs[2 * i];
+    if (index < 0 || index >= elements) {
+        raise_error(error, kErrBounds);
+        return;
+    }
+    tables[index] = pairs[2 * i + 1];
+}
+
+}  // namespace
+
+cudaError_t launch_embed_rmsnorm(const int32_t* tokens, const float* embed, int vocabulary, const float* norm_w,
+                                 float eps, float* x, float* normed, int rows, int hidden, unsigned* error,
+                                 cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    embed_rmsnorm_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(tokens, embed, vocabulary, norm_w, eps, x, normed, rows,
+                                                            hidden, error);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, float* out, int count,
+                           int hidden, cudaStream_t stream) {
+    if (count <= 0) return cudaSuccess;
+    rmsnorm_kernel<<<(count + 7) / 8, 256, 0, stream>>>(x, rows, norm_w, eps, out, count, hidden);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rope_append(const RopeAppendArgs& a, cudaStream_t stream) {
+    if (a.rows <= 0) return cudaSuccess;
+    rope_append_kernel<<<a.rows, 384, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float* logits, int rows, int vocabulary, int32_t* tokens, int32_t* finite,
+                          cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    argmax_kernel<<<rows, 1024, 0, stream>>>(logits, vocabulary, tokens, finite);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_cow_copy(const CowRegion* regions, int count, int max_rows, float* keys, float* values,
+                            uint64_t pool_elements, unsigned* error, cudaStream_t stream) {
+    if (count <= 0 || max_rows <= 0) return cudaSuccess;
+    cow_copy_kernel<<<dim3(count, max_rows), 256, 0, stream>>>(regions, keys, values, pool_elements, error);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_table_patch(const int32_t* pairs, int count, int32_t* tables, int64_t table_elements,
+                               unsigned* error, cudaStream_t stream) {
+    if (count <= 0) return cudaSuccess;
+    table_patch_kernel<<<(count + 255) / 256, 256, 0, stream>>>(pairs, count, tables, table_elements, error);
+    return cudaGetLastError();
+}
+
+}  // namespace mpb

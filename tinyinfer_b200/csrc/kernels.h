@@ -1,0 +1,124 @@
+// Host-visible launch interfaces of the sm_100a kernels (internal to the library;
+// the public boundary is include/miniprefix_b200.h).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace mpb {
+
+// Attention geometry the kernels are specialised for (SmolLM2-135M shape):
+// 9 query heads share 3 KV heads of dimension 64 (GQA group 3).
+constexpr int kHeads = 9;
+constexpr int kKvHeads = 3;
+constexpr int kHeadDim = 64;
+constexpr int kGroup = kHeads / kKvHeads;
+constexpr int kKvWidth = kKvHeads * kHeadDim;  // 192 floats per token per pool
+constexpr int kQWidth = kHeads * kHeadDim;     // 576
+
+// Device error word bits (read back by the host after each step).
+enum : unsigned {
+    kErrBounds = 1u,    // a block-table entry or index fell outside its buffer
+    kErrTimeout = 2u,   // a bounded wait on a copy gave up
+};
+
+
+// One CTA of paged attention: query row `row`, context pages [page_begin, page_end).
+// Slices of a row are contiguous in the work list, in page order.
+struct AttnWork {
+    int32_t row;
+    int32_t page_begin;
+    int32_t page_end;
+    int32_t split;
+};
+
+struct AttnParams {
+    const float* q;  // roped queries, [rows][q_stride], 9 heads x 64 per row
+    int q_stride;
+    const float* keys;    // K pool [block][layers][block_tokens][192]
+    const float* values;  // V pool, same layout
+    int layers, layer, block_tokens, max_blocks;
+    const int32_t* tables;  // [slots][table_stride] physical page ids
+    int table_stride;
+    const int32_t* row_slot;    // table slot of each query row
+    const int32_t* row_len;     // causal context length of each query row
+    const int32_t* row_splits;  // slices of each row
+    const int32_t* row_work0;   // first work index of each row
+    const AttnWork* work;
+    int work_count;
+    float* partial;      // [work_count][9][66] slice results (rows with >1 slice)
+    unsigned* counters;  // [rows] zero between launches
+    float* out;          // [rows][out_stride]
+    int out_stride;
+    unsigned* error;
+};
+
+cudaError_t configure_attention();
+// Message returned by mp_last_error() on this thread.
+void set_last_error(const char* message);
+cudaError_t launch_paged_attention(const AttnParams& p, cudaStream_t stream);
+
+// ---------------------------------------------------------------- GEMM
+// C[M][N] (op) A[M][K] * B[N][K]^T, B stored K-contiguous ("nn.Linear" layout).
+enum class Epilogue : int {
+    Store = 0,    // C = acc
+    AddTo = 1,    // C = C + acc        (residual add)
+    SiluMul = 2,  // C = silu(C) * acc  (C holds the gate projection)
+};
+
+struct GemmArgs {
+    const float* a;
+    int lda;
+    const float* b;
+    int ldb;
+    float* c;
+    int ldc;
+    int m, n, k;
+    Epilogue epilogue;
+};
+
+cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t stream);
+
+// ---------------------------------------------------------------- fused small ops
+// x[r][:] = embed[tokens[r]][:]; out[r][:] = rmsnorm(x[r]) * w (both written).
+cudaError_t launch_embed_rmsnorm(const int32_t* tokens, const float* embed, int vocabulary, const float* norm_w,
+                                 float eps, float* x, float* normed, int rows, int hidden, unsigned* error,
+                                 cudaStream_t stream);
+// out[i][:] = rmsnorm(x[rows ? rows[i] : i]) * w for i < count.
+cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, float* out,
+                           int count, int hidden, cudaStream_t stream);
+// Split-half RoPE of q and k from qkv[r][960] with host-computed cos/sin tables
+// [position][32]; writes roped q to q_out[r][576] and k, v rows into the pools.
+struct RopeAppendArgs {
+    const float* qkv;
+    int qkv_stride;
+    const int32_t* row_pos;
+    const int32_t* row_slot;
+    const float* rope_cos;
+    const float* rope_sin;
+    int max_position;
+    float* q_out;
+    int q_stride;
+    float* keys;
+    float* values;
+    const int32_t* tables;
+    int table_stride;
+    int layers, layer, block_tokens, max_blocks;
+    int rows;
+    unsigned* error;
+};
+cudaError_t launch_rope_append(const RopeAppendArgs& a, cudaStream_t stream);
+// Greedy token (first index of the maximum) and finiteness of each logits row.
+cudaError_t launch_argmax(const float* logits, int rows, int vocabulary, int32_t* tokens, int32_t* finite,
+                          cudaStream_t stream);
+// COW regions {destination, source, pitch, width, rows} in float elements, applied to both pools.
+struct CowRegion {
+    uint64_t destination, source, pitch, width, rows;
+};
+cudaError_t launch_cow_copy(const CowRegion* regions, int count, int max_rows, float* keys, float* values,
+                            uint64_t pool_elements, unsigned* error, cudaStream_t stream);
+// tables[index[i]] = value[i]
+cudaError_t launch_table_patch(const int32_t* pairs, int count, int32_t* tables, int64_t table_elements,
+                               unsigned* error, cudaStream_t stream);
+
+}  // namespace mpb

@@ -1,0 +1,157 @@
+// mp_paged_attention_decode: the paged-attention decode operator on caller
+// buffers (one query row per sequence), with an internal per-device scratch
+// (work list, per-row metadata, slice partials, arrival counters) that grows on
+// demand.
+#include <algorithm>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+#include "miniprefix_b200.h"
+
+namespace {
+
+struct Scratch {
+    int32_t* meta = nullptr;  // row arrays + work list
+    size_t meta_capacity = 0;
+    float* partial = nullptr;
+    size_t partial_capacity = 0;  // work items
+    unsigned* counters = nullptr;
+    size_t counter_capacity = 0;
+    unsigned* error = nullptr;
+};
+
+std::mutex g_scratch_mutex;
+Scratch g_scratch[64];
+
+template <class T>
+cudaError_t grow(T*& p, size_t& capacity, size_t need, cudaStream_t stream, bool zero) {
+    if (need <= capacity) return cudaSuccess;
+    cudaError_t e = cudaStreamSynchronize(stream);  // in-flight launches may still use the old buffer
+    if (e != cudaSuccess) return e;
+    if (p) cudaFree(p);
+    p = nullptr;
+    capacity = 0;
+    need = std::max(need, size_t(1024));
+    e = cudaMalloc(reinterpret_cast<void**>(&p), need * sizeof(T));
+    if (e != cudaSuccess) return e;
+    if (zero) {
+        e = cudaMemsetAsync(p, 0, need * sizeof(T), stream);
+        if (e != cudaSuccess) return e;
+    }
+    capacity = need;
+    return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" int mp_paged_attention_decode(const float* q, const float* keys, const float* values, int32_t layers,
+                                         int32_t layer, int32_t block_tokens, int32_t max_blocks,
+                                         const int32_t* tables, int32_t table_stride, const int32_t* lengths,
+                                         int32_t count, float* out, int32_t pages_per_split, void* stream_ptr) {
+    if (!q || !keys || !values || !tables || !lengths || !out || count < 1 || layers < 1 || layer < 0 ||
+        layer >= layers || block_tokens < 1 || max_blocks < 1 || table_stride < 1) {
+        mpb::set_last_error("invalid argument");
+        return MP_ERR_INVALID;
+    }
+    for (int i = 0; i < count; ++i)
+        if (lengths[i] < 1 || int64_t(lengths[i]) > int64_t(table_stride) * block_tokens) {
+            mpb::set_last_error("sequence length outside its block table");
+            return MP_ERR_INVALID;
+        }
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return MP_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    Scratch& s = g_scratch[device];
+    // Work list: slices of `pps` pages (auto: ~8 CTAs per SM, >= 64 tokens).
+    int pps = pages_per_split;
+    if (pps <= 0) {
+        long long total = 0;
+        for (int i = 0; i < count; ++i) total += lengths[i];
+        long long slice = std::max<long long>(64, (total + 148 * 8 - 1) / (148 * 8));
+        slice = (slice + 31) / 32 * 32;
+        pps = int(std::max<long long>(1, slice / block_tokens));
+    }
+    std::vector<int32_t> host(size_t(count) * 4);
+    std::vector<mpb::AttnWork> work;
+    for (int r = 0; r < count; ++r) {
+        const int pages = (lengths[r] + block_tokens - 1) / block_tokens;
+        const int n = std::max(1, (pages + pps - 1) / pps);
+        host[r] = r;                              // slot
+        host[count + r] = lengths[r];             // length
+        host[2 * count + r] = n;                  // splits
+        host[3 * count + r] = int(work.size());   // first work item
+        for (int k = 0; k < n; ++k) work.push_back({r, k * pps, std::min(pages, (k + 1) * pps), k});
+    }
+    const size_t words = host.size() + 4 * work.size();
+    cudaError_t e = grow(s.meta, s.meta_capacity, words, stream, false);
+    if (e == cudaSuccess) e = grow(s.partial, s.partial_capacity, work.size() * mpb::kHeads * (mpb::kHeadDim + 2),
+                                   stream, false);
+    if (e == cudaSuccess) e = grow(s.counters, s.counter_capacity, size_t(count), stream, true);
+    if (e == cudaSuccess && !s.error) {
+        e = cudaMalloc(reinterpret_cast<void**>(&s.error), sizeof(unsigned));
+        if (e == cudaSuccess) e = cudaMemsetAsync(s.error, 0, sizeof(unsigned), stream);
+    }
+    if (e == cudaSuccess) e = mpb::configure_attention();
+    if (e != cudaSuccess) {
+        mpb::set_last_error(cudaGetErrorString(e));
+        return e == cudaErrorMemoryAllocation ? MP_ERR_NOMEM : MP_ERR_CUDA;
+    }
+    host.resize(words);
+    std::copy(reinterpret_cast<const int32_t*>(work.data()), reinterpret_cast<const int32_t*>(work.data()) + 4 * work.size(),
+              host.begin() + 4 * count);
+    // Pageable source: the copy is staged before cudaMemcpyAsync returns.
+    e = cudaMemcpyAsync(s.meta, host.data(), words * 4, cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) {
+        mpb::set_last_error(cudaGetErrorString(e));
+        return MP_ERR_CUDA;
+    }
+    mpb::AttnParams p{};
+    p.q = q;
+    p.q_stride = mpb::kQWidth;
+    p.keys = keys;
+    p.values = values;
+    p.layers = layers;
+    p.layer = layer;
+    p.block_tokens = block_tokens;
+    p.max_blocks = max_blocks;
+    p.tables = tables;
+    p.table_stride = table_stride;
+    p.row_slot = s.meta;
+    p.row_len = s.meta + count;
+    p.row_splits = s.meta + 2 * count;
+    p.row_work0 = s.meta + 3 * count;
+    p.work = reinterpret_cast<const mpb::AttnWork*>(s.meta + 4 * count);
+    p.work_count = int(work.size());
+    p.partial = s.partial;
+    p.counters = s.counters;
+    p.out = out;
+    p.out_stride = mpb::kQWidth;
+    p.error = s.error;
+    e = mpb::launch_paged_attention(p, stream);
+    if (e != cudaSuccess) {
+        mpb::set_last_error(cudaGetErrorString(e));
+        return MP_ERR_CUDA;
+    }
+    return MP_OK;
+}
+
+// Reads and clears the operator's device error word for the current device
+// (synchronises `stream`). Returns MP_OK, MP_ERR_BOUNDS or MP_ERR_TIMEOUT.
+extern "C" int mp_paged_attention_status(void* stream_ptr) {
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return MP_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    Scratch& s = g_scratch[device];
+    if (!s.error) return MP_OK;
+    unsigned err = 0;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    if (cudaMemcpyAsync(&err, s.error, sizeof(unsigned), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+        cudaStreamSynchronize(stream) != cudaSuccess)
+        return MP_ERR_CUDA;
+    if (!err) return MP_OK;
+    cudaMemsetAsync(s.error, 0, sizeof(unsigned), stream);
+    return (err & mpb::kErrTimeout) ? MP_ERR_TIMEOUT : MP_ERR_BOUNDS;
+}
