@@ -60,6 +60,11 @@ typedef struct {
     int32_t slot, start, count;
 } mp_sequence_desc;
 
+/* One block-table entry: tables[slot][index] = block. */
+typedef struct {
+    int32_t slot, index, block;
+} mp_table_entry;
+
 /* KVManager::TailCopyRegion (miniprefix/include/miniprefix/kv_manager.h:38): float
  * element offsets into ONE pool; the copy is applied to both the K and V pools. */
 typedef struct {
@@ -89,8 +94,10 @@ int mp_table_write(mp_context* ctx, int32_t slot, int32_t first, const int32_t* 
  * every region copies rows x width floats at pitch in both pools. */
 int mp_cow_copy(mp_context* ctx, const mp_tail_copy_region* regions, int32_t count);
 
-/* Replaces the append body (llama_runner.cu:144-170) for a BATCH of sequences:
- * uploads tokens and descriptors, runs the 30-layer forward, and downloads per
+/* Replaces the append body (llama_runner.cu:128-170) for a BATCH of sequences:
+ * uploads tokens, descriptors, block-table entries and COW regions in one copy,
+ * applies the table entries, performs the COW copies (all layers, both pools,
+ * before any layer runs), runs the 30-layer forward, and downloads per
  * sequence the greedy token (first index of the maximum, engine.cpp:99), a
  * finiteness flag (:94-95) and, when out_logits is not NULL, the full last-row
  * logits (sequences x vocabulary floats, the reference's append() result).
@@ -98,12 +105,16 @@ int mp_cow_copy(mp_context* ctx, const mp_tail_copy_region* regions, int32_t cou
  * Returns MP_ERR_NONFINITE when any sequence had a nonfinite logit (outputs are
  * still written) and MP_ERR_BOUNDS when a device bounds check tripped. */
 int mp_forward(mp_context* ctx, const mp_sequence_desc* sequences, int32_t count, const int32_t* tokens,
-               int32_t* out_tokens, int32_t* out_finite, float* out_logits, int32_t timeout_ms);
+               const mp_table_entry* entries, int32_t entry_count, const mp_tail_copy_region* regions,
+               int32_t region_count, int32_t* out_tokens, int32_t* out_finite, float* out_logits,
+               int32_t timeout_ms);
 
 /* The same step split in three, for callers that keep inputs resident and time
  * the device work alone: prepare uploads, launch only enqueues kernels that read
  * device memory, collect downloads and waits. */
-int mp_forward_prepare(mp_context* ctx, const mp_sequence_desc* sequences, int32_t count, const int32_t* tokens);
+int mp_forward_prepare(mp_context* ctx, const mp_sequence_desc* sequences, int32_t count, const int32_t* tokens,
+                       const mp_table_entry* entries, int32_t entry_count, const mp_tail_copy_region* regions,
+                       int32_t region_count);
 int mp_forward_launch(mp_context* ctx);
 int mp_forward_collect(mp_context* ctx, int32_t* out_tokens, int32_t* out_finite, float* out_logits,
                        int32_t timeout_ms);
@@ -129,6 +140,10 @@ int mp_timer_elapsed(mp_context* ctx, float* milliseconds);
  * since the last read (and resets them). */
 int mp_profile_enable(mp_context* ctx, int32_t enabled);
 int mp_profile_read(mp_context* ctx, float* attention_ms, int32_t* attention_launches, double* attention_bytes);
+/* Device time of the COW copies of the last collected forward that had any
+ * (milliseconds; 0 when it had none). Recorded only while cost timing is on. */
+int mp_cow_timing(mp_context* ctx, int32_t enabled);
+int mp_cow_elapsed(mp_context* ctx, float* milliseconds);
 
 /* The paged-attention decode OPERATOR alone (one query row per sequence), on
  * caller device buffers: q [count][9*64] roped queries, pools in the reference

@@ -382,9 +382,8 @@ class RefEngine:
         return bool(self.ref.check(self.ref.lib.ref_engine_step(self.h)))
 
     def poll_events(self):
-        need = self.ref.lib.ref_engine_poll(self.h, None, 0)
         # ref_engine_poll drains on every call; call once with room for all text.
-        return _parse_events(need, lambda buf, cap: self.ref.lib.ref_engine_poll(self.h, buf, cap))
+        return _parse_events(None, lambda buf, cap: self.ref.lib.ref_engine_poll(self.h, buf, cap))
 
     def cancel(self, id):
         self.ref.check(self.ref.lib.ref_engine_cancel(self.h, _ids(id)))
@@ -446,3 +445,69 @@ def _parse_events(_need, fetch):
         rid, tok, reason, err = line.split("\t", 3)
         events.append((rid, None if int(tok) < 0 else int(tok), None if int(reason) < 0 else int(reason), err))
     return events
+
+
+CACHE_STATS_FIELDS = ("size", "index_nodes", "key_token_bytes", "hits", "misses", "reused_tokens", "evictions",
+                      "cache_only_blocks", "live_blocks", "peak_blocks", "free_blocks")
+
+
+class RefCache:
+    """The reference KvBlockPool + ExactPrefixCache over named sequences."""
+
+    def __init__(self, ref: RefLib, block_tokens, max_blocks, prefix_blocks, layers=1, width=1):
+        self.ref = ref
+        ref.lib.ref_cache_new.restype = C.c_void_p
+        ref.lib.ref_cache_reuse.restype = C.c_long
+        h = ref.lib.ref_cache_new(block_tokens, max_blocks, prefix_blocks, layers, width)
+        if not h:
+            raise RefError(-1, ref.error())
+        self.h = C.c_void_p(h)
+        self.max_blocks = max_blocks
+
+    def close(self):
+        if self.h:
+            self.ref.lib.ref_cache_free(self.h)
+            self.h = None
+
+    def append(self, seq, tokens):
+        a, p, n = _toks(tokens)
+        self.ref.check(self.ref.lib.ref_cache_append(self.h, _ids(seq), p, n))
+
+    def publish(self, seq):
+        self.ref.check(self.ref.lib.ref_cache_publish(self.h, _ids(seq)))
+
+    def reuse(self, seq, prompt):
+        a, p, n = _toks(prompt)
+        return self.ref.check(self.ref.lib.ref_cache_reuse(self.h, _ids(seq), p, n))
+
+    def release(self, seq):
+        self.ref.check(self.ref.lib.ref_cache_release(self.h, _ids(seq)))
+
+    def evict_one(self):
+        return bool(self.ref.check(self.ref.lib.ref_cache_evict_one(self.h)))
+
+    def clear(self):
+        self.ref.lib.ref_cache_clear(self.h)
+
+    def stats(self):
+        out = (C.c_uint64 * 11)()
+        self.ref.lib.ref_cache_stats(self.h, out)
+        return dict(zip(CACHE_STATS_FIELDS, list(out)))
+
+    def references(self):
+        out = (C.c_uint64 * self.max_blocks)()
+        self.ref.check(self.ref.lib.ref_cache_references(self.h, out, self.max_blocks))
+        return list(out)
+
+    def define(self, seq, used, tokens, blocks):
+        """Set a sequence verbatim (no page accounting) to build malformed inputs."""
+        a, p, n = _toks(tokens)
+        b, q, m = _toks(blocks)
+        self.ref.check(self.ref.lib.ref_cache_define(self.h, _ids(seq), int(used), p, n, q, m))
+
+    def sequence(self, seq):
+        used = C.c_int()
+        blocks = (C.c_int * 65536)()
+        toks = (C.c_int * 65536)()
+        n = self.ref.check(self.ref.lib.ref_cache_sequence(self.h, _ids(seq), C.byref(used), blocks, 65536, toks, 65536))
+        return used.value, list(blocks[:n]), list(toks[:used.value])

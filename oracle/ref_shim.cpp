@@ -17,6 +17,7 @@
 #include "miniprefix/engine.h"
 #include "miniprefix/kv_manager.h"
 #include "miniprefix/model.h"
+#include "miniprefix/prefix_cache.h"
 #include <cstring>
 #include <map>
 #include <set>
@@ -104,6 +105,17 @@ public:
         return r;
     }
     CostStats cost_stats() const override { return kv_.cost_stats(); }
+};
+
+struct CacheHandle {
+    KvBlockPool pool;
+    ExactPrefixCache cache;
+    std::map<std::string, PagedSequence> sequences;
+    CacheHandle(KvCacheConfig c, int layers, int width) : pool(c, layers, width), cache(pool) {}
+    ~CacheHandle() {
+        for (auto& s : sequences) pool.release(s.second);
+        cache.clear();
+    }
 };
 
 struct RunnerHandle {
@@ -264,6 +276,66 @@ int ref_runner_set_cost_timing(void* handle, int enabled) { RUNNER->set_cost_tim
 int ref_runner_context_limit(void* handle) { return RUNNER->context_limit(); }
 #undef RUNNER
 
+// ---------------------------------------------------------------- pool + prefix cache
+void* ref_cache_new(int block_tokens, int max_blocks, int prefix_blocks, int layers, int width) {
+    CacheHandle* h = nullptr;
+    if (guarded([&] {
+            h = new CacheHandle(KvCacheConfig{block_tokens, max_blocks, prefix_blocks}, layers, width);
+            return 0;
+        }) < 0)
+        return nullptr;
+    return h;
+}
+void ref_cache_free(void* h) { delete static_cast<CacheHandle*>(h); }
+#define CH (static_cast<CacheHandle*>(h))
+int ref_cache_append(void* h, const char* seq, const int* tokens, int count) {
+    return guarded([&] {
+        auto& s = CH->sequences[seq];
+        CH->pool.reserve(s, s.used + count);
+        s.tokens.insert(s.tokens.end(), tokens, tokens + count);
+        s.used += count;
+        return 0;
+    });
+}
+int ref_cache_publish(void* h, const char* seq) { return guarded([&] { CH->cache.publish(CH->sequences[seq]); return 0; }); }
+long ref_cache_reuse(void* h, const char* seq, const int* prompt, int count) {
+    long r = 0;
+    const int rc = guarded([&] { r = CH->cache.reuse(CH->sequences[seq], tokens_of(prompt, count)); return 0; });
+    return rc < 0 ? rc : r;
+}
+int ref_cache_release(void* h, const char* seq) { return guarded([&] { CH->pool.release(CH->sequences[seq]); return 0; }); }
+int ref_cache_evict_one(void* h) { return guarded([&] { return CH->cache.evict_one() ? 1 : 0; }); }
+int ref_cache_clear(void* h) { CH->cache.clear(); return 0; }
+int ref_cache_stats(void* h, std::uint64_t* out) {
+    const std::uint64_t v[11] = {CH->cache.size(), CH->cache.index_nodes(), CH->cache.key_token_bytes(),
+                                 CH->cache.hits(), CH->cache.misses(), CH->cache.reused_tokens(),
+                                 CH->cache.evictions(), CH->cache.cache_only_blocks(), CH->pool.live_blocks(),
+                                 CH->pool.peak_blocks(), CH->pool.free_blocks()};
+    std::memcpy(out, v, sizeof(v));
+    return 0;
+}
+int ref_cache_references(void* h, std::uint64_t* out, int count) {
+    return guarded([&] { for (int i = 0; i < count; ++i) out[i] = CH->pool.references(i); return 0; });
+}
+int ref_cache_define(void* h, const char* seq, int used, const int* tokens, int token_count, const int* blocks,
+                     int block_count) {
+    return guarded([&] {
+        auto& s = CH->sequences[seq];
+        s.used = used;
+        s.tokens.assign(tokens, tokens + token_count);
+        s.blocks.assign(blocks, blocks + block_count);
+        return 0;
+    });
+}
+int ref_cache_sequence(void* h, const char* seq, int* used, int* blocks, int capacity, int* tokens, int token_capacity) {
+    return guarded([&] {
+        const auto& s = CH->sequences.at(seq);
+        for (int i = 0; i < int(s.tokens.size()) && i < token_capacity; ++i) tokens[i] = s.tokens[i];
+        return sequence_out(s, used, blocks, capacity);
+    });
+}
+#undef CH
+
 // ---------------------------------------------------------------- KVManager
 void* ref_kv_new(int block_tokens, int max_blocks, int prefix_blocks, int layers, int width, int context,
                  int vocabulary) {
@@ -342,8 +414,7 @@ void* ref_engine_new(void* runner, int max_batch, int budget, int chunk, int con
     if (guarded([&] {
             h->scripted = rh->scripted;
             h->engine = std::make_unique<Engine>(std::move(rh->owned), EngineConfig{max_batch, budget, chunk, context});
-            rh->runner = nullptr;
-            rh->scripted = nullptr;
+            rh->runner = nullptr;  // owned by the engine now; script/poison stay usable
             return 0;
         }) < 0) {
         delete h;

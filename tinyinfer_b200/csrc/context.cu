@@ -63,40 +63,70 @@ T* host_alloc(size_t count, const char* what) {
     return static_cast<T*>(p);
 }
 
-// Work decomposition of paged attention: each query row's context pages are cut
-// into slices of `pages_per_split` pages. With pages_per_split == 0 the slice
-// length targets about eight CTAs per SM over the whole launch (148 SMs), never
-// below 64 tokens per slice.
+// Work decomposition of paged attention.
+//  * Decode rows (sequences appending fewer than kPrefillMinRows rows): each
+//    row's context pages are cut into slices of `pages_per_split` pages. With
+//    pages_per_split == 0 the slice length targets about eight CTAs per SM over
+//    the whole launch (148 SMs), never below 64 tokens per slice.
+//  * Prefill sequences: one work item per (64-row tile, kv head).
 struct AttnPlan {
     std::vector<int32_t> splits, work0;
     std::vector<mpb::AttnWork> work;
-    double bytes = 0;  // algorithmic K/V bytes one layer reads
+    std::vector<mpb::PrefillWork> prefill;
+    double bytes = 0;  // algorithmic bytes of one layer's attention
 };
 
-void plan_attention(const int32_t* lengths, int rows, int block_tokens, int pages_per_split, AttnPlan& plan) {
+void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, int pages_per_split, AttnPlan& plan) {
+    int rows = 0;
+    for (int i = 0; i < count; ++i) rows += seqs[i].count;
     plan.splits.assign(rows, 0);
     plan.work0.assign(rows, 0);
     plan.work.clear();
+    plan.prefill.clear();
     plan.bytes = 0;
-    long long total_tokens = 0;
-    for (int r = 0; r < rows; ++r) total_tokens += lengths[r];
+    long long decode_tokens = 0;
+    for (int i = 0; i < count; ++i)
+        if (seqs[i].count < mpb::kPrefillMinRows)
+            for (int j = 0; j < seqs[i].count; ++j) decode_tokens += seqs[i].start + j + 1;
     int pps = pages_per_split;
     if (pps <= 0) {
         const long long target = 148LL * 8;
-        long long slice_tokens = std::max<long long>(64, (total_tokens + target - 1) / target);
+        long long slice_tokens = std::max<long long>(64, (decode_tokens + target - 1) / target);
         slice_tokens = (slice_tokens + 31) / 32 * 32;
         pps = int(std::max<long long>(1, slice_tokens / block_tokens));
     }
-    for (int r = 0; r < rows; ++r) {
-        const int pages = (lengths[r] + block_tokens - 1) / block_tokens;
-        const int n = std::max(1, (pages + pps - 1) / pps);
-        plan.splits[r] = n;
-        plan.work0[r] = int(plan.work.size());
-        for (int s = 0; s < n; ++s)
-            plan.work.push_back({r, s * pps, std::min(pages, (s + 1) * pps), s});
-        // K and V rows, the query row and output row, the table entries.
-        plan.bytes += double(lengths[r]) * 2 * mpb::kKvWidth * sizeof(float) +
-                      2.0 * mpb::kQWidth * sizeof(float) + double(pages) * sizeof(int32_t);
+    const double kv_token_bytes = 2.0 * mpb::kKvWidth * sizeof(float);
+    int row = 0;
+    for (int i = 0; i < count; ++i) {
+        const auto& s = seqs[i];
+        if (s.count >= mpb::kPrefillMinRows) {
+            for (int t = 0; t * mpb::kPrefillTileRows < s.count; ++t) {
+                const int rows_in = std::min(mpb::kPrefillTileRows, s.count - t * mpb::kPrefillTileRows);
+                for (int kh = 0; kh < mpb::kKvHeads; ++kh)
+                    plan.prefill.push_back({row + t * mpb::kPrefillTileRows, rows_in,
+                                            s.start + t * mpb::kPrefillTileRows, s.slot, kh, {0, 0, 0}});
+            }
+            // The context of the whole chunk is read once per 64-row tile.
+            const int tiles = (s.count + mpb::kPrefillTileRows - 1) / mpb::kPrefillTileRows;
+            for (int t = 0; t < tiles; ++t) {
+                const int last = s.start + std::min(s.count, (t + 1) * mpb::kPrefillTileRows);
+                plan.bytes += double(last) * kv_token_bytes;
+            }
+            plan.bytes += double(s.count) * 2.0 * mpb::kQWidth * sizeof(float);
+            row += s.count;
+            continue;
+        }
+        for (int j = 0; j < s.count; ++j, ++row) {
+            const int len = s.start + j + 1;
+            const int pages = (len + block_tokens - 1) / block_tokens;
+            const int n = std::max(1, (pages + pps - 1) / pps);
+            plan.splits[row] = n;
+            plan.work0[row] = int(plan.work.size());
+            for (int k = 0; k < n; ++k) plan.work.push_back({row, k * pps, std::min(pages, (k + 1) * pps), k});
+            // K and V rows, the query row and output row, the table entries.
+            plan.bytes += double(len) * kv_token_bytes + 2.0 * mpb::kQWidth * sizeof(float) +
+                          double(pages) * sizeof(int32_t);
+        }
     }
 }
 
@@ -139,12 +169,16 @@ struct mp_context {
     uint64_t* h_cow = nullptr;
     size_t cow_capacity = 0;
     // current step
-    int rows = 0, seqs = 0, work_count = 0;
+    int rows = 0, seqs = 0, work_count = 0, prefill_count = 0, entry_count = 0, region_count = 0, region_rows = 0;
+    size_t off_entries = 0, off_regions = 0, entry_capacity = 0, region_capacity = 0;
+    bool cow_timing = false, cow_timed = false;
+    cudaEvent_t cow_events[2] = {nullptr, nullptr};
+    float cow_ms = 0.f;
     size_t off_tokens = 0, off_pos = 0, off_slot = 0, off_len = 0, off_splits = 0, off_work0 = 0, off_last = 0,
-           off_work = 0;
+           off_work = 0, off_prefill = 0;
+    size_t prefill_capacity = 0;
     bool prepared = false;
     AttnPlan plan;
-    std::vector<int32_t> lengths;
     // attention profiling
     bool profile = false;
     std::vector<cudaEvent_t> prof_events;
@@ -174,6 +208,8 @@ void free_context(mp_context* c) {
                     (void*)c->h_cow})
         if (p) cudaFreeHost(p);
     for (auto e : c->prof_events) cudaEventDestroy(e);
+    for (auto e : c->cow_events)
+        if (e) cudaEventDestroy(e);
     if (c->done) cudaEventDestroy(c->done);
     for (auto e : c->mark)
         if (e) cudaEventDestroy(e);
@@ -320,6 +356,7 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         cuda_check(cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming), "create event");
         for (auto& e : c->mark) cuda_check(cudaEventCreate(&e), "create timer event");
         cuda_check(mpb::configure_attention(), "configure attention kernel");
+        cuda_check(mpb::configure_prefill_attention(), "configure prefill attention kernel");
         const size_t H = m.hidden, I = m.intermediate, L = m.layers, V = m.vocabulary;
         c->embed = device_alloc<float>(V * H, "embedding");
         c->final_norm = device_alloc<float>(H, "final norm");
@@ -370,7 +407,12 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         cuda_check(cudaMemsetAsync(c->counters, 0, T * sizeof(unsigned), c->stream), "zero counters");
         c->error = device_alloc<unsigned>(1, "error word");
         cuda_check(cudaMemsetAsync(c->error, 0, sizeof(unsigned), c->stream), "zero error word");
-        c->meta_capacity = 6 * T + S + 4 * c->work_capacity;
+        c->prefill_capacity = (T / mpb::kPrefillTileRows + S) * mpb::kKvHeads;
+        c->entry_capacity = S * size_t(r.table_stride);
+        c->region_capacity = S;
+        c->meta_capacity = 6 * T + S + 4 * c->work_capacity + 8 * c->prefill_capacity + 2 * c->entry_capacity +
+                           10 * c->region_capacity + 2;
+        for (auto& e : c->cow_events) cuda_check(cudaEventCreate(&e), "create cow timing event");
         c->meta = device_alloc<int32_t>(c->meta_capacity, "step metadata");
         c->h_meta = host_alloc<int32_t>(c->meta_capacity, "step metadata staging");
         c->out_tokens = device_alloc<int32_t>(S, "greedy tokens");
@@ -480,9 +522,29 @@ int mp_cow_copy(mp_context* c, const mp_tail_copy_region* regions, int32_t count
     });
 }
 
-int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t count, const int32_t* tokens) {
+int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t count, const int32_t* tokens,
+                       const mp_table_entry* entries, int32_t entry_count, const mp_tail_copy_region* regions,
+                       int32_t region_count) {
     return guarded([&] {
-        if (!c || !seqs || !tokens) fail(MP_ERR_INVALID, "null argument");
+        if (!c || !seqs || !tokens || (entry_count > 0 && !entries) || (region_count > 0 && !regions))
+            fail(MP_ERR_INVALID, "null argument");
+        if (entry_count < 0 || size_t(entry_count) > c->entry_capacity) fail(MP_ERR_INVALID, "too many table entries");
+        if (region_count < 0 || size_t(region_count) > c->region_capacity) fail(MP_ERR_INVALID, "too many COW regions");
+        for (int i = 0; i < entry_count; ++i) {
+            const auto& e = entries[i];
+            if (e.slot < 0 || e.slot >= c->rt.max_sequences || e.index < 0 || e.index >= c->rt.table_stride ||
+                e.block < 0 || e.block >= c->rt.max_blocks)
+                fail(MP_ERR_INVALID, "invalid block table entry");
+        }
+        int region_rows = 0;
+        for (int i = 0; i < region_count; ++i) {
+            const auto& r = regions[i];
+            if (r.width % 4 || r.destination % 4 || r.source % 4 || r.pitch % 4 || r.width > r.pitch ||
+                r.destination + (r.rows ? (r.rows - 1) * r.pitch + r.width : 0) > c->pool_elements ||
+                r.source + (r.rows ? (r.rows - 1) * r.pitch + r.width : 0) > c->pool_elements)
+                fail(MP_ERR_INVALID, "COW region outside the pools");
+            region_rows = std::max(region_rows, int(r.rows));
+        }
         if (!c->finalized) fail(MP_ERR_INVALID, "weights not finalized");
         const auto& r = c->rt;
         if (count < 1 || count > r.max_step_sequences) fail(MP_ERR_INVALID, "invalid sequence count");
@@ -499,13 +561,10 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         const int T = int(total);
         for (int i = 0; i < T; ++i)
             if (tokens[i] < 0 || tokens[i] >= c->model.vocabulary) fail(MP_ERR_INVALID, "invalid token");
-        c->lengths.resize(T);
-        int row = 0;
-        for (int i = 0; i < count; ++i)
-            for (int j = 0; j < seqs[i].count; ++j) c->lengths[row++] = seqs[i].start + j + 1;
-        plan_attention(c->lengths.data(), T, r.block_tokens, 0, c->plan);
-        const size_t W = c->plan.work.size();
+        plan_attention(seqs, count, r.block_tokens, 0, c->plan);
+        const size_t W = c->plan.work.size(), P = c->plan.prefill.size();
         if (W > c->work_capacity) fail(MP_ERR_INVALID, "attention work list exceeds capacity");
+        if (P > c->prefill_capacity) fail(MP_ERR_INVALID, "prefill work list exceeds capacity");
         // layout: tokens | pos | slot | len | splits | work0 | last | work
         cuda_check(cudaSetDevice(c->device), "select device");
         cuda_check(cudaStreamSynchronize(c->stream), "metadata staging reuse");
@@ -518,8 +577,11 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         c->off_work0 = c->off_splits + T;
         c->off_last = c->off_work0 + T;
         c->off_work = c->off_last + count;
+        c->off_prefill = c->off_work + 4 * W;
+        c->off_entries = c->off_prefill + 8 * P;
+        c->off_regions = (c->off_entries + 2 * size_t(entry_count) + 1) & ~size_t(1);  // 8-byte aligned
         std::memcpy(h + c->off_tokens, tokens, size_t(T) * 4);
-        row = 0;
+        int row = 0;
         for (int i = 0; i < count; ++i) {
             for (int j = 0; j < seqs[i].count; ++j, ++row) {
                 h[c->off_pos + row] = seqs[i].start + j;
@@ -531,11 +593,22 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         std::memcpy(h + c->off_splits, c->plan.splits.data(), size_t(T) * 4);
         std::memcpy(h + c->off_work0, c->plan.work0.data(), size_t(T) * 4);
         std::memcpy(h + c->off_work, c->plan.work.data(), W * sizeof(mpb::AttnWork));
-        const size_t bytes = (c->off_work + 4 * W) * 4;
+        std::memcpy(h + c->off_prefill, c->plan.prefill.data(), P * sizeof(mpb::PrefillWork));
+        for (int i = 0; i < entry_count; ++i) {
+            h[c->off_entries + 2 * i] = entries[i].slot * c->rt.table_stride + entries[i].index;
+            h[c->off_entries + 2 * i + 1] = entries[i].block;
+        }
+        if (region_count)
+            std::memcpy(h + c->off_regions, regions, size_t(region_count) * sizeof(mp_tail_copy_region));
+        const size_t bytes = (c->off_regions + 10 * size_t(region_count)) * 4;
         cuda_check(cudaMemcpyAsync(c->meta, h, bytes, cudaMemcpyHostToDevice, c->stream), "upload step metadata");
         c->rows = T;
         c->seqs = count;
         c->work_count = int(W);
+        c->prefill_count = int(P);
+        c->entry_count = entry_count;
+        c->region_count = region_count;
+        c->region_rows = region_rows;
         c->prepared = true;
     });
 }
@@ -550,6 +623,16 @@ int mp_forward_launch(mp_context* c) {
         cudaStream_t st = c->stream;
         const int32_t* meta = c->meta;
         cuda_check(cudaMemsetAsync(c->error, 0, sizeof(unsigned), st), "reset error word");
+        cuda_check(mpb::launch_table_patch(meta + c->off_entries, c->entry_count, c->tables,
+                                           int64_t(r.max_sequences) * r.table_stride, c->error, st),
+                   "table patch launch");
+        c->cow_timed = c->cow_timing && c->region_count > 0;
+        if (c->cow_timed) cuda_check(cudaEventRecord(c->cow_events[0], st), "cow timing");
+        cuda_check(mpb::launch_cow_copy(reinterpret_cast<const mpb::CowRegion*>(meta + c->off_regions),
+                                        c->region_count, c->region_rows, c->keys, c->values, c->pool_elements,
+                                        c->error, st),
+                   "cow launch");
+        if (c->cow_timed) cuda_check(cudaEventRecord(c->cow_events[1], st), "cow timing");
         cuda_check(mpb::launch_embed_rmsnorm(meta + c->off_tokens, c->embed, m.vocabulary, c->in_norm, m.rms_epsilon,
                                              c->x, c->xn, T, H, c->error, st),
                    "embed launch");
@@ -574,6 +657,21 @@ int mp_forward_launch(mp_context* c) {
         ap.out = c->attn;
         ap.out_stride = H;
         ap.error = c->error;
+        mpb::PrefillParams pp{};
+        pp.q = c->q;
+        pp.q_stride = H;
+        pp.keys = c->keys;
+        pp.values = c->values;
+        pp.layers = m.layers;
+        pp.block_tokens = r.block_tokens;
+        pp.max_blocks = r.max_blocks;
+        pp.tables = c->tables;
+        pp.table_stride = r.table_stride;
+        pp.work = reinterpret_cast<const mpb::PrefillWork*>(meta + c->off_prefill);
+        pp.work_count = c->prefill_count;
+        pp.out = c->attn;
+        pp.out_stride = H;
+        pp.error = c->error;
         mpb::RopeAppendArgs ra{};
         ra.qkv = c->qkv;
         ra.qkv_stride = c->qkvw;
@@ -605,7 +703,9 @@ int mp_forward_launch(mp_context* c) {
             ra.layer = l;
             cuda_check(mpb::launch_rope_append(ra, st), "rope/append launch");
             ap.layer = l;
+            pp.layer = l;
             if (c->profile) record_attention_event(c);
+            cuda_check(mpb::launch_prefill_attention(pp, st), "prefill attention launch");
             cuda_check(mpb::launch_paged_attention(ap, st), "attention launch");
             if (c->profile) record_attention_event(c);
             cuda_check(mpb::launch_gemm_simt({c->attn, H, c->wo + L * H * H, H, c->x, H, T, H, H, mpb::Epilogue::AddTo},
@@ -658,6 +758,10 @@ int mp_forward_collect(mp_context* c, int32_t* out_tokens, int32_t* out_finite, 
         cuda_check(cudaEventRecord(c->done, st), "record completion");
         wait_event(c->done, timeout_ms);
         if (c->profile) harvest_profile(c);
+        if (c->cow_timed) {
+            cuda_check(cudaEventElapsedTime(&c->cow_ms, c->cow_events[0], c->cow_events[1]), "cow elapsed");
+            c->cow_timed = false;
+        }
         if (out_tokens) std::memcpy(out_tokens, c->h_tokens, size_t(S) * 4);
         if (out_finite) std::memcpy(out_finite, c->h_finite, size_t(S) * 4);
         for (int i = 0; i < S; ++i) finite_all &= c->h_finite[i] != 0;
@@ -673,9 +777,11 @@ int mp_forward_collect(mp_context* c, int32_t* out_tokens, int32_t* out_finite, 
     return rc;
 }
 
-int mp_forward(mp_context* c, const mp_sequence_desc* seqs, int32_t count, const int32_t* tokens, int32_t* out_tokens,
-               int32_t* out_finite, float* out_logits, int32_t timeout_ms) {
-    int rc = mp_forward_prepare(c, seqs, count, tokens);
+int mp_forward(mp_context* c, const mp_sequence_desc* seqs, int32_t count, const int32_t* tokens,
+               const mp_table_entry* entries, int32_t entry_count, const mp_tail_copy_region* regions,
+               int32_t region_count, int32_t* out_tokens, int32_t* out_finite, float* out_logits,
+               int32_t timeout_ms) {
+    int rc = mp_forward_prepare(c, seqs, count, tokens, entries, entry_count, regions, region_count);
     if (rc != MP_OK) return rc;
     rc = mp_forward_launch(c);
     if (rc != MP_OK) {
@@ -748,6 +854,19 @@ int mp_timer_elapsed(mp_context* c, float* ms) {
         cuda_check(cudaEventSynchronize(b), "timer wait");
         cuda_check(cudaEventElapsedTime(ms, a, b), "timer elapsed");
     });
+}
+
+int mp_cow_timing(mp_context* c, int32_t enabled) {
+    if (!c) return MP_ERR_INVALID;
+    c->cow_timing = enabled != 0;
+    return MP_OK;
+}
+
+int mp_cow_elapsed(mp_context* c, float* ms) {
+    if (!c || !ms) return MP_ERR_INVALID;
+    *ms = c->cow_ms;
+    c->cow_ms = 0.f;
+    return MP_OK;
 }
 
 int mp_profile_enable(mp_context* c, int32_t enabled) {

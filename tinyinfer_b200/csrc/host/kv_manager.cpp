@@ -1,0 +1,362 @@
+#include "kv_manager.h"
+
+namespace miniprefix_b200 {
+
+KVManager::KVManager(KvCacheConfig config, int layers, int width, int context, int vocabulary)
+    : layers_(layers), width_(width), context_(context), vocabulary_(vocabulary), pool_(config, layers, width),
+      prefix_(pool_) {
+    if (context < 1 || vocabulary < 1) throw std::invalid_argument("invalid KV manager context/vocabulary");
+}
+
+KVManager::~KVManager() {
+    checkpoint_.reset();
+    pool_.attach_journal(nullptr);
+    for (auto& item : sequences_) pool_.release(item.second.sequence);
+    prefix_.clear();
+}
+
+std::size_t KVManager::max_sequence_blocks() const {
+    const int bt = config().block_tokens;
+    return std::size_t(context_ / bt + (context_ % bt != 0));
+}
+
+void KVManager::require_idle() const {
+    if (append_active_) throw std::logic_error("KV append transaction is active");
+}
+
+KVManager::State& KVManager::idle_state(const RequestId& id) {
+    require_idle();
+    auto& state = sequences_.at(id);
+    if (state.appending) throw std::logic_error("sequence has an active KV append");
+    return state;
+}
+
+void KVManager::validate_tokens(const std::vector<TokenId>& tokens) const {
+    for (auto t : tokens)
+        if (t < 0 || t >= vocabulary_) throw std::invalid_argument("invalid token");
+}
+
+// Pages held logically: every reservation, plus the pages of sequences that
+// have no reservation (kv_manager.cpp:93-98).
+std::size_t KVManager::committed_blocks() const {
+    std::size_t count = reserved_pages_;
+    for (const auto& [id, state] : sequences_)
+        if (!reservations_.count(id)) count += state.sequence.blocks.size();
+    return count;
+}
+
+void KVManager::touch_sequence(const RequestId& id, bool dropping) {
+    if (!checkpoint_) return;
+    auto found = checkpoint_->sequences.find(id);
+    if (found == checkpoint_->sequences.end()) {
+        SavedSequence saved;
+        auto it = sequences_.find(id);
+        if (it != sequences_.end()) {
+            saved.existed = true;
+            saved.used = it->second.sequence.used;
+            saved.blocks = it->second.sequence.blocks;
+            saved.token_count = it->second.sequence.tokens.size();
+        }
+        found = checkpoint_->sequences.emplace(id, std::move(saved)).first;
+    }
+    auto& saved = found->second;
+    if (dropping && saved.existed && !saved.tokens) {
+        const auto& t = sequences_.at(id).sequence.tokens;
+        saved.tokens.emplace(t.begin(), t.begin() + std::ptrdiff_t(std::min(saved.token_count, t.size())));
+    }
+}
+
+void KVManager::touch_reservation(const RequestId& id) {
+    if (!checkpoint_ || checkpoint_->reservations.count(id)) return;
+    auto it = reservations_.find(id);
+    checkpoint_->reservations.emplace(id, it == reservations_.end() ? std::nullopt
+                                                                    : std::optional<std::size_t>(it->second));
+}
+
+KvAdmission KVManager::reserve_request(const RequestId& id, std::size_t max_tokens) {
+    require_idle();
+    if (contains(id) || reservations_.count(id)) throw std::invalid_argument("duplicate KV reservation");
+    if (!max_tokens || max_tokens > std::size_t(context_)) throw std::invalid_argument("invalid KV reservation context");
+    const std::size_t pages = 1 + (max_tokens - 1) / std::size_t(config().block_tokens);
+    const std::size_t total = std::size_t(config().max_blocks);
+    if (pages > total) return KvAdmission::Impossible;
+    const std::size_t committed = committed_blocks();
+    if (committed > total || pages > total - committed) return KvAdmission::Wait;
+    touch_reservation(id);
+    reservations_.emplace(id, pages);
+    reserved_pages_ += pages;
+    return KvAdmission::Ready;
+}
+
+void KVManager::release_reservation(const RequestId& id) noexcept {
+    auto it = reservations_.find(id);
+    if (it == reservations_.end()) return;
+    try {
+        touch_reservation(id);
+    } catch (...) {
+    }
+    reserved_pages_ -= it->second;
+    reservations_.erase(it);
+}
+
+void KVManager::create(const RequestId& id) {
+    require_idle();
+    if (sequences_.count(id)) throw std::invalid_argument("sequence already exists");
+    touch_sequence(id);
+    sequences_.emplace(id, State{});
+}
+
+void KVManager::fork_sequence(const RequestId& source, const RequestId& target) {
+    require_idle();
+    const auto& original = sequences_.at(source).sequence;
+    auto& destination = idle_state(target).sequence;
+    if (source == target || destination.used || !destination.blocks.empty() || !destination.tokens.empty())
+        throw std::invalid_argument("fork requires a distinct empty target");
+    const auto reservation = reservations_.find(target);
+    if (reservation != reservations_.end()) {
+        if (original.blocks.size() > reservation->second) throw KvCapacityError("fork exceeds KV reservation");
+    } else {
+        const std::size_t used = committed_blocks(), total = std::size_t(config().max_blocks);
+        if (used > total || original.blocks.size() > total - used)
+            throw KvCapacityError("fork exceeds unreserved KV capacity");
+    }
+    PagedSequence copy = original;  // host metadata first, then leases
+    touch_sequence(target);
+    for (int block : copy.blocks) pool_.retain(block);
+    destination = std::move(copy);
+}
+
+std::size_t KVManager::reuse_prefix(const RequestId& id, const std::vector<TokenId>& prompt) {
+    if (prompt.empty() || prompt.size() > std::size_t(context_)) throw std::invalid_argument("invalid prefix context");
+    for (auto t : prompt)
+        if (t < 0 || t >= vocabulary_) throw std::invalid_argument("invalid prefix token");
+    auto& sequence = idle_state(id).sequence;
+    ++costs_.lookup_calls;
+    CostTimer timer(cost_timing_, costs_.lookup_ns);
+    touch_sequence(id);
+    const std::size_t count = std::size_t(prefix_.reuse(sequence, prompt));
+    const auto reservation = reservations_.find(id);
+    if (reservation != reservations_.end() && sequence.blocks.size() > reservation->second) {
+        pool_.release(sequence);
+        throw KvCapacityError("request exceeds KV reservation");
+    }
+    if (!reservations_.empty() && committed_blocks() > std::size_t(config().max_blocks)) {
+        pool_.release(sequence);
+        throw KvCapacityError("KV capacity reserved by active requests");
+    }
+    return count;
+}
+
+void KVManager::cache_prefix(const RequestId& id) {
+    auto& sequence = idle_state(id).sequence;
+    ++costs_.publish_calls;
+    CostTimer timer(cost_timing_, costs_.publish_ns);
+    prefix_.publish(sequence);
+}
+
+void KVManager::clear_prefix_cache() {
+    require_idle();
+    for (const auto& item : sequences_)
+        if (item.second.appending) throw std::logic_error("cannot clear prefix cache during KV append");
+    prefix_.clear();
+}
+
+void KVManager::reserve_pages(const RequestId& id, PagedSequence& sequence, int end, bool& cow) {
+    const int bt = config().block_tokens;
+    const std::size_t count = std::size_t(end / bt + (end % bt != 0));
+    const std::size_t required = count > sequence.blocks.size() ? count - sequence.blocks.size() : 0;
+    if (!reservations_.empty()) {
+        const auto found = reservations_.find(id);
+        if (found != reservations_.end()) {
+            if (count > found->second) throw KvCapacityError("request exceeds KV reservation");
+        } else {
+            const std::size_t committed = committed_blocks(), total = std::size_t(config().max_blocks);
+            if (committed > total || required > total - committed)
+                throw KvCapacityError("KV capacity reserved by active requests");
+        }
+    }
+    // Evict LRU cache leases while physically short; a victim may have been the
+    // only other holder of the shared tail, which then needs no copy.
+    while (pool_.free_blocks() < required + std::size_t(cow) && prefix_.evict_one())
+        if (cow && pool_.references(sequence.blocks.back()) == 1) cow = false;
+    if (cow && pool_.free_blocks() < required + 1) throw KvCapacityError("paged KV block pool exhausted");
+    pool_.reserve(sequence, end);
+}
+
+KVManager::Append::Append(KVManager& owner, const RequestId& id, const std::vector<TokenId>& tokens)
+    : owner_(&owner), id_(id), state_(&owner.idle_state(id)), tokens_(tokens),
+      original_blocks_(state_->sequence.blocks.size()) {
+    auto& sequence = state_->sequence;
+    if (tokens.empty() || tokens.size() > std::size_t(owner.context_ - sequence.used))
+        throw std::invalid_argument("context overflow/empty input");
+    owner.validate_tokens(tokens);
+    owner.touch_sequence(id);
+    sequence.tokens.reserve(std::size_t(sequence.used) + tokens.size());
+    const int valid = sequence.used % owner.config().block_tokens;
+    bool cow = valid && owner.pool_.references(sequence.blocks.back()) > 1;
+    owner.reserve_pages(id, sequence, sequence.used + int(tokens.size()), cow);
+    if (cow) {
+        const int old = sequence.blocks[original_blocks_ - 1];
+        const int replacement = owner.pool_.allocate();
+        copy_ = TailCopy{old, replacement, valid};
+        sequence.blocks[original_blocks_ - 1] = replacement;
+    }
+    state_->appending = true;
+    owner.append_active_ = true;
+}
+
+KVManager::Append::~Append() { rollback(); }
+
+const PagedSequence& KVManager::Append::sequence() const {
+    if (!owner_) throw std::logic_error("KV append already finished");
+    return state_->sequence;
+}
+
+void KVManager::Append::copy_shared_tail(const std::function<void(std::size_t, std::size_t, std::size_t)>& copier) {
+    copy_shared_tail_region([&](const TailCopyRegion& r) {
+        for (std::size_t row = 0; row < r.rows; ++row)
+            copier(r.destination + row * r.pitch, r.source + row * r.pitch, r.width);
+    });
+}
+
+void KVManager::Append::copy_shared_tail_region(const std::function<void(const TailCopyRegion&)>& copier) {
+    if (!owner_) throw std::logic_error("KV append already finished");
+    if (!copy_) return;
+    copied_ = false;
+    const std::size_t pitch = std::size_t(owner_->config().block_tokens) * std::size_t(owner_->width_);
+    const std::size_t rows = std::size_t(owner_->layers_);
+    copier({std::size_t(copy_->destination) * rows * pitch, std::size_t(copy_->source) * rows * pitch, pitch,
+            std::size_t(copy_->valid_tokens) * std::size_t(owner_->width_), rows});
+    copied_ = true;
+}
+
+void KVManager::Append::commit() {
+    if (!owner_) throw std::logic_error("KV append already finished");
+    if (copy_ && !copied_) throw std::logic_error("shared tail payload was not copied");
+    auto& sequence = state_->sequence;
+    sequence.tokens.insert(sequence.tokens.end(), tokens_.begin(), tokens_.end());
+    sequence.used += int(tokens_.size());
+    owner_->forward_tokens_ += tokens_.size();
+    if (copy_) owner_->pool_.unref(copy_->source);
+    state_->appending = false;
+    owner_->append_active_ = false;
+    owner_ = nullptr;
+}
+
+void KVManager::Append::rollback() noexcept {
+    if (!owner_) return;
+    owner_->pool_.rollback(state_->sequence, original_blocks_);
+    if (copy_) {
+        state_->sequence.blocks[original_blocks_ - 1] = copy_->source;
+        owner_->pool_.unref(copy_->destination);
+    }
+    state_->appending = false;
+    owner_->append_active_ = false;
+    owner_ = nullptr;
+}
+
+void KVManager::reset_sequence(const RequestId& id) {
+    auto& state = idle_state(id);
+    touch_sequence(id, true);
+    pool_.release(state.sequence);
+}
+
+void KVManager::release(const RequestId& id) {
+    require_idle();
+    auto it = sequences_.find(id);
+    if (it == sequences_.end()) throw std::invalid_argument("unknown sequence");
+    if (it->second.appending) throw std::logic_error("cannot release sequence during KV append");
+    touch_sequence(id, true);
+    touch_reservation(id);
+    pool_.release(it->second.sequence);
+    sequences_.erase(it);
+    auto r = reservations_.find(id);
+    if (r != reservations_.end()) {
+        reserved_pages_ -= r->second;
+        reservations_.erase(r);
+    }
+}
+
+void KVManager::clear() {
+    require_idle();
+    for (const auto& item : sequences_)
+        if (item.second.appending) throw std::logic_error("cannot clear sequences during KV append");
+    for (auto& item : sequences_) {
+        touch_sequence(item.first, true);
+        pool_.release(item.second.sequence);
+    }
+    sequences_.clear();
+    prefix_.clear();
+    for (const auto& r : reservations_) touch_reservation(r.first);
+    reservations_.clear();
+    reserved_pages_ = 0;
+}
+
+KvStats KVManager::stats() const {
+    KvStats r;
+    r.live_sequences = sequences_.size();
+    r.forward_tokens = forward_tokens_;
+    r.kv_block_tokens = std::size_t(config().block_tokens);
+    r.kv_total_blocks = std::size_t(config().max_blocks);
+    r.kv_live_blocks = pool_.live_blocks();
+    r.kv_peak_blocks = pool_.peak_blocks();
+    r.kv_reserved_bytes = pool_.reserved_bytes();
+    r.live_kv_bytes = pool_.live_blocks() * pool_.block_bytes();
+    r.peak_kv_bytes = pool_.peak_blocks() * pool_.block_bytes();
+    r.prefix_cache_capacity = std::size_t(config().prefix_cache_blocks);
+    r.kv_cached_blocks = prefix_.size();
+    r.kv_cache_only_blocks = prefix_.cache_only_blocks();
+    r.prefix_hits = prefix_.hits();
+    r.prefix_misses = prefix_.misses();
+    r.prefix_reused_tokens = prefix_.reused_tokens();
+    r.prefix_evictions = prefix_.evictions();
+    return r;
+}
+
+void KVManager::begin_checkpoint() {
+    require_idle();
+    checkpoint_ = std::make_unique<Checkpoint>();
+    checkpoint_->live = pool_.live_blocks();
+    checkpoint_->peak = pool_.peak_blocks();
+    checkpoint_->prefix = prefix_.snapshot();
+    checkpoint_->reserved_pages = reserved_pages_;
+    checkpoint_->forward_tokens = forward_tokens_;
+    checkpoint_->costs = costs_;
+    pool_.attach_journal(&checkpoint_->pool_journal);
+}
+
+void KVManager::restore_checkpoint() {
+    if (!checkpoint_) throw std::logic_error("no KV checkpoint");
+    auto& cp = *checkpoint_;
+    pool_.attach_journal(nullptr);
+    pool_.undo(cp.pool_journal, 0, cp.live, cp.peak);
+    prefix_.restore(cp.prefix);
+    for (auto& [id, saved] : cp.sequences) {
+        if (!saved.existed) {
+            sequences_.erase(id);
+            continue;
+        }
+        auto& state = sequences_[id];
+        state.appending = false;
+        state.sequence.used = saved.used;
+        state.sequence.blocks = std::move(saved.blocks);
+        if (saved.tokens) state.sequence.tokens = std::move(*saved.tokens);
+        else state.sequence.tokens.resize(saved.token_count);
+    }
+    for (auto& [id, pages] : cp.reservations) {
+        if (pages) reservations_[id] = *pages;
+        else reservations_.erase(id);
+    }
+    reserved_pages_ = cp.reserved_pages;
+    forward_tokens_ = cp.forward_tokens;
+    costs_ = cp.costs;
+    append_active_ = false;
+    checkpoint_.reset();
+}
+
+void KVManager::end_checkpoint() {
+    pool_.attach_journal(nullptr);
+    checkpoint_.reset();
+}
+
+}  // namespace miniprefix_b200

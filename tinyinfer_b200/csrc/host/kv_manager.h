@@ -1,0 +1,149 @@
+// Sequence metadata, page references, reservations and prefix leases of one
+// runner (host side). Payload, device tables and completion stay in the backend.
+// Single-threaded API.
+//
+// Contract of the reference KVManager (miniprefix/include/miniprefix/kv_manager.h:18-96,
+// miniprefix/src/kv/kv_manager.cpp), including every error class and message:
+// logical reservations of 1+(max_tokens-1)/block_tokens pages without a sharing
+// discount (:99-109), forks that share all pages (:115-130), prefix reuse with
+// reservation checks (:131-145), and the Append transaction (:157-242): validate,
+// reserve pages (evicting LRU cache leases while physically short, re-checking
+// after every victim whether a shared partial tail still needs its copy-on-write
+// page, :174-183), allocate the COW replacement, then commit or roll back.
+//
+// Batched steps: begin_checkpoint()/restore_checkpoint() bracket a window in
+// which every mutation is recorded so that the exact state at the checkpoint can
+// be restored (pages, references, free-list order, sequences, reservations,
+// prefix index and counters).
+#pragma once
+#include <functional>
+#include <map>
+#include <memory>
+#include <optional>
+
+#include "prefix_cache.h"
+
+namespace miniprefix_b200 {
+
+class KVManager {
+    struct State {
+        PagedSequence sequence;
+        bool appending = false;
+    };
+
+public:
+    struct TailCopy {
+        int source, destination, valid_tokens;
+    };
+    // Float-element offsets into ONE pool; rows are layers. Copy K and V alike.
+    struct TailCopyRegion {
+        std::size_t destination, source, pitch, width, rows;
+    };
+
+    class Append {
+        friend class KVManager;
+        KVManager* owner_;
+        RequestId id_;
+        State* state_;
+        std::vector<TokenId> tokens_;
+        std::size_t original_blocks_;
+        std::optional<TailCopy> copy_;
+        bool copied_ = false;
+        Append(KVManager& owner, const RequestId& id, const std::vector<TokenId>& tokens);
+
+    public:
+        Append(const Append&) = delete;
+        Append& operator=(const Append&) = delete;
+        Append(Append&&) = delete;
+        Append& operator=(Append&&) = delete;
+        ~Append();
+        const PagedSequence& sequence() const;
+        std::size_t original_blocks() const { return original_blocks_; }
+        const std::optional<TailCopy>& tail_copy() const { return copy_; }
+        void copy_shared_tail(const std::function<void(std::size_t, std::size_t, std::size_t)>& copier);
+        void copy_shared_tail_region(const std::function<void(const TailCopyRegion&)>& copier);
+        void commit();
+        void rollback() noexcept;
+    };
+
+    KVManager(KvCacheConfig config, int layers, int width, int context, int vocabulary);
+    KVManager(const KVManager&) = delete;
+    KVManager& operator=(const KVManager&) = delete;
+    ~KVManager();
+
+    const KvCacheConfig& config() const { return pool_.config(); }
+    int context_limit() const { return context_; }
+    std::size_t reserved_bytes() const { return pool_.reserved_bytes(); }
+    std::size_t max_sequence_blocks() const;
+    bool contains(const RequestId& id) const { return sequences_.count(id) != 0; }
+    const PagedSequence& sequence(const RequestId& id) const { return sequences_.at(id).sequence; }
+    std::size_t offset(const PagedSequence& sequence, int layer, int token) const {
+        return pool_.offset(sequence, layer, token, layers_, width_);
+    }
+    KvAdmission reserve_request(const RequestId& id, std::size_t max_tokens);
+    void release_reservation(const RequestId& id) noexcept;
+    void create(const RequestId& id);
+    void fork_sequence(const RequestId& source, const RequestId& target);
+    std::size_t reuse_prefix(const RequestId& id, const std::vector<TokenId>& prompt);
+    void cache_prefix(const RequestId& id);
+    void clear_prefix_cache();
+    Append prepare_append(const RequestId& id, const std::vector<TokenId>& tokens) {
+        return Append(*this, id, tokens);
+    }
+    void reset_sequence(const RequestId& id);
+    void release(const RequestId& id);
+    void clear();
+    KvStats stats() const;
+    void set_cost_timing(bool enabled) { cost_timing_ = enabled; }
+    CostStats cost_stats() const { return costs_; }
+    const KvBlockPool& pool() const { return pool_; }
+    bool freed_this_epoch(int block) const { return pool_.freed_this_epoch(block); }
+    void next_epoch() { pool_.next_epoch(); }
+
+    // ---- checkpoints for batched steps
+    void begin_checkpoint();
+    void restore_checkpoint();
+    void end_checkpoint();
+
+private:
+    void require_idle() const;
+    State& idle_state(const RequestId& id);
+    void validate_tokens(const std::vector<TokenId>& tokens) const;
+    std::size_t committed_blocks() const;
+    void reserve_pages(const RequestId& id, PagedSequence& sequence, int end, bool& cow);
+    void touch_sequence(const RequestId& id, bool dropping = false);  // journal a sequence mutation
+    void touch_reservation(const RequestId& id);
+
+    int layers_, width_, context_, vocabulary_;
+    KvBlockPool pool_;
+    ExactPrefixCache prefix_;
+    std::map<RequestId, State> sequences_;
+    std::map<RequestId, std::size_t> reservations_;
+    std::size_t reserved_pages_ = 0;  // sum of reservations_
+    std::size_t forward_tokens_ = 0;
+    bool append_active_ = false;
+    bool cost_timing_ = false;
+    CostStats costs_;
+
+    // A sequence as it was at the checkpoint. Tokens only grow inside a window
+    // unless the sequence is released, so only their count is kept until then.
+    struct SavedSequence {
+        bool existed = false;
+        int used = 0;
+        std::vector<int> blocks;
+        std::size_t token_count = 0;
+        std::optional<std::vector<std::int32_t>> tokens;
+    };
+    struct Checkpoint {
+        std::vector<KvBlockPool::JournalEntry> pool_journal;
+        std::size_t live = 0, peak = 0;
+        ExactPrefixCache::Snapshot prefix;
+        std::map<RequestId, SavedSequence> sequences;
+        std::map<RequestId, std::optional<std::size_t>> reservations;  // nullopt: did not exist
+        std::size_t reserved_pages = 0, forward_tokens = 0;
+        CostStats costs;
+    };
+    std::unique_ptr<Checkpoint> checkpoint_;
+};
+
+}  // namespace miniprefix_b200

@@ -53,6 +53,38 @@ struct AttnParams {
     unsigned* error;
 };
 
+// Chunked prefill: one CTA per (64-row query tile of one sequence, kv head).
+struct PrefillWork {
+    int32_t row0;      // batch row of the tile's first query
+    int32_t rows;      // valid rows in the tile (1..64)
+    int32_t position;  // sequence position of the first row
+    int32_t slot;      // block-table slot of the sequence
+    int32_t kv_head;
+    int32_t pad[3];
+};
+
+struct PrefillParams {
+    const float* q;
+    int q_stride;
+    const float* keys;
+    const float* values;
+    int layers, layer, block_tokens, max_blocks;
+    const int32_t* tables;
+    int table_stride;
+    const PrefillWork* work;
+    int work_count;
+    float* out;
+    int out_stride;
+    unsigned* error;
+};
+
+// Sequences appending at least this many rows in one forward take the tiled
+// prefill kernel; shorter appends (decode) take the split-K decode kernel per row.
+constexpr int kPrefillMinRows = 8;
+constexpr int kPrefillTileRows = 64;
+
+cudaError_t configure_prefill_attention();
+cudaError_t launch_prefill_attention(const PrefillParams& p, cudaStream_t stream);
 cudaError_t configure_attention();
 // Message returned by mp_last_error() on this thread.
 void set_last_error(const char* message);

@@ -43,6 +43,10 @@ class SequenceDescC(C.Structure):
     _fields_ = [("slot", C.c_int32), ("start", C.c_int32), ("count", C.c_int32)]
 
 
+class TableEntryC(C.Structure):
+    _fields_ = [("slot", C.c_int32), ("index", C.c_int32), ("block", C.c_int32)]
+
+
 class TailCopyRegionC(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("destination", "source", "pitch", "width", "rows")]
 
@@ -66,9 +70,12 @@ def library() -> C.CDLL:
         lib.mp_finalize_weights.argtypes = [C.c_void_p]
         lib.mp_table_write.argtypes = [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_int32]
         lib.mp_cow_copy.argtypes = [C.c_void_p, C.c_void_p, C.c_int32]
-        lib.mp_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
-                                   C.c_int32]
-        lib.mp_forward_prepare.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p]
+        lib.mp_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p,
+                                   C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32]
+        lib.mp_forward_prepare.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32,
+                                           C.c_void_p, C.c_int32]
+        lib.mp_cow_timing.argtypes = [C.c_void_p, C.c_int32]
+        lib.mp_cow_elapsed.argtypes = [C.c_void_p, C.POINTER(C.c_float)]
         lib.mp_forward_launch.argtypes = [C.c_void_p]
         lib.mp_forward_collect.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32]
         lib.mp_sync.argtypes = [C.c_void_p, C.c_int32]
@@ -148,25 +155,34 @@ class DeviceContext:
         arr = (TailCopyRegionC * len(regions))(*[TailCopyRegionC(*r) for r in regions])
         check(self.lib.mp_cow_copy(self.h, arr, len(regions)))
 
-    def forward(self, sequences, tokens, *, logits: bool = True, timeout_ms: int = 60000):
-        """sequences: list of (slot, start, count). Returns (tokens, finite, logits|None, rc)."""
+    @staticmethod
+    def _extras(entries, regions):
+        e = (TableEntryC * max(1, len(entries)))(*[TableEntryC(*x) for x in entries])
+        r = (TailCopyRegionC * max(1, len(regions)))(*[TailCopyRegionC(*x) for x in regions])
+        return e, len(entries), r, len(regions)
+
+    def forward(self, sequences, tokens, *, entries=(), regions=(), logits: bool = True, timeout_ms: int = 60000):
+        """sequences: list of (slot, start, count); entries: (slot, index, block) table
+        writes; regions: COW regions. Returns (tokens, finite, logits|None, rc)."""
         n = len(sequences)
         descs = (SequenceDescC * n)(*[SequenceDescC(*s) for s in sequences])
         toks = np.ascontiguousarray(tokens, dtype=np.int32)
         out_t = np.zeros(n, dtype=np.int32)
         out_f = np.zeros(n, dtype=np.int32)
         out_l = np.zeros((n, self.config.vocabulary), dtype=np.float32) if logits else None
-        rc = self.lib.mp_forward(self.h, descs, n, _ptr(toks), _ptr(out_t), _ptr(out_f),
+        e, ne, r, nr = self._extras(entries, regions)
+        rc = self.lib.mp_forward(self.h, descs, n, _ptr(toks), e, ne, r, nr, _ptr(out_t), _ptr(out_f),
                                  _ptr(out_l) if logits else None, timeout_ms)
         if rc not in (MP_OK, MP_ERR_NONFINITE):
             check(rc)
         return out_t, out_f.astype(bool), out_l, rc
 
-    def prepare(self, sequences, tokens) -> None:
+    def prepare(self, sequences, tokens, entries=(), regions=()) -> None:
         n = len(sequences)
         descs = (SequenceDescC * n)(*[SequenceDescC(*s) for s in sequences])
         toks = np.ascontiguousarray(tokens, dtype=np.int32)
-        check(self.lib.mp_forward_prepare(self.h, descs, n, _ptr(toks)))
+        e, ne, r, nr = self._extras(entries, regions)
+        check(self.lib.mp_forward_prepare(self.h, descs, n, _ptr(toks), e, ne, r, nr))
 
     def launch(self) -> None:
         check(self.lib.mp_forward_launch(self.h))
