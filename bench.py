@@ -1,0 +1,398 @@
+"""Benchmark: batched greedy decode of the 135M-shape FP32 model over paged KV
+on N GPUs, one process per GPU, requests sharded by GPU.
+
+Per GPU: 256 requests whose 2048-token prompts share a 1032-token prefix (64 full
+pages + 8 tokens of a partial page that every follower reuses and copies on
+write), page size 16. A seed request is prefilled first so that the prefix is
+published; the followers then prefill their 1016-token suffixes. A "step" is one
+Engine.step() in which all 256 requests decode one token. W untimed warm-up steps,
+then exactly K timed steps.
+
+  value  = decode tokens / device time of the K steps' forwards (inputs resident:
+           CUDA events around the kernels of each forward on the context stream)
+  e2e    = decode tokens / time of the K Engine.step() calls through the C ABI,
+           CUDA events on the context stream bracketing them (host bookkeeping,
+           H2D of tokens/tables/work lists, forward, D2H of tokens included)
+  roofline: the paged-attention kernel (CUDA events around each launch), bytes =
+           each decode row's K/V tokens x 1536 B + q/out rows + table entries.
+
+--impl reference times the reference's own CPU engine (oracle/_ref, built from the
+reference sources) on the host cores instead. Synthetic seeded data throughout.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import multiprocessing as mp
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+METRIC = "decode tok/s, 135M FP32 paged-KV, batch 256/GPU, ctx 2k (shared 1032-token prefix, COW)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--requests", type=int, default=256)
+    p.add_argument("--prompt", type=int, default=2048)
+    p.add_argument("--shared", type=int, default=1032)
+    p.add_argument("--block-tokens", type=int, default=16)
+    p.add_argument("--prefix-blocks", type=int, default=66)
+    p.add_argument("--layers", type=int, default=30)
+    p.add_argument("--prefill-budget", type=int, default=8192)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-workers", type=int, default=0)
+    p.add_argument("--cpu-context", type=int, default=512)
+    p.add_argument("--cpu-seconds", type=float, default=12.0)
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        with open(PEAKS) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------------------- workload
+def max_new_tokens(args):
+    """Enough new tokens that no request finishes before the timed steps end: the
+    followers that start decoding first run ahead by up to the prefill steps."""
+    prefill_steps = -(-args.requests * (args.prompt - args.shared) // args.prefill_budget)
+    return args.warmup + args.steps + prefill_steps + 8
+
+
+def model_config(args):
+    from tinyinfer_b200.synthetic import ModelConfig
+
+    return ModelConfig(layers=args.layers, context=args.prompt + max_new_tokens(args) + 32)
+
+
+def prompts(args, rank):
+    """Seeded prompts: one shared prefix (same on every GPU), unique suffixes per request."""
+    rng = np.random.default_rng(20240 + rank)
+    vocab = 49152
+    shared = np.random.default_rng(7).integers(0, vocab, args.shared).astype(np.int32)
+    out = []
+    for i in range(args.requests):
+        suffix = rng.integers(0, vocab, args.prompt - args.shared).astype(np.int32)
+        out.append(np.concatenate([shared, suffix]))
+    return out
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+                for name, v in zip(names, f[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(name)
+            except Exception:
+                continue
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        loaded = [s for s in sm if s > 0.5 * (mx or max(sm))] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def unique_decode_bytes(engine, ids, block_tokens):
+    """Distinct (page, slot) K/V rows the decode step reads, x 1536 B (shared pages once)."""
+    seen = {}
+    for rid in ids:
+        s = engine.sequence(rid)
+        if not s:
+            continue
+        used, blocks = s
+        for i, b in enumerate(blocks):
+            valid = min(block_tokens, used + 1 - i * block_tokens)
+            if valid > 0:
+                seen[b] = max(seen.get(b, 0), valid)
+    return sum(seen.values()) * 2 * 192 * 4
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def _cpu_worker(args_tuple):
+    """One reference CPU runner: build a context of `context` tokens (untimed), then
+    decode greedily for `seconds`. Returns (steps, elapsed)."""
+    context, seconds, layers, worker = args_tuple
+    sys.path.insert(0, ROOT)
+    from oracle.oracle import RefLib, RefRunner
+    from tinyinfer_b200.synthetic import ModelConfig, random_tokens, random_weights
+
+    c = ModelConfig(layers=layers, context=context + 4096)
+    w = random_weights(c, seed=0)
+    ref = RefLib()
+    r = RefRunner.cpu(ref, c, w, c.context, 16, (c.context + 15) // 16 + 1, 0)
+    r.create("s")
+    logits = r.append("s", random_tokens(context, c.vocabulary, 100 + worker))
+    steps, start = 0, time.perf_counter()
+    while time.perf_counter() - start < seconds:
+        logits = r.append("s", [int(np.argmax(logits))])
+        steps += 1
+    return steps, time.perf_counter() - start
+
+
+def cpu_baseline(args, workers=None, seconds=None):
+    from oracle import oracle as orc
+
+    kind = "reference" if os.path.exists(orc.REF_SO) else None
+    if kind is None:
+        return {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
+                "sample": "oracle/_ref/libmpref.so not present on this host"}
+    n = workers or args.cpu_workers or min(os.cpu_count() or 1, 16)
+    seconds = seconds or args.cpu_seconds
+    ctx = mp.get_context("spawn")
+    t0 = time.perf_counter()
+    with ctx.Pool(n) as pool:
+        res = pool.map(_cpu_worker, [(args.cpu_context, seconds, args.layers, i) for i in range(n)])
+    steps = sum(r[0] for r in res)
+    elapsed = max(r[1] for r in res)
+    return {"value": steps / elapsed, "unit": "tok/s", "cores": n, "kind": kind,
+            "sample": (f"{n} single-threaded reference CpuRunner processes (oracle/_ref, AVX2+FMA), each "
+                       f"greedy-decoding one sequence at context {args.cpu_context} for ~{seconds:.0f} s after an "
+                       f"untimed {args.cpu_context}-token prefill ({steps} tokens, {time.perf_counter() - t0:.0f} s "
+                       f"wall); a 2048-token context takes minutes per core to build, and the CPU cost per token "
+                       f"grows with context, so this overstates the CPU rate at ctx 2k")}
+
+
+# ----------------------------------------------------------------------------- B200 arm
+def run_b200(args, rank, world, local_rank):
+    import torch
+
+    from tinyinfer_b200.host import Engine, Runner
+    from tinyinfer_b200.synthetic import random_weights
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+    torch.cuda.set_device(local_rank)
+
+    cfg = model_config(args)
+    weights = random_weights(cfg, seed=0)
+    bt = args.block_tokens
+    n = args.requests
+    max_new = max_new_tokens(args)
+    pages_per_request = -(-(args.prompt + max_new - 1) // bt)
+    max_blocks = (n + 1) * pages_per_request + 64
+    runner = Runner.b200(cfg, weights, context=cfg.context, block_tokens=bt, max_blocks=max_blocks,
+                         prefix_blocks=args.prefix_blocks, device=local_rank, max_sequences=n + 8,
+                         max_step_tokens=args.prefill_budget, max_step_sequences=n + 8)
+    del weights
+    engine = Engine(runner, n, args.prefill_budget, args.prompt, cfg.context)
+    dev = engine.device()
+    ps = prompts(args, rank)
+    ids = [f"r{i}" for i in range(n)]
+
+    # Seed: prefill to completion so the shared prefix is published.
+    t_setup = time.perf_counter()
+    engine.submit(ids[0], ps[0], max_new)
+    while not any(e[1] is not None for e in engine.poll_events()):
+        engine.step()
+    for i in range(1, n):
+        engine.submit(ids[i], ps[i], max_new)
+    started = {ids[0]}
+    while len(started) < n:
+        engine.step()
+        for rid, tok, reason, err in engine.poll_events():
+            if reason == 3:
+                raise RuntimeError(f"request {rid} failed: {err}")
+            if tok is not None:
+                started.add(rid)
+    setup_s = time.perf_counter() - t_setup
+    reused = engine.runner_stats()["prefix_reused_tokens"]
+    cow = engine.cost_stats()["cow_pages"]
+
+    def decode_step():
+        engine.step()
+        evs = engine.poll_compact()
+        return len(evs[0])
+
+    for _ in range(args.warmup):
+        decode_step()
+    uniq = unique_decode_bytes(engine, ids, bt)
+    dev.counters(reset=True)
+    dev.profile_read()
+    dev.profile(True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    dev.sync()
+    tokens = 0
+    with ClockSampler(local_rank) as clocks:
+        dev.timer_mark()
+        for _ in range(args.steps):
+            tokens += decode_step()
+        dev.timer_mark()
+        e2e_ms = dev.timer_elapsed()
+    dev.sync()
+    torch.cuda.synchronize()
+    dev.profile(False)
+    counters = dev.counters(reset=True)
+    attn_ms, attn_launches, attn_bytes = dev.profile_read()
+    if dist:
+        dist.barrier()
+
+    device_ms = counters["forward_ms"]
+    stats = torch.tensor([e2e_ms, device_ms, float(tokens)], dtype=torch.float64, device="cuda")
+    if dist:
+        mx = stats.clone()
+        dist.all_reduce(mx[:2], op=dist.ReduceOp.MAX)
+        tot = stats.clone()
+        dist.all_reduce(tot[2:], op=dist.ReduceOp.SUM)
+        e2e_ms, device_ms, tokens_all = float(mx[0]), float(mx[1]), float(tot[2])
+    else:
+        tokens_all = float(tokens)
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return None
+
+    hbm, peak_kind = peaks()
+    launch_ms = attn_ms / max(attn_launches, 1)
+    bytes_per_launch = attn_bytes / max(attn_launches, 1)
+    unique_per_launch = uniq / args.layers
+    achieved = bytes_per_launch / (launch_ms * 1e-3) / 1e9 if launch_ms > 0 else None
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "attention_decode_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                t = json.load(f)
+            traffic = t["dram_bytes_per_token_row"] * bytes_per_launch / t["algorithmic_bytes_per_token_row"]
+        except Exception:
+            traffic = None
+    line = {
+        "metric": METRIC,
+        "value": tokens_all / (device_ms * 1e-3),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": device_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,0.02) weights, uniform random token ids)",
+        "config": {"workload": "config3: batched greedy decode, 256 requests/GPU at ctx 2048, 1032-token shared "
+                               "prefix reused with COW of its partial page",
+                   "model": "SmolLM2-135M shape, 30 layers, FP32, tied head", "requests_per_gpu": args.requests,
+                   "prompt_tokens": args.prompt, "shared_prefix_tokens": args.shared, "block_tokens": bt,
+                   "prefix_cache_blocks": args.prefix_blocks, "parallelism": f"request-sharded replicas x{world}",
+                   "l2": "inputs larger than L2 (>= 24 GB of K/V read per step)",
+                   "setup_seconds": round(setup_s, 1), "prefix_reused_tokens": reused, "cow_pages": cow},
+        "e2e": {"value": tokens_all / (e2e_ms * 1e-3), "unit": "tok/s",
+                "h2d_bytes_per_step": counters["h2d_bytes"] / max(counters["forwards"], 1),
+                "d2h_bytes_per_step": counters["d2h_bytes"] / max(counters["forwards"], 1),
+                "ms_per_step": e2e_ms / args.steps},
+        "gpu_launches": int(counters["kernel_launches"]),
+        "roofline": {"bound": "hbm", "kernel": "paged_attention_kernel (decode, split-K)",
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm if achieved else None, "traffic": traffic,
+                     "peak_kind": peak_kind, "launch_ms": launch_ms, "launches": attn_launches,
+                     "algorithmic_bytes_per_launch": bytes_per_launch,
+                     "unique_bytes_per_launch": unique_per_launch,
+                     "unique_achieved": unique_per_launch / (launch_ms * 1e-3) / 1e9 if launch_ms > 0 else None,
+                     "attention_share_of_forward": attn_ms / device_ms if device_ms else None},
+        "clocks": clocks.summary(),
+    }
+    engine.shutdown()
+    engine.close()
+    if dist:
+        dist.destroy_process_group()
+    return line
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    from oracle import oracle as orc
+
+    if not os.path.exists(orc.REF_SO):
+        return {"impl": "reference", "unavailable": "oracle/_ref/libmpref.so (reference CPU engine) not built on this host"}
+    n = args.cpu_workers or min(os.cpu_count() or 1, 16)
+    per_step = max(2.0, args.cpu_seconds / max(args.steps, 1))
+    res = cpu_baseline(args, n, per_step * (args.steps + args.warmup))
+    value = res["value"]
+    return {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": None if not value else 1000.0 * n / value,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "config3 decode on the reference CPU engine (see cpu_baseline.sample)",
+                       "model": "SmolLM2-135M shape, 30 layers, FP32"},
+            "cpu_baseline": res,
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+    else:
+        line = run_b200(args, rank, world, local_rank)
+        if line is not None and world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -140,6 +140,17 @@ int mp_timer_elapsed(mp_context* ctx, float* milliseconds);
  * since the last read (and resets them). */
 int mp_profile_enable(mp_context* ctx, int32_t enabled);
 int mp_profile_read(mp_context* ctx, float* attention_ms, int32_t* attention_launches, double* attention_bytes);
+/* Cumulative counters of collected forwards: device time from the first to the
+ * last kernel of each forward (CUDA events on the context stream), kernels
+ * launched, and bytes moved host->device / device->host by the forwards. */
+typedef struct {
+    uint64_t forwards;
+    double forward_ms;
+    uint64_t kernel_launches;
+    uint64_t h2d_bytes, d2h_bytes;
+} mp_counters;
+int mp_read_counters(mp_context* ctx, mp_counters* out, int32_t reset);
+
 /* Device time of the COW copies of the last collected forward that had any
  * (milliseconds; 0 when it had none). Recorded only while cost timing is on. */
 int mp_cow_timing(mp_context* ctx, int32_t enabled);

@@ -139,6 +139,9 @@ int mph_engine_sequence(mph_engine* e, const char* id, int32_t* used, int32_t* b
 /* Device forwards launched by the B200 runner so far, and how many of them were
  * split off early to keep a reused page's old readers ahead of its new writer. */
 int mph_engine_flushes(mph_engine* e, size_t* flushes, size_t* hazard_flushes);
+/* The device context of the engine's B200 runner (NULL for other runners), for
+ * timing and counters through include/miniprefix_b200.h. */
+mp_context* mph_engine_device(mph_engine* e);
 
 #ifdef __cplusplus
 }

@@ -173,6 +173,9 @@ struct mp_context {
     size_t off_entries = 0, off_regions = 0, entry_capacity = 0, region_capacity = 0;
     bool cow_timing = false, cow_timed = false;
     cudaEvent_t cow_events[2] = {nullptr, nullptr};
+    cudaEvent_t fwd_events[2] = {nullptr, nullptr};
+    mp_counters counters_total{};
+    uint64_t step_launches = 0, step_h2d = 0, step_d2h = 0;
     float cow_ms = 0.f;
     size_t off_tokens = 0, off_pos = 0, off_slot = 0, off_len = 0, off_splits = 0, off_work0 = 0, off_last = 0,
            off_work = 0, off_prefill = 0;
@@ -209,6 +212,8 @@ void free_context(mp_context* c) {
         if (p) cudaFreeHost(p);
     for (auto e : c->prof_events) cudaEventDestroy(e);
     for (auto e : c->cow_events)
+        if (e) cudaEventDestroy(e);
+    for (auto e : c->fwd_events)
         if (e) cudaEventDestroy(e);
     if (c->done) cudaEventDestroy(c->done);
     for (auto e : c->mark)
@@ -413,6 +418,7 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         c->meta_capacity = 6 * T + S + 4 * c->work_capacity + 8 * c->prefill_capacity + 2 * c->entry_capacity +
                            10 * c->region_capacity + 2;
         for (auto& e : c->cow_events) cuda_check(cudaEventCreate(&e), "create cow timing event");
+        for (auto& e : c->fwd_events) cuda_check(cudaEventCreate(&e), "create forward timing event");
         c->meta = device_alloc<int32_t>(c->meta_capacity, "step metadata");
         c->h_meta = host_alloc<int32_t>(c->meta_capacity, "step metadata staging");
         c->out_tokens = device_alloc<int32_t>(S, "greedy tokens");
@@ -602,6 +608,7 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
             std::memcpy(h + c->off_regions, regions, size_t(region_count) * sizeof(mp_tail_copy_region));
         const size_t bytes = (c->off_regions + 10 * size_t(region_count)) * 4;
         cuda_check(cudaMemcpyAsync(c->meta, h, bytes, cudaMemcpyHostToDevice, c->stream), "upload step metadata");
+        c->step_h2d = bytes;
         c->rows = T;
         c->seqs = count;
         c->work_count = int(W);
@@ -623,6 +630,12 @@ int mp_forward_launch(mp_context* c) {
         cudaStream_t st = c->stream;
         const int32_t* meta = c->meta;
         cuda_check(cudaMemsetAsync(c->error, 0, sizeof(unsigned), st), "reset error word");
+        cuda_check(cudaEventRecord(c->fwd_events[0], st), "forward timing");
+        // kernels of this forward: embed, per layer 8 (+1 norm after layer 0, +1 per
+        // attention kind present), final norm, head, argmax; table patch / COW if any
+        c->step_launches = uint64_t(c->entry_count > 0) + uint64_t(c->region_count > 0 && c->region_rows > 0) + 1 +
+                           uint64_t(m.layers) * (7 + uint64_t(c->prefill_count > 0) + uint64_t(c->work_count > 0)) +
+                           uint64_t(m.layers - 1) + 3;
         cuda_check(mpb::launch_table_patch(meta + c->off_entries, c->entry_count, c->tables,
                                            int64_t(r.max_sequences) * r.table_stride, c->error, st),
                    "table patch launch");
@@ -733,6 +746,7 @@ int mp_forward_launch(mp_context* c) {
                                          st),
                    "lm head gemm");
         cuda_check(mpb::launch_argmax(c->logits, S, m.vocabulary, c->out_tokens, c->out_finite, st), "argmax launch");
+        cuda_check(cudaEventRecord(c->fwd_events[1], st), "forward timing");
         if (c->profile) c->prof_bytes += c->plan.bytes * m.layers;
     });
 }
@@ -758,6 +772,16 @@ int mp_forward_collect(mp_context* c, int32_t* out_tokens, int32_t* out_finite, 
         cuda_check(cudaEventRecord(c->done, st), "record completion");
         wait_event(c->done, timeout_ms);
         if (c->profile) harvest_profile(c);
+        {
+            float ms = 0.f;
+            cuda_check(cudaEventElapsedTime(&ms, c->fwd_events[0], c->fwd_events[1]), "forward elapsed");
+            c->counters_total.forwards += 1;
+            c->counters_total.forward_ms += ms;
+            c->counters_total.kernel_launches += c->step_launches;
+            c->counters_total.h2d_bytes += c->step_h2d;
+            c->counters_total.d2h_bytes += size_t(S) * 8 + sizeof(unsigned) +
+                                           (out_logits ? size_t(S) * c->model.vocabulary * 4 : 0);
+        }
         if (c->cow_timed) {
             cuda_check(cudaEventElapsedTime(&c->cow_ms, c->cow_events[0], c->cow_events[1]), "cow elapsed");
             c->cow_timed = false;
@@ -854,6 +878,13 @@ int mp_timer_elapsed(mp_context* c, float* ms) {
         cuda_check(cudaEventSynchronize(b), "timer wait");
         cuda_check(cudaEventElapsedTime(ms, a, b), "timer elapsed");
     });
+}
+
+int mp_read_counters(mp_context* c, mp_counters* out, int32_t reset) {
+    if (!c || !out) return MP_ERR_INVALID;
+    *out = c->counters_total;
+    if (reset) c->counters_total = mp_counters{};
+    return MP_OK;
 }
 
 int mp_cow_timing(mp_context* c, int32_t enabled) {

@@ -551,4 +551,6 @@ int mph_engine_flushes(mph_engine* e, size_t* flushes, size_t* hazard_flushes) {
     return 0;
 }
 
+mp_context* mph_engine_device(mph_engine* e) { return e->b200 ? e->b200->device() : nullptr; }
+
 }  // extern "C"

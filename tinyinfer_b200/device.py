@@ -43,6 +43,11 @@ class SequenceDescC(C.Structure):
     _fields_ = [("slot", C.c_int32), ("start", C.c_int32), ("count", C.c_int32)]
 
 
+class CountersC(C.Structure):
+    _fields_ = [("forwards", C.c_uint64), ("forward_ms", C.c_double), ("kernel_launches", C.c_uint64),
+                ("h2d_bytes", C.c_uint64), ("d2h_bytes", C.c_uint64)]
+
+
 class TableEntryC(C.Structure):
     _fields_ = [("slot", C.c_int32), ("index", C.c_int32), ("block", C.c_int32)]
 
@@ -75,6 +80,7 @@ def library() -> C.CDLL:
         lib.mp_forward_prepare.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32,
                                            C.c_void_p, C.c_int32]
         lib.mp_cow_timing.argtypes = [C.c_void_p, C.c_int32]
+        lib.mp_read_counters.argtypes = [C.c_void_p, C.POINTER(CountersC), C.c_int32]
         lib.mp_cow_elapsed.argtypes = [C.c_void_p, C.POINTER(C.c_float)]
         lib.mp_forward_launch.argtypes = [C.c_void_p]
         lib.mp_forward_collect.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32]
@@ -232,6 +238,38 @@ class DeviceContext:
         ms, n, b = C.c_float(), C.c_int32(), C.c_double()
         check(self.lib.mp_profile_read(self.h, C.byref(ms), C.byref(n), C.byref(b)))
         return ms.value, n.value, b.value
+
+
+class ContextView:
+    """Timing and counters of a device context owned elsewhere (e.g. by an engine)."""
+
+    def __init__(self, handle):
+        self.lib = library()
+        self.h = C.c_void_p(handle)
+
+    def timer_mark(self) -> None:
+        check(self.lib.mp_timer_mark(self.h))
+
+    def timer_elapsed(self) -> float:
+        ms = C.c_float()
+        check(self.lib.mp_timer_elapsed(self.h, C.byref(ms)))
+        return ms.value
+
+    def profile(self, enabled: bool) -> None:
+        check(self.lib.mp_profile_enable(self.h, int(enabled)))
+
+    def profile_read(self):
+        ms, n, b = C.c_float(), C.c_int32(), C.c_double()
+        check(self.lib.mp_profile_read(self.h, C.byref(ms), C.byref(n), C.byref(b)))
+        return ms.value, n.value, b.value
+
+    def counters(self, reset: bool = False) -> dict:
+        out = CountersC()
+        check(self.lib.mp_read_counters(self.h, C.byref(out), int(reset)))
+        return {k: getattr(out, k) for k, _ in CountersC._fields_}
+
+    def sync(self, timeout_ms: int = 600000) -> None:
+        check(self.lib.mp_sync(self.h, timeout_ms))
 
 
 def paged_attention_decode(q_ptr: int, keys_ptr: int, values_ptr: int, layers: int, layer: int, block_tokens: int,

@@ -73,9 +73,9 @@ def library() -> C.CDLL:
             getattr(lib, name).restype = C.c_long
         for name in ("mph_kv_reserve", "mph_runner_reserve"):
             getattr(lib, name).argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
+        lib.mph_engine_device.restype = C.c_void_p
+        lib.mph_engine_device.argtypes = [C.c_void_p]
         lib.mph_engine_submit.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_int32, C.c_uint32, C.c_int32]
-        for name in dir(lib):
-            pass
         _lib = lib
     return _lib
 
@@ -432,3 +432,8 @@ class Engine(_Base):
 
     def script(self, id, tokens):
         self.runner.script(id, tokens)
+
+    def device(self):
+        """A device.ContextView of the engine's B200 context (None for other runners)."""
+        h = self.lib.mph_engine_device(self.h)
+        return _device.ContextView(h) if h else None
