@@ -42,7 +42,7 @@ METRIC = "decode tok/s, 135M FP32 paged-KV, batch 256/GPU, ctx 2k (shared 1032-t
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=128)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--requests", type=int, default=256)
@@ -95,7 +95,7 @@ def prompts(args, rank):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms while running."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -108,7 +108,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -146,7 +146,8 @@ class ClockSampler:
 
 
 def unique_decode_bytes(engine, ids, block_tokens):
-    """Distinct (page, slot) K/V rows the decode step reads, x 1536 B (shared pages once)."""
+    """Bytes of the distinct (page, slot) K/V rows one layer's decode attention reads
+    (each shared prefix page once), x 1536 B per token row."""
     seen = {}
     for rid in ids:
         s = engine.sequence(rid)
@@ -304,7 +305,7 @@ def run_b200(args, rank, world, local_rank):
     hbm, peak_kind = peaks()
     launch_ms = attn_ms / max(attn_launches, 1)
     bytes_per_launch = attn_bytes / max(attn_launches, 1)
-    unique_per_launch = uniq / args.layers
+    unique_per_launch = uniq
     achieved = bytes_per_launch / (launch_ms * 1e-3) / 1e9 if launch_ms > 0 else None
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "attention_decode_traffic.json")
