@@ -166,6 +166,22 @@ int mp_cow_elapsed(mp_context* ctx, float* milliseconds);
 int mp_paged_attention_decode(const float* q, const float* keys, const float* values, int32_t layers, int32_t layer,
                               int32_t block_tokens, int32_t max_blocks, const int32_t* tables, int32_t table_stride,
                               const int32_t* lengths, int32_t count, float* out, int32_t pages_per_split, void* stream);
+/* No counterpart in the reference. The same decode operator for callers that
+ * cannot allocate device memory -- e.g. a host embedding this library in another
+ * runtime that owns all GPU memory or fixes its budget up front, or a path where
+ * cudaMalloc/cudaFree must not run because they synchronise the device. It calls
+ * no allocator: its scratch is one file-scope __device__ array of about 5 MB held
+ * by every GPU that loads the library. At most 512 sequences and 2048 slices per
+ * call (pages_per_split 0 picks a slice length that fits); larger requests return
+ * MP_ERR_INVALID. All calls on a device share that array: calls whose device work
+ * overlaps race. The first call on a device, with that device current, looks up
+ * the array's address; make it before any stream capture. `device_error`
+ * (optional, caller-owned device word, zeroed by the caller) receives the kernel's
+ * error bits (1 = page id out of range, 2 = copy wait expired). */
+int mp_paged_attention_decode_noalloc(const float* q, const float* keys, const float* values, int32_t layers,
+                                      int32_t layer, int32_t block_tokens, int32_t max_blocks, const int32_t* tables,
+                                      int32_t table_stride, const int32_t* lengths, int32_t count, float* out,
+                                      int32_t pages_per_split, void* stream, uint32_t* device_error);
 /* Synchronises `stream`, then reads and clears the operator's device error word on
  * the current device: MP_OK, MP_ERR_BOUNDS (a page id outside [0, max_blocks)) or
  * MP_ERR_TIMEOUT (an in-kernel copy wait expired). */
