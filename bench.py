@@ -56,6 +56,8 @@ def parse():
     p.add_argument("--cpu-workers", type=int, default=0)
     p.add_argument("--cpu-context", type=int, default=512)
     p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--operator", action="store_true",
+                   help="time the paged-attention decode operator alone on BASELINE config 2")
     return p.parse_args()
 
 
@@ -265,7 +267,9 @@ def run_b200(args, rank, world, local_rank):
     for _ in range(args.warmup):
         decode_step()
     uniq = unique_decode_bytes(engine, ids, bt)
-    dev.counters(reset=True)
+    before = dev.counters(reset=True)
+    # kernels launched before the timed steps (for `ncu -s` on this command)
+    print(f"launches_before_timed={before['kernel_launches']}", file=sys.stderr, flush=True)
     dev.profile_read()
     dev.profile(True)
     if dist:
@@ -358,6 +362,73 @@ def run_b200(args, rank, world, local_rank):
     return line
 
 
+# ----------------------------------------------------------------------------- operator (config 2)
+def config2(seed=2, count=64, max_len=4096, block_tokens=16, pool=32768):
+    """64 sequences, lengths U[1, 4096], page 16, tables a random
+    permutation of a 32768-page one-layer pool, Q/K/V ~ N(0, 1)."""
+    rng = np.random.default_rng(seed)
+    lengths = rng.integers(1, max_len + 1, size=count).astype(np.int32)
+    pages = (lengths + block_tokens - 1) // block_tokens
+    perm = rng.permutation(pool).astype(np.int32)
+    tables = np.zeros((count, int(pages.max())), dtype=np.int32)
+    at = 0
+    for i, p in enumerate(pages):
+        tables[i, :p] = perm[at:at + p]
+        at += p
+    return lengths, tables, pool
+
+
+def run_operator(args, local_rank):
+    import torch
+
+    from tinyinfer_b200 import device
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    lengths, tables, pool = config2()
+    bt = 16
+    gen = torch.Generator(device=dev).manual_seed(2)
+    keys = torch.randn(pool * bt * 192, device=dev, generator=gen)
+    values = torch.randn(pool * bt * 192, device=dev, generator=gen)
+    q = torch.randn(len(lengths), 576, device=dev, generator=gen)
+    out = torch.empty_like(q)
+    tt = torch.from_numpy(tables).to(dev)
+    stream = torch.cuda.current_stream()
+    algorithmic = float(lengths.sum()) * 1536 + len(lengths) * 576 * 4 * 2 + float(((lengths + 15) // 16).sum()) * 4 + \
+        len(lengths) * 4
+
+    def launch():
+        device.paged_attention_decode(q.data_ptr(), keys.data_ptr(), values.data_ptr(), 1, 0, bt, pool, tt.data_ptr(),
+                                      tables.shape[1], lengths, out.data_ptr(), 0, stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        launch()
+    torch.cuda.synchronize()
+    times = []
+    with ClockSampler(local_rank) as clocks:
+        for _ in range(args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            launch()
+            b.record(stream)
+            times.append((a, b))
+        torch.cuda.synchronize()
+    assert device.paged_attention_status(stream.cuda_stream) == 0
+    ms = [a.elapsed_time(b) for a, b in times]
+    avg = sum(ms) / len(ms)
+    hbm, kind = peaks()
+    gbs = algorithmic / (avg * 1e-3) / 1e9
+    return {"metric": "paged-attention decode HBM GB/s (BASELINE config 2)", "value": gbs, "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": avg, "higher_is_better": True,
+            "dtype": "f32", "data": "synthetic (seeded N(0,1) Q/K/V)",
+            "config": {"workload": "config2: 64 sequences, lengths U[1,4096], 9q/3kv heads, d 64, page 16, "
+                                   "32768-page pool, random-permutation tables",
+                       "algorithmic_bytes": algorithmic, "l2": "inputs larger than L2 (201 MB per launch)"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "peak_kind": kind, "min_ms": min(ms), "max_ms": max(ms)},
+            "clocks": clocks.summary()}
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args, rank, world):
     if rank != 0:
@@ -387,6 +458,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         line = run_reference(args, rank, world)
+    elif args.operator:
+        line = run_operator(args, local_rank) if rank == 0 else None
     else:
         line = run_b200(args, rank, world, local_rank)
         if line is not None and world == 1 and not args.no_cpu_baseline:
