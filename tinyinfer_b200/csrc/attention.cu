@@ -47,6 +47,18 @@ struct Shared {
     uint64_t* bar;  // [kStages]
 };
 
+// Output element: plain FP32, or TF32 hi/lo halves when the caller asked for them.
+__device__ __forceinline__ void write_out(const AttnParams& p, size_t i, float v) {
+    if (p.out_lo) {
+        float h, l;
+        split_tf32(v, h, l);
+        p.out[i] = h;
+        p.out_lo[i] = l;
+    } else {
+        p.out[i] = v;
+    }
+}
+
 // Issue the copies for context tokens [a, b) into stage buffers (warp 0 only).
 __device__ __forceinline__ void issue_stage(const AttnParams& p, const int32_t* table, int a, int b, float* kdst,
                                             float* vdst, uint64_t* bar, int lane) {
@@ -215,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_kernel(const Attn
             const float total = acc[hh] + red[hh * kKvWidth + col];
             const int h = pkh * kGroup + hh, d = col % kHeadDim;
             if (splits == 1) {
-                p.out[size_t(row) * p.out_stride + h * kHeadDim + d] = total / s.l[h];
+                write_out(p, size_t(row) * p.out_stride + h * kHeadDim + d, total / s.l[h]);
             } else {
                 float* part = p.partial + (size_t(blockIdx.x) * kHeads + h) * (kHeadDim + 2);
                 part[2 + d] = total;
@@ -250,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_kernel(const Attn
             den = fmaf(__ldcg(part + 1), sc, den);
             num = fmaf(__ldcg(part + 2 + d), sc, num);
         }
-        p.out[size_t(row) * p.out_stride + o] = num / den;
+        write_out(p, size_t(row) * p.out_stride + o, num / den);
     }
     if (tid == 0) p.counters[row] = 0u;  // ready for the next launch
 }

@@ -196,12 +196,22 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_attention_kernel(const Pr
         const int r = v / kGroup, hh = v % kGroup;
         if (r >= rows) continue;
         const float den = alpha_s[v];
-        float* o = p.out + size_t(w.row0 + r) * p.out_stride + (kh * kGroup + hh) * kHeadDim + od;
-        float4 a, b;
-        a.x = acc[i][0] / den; a.y = acc[i][1] / den; a.z = acc[i][2] / den; a.w = acc[i][3] / den;
-        b.x = acc[i][4] / den; b.y = acc[i][5] / den; b.z = acc[i][6] / den; b.w = acc[i][7] / den;
-        *reinterpret_cast<float4*>(o) = a;
-        *reinterpret_cast<float4*>(o + 4) = b;
+        const size_t at = size_t(w.row0 + r) * p.out_stride + (kh * kGroup + hh) * kHeadDim + od;
+        float val[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) val[j] = acc[i][j] / den;
+        if (p.out_lo) {
+            float hi[8], lo[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) split_tf32(val[j], hi[j], lo[j]);
+            *reinterpret_cast<float4*>(p.out + at) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<float4*>(p.out + at + 4) = make_float4(hi[4], hi[5], hi[6], hi[7]);
+            *reinterpret_cast<float4*>(p.out_lo + at) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+            *reinterpret_cast<float4*>(p.out_lo + at + 4) = make_float4(lo[4], lo[5], lo[6], lo[7]);
+        } else {
+            *reinterpret_cast<float4*>(p.out + at) = make_float4(val[0], val[1], val[2], val[3]);
+            *reinterpret_cast<float4*>(p.out + at + 4) = make_float4(val[4], val[5], val[6], val[7]);
+        }
     }
 }
 

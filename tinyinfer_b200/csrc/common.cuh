@@ -76,6 +76,13 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
         : "memory");
 }
 
+// TF32 hi/lo split: hi keeps sign, exponent and the 10 leading mantissa bits
+// (exact in TF32), lo = x - hi is exact in FP32.
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+    hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+    lo = __fsub_rn(x, hi);
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -11,6 +11,9 @@
 #include <thread>
 #include <vector>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "kernels.h"
 #include "miniprefix_b200.h"
 
@@ -144,9 +147,14 @@ struct mp_context {
     cudaStream_t stream = nullptr;
     cudaEvent_t done = nullptr, mark[2] = {nullptr, nullptr};
     int mark_count = 0;
-    // weights, packed [N][K] (K contiguous)
-    float *embed = nullptr, *final_norm = nullptr, *head = nullptr, *in_norm = nullptr, *post_norm = nullptr;
-    float *wqkv = nullptr, *wo = nullptr, *wgate = nullptr, *wup = nullptr, *wdown = nullptr;
+    // weights: the embedding in FP32 (row gather), every GEMM operand packed [N][K]
+    // (K contiguous) as TF32 hi/lo halves; per-layer matrices stacked by layer
+    float *embed = nullptr, *final_norm = nullptr, *in_norm = nullptr, *post_norm = nullptr;
+    struct Split {
+        float* hi = nullptr;
+        float* lo = nullptr;
+    };
+    Split wqkv, wo, wgate, wup, wdown, head;
     std::set<std::string> received;
     bool finalized = false;
     // pools and tables
@@ -154,9 +162,16 @@ struct mp_context {
     uint64_t pool_elements = 0;
     int32_t* tables = nullptr;
     float *rope_cos = nullptr, *rope_sin = nullptr;
-    // workspace
-    float *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr;
-    float *xl = nullptr, *logits = nullptr, *partial = nullptr;
+    // workspace (GEMM inputs as hi/lo halves)
+    float *x = nullptr, *qkv = nullptr, *q = nullptr, *gate = nullptr, *logits = nullptr, *partial = nullptr;
+    Split xn, attn, h, xl;
+    // TMA tensor maps of every GEMM operand
+    struct alignas(64) Maps {
+        CUtensorMap xn_hi, xn_lo, attn_hi, attn_lo, h_hi, h_lo, xl_hi, xl_lo;
+        CUtensorMap wqkv_hi, wqkv_lo, wo_hi, wo_lo, wgate_hi, wgate_lo, wup_hi, wup_lo, wdown_hi, wdown_lo, head_hi,
+            head_lo;
+    };
+    Maps maps;
     unsigned *counters = nullptr, *error = nullptr;
     int32_t *meta = nullptr, *out_tokens = nullptr, *out_finite = nullptr, *cow = nullptr, *patch = nullptr;
     size_t meta_capacity = 0, work_capacity = 0;
@@ -195,18 +210,60 @@ namespace {
 
 size_t max_work(const mp_runtime_config& rt) { return size_t(rt.max_step_tokens) + 2048; }
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q{};
+        void* p = nullptr;
+        cuda_check(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q),
+                   "locate cuTensorMapEncodeTiled");
+        if (q != cudaDriverEntryPointSuccess || !p) fail(MP_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D fp32 map over a row-major [rows][cols] buffer, boxes of 32 columns (one
+// 128-byte swizzled row) x box_rows rows.
+void encode_map(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * sizeof(float)};
+    const cuuint32_t box[2] = {32, box_rows};
+    const cuuint32_t element_strides[2] = {1, 1};
+    const CUresult r = tensor_map_encoder()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                                            strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(MP_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+}
+
+// TF32 hi/lo halves on the host (same rule as the device split_tf32).
+void split_host(const float* x, float* hi, float* lo, size_t n) {
+    for (size_t i = 0; i < n; ++i) {
+        uint32_t b;
+        std::memcpy(&b, &x[i], 4);
+        b &= 0xFFFFE000u;
+        float h;
+        std::memcpy(&h, &b, 4);
+        hi[i] = h;
+        lo[i] = x[i] - h;
+    }
+}
+
 void free_context(mp_context* c) {
     if (!c) return;
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
-    for (void* p : {(void*)c->embed, (void*)c->final_norm, (void*)c->in_norm, (void*)c->post_norm, (void*)c->wqkv,
-                    (void*)c->wo, (void*)c->wgate, (void*)c->wup, (void*)c->wdown, (void*)c->keys, (void*)c->values,
-                    (void*)c->tables, (void*)c->rope_cos, (void*)c->rope_sin, (void*)c->x, (void*)c->xn,
-                    (void*)c->qkv, (void*)c->q, (void*)c->attn, (void*)c->h, (void*)c->xl, (void*)c->logits,
-                    (void*)c->partial, (void*)c->counters, (void*)c->error, (void*)c->meta, (void*)c->out_tokens,
-                    (void*)c->out_finite, (void*)c->cow, (void*)c->patch})
+    for (void* p : {(void*)c->embed, (void*)c->final_norm, (void*)c->in_norm, (void*)c->post_norm, (void*)c->keys,
+                    (void*)c->values, (void*)c->tables, (void*)c->rope_cos, (void*)c->rope_sin, (void*)c->x,
+                    (void*)c->qkv, (void*)c->q, (void*)c->gate, (void*)c->logits, (void*)c->partial,
+                    (void*)c->counters, (void*)c->error, (void*)c->meta, (void*)c->out_tokens, (void*)c->out_finite,
+                    (void*)c->cow, (void*)c->patch})
         if (p) cudaFree(p);
-    if (c->head && c->head != c->embed) cudaFree(c->head);
+    for (auto* s : {&c->wqkv, &c->wo, &c->wgate, &c->wup, &c->wdown, &c->head, &c->xn, &c->attn, &c->h, &c->xl}) {
+        if (s->hi) cudaFree(s->hi);
+        if (s->lo) cudaFree(s->lo);
+    }
     for (void* p : {(void*)c->h_meta, (void*)c->h_tokens, (void*)c->h_finite, (void*)c->h_error, (void*)c->h_patch,
                     (void*)c->h_cow})
         if (p) cudaFreeHost(p);
@@ -254,10 +311,12 @@ void validate_geometry(const mp_model_config& m, const mp_runtime_config& r) {
 }
 
 struct WeightSlot {
-    float* base;
-    int rows_n;  // N of the packed [N][K] matrix slice
-    int k;       // K
-    bool transpose;
+    float* base;     // fp32 destination (embedding, norms) or nullptr
+    float* hi;       // TF32 halves destination of a GEMM operand slice, or nullptr
+    float* lo;
+    int rows_n;      // N of the packed [N][K] matrix slice
+    int k;           // K
+    bool transpose;  // MPFX [K][N] -> packed [N][K]
     size_t elements;
 };
 
@@ -265,11 +324,12 @@ struct WeightSlot {
 WeightSlot resolve(mp_context* c, const std::string& name) {
     const auto& m = c->model;
     const int H = m.hidden, I = m.intermediate, kvw = c->kvw, V = m.vocabulary;
-    if (name == "model.embed_tokens.weight") return {c->embed, V, H, false, size_t(V) * H};
-    if (name == "model.norm.weight") return {c->final_norm, 1, H, false, size_t(H)};
+    if (name == "model.embed_tokens.weight")
+        return {c->embed, m.tied ? c->head.hi : nullptr, m.tied ? c->head.lo : nullptr, V, H, false, size_t(V) * H};
+    if (name == "model.norm.weight") return {c->final_norm, nullptr, nullptr, 1, H, false, size_t(H)};
     if (name == "lm_head.weight") {
         if (m.tied) fail(MP_ERR_INVALID, "tied model has no lm_head.weight");
-        return {c->head, V, H, true, size_t(V) * H};
+        return {nullptr, c->head.hi, c->head.lo, V, H, true, size_t(V) * H};
     }
     const std::string prefix = "model.layers.";
     if (name.compare(0, prefix.size(), prefix) != 0) fail(MP_ERR_INVALID, "unknown tensor: " + name);
@@ -284,18 +344,41 @@ WeightSlot resolve(mp_context* c, const std::string& name) {
     if (layer < 0 || layer >= m.layers) fail(MP_ERR_INVALID, "unknown tensor: " + name);
     const std::string s = name.substr(dot + 1);
     const size_t L = size_t(layer);
-    if (s == "input_layernorm.weight") return {c->in_norm + L * H, 1, H, false, size_t(H)};
-    if (s == "post_attention_layernorm.weight") return {c->post_norm + L * H, 1, H, false, size_t(H)};
-    float* qkv = c->wqkv + L * size_t(c->qkvw) * H;
-    if (s == "self_attn.q_proj.weight") return {qkv, H, H, true, size_t(H) * H};
-    if (s == "self_attn.k_proj.weight") return {qkv + size_t(H) * H, kvw, H, true, size_t(H) * kvw};
-    if (s == "self_attn.v_proj.weight") return {qkv + size_t(H + kvw) * H, kvw, H, true, size_t(H) * kvw};
-    if (s == "self_attn.o_proj.weight") return {c->wo + L * size_t(H) * H, H, H, true, size_t(H) * H};
-    if (s == "mlp.gate_proj.weight") return {c->wgate + L * size_t(I) * H, I, H, true, size_t(H) * I};
-    if (s == "mlp.up_proj.weight") return {c->wup + L * size_t(I) * H, I, H, true, size_t(H) * I};
-    if (s == "mlp.down_proj.weight") return {c->wdown + L * size_t(H) * I, H, I, true, size_t(I) * H};
+    if (s == "input_layernorm.weight") return {c->in_norm + L * H, nullptr, nullptr, 1, H, false, size_t(H)};
+    if (s == "post_attention_layernorm.weight")
+        return {c->post_norm + L * H, nullptr, nullptr, 1, H, false, size_t(H)};
+    auto slice = [](const mp_context::Split& s, size_t offset) { return std::pair<float*, float*>(s.hi + offset, s.lo + offset); };
+    const size_t qkv = L * size_t(c->qkvw) * H;
+    if (s == "self_attn.q_proj.weight") {
+        auto p = slice(c->wqkv, qkv);
+        return {nullptr, p.first, p.second, H, H, true, size_t(H) * H};
+    }
+    if (s == "self_attn.k_proj.weight") {
+        auto p = slice(c->wqkv, qkv + size_t(H) * H);
+        return {nullptr, p.first, p.second, kvw, H, true, size_t(H) * kvw};
+    }
+    if (s == "self_attn.v_proj.weight") {
+        auto p = slice(c->wqkv, qkv + size_t(H + kvw) * H);
+        return {nullptr, p.first, p.second, kvw, H, true, size_t(H) * kvw};
+    }
+    if (s == "self_attn.o_proj.weight") {
+        auto p = slice(c->wo, L * size_t(H) * H);
+        return {nullptr, p.first, p.second, H, H, true, size_t(H) * H};
+    }
+    if (s == "mlp.gate_proj.weight") {
+        auto p = slice(c->wgate, L * size_t(I) * H);
+        return {nullptr, p.first, p.second, I, H, true, size_t(H) * I};
+    }
+    if (s == "mlp.up_proj.weight") {
+        auto p = slice(c->wup, L * size_t(I) * H);
+        return {nullptr, p.first, p.second, I, H, true, size_t(H) * I};
+    }
+    if (s == "mlp.down_proj.weight") {
+        auto p = slice(c->wdown, L * size_t(H) * I);
+        return {nullptr, p.first, p.second, H, I, true, size_t(I) * H};
+    }
     fail(MP_ERR_INVALID, "unknown tensor: " + name);
-    return {};
+    return {nullptr, nullptr, nullptr, 0, 0, false, 0};
 }
 
 size_t expected_tensors(const mp_model_config& m) { return size_t(m.layers) * 9 + 2 + (m.tied ? 0 : 1); }
@@ -363,16 +446,21 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         cuda_check(mpb::configure_attention(), "configure attention kernel");
         cuda_check(mpb::configure_prefill_attention(), "configure prefill attention kernel");
         const size_t H = m.hidden, I = m.intermediate, L = m.layers, V = m.vocabulary;
+        cuda_check(mpb::configure_tc_gemm(), "configure tensor-core GEMM");
+        auto split = [](mp_context::Split& s, size_t n, const char* what) {
+            s.hi = device_alloc<float>(n, what);
+            s.lo = device_alloc<float>(n, what);
+        };
         c->embed = device_alloc<float>(V * H, "embedding");
         c->final_norm = device_alloc<float>(H, "final norm");
-        c->head = m.tied ? c->embed : device_alloc<float>(V * H, "lm head");
         c->in_norm = device_alloc<float>(L * H, "input norms");
         c->post_norm = device_alloc<float>(L * H, "post-attention norms");
-        c->wqkv = device_alloc<float>(L * c->qkvw * H, "qkv projections");
-        c->wo = device_alloc<float>(L * H * H, "o projections");
-        c->wgate = device_alloc<float>(L * I * H, "gate projections");
-        c->wup = device_alloc<float>(L * I * H, "up projections");
-        c->wdown = device_alloc<float>(L * H * I, "down projections");
+        split(c->head, V * H, "lm head");
+        split(c->wqkv, L * c->qkvw * H, "qkv projections");
+        split(c->wo, L * H * H, "o projections");
+        split(c->wgate, L * I * H, "gate projections");
+        split(c->wup, L * I * H, "up projections");
+        split(c->wdown, L * H * I, "down projections");
         c->pool_elements = uint64_t(r.max_blocks) * L * r.block_tokens * c->kvw;
         c->keys = device_alloc<float>(c->pool_elements, "K pool");
         c->values = device_alloc<float>(c->pool_elements, "V pool");
@@ -397,15 +485,42 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
             cuda_check(cudaMemcpy(c->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "upload rope cos");
             cuda_check(cudaMemcpy(c->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "upload rope sin");
         }
-        const size_t T = r.max_step_tokens, S = r.max_step_sequences;
+        // Row capacities rounded up to whole 128-row GEMM tiles: every TMA box of an
+        // activation operand then lies inside its allocation.
+        const size_t T = (size_t(r.max_step_tokens) + 127) / 128 * 128;
+        const size_t S = (size_t(r.max_step_sequences) + 127) / 128 * 128;
         c->x = device_alloc<float>(T * H, "residual stream");
-        c->xn = device_alloc<float>(T * H, "normed activations");
+        split(c->xn, T * H, "normed activations");
         c->qkv = device_alloc<float>(T * c->qkvw, "qkv activations");
         c->q = device_alloc<float>(T * H, "roped queries");
-        c->attn = device_alloc<float>(T * H, "attention output");
-        c->h = device_alloc<float>(T * I, "mlp activations");
-        c->xl = device_alloc<float>(S * H, "last-row activations");
+        split(c->attn, T * H, "attention output");
+        c->gate = device_alloc<float>(T * I, "gate activations");
+        split(c->h, T * I, "mlp activations");
+        split(c->xl, S * H, "last-row activations");
         c->logits = device_alloc<float>(S * V, "logits");
+        // TMA maps: activations in 128-row boxes (the A tile), weights in kTcBN-row boxes.
+        auto& mp = c->maps;
+        encode_map(&mp.xn_hi, c->xn.hi, T, H, 128);
+        encode_map(&mp.xn_lo, c->xn.lo, T, H, 128);
+        encode_map(&mp.attn_hi, c->attn.hi, T, H, 128);
+        encode_map(&mp.attn_lo, c->attn.lo, T, H, 128);
+        encode_map(&mp.h_hi, c->h.hi, T, I, 128);
+        encode_map(&mp.h_lo, c->h.lo, T, I, 128);
+        encode_map(&mp.xl_hi, c->xl.hi, S, H, 128);
+        encode_map(&mp.xl_lo, c->xl.lo, S, H, 128);
+        const uint32_t bn = mpb::kTcBN;
+        encode_map(&mp.wqkv_hi, c->wqkv.hi, L * c->qkvw, H, bn);
+        encode_map(&mp.wqkv_lo, c->wqkv.lo, L * c->qkvw, H, bn);
+        encode_map(&mp.wo_hi, c->wo.hi, L * H, H, bn);
+        encode_map(&mp.wo_lo, c->wo.lo, L * H, H, bn);
+        encode_map(&mp.wgate_hi, c->wgate.hi, L * I, H, bn);
+        encode_map(&mp.wgate_lo, c->wgate.lo, L * I, H, bn);
+        encode_map(&mp.wup_hi, c->wup.hi, L * I, H, bn);
+        encode_map(&mp.wup_lo, c->wup.lo, L * I, H, bn);
+        encode_map(&mp.wdown_hi, c->wdown.hi, L * H, I, bn);
+        encode_map(&mp.wdown_lo, c->wdown.lo, L * H, I, bn);
+        encode_map(&mp.head_hi, c->head.hi, V, H, bn);
+        encode_map(&mp.head_lo, c->head.lo, V, H, bn);
         c->work_capacity = max_work(r);
         c->partial = device_alloc<float>(c->work_capacity * mpb::kHeads * (mpb::kHeadDim + 2), "attention partials");
         c->counters = device_alloc<unsigned>(T, "attention counters");
@@ -444,15 +559,22 @@ int mp_set_weight(mp_context* c, const char* name, const float* host, size_t ele
         cuda_check(cudaSetDevice(c->device), "select device");
         const WeightSlot slot = resolve(c, name);
         if (elements != slot.elements) fail(MP_ERR_INVALID, std::string("tensor shape mismatch: ") + name);
-        if (!slot.transpose) {
-            cuda_check(cudaMemcpy(slot.base, host, elements * 4, cudaMemcpyHostToDevice), "upload weight");
-        } else {
-            // MPFX stores [K][N] ([in][out]); the kernels read [N][K].
-            const int N = slot.rows_n, K = slot.k;
-            std::vector<float> t(elements);
-            for (int k = 0; k < K; ++k)
-                for (int n = 0; n < N; ++n) t[size_t(n) * K + k] = host[size_t(k) * N + n];
-            cuda_check(cudaMemcpy(slot.base, t.data(), elements * 4, cudaMemcpyHostToDevice), "upload weight");
+        if (slot.base) cuda_check(cudaMemcpy(slot.base, host, elements * 4, cudaMemcpyHostToDevice), "upload weight");
+        if (slot.hi) {
+            // MPFX stores [K][N] ([in][out]); the GEMM reads [N][K] as TF32 halves.
+            std::vector<float> t;
+            const float* packed = host;
+            if (slot.transpose) {
+                const int N = slot.rows_n, K = slot.k;
+                t.resize(elements);
+                for (int k = 0; k < K; ++k)
+                    for (int n = 0; n < N; ++n) t[size_t(n) * K + k] = host[size_t(k) * N + n];
+                packed = t.data();
+            }
+            std::vector<float> hi(elements), lo(elements);
+            split_host(packed, hi.data(), lo.data(), elements);
+            cuda_check(cudaMemcpy(slot.hi, hi.data(), elements * 4, cudaMemcpyHostToDevice), "upload weight");
+            cuda_check(cudaMemcpy(slot.lo, lo.data(), elements * 4, cudaMemcpyHostToDevice), "upload weight");
         }
         c->received.insert(name);
         c->finalized = false;
@@ -647,8 +769,27 @@ int mp_forward_launch(mp_context* c) {
                    "cow launch");
         if (c->cow_timed) cuda_check(cudaEventRecord(c->cow_events[1], st), "cow timing");
         cuda_check(mpb::launch_embed_rmsnorm(meta + c->off_tokens, c->embed, m.vocabulary, c->in_norm, m.rms_epsilon,
-                                             c->x, c->xn, T, H, c->error, st),
+                                             c->x, c->xn.hi, c->xn.lo, T, H, c->error, st),
                    "embed launch");
+        const auto& mp = c->maps;
+        auto gemm = [&](const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
+                        const CUtensorMap& b_lo, int rows, int n, int k, int b_row0, float* out, int ldc,
+                        mpb::Epilogue e, const char* what) {
+            mpb::TcGemmParams g{};
+            g.m = rows;
+            g.n = n;
+            g.k = k;
+            g.b_row0 = b_row0;
+            g.c = out;
+            g.ldc = ldc;
+            g.gate = c->gate;
+            g.ld_gate = I;
+            g.out_hi = c->h.hi;
+            g.out_lo = c->h.lo;
+            g.ld_out = I;
+            g.error = c->error;
+            cuda_check(mpb::launch_tc_gemm({&a_hi, &a_lo, &b_hi, &b_lo}, g, e, st), what);
+        };
         mpb::AttnParams ap{};
         ap.q = c->q;
         ap.q_stride = H;
@@ -667,7 +808,8 @@ int mp_forward_launch(mp_context* c) {
         ap.work_count = c->work_count;
         ap.partial = c->partial;
         ap.counters = c->counters;
-        ap.out = c->attn;
+        ap.out = c->attn.hi;
+        ap.out_lo = c->attn.lo;
         ap.out_stride = H;
         ap.error = c->error;
         mpb::PrefillParams pp{};
@@ -682,7 +824,8 @@ int mp_forward_launch(mp_context* c) {
         pp.table_stride = r.table_stride;
         pp.work = reinterpret_cast<const mpb::PrefillWork*>(meta + c->off_prefill);
         pp.work_count = c->prefill_count;
-        pp.out = c->attn;
+        pp.out = c->attn.hi;
+        pp.out_lo = c->attn.lo;
         pp.out_stride = H;
         pp.error = c->error;
         mpb::RopeAppendArgs ra{};
@@ -707,12 +850,11 @@ int mp_forward_launch(mp_context* c) {
         for (int l = 0; l < m.layers; ++l) {
             const size_t L = size_t(l);
             if (l > 0)
-                cuda_check(mpb::launch_rmsnorm(c->x, nullptr, c->in_norm + L * H, m.rms_epsilon, c->xn, T, H, st),
+                cuda_check(mpb::launch_rmsnorm(c->x, nullptr, c->in_norm + L * H, m.rms_epsilon, c->xn.hi, c->xn.lo,
+                                               T, H, st),
                            "rmsnorm launch");
-            cuda_check(mpb::launch_gemm_simt({c->xn, H, c->wqkv + L * c->qkvw * H, H, c->qkv, c->qkvw, T, c->qkvw, H,
-                                              mpb::Epilogue::Store},
-                                             st),
-                       "qkv gemm");
+            gemm(mp.xn_hi, mp.xn_lo, mp.wqkv_hi, mp.wqkv_lo, T, c->qkvw, H, l * c->qkvw, c->qkv, c->qkvw,
+                 mpb::Epilogue::Store, "qkv gemm");
             ra.layer = l;
             cuda_check(mpb::launch_rope_append(ra, st), "rope/append launch");
             ap.layer = l;
@@ -721,30 +863,22 @@ int mp_forward_launch(mp_context* c) {
             cuda_check(mpb::launch_prefill_attention(pp, st), "prefill attention launch");
             cuda_check(mpb::launch_paged_attention(ap, st), "attention launch");
             if (c->profile) record_attention_event(c);
-            cuda_check(mpb::launch_gemm_simt({c->attn, H, c->wo + L * H * H, H, c->x, H, T, H, H, mpb::Epilogue::AddTo},
-                                             st),
-                       "o gemm");
-            cuda_check(mpb::launch_rmsnorm(c->x, nullptr, c->post_norm + L * H, m.rms_epsilon, c->xn, T, H, st),
+            gemm(mp.attn_hi, mp.attn_lo, mp.wo_hi, mp.wo_lo, T, H, H, l * H, c->x, H, mpb::Epilogue::AddTo, "o gemm");
+            cuda_check(mpb::launch_rmsnorm(c->x, nullptr, c->post_norm + L * H, m.rms_epsilon, c->xn.hi, c->xn.lo, T,
+                                           H, st),
                        "rmsnorm launch");
-            cuda_check(mpb::launch_gemm_simt({c->xn, H, c->wgate + L * size_t(I) * H, H, c->h, I, T, I, H,
-                                              mpb::Epilogue::Store},
-                                             st),
-                       "gate gemm");
-            cuda_check(mpb::launch_gemm_simt({c->xn, H, c->wup + L * size_t(I) * H, H, c->h, I, T, I, H,
-                                              mpb::Epilogue::SiluMul},
-                                             st),
-                       "up gemm");
-            cuda_check(mpb::launch_gemm_simt({c->h, I, c->wdown + L * size_t(H) * I, I, c->x, H, T, H, I,
-                                              mpb::Epilogue::AddTo},
-                                             st),
-                       "down gemm");
+            gemm(mp.xn_hi, mp.xn_lo, mp.wgate_hi, mp.wgate_lo, T, I, H, l * I, c->gate, I, mpb::Epilogue::Store,
+                 "gate gemm");
+            gemm(mp.xn_hi, mp.xn_lo, mp.wup_hi, mp.wup_lo, T, I, H, l * I, nullptr, I, mpb::Epilogue::SiluMul,
+                 "up gemm");
+            gemm(mp.h_hi, mp.h_lo, mp.wdown_hi, mp.wdown_lo, T, H, I, l * H, c->x, H, mpb::Epilogue::AddTo,
+                 "down gemm");
         }
-        cuda_check(mpb::launch_rmsnorm(c->x, meta + c->off_last, c->final_norm, m.rms_epsilon, c->xl, S, H, st),
+        cuda_check(mpb::launch_rmsnorm(c->x, meta + c->off_last, c->final_norm, m.rms_epsilon, c->xl.hi, c->xl.lo, S,
+                                       H, st),
                    "final norm launch");
-        cuda_check(mpb::launch_gemm_simt({c->xl, H, c->head, H, c->logits, m.vocabulary, S, m.vocabulary, H,
-                                          mpb::Epilogue::Store},
-                                         st),
-                   "lm head gemm");
+        gemm(mp.xl_hi, mp.xl_lo, mp.head_hi, mp.head_lo, S, m.vocabulary, H, 0, c->logits, m.vocabulary,
+             mpb::Epilogue::Store, "lm head gemm");
         cuda_check(mpb::launch_argmax(c->logits, S, m.vocabulary, c->out_tokens, c->out_finite, st), "argmax launch");
         cuda_check(cudaEventRecord(c->fwd_events[1], st), "forward timing");
         if (c->profile) c->prof_bytes += c->plan.bytes * m.layers;
@@ -915,6 +1049,55 @@ int mp_profile_read(mp_context* c, float* attention_ms, int32_t* launches, doubl
     c->prof_launches = 0;
     c->prof_bytes = 0;
     return MP_OK;
+}
+
+// C = A . B^T through the 3xTF32 tensor-core GEMM on caller device buffers (a [m][k],
+// b [n][k], c [m][n], row-major). Allocates and frees its own hi/lo scratch and
+// synchronises `stream`; meant for tests and tools, not for the hot path.
+int mp_gemm_f32(const float* a, const float* b, float* out, int32_t m, int32_t n, int32_t k, void* stream_ptr) {
+    std::vector<float*> scratch;
+    cudaStream_t st = static_cast<cudaStream_t>(stream_ptr);
+    const int rc = guarded([&] {
+        if (!a || !b || !out || m < 1 || n < 1 || k < 1) fail(MP_ERR_INVALID, "invalid argument");
+        if (n % mpb::kTcBN || k % 32) fail(MP_ERR_INVALID, "n must be a multiple of 64 and k of 32");
+        cuda_check(mpb::configure_tc_gemm(), "configure tensor-core GEMM");
+        const size_t rows_a = (size_t(m) + 127) / 128 * 128, rows_b = size_t(n);
+        auto alloc = [&](size_t count) {
+            float* p = device_alloc<float>(count, "gemm scratch");
+            scratch.push_back(p);
+            cuda_check(cudaMemsetAsync(p, 0, count * 4, st), "clear gemm scratch");
+            return p;
+        };
+        float *ah = alloc(rows_a * k), *al = alloc(rows_a * k), *bh = alloc(rows_b * k), *bl = alloc(rows_b * k);
+        cuda_check(mpb::launch_split(a, ah, al, size_t(m) * k, st), "split a");
+        cuda_check(mpb::launch_split(b, bh, bl, size_t(n) * k, st), "split b");
+        struct alignas(64) M4 {
+            CUtensorMap ah, al, bh, bl;
+        };
+        auto maps = std::make_unique<M4>();
+        encode_map(&maps->ah, ah, rows_a, k, 128);
+        encode_map(&maps->al, al, rows_a, k, 128);
+        encode_map(&maps->bh, bh, rows_b, k, mpb::kTcBN);
+        encode_map(&maps->bl, bl, rows_b, k, mpb::kTcBN);
+        unsigned* err = device_alloc<unsigned>(1, "gemm error word");
+        scratch.push_back(reinterpret_cast<float*>(err));
+        cuda_check(cudaMemsetAsync(err, 0, 4, st), "clear error word");
+        mpb::TcGemmParams g{};
+        g.m = m;
+        g.n = n;
+        g.k = k;
+        g.c = out;
+        g.ldc = n;
+        g.error = err;
+        cuda_check(mpb::launch_tc_gemm({&maps->ah, &maps->al, &maps->bh, &maps->bl}, g, mpb::Epilogue::Store, st),
+                   "gemm launch");
+        unsigned herr = 0;
+        cuda_check(cudaMemcpyAsync(&herr, err, 4, cudaMemcpyDeviceToHost, st), "read error word");
+        cuda_check(cudaStreamSynchronize(st), "gemm completion");
+        if (herr) fail(MP_ERR_TIMEOUT, "tensor-core GEMM wait expired");
+    });
+    for (float* p : scratch) cudaFree(p);
+    return rc;
 }
 
 }  // extern "C"

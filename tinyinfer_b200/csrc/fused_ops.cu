@@ -17,7 +17,8 @@ namespace {
 // One warp per row. Sum of squares by per-lane partials and a butterfly; the
 // normalisation order matches the CPU runner: (x * scale) * w
 // (miniprefix/src/backend/cpu/llama_runner.cpp:10-16).
-__device__ __forceinline__ void rms_row(const float* x, const float* w, float eps, float* out, int hidden, int lane) {
+__device__ __forceinline__ void rms_row(const float* x, const float* w, float eps, float* out_hi, float* out_lo,
+                                        int hidden, int lane) {
     float sum = 0.f;
     for (int d = lane * 4; d < hidden; d += 128) {
         const float4 v = *reinterpret_cast<const float4*>(x + d);
@@ -31,17 +32,19 @@ __device__ __forceinline__ void rms_row(const float* x, const float* w, float ep
     for (int d = lane * 4; d < hidden; d += 128) {
         const float4 v = *reinterpret_cast<const float4*>(x + d);
         const float4 g = *reinterpret_cast<const float4*>(w + d);
-        float4 r;
-        r.x = __fmul_rn(__fmul_rn(v.x, scale), g.x);
-        r.y = __fmul_rn(__fmul_rn(v.y, scale), g.y);
-        r.z = __fmul_rn(__fmul_rn(v.z, scale), g.z);
-        r.w = __fmul_rn(__fmul_rn(v.w, scale), g.w);
-        *reinterpret_cast<float4*>(out + d) = r;
+        float4 h, l;
+        split_tf32(__fmul_rn(__fmul_rn(v.x, scale), g.x), h.x, l.x);
+        split_tf32(__fmul_rn(__fmul_rn(v.y, scale), g.y), h.y, l.y);
+        split_tf32(__fmul_rn(__fmul_rn(v.z, scale), g.z), h.z, l.z);
+        split_tf32(__fmul_rn(__fmul_rn(v.w, scale), g.w), h.w, l.w);
+        *reinterpret_cast<float4*>(out_hi + d) = h;
+        *reinterpret_cast<float4*>(out_lo + d) = l;
     }
 }
 
 __global__ void embed_rmsnorm_kernel(const int32_t* tokens, const float* embed, int vocabulary, const float* w,
-                                     float eps, float* x, float* normed, int rows, int hidden, unsigned* error) {
+                                     float eps, float* x, float* normed_hi, float* normed_lo, int rows, int hidden,
+                                     unsigned* error) {
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
     if (row >= rows) return;
     int tok = tokens[row];
@@ -54,15 +57,15 @@ __global__ void embed_rmsnorm_kernel(const int32_t* tokens, const float* embed, 
     for (int d = lane * 4; d < hidden; d += 128)
         *reinterpret_cast<float4*>(xr + d) = *reinterpret_cast<const float4*>(src + d);
     __syncwarp();
-    rms_row(xr, w, eps, normed + size_t(row) * hidden, hidden, lane);
+    rms_row(xr, w, eps, normed_hi + size_t(row) * hidden, normed_lo + size_t(row) * hidden, hidden, lane);
 }
 
-__global__ void rmsnorm_kernel(const float* x, const int32_t* rows, const float* w, float eps, float* out, int count,
-                               int hidden) {
+__global__ void rmsnorm_kernel(const float* x, const int32_t* rows, const float* w, float eps, float* out_hi,
+                               float* out_lo, int count, int hidden) {
     const int i = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
     if (i >= count) return;
     const int r = rows ? rows[i] : i;
-    rms_row(x + size_t(r) * hidden, w, eps, out + size_t(i) * hidden, hidden, lane);
+    rms_row(x + size_t(r) * hidden, w, eps, out_hi + size_t(i) * hidden, out_lo + size_t(i) * hidden, hidden, lane);
 }
 
 // One CTA of 384 threads per row: threads 0..287 rotate the 9 q heads' 32 pairs,
@@ -207,18 +210,18 @@ __global__ void table_patch_kernel(const int32_t* pairs, int count, int32_t* tab
 }  // namespace
 
 cudaError_t launch_embed_rmsnorm(const int32_t* tokens, const float* embed, int vocabulary, const float* norm_w,
-                                 float eps, float* x, float* normed, int rows, int hidden, unsigned* error,
-                                 cudaStream_t stream) {
+                                 float eps, float* x, float* normed_hi, float* normed_lo, int rows, int hidden,
+                                 unsigned* error, cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
-    embed_rmsnorm_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(tokens, embed, vocabulary, norm_w, eps, x, normed, rows,
-                                                            hidden, error);
+    embed_rmsnorm_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(tokens, embed, vocabulary, norm_w, eps, x, normed_hi,
+                                                            normed_lo, rows, hidden, error);
     return cudaGetLastError();
 }
 
-cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, float* out, int count,
-                           int hidden, cudaStream_t stream) {
+cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, float* out_hi,
+                           float* out_lo, int count, int hidden, cudaStream_t stream) {
     if (count <= 0) return cudaSuccess;
-    rmsnorm_kernel<<<(count + 7) / 8, 256, 0, stream>>>(x, rows, norm_w, eps, out, count, hidden);
+    rmsnorm_kernel<<<(count + 7) / 8, 256, 0, stream>>>(x, rows, norm_w, eps, out_hi, out_lo, count, hidden);
     return cudaGetLastError();
 }
 

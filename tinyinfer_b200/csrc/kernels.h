@@ -48,7 +48,8 @@ struct AttnParams {
     int work_count;
     float* partial;      // [work_count][9][66] slice results (rows with >1 slice)
     unsigned* counters;  // [rows] zero between launches
-    float* out;          // [rows][out_stride]
+    float* out;          // [rows][out_stride]; the TF32 hi half when out_lo is set
+    float* out_lo;       // optional: lo halves (GEMM input), same layout
     int out_stride;
     unsigned* error;
 };
@@ -74,6 +75,7 @@ struct PrefillParams {
     const PrefillWork* work;
     int work_count;
     float* out;
+    float* out_lo;  // optional lo halves, as in AttnParams
     int out_stride;
     unsigned* error;
 };
@@ -98,27 +100,43 @@ enum class Epilogue : int {
     SiluMul = 2,  // C = silu(C) * acc  (C holds the gate projection)
 };
 
-struct GemmArgs {
-    const float* a;
-    int lda;
-    const float* b;
-    int ldb;
+// Tensor-core 3xTF32 GEMM (tc_gemm.cu). A and B come as TF32 hi/lo halves through
+// 2-D TMA tensor maps (fp32, rows x K, 128-byte swizzle, boxes of 32 x 128 rows
+// for A and 32 x kTcBN rows for B); B's rows start at b_row0 (stacked per-layer
+// weights). Epilogues: Store / AddTo into c; SiluMul reads gate and writes the
+// product as hi/lo halves (out_hi, out_lo).
+constexpr int kTcBN = 64;
+struct TcGemmMaps {
+    const struct CUtensorMap_st* a_hi;
+    const struct CUtensorMap_st* a_lo;
+    const struct CUtensorMap_st* b_hi;
+    const struct CUtensorMap_st* b_lo;
+};
+struct TcGemmParams {
+    int m, n, k;
+    int b_row0;
     float* c;
     int ldc;
-    int m, n, k;
-    Epilogue epilogue;
+    const float* gate;
+    int ld_gate;
+    float* out_hi;
+    float* out_lo;
+    int ld_out;
+    unsigned* error;
 };
-
-cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t stream);
+cudaError_t configure_tc_gemm();
+cudaError_t launch_tc_gemm(const TcGemmMaps& maps, const TcGemmParams& p, Epilogue e, cudaStream_t stream);
+// hi = x with the 13 low mantissa bits cleared, lo = x - hi, elementwise.
+cudaError_t launch_split(const float* x, float* hi, float* lo, size_t n, cudaStream_t stream);
 
 // ---------------------------------------------------------------- fused small ops
-// x[r][:] = embed[tokens[r]][:]; out[r][:] = rmsnorm(x[r]) * w (both written).
+// x[r][:] = embed[tokens[r]][:]; rmsnorm(x[r]) * w written as TF32 hi/lo halves.
 cudaError_t launch_embed_rmsnorm(const int32_t* tokens, const float* embed, int vocabulary, const float* norm_w,
-                                 float eps, float* x, float* normed, int rows, int hidden, unsigned* error,
-                                 cudaStream_t stream);
-// out[i][:] = rmsnorm(x[rows ? rows[i] : i]) * w for i < count.
-cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, float* out,
-                           int count, int hidden, cudaStream_t stream);
+                                 float eps, float* x, float* normed_hi, float* normed_lo, int rows, int hidden,
+                                 unsigned* error, cudaStream_t stream);
+// rmsnorm(x[rows ? rows[i] : i]) * w as hi/lo halves into out_hi/out_lo[i] for i < count.
+cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, float* out_hi,
+                           float* out_lo, int count, int hidden, cudaStream_t stream);
 // Split-half RoPE of q and k from qkv[r][960] with host-computed cos/sin tables
 // [position][32]; writes roped q to q_out[r][576] and k, v rows into the pools.
 struct RopeAppendArgs {

@@ -98,6 +98,7 @@ def library() -> C.CDLL:
                                                   C.c_int32, C.c_void_p, C.c_int32, C.c_void_p, C.c_int32,
                                                   C.c_void_p, C.c_int32, C.c_void_p]
         lib.mp_paged_attention_status.argtypes = [C.c_void_p]
+        lib.mp_gemm_f32.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p]
         _lib = lib
     return _lib
 
@@ -281,6 +282,11 @@ def paged_attention_decode(q_ptr: int, keys_ptr: int, values_ptr: int, layers: i
     check(lib.mp_paged_attention_decode(q_ptr, keys_ptr, values_ptr, layers, layer, block_tokens, max_blocks,
                                         tables_ptr, table_stride, _ptr(lens), len(lens), out_ptr, pages_per_split,
                                         stream))
+
+
+def gemm_f32(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, stream: int | None = None) -> None:
+    """C = A . B^T on device buffers through the 3xTF32 tensor-core GEMM (test/tool entry)."""
+    check(library().mp_gemm_f32(a_ptr, b_ptr, c_ptr, m, n, k, stream))
 
 
 def paged_attention_status(stream: int | None = None) -> int:
