@@ -1,10 +1,11 @@
 """The 3xTF32 tcgen05 GEMM alone vs float64 numpy: C = A . B^T.
 
-3xTF32 keeps FP32-level accuracy. Per product the dropped a_lo.b_lo term and the
-TF32 truncation of the lo halves are below ~3 x 2^-20 relative and of random
-sign, so per element |gpu - exact| stays far below 2^-20 * sum_k |a_k b_k|; plain
-TF32 (2^-11 relative per product) lands around 2^-12 / sqrt(k) of that sum --
-above the bound for every k tested here.
+Two checks per shape, on the worst element's |gpu - exact| / sum_k |a_k b_k|:
+  * absolute: at most 2^-18 (about 4e-6);
+  * against plain TF32 (both operands truncated to TF32, computed in float64
+    here): the 3xTF32 error must be at least 8x smaller -- the split must buy
+    back the precision TF32 drops. (The remaining error is dominated by the
+    tensor core's FP32 accumulation, and grows slowly with K.)
 """
 import numpy as np
 import pytest
@@ -30,5 +31,11 @@ def test_tc_gemm_matches_float64(built, m, n, k):
     err = np.abs(got - exact)
     assert np.isfinite(got).all()
     worst = float((err / scale).max())
-    print(f"m={m} n={n} k={k}: max |err| / sum|ab| = {worst:.3e}")
-    assert worst <= 2.0 ** -20, worst
+
+    def tf32(x):
+        return (x.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32).astype(np.float64)
+
+    plain = float((np.abs(tf32(a) @ tf32(b).T - exact) / scale).max())
+    print(f"m={m} n={n} k={k}: 3xTF32 {worst:.3e}  plain TF32 {plain:.3e}")
+    assert worst <= 2.0 ** -18, worst
+    assert worst * 8 <= plain, (worst, plain)
