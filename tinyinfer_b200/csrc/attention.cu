@@ -10,16 +10,17 @@
 //  * A CTA owns one slice [page_begin, page_end) of one query row's context. A row
 //    with more than one slice is merged by the last slice to finish (arrival
 //    counter per row), so one launch produces the final output.
-//  * K and V of 32 consecutive tokens form one stage. Runs of tokens that are
+//  * K and V of 16 consecutive tokens form one stage. Runs of tokens that are
 //    contiguous inside a page (a page is [slot][192] floats for one layer) are
 //    moved by the bulk-copy engine (cp.async.bulk) into shared memory and
 //    complete on a per-stage mbarrier, so 2 stages stay in flight while one is
 //    consumed. Each K/V byte is read from HBM once for all 3 q heads of its group.
-//  * Scores: 96 (token, kv head) pairs x 4 lanes; each lane keeps its 3 heads'
+//    192 threads and ~75 KB of shared memory let 3 CTAs share an SM.
+//  * Scores: 48 (token, kv head) pairs x 4 lanes; each lane keeps its 3 heads'
 //    16 query values in registers and dots one 64-byte quarter of the key row,
 //    quarters rotated by pair parity so the 8 lanes of a 128-bit phase hit
-//    distinct banks. Softmax: one warp per head, online (running max / sum).
-//    P.V: 2 token halves x 192 (kv head, dim) columns, 3 heads per thread.
+//    distinct banks. Softmax: 16 lanes per head, online (running max / sum).
+//    P.V: one (kv head, dim) column per thread, 3 heads.
 //  * Tokens past the row length are masked by select (never by multiplying), so
 //    stale or uninitialised shared memory cannot leak NaN into the result.
 #include "common.cuh"
@@ -28,8 +29,8 @@
 namespace mpb {
 namespace {
 
-constexpr int kStageTokens = 32;
-constexpr int kThreads = 384;
+constexpr int kStageTokens = 16;
+constexpr int kThreads = 192;  // 48 (token, kv head) pairs x 4 lanes; 192 (kv head, dim) columns
 constexpr int kStages = 3;
 constexpr int kStageFloats = kStageTokens * kKvWidth;  // per pool
 constexpr size_t kAttnSmem = size_t(kStages) * 2 * kStageFloats * sizeof(float) +
@@ -38,8 +39,8 @@ constexpr size_t kAttnSmem = size_t(kStages) * 2 * kStageFloats * sizeof(float) 
 
 struct Shared {
     float* stages;  // stage i: K at stages + 2*i*kStageFloats, V right after
-    float* scores;  // [9][32]
-    float* probs;   // [9][32]
+    float* scores;  // [9][16]
+    float* probs;   // [9][16]
     float* alpha;   // [9]
     float* m;       // [9]
     float* l;       // [9]
@@ -82,7 +83,7 @@ __device__ __forceinline__ void issue_stage(const AttnParams& p, const int32_t* 
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) paged_attention_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(kThreads, 3) paged_attention_kernel(const AttnParams p) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     Shared s;
     {
@@ -119,7 +120,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_kernel(const Attn
                         s.stages + (2 * i + 1) * kStageFloats, &s.bar[i], lane);
         }
 
-    // Score-phase identity: pair = (token t, kv head kh), 4 lanes per pair.
+    // Score identity: pair = (token st, kv head skh), 4 lanes per pair; each lane
+    // holds its kv group's 3 heads x 16 query values (4 of the 16 float4 chunks of
+    // a 64-dim row, rotated by pair parity so a 128-bit phase hits distinct banks).
     const int pair = tid >> 2, sub = tid & 3;
     const int st = pair / kKvHeads, skh = pair % kKvHeads, rot = pair & 1;
     float4 qr[kGroup][4];
@@ -133,17 +136,18 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_kernel(const Attn
                 qr[hh][j] = *reinterpret_cast<const float4*>(qrow + (skh * kGroup + hh) * kHeadDim + 4 * chunk);
             }
     }
-    // P.V identity: token half, column (kv head, dim).
-    const int half = tid / kKvWidth, col = tid % kKvWidth, pkh = col / kHeadDim;
+    // Softmax identity: 16 lanes per head (two heads per warp, warps 0..4).
+    const int shead = warp * 2 + (lane >> 4), stok = lane & 15;
+    // P.V identity: one (kv head, dim) column per thread, 3 heads.
+    const int pkh = tid / kHeadDim;
     float acc[kGroup] = {0.f, 0.f, 0.f};
-    float m_run = -INFINITY, l_run = 0.f;  // meaningful in warps 0..8 (head = warp)
+    float m_run = -INFINITY, l_run = 0.f;  // of head `shead`
 
     for (int i = 0; i < n_stages; ++i) {
         const int stage = i % kStages;
         const int a = tok_begin + i * kStageTokens;
         const int n_valid = min(kStageTokens, tok_end - a);
         if (!mbar_wait_bounded(&s.bar[stage], (i / kStages) & 1)) s.flag[0] = 1;
-        // scores
         {
             const float* krow = s.stages + 2 * stage * kStageFloats + st * kKvWidth + skh * kHeadDim;
             float part[kGroup] = {0.f, 0.f, 0.f};
@@ -171,30 +175,37 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_kernel(const Attn
         }
         __syncthreads();
         if (s.flag[0]) break;
-        // online softmax, one warp per head
-        if (warp < kHeads) {
-            const float sc = s.scores[warp * kStageTokens + lane];
-            const float m_new = fmaxf(m_run, warp_max(sc));
-            const float alpha = expf(m_run - m_new);
-            const float pr = expf(sc - m_new);
-            l_run = l_run * alpha + warp_sum(pr);
-            m_run = m_new;
-            s.probs[warp * kStageTokens + lane] = pr;
-            if (lane == 0) s.alpha[warp] = alpha;
+        if (warp < 5) {
+            // all 32 lanes take part in the shuffles; heads >= 9 use a dummy row
+            const bool live = shead < kHeads;
+            const float sc = live ? s.scores[shead * kStageTokens + stok] : -INFINITY;
+            float mx = sc;
+#pragma unroll
+            for (int o = 8; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float m_new = fmaxf(m_run, mx);
+            const float alpha = live ? expf(m_run - m_new) : 0.f;
+            const float pr = live ? expf(sc - m_new) : 0.f;
+            float sum = pr;
+#pragma unroll
+            for (int o = 8; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (live) {
+                l_run = l_run * alpha + sum;
+                m_run = m_new;
+                s.probs[shead * kStageTokens + stok] = pr;
+                if (stok == 0) s.alpha[shead] = alpha;
+            }
         }
         __syncthreads();
-        // P.V
         {
-            const float* vbase = s.stages + (2 * stage + 1) * kStageFloats + col;
-            const float* pb = s.probs + (pkh * kGroup) * kStageTokens + half * 16;
+            const float* vbase = s.stages + (2 * stage + 1) * kStageFloats + tid;
+            const float* pb = s.probs + (pkh * kGroup) * kStageTokens;
 #pragma unroll
             for (int hh = 0; hh < kGroup; ++hh) acc[hh] *= s.alpha[pkh * kGroup + hh];
 #pragma unroll
-            for (int tt = 0; tt < 16; ++tt) {
-                const int t = half * 16 + tt;
+            for (int t = 0; t < kStageTokens; ++t) {
                 const float v = t < n_valid ? vbase[t * kKvWidth] : 0.f;
 #pragma unroll
-                for (int hh = 0; hh < kGroup; ++hh) acc[hh] = fmaf(pb[hh * kStageTokens + tt], v, acc[hh]);
+                for (int hh = 0; hh < kGroup; ++hh) acc[hh] = fmaf(pb[hh * kStageTokens + t], v, acc[hh]);
             }
         }
         __syncthreads();
@@ -209,28 +220,22 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_kernel(const Attn
         if (tid == 0) raise_error(p.error, kErrTimeout);
         return;
     }
-    // Merge the two token halves; head statistics to shared memory.
-    float* red = s.stages;  // all copies have landed: stage 0 is free
-    if (half == 1) {
-#pragma unroll
-        for (int hh = 0; hh < kGroup; ++hh) red[hh * kKvWidth + col] = acc[hh];
-    }
-    if (warp < kHeads && lane == 0) {
-        s.m[warp] = m_run;
-        s.l[warp] = l_run;
+    if (warp < 5 && stok == 0 && shead < kHeads) {
+        s.m[shead] = m_run;
+        s.l[shead] = l_run;
     }
     __syncthreads();
     const int splits = p.row_splits[row];
-    if (half == 0) {
+    {
+        const int d = tid % kHeadDim;
 #pragma unroll
         for (int hh = 0; hh < kGroup; ++hh) {
-            const float total = acc[hh] + red[hh * kKvWidth + col];
-            const int h = pkh * kGroup + hh, d = col % kHeadDim;
+            const int h = pkh * kGroup + hh;
             if (splits == 1) {
-                write_out(p, size_t(row) * p.out_stride + h * kHeadDim + d, total / s.l[h]);
+                write_out(p, size_t(row) * p.out_stride + h * kHeadDim + d, acc[hh] / s.l[h]);
             } else {
                 float* part = p.partial + (size_t(blockIdx.x) * kHeads + h) * (kHeadDim + 2);
-                part[2 + d] = total;
+                part[2 + d] = acc[hh];
                 if (d == 0) {
                     part[0] = s.m[h];
                     part[1] = s.l[h];

@@ -68,9 +68,8 @@ T* host_alloc(size_t count, const char* what) {
 
 // Work decomposition of paged attention.
 //  * Decode rows (sequences appending fewer than kPrefillMinRows rows): each
-//    row's context pages are cut into slices of `pages_per_split` pages. With
-//    pages_per_split == 0 the slice length targets about eight CTAs per SM over
-//    the whole launch (148 SMs), never below 64 tokens per slice.
+//    row's context pages are cut into slices of `pages_per_split` pages
+//    (0: mpb::auto_pages_per_split over all decode rows' tokens).
 //  * Prefill sequences: one work item per (64-row tile, kv head).
 struct AttnPlan {
     std::vector<int32_t> splits, work0;
@@ -91,13 +90,7 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
     for (int i = 0; i < count; ++i)
         if (seqs[i].count < mpb::kPrefillMinRows)
             for (int j = 0; j < seqs[i].count; ++j) decode_tokens += seqs[i].start + j + 1;
-    int pps = pages_per_split;
-    if (pps <= 0) {
-        const long long target = 148LL * 8;
-        long long slice_tokens = std::max<long long>(64, (decode_tokens + target - 1) / target);
-        slice_tokens = (slice_tokens + 31) / 32 * 32;
-        pps = int(std::max<long long>(1, slice_tokens / block_tokens));
-    }
+    const int pps = pages_per_split > 0 ? pages_per_split : mpb::auto_pages_per_split(decode_tokens, block_tokens);
     const double kv_token_bytes = 2.0 * mpb::kKvWidth * sizeof(float);
     int row = 0;
     for (int i = 0; i < count; ++i) {

@@ -87,6 +87,18 @@ constexpr int kPrefillTileRows = 64;
 
 cudaError_t configure_prefill_attention();
 cudaError_t launch_prefill_attention(const PrefillParams& p, cudaStream_t stream);
+// Slice length (pages) of the split-K decode work list when the caller leaves it
+// open: about two waves of the 148 SMs x 3 resident CTAs over all rows' tokens,
+// never below 64 tokens per slice, rounded to whole 16-token stages.
+inline int auto_pages_per_split(long long total_tokens, int block_tokens) {
+    const long long target = 148LL * 3 * 2;
+    long long slice = (total_tokens + target - 1) / target;
+    if (slice < 64) slice = 64;
+    slice = (slice + 15) / 16 * 16;
+    const long long pages = slice / block_tokens;
+    return int(pages < 1 ? 1 : pages);
+}
+
 cudaError_t configure_attention();
 // Message returned by mp_last_error() on this thread.
 void set_last_error(const char* message);

@@ -65,14 +65,12 @@ extern "C" int mp_paged_attention_decode(const float* q, const float* keys, cons
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return MP_ERR_CUDA;
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
     Scratch& s = g_scratch[device];
-    // Work list: slices of `pps` pages (auto: ~8 CTAs per SM, >= 64 tokens).
+    // Work list: slices of `pps` pages (0: mpb::auto_pages_per_split).
     int pps = pages_per_split;
     if (pps <= 0) {
         long long total = 0;
         for (int i = 0; i < count; ++i) total += lengths[i];
-        long long slice = std::max<long long>(64, (total + 148 * 8 - 1) / (148 * 8));
-        slice = (slice + 31) / 32 * 32;
-        pps = int(std::max<long long>(1, slice / block_tokens));
+        pps = mpb::auto_pages_per_split(total, block_tokens);
     }
     std::vector<int32_t> host(size_t(count) * 4);
     std::vector<mpb::AttnWork> work;

@@ -94,9 +94,7 @@ extern "C" int mp_paged_attention_decode_noalloc(const float* q, const float* ke
     if (pps == 0) {
         long long total_tokens = 0;
         for (int i = 0; i < count; ++i) total_tokens += lengths[i];
-        long long slice = std::max<long long>(64, (total_tokens + 148 * 8 - 1) / (148 * 8));
-        slice = (slice + 31) / 32 * 32;
-        pps = int(std::max<long long>(1, slice / block_tokens));
+        pps = mpb::auto_pages_per_split(total_tokens, block_tokens);
         while (slices(pps) > kMaxWork) pps *= 2;
     } else if (slices(pps) > kMaxWork) {
         mpb::set_last_error("mp_paged_attention_decode_noalloc: more than 2048 slices; raise pages_per_split");
