@@ -157,8 +157,10 @@ int mp_cow_timing(mp_context* ctx, int32_t enabled);
 int mp_cow_elapsed(mp_context* ctx, float* milliseconds);
 
 /* C = A . B^T (a [m][k], b [n][k], c [m][n] row-major, device buffers) through the
- * 3xTF32 tcgen05 GEMM of the forward; n a multiple of 64, k of 32. Allocates its
- * own scratch and synchronises `stream`: a test/tool entry, not the hot path. */
+ * 3xTF32 tcgen05 GEMM of the forward (Store epilogue, with the forward's split-K
+ * choice: shapes with few output tiles run as K slices summed in slice order);
+ * n a multiple of 64, k of 32. Allocates its own scratch and synchronises
+ * `stream`: a test/tool entry, not the hot path. */
 int mp_gemm_f32(const float* a, const float* b, float* c, int32_t m, int32_t n, int32_t k, void* stream);
 
 /* The paged-attention decode OPERATOR alone (one query row per sequence), on

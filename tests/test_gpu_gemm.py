@@ -13,7 +13,8 @@ import pytest
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("m,n,k", [(1, 64, 32), (7, 128, 576), (128, 960, 576), (130, 576, 576), (256, 1536, 576),
-                                   (256, 576, 1536), (300, 64, 64), (1000, 192, 128), (256, 4096, 576)])
+                                   (256, 576, 1536), (300, 64, 64), (1000, 192, 128), (256, 4096, 576),
+                                   (3, 64, 160), (5, 64, 1536), (33, 3072, 576)])
 def test_tc_gemm_matches_float64(built, m, n, k):
     import torch
     from tinyinfer_b200 import device
@@ -39,3 +40,31 @@ def test_tc_gemm_matches_float64(built, m, n, k):
     print(f"m={m} n={n} k={k}: 3xTF32 {worst:.3e}  plain TF32 {plain:.3e}")
     assert worst <= 2.0 ** -18, worst
     assert worst * 8 <= plain, (worst, plain)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k", [(7, 576, 1536), (64, 3072, 576)])
+def test_tc_gemm_split_k_is_deterministic(built, m, n, k):
+    """Split-K partials are summed in slice order by whichever CTA finishes last:
+    repeated launches give bit-identical results, and a row's result does not
+    depend on the other rows of the batch (the first rows of a larger M match
+    the same rows computed alone)."""
+    import torch
+    from tinyinfer_b200 import device
+
+    rng = np.random.default_rng(k + n)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    b = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float32)
+    dev = torch.device("cuda:0")
+    stream = torch.cuda.current_stream().cuda_stream
+    ta, tb = torch.from_numpy(a).to(dev), torch.from_numpy(b).to(dev)
+    runs = []
+    for _ in range(4):
+        tc = torch.empty((m, n), device=dev)
+        device.gemm_f32(ta.data_ptr(), tb.data_ptr(), tc.data_ptr(), m, n, k, stream)
+        runs.append(tc.cpu().numpy())
+    for r in runs[1:]:
+        assert np.array_equal(r.view(np.uint32), runs[0].view(np.uint32))
+    one = torch.empty((1, n), device=dev)
+    device.gemm_f32(ta[:1].contiguous().data_ptr(), tb.data_ptr(), one.data_ptr(), 1, n, k, stream)
+    assert np.array_equal(one.cpu().numpy()[0].view(np.uint32), runs[0][0].view(np.uint32))

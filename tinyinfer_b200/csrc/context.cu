@@ -147,7 +147,10 @@ struct mp_context {
         float* hi = nullptr;
         float* lo = nullptr;
     };
-    Split wqkv, wo, wgate, wup, wdown, head;
+    // gate and up are fused: rows 64b..64b+31 of wgu hold gate rows 32b..32b+31 and
+    // rows 64b+32..64b+63 the matching up rows, so a 64-row GEMM tile carries both
+    // halves of 32 SwiGLU outputs.
+    Split wqkv, wo, wgu, wdown, head;
     std::set<std::string> received;
     bool finalized = false;
     // pools and tables
@@ -156,13 +159,14 @@ struct mp_context {
     int32_t* tables = nullptr;
     float *rope_cos = nullptr, *rope_sin = nullptr;
     // workspace (GEMM inputs as hi/lo halves)
-    float *x = nullptr, *qkv = nullptr, *q = nullptr, *gate = nullptr, *logits = nullptr, *partial = nullptr;
+    float *x = nullptr, *qkv = nullptr, *q = nullptr, *logits = nullptr, *partial = nullptr;
+    float* gemm_workspace = nullptr;
+    unsigned* gemm_counters = nullptr;
     Split xn, attn, h, xl;
     // TMA tensor maps of every GEMM operand
     struct alignas(64) Maps {
         CUtensorMap xn_hi, xn_lo, attn_hi, attn_lo, h_hi, h_lo, xl_hi, xl_lo;
-        CUtensorMap wqkv_hi, wqkv_lo, wo_hi, wo_lo, wgate_hi, wgate_lo, wup_hi, wup_lo, wdown_hi, wdown_lo, head_hi,
-            head_lo;
+        CUtensorMap wqkv_hi, wqkv_lo, wo_hi, wo_lo, wgu_hi, wgu_lo, wdown_hi, wdown_lo, head_hi, head_lo;
     };
     Maps maps;
     unsigned *counters = nullptr, *error = nullptr;
@@ -249,11 +253,12 @@ void free_context(mp_context* c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     for (void* p : {(void*)c->embed, (void*)c->final_norm, (void*)c->in_norm, (void*)c->post_norm, (void*)c->keys,
                     (void*)c->values, (void*)c->tables, (void*)c->rope_cos, (void*)c->rope_sin, (void*)c->x,
-                    (void*)c->qkv, (void*)c->q, (void*)c->gate, (void*)c->logits, (void*)c->partial,
+                    (void*)c->qkv, (void*)c->q, (void*)c->gemm_workspace, (void*)c->gemm_counters, (void*)c->logits,
+                    (void*)c->partial,
                     (void*)c->counters, (void*)c->error, (void*)c->meta, (void*)c->out_tokens, (void*)c->out_finite,
                     (void*)c->cow, (void*)c->patch})
         if (p) cudaFree(p);
-    for (auto* s : {&c->wqkv, &c->wo, &c->wgate, &c->wup, &c->wdown, &c->head, &c->xn, &c->attn, &c->h, &c->xl}) {
+    for (auto* s : {&c->wqkv, &c->wo, &c->wgu, &c->wdown, &c->head, &c->xn, &c->attn, &c->h, &c->xl}) {
         if (s->hi) cudaFree(s->hi);
         if (s->lo) cudaFree(s->lo);
     }
@@ -311,6 +316,7 @@ struct WeightSlot {
     int k;           // K
     bool transpose;  // MPFX [K][N] -> packed [N][K]
     size_t elements;
+    int interleave;  // 0: packed row n at n; 1/2: gate/up row n at 64*(n/32) + 32*(interleave-1) + n%32
 };
 
 // Resolve an MPFX0001 tensor name to its packed destination.
@@ -318,11 +324,11 @@ WeightSlot resolve(mp_context* c, const std::string& name) {
     const auto& m = c->model;
     const int H = m.hidden, I = m.intermediate, kvw = c->kvw, V = m.vocabulary;
     if (name == "model.embed_tokens.weight")
-        return {c->embed, m.tied ? c->head.hi : nullptr, m.tied ? c->head.lo : nullptr, V, H, false, size_t(V) * H};
-    if (name == "model.norm.weight") return {c->final_norm, nullptr, nullptr, 1, H, false, size_t(H)};
+        return {c->embed, m.tied ? c->head.hi : nullptr, m.tied ? c->head.lo : nullptr, V, H, false, size_t(V) * H, 0};
+    if (name == "model.norm.weight") return {c->final_norm, nullptr, nullptr, 1, H, false, size_t(H), 0};
     if (name == "lm_head.weight") {
         if (m.tied) fail(MP_ERR_INVALID, "tied model has no lm_head.weight");
-        return {nullptr, c->head.hi, c->head.lo, V, H, true, size_t(V) * H};
+        return {nullptr, c->head.hi, c->head.lo, V, H, true, size_t(V) * H, 0};
     }
     const std::string prefix = "model.layers.";
     if (name.compare(0, prefix.size(), prefix) != 0) fail(MP_ERR_INVALID, "unknown tensor: " + name);
@@ -337,41 +343,41 @@ WeightSlot resolve(mp_context* c, const std::string& name) {
     if (layer < 0 || layer >= m.layers) fail(MP_ERR_INVALID, "unknown tensor: " + name);
     const std::string s = name.substr(dot + 1);
     const size_t L = size_t(layer);
-    if (s == "input_layernorm.weight") return {c->in_norm + L * H, nullptr, nullptr, 1, H, false, size_t(H)};
+    if (s == "input_layernorm.weight") return {c->in_norm + L * H, nullptr, nullptr, 1, H, false, size_t(H), 0};
     if (s == "post_attention_layernorm.weight")
-        return {c->post_norm + L * H, nullptr, nullptr, 1, H, false, size_t(H)};
+        return {c->post_norm + L * H, nullptr, nullptr, 1, H, false, size_t(H), 0};
     auto slice = [](const mp_context::Split& s, size_t offset) { return std::pair<float*, float*>(s.hi + offset, s.lo + offset); };
     const size_t qkv = L * size_t(c->qkvw) * H;
     if (s == "self_attn.q_proj.weight") {
         auto p = slice(c->wqkv, qkv);
-        return {nullptr, p.first, p.second, H, H, true, size_t(H) * H};
+        return {nullptr, p.first, p.second, H, H, true, size_t(H) * H, 0};
     }
     if (s == "self_attn.k_proj.weight") {
         auto p = slice(c->wqkv, qkv + size_t(H) * H);
-        return {nullptr, p.first, p.second, kvw, H, true, size_t(H) * kvw};
+        return {nullptr, p.first, p.second, kvw, H, true, size_t(H) * kvw, 0};
     }
     if (s == "self_attn.v_proj.weight") {
         auto p = slice(c->wqkv, qkv + size_t(H + kvw) * H);
-        return {nullptr, p.first, p.second, kvw, H, true, size_t(H) * kvw};
+        return {nullptr, p.first, p.second, kvw, H, true, size_t(H) * kvw, 0};
     }
     if (s == "self_attn.o_proj.weight") {
         auto p = slice(c->wo, L * size_t(H) * H);
-        return {nullptr, p.first, p.second, H, H, true, size_t(H) * H};
+        return {nullptr, p.first, p.second, H, H, true, size_t(H) * H, 0};
     }
     if (s == "mlp.gate_proj.weight") {
-        auto p = slice(c->wgate, L * size_t(I) * H);
-        return {nullptr, p.first, p.second, I, H, true, size_t(H) * I};
+        auto p = slice(c->wgu, L * size_t(2 * I) * H);
+        return {nullptr, p.first, p.second, I, H, true, size_t(H) * I, 1};
     }
     if (s == "mlp.up_proj.weight") {
-        auto p = slice(c->wup, L * size_t(I) * H);
-        return {nullptr, p.first, p.second, I, H, true, size_t(H) * I};
+        auto p = slice(c->wgu, L * size_t(2 * I) * H);
+        return {nullptr, p.first, p.second, I, H, true, size_t(H) * I, 2};
     }
     if (s == "mlp.down_proj.weight") {
         auto p = slice(c->wdown, L * size_t(H) * I);
-        return {nullptr, p.first, p.second, H, I, true, size_t(I) * H};
+        return {nullptr, p.first, p.second, H, I, true, size_t(I) * H, 0};
     }
     fail(MP_ERR_INVALID, "unknown tensor: " + name);
-    return {nullptr, nullptr, nullptr, 0, 0, false, 0};
+    return {nullptr, nullptr, nullptr, 0, 0, false, 0, 0};
 }
 
 size_t expected_tensors(const mp_model_config& m) { return size_t(m.layers) * 9 + 2 + (m.tied ? 0 : 1); }
@@ -451,8 +457,7 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         split(c->head, V * H, "lm head");
         split(c->wqkv, L * c->qkvw * H, "qkv projections");
         split(c->wo, L * H * H, "o projections");
-        split(c->wgate, L * I * H, "gate projections");
-        split(c->wup, L * I * H, "up projections");
+        split(c->wgu, L * 2 * I * H, "gate/up projections");
         split(c->wdown, L * H * I, "down projections");
         c->pool_elements = uint64_t(r.max_blocks) * L * r.block_tokens * c->kvw;
         c->keys = device_alloc<float>(c->pool_elements, "K pool");
@@ -487,7 +492,10 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         c->qkv = device_alloc<float>(T * c->qkvw, "qkv activations");
         c->q = device_alloc<float>(T * H, "roped queries");
         split(c->attn, T * H, "attention output");
-        c->gate = device_alloc<float>(T * I, "gate activations");
+        c->gemm_workspace = device_alloc<float>(mpb::kGemmWorkspaceFloats, "gemm split-K workspace");
+        c->gemm_counters = device_alloc<unsigned>(mpb::kGemmCounters, "gemm split-K counters");
+        cuda_check(cudaMemsetAsync(c->gemm_counters, 0, mpb::kGemmCounters * sizeof(unsigned), c->stream),
+                   "zero gemm counters");
         split(c->h, T * I, "mlp activations");
         split(c->xl, S * H, "last-row activations");
         c->logits = device_alloc<float>(S * V, "logits");
@@ -506,10 +514,8 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         encode_map(&mp.wqkv_lo, c->wqkv.lo, L * c->qkvw, H, bn);
         encode_map(&mp.wo_hi, c->wo.hi, L * H, H, bn);
         encode_map(&mp.wo_lo, c->wo.lo, L * H, H, bn);
-        encode_map(&mp.wgate_hi, c->wgate.hi, L * I, H, bn);
-        encode_map(&mp.wgate_lo, c->wgate.lo, L * I, H, bn);
-        encode_map(&mp.wup_hi, c->wup.hi, L * I, H, bn);
-        encode_map(&mp.wup_lo, c->wup.lo, L * I, H, bn);
+        encode_map(&mp.wgu_hi, c->wgu.hi, L * 2 * I, H, bn);
+        encode_map(&mp.wgu_lo, c->wgu.lo, L * 2 * I, H, bn);
         encode_map(&mp.wdown_hi, c->wdown.hi, L * H, I, bn);
         encode_map(&mp.wdown_lo, c->wdown.lo, L * H, I, bn);
         encode_map(&mp.head_hi, c->head.hi, V, H, bn);
@@ -566,8 +572,21 @@ int mp_set_weight(mp_context* c, const char* name, const float* host, size_t ele
             }
             std::vector<float> hi(elements), lo(elements);
             split_host(packed, hi.data(), lo.data(), elements);
-            cuda_check(cudaMemcpy(slot.hi, hi.data(), elements * 4, cudaMemcpyHostToDevice), "upload weight");
-            cuda_check(cudaMemcpy(slot.lo, lo.data(), elements * 4, cudaMemcpyHostToDevice), "upload weight");
+            if (!slot.interleave) {
+                cuda_check(cudaMemcpy(slot.hi, hi.data(), elements * 4, cudaMemcpyHostToDevice), "upload weight");
+                cuda_check(cudaMemcpy(slot.lo, lo.data(), elements * 4, cudaMemcpyHostToDevice), "upload weight");
+            } else {
+                // gate/up rows go to alternating 32-row blocks of the fused matrix
+                const size_t K = size_t(slot.k), block = 32 * K;
+                const size_t half = size_t(slot.interleave - 1) * block;
+                for (int b = 0; b < slot.rows_n / 32; ++b) {
+                    const size_t dst = size_t(b) * 2 * block + half, src = size_t(b) * block;
+                    cuda_check(cudaMemcpy(slot.hi + dst, hi.data() + src, block * 4, cudaMemcpyHostToDevice),
+                               "upload weight");
+                    cuda_check(cudaMemcpy(slot.lo + dst, lo.data() + src, block * 4, cudaMemcpyHostToDevice),
+                               "upload weight");
+                }
+            }
         }
         c->received.insert(name);
         c->finalized = false;
@@ -746,10 +765,11 @@ int mp_forward_launch(mp_context* c) {
         const int32_t* meta = c->meta;
         cuda_check(cudaMemsetAsync(c->error, 0, sizeof(unsigned), st), "reset error word");
         cuda_check(cudaEventRecord(c->fwd_events[0], st), "forward timing");
-        // kernels of this forward: embed, per layer 8 (+1 norm after layer 0, +1 per
-        // attention kind present), final norm, head, argmax; table patch / COW if any
+        // kernels of this forward: embed; per layer qkv, rope/append, o, norm, gate/up,
+        // down (+1 input norm after layer 0, +1 per attention kind present); final
+        // norm, head, argmax; table patch / COW if any
         c->step_launches = uint64_t(c->entry_count > 0) + uint64_t(c->region_count > 0 && c->region_rows > 0) + 1 +
-                           uint64_t(m.layers) * (7 + uint64_t(c->prefill_count > 0) + uint64_t(c->work_count > 0)) +
+                           uint64_t(m.layers) * (6 + uint64_t(c->prefill_count > 0) + uint64_t(c->work_count > 0)) +
                            uint64_t(m.layers - 1) + 3;
         cuda_check(mpb::launch_table_patch(meta + c->off_entries, c->entry_count, c->tables,
                                            int64_t(r.max_sequences) * r.table_stride, c->error, st),
@@ -775,11 +795,13 @@ int mp_forward_launch(mp_context* c) {
             g.b_row0 = b_row0;
             g.c = out;
             g.ldc = ldc;
-            g.gate = c->gate;
-            g.ld_gate = I;
             g.out_hi = c->h.hi;
             g.out_lo = c->h.lo;
             g.ld_out = I;
+            g.workspace = c->gemm_workspace;
+            g.workspace_floats = mpb::kGemmWorkspaceFloats;
+            g.counters = c->gemm_counters;
+            g.counter_count = mpb::kGemmCounters;
             g.error = c->error;
             cuda_check(mpb::launch_tc_gemm({&a_hi, &a_lo, &b_hi, &b_lo}, g, e, st), what);
         };
@@ -860,10 +882,8 @@ int mp_forward_launch(mp_context* c) {
             cuda_check(mpb::launch_rmsnorm(c->x, nullptr, c->post_norm + L * H, m.rms_epsilon, c->xn.hi, c->xn.lo, T,
                                            H, st),
                        "rmsnorm launch");
-            gemm(mp.xn_hi, mp.xn_lo, mp.wgate_hi, mp.wgate_lo, T, I, H, l * I, c->gate, I, mpb::Epilogue::Store,
-                 "gate gemm");
-            gemm(mp.xn_hi, mp.xn_lo, mp.wup_hi, mp.wup_lo, T, I, H, l * I, nullptr, I, mpb::Epilogue::SiluMul,
-                 "up gemm");
+            gemm(mp.xn_hi, mp.xn_lo, mp.wgu_hi, mp.wgu_lo, T, 2 * I, H, l * 2 * I, nullptr, I, mpb::Epilogue::SwiGLU,
+                 "gate/up gemm");
             gemm(mp.h_hi, mp.h_lo, mp.wdown_hi, mp.wdown_lo, T, H, I, l * H, c->x, H, mpb::Epilogue::AddTo,
                  "down gemm");
         }
@@ -918,7 +938,12 @@ int mp_forward_collect(mp_context* c, int32_t* out_tokens, int32_t* out_finite, 
         for (int i = 0; i < S; ++i) finite_all &= c->h_finite[i] != 0;
         c->prepared = false;
         const unsigned err = *c->h_error;
-        if (err & mpb::kErrTimeout) fail(MP_ERR_TIMEOUT, "an in-kernel copy wait expired");
+        if (err & mpb::kErrTimeout) {
+            // a GEMM CTA that gave up never counted its K slice in
+            cuda_check(cudaMemsetAsync(c->gemm_counters, 0, mpb::kGemmCounters * sizeof(unsigned), c->stream),
+                       "reset gemm counters");
+            fail(MP_ERR_TIMEOUT, "an in-kernel copy wait expired");
+        }
         if (err & mpb::kErrBounds) fail(MP_ERR_BOUNDS, "device bounds check failed (page id, token or region)");
     });
     if (rc == MP_OK && !finite_all) {
@@ -1075,12 +1100,19 @@ int mp_gemm_f32(const float* a, const float* b, float* out, int32_t m, int32_t n
         unsigned* err = device_alloc<unsigned>(1, "gemm error word");
         scratch.push_back(reinterpret_cast<float*>(err));
         cuda_check(cudaMemsetAsync(err, 0, 4, st), "clear error word");
+        // split-K workspace, as in the forward: small-M shapes run with K slices
+        float* ws = alloc(mpb::kGemmWorkspaceFloats);
+        unsigned* counters = reinterpret_cast<unsigned*>(alloc(mpb::kGemmCounters));
         mpb::TcGemmParams g{};
         g.m = m;
         g.n = n;
         g.k = k;
         g.c = out;
         g.ldc = n;
+        g.workspace = ws;
+        g.workspace_floats = mpb::kGemmWorkspaceFloats;
+        g.counters = counters;
+        g.counter_count = mpb::kGemmCounters;
         g.error = err;
         cuda_check(mpb::launch_tc_gemm({&maps->ah, &maps->al, &maps->bh, &maps->bl}, g, mpb::Epilogue::Store, st),
                    "gemm launch");

@@ -107,16 +107,19 @@ cudaError_t launch_paged_attention(const AttnParams& p, cudaStream_t stream);
 // ---------------------------------------------------------------- GEMM
 // C[M][N] (op) A[M][K] * B[N][K]^T, B stored K-contiguous ("nn.Linear" layout).
 enum class Epilogue : int {
-    Store = 0,    // C = acc
-    AddTo = 1,    // C = C + acc        (residual add)
-    SiluMul = 2,  // C = silu(C) * acc  (C holds the gate projection)
+    Store = 0,   // C = acc
+    AddTo = 1,   // C = C + acc  (residual add)
+    SwiGLU = 2,  // gate/up column pairs -> silu(gate) * up as TF32 hi/lo halves
 };
 
 // Tensor-core 3xTF32 GEMM (tc_gemm.cu). A and B come as TF32 hi/lo halves through
 // 2-D TMA tensor maps (fp32, rows x K, 128-byte swizzle, boxes of 32 x 128 rows
 // for A and 32 x kTcBN rows for B); B's rows start at b_row0 (stacked per-layer
-// weights). Epilogues: Store / AddTo into c; SiluMul reads gate and writes the
-// product as hi/lo halves (out_hi, out_lo).
+// weights). Epilogues: Store / AddTo into c; SwiGLU expects B's rows in 32-row
+// gate/up blocks (rows 64b..64b+31 gate, 64b+32..64b+63 up) and writes
+// silu(gate) * up for output columns 32b..32b+31 as hi/lo halves (out_hi, out_lo).
+// With a workspace and counters, K is split over gridDim.z CTAs whose partial
+// tiles the last-arriving CTA sums in slice order (deterministic).
 constexpr int kTcBN = 64;
 struct TcGemmMaps {
     const struct CUtensorMap_st* a_hi;
@@ -129,11 +132,13 @@ struct TcGemmParams {
     int b_row0;
     float* c;
     int ldc;
-    const float* gate;
-    int ld_gate;
     float* out_hi;
     float* out_lo;
     int ld_out;
+    float* workspace;
+    size_t workspace_floats;
+    unsigned* counters;
+    int counter_count;
     unsigned* error;
 };
 cudaError_t configure_tc_gemm();
@@ -142,6 +147,10 @@ cudaError_t launch_tc_gemm(const TcGemmMaps& maps, const TcGemmParams& p, Epilog
 cudaError_t launch_split(const float* x, float* hi, float* lo, size_t n, cudaStream_t stream);
 
 // ---------------------------------------------------------------- fused small ops
+// Split-K workspace of the tensor-core GEMM: one wave of 148 CTAs x 2 x a 128 x kTcBN tile.
+constexpr size_t kGemmWorkspaceFloats = size_t(148) * 2 * 128 * kTcBN;
+constexpr int kGemmCounters = 148 * 2;
+
 // x[r][:] = embed[tokens[r]][:]; rmsnorm(x[r]) * w written as TF32 hi/lo halves.
 cudaError_t launch_embed_rmsnorm(const int32_t* tokens, const float* embed, int vocabulary, const float* norm_w,
                                  float eps, float* x, float* normed_hi, float* normed_lo, int rows, int hidden,

@@ -12,7 +12,7 @@
 // 2^-20 relative per product. Weights are split once at upload; the kernels that
 // produce GEMM inputs (RMSNorm, attention, SwiGLU) write hi/lo pairs directly.
 //
-// One CTA computes a 128 x BN tile with 4 warps:
+// A CTA computes the K-slice blockIdx.z (of gridDim.z) of a 128 x BN tile with 4 warps:
 //  * warp 0 / one lane: TMA producer. Per 32-element K block it loads the four
 //    operand tiles (A_hi, A_lo, B_hi, B_lo; 128-byte swizzled rows, no multicast)
 //    into a stage and signals the stage's full mbarrier by transaction count;
@@ -21,10 +21,15 @@
 //    releases the stage to the producer, and after the last block signals the
 //    accumulator barrier;
 //  * all 4 warps: epilogue. Each warp reads its 32 TMEM lanes (= tile rows) with
-//    tcgen05.ld.32x32b and applies the fused epilogue.
+//    tcgen05.ld.32x32b and applies the fused epilogue -- directly when the tile
+//    has one K slice, else after the last slice to finish has summed every
+//    slice's partial tile in slice order (deterministic split-K for the small-M
+//    decode GEMMs, which otherwise leave most SMs idle).
 // Every mbarrier wait is bounded; a timeout sets the error word and the CTA still
 // releases its tensor memory before returning.
 #include <cuda.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -102,6 +107,44 @@ __device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// The fused epilogue for one output row of the tile: v[0..BN) are columns n0.. .
+//  Store  : c[row][n0 + j] = v[j]
+//  AddTo  : c[row][n0 + j] += v[j]                     (residual add)
+//  SwiGLU : the tile holds gate columns (v[0..BN/2)) and the matching up columns
+//           (v[BN/2..BN)) of output columns n0/2 .. n0/2 + BN/2; writes
+//           h = silu(gate) * up as TF32 hi/lo halves (the down projection's input).
+template <int BN, Epilogue E>
+__device__ __forceinline__ void epilogue(const TcGemmParams& p, int row, int n0, const float* v) {
+    if (E == Epilogue::Store) {
+        float4* dst = reinterpret_cast<float4*>(p.c + size_t(row) * p.ldc + n0);
+#pragma unroll
+        for (int i = 0; i < BN / 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else if (E == Epilogue::AddTo) {
+        float4* dst = reinterpret_cast<float4*>(p.c + size_t(row) * p.ldc + n0);
+#pragma unroll
+        for (int i = 0; i < BN / 4; ++i) {
+            const float4 x = dst[i];
+            dst[i] = make_float4(__fadd_rn(x.x, v[4 * i]), __fadd_rn(x.y, v[4 * i + 1]), __fadd_rn(x.z, v[4 * i + 2]),
+                                 __fadd_rn(x.w, v[4 * i + 3]));
+        }
+    } else {
+        constexpr int H = BN / 2;
+        const size_t at = size_t(row) * p.ld_out + n0 / 2;
+#pragma unroll
+        for (int i = 0; i < H / 4; ++i) {
+            float hv[4], lv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float g = v[4 * i + e], u = v[H + 4 * i + e];
+                const float o = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+                split_tf32(o, hv[e], lv[e]);
+            }
+            reinterpret_cast<float4*>(p.out_hi + at)[i] = make_float4(hv[0], hv[1], hv[2], hv[3]);
+            reinterpret_cast<float4*>(p.out_lo + at)[i] = make_float4(lv[0], lv[1], lv[2], lv[3]);
+        }
+    }
+}
+
 template <int BN, Epilogue E>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
@@ -119,7 +162,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
-    const int kblocks = p.k / kBK;
+    // K blocks of this CTA's split: [kb_begin, kb_end)
+    const int kb_total = p.k / kBK, splits = gridDim.z;
+    const int kb_per = (kb_total + splits - 1) / splits;
+    const int kb_begin = blockIdx.z * kb_per, kb_end = min(kb_total, kb_begin + kb_per);
+    const int kblocks = kb_end - kb_begin;
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
@@ -151,10 +198,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             unsigned char* st = smem + s * Cfg::kStage;
             mbar_arrive_expect_tx(&full[s], Cfg::kStage);
-            tma_load_2d(st, &a_hi, kb * kBK, m0, &full[s]);
-            tma_load_2d(st + Cfg::kATile, &a_lo, kb * kBK, m0, &full[s]);
-            tma_load_2d(st + 2 * Cfg::kATile, &b_hi, kb * kBK, p.b_row0 + n0, &full[s]);
-            tma_load_2d(st + 2 * Cfg::kATile + Cfg::kBTile, &b_lo, kb * kBK, p.b_row0 + n0, &full[s]);
+            const int kx = (kb_begin + kb) * kBK;
+            tma_load_2d(st, &a_hi, kx, m0, &full[s]);
+            tma_load_2d(st + Cfg::kATile, &a_lo, kx, m0, &full[s]);
+            tma_load_2d(st + 2 * Cfg::kATile, &b_hi, kx, p.b_row0 + n0, &full[s]);
+            tma_load_2d(st + 2 * Cfg::kATile + Cfg::kBTile, &b_lo, kx, p.b_row0 + n0, &full[s]);
         }
     } else if (warp == 1 && lane == 0) {
         // MMA issuer
@@ -184,58 +232,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
     // Epilogue: all 4 warps; warp w owns TMEM lanes / tile rows 32w .. 32w+31.
-    const bool ready = mbar_wait_bounded(accum, 0);
-    if (!ready || *failed) {
+    // The outcome is made CTA-uniform before any branch that holds a barrier.
+    if (!mbar_wait_bounded(accum, 0)) *failed = 1;
+    __syncthreads();
+    const bool ok = *failed == 0;
+    __syncthreads();
+    const int row_in_tile = warp * 32 + lane;
+    const int row = m0 + row_in_tile;
+    if (!ok) {
         if (threadIdx.x == 0) raise_error(p.error, kErrTimeout);
-    } else {
+    } else if (splits == 1) {
         tmem_fence_after();
-        const int row = m0 + warp * 32 + lane;
+        uint32_t r[BN];
+#pragma unroll
+        for (int c0 = 0; c0 < BN; c0 += 32)
+            tmem_load32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c0), *reinterpret_cast<uint32_t(*)[32]>(&r[c0]));
+        if (row < p.m) epilogue<BN, E>(p, row, n0, reinterpret_cast<const float*>(r));
+    } else {
+        // Deterministic split-K: park this slice's partial tile, and let the last
+        // slice to arrive sum all partials in slice order before the epilogue.
+        tmem_fence_after();
+        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+        float* part = p.workspace + (size_t(tile) * splits + blockIdx.z) * (kBM * BN) + size_t(row_in_tile) * BN;
 #pragma unroll
         for (int c0 = 0; c0 < BN; c0 += 32) {
             uint32_t r[32];
             tmem_load32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c0), r);
-            if (row < p.m) {
-                const int col = n0 + c0;
-                if (E == Epilogue::Store) {
-                    float4* dst = reinterpret_cast<float4*>(p.c + size_t(row) * p.ldc + col);
 #pragma unroll
-                    for (int v = 0; v < 8; ++v)
-                        dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                             __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
-                } else if (E == Epilogue::AddTo) {
-                    float4* dst = reinterpret_cast<float4*>(p.c + size_t(row) * p.ldc + col);
+            for (int v = 0; v < 8; ++v)
+                __stcg(reinterpret_cast<float4*>(part + c0) + v,
+                       make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                   __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3])));
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) *failed = atomicAdd(&p.counters[tile], 1u) == unsigned(splits - 1) ? 2 : 0;
+        __syncthreads();
+        if (*failed == 2) {
+            __threadfence();
+            float acc[BN];
 #pragma unroll
-                    for (int v = 0; v < 8; ++v) {
-                        const float4 x = dst[v];
-                        dst[v] = make_float4(__fadd_rn(x.x, __uint_as_float(r[4 * v])),
-                                             __fadd_rn(x.y, __uint_as_float(r[4 * v + 1])),
-                                             __fadd_rn(x.z, __uint_as_float(r[4 * v + 2])),
-                                             __fadd_rn(x.w, __uint_as_float(r[4 * v + 3])));
-                    }
-                } else {  // SiluMul: h = silu(gate) * up, written as TF32 hi/lo halves
-                    const float4* g = reinterpret_cast<const float4*>(p.gate + size_t(row) * p.ld_gate + col);
-                    float4* hi = reinterpret_cast<float4*>(p.out_hi + size_t(row) * p.ld_out + col);
-                    float4* lo = reinterpret_cast<float4*>(p.out_lo + size_t(row) * p.ld_out + col);
+            for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+            for (int s = 0; s < splits; ++s) {
+                const float4* src = reinterpret_cast<const float4*>(
+                    p.workspace + (size_t(tile) * splits + s) * (kBM * BN) + size_t(row_in_tile) * BN);
 #pragma unroll
-                    for (int v = 0; v < 8; ++v) {
-                        const float4 gv = g[v];
-                        float o[4];
-                        const float gs[4] = {gv.x, gv.y, gv.z, gv.w};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float a = gs[e];
-                            o[e] = __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))), __uint_as_float(r[4 * v + e]));
-                        }
-                        float4 h, l;
-                        split_tf32(o[0], h.x, l.x);
-                        split_tf32(o[1], h.y, l.y);
-                        split_tf32(o[2], h.z, l.z);
-                        split_tf32(o[3], h.w, l.w);
-                        hi[v] = h;
-                        lo[v] = l;
-                    }
+                for (int v = 0; v < BN / 4; ++v) {
+                    const float4 x = __ldcg(src + v);
+                    acc[4 * v] += x.x;
+                    acc[4 * v + 1] += x.y;
+                    acc[4 * v + 2] += x.z;
+                    acc[4 * v + 3] += x.w;
                 }
             }
+            if (row < p.m) epilogue<BN, E>(p, row, n0, acc);
+            if (threadIdx.x == 0) p.counters[tile] = 0u;  // ready for the next launch
         }
     }
     tmem_fence_before();
@@ -251,7 +302,19 @@ template <int BN, Epilogue E>
 cudaError_t launch_bn(const TcGemmMaps& maps, const TcGemmParams& p, cudaStream_t stream) {
     using Cfg = TcConfig<BN>;
     static_assert(Cfg::kSmem <= 232448, "stage buffers exceed shared memory");
-    const dim3 grid(p.n / BN, (p.m + kBM - 1) / kBM);
+    const int tiles = (p.n / BN) * ((p.m + kBM - 1) / kBM);
+    const int kb = p.k / kBK;
+    // K slices: fill about one wave of the 148 SMs, at least 2 K blocks per slice,
+    // within the workspace the caller provides.
+    int splits = 1;
+    if (p.workspace && p.counters) {
+        splits = std::max(1, std::min(148 / std::max(tiles, 1), kb / 2));
+        while (splits > 1 && size_t(tiles) * splits * kBM * BN > p.workspace_floats) --splits;
+        if (tiles > p.counter_count) splits = 1;
+        // equalise: no empty trailing slice
+        while (splits > 1 && (splits - 1) * ((kb + splits - 1) / splits) >= kb) --splits;
+    }
+    const dim3 grid(p.n / BN, (p.m + kBM - 1) / kBM, splits);
     tc_gemm_kernel<BN, E><<<grid, kThreads, Cfg::kSmem, stream>>>(*maps.a_hi, *maps.a_lo, *maps.b_hi, *maps.b_lo, p);
     return cudaGetLastError();
 }
@@ -263,7 +326,7 @@ cudaError_t configure_bn() {
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(tc_gemm_kernel<BN, Epilogue::AddTo>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(tc_gemm_kernel<BN, Epilogue::SiluMul>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+        e = cudaFuncSetAttribute(tc_gemm_kernel<BN, Epilogue::SwiGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     return e;
 }
 
@@ -283,7 +346,7 @@ cudaError_t launch_tc_gemm(const TcGemmMaps& maps, const TcGemmParams& p, Epilog
     switch (e) {
         case Epilogue::Store: return launch_bn<kTcBN, Epilogue::Store>(maps, p, stream);
         case Epilogue::AddTo: return launch_bn<kTcBN, Epilogue::AddTo>(maps, p, stream);
-        case Epilogue::SiluMul: return launch_bn<kTcBN, Epilogue::SiluMul>(maps, p, stream);
+        case Epilogue::SwiGLU: return launch_bn<kTcBN, Epilogue::SwiGLU>(maps, p, stream);
     }
     return cudaErrorInvalidValue;
 }
