@@ -84,14 +84,14 @@ def model_config(args):
     return ModelConfig(layers=args.layers, context=args.prompt + max_new_tokens(args) + 32)
 
 
-def prompts(args, rank):
-    """Seeded prompts: one shared prefix (same on every GPU), unique suffixes per request."""
-    rng = np.random.default_rng(20240 + rank)
+def prompts(args, indices):
+    """Seeded prompts of the given global requests: one shared prefix, a unique
+    suffix per request seeded by its global index (independent of the GPU count)."""
     vocab = 49152
     shared = np.random.default_rng(7).integers(0, vocab, args.shared).astype(np.int32)
     out = []
-    for i in range(args.requests):
-        suffix = rng.integers(0, vocab, args.prompt - args.shared).astype(np.int32)
+    for i in indices:
+        suffix = np.random.default_rng([20240, i]).integers(0, vocab, args.prompt - args.shared).astype(np.int32)
         out.append(np.concatenate([shared, suffix]))
     return out
 
@@ -212,6 +212,7 @@ def cpu_baseline(args, workers=None, seconds=None):
 def run_b200(args, rank, world, local_rank):
     import torch
 
+    from tinyinfer_b200 import router
     from tinyinfer_b200.host import Engine, Runner
     from tinyinfer_b200.synthetic import random_weights
 
@@ -221,7 +222,7 @@ def run_b200(args, rank, world, local_rank):
         from datetime import timedelta
 
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
     torch.cuda.set_device(local_rank)
 
     cfg = model_config(args)
@@ -237,8 +238,10 @@ def run_b200(args, rank, world, local_rank):
     del weights
     engine = Engine(runner, n, args.prefill_budget, args.prompt, cfg.context)
     dev = engine.device()
-    ps = prompts(args, rank)
-    ids = [f"r{i}" for i in range(n)]
+    # this GPU's shard of the world's requests (round-robin, no collective)
+    mine = router.round_robin(n * world, world, rank)
+    ps = prompts(args, mine)
+    ids = [f"r{i}" for i in mine]
 
     # Seed: prefill to completion so the shared prefix is published.
     t_setup = time.perf_counter()
@@ -338,6 +341,8 @@ def run_b200(args, rank, world, local_rank):
                    "model": "SmolLM2-135M shape, 30 layers, FP32, tied head", "requests_per_gpu": args.requests,
                    "prompt_tokens": args.prompt, "shared_prefix_tokens": args.shared, "block_tokens": bt,
                    "prefix_cache_blocks": args.prefix_blocks, "parallelism": f"request-sharded replicas x{world}",
+                   "routing": "round-robin by global request index; each GPU its own weights, KV pool, "
+                              "prefix cache and engine; no collective in a step",
                    "l2": "inputs larger than L2 (>= 24 GB of K/V read per step)",
                    "setup_seconds": round(setup_s, 1), "prefix_reused_tokens": reused, "cow_pages": cow},
         "e2e": {"value": tokens_all / (e2e_ms * 1e-3), "unit": "tok/s",

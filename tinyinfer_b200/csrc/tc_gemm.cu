@@ -14,7 +14,7 @@
 //
 // A CTA computes the K-slice blockIdx.z (of gridDim.z) of a 128 x BN tile with 4 warps:
 //  * warp 0 / one lane: TMA producer. Per 32-element K block it loads the four
-//    operand tiles (A_hi, A_lo, B_hi, B_lo; 128-byte swizzled rows, no multicast)
+//    operand tiles (A_hi, A_lo, B_hi, B_lo; 128-byte swizzled rows, one CTA per load)
 //    into a stage and signals the stage's full mbarrier by transaction count;
 //  * warp 1 / one lane: MMA issuer. Per K block 4 K-steps x 3 tcgen05.mma
 //    (kind::tf32, M=128, N=BN, K=8) into one TMEM accumulator; tcgen05.commit

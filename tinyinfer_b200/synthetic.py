@@ -123,3 +123,57 @@ def sine_weights(c: ModelConfig) -> dict[str, np.ndarray]:
 def random_tokens(count: int, vocabulary: int, seed: int) -> np.ndarray:
     rng = np.random.Generator(np.random.PCG64(seed))
     return rng.integers(0, vocabulary, size=count, dtype=np.int64).astype(np.int32)
+
+
+@dataclass(frozen=True)
+class PrefixTreeRequest:
+    root: int          # prefix-tree root the prompt starts from (routing key)
+    path: tuple        # child index at each depth below the root (may be empty)
+    prompt: np.ndarray  # int32 token ids
+    max_new_tokens: int
+
+
+def prefix_tree_requests(seed: int = 5, count: int = 2048, roots: int = 16, root_tokens: int = 2048,
+                         branching: int = 4, depth: int = 3, segment: int = 256, min_len: int = 512,
+                         max_len: int = 8192, min_new: int = 32, max_new: int = 512,
+                         vocabulary: int = 49152) -> list[PrefixTreeRequest]:
+    """Seeded requests drawn from a prefix tree (BASELINE config 5's workload).
+
+    The tree: `roots` random root sequences of `root_tokens` tokens; every node
+    has `branching` children, each adding its own random `segment`-token
+    segment, down to `depth` levels (4 + 16 + 64 descendant paths per root at the
+    defaults). A request picks a root and a depth uniformly, then a node at that
+    depth uniformly; its path tokens are the root followed by the segments down
+    to the node. The prompt length is uniform in [min_len, max_len]: a path
+    longer than that is truncated, a shorter one is extended with tokens unique
+    to the request. Decode lengths are uniform in [min_new, max_new].
+    Segments are derived from (seed, root, path) alone, so the same node yields
+    the same tokens in every request and on every rank.
+    """
+    rng = np.random.Generator(np.random.PCG64(seed))
+    cache: dict = {}
+
+    def tokens(root: int, path: tuple) -> np.ndarray:
+        key = (root, path)
+        if key not in cache:
+            n = root_tokens if not path else segment
+            g = np.random.Generator(np.random.PCG64([seed, 1 + root, len(path), *path]))
+            cache[key] = g.integers(0, vocabulary, size=n, dtype=np.int64).astype(np.int32)
+        return cache[key]
+
+    out = []
+    for i in range(count):
+        root = int(rng.integers(0, roots))
+        d = int(rng.integers(0, depth + 1))
+        path = tuple(int(x) for x in rng.integers(0, branching, size=d))
+        parts = [tokens(root, path[:k]) for k in range(d + 1)]
+        full = np.concatenate(parts)
+        length = int(rng.integers(min_len, max_len + 1))
+        if length <= full.size:
+            prompt = full[:length]
+        else:
+            extra = rng.integers(0, vocabulary, size=length - full.size, dtype=np.int64).astype(np.int32)
+            prompt = np.concatenate([full, extra])
+        new = int(rng.integers(min_new, max_new + 1))
+        out.append(PrefixTreeRequest(root, path, prompt.astype(np.int32), new))
+    return out
