@@ -281,11 +281,16 @@ def run_b200(args, rank, world, local_rank):
     dev.sync()
     tokens = 0
     with ClockSampler(local_rank) as clocks:
+        # profiler range = the timed steps (`ncu --profile-from-start off` captures
+        # exactly these launches; a no-op without a profiler)
+        torch.cuda.cudart().cudaProfilerStart()
         dev.timer_mark()
         for _ in range(args.steps):
             tokens += decode_step()
         dev.timer_mark()
         e2e_ms = dev.timer_elapsed()
+        dev.sync()
+        torch.cuda.cudart().cudaProfilerStop()
     dev.sync()
     torch.cuda.synchronize()
     dev.profile(False)
@@ -315,12 +320,14 @@ def run_b200(args, rank, world, local_rank):
     unique_per_launch = uniq
     achieved = bytes_per_launch / (launch_ms * 1e-3) / 1e9 if launch_ms > 0 else None
     traffic = None
-    tpath = os.path.join(ROOT, "profiles", "attention_decode_traffic.json")
+    # DRAM bytes per launch from the committed ncu capture of the same kernel on the
+    # same rows, scaled to this run's algorithmic bytes per launch
+    tpath = os.path.join(ROOT, "profiles", "paged_attention_decode_config3_traffic.json")
     if os.path.exists(tpath):
         try:
             with open(tpath) as f:
                 t = json.load(f)
-            traffic = t["dram_bytes_per_token_row"] * bytes_per_launch / t["algorithmic_bytes_per_token_row"]
+            traffic = t["dram_bytes_per_launch"] * bytes_per_launch / t["algorithmic_bytes_per_launch"]
         except Exception:
             traffic = None
     line = {
@@ -411,6 +418,7 @@ def run_operator(args, local_rank):
     torch.cuda.synchronize()
     times = []
     with ClockSampler(local_rank) as clocks:
+        torch.cuda.cudart().cudaProfilerStart()
         for _ in range(args.steps):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
@@ -418,6 +426,7 @@ def run_operator(args, local_rank):
             b.record(stream)
             times.append((a, b))
         torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
     assert device.paged_attention_status(stream.cuda_stream) == 0
     ms = [a.elapsed_time(b) for a, b in times]
     avg = sum(ms) / len(ms)
