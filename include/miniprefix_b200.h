@@ -142,12 +142,16 @@ int mp_profile_enable(mp_context* ctx, int32_t enabled);
 int mp_profile_read(mp_context* ctx, float* attention_ms, int32_t* attention_launches, double* attention_bytes);
 /* Cumulative counters of collected forwards: device time from the first to the
  * last kernel of each forward (CUDA events on the context stream), kernels
- * launched, and bytes moved host->device / device->host by the forwards. */
+ * launched, and bytes moved host->device / device->host by the forwards;
+ * shared_prefix_rows counts decode rows whose leading pages were served by the
+ * shared-prefix kernel (once per forward), shared_prefix_tokens the tokens those
+ * rows did not read themselves. */
 typedef struct {
     uint64_t forwards;
     double forward_ms;
     uint64_t kernel_launches;
     uint64_t h2d_bytes, d2h_bytes;
+    uint64_t shared_prefix_rows, shared_prefix_tokens;
 } mp_counters;
 int mp_read_counters(mp_context* ctx, mp_counters* out, int32_t reset);
 

@@ -25,7 +25,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", f"-I{CSRC}"]
 
-DEVICE_SOURCES = ["attention.cu", "attention_prefill.cu", "tc_gemm.cu", "fused_ops.cu", "context.cu", "operator.cu", "operator_noalloc.cu"]
+DEVICE_SOURCES = ["attention.cu", "attention_shared.cu", "attention_prefill.cu", "tc_gemm.cu", "fused_ops.cu", "context.cu", "operator.cu", "operator_noalloc.cu"]
 HOST_SOURCES = []  # filled in by host/ when present
 
 

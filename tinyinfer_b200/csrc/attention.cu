@@ -8,8 +8,9 @@
 //
 // Design (one query row, all 9 heads, per CTA; split-K over pages):
 //  * A CTA owns one slice [page_begin, page_end) of one query row's context. A row
-//    with more than one slice is merged by the last slice to finish (arrival
-//    counter per row), so one launch produces the final output.
+//    with more than one slice, or with shared-prefix partials computed earlier on
+//    the stream by attention_shared.cu, is merged by the last slice to finish
+//    (arrival counter per row), so one launch produces the final output.
 //  * K and V of 16 consecutive tokens form one stage. Runs of tokens that are
 //    contiguous inside a page (a page is [slot][192] floats for one layer) are
 //    moved by the bulk-copy engine (cp.async.bulk) into shared memory and
@@ -226,12 +227,16 @@ __global__ void __launch_bounds__(kThreads, 3) paged_attention_kernel(const Attn
     }
     __syncthreads();
     const int splits = p.row_splits[row];
+    // shared-prefix partials of this row (written by the prefix kernel earlier on
+    // the same stream) join the merge as extra slots
+    const int nx = p.row_nx ? p.row_nx[row] : 0;
+    const bool direct = splits == 1 && nx == 0;
     {
         const int d = tid % kHeadDim;
 #pragma unroll
         for (int hh = 0; hh < kGroup; ++hh) {
             const int h = pkh * kGroup + hh;
-            if (splits == 1) {
+            if (direct) {
                 write_out(p, size_t(row) * p.out_stride + h * kHeadDim + d, acc[hh] / s.l[h]);
             } else {
                 float* part = p.partial + (size_t(blockIdx.x) * kHeads + h) * (kHeadDim + 2);
@@ -243,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 3) paged_attention_kernel(const Attn
             }
         }
     }
-    if (splits == 1) return;
+    if (direct) return;
     __threadfence();
     __syncthreads();
     if (tid == 0) {
@@ -253,16 +258,19 @@ __global__ void __launch_bounds__(kThreads, 3) paged_attention_kernel(const Attn
     __syncthreads();
     if (s.flag[0] != 2) return;
     __threadfence();
-    // Last slice of this row: merge all slices' (m, l, acc) in slice order.
+    // Last slice of this row: merge the shared-prefix slots, then all slices'
+    // (m, l, acc), in that fixed order.
     const int w0 = p.row_work0[row];
+    const int x0 = nx ? p.row_x0[row] : 0;
+    auto slot = [&](int k) { return k < nx ? x0 + k : w0 + (k - nx); };
     for (int o = tid; o < kHeads * kHeadDim; o += kThreads) {
         const int h = o / kHeadDim, d = o % kHeadDim;
         float mx = -INFINITY;
-        for (int k = 0; k < splits; ++k)
-            mx = fmaxf(mx, __ldcg(p.partial + (size_t(w0 + k) * kHeads + h) * (kHeadDim + 2)));
+        for (int k = 0; k < nx + splits; ++k)
+            mx = fmaxf(mx, __ldcg(p.partial + (size_t(slot(k)) * kHeads + h) * (kHeadDim + 2)));
         float num = 0.f, den = 0.f;
-        for (int k = 0; k < splits; ++k) {
-            const float* part = p.partial + (size_t(w0 + k) * kHeads + h) * (kHeadDim + 2);
+        for (int k = 0; k < nx + splits; ++k) {
+            const float* part = p.partial + (size_t(slot(k)) * kHeads + h) * (kHeadDim + 2);
             const float sc = expf(__ldcg(part) - mx);
             den = fmaf(__ldcg(part + 1), sc, den);
             num = fmaf(__ldcg(part + 2 + d), sc, num);

@@ -70,28 +70,132 @@ T* host_alloc(size_t count, const char* what) {
 //  * Decode rows (sequences appending fewer than kPrefillMinRows rows): each
 //    row's context pages are cut into slices of `pages_per_split` pages
 //    (0: mpb::auto_pages_per_split over all decode rows' tokens).
+//  * Shared prefixes: decode rows whose block tables begin with the same physical
+//    pages (prefix reuse, forks) form a group when at least kGroupMinRows rows
+//    share at least kGroupMinTokens tokens of full pages. The group's shared
+//    tokens become prefix work (attention_shared.cu, one CTA per kv head x 64
+//    query vectors x chunk) and each row's slices start after them. A page that
+//    holds a row's newest token is never shared (it was just written), so only
+//    pages before it count.
 //  * Prefill sequences: one work item per (64-row tile, kv head).
 struct AttnPlan {
-    std::vector<int32_t> splits, work0;
+    std::vector<int32_t> splits, work0, x0, nx;
     std::vector<mpb::AttnWork> work;
     std::vector<mpb::PrefillWork> prefill;
-    double bytes = 0;  // algorithmic bytes of one layer's attention
+    std::vector<mpb::PrefixWork> prefix;
+    std::vector<int32_t> group_rows, group_row0, group_slot;
+    int extra_slots = 0;
+    double bytes = 0;          // algorithmic bytes of one layer's attention (shared tokens once per group)
+    double logical_bytes = 0;  // the same with every row reading its whole context
 };
 
-void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, int pages_per_split, AttnPlan& plan) {
+constexpr int kGroupMinRows = 8;
+constexpr int kGroupMinTokens = 128;
+constexpr int kPrefixChunkTokens = 128;
+constexpr int kPrefixMaxChunks = 64;
+
+// tables: host mirror of the device block tables ([slots][table_stride]).
+void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, int table_stride,
+                    const std::vector<int32_t>& tables, int pages_per_split, size_t extra_capacity,
+                    size_t prefix_capacity, AttnPlan& plan) {
     int rows = 0;
     for (int i = 0; i < count; ++i) rows += seqs[i].count;
     plan.splits.assign(rows, 0);
     plan.work0.assign(rows, 0);
+    plan.x0.assign(rows, 0);
+    plan.nx.assign(rows, 0);
     plan.work.clear();
     plan.prefill.clear();
+    plan.prefix.clear();
+    plan.group_rows.clear();
+    plan.group_row0.assign(1, 0);
+    plan.group_slot.clear();
+    plan.extra_slots = 0;
     plan.bytes = 0;
-    long long decode_tokens = 0;
-    for (int i = 0; i < count; ++i)
-        if (seqs[i].count < mpb::kPrefillMinRows)
-            for (int j = 0; j < seqs[i].count; ++j) decode_tokens += seqs[i].start + j + 1;
-    const int pps = pages_per_split > 0 ? pages_per_split : mpb::auto_pages_per_split(decode_tokens, block_tokens);
+    plan.logical_bytes = 0;
     const double kv_token_bytes = 2.0 * mpb::kKvWidth * sizeof(float);
+
+    // decode rows: (row, slot, len)
+    struct DecodeRow {
+        int row, slot, len;
+    };
+    std::vector<DecodeRow> decode;
+    {
+        int row = 0;
+        for (int i = 0; i < count; ++i) {
+            const auto& s = seqs[i];
+            if (s.count < mpb::kPrefillMinRows)
+                for (int j = 0; j < s.count; ++j) decode.push_back({row + j, s.slot, s.start + j + 1});
+            row += s.count;
+        }
+    }
+    // shared-prefix groups: bucket rows by their first page, then the longest
+    // common run of page ids within the bucket
+    std::vector<int> shared_pages(rows, 0);
+    {
+        std::vector<std::pair<int32_t, int>> keyed;  // (first page, index into decode)
+        for (int i = 0; i < int(decode.size()); ++i) {
+            const int full = (decode[i].len - 1) / block_tokens;
+            if (full * block_tokens >= kGroupMinTokens)
+                keyed.push_back({tables[size_t(decode[i].slot) * table_stride], i});
+        }
+        std::stable_sort(keyed.begin(), keyed.end(),
+                         [](const auto& a, const auto& b) { return a.first < b.first; });
+        for (size_t b = 0; b < keyed.size();) {
+            size_t e = b;
+            while (e < keyed.size() && keyed[e].first == keyed[b].first) ++e;
+            const int n = int(e - b);
+            if (n >= kGroupMinRows && keyed[b].first >= 0) {
+                const DecodeRow& ref = decode[keyed[b].second];
+                const int32_t* rt = tables.data() + size_t(ref.slot) * table_stride;
+                int lcp = (ref.len - 1) / block_tokens;
+                for (size_t k = b + 1; k < e && lcp > 0; ++k) {
+                    const DecodeRow& d = decode[keyed[k].second];
+                    lcp = std::min(lcp, (d.len - 1) / block_tokens);
+                    const int32_t* t = tables.data() + size_t(d.slot) * table_stride;
+                    for (int i = 1; i < lcp; ++i)
+                        if (t[i] != rt[i]) {
+                            lcp = i;
+                            break;
+                        }
+                }
+                const int shared = lcp * block_tokens;
+                int chunk_tokens = std::max(kPrefixChunkTokens, (shared + kPrefixMaxChunks - 1) / kPrefixMaxChunks);
+                chunk_tokens = (chunk_tokens + 31) / 32 * 32;
+                const int chunks = (shared + chunk_tokens - 1) / chunk_tokens;
+                const int qvecs = n * mpb::kGroup;
+                const int qblocks = (qvecs + mpb::kPrefixQueries - 1) / mpb::kPrefixQueries;
+                const size_t works = size_t(mpb::kKvHeads) * qblocks * chunks;
+                if (shared >= kGroupMinTokens && size_t(plan.extra_slots) + size_t(n) * chunks <= extra_capacity &&
+                    plan.prefix.size() + works <= prefix_capacity) {
+                    const int g = int(plan.group_slot.size());
+                    plan.group_slot.push_back(ref.slot);
+                    for (size_t k = b; k < e; ++k) {
+                        const DecodeRow& d = decode[keyed[k].second];
+                        plan.group_rows.push_back(d.row);
+                        shared_pages[d.row] = lcp;
+                        plan.nx[d.row] = chunks;
+                        plan.x0[d.row] = plan.extra_slots;  // made absolute below
+                        plan.extra_slots += chunks;
+                    }
+                    plan.group_row0.push_back(int(plan.group_rows.size()));
+                    for (int kh = 0; kh < mpb::kKvHeads; ++kh)
+                        for (int ch = 0; ch < chunks; ++ch)
+                            for (int qb = 0; qb < qblocks; ++qb) {
+                                const int q0 = qb * mpb::kPrefixQueries;
+                                plan.prefix.push_back({g, kh, q0, std::min(mpb::kPrefixQueries, qvecs - q0),
+                                                       ch * chunk_tokens, std::min(shared, (ch + 1) * chunk_tokens),
+                                                       ch, 0});
+                            }
+                    plan.bytes += double(shared) * kv_token_bytes;
+                }
+            }
+            b = e;
+        }
+    }
+    long long decode_tokens = 0;
+    for (const auto& d : decode) decode_tokens += d.len - shared_pages[d.row] * block_tokens;
+    const int pps = pages_per_split > 0 ? pages_per_split : mpb::auto_pages_per_split(decode_tokens, block_tokens);
     int row = 0;
     for (int i = 0; i < count; ++i) {
         const auto& s = seqs[i];
@@ -104,26 +208,35 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
             }
             // The context of the whole chunk is read once per 64-row tile.
             const int tiles = (s.count + mpb::kPrefillTileRows - 1) / mpb::kPrefillTileRows;
+            double b = 0;
             for (int t = 0; t < tiles; ++t) {
                 const int last = s.start + std::min(s.count, (t + 1) * mpb::kPrefillTileRows);
-                plan.bytes += double(last) * kv_token_bytes;
+                b += double(last) * kv_token_bytes;
             }
-            plan.bytes += double(s.count) * 2.0 * mpb::kQWidth * sizeof(float);
+            b += double(s.count) * 2.0 * mpb::kQWidth * sizeof(float);
+            plan.bytes += b;
+            plan.logical_bytes += b;
             row += s.count;
             continue;
         }
         for (int j = 0; j < s.count; ++j, ++row) {
             const int len = s.start + j + 1;
             const int pages = (len + block_tokens - 1) / block_tokens;
-            const int n = std::max(1, (pages + pps - 1) / pps);
+            const int first = shared_pages[row];
+            const int n = std::max(1, (pages - first + pps - 1) / pps);
             plan.splits[row] = n;
             plan.work0[row] = int(plan.work.size());
-            for (int k = 0; k < n; ++k) plan.work.push_back({row, k * pps, std::min(pages, (k + 1) * pps), k});
+            for (int k = 0; k < n; ++k)
+                plan.work.push_back({row, first + k * pps, std::min(pages, first + (k + 1) * pps), k});
             // K and V rows, the query row and output row, the table entries.
-            plan.bytes += double(len) * kv_token_bytes + 2.0 * mpb::kQWidth * sizeof(float) +
-                          double(pages) * sizeof(int32_t);
+            const double own = 2.0 * mpb::kQWidth * sizeof(float) + double(pages) * sizeof(int32_t);
+            plan.bytes += double(len - first * block_tokens) * kv_token_bytes + own;
+            plan.logical_bytes += double(len) * kv_token_bytes + own;
         }
     }
+    // shared-prefix slots follow the decode work items in the partial array
+    for (int r = 0; r < rows; ++r)
+        if (plan.nx[r]) plan.x0[r] += int(plan.work.size());
 }
 
 }  // namespace
@@ -157,6 +270,8 @@ struct mp_context {
     float *keys = nullptr, *values = nullptr;
     uint64_t pool_elements = 0;
     int32_t* tables = nullptr;
+    // host mirror of the device block tables (shared-prefix grouping reads it)
+    std::vector<int32_t> h_tables;
     float *rope_cos = nullptr, *rope_sin = nullptr;
     // workspace (GEMM inputs as hi/lo halves)
     float *x = nullptr, *qkv = nullptr, *q = nullptr, *logits = nullptr, *partial = nullptr;
@@ -181,7 +296,10 @@ struct mp_context {
     uint64_t* h_cow = nullptr;
     size_t cow_capacity = 0;
     // current step
-    int rows = 0, seqs = 0, work_count = 0, prefill_count = 0, entry_count = 0, region_count = 0, region_rows = 0;
+    int rows = 0, seqs = 0, work_count = 0, prefill_count = 0, prefix_count = 0, entry_count = 0, region_count = 0,
+        region_rows = 0;
+    size_t extra_capacity = 0, prefix_capacity = 0;
+    uint64_t step_prefix_rows = 0, step_prefix_tokens = 0;
     size_t off_entries = 0, off_regions = 0, entry_capacity = 0, region_capacity = 0;
     bool cow_timing = false, cow_timed = false;
     cudaEvent_t cow_events[2] = {nullptr, nullptr};
@@ -190,7 +308,8 @@ struct mp_context {
     uint64_t step_launches = 0, step_h2d = 0, step_d2h = 0;
     float cow_ms = 0.f;
     size_t off_tokens = 0, off_pos = 0, off_slot = 0, off_len = 0, off_splits = 0, off_work0 = 0, off_last = 0,
-           off_work = 0, off_prefill = 0;
+           off_work = 0, off_prefill = 0, off_x0 = 0, off_nx = 0, off_group_rows = 0, off_group_row0 = 0,
+           off_group_slot = 0, off_prefix = 0;
     size_t prefill_capacity = 0;
     bool prepared = false;
     AttnPlan plan;
@@ -443,6 +562,7 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         cuda_check(cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming), "create event");
         for (auto& e : c->mark) cuda_check(cudaEventCreate(&e), "create timer event");
         cuda_check(mpb::configure_attention(), "configure attention kernel");
+        cuda_check(mpb::configure_prefix_attention(), "configure shared-prefix attention kernel");
         cuda_check(mpb::configure_prefill_attention(), "configure prefill attention kernel");
         const size_t H = m.hidden, I = m.intermediate, L = m.layers, V = m.vocabulary;
         cuda_check(mpb::configure_tc_gemm(), "configure tensor-core GEMM");
@@ -467,6 +587,7 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         const size_t table_elements = size_t(r.max_sequences) * r.table_stride;
         c->tables = device_alloc<int32_t>(table_elements, "block tables");
         cuda_check(cudaMemsetAsync(c->tables, 0xff, table_elements * sizeof(int32_t), c->stream), "clear tables");
+        c->h_tables.assign(table_elements, -1);
         // RoPE tables, computed exactly as the CPU runner computes each angle
         // (miniprefix/src/backend/cpu/llama_runner.cpp:19-20).
         {
@@ -521,7 +642,11 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         encode_map(&mp.head_hi, c->head.hi, V, H, bn);
         encode_map(&mp.head_lo, c->head.lo, V, H, bn);
         c->work_capacity = max_work(r);
-        c->partial = device_alloc<float>(c->work_capacity * mpb::kHeads * (mpb::kHeadDim + 2), "attention partials");
+        // shared-prefix slots (rows x chunks) and prefix work items of one step
+        c->extra_capacity = 8192;
+        c->prefix_capacity = 8192;
+        c->partial = device_alloc<float>((c->work_capacity + c->extra_capacity) * mpb::kHeads * (mpb::kHeadDim + 2),
+                                         "attention partials");
         c->counters = device_alloc<unsigned>(T, "attention counters");
         cuda_check(cudaMemsetAsync(c->counters, 0, T * sizeof(unsigned), c->stream), "zero counters");
         c->error = device_alloc<unsigned>(1, "error word");
@@ -530,7 +655,7 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         c->entry_capacity = S * size_t(r.table_stride);
         c->region_capacity = S;
         c->meta_capacity = 6 * T + S + 4 * c->work_capacity + 8 * c->prefill_capacity + 2 * c->entry_capacity +
-                           10 * c->region_capacity + 2;
+                           10 * c->region_capacity + 2 + 4 * T + 2 + 8 * c->prefix_capacity;
         for (auto& e : c->cow_events) cuda_check(cudaEventCreate(&e), "create cow timing event");
         for (auto& e : c->fwd_events) cuda_check(cudaEventCreate(&e), "create forward timing event");
         c->meta = device_alloc<int32_t>(c->meta_capacity, "step metadata");
@@ -617,6 +742,7 @@ int mp_table_write(mp_context* c, int32_t slot, int32_t first, const int32_t* bl
         for (int i = 0; i < count; ++i) {
             c->h_patch[2 * i] = slot * c->rt.table_stride + first + i;
             c->h_patch[2 * i + 1] = blocks[i];
+            c->h_tables[size_t(slot) * c->rt.table_stride + first + i] = blocks[i];
         }
         cuda_check(cudaMemcpyAsync(c->patch, c->h_patch, size_t(count) * 8, cudaMemcpyHostToDevice, c->stream),
                    "upload block table entries");
@@ -701,8 +827,28 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         const int T = int(total);
         for (int i = 0; i < T; ++i)
             if (tokens[i] < 0 || tokens[i] >= c->model.vocabulary) fail(MP_ERR_INVALID, "invalid token");
-        plan_attention(seqs, count, r.block_tokens, 0, c->plan);
-        const size_t W = c->plan.work.size(), P = c->plan.prefill.size();
+        // the device applies this step's table entries first; so does the mirror
+        // (restored below if the step is rejected before it is queued)
+        std::vector<std::pair<size_t, int32_t>> mirror_undo;
+        mirror_undo.reserve(size_t(entry_count));
+        for (int i = 0; i < entry_count; ++i) {
+            const size_t at = size_t(entries[i].slot) * r.table_stride + entries[i].index;
+            mirror_undo.push_back({at, c->h_tables[at]});
+            c->h_tables[at] = entries[i].block;
+        }
+        struct MirrorGuard {
+            std::vector<int32_t>& tables;
+            std::vector<std::pair<size_t, int32_t>>& undo;
+            bool keep = false;
+            ~MirrorGuard() {
+                if (!keep)
+                    for (auto it = undo.rbegin(); it != undo.rend(); ++it) tables[it->first] = it->second;
+            }
+        } mirror_guard{c->h_tables, mirror_undo};
+        plan_attention(seqs, count, r.block_tokens, r.table_stride, c->h_tables, 0, c->extra_capacity,
+                       c->prefix_capacity, c->plan);
+        const size_t W = c->plan.work.size(), P = c->plan.prefill.size(), X = c->plan.prefix.size();
+        const size_t G = c->plan.group_slot.size();
         if (W > c->work_capacity) fail(MP_ERR_INVALID, "attention work list exceeds capacity");
         if (P > c->prefill_capacity) fail(MP_ERR_INVALID, "prefill work list exceeds capacity");
         // layout: tokens | pos | slot | len | splits | work0 | last | work
@@ -718,7 +864,13 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         c->off_last = c->off_work0 + T;
         c->off_work = c->off_last + count;
         c->off_prefill = c->off_work + 4 * W;
-        c->off_entries = c->off_prefill + 8 * P;
+        c->off_x0 = c->off_prefill + 8 * P;
+        c->off_nx = c->off_x0 + T;
+        c->off_group_rows = c->off_nx + T;
+        c->off_group_row0 = c->off_group_rows + c->plan.group_rows.size();
+        c->off_group_slot = c->off_group_row0 + G + 1;
+        c->off_prefix = c->off_group_slot + G;
+        c->off_entries = c->off_prefix + 8 * X;
         c->off_regions = (c->off_entries + 2 * size_t(entry_count) + 1) & ~size_t(1);  // 8-byte aligned
         std::memcpy(h + c->off_tokens, tokens, size_t(T) * 4);
         int row = 0;
@@ -734,6 +886,12 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         std::memcpy(h + c->off_work0, c->plan.work0.data(), size_t(T) * 4);
         std::memcpy(h + c->off_work, c->plan.work.data(), W * sizeof(mpb::AttnWork));
         std::memcpy(h + c->off_prefill, c->plan.prefill.data(), P * sizeof(mpb::PrefillWork));
+        std::memcpy(h + c->off_x0, c->plan.x0.data(), size_t(T) * 4);
+        std::memcpy(h + c->off_nx, c->plan.nx.data(), size_t(T) * 4);
+        std::memcpy(h + c->off_group_rows, c->plan.group_rows.data(), c->plan.group_rows.size() * 4);
+        std::memcpy(h + c->off_group_row0, c->plan.group_row0.data(), (G + 1) * 4);
+        std::memcpy(h + c->off_group_slot, c->plan.group_slot.data(), G * 4);
+        std::memcpy(h + c->off_prefix, c->plan.prefix.data(), X * sizeof(mpb::PrefixWork));
         for (int i = 0; i < entry_count; ++i) {
             h[c->off_entries + 2 * i] = entries[i].slot * c->rt.table_stride + entries[i].index;
             h[c->off_entries + 2 * i + 1] = entries[i].block;
@@ -747,10 +905,23 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         c->seqs = count;
         c->work_count = int(W);
         c->prefill_count = int(P);
+        c->prefix_count = int(X);
+        c->step_prefix_rows = c->plan.group_rows.size();
+        c->step_prefix_tokens = 0;
+        for (int g = 0; g < int(G); ++g) {
+            const auto& pl = c->plan;
+            const int n = pl.group_row0[g + 1] - pl.group_row0[g];
+            int tokens = 0;
+            for (size_t w = 0; w < pl.prefix.size(); ++w)
+                if (pl.prefix[w].group == g && pl.prefix[w].kv_head == 0 && pl.prefix[w].q_begin == 0)
+                    tokens += pl.prefix[w].tok_end - pl.prefix[w].tok_begin;
+            c->step_prefix_tokens += uint64_t(n) * tokens;
+        }
         c->entry_count = entry_count;
         c->region_count = region_count;
         c->region_rows = region_rows;
         c->prepared = true;
+        mirror_guard.keep = true;
     });
 }
 
@@ -769,7 +940,8 @@ int mp_forward_launch(mp_context* c) {
         // down (+1 input norm after layer 0, +1 per attention kind present); final
         // norm, head, argmax; table patch / COW if any
         c->step_launches = uint64_t(c->entry_count > 0) + uint64_t(c->region_count > 0 && c->region_rows > 0) + 1 +
-                           uint64_t(m.layers) * (6 + uint64_t(c->prefill_count > 0) + uint64_t(c->work_count > 0)) +
+                           uint64_t(m.layers) * (6 + uint64_t(c->prefill_count > 0) + uint64_t(c->work_count > 0) +
+                                                 uint64_t(c->prefix_count > 0)) +
                            uint64_t(m.layers - 1) + 3;
         cuda_check(mpb::launch_table_patch(meta + c->off_entries, c->entry_count, c->tables,
                                            int64_t(r.max_sequences) * r.table_stride, c->error, st),
@@ -819,6 +991,8 @@ int mp_forward_launch(mp_context* c) {
         ap.row_len = meta + c->off_len;
         ap.row_splits = meta + c->off_splits;
         ap.row_work0 = meta + c->off_work0;
+        ap.row_x0 = meta + c->off_x0;
+        ap.row_nx = meta + c->off_nx;
         ap.work = reinterpret_cast<const mpb::AttnWork*>(meta + c->off_work);
         ap.work_count = c->work_count;
         ap.partial = c->partial;
@@ -827,6 +1001,24 @@ int mp_forward_launch(mp_context* c) {
         ap.out_lo = c->attn.lo;
         ap.out_stride = H;
         ap.error = c->error;
+        mpb::PrefixParams xp{};
+        xp.q = c->q;
+        xp.q_stride = H;
+        xp.keys = c->keys;
+        xp.values = c->values;
+        xp.layers = m.layers;
+        xp.block_tokens = r.block_tokens;
+        xp.max_blocks = r.max_blocks;
+        xp.tables = c->tables;
+        xp.table_stride = r.table_stride;
+        xp.group_rows = meta + c->off_group_rows;
+        xp.group_row0 = meta + c->off_group_row0;
+        xp.group_slot = meta + c->off_group_slot;
+        xp.row_x0 = meta + c->off_x0;
+        xp.work = reinterpret_cast<const mpb::PrefixWork*>(meta + c->off_prefix);
+        xp.work_count = c->prefix_count;
+        xp.partial = c->partial;
+        xp.error = c->error;
         mpb::PrefillParams pp{};
         pp.q = c->q;
         pp.q_stride = H;
@@ -874,8 +1066,10 @@ int mp_forward_launch(mp_context* c) {
             cuda_check(mpb::launch_rope_append(ra, st), "rope/append launch");
             ap.layer = l;
             pp.layer = l;
+            xp.layer = l;
             if (c->profile) record_attention_event(c);
             cuda_check(mpb::launch_prefill_attention(pp, st), "prefill attention launch");
+            cuda_check(mpb::launch_prefix_attention(xp, st), "shared-prefix attention launch");
             cuda_check(mpb::launch_paged_attention(ap, st), "attention launch");
             if (c->profile) record_attention_event(c);
             gemm(mp.attn_hi, mp.attn_lo, mp.wo_hi, mp.wo_lo, T, H, H, l * H, c->x, H, mpb::Epilogue::AddTo, "o gemm");
@@ -926,6 +1120,8 @@ int mp_forward_collect(mp_context* c, int32_t* out_tokens, int32_t* out_finite, 
             c->counters_total.forward_ms += ms;
             c->counters_total.kernel_launches += c->step_launches;
             c->counters_total.h2d_bytes += c->step_h2d;
+            c->counters_total.shared_prefix_rows += c->step_prefix_rows;
+            c->counters_total.shared_prefix_tokens += c->step_prefix_tokens;
             c->counters_total.d2h_bytes += size_t(S) * 8 + sizeof(unsigned) +
                                            (out_logits ? size_t(S) * c->model.vocabulary * 4 : 0);
         }

@@ -44,15 +44,54 @@ struct AttnParams {
     const int32_t* row_len;     // causal context length of each query row
     const int32_t* row_splits;  // slices of each row
     const int32_t* row_work0;   // first work index of each row
+    const int32_t* row_x0;      // first shared-prefix partial slot of each row
+    const int32_t* row_nx;      // shared-prefix partial slots of each row (0: none)
     const AttnWork* work;
     int work_count;
-    float* partial;      // [work_count][9][66] slice results (rows with >1 slice)
+    float* partial;      // [slots][9][66] slice results: work items first, then shared-prefix slots
     unsigned* counters;  // [rows] zero between launches
     float* out;          // [rows][out_stride]; the TF32 hi half when out_lo is set
     float* out_lo;       // optional: lo halves (GEMM input), same layout
     int out_stride;
     unsigned* error;
 };
+
+// Shared-prefix decode attention (attention_shared.cu). Decode rows whose block
+// tables start with the same physical pages form a group; the group's shared
+// tokens are read once per launch for all its rows. One CTA per (group, kv head,
+// block of kPrefixQueries (row, head) query vectors, token chunk) writes
+// (max, sum, unnormalised output) partials that the decode kernel's split merge
+// combines with the rows' own slices.
+constexpr int kPrefixQueries = 64;
+struct PrefixWork {
+    int32_t group;
+    int32_t kv_head;
+    int32_t q_begin;    // first query vector (row_in_group * 3 + head_in_group)
+    int32_t q_count;    // 1..kPrefixQueries
+    int32_t tok_begin;  // shared tokens [tok_begin, tok_end) of this chunk
+    int32_t tok_end;
+    int32_t chunk;      // partial slot offset within each row's shared-prefix slots
+    int32_t pad;
+};
+struct PrefixParams {
+    const float* q;
+    int q_stride;
+    const float* keys;
+    const float* values;
+    int layers, layer, block_tokens, max_blocks;
+    const int32_t* tables;
+    int table_stride;
+    const int32_t* group_rows;  // batch rows of every group, concatenated
+    const int32_t* group_row0;  // [groups + 1] offsets into group_rows
+    const int32_t* group_slot;  // [groups] table slot whose table maps the shared pages
+    const int32_t* row_x0;      // first shared-prefix partial slot of each row
+    const PrefixWork* work;
+    int work_count;
+    float* partial;
+    unsigned* error;
+};
+cudaError_t launch_prefix_attention(const PrefixParams& p, cudaStream_t stream);
+cudaError_t configure_prefix_attention();
 
 // Chunked prefill: one CTA per (64-row query tile of one sequence, kv head).
 struct PrefillWork {
