@@ -1,4 +1,4 @@
-// Paged attention over the MiniPrefix K/V page pools (sm_100a).
+// Paged attention over the MiniPrefix K/V page pools (sm_100a), decode rows.
 //
 // Replaces the reference's attention_kernel (miniprefix/src/backend/cuda/
 // llama_runner.cu:33-48: one block per (row, q head), one token per iteration,
@@ -6,24 +6,34 @@
 // computes the CPU runner's attention (miniprefix/src/backend/cpu/
 // llama_runner.cpp:85-93): causal GQA, kv head = h / 3, scale 1/sqrt(64), softmax.
 //
-// Design (one query row, all 9 heads, per CTA; split-K over pages):
-//  * A CTA owns one slice [page_begin, page_end) of one query row's context. A row
-//    with more than one slice, or with shared-prefix partials computed earlier on
-//    the stream by attention_shared.cu, is merged by the last slice to finish
-//    (arrival counter per row), so one launch produces the final output.
-//  * K and V of 16 consecutive tokens form one stage. Runs of tokens that are
-//    contiguous inside a page (a page is [slot][192] floats for one layer) are
-//    moved by the bulk-copy engine (cp.async.bulk) into shared memory and
-//    complete on a per-stage mbarrier, so 2 stages stay in flight while one is
-//    consumed. Each K/V byte is read from HBM once for all 3 q heads of its group.
-//    192 threads and ~75 KB of shared memory let 3 CTAs share an SM.
-//  * Scores: 48 (token, kv head) pairs x 4 lanes; each lane keeps its 3 heads'
-//    16 query values in registers and dots one 64-byte quarter of the key row,
-//    quarters rotated by pair parity so the 8 lanes of a 128-bit phase hit
-//    distinct banks. Softmax: 16 lanes per head, online (running max / sum).
-//    P.V: one (kv head, dim) column per thread, 3 heads.
-//  * Tokens past the row length are masked by select (never by multiplying), so
-//    stale or uninitialised shared memory cannot leak NaN into the result.
+// Work: a row's context is cut into slices [page_begin, page_end) (work items).
+// Rows with several slices, or with shared-prefix partials written earlier on the
+// stream by attention_shared.cu, are merged per (row, kv head) by the last slice
+// to finish (an arrival counter per (row, kv head)), so one launch produces the
+// final output.
+//
+// CTA = 4 warps, warp-specialised, no block-wide barrier in the steady state:
+//  * warp 3 (producer) walks its work items -- one, or with a schedule, items
+//    pulled from a shared counter in the given order (persistent, one wave) --
+//    and for every 16-token stage writes a stage descriptor (item, row, first
+//    token, valid tokens, first/last flags) and moves the stage's K and V runs
+//    (contiguous inside a page: [slot][192] floats of one layer) into a ring of 3
+//    shared-memory stages with the bulk-copy engine (cp.async.bulk), completing
+//    on the stage's `full` mbarrier. It refills a stage once the three consumers
+//    released it (`empty` mbarrier, count 3).
+//  * warps 0..2 (consumers) each own one kv head and its 3 query heads. Lane =
+//    (token t of 8, quarter c of the 64 dims); two passes cover 16 tokens. A lane
+//    keeps its 3 heads' 16 query values (rotated by t so a 128-bit phase spans all
+//    banks) in registers. Scores are reduced over the quarters by shuffles, the
+//    online softmax over the 16 tokens by shuffles, probabilities go through a
+//    per-warp scratch row, and P.V accumulates dims (lane, lane + 32) of 3 heads.
+//  * Each consumer finishes a slice on its own: direct output for a single-slice
+//    row, else its partial (max, sum, unnormalised output) and the merge when it
+//    is the last arrival for (row, its kv head).
+// Every wait is bounded (common.cuh); a timeout sets the error word and the warp
+// stops. Tokens past the row length are masked by select (never by multiplying).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -31,23 +41,24 @@ namespace mpb {
 namespace {
 
 constexpr int kStageTokens = 16;
-constexpr int kThreads = 192;  // 48 (token, kv head) pairs x 4 lanes; 192 (kv head, dim) columns
 constexpr int kStages = 3;
+constexpr int kConsumers = kKvHeads;                   // 3 consumer warps
+constexpr int kThreads = (kConsumers + 1) * 32;        // + producer warp
 constexpr int kStageFloats = kStageTokens * kKvWidth;  // per pool
-constexpr size_t kAttnSmem = size_t(kStages) * 2 * kStageFloats * sizeof(float) +
-                             2 * kHeads * kStageTokens * sizeof(float) + 4 * kHeads * sizeof(float) +
-                             kStages * sizeof(uint64_t) + 16;
 
-struct Shared {
-    float* stages;  // stage i: K at stages + 2*i*kStageFloats, V right after
-    float* scores;  // [9][16]
-    float* probs;   // [9][16]
-    float* alpha;   // [9]
-    float* m;       // [9]
-    float* l;       // [9]
-    int* flag;      // [1] error / last-arriver broadcast
-    uint64_t* bar;  // [kStages]
+struct StageDesc {
+    int32_t work;     // work item index, -1: no more work
+    int32_t row;
+    int32_t token;    // first context token of the stage
+    int32_t n_valid;  // tokens of the stage inside the row (0..16)
+    int32_t flags;    // kFirst: first stage of its item; kLast: last
+    int32_t pad[3];
 };
+constexpr int kFirst = 1, kLast = 2;
+
+constexpr size_t kAttnSmem = size_t(kStages) * 2 * kStageFloats * sizeof(float) +         // K/V stages
+                             size_t(kConsumers) * kGroup * kStageTokens * sizeof(float) +  // probabilities
+                             kStages * sizeof(StageDesc) + 2 * kStages * sizeof(uint64_t) + 16;
 
 // Output element: plain FP32, or TF32 hi/lo halves when the caller asked for them.
 __device__ __forceinline__ void write_out(const AttnParams& p, size_t i, float v) {
@@ -61,18 +72,23 @@ __device__ __forceinline__ void write_out(const AttnParams& p, size_t i, float v
     }
 }
 
-// Issue the copies for context tokens [a, b) into stage buffers (warp 0 only).
-__device__ __forceinline__ void issue_stage(const AttnParams& p, const int32_t* table, int a, int b, float* kdst,
-                                            float* vdst, uint64_t* bar, int lane) {
+// Producer: copy context tokens [a, b) into stage buffers kdst/vdst; the whole
+// warp calls it. Lane L moves the run inside page a/bt + L. Page ids come from the
+// warp's window of staged table entries (lane i holds page win0 + i) when they
+// fall inside it, else from the table.
+__device__ __forceinline__ void issue_stage(const AttnParams& p, const int32_t* table, int win0, int window, int a,
+                                            int b, float* kdst, float* vdst, uint64_t* bar, int lane) {
     const int bt = p.block_tokens;
     const int first_page = a / bt;
     const int run_begin = max(a, (first_page + lane) * bt);
     const int run_end = min(b, (first_page + lane + 1) * bt);
+    const int page = first_page + lane;
+    const int rel = page - win0;
+    const int staged = __shfl_sync(0xffffffffu, window, rel & 31);
     if (lane == 0) mbar_arrive_expect_tx(bar, uint32_t(b - a) * 2u * kKvWidth * sizeof(float));
     __syncwarp();
     if (run_begin < run_end) {
-        const int page = first_page + lane;
-        int block = page < p.table_stride ? table[page] : -1;
+        int block = rel >= 0 && rel < 32 ? staged : (page < p.table_stride ? table[page] : -1);
         if (block < 0 || block >= p.max_blocks) {
             raise_error(p.error, kErrBounds);
             block = 0;  // stay in bounds; the error word fails the step
@@ -84,78 +100,131 @@ __device__ __forceinline__ void issue_stage(const AttnParams& p, const int32_t* 
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 3) paged_attention_kernel(const AttnParams p) {
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    Shared s;
-    {
-        float* f = reinterpret_cast<float*>(smem_raw);
-        s.stages = f;
-        f += 2 * kStages * kStageFloats;
-        s.scores = f; f += kHeads * kStageTokens;
-        s.probs = f; f += kHeads * kStageTokens;
-        s.alpha = f; f += kHeads;
-        s.m = f; f += kHeads;
-        s.l = f; f += kHeads;
-        s.flag = reinterpret_cast<int*>(f); f += kHeads;
-        s.bar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(f) + 7) & ~uintptr_t(7));
-    }
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const AttnWork w = p.work[blockIdx.x];
-    const int row = w.row;
-    const int len = p.row_len[row];
-    const int32_t* table = p.tables + size_t(p.row_slot[row]) * p.table_stride;
-    const int tok_begin = w.page_begin * p.block_tokens;
-    const int tok_end = min(w.page_end * p.block_tokens, len);
-    const int n_stages = tok_end > tok_begin ? (tok_end - tok_begin + kStageTokens - 1) / kStageTokens : 0;
-
-    if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) mbar_init(&s.bar[i], 1);
-        s.flag[0] = 0;
-        fence_barrier_init();
-    }
-    __syncthreads();
-    if (warp == 0)
-        for (int i = 0; i < kStages && i < n_stages; ++i) {
-            const int a = tok_begin + i * kStageTokens;
-            issue_stage(p, table, a, min(a + kStageTokens, tok_end), s.stages + 2 * i * kStageFloats,
-                        s.stages + (2 * i + 1) * kStageFloats, &s.bar[i], lane);
-        }
-
-    // Score identity: pair = (token st, kv head skh), 4 lanes per pair; each lane
-    // holds its kv group's 3 heads x 16 query values (4 of the 16 float4 chunks of
-    // a 64-dim row, rotated by pair parity so a 128-bit phase hits distinct banks).
-    const int pair = tid >> 2, sub = tid & 3;
-    const int st = pair / kKvHeads, skh = pair % kKvHeads, rot = pair & 1;
-    float4 qr[kGroup][4];
-    {
-        const float* qrow = p.q + size_t(row) * p.q_stride;
-#pragma unroll
-        for (int hh = 0; hh < kGroup; ++hh)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int chunk = sub + 4 * ((j + rot) & 3);
-                qr[hh][j] = *reinterpret_cast<const float4*>(qrow + (skh * kGroup + hh) * kHeadDim + 4 * chunk);
+__device__ void producer(const AttnParams& p, float* stages, StageDesc* desc, uint64_t* full, uint64_t* empty,
+                         bool persistent, unsigned* failed, int lane) {
+    uint32_t g = 0;  // stages issued so far
+    int item = blockIdx.x;
+    // a stage's previous use must have been released by the 3 consumers
+    auto acquire = [&](int buf) -> bool {
+        if (g < uint32_t(kStages)) return true;
+        return mbar_wait_bounded(&empty[buf], ((g / kStages) - 1) & 1);
+    };
+    while (true) {
+        if (item >= p.work_count) {
+            // no more work: a descriptor without copies releases the consumers
+            const int buf = g % kStages;
+            if (!acquire(buf)) {
+                if (lane == 0) atomicOr(failed, 1u);
+                return;
             }
+            if (lane == 0) {
+                desc[buf].work = -1;
+                mbar_arrive_expect_tx(&full[buf], 0);
+            }
+            return;
+        }
+        const int wi = p.order ? p.order[item] : item;
+        int next = 0;
+        if (lane == 0) next = persistent ? int(gridDim.x + atomicAdd(&p.sched[0], 1u)) : p.work_count;
+        next = __shfl_sync(0xffffffffu, next, 0);
+        const AttnWork w = p.work[wi];
+        const int row = w.row;
+        const int len = p.row_len[row];
+        const int32_t* table = p.tables + size_t(p.row_slot[row]) * p.table_stride;
+        const int tok_begin = w.page_begin * p.block_tokens;
+        const int tok_end = min(w.page_end * p.block_tokens, len);
+        const int n_stages = max(1, (tok_end - tok_begin + kStageTokens - 1) / kStageTokens);
+        // table entries of the slice's first 32 pages, one per lane, loaded once;
+        // the window moves on when a stage starts past it
+        int win0 = w.page_begin;
+        auto load_window = [&](int first) {
+            const int pg = first + lane;
+            return pg < w.page_end && pg < p.table_stride ? table[pg] : -1;
+        };
+        int window = load_window(win0);
+        for (int i = 0; i < n_stages; ++i) {
+            const int b = g % kStages;
+            {
+                const int first_page = (tok_begin + i * kStageTokens) / p.block_tokens;
+                if (first_page + (kStageTokens + p.block_tokens - 1) / p.block_tokens >= win0 + 32) {
+                    win0 = first_page;
+                    window = load_window(win0);
+                }
+            }
+            if (!acquire(b)) {
+                if (lane == 0) atomicOr(failed, 1u);
+                return;
+            }
+            const int a = tok_begin + i * kStageTokens;
+            const int e = min(a + kStageTokens, tok_end);
+            if (lane == 0) {
+                desc[b].work = wi;
+                desc[b].row = row;
+                desc[b].token = a;
+                desc[b].n_valid = max(0, e - a);
+                desc[b].flags = (i == 0 ? kFirst : 0) | (i == n_stages - 1 ? kLast : 0);
+            }
+            __syncwarp();
+            // buffers last read by the consumers (generic proxy) are now refilled by
+            // the bulk-copy engine (async proxy)
+            fence_proxy_async_shared();
+            if (e > a) {
+                issue_stage(p, table, win0, window, a, e, stages + 2 * b * kStageFloats,
+                            stages + (2 * b + 1) * kStageFloats, &full[b], lane);
+            } else if (lane == 0) {
+                mbar_arrive_expect_tx(&full[b], 0);  // an empty slice still reports
+            }
+            ++g;
+        }
+        item = next;
     }
-    // Softmax identity: 16 lanes per head (two heads per warp, warps 0..4).
-    const int shead = warp * 2 + (lane >> 4), stok = lane & 15;
-    // P.V identity: one (kv head, dim) column per thread, 3 heads.
-    const int pkh = tid / kHeadDim;
-    float acc[kGroup] = {0.f, 0.f, 0.f};
-    float m_run = -INFINITY, l_run = 0.f;  // of head `shead`
+}
 
-    for (int i = 0; i < n_stages; ++i) {
-        const int stage = i % kStages;
-        const int a = tok_begin + i * kStageTokens;
-        const int n_valid = min(kStageTokens, tok_end - a);
-        if (!mbar_wait_bounded(&s.bar[stage], (i / kStages) & 1)) s.flag[0] = 1;
-        {
-            const float* krow = s.stages + 2 * stage * kStageFloats + st * kKvWidth + skh * kHeadDim;
+__device__ void consumer(const AttnParams& p, const float* stages, const StageDesc* desc, uint64_t* full,
+                         uint64_t* empty, float* probs, unsigned* failed, int kh, int lane) {
+    const int t = lane >> 2, c = lane & 3;
+    float4 qr[kGroup][4];
+    float m_run[kGroup], l_run[kGroup], acc[kGroup][2];
+#pragma unroll
+    for (int hh = 0; hh < kGroup; ++hh) {
+        m_run[hh] = -INFINITY;
+        l_run[hh] = 0.f;
+        acc[hh][0] = acc[hh][1] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) qr[hh][j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    uint32_t g = 0;
+    while (true) {
+        const int buf = g % kStages;
+        if (!mbar_wait_bounded(&full[buf], (g / kStages) & 1)) {
+            if (lane == 0) atomicOr(failed, 1u);
+            return;
+        }
+        const StageDesc d = desc[buf];
+        if (d.work < 0) return;
+        if (d.flags & kFirst) {
+            const float* qrow = p.q + size_t(d.row) * p.q_stride + kh * kGroup * kHeadDim;
+#pragma unroll
+            for (int hh = 0; hh < kGroup; ++hh) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    qr[hh][j] = *reinterpret_cast<const float4*>(qrow + hh * kHeadDim + c * 16 + 4 * ((j + t) & 3));
+                m_run[hh] = -INFINITY;
+                l_run[hh] = 0.f;
+                acc[hh][0] = acc[hh][1] = 0.f;
+            }
+        }
+        const float* kst = stages + 2 * buf * kStageFloats + kh * kHeadDim + c * 16;
+        const float* vst = stages + (2 * buf + 1) * kStageFloats + kh * kHeadDim + lane;
+        // scores of tokens t and t + 8 for the 3 heads
+        float s[2][kGroup];
+#pragma unroll
+        for (int ps = 0; ps < 2; ++ps) {
+            const float* krow = kst + (t + 8 * ps) * kKvWidth;
             float part[kGroup] = {0.f, 0.f, 0.f};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const int chunk = sub + 4 * ((j + rot) & 3);
-                const float4 kv = *reinterpret_cast<const float4*>(krow + 4 * chunk);
+                const float4 kv = *reinterpret_cast<const float4*>(krow + 4 * ((j + t) & 3));
 #pragma unroll
                 for (int hh = 0; hh < kGroup; ++hh) {
                     part[hh] = fmaf(qr[hh][j].x, kv.x, part[hh]);
@@ -164,120 +233,156 @@ __global__ void __launch_bounds__(kThreads, 3) paged_attention_kernel(const Attn
                     part[hh] = fmaf(qr[hh][j].w, kv.w, part[hh]);
                 }
             }
+            const bool valid = t + 8 * ps < d.n_valid;
 #pragma unroll
             for (int hh = 0; hh < kGroup; ++hh) {
                 part[hh] += __shfl_xor_sync(0xffffffffu, part[hh], 1);
                 part[hh] += __shfl_xor_sync(0xffffffffu, part[hh], 2);
-            }
-            if (sub < kGroup) {
-                const float sc = sub == 0 ? part[0] : (sub == 1 ? part[1] : part[2]);
-                s.scores[(skh * kGroup + sub) * kStageTokens + st] = st < n_valid ? sc * 0.125f : -INFINITY;
+                s[ps][hh] = valid ? part[hh] * 0.125f : -INFINITY;
             }
         }
-        __syncthreads();
-        if (s.flag[0]) break;
-        if (warp < 5) {
-            // all 32 lanes take part in the shuffles; heads >= 9 use a dummy row
-            const bool live = shead < kHeads;
-            const float sc = live ? s.scores[shead * kStageTokens + stok] : -INFINITY;
-            float mx = sc;
-#pragma unroll
-            for (int o = 8; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            const float m_new = fmaxf(m_run, mx);
-            const float alpha = live ? expf(m_run - m_new) : 0.f;
-            const float pr = live ? expf(sc - m_new) : 0.f;
-            float sum = pr;
-#pragma unroll
-            for (int o = 8; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if (live) {
-                l_run = l_run * alpha + sum;
-                m_run = m_new;
-                s.probs[shead * kStageTokens + stok] = pr;
-                if (stok == 0) s.alpha[shead] = alpha;
-            }
-        }
-        __syncthreads();
-        {
-            const float* vbase = s.stages + (2 * stage + 1) * kStageFloats + tid;
-            const float* pb = s.probs + (pkh * kGroup) * kStageTokens;
-#pragma unroll
-            for (int hh = 0; hh < kGroup; ++hh) acc[hh] *= s.alpha[pkh * kGroup + hh];
-#pragma unroll
-            for (int t = 0; t < kStageTokens; ++t) {
-                const float v = t < n_valid ? vbase[t * kKvWidth] : 0.f;
-#pragma unroll
-                for (int hh = 0; hh < kGroup; ++hh) acc[hh] = fmaf(pb[hh * kStageTokens + t], v, acc[hh]);
-            }
-        }
-        __syncthreads();
-        if (warp == 0 && i + kStages < n_stages) {
-            fence_proxy_async_shared();
-            const int a2 = tok_begin + (i + kStages) * kStageTokens;
-            issue_stage(p, table, a2, min(a2 + kStageTokens, tok_end), s.stages + 2 * stage * kStageFloats,
-                        s.stages + (2 * stage + 1) * kStageFloats, &s.bar[stage], lane);
-        }
-    }
-    if (s.flag[0]) {
-        if (tid == 0) raise_error(p.error, kErrTimeout);
-        return;
-    }
-    if (warp < 5 && stok == 0 && shead < kHeads) {
-        s.m[shead] = m_run;
-        s.l[shead] = l_run;
-    }
-    __syncthreads();
-    const int splits = p.row_splits[row];
-    // shared-prefix partials of this row (written by the prefix kernel earlier on
-    // the same stream) join the merge as extra slots
-    const int nx = p.row_nx ? p.row_nx[row] : 0;
-    const bool direct = splits == 1 && nx == 0;
-    {
-        const int d = tid % kHeadDim;
+        // online softmax over the stage's 16 tokens (lanes differ in t across bits 2..4)
 #pragma unroll
         for (int hh = 0; hh < kGroup; ++hh) {
-            const int h = pkh * kGroup + hh;
-            if (direct) {
-                write_out(p, size_t(row) * p.out_stride + h * kHeadDim + d, acc[hh] / s.l[h]);
-            } else {
-                float* part = p.partial + (size_t(blockIdx.x) * kHeads + h) * (kHeadDim + 2);
-                part[2 + d] = acc[hh];
-                if (d == 0) {
-                    part[0] = s.m[h];
-                    part[1] = s.l[h];
+            float mx = fmaxf(s[0][hh], s[1][hh]);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float m_new = fmaxf(m_run[hh], mx);
+            const float ms = m_new == -INFINITY ? 0.f : m_new;  // no valid token yet: all terms stay 0
+            const float alpha = expf(m_run[hh] - ms);
+            const float p0 = expf(s[0][hh] - ms), p1 = expf(s[1][hh] - ms);
+            float sum = p0 + p1;
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+            l_run[hh] = l_run[hh] * alpha + sum;
+            m_run[hh] = m_new;
+            acc[hh][0] *= alpha;
+            acc[hh][1] *= alpha;
+            if (c == 0) {
+                probs[hh * kStageTokens + t] = p0;
+                probs[hh * kStageTokens + t + 8] = p1;
+            }
+        }
+        __syncwarp();
+        // P.V: dims (lane, lane + 32) of this kv head
+#pragma unroll
+        for (int q4 = 0; q4 < kStageTokens / 4; ++q4) {
+            float4 pr[kGroup];
+#pragma unroll
+            for (int hh = 0; hh < kGroup; ++hh)
+                pr[hh] = *reinterpret_cast<const float4*>(probs + hh * kStageTokens + 4 * q4);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int tt = 4 * q4 + u;
+                const bool valid = tt < d.n_valid;
+                const float v0 = valid ? vst[tt * kKvWidth] : 0.f;
+                const float v1 = valid ? vst[tt * kKvWidth + 32] : 0.f;
+#pragma unroll
+                for (int hh = 0; hh < kGroup; ++hh) {
+                    const float pv = u == 0 ? pr[hh].x : (u == 1 ? pr[hh].y : (u == 2 ? pr[hh].z : pr[hh].w));
+                    acc[hh][0] = fmaf(pv, v0, acc[hh][0]);
+                    acc[hh][1] = fmaf(pv, v1, acc[hh][1]);
                 }
             }
         }
-    }
-    if (direct) return;
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const unsigned prev = atomicAdd(&p.counters[row], 1u);
-        s.flag[0] = prev == unsigned(splits - 1) ? 2 : 0;
-    }
-    __syncthreads();
-    if (s.flag[0] != 2) return;
-    __threadfence();
-    // Last slice of this row: merge the shared-prefix slots, then all slices'
-    // (m, l, acc), in that fixed order.
-    const int w0 = p.row_work0[row];
-    const int x0 = nx ? p.row_x0[row] : 0;
-    auto slot = [&](int k) { return k < nx ? x0 + k : w0 + (k - nx); };
-    for (int o = tid; o < kHeads * kHeadDim; o += kThreads) {
-        const int h = o / kHeadDim, d = o % kHeadDim;
-        float mx = -INFINITY;
-        for (int k = 0; k < nx + splits; ++k)
-            mx = fmaxf(mx, __ldcg(p.partial + (size_t(slot(k)) * kHeads + h) * (kHeadDim + 2)));
-        float num = 0.f, den = 0.f;
-        for (int k = 0; k < nx + splits; ++k) {
-            const float* part = p.partial + (size_t(slot(k)) * kHeads + h) * (kHeadDim + 2);
-            const float sc = expf(__ldcg(part) - mx);
-            den = fmaf(__ldcg(part + 1), sc, den);
-            num = fmaf(__ldcg(part + 2 + d), sc, num);
+        __syncwarp();  // every lane is done with the stage and the scratch row
+        if (lane == 0) mbar_arrive(&empty[buf]);
+        ++g;
+        if (!(d.flags & kLast)) continue;
+
+        // ---- slice finished: output, or partial + merge for (row, kv head)
+        const int row = d.row;
+        const int splits = p.row_splits[row];
+        const int nx = p.row_nx ? p.row_nx[row] : 0;
+        if (splits == 1 && nx == 0) {
+#pragma unroll
+            for (int hh = 0; hh < kGroup; ++hh) {
+                const size_t o = size_t(row) * p.out_stride + (kh * kGroup + hh) * kHeadDim;
+                write_out(p, o + lane, acc[hh][0] / l_run[hh]);
+                write_out(p, o + lane + 32, acc[hh][1] / l_run[hh]);
+            }
+            continue;
         }
-        write_out(p, size_t(row) * p.out_stride + o, num / den);
+#pragma unroll
+        for (int hh = 0; hh < kGroup; ++hh) {
+            float* part = p.partial + (size_t(d.work) * kHeads + kh * kGroup + hh) * (kHeadDim + 2);
+            part[2 + lane] = acc[hh][0];
+            part[2 + lane + 32] = acc[hh][1];
+            if (lane == 0) {
+                part[0] = m_run[hh];
+                part[1] = l_run[hh];
+            }
+        }
+        __threadfence();
+        __syncwarp();
+        unsigned prev = 0;
+        unsigned* counter = p.counters + size_t(row) * kKvHeads + kh;
+        if (lane == 0) prev = atomicAdd(counter, 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev != unsigned(splits - 1)) continue;
+        __threadfence();
+        // last slice of (row, kv head): merge the shared-prefix slots, then all
+        // slices, in that fixed order
+        const int w0 = p.row_work0[row];
+        const int x0 = nx ? p.row_x0[row] : 0;
+#pragma unroll
+        for (int hh = 0; hh < kGroup; ++hh) {
+            const int h = kh * kGroup + hh;
+            float mx = -INFINITY;
+            for (int k = 0; k < nx + splits; ++k) {
+                const int sl = k < nx ? x0 + k : w0 + (k - nx);
+                mx = fmaxf(mx, __ldcg(p.partial + (size_t(sl) * kHeads + h) * (kHeadDim + 2)));
+            }
+            float n0 = 0.f, n1 = 0.f, den = 0.f;
+            for (int k = 0; k < nx + splits; ++k) {
+                const int sl = k < nx ? x0 + k : w0 + (k - nx);
+                const float* part = p.partial + (size_t(sl) * kHeads + h) * (kHeadDim + 2);
+                const float sc = expf(__ldcg(part) - mx);
+                den = fmaf(__ldcg(part + 1), sc, den);
+                n0 = fmaf(__ldcg(part + 2 + lane), sc, n0);
+                n1 = fmaf(__ldcg(part + 2 + lane + 32), sc, n1);
+            }
+            const size_t o = size_t(row) * p.out_stride + h * kHeadDim;
+            write_out(p, o + lane, n0 / den);
+            write_out(p, o + lane + 32, n1 / den);
+        }
+        if (lane == 0) *counter = 0u;  // ready for the next launch
     }
-    if (tid == 0) p.counters[row] = 0u;  // ready for the next launch
+}
+
+__global__ void __launch_bounds__(kThreads, 3) paged_attention_kernel(const AttnParams p) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    float* stages = reinterpret_cast<float*>(smem_raw);
+    float* probs = stages + 2 * kStages * kStageFloats;  // [3 consumers][3][16]
+    StageDesc* desc = reinterpret_cast<StageDesc*>(probs + kConsumers * kGroup * kStageTokens);
+    uint64_t* full = reinterpret_cast<uint64_t*>(desc + kStages);
+    uint64_t* empty = full + kStages;
+    unsigned* failed = reinterpret_cast<unsigned*>(empty + kStages);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kConsumers);
+        }
+        *failed = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const bool persistent = p.sched != nullptr;
+    if (warp == kConsumers)
+        producer(p, stages, desc, full, empty, persistent, failed, lane);
+    else
+        consumer(p, stages, desc, full, empty, probs + warp * kGroup * kStageTokens, failed, warp, lane);
+    __syncthreads();
+    if (tid == 0 && *failed) raise_error(p.error, kErrTimeout);
+    if (persistent && tid == 0 && atomicAdd(&p.sched[1], 1u) == gridDim.x - 1) {
+        // the last CTA to leave resets the schedule for the next launch
+        p.sched[0] = 0u;
+        p.sched[1] = 0u;
+    }
 }
 
 }  // namespace
@@ -288,7 +393,9 @@ cudaError_t configure_attention() {
 
 cudaError_t launch_paged_attention(const AttnParams& p, cudaStream_t stream) {
     if (p.work_count <= 0) return cudaSuccess;
-    paged_attention_kernel<<<p.work_count, kThreads, kAttnSmem, stream>>>(p);
+    // persistent: one wave of 3 CTAs per SM pulls the work items
+    const int grid = p.sched ? std::min(p.work_count, kAttnPersistentCtas) : p.work_count;
+    paged_attention_kernel<<<grid, kThreads, kAttnSmem, stream>>>(p);
     return cudaGetLastError();
 }
 

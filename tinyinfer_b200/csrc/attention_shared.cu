@@ -16,9 +16,10 @@
 //
 // CTA = (group, kv head, 64 query vectors, token chunk), 128 threads. Per 32-token
 // tile (double-buffered 16-byte cp.async gathers through the group's table):
-//   S[64][32] = Q K^T / 8: thread (query qi = tid/2, tokens sub + 2k) 16 scores;
-//   online softmax per query vector (2 lanes per vector, shuffles);
-//   O[64][64] = O * alpha + P V: thread (qi, dims sub*4 + 8k) 32 outputs.
+//   S[64][32] = Q K^T / 8: thread (queries qp and qp + 32, tokens sub + 4k) 16 scores,
+//     2 query and 8 key float4 loads per 64 FMA;
+//   online softmax per query vector (4 lanes per vector, shuffles);
+//   O[64][64] = O * alpha + P V: thread (both queries, dims sub*4 + 16k) 32 outputs.
 // All FP32 FMA. Tokens past the chunk end are masked by select, never by
 // multiplying, so stale shared memory cannot reach the result.
 #include "common.cuh"
@@ -102,11 +103,14 @@ __global__ void __launch_bounds__(kPThreads, 3) prefix_attention_kernel(const Pr
     const int n_tiles = (w.tok_end - w.tok_begin + kPT - 1) / kPT;
     load_tile(p, table, kh, w.tok_begin, w.tok_end, Kt, Vt, tid);
 
-    const int qi = tid >> 1, sub = tid & 1;
-    float acc[32];
+    // Thread = (query pair qp / qp + 32, token / dim quarter sub).
+    const int qp = tid >> 2, sub = tid & 3;
+    float acc[2][16];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[a][i] = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
 
     for (int i = 0; i < n_tiles; ++i) {
         const int buf = i & 1;
@@ -123,79 +127,103 @@ __global__ void __launch_bounds__(kPThreads, 3) prefix_attention_kernel(const Pr
         const float* kt = Kt + buf * kPT * kRowStride;
         const float* vt = Vt + buf * kPT * kRowStride;
 
-        // scores of tokens sub + 2k
-        float s[16];
+        // S: queries qp, qp + 32 x tokens sub + 4k
+        float s[2][8];
 #pragma unroll
-        for (int k = 0; k < 16; ++k) s[k] = 0.f;
-        const float* qrow = Qs + qi * kRowStride;
-#pragma unroll 4
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) s[a][k] = 0.f;
+        const float* q0 = Qs + qp * kRowStride;
+        const float* q1 = Qs + (qp + 32) * kRowStride;
+#pragma unroll 2
         for (int d4 = 0; d4 < kHeadDim / 4; ++d4) {
-            const float4 qv = *reinterpret_cast<const float4*>(qrow + 4 * d4);
+            const float4 qa = *reinterpret_cast<const float4*>(q0 + 4 * d4);
+            const float4 qb = *reinterpret_cast<const float4*>(q1 + 4 * d4);
 #pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                const float4 kv = *reinterpret_cast<const float4*>(kt + (sub + 2 * k) * kRowStride + 4 * d4);
-                s[k] = fmaf(qv.x, kv.x, s[k]);
-                s[k] = fmaf(qv.y, kv.y, s[k]);
-                s[k] = fmaf(qv.z, kv.z, s[k]);
-                s[k] = fmaf(qv.w, kv.w, s[k]);
+            for (int k = 0; k < 8; ++k) {
+                const float4 kv = *reinterpret_cast<const float4*>(kt + (sub + 4 * k) * kRowStride + 4 * d4);
+                s[0][k] = fmaf(qa.x, kv.x, s[0][k]);
+                s[0][k] = fmaf(qa.y, kv.y, s[0][k]);
+                s[0][k] = fmaf(qa.z, kv.z, s[0][k]);
+                s[0][k] = fmaf(qa.w, kv.w, s[0][k]);
+                s[1][k] = fmaf(qb.x, kv.x, s[1][k]);
+                s[1][k] = fmaf(qb.y, kv.y, s[1][k]);
+                s[1][k] = fmaf(qb.z, kv.z, s[1][k]);
+                s[1][k] = fmaf(qb.w, kv.w, s[1][k]);
             }
         }
-        float mx = -INFINITY;
+        // online softmax; the 4 lanes of a query pair hold its 32 scores
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            s[k] = sub + 2 * k < n_valid ? s[k] * 0.125f : -INFINITY;
-            mx = fmaxf(mx, s[k]);
+        for (int a = 0; a < 2; ++a) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                s[a][k] = sub + 4 * k < n_valid ? s[a][k] * 0.125f : -INFINITY;
+                mx = fmaxf(mx, s[a][k]);
+            }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float m_new = fmaxf(m_run[a], mx);
+            const float alpha = expf(m_run[a] - m_new);
+            float sum = 0.f;
+            float* prow = Ps + (qp + 32 * a) * kPStride + sub;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float pr = expf(s[a][k] - m_new);
+                sum += pr;
+                prow[4 * k] = pr;
+            }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            l_run[a] = l_run[a] * alpha + sum;
+            m_run[a] = m_new;
+#pragma unroll
+            for (int i2 = 0; i2 < 16; ++i2) acc[a][i2] *= alpha;
         }
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        const float m_new = fmaxf(m_run, mx);
-        const float alpha = expf(m_run - m_new);
-        float sum = 0.f;
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            const float pr = expf(s[k] - m_new);
-            sum += pr;
-            Ps[qi * kPStride + sub + 2 * k] = pr;
-        }
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        l_run = l_run * alpha + sum;
-        m_run = m_new;
-#pragma unroll
-        for (int i2 = 0; i2 < 32; ++i2) acc[i2] *= alpha;
-        __syncwarp();  // the two lanes of a query vector read each other's probabilities
+        __syncwarp();  // the 4 lanes of a query pair read each other's probabilities
 
-        // O += P V over the tile: dims sub*4 + 8k
-        const float* prow = Ps + qi * kPStride;
+        // O += P V: dims sub*4 + 16k of both queries
+        const float* p0 = Ps + qp * kPStride;
+        const float* p1 = Ps + (qp + 32) * kPStride;
 #pragma unroll 4
         for (int j = 0; j < kPT; ++j) {
-            const float pr = prow[j];
+            const float pa = p0[j], pb = p1[j];
             const float* vrow = vt + j * kRowStride + sub * 4;
             const bool valid = j < n_valid;
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                float4 v = *reinterpret_cast<const float4*>(vrow + 8 * k);
+            for (int k = 0; k < 4; ++k) {
+                float4 v = *reinterpret_cast<const float4*>(vrow + 16 * k);
                 if (!valid) v = make_float4(0.f, 0.f, 0.f, 0.f);
-                acc[4 * k] = fmaf(pr, v.x, acc[4 * k]);
-                acc[4 * k + 1] = fmaf(pr, v.y, acc[4 * k + 1]);
-                acc[4 * k + 2] = fmaf(pr, v.z, acc[4 * k + 2]);
-                acc[4 * k + 3] = fmaf(pr, v.w, acc[4 * k + 3]);
+                acc[0][4 * k] = fmaf(pa, v.x, acc[0][4 * k]);
+                acc[0][4 * k + 1] = fmaf(pa, v.y, acc[0][4 * k + 1]);
+                acc[0][4 * k + 2] = fmaf(pa, v.z, acc[0][4 * k + 2]);
+                acc[0][4 * k + 3] = fmaf(pa, v.w, acc[0][4 * k + 3]);
+                acc[1][4 * k] = fmaf(pb, v.x, acc[1][4 * k]);
+                acc[1][4 * k + 1] = fmaf(pb, v.y, acc[1][4 * k + 1]);
+                acc[1][4 * k + 2] = fmaf(pb, v.z, acc[1][4 * k + 2]);
+                acc[1][4 * k + 3] = fmaf(pb, v.w, acc[1][4 * k + 3]);
             }
         }
         __syncthreads();  // the tile buffer is refilled next iteration
     }
 
-    if (qi >= w.q_count) return;
-    const int qv = w.q_begin + qi;
-    const int row = rows[qv / kGroup];
-    const int head = kh * kGroup + qv % kGroup;
-    float* part = p.partial + (size_t(p.row_x0[row] + w.chunk) * kHeads + head) * (kHeadDim + 2);
-    // partial records are 66 floats: 8-byte aligned, so scalar stores
 #pragma unroll
-    for (int k = 0; k < 8; ++k)
+    for (int a = 0; a < 2; ++a) {
+        const int qi = qp + 32 * a;
+        if (qi >= w.q_count) continue;
+        const int qv = w.q_begin + qi;
+        const int row = rows[qv / kGroup];
+        const int head = kh * kGroup + qv % kGroup;
+        float* part = p.partial + (size_t(p.row_x0[row] + w.chunk) * kHeads + head) * (kHeadDim + 2);
+        // partial records are 66 floats: 8-byte aligned, so scalar stores
 #pragma unroll
-        for (int e = 0; e < 4; ++e) part[2 + sub * 4 + 8 * k + e] = acc[4 * k + e];
-    if (sub == 0) {
-        part[0] = m_run;
-        part[1] = l_run;
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) part[2 + sub * 4 + 16 * k + e] = acc[a][4 * k + e];
+        if (sub == 0) {
+            part[0] = m_run[a];
+            part[1] = l_run[a];
+        }
     }
 }
 

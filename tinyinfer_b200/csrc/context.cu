@@ -81,6 +81,7 @@ T* host_alloc(size_t count, const char* what) {
 struct AttnPlan {
     std::vector<int32_t> splits, work0, x0, nx;
     std::vector<mpb::AttnWork> work;
+    std::vector<int32_t> order;  // decode work items, longest first (persistent schedule)
     std::vector<mpb::PrefillWork> prefill;
     std::vector<mpb::PrefixWork> prefix;
     std::vector<int32_t> group_rows, group_row0, group_slot;
@@ -91,8 +92,8 @@ struct AttnPlan {
 
 constexpr int kGroupMinRows = 8;
 constexpr int kGroupMinTokens = 128;
-constexpr int kPrefixChunkTokens = 128;
 constexpr int kPrefixMaxChunks = 64;
+constexpr double kPrefixTargetCtas = 148.0 * 3;  // one wave at 3 CTAs per SM
 
 // tables: host mirror of the device block tables ([slots][table_stride]).
 void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, int table_stride,
@@ -141,11 +142,16 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
         }
         std::stable_sort(keyed.begin(), keyed.end(),
                          [](const auto& a, const auto& b) { return a.first < b.first; });
+        // candidates: (first, last) index into keyed, shared full pages
+        struct Candidate {
+            size_t b, e;
+            int pages;
+        };
+        std::vector<Candidate> candidates;
         for (size_t b = 0; b < keyed.size();) {
             size_t e = b;
             while (e < keyed.size() && keyed[e].first == keyed[b].first) ++e;
-            const int n = int(e - b);
-            if (n >= kGroupMinRows && keyed[b].first >= 0) {
+            if (int(e - b) >= kGroupMinRows && keyed[b].first >= 0) {
                 const DecodeRow& ref = decode[keyed[b].second];
                 const int32_t* rt = tables.data() + size_t(ref.slot) * table_stride;
                 int lcp = (ref.len - 1) / block_tokens;
@@ -159,38 +165,50 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
                             break;
                         }
                 }
-                const int shared = lcp * block_tokens;
-                int chunk_tokens = std::max(kPrefixChunkTokens, (shared + kPrefixMaxChunks - 1) / kPrefixMaxChunks);
-                chunk_tokens = (chunk_tokens + 31) / 32 * 32;
-                const int chunks = (shared + chunk_tokens - 1) / chunk_tokens;
-                const int qvecs = n * mpb::kGroup;
-                const int qblocks = (qvecs + mpb::kPrefixQueries - 1) / mpb::kPrefixQueries;
-                const size_t works = size_t(mpb::kKvHeads) * qblocks * chunks;
-                if (shared >= kGroupMinTokens && size_t(plan.extra_slots) + size_t(n) * chunks <= extra_capacity &&
-                    plan.prefix.size() + works <= prefix_capacity) {
-                    const int g = int(plan.group_slot.size());
-                    plan.group_slot.push_back(ref.slot);
-                    for (size_t k = b; k < e; ++k) {
-                        const DecodeRow& d = decode[keyed[k].second];
-                        plan.group_rows.push_back(d.row);
-                        shared_pages[d.row] = lcp;
-                        plan.nx[d.row] = chunks;
-                        plan.x0[d.row] = plan.extra_slots;  // made absolute below
-                        plan.extra_slots += chunks;
-                    }
-                    plan.group_row0.push_back(int(plan.group_rows.size()));
-                    for (int kh = 0; kh < mpb::kKvHeads; ++kh)
-                        for (int ch = 0; ch < chunks; ++ch)
-                            for (int qb = 0; qb < qblocks; ++qb) {
-                                const int q0 = qb * mpb::kPrefixQueries;
-                                plan.prefix.push_back({g, kh, q0, std::min(mpb::kPrefixQueries, qvecs - q0),
-                                                       ch * chunk_tokens, std::min(shared, (ch + 1) * chunk_tokens),
-                                                       ch, 0});
-                            }
-                    plan.bytes += double(shared) * kv_token_bytes;
-                }
+                if (lcp * block_tokens >= kGroupMinTokens) candidates.push_back({b, e, lcp});
             }
             b = e;
+        }
+        // One chunk length for the step: the groups' (tokens x query blocks x kv
+        // heads) spread over about kPrefixTargetCtas CTAs, in whole 32-token tiles.
+        double work = 0;
+        for (const auto& g : candidates) {
+            const int qblocks = (int(g.e - g.b) * mpb::kGroup + mpb::kPrefixQueries - 1) / mpb::kPrefixQueries;
+            work += double(g.pages) * block_tokens * qblocks * mpb::kKvHeads;
+        }
+        const int step_chunk = std::max(32, int(std::ceil(work / kPrefixTargetCtas / 32.0)) * 32);
+        for (const auto& g : candidates) {
+            const int n = int(g.e - g.b);
+            const DecodeRow& ref = decode[keyed[g.b].second];
+            const int shared = g.pages * block_tokens;
+            int chunk_tokens = std::max(step_chunk, (shared + kPrefixMaxChunks - 1) / kPrefixMaxChunks);
+            chunk_tokens = (chunk_tokens + 31) / 32 * 32;
+            const int chunks = (shared + chunk_tokens - 1) / chunk_tokens;
+            const int qvecs = n * mpb::kGroup;
+            const int qblocks = (qvecs + mpb::kPrefixQueries - 1) / mpb::kPrefixQueries;
+            const size_t works = size_t(mpb::kKvHeads) * qblocks * chunks;
+            if (size_t(plan.extra_slots) + size_t(n) * chunks > extra_capacity ||
+                plan.prefix.size() + works > prefix_capacity)
+                continue;
+            const int gi = int(plan.group_slot.size());
+            plan.group_slot.push_back(ref.slot);
+            for (size_t k = g.b; k < g.e; ++k) {
+                const DecodeRow& d = decode[keyed[k].second];
+                plan.group_rows.push_back(d.row);
+                shared_pages[d.row] = g.pages;
+                plan.nx[d.row] = chunks;
+                plan.x0[d.row] = plan.extra_slots;  // made absolute below
+                plan.extra_slots += chunks;
+            }
+            plan.group_row0.push_back(int(plan.group_rows.size()));
+            for (int kh = 0; kh < mpb::kKvHeads; ++kh)
+                for (int ch = 0; ch < chunks; ++ch)
+                    for (int qb = 0; qb < qblocks; ++qb) {
+                        const int q0 = qb * mpb::kPrefixQueries;
+                        plan.prefix.push_back({gi, kh, q0, std::min(mpb::kPrefixQueries, qvecs - q0),
+                                               ch * chunk_tokens, std::min(shared, (ch + 1) * chunk_tokens), ch, 0});
+                    }
+            plan.bytes += double(shared) * kv_token_bytes;
         }
     }
     long long decode_tokens = 0;
@@ -237,6 +255,22 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
     // shared-prefix slots follow the decode work items in the partial array
     for (int r = 0; r < rows; ++r)
         if (plan.nx[r]) plan.x0[r] += int(plan.work.size());
+    // longest slices first: the persistent decode CTAs then finish together
+    std::vector<int32_t> tokens(plan.work.size());
+    {
+        std::vector<int32_t> row_len(rows, 0);
+        int r = 0;
+        for (int i = 0; i < count; ++i)
+            for (int j = 0; j < seqs[i].count; ++j, ++r) row_len[r] = seqs[i].start + j + 1;
+        for (size_t w = 0; w < plan.work.size(); ++w) {
+            const auto& it = plan.work[w];
+            tokens[w] = std::min(it.page_end * block_tokens, row_len[it.row]) - it.page_begin * block_tokens;
+        }
+    }
+    plan.order.resize(plan.work.size());
+    for (size_t w = 0; w < plan.order.size(); ++w) plan.order[w] = int32_t(w);
+    std::stable_sort(plan.order.begin(), plan.order.end(),
+                     [&](int32_t a, int32_t b) { return tokens[a] > tokens[b]; });
 }
 
 }  // namespace
@@ -284,7 +318,7 @@ struct mp_context {
         CUtensorMap wqkv_hi, wqkv_lo, wo_hi, wo_lo, wgu_hi, wgu_lo, wdown_hi, wdown_lo, head_hi, head_lo;
     };
     Maps maps;
-    unsigned *counters = nullptr, *error = nullptr;
+    unsigned *counters = nullptr, *error = nullptr, *attn_sched = nullptr;
     int32_t *meta = nullptr, *out_tokens = nullptr, *out_finite = nullptr, *cow = nullptr, *patch = nullptr;
     size_t meta_capacity = 0, work_capacity = 0;
     // pinned host staging
@@ -309,7 +343,7 @@ struct mp_context {
     float cow_ms = 0.f;
     size_t off_tokens = 0, off_pos = 0, off_slot = 0, off_len = 0, off_splits = 0, off_work0 = 0, off_last = 0,
            off_work = 0, off_prefill = 0, off_x0 = 0, off_nx = 0, off_group_rows = 0, off_group_row0 = 0,
-           off_group_slot = 0, off_prefix = 0;
+           off_group_slot = 0, off_prefix = 0, off_order = 0;
     size_t prefill_capacity = 0;
     bool prepared = false;
     AttnPlan plan;
@@ -374,7 +408,7 @@ void free_context(mp_context* c) {
                     (void*)c->values, (void*)c->tables, (void*)c->rope_cos, (void*)c->rope_sin, (void*)c->x,
                     (void*)c->qkv, (void*)c->q, (void*)c->gemm_workspace, (void*)c->gemm_counters, (void*)c->logits,
                     (void*)c->partial,
-                    (void*)c->counters, (void*)c->error, (void*)c->meta, (void*)c->out_tokens, (void*)c->out_finite,
+                    (void*)c->counters, (void*)c->attn_sched, (void*)c->error, (void*)c->meta, (void*)c->out_tokens, (void*)c->out_finite,
                     (void*)c->cow, (void*)c->patch})
         if (p) cudaFree(p);
     for (auto* s : {&c->wqkv, &c->wo, &c->wgu, &c->wdown, &c->head, &c->xn, &c->attn, &c->h, &c->xl}) {
@@ -647,15 +681,18 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         c->prefix_capacity = 8192;
         c->partial = device_alloc<float>((c->work_capacity + c->extra_capacity) * mpb::kHeads * (mpb::kHeadDim + 2),
                                          "attention partials");
-        c->counters = device_alloc<unsigned>(T, "attention counters");
-        cuda_check(cudaMemsetAsync(c->counters, 0, T * sizeof(unsigned), c->stream), "zero counters");
+        // one arrival counter per (row, kv head)
+        c->counters = device_alloc<unsigned>(T * mpb::kKvHeads, "attention counters");
+        cuda_check(cudaMemsetAsync(c->counters, 0, T * mpb::kKvHeads * sizeof(unsigned), c->stream), "zero counters");
+        c->attn_sched = device_alloc<unsigned>(2, "attention schedule");
+        cuda_check(cudaMemsetAsync(c->attn_sched, 0, 2 * sizeof(unsigned), c->stream), "zero schedule");
         c->error = device_alloc<unsigned>(1, "error word");
         cuda_check(cudaMemsetAsync(c->error, 0, sizeof(unsigned), c->stream), "zero error word");
         c->prefill_capacity = (T / mpb::kPrefillTileRows + S) * mpb::kKvHeads;
         c->entry_capacity = S * size_t(r.table_stride);
         c->region_capacity = S;
         c->meta_capacity = 6 * T + S + 4 * c->work_capacity + 8 * c->prefill_capacity + 2 * c->entry_capacity +
-                           10 * c->region_capacity + 2 + 4 * T + 2 + 8 * c->prefix_capacity;
+                           10 * c->region_capacity + 2 + 4 * T + 2 + 8 * c->prefix_capacity + c->work_capacity;
         for (auto& e : c->cow_events) cuda_check(cudaEventCreate(&e), "create cow timing event");
         for (auto& e : c->fwd_events) cuda_check(cudaEventCreate(&e), "create forward timing event");
         c->meta = device_alloc<int32_t>(c->meta_capacity, "step metadata");
@@ -870,7 +907,8 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         c->off_group_row0 = c->off_group_rows + c->plan.group_rows.size();
         c->off_group_slot = c->off_group_row0 + G + 1;
         c->off_prefix = c->off_group_slot + G;
-        c->off_entries = c->off_prefix + 8 * X;
+        c->off_order = c->off_prefix + 8 * X;
+        c->off_entries = c->off_order + W;
         c->off_regions = (c->off_entries + 2 * size_t(entry_count) + 1) & ~size_t(1);  // 8-byte aligned
         std::memcpy(h + c->off_tokens, tokens, size_t(T) * 4);
         int row = 0;
@@ -892,6 +930,7 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         std::memcpy(h + c->off_group_row0, c->plan.group_row0.data(), (G + 1) * 4);
         std::memcpy(h + c->off_group_slot, c->plan.group_slot.data(), G * 4);
         std::memcpy(h + c->off_prefix, c->plan.prefix.data(), X * sizeof(mpb::PrefixWork));
+        std::memcpy(h + c->off_order, c->plan.order.data(), W * 4);
         for (int i = 0; i < entry_count; ++i) {
             h[c->off_entries + 2 * i] = entries[i].slot * c->rt.table_stride + entries[i].index;
             h[c->off_entries + 2 * i + 1] = entries[i].block;
@@ -993,6 +1032,8 @@ int mp_forward_launch(mp_context* c) {
         ap.row_work0 = meta + c->off_work0;
         ap.row_x0 = meta + c->off_x0;
         ap.row_nx = meta + c->off_nx;
+        ap.order = meta + c->off_order;
+        ap.sched = c->attn_sched;
         ap.work = reinterpret_cast<const mpb::AttnWork*>(meta + c->off_work);
         ap.work_count = c->work_count;
         ap.partial = c->partial;
@@ -1135,9 +1176,13 @@ int mp_forward_collect(mp_context* c, int32_t* out_tokens, int32_t* out_finite, 
         c->prepared = false;
         const unsigned err = *c->h_error;
         if (err & mpb::kErrTimeout) {
-            // a GEMM CTA that gave up never counted its K slice in
+            // a CTA that gave up never counted its K slice / attention slice in
             cuda_check(cudaMemsetAsync(c->gemm_counters, 0, mpb::kGemmCounters * sizeof(unsigned), c->stream),
                        "reset gemm counters");
+            cuda_check(cudaMemsetAsync(c->counters, 0, size_t(c->rt.max_step_tokens) * mpb::kKvHeads * sizeof(unsigned),
+                                       c->stream),
+                       "reset attention counters");
+            cuda_check(cudaMemsetAsync(c->attn_sched, 0, 2 * sizeof(unsigned), c->stream), "reset schedule");
             fail(MP_ERR_TIMEOUT, "an in-kernel copy wait expired");
         }
         if (err & mpb::kErrBounds) fail(MP_ERR_BOUNDS, "device bounds check failed (page id, token or region)");

@@ -48,8 +48,10 @@ struct AttnParams {
     const int32_t* row_nx;      // shared-prefix partial slots of each row (0: none)
     const AttnWork* work;
     int work_count;
+    const int32_t* order;  // optional processing order of the work items (longest first)
+    unsigned* sched;       // optional [2] zeroed counters: persistent CTAs pull work items
     float* partial;      // [slots][9][66] slice results: work items first, then shared-prefix slots
-    unsigned* counters;  // [rows] zero between launches
+    unsigned* counters;  // [rows][3 kv heads] zero between launches
     float* out;          // [rows][out_stride]; the TF32 hi half when out_lo is set
     float* out_lo;       // optional: lo halves (GEMM input), same layout
     int out_stride;
@@ -141,6 +143,7 @@ inline int auto_pages_per_split(long long total_tokens, int block_tokens) {
 cudaError_t configure_attention();
 // Message returned by mp_last_error() on this thread.
 void set_last_error(const char* message);
+constexpr int kAttnPersistentCtas = 148 * 3;  // one wave of the decode kernel
 cudaError_t launch_paged_attention(const AttnParams& p, cudaStream_t stream);
 
 // ---------------------------------------------------------------- GEMM

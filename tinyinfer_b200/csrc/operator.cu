@@ -87,7 +87,7 @@ extern "C" int mp_paged_attention_decode(const float* q, const float* keys, cons
     cudaError_t e = grow(s.meta, s.meta_capacity, words, stream, false);
     if (e == cudaSuccess) e = grow(s.partial, s.partial_capacity, work.size() * mpb::kHeads * (mpb::kHeadDim + 2),
                                    stream, false);
-    if (e == cudaSuccess) e = grow(s.counters, s.counter_capacity, size_t(count), stream, true);
+    if (e == cudaSuccess) e = grow(s.counters, s.counter_capacity, size_t(count) * mpb::kKvHeads, stream, true);
     if (e == cudaSuccess && !s.error) {
         e = cudaMalloc(reinterpret_cast<void**>(&s.error), sizeof(unsigned));
         if (e == cudaSuccess) e = cudaMemsetAsync(s.error, 0, sizeof(unsigned), stream);

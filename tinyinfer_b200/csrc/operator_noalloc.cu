@@ -7,7 +7,7 @@
 // path where cudaMalloc/cudaFree are not allowed because they synchronise the
 // device or fail mid-run. mp_paged_attention_decode grows its scratch with
 // cudaMalloc on demand; this variant never does. Its scratch -- the slice work
-// list and per-row metadata, the slice partial results, the per-row arrival
+// list and per-row metadata, the slice partial results, the per-(row, kv head) arrival
 // counters and an error word -- lives in one file-scope __device__ array of
 // fixed size (kScratchBytes below, about 5 MB), which every GPU that loads the
 // library holds until the process exits.
@@ -41,12 +41,13 @@ constexpr int kMaxRows = 512;
 constexpr int kMaxWork = 2048;
 constexpr int kMaxDevices = 64;
 constexpr size_t kPartialFloats = size_t(kMaxWork) * mpb::kHeads * (mpb::kHeadDim + 2);
-// Layout (bytes): partials | metadata (4 x kMaxRows row words + 4 x kMaxWork work words) | counters | error
+// Layout (bytes): partials | metadata (4 x kMaxRows row words + 4 x kMaxWork work words) |
+// counters (kMaxRows x 3 kv heads) | error
 constexpr size_t kPartialBytes = kPartialFloats * sizeof(float);
 constexpr size_t kMetaWords = 4 * size_t(kMaxRows) + 4 * size_t(kMaxWork);
 constexpr size_t kMetaOffset = kPartialBytes;
 constexpr size_t kCounterOffset = kMetaOffset + kMetaWords * sizeof(int32_t);
-constexpr size_t kErrorOffset = kCounterOffset + size_t(kMaxRows) * sizeof(unsigned);
+constexpr size_t kErrorOffset = kCounterOffset + size_t(kMaxRows) * mpb::kKvHeads * sizeof(unsigned);
 constexpr size_t kScratchBytes = (kErrorOffset + sizeof(unsigned) + 255) / 256 * 256;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
@@ -144,7 +145,7 @@ extern "C" int mp_paged_attention_decode_noalloc(const float* q, const float* ke
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     cudaError_t e = cudaMemcpyAsync(meta, g_host_meta, size_t(4 * count + 4 * work) * sizeof(int32_t),
                                     cudaMemcpyHostToDevice, stream);
-    if (e == cudaSuccess) e = cudaMemsetAsync(counters, 0, size_t(count) * sizeof(unsigned), stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(counters, 0, size_t(count) * mpb::kKvHeads * sizeof(unsigned), stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(error, 0, sizeof(unsigned), stream);
     if (e == cudaSuccess) e = mpb::configure_attention();
     if (e != cudaSuccess) {
