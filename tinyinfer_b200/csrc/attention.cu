@@ -30,6 +30,9 @@
 //  * Each consumer finishes a slice on its own: direct output for a single-slice
 //    row, else its partial (max, sum, unnormalised output) and the merge when it
 //    is the last arrival for (row, its kv head).
+//  * Arithmetic: packed FP32 FMAs (fma.rn.f32x2) for Q.K (even / odd dims) and
+//    P.V (dims lane / lane + 32); softmax weights as exp2 of scores scaled by
+//    log2(e) / 8, so maxima in partials are base-2 quantities.
 // Every wait is bounded (common.cuh); a timeout sets the error word and the warp
 // stops. Tokens past the row length are masked by select (never by multiplying).
 #include <algorithm>
@@ -216,29 +219,30 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
         }
         const float* kst = stages + 2 * buf * kStageFloats + kh * kHeadDim + c * 16;
         const float* vst = stages + (2 * buf + 1) * kStageFloats + kh * kHeadDim + lane;
-        // scores of tokens t and t + 8 for the 3 heads
+        const bool full_stage = d.n_valid == kStageTokens;
+        // scores of tokens t and t + 8 for the 3 heads, in base-2 units
+        // (dot / 8 * log2 e); even / odd dims in the two halves of a packed FMA
         float s[2][kGroup];
 #pragma unroll
         for (int ps = 0; ps < 2; ++ps) {
             const float* krow = kst + (t + 8 * ps) * kKvWidth;
-            float part[kGroup] = {0.f, 0.f, 0.f};
+            float pe[kGroup] = {0.f, 0.f, 0.f}, po[kGroup] = {0.f, 0.f, 0.f};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const float4 kv = *reinterpret_cast<const float4*>(krow + 4 * ((j + t) & 3));
 #pragma unroll
                 for (int hh = 0; hh < kGroup; ++hh) {
-                    part[hh] = fmaf(qr[hh][j].x, kv.x, part[hh]);
-                    part[hh] = fmaf(qr[hh][j].y, kv.y, part[hh]);
-                    part[hh] = fmaf(qr[hh][j].z, kv.z, part[hh]);
-                    part[hh] = fmaf(qr[hh][j].w, kv.w, part[hh]);
+                    fma2(pe[hh], po[hh], qr[hh][j].x, qr[hh][j].y, kv.x, kv.y);
+                    fma2(pe[hh], po[hh], qr[hh][j].z, qr[hh][j].w, kv.z, kv.w);
                 }
             }
-            const bool valid = t + 8 * ps < d.n_valid;
+            const bool valid = full_stage || t + 8 * ps < d.n_valid;
 #pragma unroll
             for (int hh = 0; hh < kGroup; ++hh) {
-                part[hh] += __shfl_xor_sync(0xffffffffu, part[hh], 1);
-                part[hh] += __shfl_xor_sync(0xffffffffu, part[hh], 2);
-                s[ps][hh] = valid ? part[hh] * 0.125f : -INFINITY;
+                float part = pe[hh] + po[hh];
+                part += __shfl_xor_sync(0xffffffffu, part, 1);
+                part += __shfl_xor_sync(0xffffffffu, part, 2);
+                s[ps][hh] = valid ? part * (0.125f * kLog2e) : -INFINITY;
             }
         }
         // online softmax over the stage's 16 tokens (lanes differ in t across bits 2..4)
@@ -250,8 +254,8 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
             const float m_new = fmaxf(m_run[hh], mx);
             const float ms = m_new == -INFINITY ? 0.f : m_new;  // no valid token yet: all terms stay 0
-            const float alpha = expf(m_run[hh] - ms);
-            const float p0 = expf(s[0][hh] - ms), p1 = expf(s[1][hh] - ms);
+            const float alpha = exp2f(m_run[hh] - ms);
+            const float p0 = exp2f(s[0][hh] - ms), p1 = exp2f(s[1][hh] - ms);
             float sum = p0 + p1;
             sum += __shfl_xor_sync(0xffffffffu, sum, 4);
             sum += __shfl_xor_sync(0xffffffffu, sum, 8);
@@ -266,7 +270,7 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
             }
         }
         __syncwarp();
-        // P.V: dims (lane, lane + 32) of this kv head
+        // P.V: dims (lane, lane + 32) of this kv head, one packed FMA per head and token
 #pragma unroll
         for (int q4 = 0; q4 < kStageTokens / 4; ++q4) {
             float4 pr[kGroup];
@@ -276,14 +280,12 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const int tt = 4 * q4 + u;
-                const bool valid = tt < d.n_valid;
-                const float v0 = valid ? vst[tt * kKvWidth] : 0.f;
-                const float v1 = valid ? vst[tt * kKvWidth + 32] : 0.f;
+                float v0 = vst[tt * kKvWidth], v1 = vst[tt * kKvWidth + 32];
+                if (!full_stage && tt >= d.n_valid) v0 = v1 = 0.f;
 #pragma unroll
                 for (int hh = 0; hh < kGroup; ++hh) {
                     const float pv = u == 0 ? pr[hh].x : (u == 1 ? pr[hh].y : (u == 2 ? pr[hh].z : pr[hh].w));
-                    acc[hh][0] = fmaf(pv, v0, acc[hh][0]);
-                    acc[hh][1] = fmaf(pv, v1, acc[hh][1]);
+                    fma2(acc[hh][0], acc[hh][1], pv, pv, v0, v1);
                 }
             }
         }
@@ -339,7 +341,7 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
             for (int k = 0; k < nx + splits; ++k) {
                 const int sl = k < nx ? x0 + k : w0 + (k - nx);
                 const float* part = p.partial + (size_t(sl) * kHeads + h) * (kHeadDim + 2);
-                const float sc = expf(__ldcg(part) - mx);
+                const float sc = exp2f(__ldcg(part) - mx);  // maxima are in base-2 units
                 den = fmaf(__ldcg(part + 1), sc, den);
                 n0 = fmaf(__ldcg(part + 2 + lane), sc, n0);
                 n1 = fmaf(__ldcg(part + 2 + lane + 32), sc, n1);

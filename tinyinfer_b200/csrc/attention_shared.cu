@@ -20,8 +20,10 @@
 //     2 query and 8 key float4 loads per 64 FMA;
 //   online softmax per query vector (4 lanes per vector, shuffles);
 //   O[64][64] = O * alpha + P V: thread (both queries, dims sub*4 + 16k) 32 outputs.
-// All FP32 FMA. Tokens past the chunk end are masked by select, never by
-// multiplying, so stale shared memory cannot reach the result.
+// All FP32 FMA; softmax weights are exp2 of scores scaled by log2(e) / 8, so the
+// partials' maxima are base-2 quantities like the decode kernel's. Tokens past
+// the chunk end are masked by select, never by multiplying, so stale shared
+// memory cannot reach the result.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -158,18 +160,18 @@ __global__ void __launch_bounds__(kPThreads, 3) prefix_attention_kernel(const Pr
             float mx = -INFINITY;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
-                s[a][k] = sub + 4 * k < n_valid ? s[a][k] * 0.125f : -INFINITY;
+                s[a][k] = sub + 4 * k < n_valid ? s[a][k] * (0.125f * kLog2e) : -INFINITY;
                 mx = fmaxf(mx, s[a][k]);
             }
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
             const float m_new = fmaxf(m_run[a], mx);
-            const float alpha = expf(m_run[a] - m_new);
+            const float alpha = exp2f(m_run[a] - m_new);
             float sum = 0.f;
             float* prow = Ps + (qp + 32 * a) * kPStride + sub;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
-                const float pr = expf(s[a][k] - m_new);
+                const float pr = exp2f(s[a][k] - m_new);
                 sum += pr;
                 prow[4 * k] = pr;
             }

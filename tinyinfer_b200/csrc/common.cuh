@@ -80,6 +80,23 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
         : "memory");
 }
 
+// Packed FP32: (a0, a1) = (b0 * c0 + a0, b1 * c1 + a1), each an IEEE fused
+// multiply-add (fma.rn.f32x2, sm_100).
+__device__ __forceinline__ void fma2(float& a0, float& a1, float b0, float b1, float c0, float c1) {
+    asm("{\n\t.reg .b64 pa, pb, pc;\n\t"
+        "mov.b64 pa, {%2, %3};\n\t"
+        "mov.b64 pb, {%4, %5};\n\t"
+        "mov.b64 pc, {%0, %1};\n\t"
+        "fma.rn.f32x2 pc, pa, pb, pc;\n\t"
+        "mov.b64 {%0, %1}, pc;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+// log2(e): softmax weights are evaluated as exp2 of scores pre-scaled by it
+// (exp(x) = 2^(x log2 e)); running maxima are kept in the same base-2 units.
+constexpr float kLog2e = 1.4426950408889634f;
+
 // TF32 hi/lo split: hi keeps sign, exponent and the 10 leading mantissa bits
 // (exact in TF32), lo = x - hi is exact in FP32.
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
