@@ -309,8 +309,6 @@ struct mp_context {
     float *rope_cos = nullptr, *rope_sin = nullptr;
     // workspace (GEMM inputs as hi/lo halves)
     float *x = nullptr, *qkv = nullptr, *q = nullptr, *logits = nullptr, *partial = nullptr;
-    float* gemm_workspace = nullptr;
-    unsigned* gemm_counters = nullptr;
     Split xn, attn, h, xl;
     // TMA tensor maps of every GEMM operand
     struct alignas(64) Maps {
@@ -360,6 +358,16 @@ namespace {
 
 size_t max_work(const mp_runtime_config& rt) { return size_t(rt.max_step_tokens) + 2048; }
 
+// Tile widths (B rows per CTA tile) of the wide projections: fewer re-reads of the
+// activations per output column block.
+constexpr int kGateUpBN = 128;  // 2 x intermediate is a multiple of 128 (intermediate % 64 == 0)
+int head_tile_n(int vocabulary) { return vocabulary % 256 == 0 ? 256 : (vocabulary % 128 == 0 ? 128 : 64); }
+int gemm_tile_n(int n) {
+    if (n >= 8192) return head_tile_n(n);
+    if (n % kGateUpBN == 0 && n >= 2048) return kGateUpBN;
+    return mpb::kTcBN;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     if (!fn) {
@@ -406,7 +414,7 @@ void free_context(mp_context* c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     for (void* p : {(void*)c->embed, (void*)c->final_norm, (void*)c->in_norm, (void*)c->post_norm, (void*)c->keys,
                     (void*)c->values, (void*)c->tables, (void*)c->rope_cos, (void*)c->rope_sin, (void*)c->x,
-                    (void*)c->qkv, (void*)c->q, (void*)c->gemm_workspace, (void*)c->gemm_counters, (void*)c->logits,
+                    (void*)c->qkv, (void*)c->q, (void*)c->logits,
                     (void*)c->partial,
                     (void*)c->counters, (void*)c->attn_sched, (void*)c->error, (void*)c->meta, (void*)c->out_tokens, (void*)c->out_finite,
                     (void*)c->cow, (void*)c->patch})
@@ -647,14 +655,11 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         c->qkv = device_alloc<float>(T * c->qkvw, "qkv activations");
         c->q = device_alloc<float>(T * H, "roped queries");
         split(c->attn, T * H, "attention output");
-        c->gemm_workspace = device_alloc<float>(mpb::kGemmWorkspaceFloats, "gemm split-K workspace");
-        c->gemm_counters = device_alloc<unsigned>(mpb::kGemmCounters, "gemm split-K counters");
-        cuda_check(cudaMemsetAsync(c->gemm_counters, 0, mpb::kGemmCounters * sizeof(unsigned), c->stream),
-                   "zero gemm counters");
         split(c->h, T * I, "mlp activations");
         split(c->xl, S * H, "last-row activations");
         c->logits = device_alloc<float>(S * V, "logits");
-        // TMA maps: activations in 128-row boxes (the A tile), weights in kTcBN-row boxes.
+        // TMA maps: activations in 128-row boxes (the A tile), weights in boxes of their
+        // GEMM's tile width (64; 128 gate/up; up to 256 LM head).
         auto& mp = c->maps;
         encode_map(&mp.xn_hi, c->xn.hi, T, H, 128);
         encode_map(&mp.xn_lo, c->xn.lo, T, H, 128);
@@ -669,12 +674,12 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         encode_map(&mp.wqkv_lo, c->wqkv.lo, L * c->qkvw, H, bn);
         encode_map(&mp.wo_hi, c->wo.hi, L * H, H, bn);
         encode_map(&mp.wo_lo, c->wo.lo, L * H, H, bn);
-        encode_map(&mp.wgu_hi, c->wgu.hi, L * 2 * I, H, bn);
-        encode_map(&mp.wgu_lo, c->wgu.lo, L * 2 * I, H, bn);
+        encode_map(&mp.wgu_hi, c->wgu.hi, L * 2 * I, H, kGateUpBN);
+        encode_map(&mp.wgu_lo, c->wgu.lo, L * 2 * I, H, kGateUpBN);
         encode_map(&mp.wdown_hi, c->wdown.hi, L * H, I, bn);
         encode_map(&mp.wdown_lo, c->wdown.lo, L * H, I, bn);
-        encode_map(&mp.head_hi, c->head.hi, V, H, bn);
-        encode_map(&mp.head_lo, c->head.lo, V, H, bn);
+        encode_map(&mp.head_hi, c->head.hi, V, H, uint32_t(head_tile_n(int(V))));
+        encode_map(&mp.head_lo, c->head.lo, V, H, uint32_t(head_tile_n(int(V))));
         c->work_capacity = max_work(r);
         // shared-prefix slots (rows x chunks) and prefix work items of one step
         c->extra_capacity = 8192;
@@ -998,21 +1003,18 @@ int mp_forward_launch(mp_context* c) {
         const auto& mp = c->maps;
         auto gemm = [&](const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
                         const CUtensorMap& b_lo, int rows, int n, int k, int b_row0, float* out, int ldc,
-                        mpb::Epilogue e, const char* what) {
+                        mpb::Epilogue e, const char* what, int bn = mpb::kTcBN) {
             mpb::TcGemmParams g{};
             g.m = rows;
             g.n = n;
             g.k = k;
+            g.bn = bn;
             g.b_row0 = b_row0;
             g.c = out;
             g.ldc = ldc;
             g.out_hi = c->h.hi;
             g.out_lo = c->h.lo;
             g.ld_out = I;
-            g.workspace = c->gemm_workspace;
-            g.workspace_floats = mpb::kGemmWorkspaceFloats;
-            g.counters = c->gemm_counters;
-            g.counter_count = mpb::kGemmCounters;
             g.error = c->error;
             cuda_check(mpb::launch_tc_gemm({&a_hi, &a_lo, &b_hi, &b_lo}, g, e, st), what);
         };
@@ -1118,7 +1120,7 @@ int mp_forward_launch(mp_context* c) {
                                            H, st),
                        "rmsnorm launch");
             gemm(mp.xn_hi, mp.xn_lo, mp.wgu_hi, mp.wgu_lo, T, 2 * I, H, l * 2 * I, nullptr, I, mpb::Epilogue::SwiGLU,
-                 "gate/up gemm");
+                 "gate/up gemm", kGateUpBN);
             gemm(mp.h_hi, mp.h_lo, mp.wdown_hi, mp.wdown_lo, T, H, I, l * H, c->x, H, mpb::Epilogue::AddTo,
                  "down gemm");
         }
@@ -1126,7 +1128,7 @@ int mp_forward_launch(mp_context* c) {
                                        H, st),
                    "final norm launch");
         gemm(mp.xl_hi, mp.xl_lo, mp.head_hi, mp.head_lo, S, m.vocabulary, H, 0, c->logits, m.vocabulary,
-             mpb::Epilogue::Store, "lm head gemm");
+             mpb::Epilogue::Store, "lm head gemm", head_tile_n(m.vocabulary));
         cuda_check(mpb::launch_argmax(c->logits, S, m.vocabulary, c->out_tokens, c->out_finite, st), "argmax launch");
         cuda_check(cudaEventRecord(c->fwd_events[1], st), "forward timing");
         if (c->profile) c->prof_bytes += c->plan.bytes * m.layers;
@@ -1176,9 +1178,7 @@ int mp_forward_collect(mp_context* c, int32_t* out_tokens, int32_t* out_finite, 
         c->prepared = false;
         const unsigned err = *c->h_error;
         if (err & mpb::kErrTimeout) {
-            // a CTA that gave up never counted its K slice / attention slice in
-            cuda_check(cudaMemsetAsync(c->gemm_counters, 0, mpb::kGemmCounters * sizeof(unsigned), c->stream),
-                       "reset gemm counters");
+            // an attention CTA that gave up never counted its slice in
             cuda_check(cudaMemsetAsync(c->counters, 0, size_t(c->rt.max_step_tokens) * mpb::kKvHeads * sizeof(unsigned),
                                        c->stream),
                        "reset attention counters");
@@ -1336,24 +1336,20 @@ int mp_gemm_f32(const float* a, const float* b, float* out, int32_t m, int32_t n
         auto maps = std::make_unique<M4>();
         encode_map(&maps->ah, ah, rows_a, k, 128);
         encode_map(&maps->al, al, rows_a, k, 128);
-        encode_map(&maps->bh, bh, rows_b, k, mpb::kTcBN);
-        encode_map(&maps->bl, bl, rows_b, k, mpb::kTcBN);
+        // the forward's tile width for this N: 256 for the LM head, 128 for gate/up, else 64
+        const int bn = gemm_tile_n(n);
+        encode_map(&maps->bh, bh, rows_b, k, uint32_t(bn));
+        encode_map(&maps->bl, bl, rows_b, k, uint32_t(bn));
         unsigned* err = device_alloc<unsigned>(1, "gemm error word");
         scratch.push_back(reinterpret_cast<float*>(err));
         cuda_check(cudaMemsetAsync(err, 0, 4, st), "clear error word");
-        // split-K workspace, as in the forward: small-M shapes run with K slices
-        float* ws = alloc(mpb::kGemmWorkspaceFloats);
-        unsigned* counters = reinterpret_cast<unsigned*>(alloc(mpb::kGemmCounters));
         mpb::TcGemmParams g{};
         g.m = m;
         g.n = n;
         g.k = k;
+        g.bn = bn;
         g.c = out;
         g.ldc = n;
-        g.workspace = ws;
-        g.workspace_floats = mpb::kGemmWorkspaceFloats;
-        g.counters = counters;
-        g.counter_count = mpb::kGemmCounters;
         g.error = err;
         cuda_check(mpb::launch_tc_gemm({&maps->ah, &maps->al, &maps->bh, &maps->bl}, g, mpb::Epilogue::Store, st),
                    "gemm launch");

@@ -156,12 +156,13 @@ enum class Epilogue : int {
 
 // Tensor-core 3xTF32 GEMM (tc_gemm.cu). A and B come as TF32 hi/lo halves through
 // 2-D TMA tensor maps (fp32, rows x K, 128-byte swizzle, boxes of 32 x 128 rows
-// for A and 32 x kTcBN rows for B); B's rows start at b_row0 (stacked per-layer
-// weights). Epilogues: Store / AddTo into c; SwiGLU expects B's rows in 32-row
-// gate/up blocks (rows 64b..64b+31 gate, 64b+32..64b+63 up) and writes
-// silu(gate) * up for output columns 32b..32b+31 as hi/lo halves (out_hi, out_lo).
-// With a workspace and counters, K is split over gridDim.z CTAs whose partial
-// tiles the last-arriving CTA sums in slice order (deterministic).
+// for A and 32 x bn rows for B, bn = 64, 128 or 256); B's rows start at b_row0
+// (stacked per-layer weights). Epilogues: Store / AddTo into c; SwiGLU expects B's
+// rows in 32-row gate/up blocks (rows 64b..64b+31 gate, 64b+32..64b+63 up) and
+// writes silu(gate) * up for output columns 32b..32b+31 as hi/lo halves (out_hi,
+// out_lo). Small-M problems split K over a thread-block cluster of up to 8 CTAs
+// per output tile, reduced in slice order through distributed shared memory
+// (deterministic).
 constexpr int kTcBN = 64;
 struct TcGemmMaps {
     const struct CUtensorMap_st* a_hi;
@@ -171,16 +172,13 @@ struct TcGemmMaps {
 };
 struct TcGemmParams {
     int m, n, k;
+    int bn;  // B tile rows (the B maps' box): 64, 128 or 256 (0: 64)
     int b_row0;
     float* c;
     int ldc;
     float* out_hi;
     float* out_lo;
     int ld_out;
-    float* workspace;
-    size_t workspace_floats;
-    unsigned* counters;
-    int counter_count;
     unsigned* error;
 };
 cudaError_t configure_tc_gemm();
@@ -189,10 +187,6 @@ cudaError_t launch_tc_gemm(const TcGemmMaps& maps, const TcGemmParams& p, Epilog
 cudaError_t launch_split(const float* x, float* hi, float* lo, size_t n, cudaStream_t stream);
 
 // ---------------------------------------------------------------- fused small ops
-// Split-K workspace of the tensor-core GEMM: one wave of 148 CTAs x 2 x a 128 x kTcBN tile.
-constexpr size_t kGemmWorkspaceFloats = size_t(148) * 2 * 128 * kTcBN;
-constexpr int kGemmCounters = 148 * 2;
-
 // x[r][:] = embed[tokens[r]][:]; rmsnorm(x[r]) * w written as TF32 hi/lo halves.
 cudaError_t launch_embed_rmsnorm(const int32_t* tokens, const float* embed, int vocabulary, const float* norm_w,
                                  float eps, float* x, float* normed_hi, float* normed_lo, int rows, int hidden,

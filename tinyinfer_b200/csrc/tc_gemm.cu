@@ -20,13 +20,17 @@
 //    (kind::tf32, M=128, N=BN, K=8) into one TMEM accumulator; tcgen05.commit
 //    releases the stage to the producer, and after the last block signals the
 //    accumulator barrier;
-//  * all 4 warps: epilogue. Each warp reads its 32 TMEM lanes (= tile rows) with
-//    tcgen05.ld.32x32b and applies the fused epilogue -- directly when the tile
-//    has one K slice, else after the last slice to finish has summed every
-//    slice's partial tile in slice order (deterministic split-K for the small-M
-//    decode GEMMs, which otherwise leave most SMs idle).
-// Every mbarrier wait is bounded; a timeout sets the error word and the CTA still
-// releases its tensor memory before returning.
+//  * all 4 warps: each thread moves its TMEM lane (= tile row) with
+//    tcgen05.ld.32x32b into a row of a shared-memory tile (the stage ring is idle
+//    by then). The K slices of one output tile form a thread-block cluster
+//    (cluster dims 1 x 1 x slices): after a cluster barrier every CTA sums its
+//    share of the rows over all slices' tiles in slice order, reading the peers'
+//    shared memory directly (deterministic split-K for the small-M decode GEMMs,
+//    with no global round trip), and applies the fused epilogue with coalesced
+//    row-contiguous stores. A second cluster barrier keeps each tile alive until
+//    the peers have read it.
+// Every mbarrier wait is bounded; a timeout sets the error word, and the CTA still
+// passes both cluster barriers and releases its tensor memory.
 #include <cuda.h>
 
 #include <algorithm>
@@ -47,9 +51,13 @@ struct TcConfig {
     static constexpr int kATile = kBM * kBK * 4;  // bytes
     static constexpr int kBTile = BN * kBK * 4;
     static constexpr int kStage = 2 * kATile + 2 * kBTile;
-    static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int kTileStride = BN + 4;  // floats per staged accumulator row (bank spread)
+    static constexpr int kTileBytes = kBM * kTileStride * 4;
+    static constexpr int kRing = kStages * kStage > kTileBytes ? kStages * kStage : kTileBytes;
+    static constexpr int kSmem = kRing + 1024 /*align*/ + 256 /*barriers*/;
     static constexpr int kTmemCols = BN < 32 ? 32 : BN;
 };
+constexpr int kMaxSlices = 8;  // portable cluster size
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -107,40 +115,114 @@ __device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// The fused epilogue for one output row of the tile: v[0..BN) are columns n0.. .
-//  Store  : c[row][n0 + j] = v[j]
-//  AddTo  : c[row][n0 + j] += v[j]                     (residual add)
-//  SwiGLU : the tile holds gate columns (v[0..BN/2)) and the matching up columns
-//           (v[BN/2..BN)) of output columns n0/2 .. n0/2 + BN/2; writes
-//           h = silu(gate) * up as TF32 hi/lo halves (the down projection's input).
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// float4 at the same shared-memory offset in cluster CTA `rank` (its own included).
+__device__ __forceinline__ float4 ld_cluster(const float* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(remote)
+                 : "memory");
+    return v;
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    // g / (1 + exp(-g)) * u with an IEEE-rounded reciprocal
+    return __fmul_rn(__fmul_rn(g, __frcp_rn(__fadd_rn(1.0f, expf(-g)))), u);
+}
+
+// Fused epilogue over rows [r0, r1) of the tile, columns in parallel (coalesced).
+// Each output float4 is the sum over the cluster's slices, in slice order, of the
+// staged tiles at the same offset; a thread takes kUnroll outputs per round and
+// issues all their loads of one slice before adding, so loads overlap.
+//  Store  : c[row][n0 + j] = acc
+//  AddTo  : c[row][n0 + j] += acc                        (residual add)
+//  SwiGLU : per 64-column group g of the tile, columns 0..31 are gate and 32..63 up
+//           of output columns (n0 + 64 g) / 2 + 0..31; writes h = silu(gate) * up as
+//           TF32 hi/lo halves (the down projection's input).
+constexpr int kUnroll = 4;
+
 template <int BN, Epilogue E>
-__device__ __forceinline__ void epilogue(const TcGemmParams& p, int row, int n0, const float* v) {
-    if (E == Epilogue::Store) {
-        float4* dst = reinterpret_cast<float4*>(p.c + size_t(row) * p.ldc + n0);
+__device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float* tile, int m0, int n0, int r0,
+                                              int r1, int slices) {
+    using Cfg = TcConfig<BN>;
+    constexpr bool kSwiGLU = E == Epilogue::SwiGLU;
+    // items per row: float4 of the tile (Store/AddTo) or of the gate halves (SwiGLU)
+    constexpr int kItems = kSwiGLU ? (BN / 64) * 8 : BN / 4;
+    constexpr int kLoads = kSwiGLU ? 2 : 1;  // gate and up
+    const int total = (r1 - r0) * kItems;
+    for (int base = threadIdx.x; base < total; base += kThreads * kUnroll) {
+        int off[kUnroll];
+        bool live[kUnroll];
 #pragma unroll
-        for (int i = 0; i < BN / 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-    } else if (E == Epilogue::AddTo) {
-        float4* dst = reinterpret_cast<float4*>(p.c + size_t(row) * p.ldc + n0);
-#pragma unroll
-        for (int i = 0; i < BN / 4; ++i) {
-            const float4 x = dst[i];
-            dst[i] = make_float4(__fadd_rn(x.x, v[4 * i]), __fadd_rn(x.y, v[4 * i + 1]), __fadd_rn(x.z, v[4 * i + 2]),
-                                 __fadd_rn(x.w, v[4 * i + 3]));
+        for (int u = 0; u < kUnroll; ++u) {
+            const int i = base + u * kThreads;
+            live[u] = i < total;
+            const int row = r0 + (live[u] ? i / kItems : 0), it = i % kItems;
+            off[u] = row * Cfg::kTileStride + (kSwiGLU ? 64 * (it / 8) + 4 * (it % 8) : 4 * it);
         }
-    } else {
-        constexpr int H = BN / 2;
-        const size_t at = size_t(row) * p.ld_out + n0 / 2;
+        float4 acc[kUnroll][kLoads];
+        for (int k = 0; k < slices; ++k) {
+            float4 v[kUnroll][kLoads];
 #pragma unroll
-        for (int i = 0; i < H / 4; ++i) {
-            float hv[4], lv[4];
+            for (int u = 0; u < kUnroll; ++u)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float g = v[4 * i + e], u = v[H + 4 * i + e];
-                const float o = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-                split_tf32(o, hv[e], lv[e]);
+                for (int h = 0; h < kLoads; ++h) {
+                    const float* at = tile + off[u] + 32 * h;
+                    v[u][h] = slices == 1 ? *reinterpret_cast<const float4*>(at) : ld_cluster(at, uint32_t(k));
+                }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+                for (int h = 0; h < kLoads; ++h) {
+                    if (k == 0) {
+                        acc[u][h] = v[u][h];
+                    } else {
+                        acc[u][h].x += v[u][h].x;
+                        acc[u][h].y += v[u][h].y;
+                        acc[u][h].z += v[u][h].z;
+                        acc[u][h].w += v[u][h].w;
+                    }
+                }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            if (!live[u]) continue;
+            const int i = base + u * kThreads;
+            const int row = r0 + i / kItems, it = i % kItems;
+            if (m0 + row >= p.m) continue;
+            if (kSwiGLU) {
+                const float4 gt = acc[u][0], up = acc[u][kLoads - 1];
+                const float o[4] = {silu_mul(gt.x, up.x), silu_mul(gt.y, up.y), silu_mul(gt.z, up.z),
+                                    silu_mul(gt.w, up.w)};
+                float hv[4], lv[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) split_tf32(o[e], hv[e], lv[e]);
+                const size_t dst = size_t(m0 + row) * p.ld_out + (n0 + 64 * (it / 8)) / 2 + 4 * (it % 8);
+                *reinterpret_cast<float4*>(p.out_hi + dst) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+                *reinterpret_cast<float4*>(p.out_lo + dst) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+            } else {
+                const float4 v = acc[u][0];
+                float4* dst = reinterpret_cast<float4*>(p.c + size_t(m0 + row) * p.ldc + n0 + 4 * it);
+                if (E == Epilogue::Store) {
+                    *dst = v;
+                } else {
+                    const float4 x = *dst;
+                    *dst = make_float4(__fadd_rn(x.x, v.x), __fadd_rn(x.y, v.y), __fadd_rn(x.z, v.z),
+                                       __fadd_rn(x.w, v.w));
+                }
             }
-            reinterpret_cast<float4*>(p.out_hi + at)[i] = make_float4(hv[0], hv[1], hv[2], hv[3]);
-            reinterpret_cast<float4*>(p.out_lo + at)[i] = make_float4(lv[0], lv[1], lv[2], lv[3]);
         }
     }
 }
@@ -231,65 +313,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) mma_commit(accum);
     }
     __syncwarp();
-    // Epilogue: all 4 warps; warp w owns TMEM lanes / tile rows 32w .. 32w+31.
-    // The outcome is made CTA-uniform before any branch that holds a barrier.
+    // Epilogue. The outcome is made CTA-uniform before anything that holds a barrier.
     if (!mbar_wait_bounded(accum, 0)) *failed = 1;
     __syncthreads();
     const bool ok = *failed == 0;
-    __syncthreads();
-    const int row_in_tile = warp * 32 + lane;
-    const int row = m0 + row_in_tile;
-    if (!ok) {
-        if (threadIdx.x == 0) raise_error(p.error, kErrTimeout);
-    } else if (splits == 1) {
+    // Stage this slice's accumulator in shared memory: thread = tile row.
+    float* tile = reinterpret_cast<float*>(smem);
+    if (ok) {
         tmem_fence_after();
-        uint32_t r[BN];
-#pragma unroll
-        for (int c0 = 0; c0 < BN; c0 += 32)
-            tmem_load32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c0), *reinterpret_cast<uint32_t(*)[32]>(&r[c0]));
-        if (row < p.m) epilogue<BN, E>(p, row, n0, reinterpret_cast<const float*>(r));
-    } else {
-        // Deterministic split-K: park this slice's partial tile, and let the last
-        // slice to arrive sum all partials in slice order before the epilogue.
-        tmem_fence_after();
-        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-        float* part = p.workspace + (size_t(tile) * splits + blockIdx.z) * (kBM * BN) + size_t(row_in_tile) * BN;
+        const int row = warp * 32 + lane;
 #pragma unroll
         for (int c0 = 0; c0 < BN; c0 += 32) {
             uint32_t r[32];
             tmem_load32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c0), r);
+            float4* dst = reinterpret_cast<float4*>(tile + row * Cfg::kTileStride + c0);
 #pragma unroll
             for (int v = 0; v < 8; ++v)
-                __stcg(reinterpret_cast<float4*>(part + c0) + v,
-                       make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                   __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3])));
+                dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                     __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
         }
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) *failed = atomicAdd(&p.counters[tile], 1u) == unsigned(splits - 1) ? 2 : 0;
-        __syncthreads();
-        if (*failed == 2) {
-            __threadfence();
-            float acc[BN];
-#pragma unroll
-            for (int j = 0; j < BN; ++j) acc[j] = 0.f;
-            for (int s = 0; s < splits; ++s) {
-                const float4* src = reinterpret_cast<const float4*>(
-                    p.workspace + (size_t(tile) * splits + s) * (kBM * BN) + size_t(row_in_tile) * BN);
-#pragma unroll
-                for (int v = 0; v < BN / 4; ++v) {
-                    const float4 x = __ldcg(src + v);
-                    acc[4 * v] += x.x;
-                    acc[4 * v + 1] += x.y;
-                    acc[4 * v + 2] += x.z;
-                    acc[4 * v + 3] += x.w;
-                }
-            }
-            if (row < p.m) epilogue<BN, E>(p, row, n0, acc);
-            if (threadIdx.x == 0) p.counters[tile] = 0u;  // ready for the next launch
-        }
+    } else if (threadIdx.x == 0) {
+        raise_error(p.error, kErrTimeout);
     }
     tmem_fence_before();
+    if (splits > 1)
+        cluster_sync();  // every slice's tile is staged
+    else
+        __syncthreads();
+    if (ok) {
+        const int rank = splits > 1 ? int(cluster_rank()) : 0;
+        const int r0 = rank * kBM / splits, r1 = (rank + 1) * kBM / splits;
+        epilogue_rows<BN, E>(p, tile, m0, n0, r0, r1, splits);
+    }
+    if (splits > 1) cluster_sync();  // the peers have read this CTA's tile
     __syncthreads();
     if (warp == 0) {
         tmem_fence_after();
@@ -298,25 +354,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// Clusters of each size (index = slices) that the device holds at once, per tile
+// width (a cluster lives inside one GPC, so this is below 148 / slices).
+int g_active_clusters[3][kMaxSlices + 1];
+
+constexpr int bn_index(int bn) { return bn == 64 ? 0 : (bn == 128 ? 1 : 2); }
+
 template <int BN, Epilogue E>
 cudaError_t launch_bn(const TcGemmMaps& maps, const TcGemmParams& p, cudaStream_t stream) {
     using Cfg = TcConfig<BN>;
     static_assert(Cfg::kSmem <= 232448, "stage buffers exceed shared memory");
     const int tiles = (p.n / BN) * ((p.m + kBM - 1) / kBM);
     const int kb = p.k / kBK;
-    // K slices: fill about one wave of the 148 SMs, at least 2 K blocks per slice,
-    // within the workspace the caller provides.
-    int splits = 1;
-    if (p.workspace && p.counters) {
-        splits = std::max(1, std::min(148 / std::max(tiles, 1), kb / 2));
-        while (splits > 1 && size_t(tiles) * splits * kBM * BN > p.workspace_floats) --splits;
-        if (tiles > p.counter_count) splits = 1;
-        // equalise: no empty trailing slice
-        while (splits > 1 && (splits - 1) * ((kb + splits - 1) / splits) >= kb) --splits;
-    }
-    const dim3 grid(p.n / BN, (p.m + kBM - 1) / kBM, splits);
-    tc_gemm_kernel<BN, E><<<grid, kThreads, Cfg::kSmem, stream>>>(*maps.a_hi, *maps.a_lo, *maps.b_hi, *maps.b_lo, p);
-    return cudaGetLastError();
+    // K slices: as many as keep every tile's cluster resident in one wave, at
+    // least 2 K blocks per slice, at most one portable cluster, no empty slice
+    int splits = std::max(1, std::min(kMaxSlices, kb / 2));
+    while (splits > 1 && tiles > g_active_clusters[bn_index(BN)][splits]) --splits;
+    while (splits > 1 && (splits - 1) * ((kb + splits - 1) / splits) >= kb) --splits;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(p.n / BN, (p.m + kBM - 1) / kBM, splits);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = unsigned(splits);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, E>, *maps.a_hi, *maps.a_lo, *maps.b_hi, *maps.b_lo, p);
 }
 
 template <int BN>
@@ -327,6 +394,23 @@ cudaError_t configure_bn() {
         e = cudaFuncSetAttribute(tc_gemm_kernel<BN, Epilogue::AddTo>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(tc_gemm_kernel<BN, Epilogue::SwiGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    // resident clusters of 1..8 CTAs (same resources for every epilogue)
+    for (int s = 1; s <= kMaxSlices && e == cudaSuccess; ++s) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(1, 1, s);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = Cfg::kSmem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = unsigned(s);
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        e = cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<BN, Epilogue::Store>, &cfg);
+        g_active_clusters[bn_index(BN)][s] = n;
+    }
     return e;
 }
 
@@ -338,15 +422,31 @@ __global__ void split_kernel(const float* x, float* hi, float* lo, size_t n) {
 
 }  // namespace
 
-cudaError_t configure_tc_gemm() { return configure_bn<kTcBN>(); }
+cudaError_t configure_tc_gemm() {
+    cudaError_t e = configure_bn<64>();
+    if (e == cudaSuccess) e = configure_bn<128>();
+    if (e == cudaSuccess) e = configure_bn<256>();
+    return e;
+}
+
+template <int BN>
+cudaError_t launch_e(const TcGemmMaps& maps, const TcGemmParams& p, Epilogue e, cudaStream_t stream) {
+    if (p.n % BN) return cudaErrorInvalidValue;
+    switch (e) {
+        case Epilogue::Store: return launch_bn<BN, Epilogue::Store>(maps, p, stream);
+        case Epilogue::AddTo: return launch_bn<BN, Epilogue::AddTo>(maps, p, stream);
+        case Epilogue::SwiGLU: return launch_bn<BN, Epilogue::SwiGLU>(maps, p, stream);
+    }
+    return cudaErrorInvalidValue;
+}
 
 cudaError_t launch_tc_gemm(const TcGemmMaps& maps, const TcGemmParams& p, Epilogue e, cudaStream_t stream) {
     if (p.m <= 0) return cudaSuccess;
-    if (p.n % kTcBN || p.k % kBK) return cudaErrorInvalidValue;
-    switch (e) {
-        case Epilogue::Store: return launch_bn<kTcBN, Epilogue::Store>(maps, p, stream);
-        case Epilogue::AddTo: return launch_bn<kTcBN, Epilogue::AddTo>(maps, p, stream);
-        case Epilogue::SwiGLU: return launch_bn<kTcBN, Epilogue::SwiGLU>(maps, p, stream);
+    if (p.k % kBK) return cudaErrorInvalidValue;
+    switch (p.bn == 0 ? 64 : p.bn) {
+        case 64: return launch_e<64>(maps, p, e, stream);
+        case 128: return launch_e<128>(maps, p, e, stream);
+        case 256: return launch_e<256>(maps, p, e, stream);
     }
     return cudaErrorInvalidValue;
 }
