@@ -1,231 +1,310 @@
-// Shared-prefix decode attention (sm_100a): the pages that a group of decode rows
-// share are read once per launch for the whole group.
+// Shared-prefix decode attention on the tensor cores (sm_100a): the pages that a
+// group of decode rows share are read once per launch for the whole group.
 //
 // Decode attention is bandwidth-bound when every row streams its whole context
 // (miniprefix/src/backend/cuda/llama_runner.cu:33-48 reads it once per row and
 // head). Rows that reuse a cached prefix (miniprefix/src/kv/prefix_cache.cpp) map
 // the same physical pages at the start of their block tables, so the host groups
 // such rows and this kernel computes their attention over the shared tokens as a
-// small dense problem per (group, kv head): Q[rows x 3 heads][64] against
-// K/V[shared tokens][64], i.e. the same causal-free softmax(QK^T / 8) V the CPU
-// runner computes (miniprefix/src/backend/cpu/llama_runner.cpp:85-93) restricted
-// to those tokens. Each CTA produces, per query vector, the running maximum, the
-// sum of exponentials and the unnormalised output of its token chunk -- the same
-// partial format as the split-K decode kernel -- and the decode kernel's last
-// slice merges them with the rows' own pages (attention.cu).
+// dense problem per (group, kv head): Q[rows x 3 heads][64] against
+// K/V[shared tokens][64] -- softmax(Q K^T / 8) V as the CPU runner computes it
+// (miniprefix/src/backend/cpu/llama_runner.cpp:85-93), restricted to those tokens.
+// Each CTA writes, per query vector, the maximum, the sum of exponentials and the
+// unnormalised output of its token chunk -- the decode kernel's partial format
+// (base-2 units) -- and the decode kernel's merge combines them with the rows'
+// own pages (attention.cu).
 //
-// CTA = (group, kv head, 64 query vectors, token chunk), 128 threads. Per 32-token
-// tile (double-buffered 16-byte cp.async gathers through the group's table):
-//   S[64][32] = Q K^T / 8: thread (queries qp and qp + 32, tokens sub + 4k) 16 scores,
-//     2 query and 8 key float4 loads per 64 FMA;
-//   online softmax per query vector (4 lanes per vector, shuffles);
-//   O[64][64] = O * alpha + P V: thread (both queries, dims sub*4 + 16k) 32 outputs.
-// All FP32 FMA; softmax weights are exp2 of scores scaled by log2(e) / 8, so the
-// partials' maxima are base-2 quantities like the decode kernel's. Tokens past
-// the chunk end are masked by select, never by multiplying, so stale shared
-// memory cannot reach the result.
+// CTA = (group, kv head, 128 query vectors, token chunk), 4 warps. Per 64-token
+// sub-chunk:
+//  * all threads gather K and V rows through the group's block table, split them
+//    into TF32 hi / lo halves and write K (64 tokens x 64 dims) and V^T (64 dims x
+//    64 tokens) as K-major 128-byte-swizzled UMMA tiles (the query block is
+//    written the same way);
+//  * one thread issues S = Q K^T as 3xTF32 tcgen05.mma (M=128, N=64: Q_lo K_hi +
+//    Q_hi K_lo + Q_hi K_hi per 8-dim step) into tensor memory;
+//  * thread = query row: tcgen05.ld of its 64 scores, exact softmax over the
+//    sub-chunk in registers (no shuffles), probabilities written as hi/lo A tiles;
+//  * one thread issues O = P V the same way (K = the 64 tokens);
+//  * thread = query row: tcgen05.ld of its 64 outputs, folded into a running
+//    (max, sum, output) in registers -- online softmax across sub-chunks.
+// All MMA waits are bounded mbarrier waits; a timeout sets the error word.
 #include "common.cuh"
 #include "kernels.h"
+#include "umma.cuh"
 
 namespace mpb {
 namespace {
 
-constexpr int kPQ = kPrefixQueries;  // 64 query vectors per CTA
-constexpr int kPT = 32;              // tokens per tile
+constexpr int kPQ = kPrefixQueries;  // 128 query vectors = UMMA M
+constexpr int kPT = 64;              // tokens per sub-chunk = UMMA N of S, K of P.V
 constexpr int kPThreads = 128;
-constexpr int kRowStride = kHeadDim + 4;  // 68 floats: 16-byte aligned rows
-constexpr int kPStride = kPT + 1;         // 33
-constexpr size_t kPrefixSmem =
-    (size_t(kPQ) * kRowStride + 2 * 2 * kPT * kRowStride + size_t(kPQ) * kPStride) * sizeof(float);
+constexpr int kQTile = kPQ * 32 * 4;   // one 32-element K block of a 128-row tile (16 KB)
+constexpr int kKTile = kPT * 32 * 4;   // one K block of a 64-row tile (8 KB)
+// shared memory (1024-aligned tiles): Q/P hi, Q/P lo (2 K blocks each), K hi, K lo,
+// V^T hi, V^T lo (2 K blocks each), then the barrier and the TMEM address
+constexpr int kOffQhi = 0, kOffQlo = 2 * kQTile;
+constexpr int kOffKhi = 4 * kQTile, kOffKlo = kOffKhi + 2 * kKTile;
+constexpr int kOffVhi = kOffKlo + 2 * kKTile, kOffVlo = kOffVhi + 2 * kKTile;
+constexpr int kOffBlk = kOffVlo + 2 * kKTile;  // [64] physical blocks of the sub-chunk's tokens
+constexpr int kOffBar = kOffBlk + kPT * 4;
+constexpr size_t kPrefixSmem = size_t(kOffBar) + 64 + 1024 /*alignment slack*/;
+constexpr uint32_t kTmemCols = 128;  // S: columns 0..63, O: 64..127
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+__device__ __forceinline__ void store_split4(unsigned char* hi_tile, unsigned char* lo_tile, uint32_t off,
+                                             float4 v) {
+    float4 h, l;
+    split_tf32(v.x, h.x, l.x);
+    split_tf32(v.y, h.y, l.y);
+    split_tf32(v.z, h.z, l.z);
+    split_tf32(v.w, h.w, l.w);
+    *reinterpret_cast<float4*>(hi_tile + off) = h;
+    *reinterpret_cast<float4*>(lo_tile + off) = l;
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// Gather tokens [t0, min(t0 + 32, t1)) of kv head kh into a K/V tile pair;
-// rows past t1 are zero-filled. 32 tokens x 16 float4 x 2 pools = 8 per thread.
-__device__ __forceinline__ void load_tile(const PrefixParams& p, const int32_t* table, int kh, int t0, int t1,
-                                          float* kt, float* vt, int tid) {
+// Query block: qv = row_in_group * 3 + head_in_group -> tile row, hi/lo halves.
+// All 16 loads of a thread are issued before any is split and stored.
+__device__ __forceinline__ void load_queries(const PrefixParams& p, const PrefixWork& w, const int32_t* rows,
+                                             unsigned char* qhi, unsigned char* qlo, int tid) {
+    constexpr int kPer = kPQ * 16 / kPThreads;  // 16
+    float4 v[kPer];
 #pragma unroll
-    for (int it = 0; it < 4; ++it) {
-        const int idx = tid + it * kPThreads;  // 0..511
-        const int tok = idx >> 4, c4 = idx & 15;
-        const int t = t0 + tok;
-        float* kd = kt + tok * kRowStride + c4 * 4;
-        float* vd = vt + tok * kRowStride + c4 * 4;
-        if (t < t1) {
-            const int page = t / p.block_tokens;
-            int block = page < p.table_stride ? table[page] : -1;
-            if (block < 0 || block >= p.max_blocks) {
-                raise_error(p.error, kErrBounds);
-                block = 0;  // stay in bounds; the error word fails the step
-            }
-            const size_t off = ((size_t(block) * p.layers + p.layer) * p.block_tokens + (t - page * p.block_tokens)) *
-                                   kKvWidth + kh * kHeadDim + c4 * 4;
-            cp_async16(kd, p.keys + off);
-            cp_async16(vd, p.values + off);
-        } else {
-            *reinterpret_cast<float4*>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
-            *reinterpret_cast<float4*>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int u = 0; u < kPer; ++u) {
+        const int i = tid + u * kPThreads;
+        const int qi = i >> 4, c4 = i & 15;
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (qi < w.q_count) {
+            const int qv = w.q_begin + qi;
+            const int row = rows[qv / kGroup];
+            const int head = w.kv_head * kGroup + qv % kGroup;
+            v[u] = *reinterpret_cast<const float4*>(p.q + size_t(row) * p.q_stride + head * kHeadDim + c4 * 4);
         }
     }
-    cp_async_commit();
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+        const int i = tid + u * kPThreads;
+        const int qi = i >> 4, c4 = i & 15;
+        store_split4(qhi + (c4 >> 3) * kQTile, qlo + (c4 >> 3) * kQTile, sw128_offset(qi, c4 & 7), v[u]);
+    }
 }
 
-__global__ void __launch_bounds__(kPThreads, 3) prefix_attention_kernel(const PrefixParams p) {
-    extern __shared__ __align__(16) float sm[];
-    float* Qs = sm;                            // [64][68]
-    float* Kt = Qs + kPQ * kRowStride;         // [2][32][68]
-    float* Vt = Kt + 2 * kPT * kRowStride;     // [2][32][68]
-    float* Ps = Vt + 2 * kPT * kRowStride;     // [64][33]
+// Float offset of the K/V row of token t0 + t (kv head kh) in either pool, from the
+// sub-chunk's staged physical block ids (blk[t]).
+__device__ __forceinline__ size_t kv_offset(const PrefixParams& p, const int* blk, int t0, int t, int kh) {
+    const int token = t0 + t;
+    return ((size_t(blk[t]) * p.layers + p.layer) * p.block_tokens + token % p.block_tokens) * kKvWidth +
+           kh * kHeadDim;
+}
 
-    const int tid = threadIdx.x;
+// 3xTF32 product over 2 K blocks of 32: D = A_lo B_hi + A_hi B_lo + A_hi B_hi.
+__device__ __forceinline__ void issue_3xtf32(uint32_t tmem_d, const unsigned char* a_hi, const unsigned char* a_lo,
+                                             int a_block_bytes, const unsigned char* b_hi, const unsigned char* b_lo,
+                                             int b_block_bytes, uint32_t idesc) {
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb) {
+        const uint64_t ah = smem_desc(a_hi + kb * a_block_bytes), al = smem_desc(a_lo + kb * a_block_bytes);
+        const uint64_t bh = smem_desc(b_hi + kb * b_block_bytes), bl = smem_desc(b_lo + kb * b_block_bytes);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint64_t step = uint64_t(j * 32) >> 4;  // 8 tf32 = 32 bytes along the swizzled row
+            mma_tf32(tmem_d, al + step, bh + step, idesc, (kb | j) != 0);
+            mma_tf32(tmem_d, ah + step, bl + step, idesc, 1);
+            mma_tf32(tmem_d, ah + step, bh + step, idesc, 1);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kPThreads, 1) prefix_attention_kernel(const PrefixParams p) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* sm =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char *qhi = sm + kOffQhi, *qlo = sm + kOffQlo;
+    unsigned char *khi = sm + kOffKhi, *klo = sm + kOffKlo;
+    unsigned char *vhi = sm + kOffVhi, *vlo = sm + kOffVlo;
+    int* blk = reinterpret_cast<int*>(sm + kOffBlk);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffBar);
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 1);
+    int* failed = reinterpret_cast<int*>(tmem_holder + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5;
     const PrefixWork w = p.work[blockIdx.x];
     const int32_t* rows = p.group_rows + p.group_row0[w.group];
     const int32_t* table = p.tables + size_t(p.group_slot[w.group]) * p.table_stride;
     const int kh = w.kv_head;
 
-    // Query vectors: qv = row_in_group * 3 + head_in_group, 64 x 16 float4.
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-        const int idx = tid + it * kPThreads;  // 0..1023
-        const int qi = idx >> 4, c4 = idx & 15;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (qi < w.q_count) {
-            const int qv = w.q_begin + qi;
-            const int row = rows[qv / kGroup];
-            const int head = kh * kGroup + qv % kGroup;
-            v = *reinterpret_cast<const float4*>(p.q + size_t(row) * p.q_stride + head * kHeadDim + c4 * 4);
-        }
-        *reinterpret_cast<float4*>(Qs + qi * kRowStride + c4 * 4) = v;
+    if (warp == 0) tmem_alloc(tmem_holder, kTmemCols);
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        *failed = 0;
+        fence_barrier_init();
     }
-    const int n_tiles = (w.tok_end - w.tok_begin + kPT - 1) / kPT;
-    load_tile(p, table, kh, w.tok_begin, w.tok_end, Kt, Vt, tid);
+    load_queries(p, w, rows, qhi, qlo, tid);
+    tmem_fence_before();
+    __syncthreads();
+    tmem_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    const uint32_t tmem_s = tmem, tmem_o = tmem + kPT;
+    constexpr uint32_t idesc = umma_idesc_tf32<kPQ, kPT>();
 
-    // Thread = (query pair qp / qp + 32, token / dim quarter sub).
-    const int qp = tid >> 2, sub = tid & 3;
-    float acc[2][16];
+    const int qrow = warp * 32 + (tid & 31);  // TMEM lane = query row of this thread
+    const uint32_t lane_base = uint32_t(warp * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f, o_run[kHeadDim];
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[a][i] = 0.f;
-    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    for (int d = 0; d < kHeadDim; ++d) o_run[d] = 0.f;
+    uint32_t phase = 0;
+    bool ok = true;
 
-    for (int i = 0; i < n_tiles; ++i) {
-        const int buf = i & 1;
-        const int t0 = w.tok_begin + i * kPT;
+    for (int t0 = w.tok_begin; t0 < w.tok_end; t0 += kPT) {
         const int n_valid = min(kPT, w.tok_end - t0);
-        if (i + 1 < n_tiles) {
-            load_tile(p, table, kh, t0 + kPT, w.tok_end, Kt + (buf ^ 1) * kPT * kRowStride,
-                      Vt + (buf ^ 1) * kPT * kRowStride, tid);
-            cp_async_wait_one();
-        } else {
-            cp_async_wait_all();
+        // physical block of each token of the sub-chunk, looked up once
+        if (tid < kPT) {
+            int block = 0;
+            if (tid < n_valid) {
+                const int page = (t0 + tid) / p.block_tokens;
+                block = page < p.table_stride ? table[page] : -1;
+                if (block < 0 || block >= p.max_blocks) {
+                    raise_error(p.error, kErrBounds);
+                    block = 0;  // stay in bounds; the error word fails the step
+                }
+            }
+            blk[tid] = block;
         }
         __syncthreads();
-        const float* kt = Kt + buf * kPT * kRowStride;
-        const float* vt = Vt + buf * kPT * kRowStride;
-
-        // S: queries qp, qp + 32 x tokens sub + 4k
-        float s[2][8];
+        // K rows (token-major) and V^T (dim-major), hi / lo; tokens past the chunk are
+        // zero. Every load of a thread is issued before any store. K: consecutive
+        // threads walk one token's dims (coalesced); V: consecutive threads walk
+        // tokens, so a warp's transposed stores (one dim row, 32 tokens) hit 32
+        // distinct banks.
+        {
+            constexpr int kPer = kPT * 16 / kPThreads;  // 8
+            float4 kv[kPer], vv[kPer];
 #pragma unroll
-        for (int a = 0; a < 2; ++a)
+            for (int u = 0; u < kPer; ++u) {
+                const int i = tid + u * kPThreads;
+                const int tk = i >> 4, ck = i & 15;
+                const int tv = i & (kPT - 1), cv = i / kPT;
+                kv[u] = tk < n_valid ? *reinterpret_cast<const float4*>(p.keys + kv_offset(p, blk, t0, tk, kh) + ck * 4)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                vv[u] = tv < n_valid
+                            ? *reinterpret_cast<const float4*>(p.values + kv_offset(p, blk, t0, tv, kh) + cv * 4)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
-            for (int k = 0; k < 8; ++k) s[a][k] = 0.f;
-        const float* q0 = Qs + qp * kRowStride;
-        const float* q1 = Qs + (qp + 32) * kRowStride;
-#pragma unroll 2
-        for (int d4 = 0; d4 < kHeadDim / 4; ++d4) {
-            const float4 qa = *reinterpret_cast<const float4*>(q0 + 4 * d4);
-            const float4 qb = *reinterpret_cast<const float4*>(q1 + 4 * d4);
+            for (int u = 0; u < kPer; ++u) {
+                const int i = tid + u * kPThreads;
+                const int tk = i >> 4, ck = i & 15;
+                store_split4(khi + (ck >> 3) * kKTile, klo + (ck >> 3) * kKTile, sw128_offset(tk, ck & 7), kv[u]);
+                const int tv = i & (kPT - 1), cv = i / kPT;
+                const float ve[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const float4 kv = *reinterpret_cast<const float4*>(kt + (sub + 4 * k) * kRowStride + 4 * d4);
-                s[0][k] = fmaf(qa.x, kv.x, s[0][k]);
-                s[0][k] = fmaf(qa.y, kv.y, s[0][k]);
-                s[0][k] = fmaf(qa.z, kv.z, s[0][k]);
-                s[0][k] = fmaf(qa.w, kv.w, s[0][k]);
-                s[1][k] = fmaf(qb.x, kv.x, s[1][k]);
-                s[1][k] = fmaf(qb.y, kv.y, s[1][k]);
-                s[1][k] = fmaf(qb.z, kv.z, s[1][k]);
-                s[1][k] = fmaf(qb.w, kv.w, s[1][k]);
+                for (int e = 0; e < 4; ++e) {
+                    const int d = 4 * cv + e;  // V^T row; column = token tv (K block tv / 32)
+                    const uint32_t off = sw128_offset(d, (tv & 31) >> 2) + uint32_t(tv & 3) * 4;
+                    float h, l;
+                    split_tf32(ve[e], h, l);
+                    *reinterpret_cast<float*>(vhi + (tv >> 5) * kKTile + off) = h;
+                    *reinterpret_cast<float*>(vlo + (tv >> 5) * kKTile + off) = l;
+                }
             }
         }
-        // online softmax; the 4 lanes of a query pair hold its 32 scores
-#pragma unroll
-        for (int a = 0; a < 2; ++a) {
-            float mx = -INFINITY;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                s[a][k] = sub + 4 * k < n_valid ? s[a][k] * (0.125f * kLog2e) : -INFINITY;
-                mx = fmaxf(mx, s[a][k]);
-            }
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            const float m_new = fmaxf(m_run[a], mx);
-            const float alpha = exp2f(m_run[a] - m_new);
-            float sum = 0.f;
-            float* prow = Ps + (qp + 32 * a) * kPStride + sub;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const float pr = exp2f(s[a][k] - m_new);
-                sum += pr;
-                prow[4 * k] = pr;
-            }
-            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-            l_run[a] = l_run[a] * alpha + sum;
-            m_run[a] = m_new;
-#pragma unroll
-            for (int i2 = 0; i2 < 16; ++i2) acc[a][i2] *= alpha;
+        fence_proxy_async_shared();  // generic-proxy tile writes -> tensor-core reads
+        tmem_fence_before();
+        __syncthreads();
+        tmem_fence_after();
+        if (tid == 0) {
+            issue_3xtf32(tmem_s, qhi, qlo, kQTile, khi, klo, kKTile, idesc);
+            mma_commit(bar);
         }
-        __syncwarp();  // the 4 lanes of a query pair read each other's probabilities
-
-        // O += P V: dims sub*4 + 16k of both queries
-        const float* p0 = Ps + qp * kPStride;
-        const float* p1 = Ps + (qp + 32) * kPStride;
-#pragma unroll 4
+        if (!mbar_wait_bounded(bar, phase)) *failed = 1;
+        phase ^= 1;
+        __syncthreads();
+        if (*failed) {
+            ok = false;
+            break;
+        }
+        tmem_fence_after();
+        // scores of this thread's query row, base-2 units; exact softmax over the sub-chunk
+        float s[kPT];
+        {
+            uint32_t r[32];
+            tmem_load32(tmem_s + lane_base, r);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) s[j] = __uint_as_float(r[j]);
+            tmem_load32(tmem_s + lane_base + 32, r);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) s[32 + j] = __uint_as_float(r[j]);
+        }
+        float mx = -INFINITY;
+#pragma unroll
         for (int j = 0; j < kPT; ++j) {
-            const float pa = p0[j], pb = p1[j];
-            const float* vrow = vt + j * kRowStride + sub * 4;
-            const bool valid = j < n_valid;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                float4 v = *reinterpret_cast<const float4*>(vrow + 16 * k);
-                if (!valid) v = make_float4(0.f, 0.f, 0.f, 0.f);
-                acc[0][4 * k] = fmaf(pa, v.x, acc[0][4 * k]);
-                acc[0][4 * k + 1] = fmaf(pa, v.y, acc[0][4 * k + 1]);
-                acc[0][4 * k + 2] = fmaf(pa, v.z, acc[0][4 * k + 2]);
-                acc[0][4 * k + 3] = fmaf(pa, v.w, acc[0][4 * k + 3]);
-                acc[1][4 * k] = fmaf(pb, v.x, acc[1][4 * k]);
-                acc[1][4 * k + 1] = fmaf(pb, v.y, acc[1][4 * k + 1]);
-                acc[1][4 * k + 2] = fmaf(pb, v.z, acc[1][4 * k + 2]);
-                acc[1][4 * k + 3] = fmaf(pb, v.w, acc[1][4 * k + 3]);
-            }
+            s[j] = j < n_valid ? s[j] * (0.125f * kLog2e) : -INFINITY;
+            mx = fmaxf(mx, s[j]);
         }
-        __syncthreads();  // the tile buffer is refilled next iteration
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < kPT; ++j) {
+            s[j] = exp2f(s[j] - mx);
+            sum += s[j];
+        }
+        // P as the A operand (rows = query vectors, K = tokens), written over the
+        // query tiles now that S is complete; they are reloaded for a next sub-chunk
+#pragma unroll
+        for (int c4 = 0; c4 < kPT / 4; ++c4)
+            store_split4(qhi + (c4 >> 3) * kQTile, qlo + (c4 >> 3) * kQTile, sw128_offset(qrow, c4 & 7),
+                         make_float4(s[4 * c4], s[4 * c4 + 1], s[4 * c4 + 2], s[4 * c4 + 3]));
+        fence_proxy_async_shared();
+        tmem_fence_before();
+        __syncthreads();
+        tmem_fence_after();
+        if (tid == 0) {
+            issue_3xtf32(tmem_o, qhi, qlo, kQTile, vhi, vlo, kKTile, idesc);
+            mma_commit(bar);
+        }
+        if (!mbar_wait_bounded(bar, phase)) *failed = 1;
+        phase ^= 1;
+        __syncthreads();
+        if (*failed) {
+            ok = false;
+            break;
+        }
+        tmem_fence_after();
+        // fold this sub-chunk into the running (max, sum, output)
+        {
+            const float m_new = fmaxf(m_run, mx);
+            const float a_old = exp2f(m_run - m_new), a_new = exp2f(mx - m_new);
+            l_run = l_run * a_old + sum * a_new;
+            m_run = m_new;
+            uint32_t r[32];
+            tmem_load32(tmem_o + lane_base, r);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o_run[j] = fmaf(o_run[j], a_old, __uint_as_float(r[j]) * a_new);
+            tmem_load32(tmem_o + lane_base + 32, r);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o_run[32 + j] = fmaf(o_run[32 + j], a_old, __uint_as_float(r[j]) * a_new);
+        }
+        if (t0 + kPT < w.tok_end) {
+            // the next sub-chunk needs the query tiles again (they hold P now)
+            tmem_fence_before();
+            __syncthreads();
+            load_queries(p, w, rows, qhi, qlo, tid);
+        }
     }
 
-#pragma unroll
-    for (int a = 0; a < 2; ++a) {
-        const int qi = qp + 32 * a;
-        if (qi >= w.q_count) continue;
-        const int qv = w.q_begin + qi;
+    if (ok && qrow < w.q_count) {
+        const int qv = w.q_begin + qrow;
         const int row = rows[qv / kGroup];
         const int head = kh * kGroup + qv % kGroup;
         float* part = p.partial + (size_t(p.row_x0[row] + w.chunk) * kHeads + head) * (kHeadDim + 2);
-        // partial records are 66 floats: 8-byte aligned, so scalar stores
+        part[0] = m_run;
+        part[1] = l_run;
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) part[2 + sub * 4 + 16 * k + e] = acc[a][4 * k + e];
-        if (sub == 0) {
-            part[0] = m_run[a];
-            part[1] = l_run[a];
-        }
+        for (int d = 0; d < kHeadDim; ++d) part[2 + d] = o_run[d];
+    }
+    if (!ok && tid == 0) raise_error(p.error, kErrTimeout);
+    tmem_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tmem_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
     }
 }
 

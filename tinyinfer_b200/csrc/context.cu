@@ -93,7 +93,7 @@ struct AttnPlan {
 constexpr int kGroupMinRows = 8;
 constexpr int kGroupMinTokens = 128;
 constexpr int kPrefixMaxChunks = 64;
-constexpr double kPrefixTargetCtas = 148.0 * 3;  // one wave at 3 CTAs per SM
+constexpr double kPrefixTargetCtas = 148.0;  // one wave (one CTA per SM)
 
 // tables: host mirror of the device block tables ([slots][table_stride]).
 void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, int table_stride,
@@ -170,19 +170,20 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
             b = e;
         }
         // One chunk length for the step: the groups' (tokens x query blocks x kv
-        // heads) spread over about kPrefixTargetCtas CTAs, in whole 32-token tiles.
+        // heads) spread over about kPrefixTargetCtas CTAs, in whole sub-chunks.
         double work = 0;
         for (const auto& g : candidates) {
             const int qblocks = (int(g.e - g.b) * mpb::kGroup + mpb::kPrefixQueries - 1) / mpb::kPrefixQueries;
             work += double(g.pages) * block_tokens * qblocks * mpb::kKvHeads;
         }
-        const int step_chunk = std::max(32, int(std::ceil(work / kPrefixTargetCtas / 32.0)) * 32);
+        const int sub = mpb::kPrefixSubChunk;
+        const int step_chunk = std::max(sub, int(std::ceil(work / kPrefixTargetCtas / sub)) * sub);
         for (const auto& g : candidates) {
             const int n = int(g.e - g.b);
             const DecodeRow& ref = decode[keyed[g.b].second];
             const int shared = g.pages * block_tokens;
             int chunk_tokens = std::max(step_chunk, (shared + kPrefixMaxChunks - 1) / kPrefixMaxChunks);
-            chunk_tokens = (chunk_tokens + 31) / 32 * 32;
+            chunk_tokens = (chunk_tokens + sub - 1) / sub * sub;
             const int chunks = (shared + chunk_tokens - 1) / chunk_tokens;
             const int qvecs = n * mpb::kGroup;
             const int qblocks = (qvecs + mpb::kPrefixQueries - 1) / mpb::kPrefixQueries;

@@ -61,10 +61,11 @@ struct AttnParams {
 // Shared-prefix decode attention (attention_shared.cu). Decode rows whose block
 // tables start with the same physical pages form a group; the group's shared
 // tokens are read once per launch for all its rows. One CTA per (group, kv head,
-// block of kPrefixQueries (row, head) query vectors, token chunk) writes
-// (max, sum, unnormalised output) partials that the decode kernel's split merge
-// combines with the rows' own slices.
-constexpr int kPrefixQueries = 64;
+// block of kPrefixQueries (row, head) query vectors, token chunk of whole
+// kPrefixSubChunk-token sub-chunks) writes (max, sum, unnormalised output)
+// partials that the decode kernel's split merge combines with the rows' own slices.
+constexpr int kPrefixQueries = 128;
+constexpr int kPrefixSubChunk = 64;
 struct PrefixWork {
     int32_t group;
     int32_t kv_head;

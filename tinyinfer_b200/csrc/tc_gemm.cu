@@ -37,6 +37,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "umma.cuh"
 
 namespace mpb {
 namespace {
@@ -65,54 +66,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
             smem_u32(dst)),
         "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
-}
-
-// K-major, 128-byte swizzle UMMA shared-memory descriptor: start address >> 4,
-// LBO (ignored for swizzled K-major) 1, SBO = 1024 B between 8-row groups,
-// version 1 (sm_100), layout type 2 (SWIZZLE_128B).
-__device__ __forceinline__ uint64_t smem_desc(const void* tile) {
-    const uint64_t addr = smem_u32(tile);
-    uint64_t d = (addr >> 4) & 0x3FFFull;
-    d |= uint64_t(1) << 16;
-    d |= uint64_t(1024 >> 4) << 32;
-    d |= uint64_t(1) << 46;
-    d |= uint64_t(2) << 61;
-    return d;
-}
-
-// Instruction descriptor: D f32 (1 @ bit 4), A/B tf32 (2 @ bits 7, 10), both
-// K-major, N >> 3 @ bit 17, M >> 4 @ bit 24.
-template <int BN>
-__host__ __device__ constexpr uint32_t instr_desc() {
-    return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -288,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1 && lane == 0) {
         // MMA issuer
-        constexpr uint32_t idesc = instr_desc<BN>();
+        constexpr uint32_t idesc = umma_idesc_tf32<kBM, BN>();
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
             const int s = kb % S;
