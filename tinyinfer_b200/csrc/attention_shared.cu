@@ -14,12 +14,13 @@
 // (base-2 units) -- and the decode kernel's merge combines them with the rows'
 // own pages (attention.cu).
 //
-// CTA = (group, kv head, 128 query vectors, token chunk), 4 warps. Per 64-token
-// sub-chunk:
-//  * all threads gather K and V rows through the group's block table, split them
-//    into TF32 hi / lo halves and write K (64 tokens x 64 dims) and V^T (64 dims x
-//    64 tokens) as K-major 128-byte-swizzled UMMA tiles (the query block is
-//    written the same way);
+// CTA = (group, kv head, 128 query vectors, token chunk), 4 warps. The query block
+// is split once into TF32 hi / lo halves and written as K-major 128-byte-swizzled
+// UMMA tiles. Per 64-token sub-chunk:
+//  * the raw K and V rows were gathered through the group's block table by 16-byte
+//    cp.async into a staging buffer while the previous sub-chunk computed; all
+//    threads split them into hi / lo K (64 tokens x 64 dims) and V^T (64 dims x 64
+//    tokens) tiles, then start the next sub-chunk's gathers;
 //  * one thread issues S = Q K^T as 3xTF32 tcgen05.mma (M=128, N=64: Q_lo K_hi +
 //    Q_hi K_lo + Q_hi K_hi per 8-dim step) into tensor memory;
 //  * thread = query row: tcgen05.ld of its 64 scores, exact softmax over the
@@ -40,15 +41,27 @@ constexpr int kPT = 64;              // tokens per sub-chunk = UMMA N of S, K of
 constexpr int kPThreads = 128;
 constexpr int kQTile = kPQ * 32 * 4;   // one 32-element K block of a 128-row tile (16 KB)
 constexpr int kKTile = kPT * 32 * 4;   // one K block of a 64-row tile (8 KB)
-// shared memory (1024-aligned tiles): Q/P hi, Q/P lo (2 K blocks each), K hi, K lo,
-// V^T hi, V^T lo (2 K blocks each), then the barrier and the TMEM address
+// shared memory (1024-aligned tiles): Q hi / lo and P hi / lo (2 K blocks each),
+// K hi / lo and V^T hi / lo (2 K blocks each), the raw K and V staging rows
+// ([64 tokens][64 floats]; V's 16-byte chunks XOR-swizzled by token so the
+// transposing reads spread over the banks), the physical blocks of the staged
+// tokens, then the barrier and the TMEM address
 constexpr int kOffQhi = 0, kOffQlo = 2 * kQTile;
-constexpr int kOffKhi = 4 * kQTile, kOffKlo = kOffKhi + 2 * kKTile;
+constexpr int kOffPhi = 4 * kQTile, kOffPlo = 6 * kQTile;
+constexpr int kOffKhi = 8 * kQTile, kOffKlo = kOffKhi + 2 * kKTile;
 constexpr int kOffVhi = kOffKlo + 2 * kKTile, kOffVlo = kOffVhi + 2 * kKTile;
-constexpr int kOffBlk = kOffVlo + 2 * kKTile;  // [64] physical blocks of the sub-chunk's tokens
+constexpr int kOffRawK = kOffVlo + 2 * kKTile, kOffRawV = kOffRawK + kPT * kHeadDim * 4;
+constexpr int kOffBlk = kOffRawV + kPT * kHeadDim * 4;
 constexpr int kOffBar = kOffBlk + kPT * 4;
 constexpr size_t kPrefixSmem = size_t(kOffBar) + 64 + 1024 /*alignment slack*/;
+static_assert(kPrefixSmem <= 232448, "shared memory of the prefix kernel");
 constexpr uint32_t kTmemCols = 128;  // S: columns 0..63, O: 64..127
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void store_split4(unsigned char* hi_tile, unsigned char* lo_tile, uint32_t off,
                                              float4 v) {
@@ -113,13 +126,40 @@ __device__ __forceinline__ void issue_3xtf32(uint32_t tmem_d, const unsigned cha
     }
 }
 
+// Physical block of shared token `token`, bounds-checked.
+__device__ __forceinline__ int token_block(const PrefixParams& p, const int32_t* table, int token) {
+    const int page = token / p.block_tokens;
+    int block = page < p.table_stride ? table[page] : -1;
+    if (block < 0 || block >= p.max_blocks) {
+        raise_error(p.error, kErrBounds);
+        block = 0;  // stay in bounds; the error word fails the step
+    }
+    return block;
+}
+
+// Start the gathers of the raw K / V rows of tokens [t0, t0 + n) into staging
+// (blk holds their physical blocks); rows past n are not fetched.
+__device__ __forceinline__ void gather_raw(const PrefixParams& p, const int* blk, int t0, int n, int kh, float* raw_k,
+                                           float* raw_v, int tid) {
+    for (int i = tid; i < kPT * 16; i += kPThreads) {
+        const int t = i >> 4, c4 = i & 15;
+        if (t >= n) continue;
+        const size_t off = kv_offset(p, blk, t0, t, kh) + c4 * 4;
+        cp_async16(raw_k + t * kHeadDim + c4 * 4, p.keys + off);
+        cp_async16(raw_v + t * kHeadDim + ((c4 ^ (t & 15)) * 4), p.values + off);
+    }
+    cp_async_commit();
+}
+
 __global__ void __launch_bounds__(kPThreads, 1) prefix_attention_kernel(const PrefixParams p) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char *qhi = sm + kOffQhi, *qlo = sm + kOffQlo;
+    unsigned char *qhi = sm + kOffQhi, *qlo = sm + kOffQlo, *phi = sm + kOffPhi, *plo = sm + kOffPlo;
     unsigned char *khi = sm + kOffKhi, *klo = sm + kOffKlo;
     unsigned char *vhi = sm + kOffVhi, *vlo = sm + kOffVlo;
+    float* raw_k = reinterpret_cast<float*>(sm + kOffRawK);
+    float* raw_v = reinterpret_cast<float*>(sm + kOffRawV);
     int* blk = reinterpret_cast<int*>(sm + kOffBlk);
     uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffBar);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 1);
@@ -137,6 +177,13 @@ __global__ void __launch_bounds__(kPThreads, 1) prefix_attention_kernel(const Pr
         *failed = 0;
         fence_barrier_init();
     }
+    // sub-chunk 0's gathers first, then the query block while they fly
+    if (tid < kPT) blk[tid] = w.tok_begin + tid < w.tok_end ? token_block(p, table, w.tok_begin + tid) : 0;
+    __syncthreads();
+    gather_raw(p, blk, w.tok_begin, min(kPT, w.tok_end - w.tok_begin), kh, raw_k, raw_v, tid);
+    // physical block of this thread's token in the next sub-chunk, fetched early
+    int next_blk = 0;
+    if (tid < kPT && w.tok_begin + kPT + tid < w.tok_end) next_blk = token_block(p, table, w.tok_begin + kPT + tid);
     load_queries(p, w, rows, qhi, qlo, tid);
     tmem_fence_before();
     __syncthreads();
@@ -155,64 +202,47 @@ __global__ void __launch_bounds__(kPThreads, 1) prefix_attention_kernel(const Pr
 
     for (int t0 = w.tok_begin; t0 < w.tok_end; t0 += kPT) {
         const int n_valid = min(kPT, w.tok_end - t0);
-        // physical block of each token of the sub-chunk, looked up once
-        if (tid < kPT) {
-            int block = 0;
-            if (tid < n_valid) {
-                const int page = (t0 + tid) / p.block_tokens;
-                block = page < p.table_stride ? table[page] : -1;
-                if (block < 0 || block >= p.max_blocks) {
-                    raise_error(p.error, kErrBounds);
-                    block = 0;  // stay in bounds; the error word fails the step
-                }
-            }
-            blk[tid] = block;
+        cp_async_wait_all();
+        __syncthreads();  // this sub-chunk's raw rows are in shared memory
+        // split into hi / lo K rows (token-major) and V^T (dim-major); tokens past
+        // the sub-chunk are zero
+        for (int i = tid; i < kPT * 16; i += kPThreads) {
+            const int t = i >> 4, c4 = i & 15;
+            const float4 kv = t < n_valid ? *reinterpret_cast<const float4*>(raw_k + t * kHeadDim + c4 * 4)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+            store_split4(khi + (c4 >> 3) * kKTile, klo + (c4 >> 3) * kKTile, sw128_offset(t, c4 & 7), kv);
         }
-        __syncthreads();
-        // K rows (token-major) and V^T (dim-major), hi / lo; tokens past the chunk are
-        // zero. Every load of a thread is issued before any store. K: consecutive
-        // threads walk one token's dims (coalesced); V: consecutive threads walk
-        // tokens, so a warp's transposed stores (one dim row, 32 tokens) hit 32
-        // distinct banks.
-        {
-            constexpr int kPer = kPT * 16 / kPThreads;  // 8
-            float4 kv[kPer], vv[kPer];
+        for (int i = tid; i < kPT * 16; i += kPThreads) {
+            const int t = i & (kPT - 1), c4 = i / kPT;  // consecutive threads: consecutive tokens
+            const float4 vv = t < n_valid ? *reinterpret_cast<const float4*>(raw_v + t * kHeadDim + ((c4 ^ (t & 15)) * 4))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float ve[4] = {vv.x, vv.y, vv.z, vv.w};
 #pragma unroll
-            for (int u = 0; u < kPer; ++u) {
-                const int i = tid + u * kPThreads;
-                const int tk = i >> 4, ck = i & 15;
-                const int tv = i & (kPT - 1), cv = i / kPT;
-                kv[u] = tk < n_valid ? *reinterpret_cast<const float4*>(p.keys + kv_offset(p, blk, t0, tk, kh) + ck * 4)
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-                vv[u] = tv < n_valid
-                            ? *reinterpret_cast<const float4*>(p.values + kv_offset(p, blk, t0, tv, kh) + cv * 4)
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int u = 0; u < kPer; ++u) {
-                const int i = tid + u * kPThreads;
-                const int tk = i >> 4, ck = i & 15;
-                store_split4(khi + (ck >> 3) * kKTile, klo + (ck >> 3) * kKTile, sw128_offset(tk, ck & 7), kv[u]);
-                const int tv = i & (kPT - 1), cv = i / kPT;
-                const float ve[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int d = 4 * cv + e;  // V^T row; column = token tv (K block tv / 32)
-                    const uint32_t off = sw128_offset(d, (tv & 31) >> 2) + uint32_t(tv & 3) * 4;
-                    float h, l;
-                    split_tf32(ve[e], h, l);
-                    *reinterpret_cast<float*>(vhi + (tv >> 5) * kKTile + off) = h;
-                    *reinterpret_cast<float*>(vlo + (tv >> 5) * kKTile + off) = l;
-                }
+            for (int e = 0; e < 4; ++e) {
+                const int d = 4 * c4 + e;  // V^T row; column = token t (K block t / 32)
+                const uint32_t off = sw128_offset(d, (t & 31) >> 2) + uint32_t(t & 3) * 4;
+                float h, l;
+                split_tf32(ve[e], h, l);
+                *reinterpret_cast<float*>(vhi + (t >> 5) * kKTile + off) = h;
+                *reinterpret_cast<float*>(vlo + (t >> 5) * kKTile + off) = l;
             }
         }
         fence_proxy_async_shared();  // generic-proxy tile writes -> tensor-core reads
         tmem_fence_before();
-        __syncthreads();
+        __syncthreads();  // split tiles complete; the staging buffer is free
         tmem_fence_after();
         if (tid == 0) {
             issue_3xtf32(tmem_s, qhi, qlo, kQTile, khi, klo, kKTile, idesc);
             mma_commit(bar);
+        }
+        // the next sub-chunk's gathers overlap this one's products
+        const int t1 = t0 + kPT;
+        if (t1 < w.tok_end) {
+            if (tid < kPT) blk[tid] = next_blk;
+            __syncthreads();
+            gather_raw(p, blk, t1, min(kPT, w.tok_end - t1), kh, raw_k, raw_v, tid);
+            next_blk = 0;
+            if (tid < kPT && t1 + kPT + tid < w.tok_end) next_blk = token_block(p, table, t1 + kPT + tid);
         }
         if (!mbar_wait_bounded(bar, phase)) *failed = 1;
         phase ^= 1;
@@ -245,18 +275,17 @@ __global__ void __launch_bounds__(kPThreads, 1) prefix_attention_kernel(const Pr
             s[j] = exp2f(s[j] - mx);
             sum += s[j];
         }
-        // P as the A operand (rows = query vectors, K = tokens), written over the
-        // query tiles now that S is complete; they are reloaded for a next sub-chunk
+        // P as the A operand (rows = query vectors, K = tokens)
 #pragma unroll
         for (int c4 = 0; c4 < kPT / 4; ++c4)
-            store_split4(qhi + (c4 >> 3) * kQTile, qlo + (c4 >> 3) * kQTile, sw128_offset(qrow, c4 & 7),
+            store_split4(phi + (c4 >> 3) * kQTile, plo + (c4 >> 3) * kQTile, sw128_offset(qrow, c4 & 7),
                          make_float4(s[4 * c4], s[4 * c4 + 1], s[4 * c4 + 2], s[4 * c4 + 3]));
         fence_proxy_async_shared();
         tmem_fence_before();
         __syncthreads();
         tmem_fence_after();
         if (tid == 0) {
-            issue_3xtf32(tmem_o, qhi, qlo, kQTile, vhi, vlo, kKTile, idesc);
+            issue_3xtf32(tmem_o, phi, plo, kQTile, vhi, vlo, kKTile, idesc);
             mma_commit(bar);
         }
         if (!mbar_wait_bounded(bar, phase)) *failed = 1;
@@ -281,13 +310,9 @@ __global__ void __launch_bounds__(kPThreads, 1) prefix_attention_kernel(const Pr
 #pragma unroll
             for (int j = 0; j < 32; ++j) o_run[32 + j] = fmaf(o_run[32 + j], a_old, __uint_as_float(r[j]) * a_new);
         }
-        if (t0 + kPT < w.tok_end) {
-            // the next sub-chunk needs the query tiles again (they hold P now)
-            tmem_fence_before();
-            __syncthreads();
-            load_queries(p, w, rows, qhi, qlo, tid);
-        }
+        tmem_fence_before();
     }
+    cp_async_wait_all();  // nothing may still land in shared memory after the CTA ends
 
     if (ok && qrow < w.q_count) {
         const int qv = w.q_begin + qrow;
