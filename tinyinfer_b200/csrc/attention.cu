@@ -355,6 +355,7 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
 }
 
 __global__ void __launch_bounds__(kThreads, 3) paged_attention_kernel(const AttnParams p) {
+    pdl_enter();  // before any global memory access
     extern __shared__ __align__(128) unsigned char smem_raw[];
     float* stages = reinterpret_cast<float*>(smem_raw);
     float* probs = stages + 2 * kStages * kStageFloats;  // [3 consumers][3][16]
@@ -397,8 +398,7 @@ cudaError_t launch_paged_attention(const AttnParams& p, cudaStream_t stream) {
     if (p.work_count <= 0) return cudaSuccess;
     // persistent: one wave of 3 CTAs per SM pulls the work items
     const int grid = p.sched ? std::min(p.work_count, kAttnPersistentCtas) : p.work_count;
-    paged_attention_kernel<<<grid, kThreads, kAttnSmem, stream>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(paged_attention_kernel, dim3(grid), dim3(kThreads), kAttnSmem, stream, p);
 }
 
 }  // namespace mpb

@@ -67,6 +67,7 @@ __device__ __forceinline__ void load_tile(const PrefillParams& p, const int32_t*
 }
 
 __global__ void __launch_bounds__(kThreads, 2) prefill_attention_kernel(const PrefillParams p) {
+    pdl_enter();  // before any global memory access
     extern __shared__ __align__(16) float sm[];
     float* Qs = sm;                                  // [192][65]
     float* Ks = Qs + kQVec * kQStride;               // [2][32][68]
@@ -224,8 +225,7 @@ cudaError_t configure_prefill_attention() {
 
 cudaError_t launch_prefill_attention(const PrefillParams& p, cudaStream_t stream) {
     if (p.work_count <= 0) return cudaSuccess;
-    prefill_attention_kernel<<<p.work_count, kThreads, kPrefillSmem, stream>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(prefill_attention_kernel, dim3(p.work_count), dim3(kThreads), kPrefillSmem, stream, p);
 }
 
 }  // namespace mpb

@@ -152,6 +152,7 @@ __device__ __forceinline__ void gather_raw(const PrefixParams& p, const int* blk
 }
 
 __global__ void __launch_bounds__(kPThreads, 1) prefix_attention_kernel(const PrefixParams p) {
+    pdl_enter();  // before any global memory access
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -342,8 +343,7 @@ cudaError_t configure_prefix_attention() {
 
 cudaError_t launch_prefix_attention(const PrefixParams& p, cudaStream_t stream) {
     if (p.work_count <= 0) return cudaSuccess;
-    prefix_attention_kernel<<<p.work_count, kPThreads, kPrefixSmem, stream>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(prefix_attention_kernel, dim3(p.work_count), dim3(kPThreads), kPrefixSmem, stream, p);
 }
 
 }  // namespace mpb

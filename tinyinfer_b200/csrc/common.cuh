@@ -120,4 +120,34 @@ __device__ __forceinline__ void raise_error(unsigned* error, unsigned bits) {
     if (error) atomicOr(error, bits);
 }
 
+// Programmatic dependent launch. Kernels of the forward are launched with
+// programmatic stream serialisation: a kernel may start while its predecessor
+// finishes, runs only work that touches no memory of earlier kernels, then waits
+// (pdl_wait) until the predecessor completed and its writes are visible. Once
+// past the wait a kernel lets its own successor launch (pdl_trigger), so at most
+// two kernels of the chain overlap. Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_enter() {
+    pdl_wait();
+    pdl_trigger();
+}
+
+// Host: launch `kernel` with programmatic stream serialisation.
+template <class... Params, class... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
 }  // namespace mpb

@@ -45,6 +45,7 @@ __device__ __forceinline__ void rms_row(const float* x, const float* w, float ep
 __global__ void embed_rmsnorm_kernel(const int32_t* tokens, const float* embed, int vocabulary, const float* w,
                                      float eps, float* x, float* normed_hi, float* normed_lo, int rows, int hidden,
                                      unsigned* error) {
+    pdl_enter();  // before any global memory access
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
     if (row >= rows) return;
     int tok = tokens[row];
@@ -62,6 +63,7 @@ __global__ void embed_rmsnorm_kernel(const int32_t* tokens, const float* embed, 
 
 __global__ void rmsnorm_kernel(const float* x, const int32_t* rows, const float* w, float eps, float* out_hi,
                                float* out_lo, int count, int hidden) {
+    pdl_enter();  // before any global memory access
     const int i = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
     if (i >= count) return;
     const int r = rows ? rows[i] : i;
@@ -74,6 +76,7 @@ __global__ void rmsnorm_kernel(const float* x, const int32_t* rows, const float*
 // the CPU runner (llama_runner.cpp:17-22) computes it; cos/sin come from tables
 // the host filled with the same libm calls as the CPU runner.
 __global__ void __launch_bounds__(384) rope_append_kernel(const RopeAppendArgs a) {
+    pdl_enter();  // before any global memory access
     const int row = blockIdx.x, t = threadIdx.x;
     const int pos = a.row_pos[row];
     const float* src = a.qkv + size_t(row) * a.qkv_stride;
@@ -119,6 +122,7 @@ __global__ void __launch_bounds__(384) rope_append_kernel(const RopeAppendArgs a
 // candidates compare by value, then by lower index.
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int vocabulary, int32_t* tokens,
                                                       int32_t* finite) {
+    pdl_enter();  // before any global memory access
     const int row = blockIdx.x, t = threadIdx.x;
     const float* x = logits + size_t(row) * vocabulary;
     float best = -INFINITY;
@@ -177,6 +181,7 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int v
 // `width` floats in both pools. Offsets are validated against the pool size.
 __global__ void cow_copy_kernel(const CowRegion* regions, float* keys, float* values, uint64_t pool_elements,
                                 unsigned* error) {
+    pdl_enter();  // before any global memory access
     const CowRegion r = regions[blockIdx.x];
     const uint64_t row = blockIdx.y;
     if (row >= r.rows) return;
@@ -197,6 +202,7 @@ __global__ void cow_copy_kernel(const CowRegion* regions, float* keys, float* va
 
 __global__ void table_patch_kernel(const int32_t* pairs, int count, int32_t* tables, int64_t elements,
                                    unsigned* error) {
+    pdl_enter();  // before any global memory access
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= count) return;
     const int64_t index = pairs[2 * i];
@@ -213,43 +219,40 @@ cudaError_t launch_embed_rmsnorm(const int32_t* tokens, const float* embed, int 
                                  float eps, float* x, float* normed_hi, float* normed_lo, int rows, int hidden,
                                  unsigned* error, cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
-    embed_rmsnorm_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(tokens, embed, vocabulary, norm_w, eps, x, normed_hi,
-                                                            normed_lo, rows, hidden, error);
-    return cudaGetLastError();
+    return launch_pdl(embed_rmsnorm_kernel, dim3((rows + 7) / 8), dim3(256), 0, stream, tokens, embed, vocabulary,
+                      norm_w, eps, x, normed_hi, normed_lo, rows, hidden, error);
 }
 
 cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, float* out_hi,
                            float* out_lo, int count, int hidden, cudaStream_t stream) {
     if (count <= 0) return cudaSuccess;
-    rmsnorm_kernel<<<(count + 7) / 8, 256, 0, stream>>>(x, rows, norm_w, eps, out_hi, out_lo, count, hidden);
-    return cudaGetLastError();
+    return launch_pdl(rmsnorm_kernel, dim3((count + 7) / 8), dim3(256), 0, stream, x, rows, norm_w, eps, out_hi, out_lo,
+                      count, hidden);
 }
 
 cudaError_t launch_rope_append(const RopeAppendArgs& a, cudaStream_t stream) {
     if (a.rows <= 0) return cudaSuccess;
-    rope_append_kernel<<<a.rows, 384, 0, stream>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(rope_append_kernel, dim3(a.rows), dim3(384), 0, stream, a);
 }
 
 cudaError_t launch_argmax(const float* logits, int rows, int vocabulary, int32_t* tokens, int32_t* finite,
                           cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
-    argmax_kernel<<<rows, 1024, 0, stream>>>(logits, vocabulary, tokens, finite);
-    return cudaGetLastError();
+    return launch_pdl(argmax_kernel, dim3(rows), dim3(1024), 0, stream, logits, vocabulary, tokens, finite);
 }
 
 cudaError_t launch_cow_copy(const CowRegion* regions, int count, int max_rows, float* keys, float* values,
                             uint64_t pool_elements, unsigned* error, cudaStream_t stream) {
     if (count <= 0 || max_rows <= 0) return cudaSuccess;
-    cow_copy_kernel<<<dim3(count, max_rows), 256, 0, stream>>>(regions, keys, values, pool_elements, error);
-    return cudaGetLastError();
+    return launch_pdl(cow_copy_kernel, dim3(count, max_rows), dim3(256), 0, stream, regions, keys, values,
+                      pool_elements, error);
 }
 
 cudaError_t launch_table_patch(const int32_t* pairs, int count, int32_t* tables, int64_t table_elements,
                                unsigned* error, cudaStream_t stream) {
     if (count <= 0) return cudaSuccess;
-    table_patch_kernel<<<(count + 255) / 256, 256, 0, stream>>>(pairs, count, tables, table_elements, error);
-    return cudaGetLastError();
+    return launch_pdl(table_patch_kernel, dim3((count + 255) / 256), dim3(256), 0, stream, pairs, count, tables,
+                      table_elements, error);
 }
 
 }  // namespace mpb

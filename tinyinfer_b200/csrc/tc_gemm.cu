@@ -223,6 +223,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_fence_after();
     const uint32_t tmem = *tmem_holder;
 
+    // The weights (B) never depend on an earlier kernel: the first stages' weight
+    // tiles are requested before waiting for the predecessor (programmatic
+    // dependent launch), the activations (A) only after.
+    const int pre = min(S, kblocks);
+    if (warp == 0 && lane == 0) {
+        for (int kb = 0; kb < pre; ++kb) {
+            unsigned char* st = smem + kb * Cfg::kStage;
+            mbar_arrive_expect_tx(&full[kb], Cfg::kStage);
+            const int kx = (kb_begin + kb) * kBK;
+            tma_load_2d(st + 2 * Cfg::kATile, &b_hi, kx, p.b_row0 + n0, &full[kb]);
+            tma_load_2d(st + 2 * Cfg::kATile + Cfg::kBTile, &b_lo, kx, p.b_row0 + n0, &full[kb]);
+        }
+    }
+    pdl_enter();
     if (warp == 0 && lane == 0) {
         // TMA producer
         for (int kb = 0; kb < kblocks; ++kb) {
@@ -232,12 +246,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             unsigned char* st = smem + s * Cfg::kStage;
-            mbar_arrive_expect_tx(&full[s], Cfg::kStage);
             const int kx = (kb_begin + kb) * kBK;
+            if (kb >= pre) {
+                mbar_arrive_expect_tx(&full[s], Cfg::kStage);
+                tma_load_2d(st + 2 * Cfg::kATile, &b_hi, kx, p.b_row0 + n0, &full[s]);
+                tma_load_2d(st + 2 * Cfg::kATile + Cfg::kBTile, &b_lo, kx, p.b_row0 + n0, &full[s]);
+            }
             tma_load_2d(st, &a_hi, kx, m0, &full[s]);
             tma_load_2d(st + Cfg::kATile, &a_lo, kx, m0, &full[s]);
-            tma_load_2d(st + 2 * Cfg::kATile, &b_hi, kx, p.b_row0 + n0, &full[s]);
-            tma_load_2d(st + 2 * Cfg::kATile + Cfg::kBTile, &b_lo, kx, p.b_row0 + n0, &full[s]);
         }
     } else if (warp == 1 && lane == 0) {
         // MMA issuer
@@ -329,13 +345,15 @@ cudaError_t launch_bn(const TcGemmMaps& maps, const TcGemmParams& p, cudaStream_
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = Cfg::kSmem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = unsigned(splits);
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, E>, *maps.a_hi, *maps.a_lo, *maps.b_hi, *maps.b_lo, p);
 }
 
