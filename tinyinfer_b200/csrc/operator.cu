@@ -20,6 +20,7 @@ struct Scratch {
     unsigned* counters = nullptr;
     size_t counter_capacity = 0;
     unsigned* error = nullptr;
+    unsigned* sched = nullptr;  // [2] persistent schedule of the decode kernel (zero between launches)
 };
 
 std::mutex g_scratch_mutex;
@@ -83,11 +84,23 @@ extern "C" int mp_paged_attention_decode(const float* q, const float* keys, cons
         host[3 * count + r] = int(work.size());   // first work item
         for (int k = 0; k < n; ++k) work.push_back({r, k * pps, std::min(pages, (k + 1) * pps), k});
     }
-    const size_t words = host.size() + 4 * work.size();
+    // processing order of the persistent kernel: longest slices first
+    std::vector<int32_t> order(work.size());
+    for (size_t i = 0; i < order.size(); ++i) order[i] = int32_t(i);
+    auto tokens = [&](int32_t i) {
+        const auto& w = work[i];
+        return std::min(w.page_end * block_tokens, int(lengths[w.row])) - w.page_begin * block_tokens;
+    };
+    std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return tokens(a) > tokens(b); });
+    const size_t words = host.size() + 4 * work.size() + order.size();
     cudaError_t e = grow(s.meta, s.meta_capacity, words, stream, false);
     if (e == cudaSuccess) e = grow(s.partial, s.partial_capacity, work.size() * mpb::kHeads * (mpb::kHeadDim + 2),
                                    stream, false);
     if (e == cudaSuccess) e = grow(s.counters, s.counter_capacity, size_t(count) * mpb::kKvHeads, stream, true);
+    if (e == cudaSuccess && !s.sched) {
+        e = cudaMalloc(reinterpret_cast<void**>(&s.sched), 2 * sizeof(unsigned));
+        if (e == cudaSuccess) e = cudaMemsetAsync(s.sched, 0, 2 * sizeof(unsigned), stream);
+    }
     if (e == cudaSuccess && !s.error) {
         e = cudaMalloc(reinterpret_cast<void**>(&s.error), sizeof(unsigned));
         if (e == cudaSuccess) e = cudaMemsetAsync(s.error, 0, sizeof(unsigned), stream);
@@ -100,6 +113,7 @@ extern "C" int mp_paged_attention_decode(const float* q, const float* keys, cons
     host.resize(words);
     std::copy(reinterpret_cast<const int32_t*>(work.data()), reinterpret_cast<const int32_t*>(work.data()) + 4 * work.size(),
               host.begin() + 4 * count);
+    std::copy(order.begin(), order.end(), host.begin() + 4 * count + 4 * work.size());
     // Pageable source: the copy is staged before cudaMemcpyAsync returns.
     e = cudaMemcpyAsync(s.meta, host.data(), words * 4, cudaMemcpyHostToDevice, stream);
     if (e != cudaSuccess) {
@@ -123,8 +137,10 @@ extern "C" int mp_paged_attention_decode(const float* q, const float* keys, cons
     p.row_work0 = s.meta + 3 * count;
     p.work = reinterpret_cast<const mpb::AttnWork*>(s.meta + 4 * count);
     p.work_count = int(work.size());
+    p.order = s.meta + 4 * count + 4 * work.size();
     p.partial = s.partial;
     p.counters = s.counters;
+    p.sched = s.sched;
     p.out = out;
     p.out_stride = mpb::kQWidth;
     p.error = s.error;

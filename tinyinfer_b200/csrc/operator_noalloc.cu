@@ -18,7 +18,7 @@
 // rejected with MP_ERR_INVALID and a message, before anything is queued.
 //
 // Sharing: all calls on a device share the one array, which keeps the last
-// call's contents. Each call clears the arrival counters (which must start at
+// call's contents. Each call clears the arrival counters and the schedule (which must start at
 // zero) on its stream before the kernel; the other regions are fully written
 // before they are read. Calls whose device work overlaps -- on different
 // streams, or from different host threads without ordering -- race on the
@@ -42,12 +42,13 @@ constexpr int kMaxWork = 2048;
 constexpr int kMaxDevices = 64;
 constexpr size_t kPartialFloats = size_t(kMaxWork) * mpb::kHeads * (mpb::kHeadDim + 2);
 // Layout (bytes): partials | metadata (4 x kMaxRows row words + 4 x kMaxWork work words) |
-// counters (kMaxRows x 3 kv heads) | error
+// counters (kMaxRows x 3 kv heads) | schedule (2 words) | error
 constexpr size_t kPartialBytes = kPartialFloats * sizeof(float);
-constexpr size_t kMetaWords = 4 * size_t(kMaxRows) + 4 * size_t(kMaxWork);
+constexpr size_t kMetaWords = 4 * size_t(kMaxRows) + 5 * size_t(kMaxWork);  // rows | work | order
 constexpr size_t kMetaOffset = kPartialBytes;
 constexpr size_t kCounterOffset = kMetaOffset + kMetaWords * sizeof(int32_t);
-constexpr size_t kErrorOffset = kCounterOffset + size_t(kMaxRows) * mpb::kKvHeads * sizeof(unsigned);
+constexpr size_t kSchedOffset = kCounterOffset + size_t(kMaxRows) * mpb::kKvHeads * sizeof(unsigned);
+constexpr size_t kErrorOffset = kSchedOffset + 2 * sizeof(unsigned);
 constexpr size_t kScratchBytes = (kErrorOffset + sizeof(unsigned) + 255) / 256 * 256;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
@@ -122,6 +123,7 @@ extern "C" int mp_paged_attention_decode_noalloc(const float* q, const float* ke
     float* partial = reinterpret_cast<float*>(base);
     int32_t* meta = reinterpret_cast<int32_t*>(base + kMetaOffset);
     unsigned* counters = reinterpret_cast<unsigned*>(base + kCounterOffset);
+    unsigned* sched = reinterpret_cast<unsigned*>(base + kSchedOffset);
     unsigned* error = reinterpret_cast<unsigned*>(base + kErrorOffset);
 
     // Row arrays (slot, length, slices, first slice) then the work list.
@@ -142,10 +144,26 @@ extern "C" int mp_paged_attention_decode_noalloc(const float* q, const float* ke
             items[4 * work + 3] = k;
         }
     }
+    // processing order of the persistent kernel: longest slices first (insertion
+    // sort into the fixed array; at most kMaxWork items)
+    int32_t* order = items + 4 * work;
+    for (int i = 0; i < work; ++i) {
+        auto tokens = [&](int k) {
+            return std::min(items[4 * k + 2] * block_tokens, int(lengths[items[4 * k]])) - items[4 * k + 1] * block_tokens;
+        };
+        const int ti = tokens(i);
+        int j = i;
+        while (j > 0 && tokens(order[j - 1]) < ti) {
+            order[j] = order[j - 1];
+            --j;
+        }
+        order[j] = i;
+    }
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-    cudaError_t e = cudaMemcpyAsync(meta, g_host_meta, size_t(4 * count + 4 * work) * sizeof(int32_t),
+    cudaError_t e = cudaMemcpyAsync(meta, g_host_meta, size_t(4 * count + 5 * work) * sizeof(int32_t),
                                     cudaMemcpyHostToDevice, stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(counters, 0, size_t(count) * mpb::kKvHeads * sizeof(unsigned), stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(sched, 0, 2 * sizeof(unsigned), stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(error, 0, sizeof(unsigned), stream);
     if (e == cudaSuccess) e = mpb::configure_attention();
     if (e != cudaSuccess) {
@@ -169,8 +187,10 @@ extern "C" int mp_paged_attention_decode_noalloc(const float* q, const float* ke
     p.row_work0 = meta + 3 * count;
     p.work = reinterpret_cast<const mpb::AttnWork*>(meta + 4 * count);
     p.work_count = work;
+    p.order = meta + 4 * count + 4 * work;
     p.partial = partial;
     p.counters = counters;
+    p.sched = sched;
     p.out = out;
     p.out_stride = mpb::kQWidth;
     p.error = device_error ? reinterpret_cast<unsigned*>(device_error) : error;
