@@ -147,6 +147,17 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def logical_decode_bytes(engine, ids):
+    """K/V bytes one layer's decode attention would read if every row streamed its
+    whole context (no shared-prefix dedup): sum of context lengths x 1536 B."""
+    total = 0
+    for rid in ids:
+        s = engine.sequence(rid)
+        if s:
+            total += s[0] + 1
+    return total * 2 * 192 * 4
+
+
 def unique_decode_bytes(engine, ids, block_tokens):
     """Bytes of the distinct (page, slot) K/V rows one layer's decode attention reads
     (each shared prefix page once), x 1536 B per token row."""
@@ -270,6 +281,7 @@ def run_b200(args, rank, world, local_rank):
     for _ in range(args.warmup):
         decode_step()
     uniq = unique_decode_bytes(engine, ids, bt)
+    logical = logical_decode_bytes(engine, ids)
     before = dev.counters(reset=True)
     # kernels launched before the timed steps (for `ncu -s` on this command)
     print(f"launches_before_timed={before['kernel_launches']}", file=sys.stderr, flush=True)
@@ -357,12 +369,15 @@ def run_b200(args, rank, world, local_rank):
                 "d2h_bytes_per_step": counters["d2h_bytes"] / max(counters["forwards"], 1),
                 "ms_per_step": e2e_ms / args.steps},
         "gpu_launches": int(counters["kernel_launches"]),
-        "roofline": {"bound": "hbm", "kernel": "paged_attention_kernel (decode, split-K)",
+        "roofline": {"bound": "hbm",
+                     "kernel": "decode attention: prefix_attention_kernel (shared pages, tcgen05) + "
+                               "paged_attention_kernel (rows' own pages, split-K), timed together per layer",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm if achieved else None, "traffic": traffic,
                      "peak_kind": peak_kind, "launch_ms": launch_ms, "launches": attn_launches,
                      "algorithmic_bytes_per_launch": bytes_per_launch,
                      "unique_bytes_per_launch": unique_per_launch,
+                     "logical_bytes_per_launch": logical,
                      "unique_achieved": unique_per_launch / (launch_ms * 1e-3) / 1e9 if launch_ms > 0 else None,
                      "attention_share_of_forward": attn_ms / device_ms if device_ms else None},
         "clocks": clocks.summary(),
