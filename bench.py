@@ -58,6 +58,10 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--operator", action="store_true",
                    help="time the paged-attention decode operator alone on BASELINE config 2")
+    p.add_argument("--workload", choices=["config3", "config4", "config5"], default="config3",
+                   help="config3: the headline decode benchmark; config4 / config5: the serving workloads "
+                        "of bench_serving.py")
+    p.add_argument("--serve-requests", type=int, default=2048, help="config 5 request count")
     return p.parse_args()
 
 
@@ -489,6 +493,11 @@ def main():
         line = run_reference(args, rank, world)
     elif args.operator:
         line = run_operator(args, local_rank) if rank == 0 else None
+    elif args.workload != "config3":
+        import bench_serving
+
+        run = bench_serving.run_config4 if args.workload == "config4" else bench_serving.run_config5
+        line = run(args, rank, world, local_rank)
     else:
         line = run_b200(args, rank, world, local_rank)
         if line is not None and world == 1 and not args.no_cpu_baseline:

@@ -130,6 +130,41 @@ def test_cow_region_copies_both_pools(built):
 
 
 @pytest.mark.gpu
+def test_forward_cow_chain_reads_sources_first(built):
+    """The COW regions of one batched step apply as if every source were read
+    before any destination is written: with per-step publishing, the page a decode
+    append copies away from is freed and handed to the next append's copy in the
+    same step (page 4 below is both a source and a destination), so each
+    destination must get its source's content from before the step."""
+    ctx = device_for(MINI, random_weights(MINI, seed=2), 4, 12, max_sequences=2, max_step_tokens=8,
+                     max_step_sequences=2)
+    kvw, layers, bt = MINI.kv_width, MINI.layers, 4
+    _, _, n = ctx.pools()
+    keys = np.arange(1, n + 1, dtype=np.float32)
+    ctx.kv_write(0, 0, keys)
+    ctx.kv_write(1, 0, -keys)
+    pitch = bt * kvw
+    page = layers * pitch
+    # (destination, source, valid rows): 3 <- 4, 4 <- 5, 5 <- 6, 6 <- 7 and an
+    # independent 10 <- 9
+    chain = [(3, 4, 3), (4, 5, 2), (5, 6, 1), (6, 7, 3), (10, 9, 2)]
+    regions = [(d * page, s * page, pitch, v * kvw, layers) for d, s, v in chain]
+    ctx.table_write(0, 0, [0])
+    ctx.forward([(0, 0, 1)], [3], regions=regions, logits=False)
+    k = ctx.kv_read(0, 0, n)
+    v = ctx.kv_read(1, 0, n)
+    expect = keys.copy()
+    for d, s, rows in chain:
+        for row in range(layers):
+            s0, d0 = s * page + row * pitch, d * page + row * pitch
+            expect[d0:d0 + rows * kvw] = keys[s0:s0 + rows * kvw]
+    # page 0 holds the step's own K/V row; everything else must match exactly
+    assert np.array_equal(k[page:], expect[page:])
+    assert np.array_equal(v[page:], -expect[page:])
+    ctx.close()
+
+
+@pytest.mark.gpu
 def test_135m_config1_prefix_and_greedy(built):
     """BASELINE config 1 shape (30 layers, vocab 49152, tied, page 16), shortened to a
     64-token prompt and 6 greedy steps so the C oracle finishes in seconds."""

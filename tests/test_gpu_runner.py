@@ -221,3 +221,53 @@ def test_batched_engine_streams_match_oracle(built):
     assert st["prefix_hits"] >= 5 and engine.cost_stats()["cow_pages"] >= 1
     engine.shutdown()
     assert engine.runner_stats()["kv_live_blocks"] == 0
+
+
+@pytest.mark.gpu
+def test_decode_steps_run_as_one_forward(built):
+    """The engine publishes every request's pages after each append (engine.cpp:
+    93-98), so every decode append copies its shared partial tail, and the page it
+    copied away from is freed and handed to the next request's copy in the same
+    step. Those copies read their sources before any destination is written, so a
+    pure decode step is one device forward with no hazard flush, and every stream
+    still equals the oracle's."""
+    from tinyinfer_b200.host import Engine, Runner
+
+    cfg = ModelConfig(layers=2, intermediate=128, vocabulary=64, context=64, tied=True)
+    w = random_weights(cfg, seed=19)
+    o = Oracle(cfg, w, 4)
+
+    def token(seq):
+        keys, values = o.new_pools(32)
+        out, _ = o.append(keys, values, list(range(32)), 0, list(seq))
+        return int(np.argmax(out))
+
+    runner = Runner.b200(cfg, w, context=64, block_tokens=4, max_blocks=256, prefix_blocks=64, max_sequences=16,
+                         max_step_tokens=128, max_step_sequences=16)
+    engine = Engine(runner, 8, 128, 32, 64)
+    rng = np.random.default_rng(9)
+    prompts = {f"r{i}": [int(t) for t in rng.integers(0, 64, int(rng.integers(5, 15)))] for i in range(8)}
+    for rid, p in prompts.items():
+        engine.submit(rid, p, 9)
+    outputs, decode_steps = {}, 0
+    while not engine.idle():
+        f0, h0 = engine.flushes()
+        engine.step()
+        f1, h1 = engine.flushes()
+        st = engine.last_step_stats()
+        if st["prefill_tokens"] == 0 and st["decode_tokens"] > 1:
+            decode_steps += 1
+            assert (f1 - f0, h1 - h0) == (1, 0), st
+        for rid, tok, reason, err in engine.poll_events():
+            assert reason in (None, 1), err
+            if tok is not None:
+                outputs.setdefault(rid, []).append(tok)
+    assert decode_steps >= 6
+    assert engine.cost_stats()["cow_pages"] >= 8 * 4
+    for rid, p in prompts.items():
+        seq = list(p)
+        assert len(outputs[rid]) == 9
+        for t in outputs[rid]:
+            assert t == token(seq), rid
+            seq.append(t)
+    engine.shutdown()

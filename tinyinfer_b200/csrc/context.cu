@@ -328,12 +328,18 @@ struct mp_context {
     size_t patch_capacity = 0;
     uint64_t* h_cow = nullptr;
     size_t cow_capacity = 0;
+    // two-phase COW: sources gathered here (keys, then values) before any
+    // destination is written, when a destination overlaps a source of the step
+    float* cow_scratch = nullptr;
+    size_t cow_scratch_capacity = 0;  // floats per pool
+    uint64_t cow_scratch_elements = 0;
+    bool cow_two_phase = false;
     // current step
     int rows = 0, seqs = 0, work_count = 0, prefill_count = 0, prefix_count = 0, entry_count = 0, region_count = 0,
         region_rows = 0;
     size_t extra_capacity = 0, prefix_capacity = 0;
     uint64_t step_prefix_rows = 0, step_prefix_tokens = 0;
-    size_t off_entries = 0, off_regions = 0, entry_capacity = 0, region_capacity = 0;
+    size_t off_entries = 0, off_regions = 0, off_scratch = 0, entry_capacity = 0, region_capacity = 0;
     bool cow_timing = false, cow_timed = false;
     cudaEvent_t cow_events[2] = {nullptr, nullptr};
     cudaEvent_t fwd_events[2] = {nullptr, nullptr};
@@ -418,7 +424,7 @@ void free_context(mp_context* c) {
                     (void*)c->qkv, (void*)c->q, (void*)c->logits,
                     (void*)c->partial,
                     (void*)c->counters, (void*)c->attn_sched, (void*)c->error, (void*)c->meta, (void*)c->out_tokens, (void*)c->out_finite,
-                    (void*)c->cow, (void*)c->patch})
+                    (void*)c->cow, (void*)c->patch, (void*)c->cow_scratch})
         if (p) cudaFree(p);
     for (auto* s : {&c->wqkv, &c->wo, &c->wgu, &c->wdown, &c->head, &c->xn, &c->attn, &c->h, &c->xl}) {
         if (s->hi) cudaFree(s->hi);
@@ -698,7 +704,7 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         c->entry_capacity = S * size_t(r.table_stride);
         c->region_capacity = S;
         c->meta_capacity = 6 * T + S + 4 * c->work_capacity + 8 * c->prefill_capacity + 2 * c->entry_capacity +
-                           10 * c->region_capacity + 2 + 4 * T + 2 + 8 * c->prefix_capacity + c->work_capacity;
+                           12 * c->region_capacity + 2 + 4 * T + 2 + 8 * c->prefix_capacity + c->work_capacity;
         for (auto& e : c->cow_events) cuda_check(cudaEventCreate(&e), "create cow timing event");
         for (auto& e : c->fwd_events) cuda_check(cudaEventCreate(&e), "create forward timing event");
         c->meta = device_alloc<int32_t>(c->meta_capacity, "step metadata");
@@ -846,6 +852,7 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
                 fail(MP_ERR_INVALID, "invalid block table entry");
         }
         int region_rows = 0;
+        uint64_t region_elements = 0;  // rows x width summed over the regions (per pool)
         for (int i = 0; i < region_count; ++i) {
             const auto& r = regions[i];
             if (r.width % 4 || r.destination % 4 || r.source % 4 || r.pitch % 4 || r.width > r.pitch ||
@@ -853,6 +860,31 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
                 r.source + (r.rows ? (r.rows - 1) * r.pitch + r.width : 0) > c->pool_elements)
                 fail(MP_ERR_INVALID, "COW region outside the pools");
             region_rows = std::max(region_rows, int(r.rows));
+            region_elements += r.rows * r.width;
+        }
+        // Regions apply as if every source were read before any destination is
+        // written: a destination span that overlaps some region's source span
+        // (a page freed and handed out again within the step) makes the copy
+        // two-phase through the gather scratch.
+        bool two_phase = false;
+        if (region_count > 1) {
+            auto span_end = [](const mp_tail_copy_region& r, uint64_t start) {
+                return start + (r.rows ? (r.rows - 1) * r.pitch + r.width : 0);
+            };
+            std::vector<std::pair<uint64_t, uint64_t>> sources(static_cast<size_t>(region_count));
+            for (int i = 0; i < region_count; ++i)
+                sources[size_t(i)] = {regions[i].source, span_end(regions[i], regions[i].source)};
+            std::sort(sources.begin(), sources.end());
+            std::vector<uint64_t> reach(sources.size());  // max end over sources[0..i]
+            for (size_t i = 0; i < sources.size(); ++i)
+                reach[i] = std::max(sources[i].second, i ? reach[i - 1] : 0);
+            for (int i = 0; i < region_count && !two_phase; ++i) {
+                const uint64_t d0 = regions[i].destination, d1 = span_end(regions[i], d0);
+                // sources starting before d1; overlap when one of them ends after d0
+                const size_t n = size_t(std::lower_bound(sources.begin(), sources.end(), std::make_pair(d1, uint64_t(0))) -
+                                        sources.begin());
+                two_phase = n > 0 && reach[n - 1] > d0;
+            }
         }
         if (!c->finalized) fail(MP_ERR_INVALID, "weights not finalized");
         const auto& r = c->rt;
@@ -916,6 +948,7 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         c->off_order = c->off_prefix + 8 * X;
         c->off_entries = c->off_order + W;
         c->off_regions = (c->off_entries + 2 * size_t(entry_count) + 1) & ~size_t(1);  // 8-byte aligned
+        c->off_scratch = c->off_regions + 10 * size_t(region_count);                   // uint64 per region
         std::memcpy(h + c->off_tokens, tokens, size_t(T) * 4);
         int row = 0;
         for (int i = 0; i < count; ++i) {
@@ -943,7 +976,21 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         }
         if (region_count)
             std::memcpy(h + c->off_regions, regions, size_t(region_count) * sizeof(mp_tail_copy_region));
-        const size_t bytes = (c->off_regions + 10 * size_t(region_count)) * 4;
+        if (two_phase) {
+            if (region_elements > c->cow_scratch_capacity) {
+                if (c->cow_scratch) cudaFree(c->cow_scratch);
+                c->cow_scratch = nullptr;
+                c->cow_scratch_capacity = 0;
+                c->cow_scratch = device_alloc<float>(2 * size_t(region_elements), "COW gather scratch");
+                c->cow_scratch_capacity = region_elements;
+            }
+            uint64_t at = 0;
+            for (int i = 0; i < region_count; ++i) {
+                std::memcpy(h + c->off_scratch + 2 * size_t(i), &at, sizeof(at));
+                at += regions[i].rows * regions[i].width;
+            }
+        }
+        const size_t bytes = (c->off_scratch + (two_phase ? 2 * size_t(region_count) : 0)) * 4;
         cuda_check(cudaMemcpyAsync(c->meta, h, bytes, cudaMemcpyHostToDevice, c->stream), "upload step metadata");
         c->step_h2d = bytes;
         c->rows = T;
@@ -965,6 +1012,8 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         c->entry_count = entry_count;
         c->region_count = region_count;
         c->region_rows = region_rows;
+        c->cow_two_phase = two_phase;
+        c->cow_scratch_elements = region_elements;
         c->prepared = true;
         mirror_guard.keep = true;
     });
@@ -984,7 +1033,8 @@ int mp_forward_launch(mp_context* c) {
         // kernels of this forward: embed; per layer qkv, rope/append, o, norm, gate/up,
         // down (+1 input norm after layer 0, +1 per attention kind present); final
         // norm, head, argmax; table patch / COW if any
-        c->step_launches = uint64_t(c->entry_count > 0) + uint64_t(c->region_count > 0 && c->region_rows > 0) + 1 +
+        c->step_launches = uint64_t(c->entry_count > 0) +
+                           uint64_t(c->region_count > 0 && c->region_rows > 0) * (c->cow_two_phase ? 2 : 1) + 1 +
                            uint64_t(m.layers) * (6 + uint64_t(c->prefill_count > 0) + uint64_t(c->work_count > 0) +
                                                  uint64_t(c->prefix_count > 0)) +
                            uint64_t(m.layers - 1) + 3;
@@ -993,10 +1043,22 @@ int mp_forward_launch(mp_context* c) {
                    "table patch launch");
         c->cow_timed = c->cow_timing && c->region_count > 0;
         if (c->cow_timed) cuda_check(cudaEventRecord(c->cow_events[0], st), "cow timing");
-        cuda_check(mpb::launch_cow_copy(reinterpret_cast<const mpb::CowRegion*>(meta + c->off_regions),
-                                        c->region_count, c->region_rows, c->keys, c->values, c->pool_elements,
-                                        c->error, st),
-                   "cow launch");
+        const auto* regions = reinterpret_cast<const mpb::CowRegion*>(meta + c->off_regions);
+        if (c->cow_two_phase) {
+            const auto* at = reinterpret_cast<const uint64_t*>(meta + c->off_scratch);
+            cuda_check(mpb::launch_cow_copy(regions, c->region_count, c->region_rows, c->keys, c->values,
+                                            c->pool_elements, c->error, st, mpb::kCowGather, at, c->cow_scratch,
+                                            c->cow_scratch_elements),
+                       "cow gather launch");
+            cuda_check(mpb::launch_cow_copy(regions, c->region_count, c->region_rows, c->keys, c->values,
+                                            c->pool_elements, c->error, st, mpb::kCowScatter, at, c->cow_scratch,
+                                            c->cow_scratch_elements),
+                       "cow scatter launch");
+        } else {
+            cuda_check(mpb::launch_cow_copy(regions, c->region_count, c->region_rows, c->keys, c->values,
+                                            c->pool_elements, c->error, st),
+                       "cow launch");
+        }
         if (c->cow_timed) cuda_check(cudaEventRecord(c->cow_events[1], st), "cow timing");
         cuda_check(mpb::launch_embed_rmsnorm(meta + c->off_tokens, c->embed, m.vocabulary, c->in_norm, m.rms_epsilon,
                                              c->x, c->xn.hi, c->xn.lo, T, H, c->error, st),

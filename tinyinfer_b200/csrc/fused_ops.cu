@@ -178,22 +178,41 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int v
 }
 
 // grid (count, max_rows): one CTA per (region, layer row), float4 copies of
-// `width` floats in both pools. Offsets are validated against the pool size.
+// `width` floats in both pools (or between the pools and the gather scratch).
+// Offsets are validated against the pool and scratch sizes.
 __global__ void cow_copy_kernel(const CowRegion* regions, float* keys, float* values, uint64_t pool_elements,
-                                unsigned* error) {
+                                unsigned* error, int mode, const uint64_t* scratch_offset, float* scratch,
+                                uint64_t scratch_elements) {
     pdl_enter();  // before any global memory access
     const CowRegion r = regions[blockIdx.x];
     const uint64_t row = blockIdx.y;
     if (row >= r.rows) return;
     const uint64_t dst = r.destination + row * r.pitch, src = r.source + row * r.pitch;
-    if (dst + r.width > pool_elements || src + r.width > pool_elements || (r.width | dst | src) & 3) {
+    const uint64_t at = mode == kCowDirect ? 0 : scratch_offset[blockIdx.x] + row * r.width;
+    bool ok = !((r.width | dst | src | at) & 3);
+    if (mode != kCowScatter) ok = ok && src + r.width <= pool_elements;
+    if (mode != kCowGather) ok = ok && dst + r.width <= pool_elements;
+    if (mode != kCowDirect) ok = ok && at + r.width <= scratch_elements && !(scratch_elements & 3);
+    if (!ok) {
         if (threadIdx.x == 0) raise_error(error, kErrBounds);
         return;
     }
-    const float4* ks = reinterpret_cast<const float4*>(keys + src);
-    const float4* vs = reinterpret_cast<const float4*>(values + src);
-    float4* kd = reinterpret_cast<float4*>(keys + dst);
-    float4* vd = reinterpret_cast<float4*>(values + dst);
+    const float4 *ks, *vs;
+    float4 *kd, *vd;
+    if (mode == kCowScatter) {
+        ks = reinterpret_cast<const float4*>(scratch + at);
+        vs = reinterpret_cast<const float4*>(scratch + scratch_elements + at);
+    } else {
+        ks = reinterpret_cast<const float4*>(keys + src);
+        vs = reinterpret_cast<const float4*>(values + src);
+    }
+    if (mode == kCowGather) {
+        kd = reinterpret_cast<float4*>(scratch + at);
+        vd = reinterpret_cast<float4*>(scratch + scratch_elements + at);
+    } else {
+        kd = reinterpret_cast<float4*>(keys + dst);
+        vd = reinterpret_cast<float4*>(values + dst);
+    }
     for (uint64_t i = threadIdx.x; i < r.width / 4; i += blockDim.x) {
         kd[i] = ks[i];
         vd[i] = vs[i];
@@ -242,10 +261,12 @@ cudaError_t launch_argmax(const float* logits, int rows, int vocabulary, int32_t
 }
 
 cudaError_t launch_cow_copy(const CowRegion* regions, int count, int max_rows, float* keys, float* values,
-                            uint64_t pool_elements, unsigned* error, cudaStream_t stream) {
+                            uint64_t pool_elements, unsigned* error, cudaStream_t stream, CowMode mode,
+                            const uint64_t* scratch_offset, float* scratch, uint64_t scratch_elements) {
     if (count <= 0 || max_rows <= 0) return cudaSuccess;
+    if (mode != kCowDirect && (!scratch_offset || !scratch)) return cudaErrorInvalidValue;
     return launch_pdl(cow_copy_kernel, dim3(count, max_rows), dim3(256), 0, stream, regions, keys, values,
-                      pool_elements, error);
+                      pool_elements, error, int(mode), scratch_offset, scratch, scratch_elements);
 }
 
 cudaError_t launch_table_patch(const int32_t* pairs, int count, int32_t* tables, int64_t table_elements,

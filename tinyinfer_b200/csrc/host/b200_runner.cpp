@@ -45,6 +45,8 @@ B200Runner::B200Runner(const ModelConfig& config, int context, KvCacheConfig kv,
     for (int s = options.max_sequences - 1; s >= 0; --s) free_slots_.push_back(s);
     mirror_.assign(std::size_t(options.max_sequences), {});
     written_epoch_.assign(std::size_t(kv.max_blocks), 0);
+    read_epoch_.assign(std::size_t(kv.max_blocks), 0);
+    pending_epoch_.assign(std::size_t(options.max_sequences), 0);
     const std::size_t kvw = std::size_t(config.kv_width());
     stats_.device_workspace_bytes =
         std::size_t(options.max_step_tokens) *
@@ -100,7 +102,15 @@ void B200Runner::fork_sequence(const RequestId& source, const RequestId& target)
     mirror_[std::size_t(slot_of(target))].clear();  // uploaded with the next append
 }
 
+void B200Runner::mark_pending_reads(const RequestId& id) {
+    if (descs_.empty() || !kv_.contains(id)) return;
+    const auto it = slots_.find(id);
+    if (it == slots_.end() || pending_epoch_[std::size_t(it->second)] != epoch_) return;
+    for (int b : kv_.sequence(id).blocks) read_epoch_[std::size_t(b)] = epoch_;
+}
+
 std::size_t B200Runner::reuse_prefix(const RequestId& id, const std::vector<TokenId>& prompt) {
+    mark_pending_reads(id);
     const std::size_t used = kv_.reuse_prefix(id, prompt);
     mirror_[std::size_t(slot_of(id))].clear();  // the table goes up with the next append
     return used;
@@ -187,10 +197,22 @@ std::size_t B200Runner::stage_append(const RequestId& id, const std::vector<Toke
             flush();
     }
     if (!replay_ && !descs_.empty()) {
-        bool hazard = copy && written_epoch_[std::size_t(copy->source)] == epoch_;
-        if (copy && kv_.freed_this_epoch(copy->destination)) hazard = true;
+        // The device applies a step as: every COW source read, then every COW
+        // destination written, then per layer every new K/V row written before any
+        // attention reads. Sequential order differs from that only when (1) a COW
+        // source was written by an earlier pending append, (2) this append writes a
+        // page (COW destination or new page) that an earlier pending append's
+        // attention still reads -- a page freed this step by that sequence -- or
+        // (3) the sequence already has a pending append. A page freed this step that
+        // pending work only read as a COW source is safe to reuse.
+        auto reused = [&](int b) {
+            return kv_.freed_this_epoch(b) && read_epoch_[std::size_t(b)] == epoch_;
+        };
+        bool hazard = pending_epoch_[std::size_t(slot)] == epoch_;
+        if (copy && written_epoch_[std::size_t(copy->source)] == epoch_) hazard = true;
+        if (copy && reused(copy->destination)) hazard = true;
         for (std::size_t b = tx.original_blocks(); b < sequence.blocks.size() && !hazard; ++b)
-            hazard = kv_.freed_this_epoch(sequence.blocks[b]);
+            hazard = reused(sequence.blocks[b]);
         if (hazard) {
             ++hazard_flushes_;
             flush();
@@ -212,6 +234,7 @@ std::size_t B200Runner::stage_append(const RequestId& id, const std::vector<Toke
     const int bt = kv_.config().block_tokens;
     for (int p = sequence.used / bt; p <= (sequence.used + int(tokens.size()) - 1) / bt; ++p)
         written_epoch_[std::size_t(sequence.blocks[std::size_t(p)])] = epoch_;
+    pending_epoch_[std::size_t(slot)] = epoch_;
     descs_.push_back({slot, sequence.used, int32_t(tokens.size())});
     tokens_.insert(tokens_.end(), tokens.begin(), tokens.end());
     tickets_.push_back(ticket);
@@ -313,6 +336,7 @@ void B200Runner::end_batch() {
 }
 
 void B200Runner::release(const RequestId& id) {
+    mark_pending_reads(id);
     kv_.release(id);
     free_slot(id);
 }

@@ -77,6 +77,7 @@ private:
     int slot_of(const RequestId& id) const;
     void table_entries(int slot, const PagedSequence& sequence, std::vector<mp_table_entry>& out);
     void free_slot(const RequestId& id);
+    void mark_pending_reads(const RequestId& id);  // before a pending sequence drops its pages
     void drain() noexcept;  // best-effort completion of queued device work
 
     ModelConfig config_;
@@ -93,6 +94,10 @@ private:
     std::vector<int> quarantine_;              // freed while device work may still read them
     std::vector<std::vector<int>> mirror_;     // device-known table of each slot
     std::vector<std::uint32_t> written_epoch_; // page -> epoch in which pending work writes it
+    // page -> epoch in which it left a sequence whose pending append's attention
+    // reads it (set when such a sequence is released or its table is replaced)
+    std::vector<std::uint32_t> read_epoch_;
+    std::vector<std::uint32_t> pending_epoch_; // slot -> epoch of its pending append
 
     // pending device work
     std::vector<mp_sequence_desc> descs_;

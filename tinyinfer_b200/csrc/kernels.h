@@ -223,8 +223,16 @@ cudaError_t launch_argmax(const float* logits, int rows, int vocabulary, int32_t
 struct CowRegion {
     uint64_t destination, source, pitch, width, rows;
 };
+// COW copies of `count` regions, both pools, all rows. kCowDirect copies source
+// to destination; a two-phase step first gathers every source into `scratch`
+// (kCowGather: region i's rows at scratch_offset[i], keys in the first
+// scratch_elements floats, values in the next) and then scatters it
+// (kCowScatter), so that every source is read before any destination is written.
+enum CowMode : int { kCowDirect = 0, kCowGather = 1, kCowScatter = 2 };
 cudaError_t launch_cow_copy(const CowRegion* regions, int count, int max_rows, float* keys, float* values,
-                            uint64_t pool_elements, unsigned* error, cudaStream_t stream);
+                            uint64_t pool_elements, unsigned* error, cudaStream_t stream, CowMode mode = kCowDirect,
+                            const uint64_t* scratch_offset = nullptr, float* scratch = nullptr,
+                            uint64_t scratch_elements = 0);
 // tables[index[i]] = value[i]
 cudaError_t launch_table_patch(const int32_t* pairs, int count, int32_t* tables, int64_t table_elements,
                                unsigned* error, cudaStream_t stream);
