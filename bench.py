@@ -371,7 +371,10 @@ def run_b200(args, rank, world, local_rank):
         "e2e": {"value": tokens_all / (e2e_ms * 1e-3), "unit": "tok/s",
                 "h2d_bytes_per_step": counters["h2d_bytes"] / max(counters["forwards"], 1),
                 "d2h_bytes_per_step": counters["d2h_bytes"] / max(counters["forwards"], 1),
-                "ms_per_step": e2e_ms / args.steps},
+                "ms_per_step": e2e_ms / args.steps,
+                # host wall time per step inside the C ABI (rank 0); the rest of
+                # e2e - device is engine bookkeeping (schedule, KV manager, publish)
+                "host_ms_per_step": {k: counters[f"host_{k}_ms"] / args.steps for k in ("prepare", "launch", "wait")}},
         "gpu_launches": int(counters["kernel_launches"]),
         "roofline": {"bound": "hbm",
                      "kernel": "decode attention: prefix_attention_kernel (shared pages, tcgen05) + "

@@ -179,7 +179,7 @@ def run_config5(args, rank, world, local_rank):
     pool = _pool_pages(0.6, cfg.layers, bt, local_rank)
     weights = random_weights(cfg, seed=0)
     runner = Runner.b200(cfg, weights, context=context, block_tokens=bt, max_blocks=pool,
-                         prefix_blocks=min(pool // 4, 16384), device=local_rank, max_sequences=batch + 8,
+                         prefix_blocks=pool // 2, device=local_rank, max_sequences=batch + 8,
                          max_step_tokens=budget, max_step_sequences=batch + 8)
     del weights
     engine = Engine(runner, batch, budget, chunk, context)
@@ -213,6 +213,7 @@ def run_config5(args, rank, world, local_rank):
               "model": f"SmolLM2-135M shape, {cfg.layers} layers, FP32, tied head", "requests": count,
               "requests_served": int(served), "output_tokens": int(outputs), "prefill_tokens": int(prefill),
               "prefix_reused_tokens": int(reused), "steps": r["steps"], "kv_pool_pages_per_gpu": pool,
+              "prefix_cache_blocks_per_gpu": pool // 2,
               "routing": "by prefix-tree root (roots dealt round-robin over GPUs); no collective while serving",
               "scaling": "strong", "parallelism": f"request-sharded replicas x{world}"}
     return _line(args, "served output tok/s (BASELINE config 5)", outputs / (device_ms * 1e-3), "tok/s", world,

@@ -145,13 +145,17 @@ int mp_profile_read(mp_context* ctx, float* attention_ms, int32_t* attention_lau
  * launched, and bytes moved host->device / device->host by the forwards;
  * shared_prefix_rows counts decode rows whose leading pages were served by the
  * shared-prefix kernel (once per forward), shared_prefix_tokens the tokens those
- * rows did not read themselves. */
+ * rows did not read themselves. host_prepare_ms, host_launch_ms and host_wait_ms
+ * are host wall time spent in mp_forward_prepare (validation, attention plan,
+ * metadata upload), mp_forward_launch (enqueueing the kernels) and waiting for
+ * completion in mp_forward_collect. */
 typedef struct {
     uint64_t forwards;
     double forward_ms;
     uint64_t kernel_launches;
     uint64_t h2d_bytes, d2h_bytes;
     uint64_t shared_prefix_rows, shared_prefix_tokens;
+    double host_prepare_ms, host_launch_ms, host_wait_ms;
 } mp_counters;
 int mp_read_counters(mp_context* ctx, mp_counters* out, int32_t reset);
 

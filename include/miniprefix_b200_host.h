@@ -46,6 +46,10 @@ int mph_cache_publish(mph_cache* c, const char* seq);
 long mph_cache_reuse(mph_cache* c, const char* seq, const int32_t* prompt, int32_t count);
 int mph_cache_release(mph_cache* c, const char* seq);
 int mph_cache_evict_one(mph_cache* c); /* 1 evicted, 0 nothing to evict */
+/* Undo window over pool, index and sequences (the batched engine's step
+ * checkpoint): op 0 opens it, 1 rolls everything back to the opening state, 2
+ * keeps the changes and closes it. */
+int mph_cache_journal(mph_cache* c, int32_t op);
 int mph_cache_clear(mph_cache* c);
 /* size, index_nodes, key_token_bytes, hits, misses, reused_tokens, evictions,
  * cache_only_blocks, live_blocks, peak_blocks, free_blocks */

@@ -187,3 +187,79 @@ def test_pool_free_list_order(built, ref):
         impl.append("c", [1] * 6)
         assert impl.sequence("c")[1] == [1, 4]
         assert impl.stats()["live_blocks"] == 5
+
+
+@pytest.mark.parametrize("capacity", [3, 12, 64])
+def test_undo_window_restores_exact_state(built, ref, capacity):
+    """The batched engine's step checkpoint: operations inside an undo window that
+    is rolled back leave no trace (the reference cache never sees them and every
+    later result, counter, LRU decision and page reference still agrees); a window
+    that is kept equals the reference applying the same operations. Sequences grow
+    and republish, so publish() runs on its path hints, stale ones included."""
+    a, b = both(ref, 4, 256, capacity)
+    rng = np.random.default_rng(91 + capacity)
+    live = []
+    counter = [0]
+
+    def random_ops(n):
+        ops, names = [], list(live)
+        for _ in range(n):
+            k = int(rng.integers(0, 10))
+            if k < 4 and names:
+                s = names[int(rng.integers(0, len(names)))]
+                ops.append(("append", s, [int(t) for t in rng.integers(0, 3, size=int(rng.integers(1, 9)))]))
+            elif k < 6 and names:
+                ops.append(("publish", names[int(rng.integers(0, len(names)))]))
+            elif k < 8 or not names:
+                counter[0] += 1
+                prompt = [int(t) for t in rng.integers(0, 3, size=int(rng.integers(1, 30)))]
+                ops.append(("reuse", f"s{counter[0]}", prompt))
+                names.append(f"s{counter[0]}")
+            elif k < 9:
+                ops.append(("release", names.pop(int(rng.integers(0, len(names))))))
+            else:
+                ops.append(("evict",))
+        return ops
+
+    def apply(c, ops, names):
+        out = []
+        for op in ops:
+            if op[0] == "append":
+                c.append(op[1], op[2])
+                c.publish(op[1])
+            elif op[0] == "publish":
+                c.publish(op[1])
+            elif op[0] == "reuse":
+                out.append(c.reuse(op[1], op[2]))
+                names.append(op[1])
+            elif op[0] == "release":
+                c.release(op[1])
+                names.remove(op[1])
+            else:
+                out.append(c.evict_one())
+        return out
+
+    for window in range(150):
+        before = list(live)
+        ops = random_ops(int(rng.integers(1, 12)))
+        a.journal("begin")
+        names_a = list(live)
+        out_a = apply(a, ops, names_a)
+        if rng.random() < 0.5:
+            a.journal("rollback")
+            live[:] = before
+        else:
+            a.journal("end")
+            names_b = list(live)
+            assert apply(b, ops, names_b) == out_a
+            assert names_a == names_b
+            live[:] = names_b
+        same_state(a, b, 256)
+        for s in live:
+            assert a.sequence(s) == b.sequence(s), s
+    for s in list(live):
+        a.release(s)
+        b.release(s)
+    a.clear()
+    b.clear()
+    same_state(a, b, 256)

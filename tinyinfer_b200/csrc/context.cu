@@ -445,16 +445,29 @@ void free_context(mp_context* c) {
     delete c;
 }
 
+// Adds the wall time of its scope to `sink` (milliseconds).
+struct HostTimer {
+    double& sink;
+    std::chrono::steady_clock::time_point start = std::chrono::steady_clock::now();
+    explicit HostTimer(double& s) : sink(s) {}
+    ~HostTimer() {
+        sink += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - start).count();
+    }
+};
+
+// Polls `e` (yielding for the first 2 ms, then sleeping 20 us between polls)
+// until it completes or `timeout_ms` elapses.
 void wait_event(cudaEvent_t e, int timeout_ms) {
     const auto start = std::chrono::steady_clock::now();
     for (;;) {
         const cudaError_t s = cudaEventQuery(e);
         if (s == cudaSuccess) return;
         if (s != cudaErrorNotReady) cuda_check(s, "step completion");
-        if (timeout_ms >= 0 &&
-            std::chrono::steady_clock::now() - start > std::chrono::milliseconds(timeout_ms))
+        const auto waited = std::chrono::steady_clock::now() - start;
+        if (timeout_ms >= 0 && waited > std::chrono::milliseconds(timeout_ms))
             fail(MP_ERR_TIMEOUT, "device work did not complete within the timeout");
-        std::this_thread::sleep_for(std::chrono::microseconds(20));
+        if (waited < std::chrono::milliseconds(2)) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
 }
 
@@ -843,6 +856,7 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
     return guarded([&] {
         if (!c || !seqs || !tokens || (entry_count > 0 && !entries) || (region_count > 0 && !regions))
             fail(MP_ERR_INVALID, "null argument");
+        HostTimer host_time(c->counters_total.host_prepare_ms);
         if (entry_count < 0 || size_t(entry_count) > c->entry_capacity) fail(MP_ERR_INVALID, "too many table entries");
         if (region_count < 0 || size_t(region_count) > c->region_capacity) fail(MP_ERR_INVALID, "too many COW regions");
         for (int i = 0; i < entry_count; ++i) {
@@ -1022,6 +1036,7 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
 int mp_forward_launch(mp_context* c) {
     return guarded([&] {
         if (!c || !c->prepared) fail(MP_ERR_INVALID, "no prepared step");
+        HostTimer host_time(c->counters_total.host_launch_ms);
         cuda_check(cudaSetDevice(c->device), "select device");
         const auto& m = c->model;
         const auto& r = c->rt;
@@ -1217,7 +1232,10 @@ int mp_forward_collect(mp_context* c, int32_t* out_tokens, int32_t* out_finite, 
                                        cudaMemcpyDeviceToHost, st),
                        "download logits");
         cuda_check(cudaEventRecord(c->done, st), "record completion");
-        wait_event(c->done, timeout_ms);
+        {
+            HostTimer host_time(c->counters_total.host_wait_ms);
+            wait_event(c->done, timeout_ms);
+        }
         if (c->profile) harvest_profile(c);
         {
             float ms = 0.f;

@@ -63,6 +63,11 @@ struct mph_cache {
     KvBlockPool pool;
     ExactPrefixCache cache;
     std::map<std::string, PagedSequence> sequences;
+    // an open undo window (mph_cache_journal)
+    std::vector<KvBlockPool::JournalEntry> journal;
+    std::size_t live = 0, peak = 0;
+    std::map<std::string, PagedSequence> saved;
+    bool journaling = false;
     mph_cache(KvCacheConfig c, int layers, int width) : pool(c, layers, width), cache(pool) {}
     ~mph_cache() {
         for (auto& s : sequences) pool.release(s.second);
@@ -135,6 +140,35 @@ int mph_cache_evict_one(mph_cache* c) {
 int mph_cache_clear(mph_cache* c) {
     c->cache.clear();
     return 0;
+}
+int mph_cache_journal(mph_cache* c, int32_t op) {
+    return int(guarded([&] {
+        if (op == 0) {
+            if (c->journaling) throw std::logic_error("undo window already open");
+            c->journal.clear();
+            c->live = c->pool.live_blocks();
+            c->peak = c->pool.peak_blocks();
+            c->saved = c->sequences;
+            c->pool.attach_journal(&c->journal);
+            c->cache.begin_journal();
+            c->journaling = true;
+        } else if (op == 1 || op == 2) {
+            if (!c->journaling) throw std::logic_error("no undo window");
+            c->pool.attach_journal(nullptr);
+            if (op == 1) {
+                c->pool.undo(c->journal, 0, c->live, c->peak);
+                c->cache.rollback_journal();
+                c->sequences = std::move(c->saved);
+            } else {
+                c->cache.end_journal();
+            }
+            c->saved.clear();
+            c->journaling = false;
+        } else {
+            throw std::invalid_argument("unknown journal operation");
+        }
+        return 0L;
+    }));
 }
 int mph_cache_stats(mph_cache* c, uint64_t* out) {
     const uint64_t v[11] = {c->cache.size(),          c->cache.index_nodes(), c->cache.key_token_bytes(),

@@ -318,7 +318,7 @@ void KVManager::begin_checkpoint() {
     checkpoint_ = std::make_unique<Checkpoint>();
     checkpoint_->live = pool_.live_blocks();
     checkpoint_->peak = pool_.peak_blocks();
-    checkpoint_->prefix = prefix_.snapshot();
+    prefix_.begin_journal();
     checkpoint_->reserved_pages = reserved_pages_;
     checkpoint_->forward_tokens = forward_tokens_;
     checkpoint_->costs = costs_;
@@ -330,7 +330,7 @@ void KVManager::restore_checkpoint() {
     auto& cp = *checkpoint_;
     pool_.attach_journal(nullptr);
     pool_.undo(cp.pool_journal, 0, cp.live, cp.peak);
-    prefix_.restore(cp.prefix);
+    prefix_.rollback_journal();
     for (auto& [id, saved] : cp.sequences) {
         if (!saved.existed) {
             sequences_.erase(id);
@@ -356,6 +356,7 @@ void KVManager::restore_checkpoint() {
 
 void KVManager::end_checkpoint() {
     pool_.attach_journal(nullptr);
+    prefix_.end_journal();
     checkpoint_.reset();
 }
 

@@ -137,7 +137,6 @@ private:
     struct Checkpoint {
         std::vector<KvBlockPool::JournalEntry> pool_journal;
         std::size_t live = 0, peak = 0;
-        ExactPrefixCache::Snapshot prefix;
         std::map<RequestId, SavedSequence> sequences;
         std::map<RequestId, std::optional<std::size_t>> reservations;  // nullopt: did not exist
         std::size_t reserved_pages = 0, forward_tokens = 0;

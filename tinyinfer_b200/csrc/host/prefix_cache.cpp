@@ -16,20 +16,30 @@ std::size_t ExactPrefixCache::cache_only_blocks() const {
     return count;
 }
 
+void ExactPrefixCache::lease_add(int page, int delta) {
+    log(Op::Lease, page, delta);
+    auto lease = s_.leases.find(page);
+    if (lease == s_.leases.end()) lease = s_.leases.emplace(page, 0u).first;
+    lease->second = std::uint32_t(int(lease->second) + delta);
+    if (lease->second == 0) s_.leases.erase(lease);
+}
+
 int ExactPrefixCache::new_node(int parent, View edge) {
     int id;
-    if (!s_.spare.empty()) {
+    const bool spare = !s_.spare.empty();
+    if (spare) {
         id = s_.spare.back();
         s_.spare.pop_back();
     } else {
         id = int(s_.nodes.size());
         s_.nodes.emplace_back();
     }
+    log(Op::NewNode, id, parent, spare ? 1 : 0);
     Node& n = s_.nodes[std::size_t(id)];
     n.parent = parent;
     n.edge.assign(edge.p, edge.p + edge.n);
     n.block = -1;
-    n.older = n.newer = -1;
+    n.stamp = 0;
     n.children.clear();
     n.leased.clear();
     s_.nodes[std::size_t(parent)].children.emplace(n.edge, id);
@@ -38,27 +48,41 @@ int ExactPrefixCache::new_node(int parent, View edge) {
     return id;
 }
 
-void ExactPrefixCache::lru_unlink(int id) noexcept {
+void ExactPrefixCache::touch(int id) {
     Node& n = s_.nodes[std::size_t(id)];
-    if (n.older >= 0) s_.nodes[std::size_t(n.older)].newer = n.newer;
-    else s_.oldest = n.newer;
-    if (n.newer >= 0) s_.nodes[std::size_t(n.newer)].older = n.older;
-    else s_.newest = n.older;
-    n.older = n.newer = -1;
+    log(Op::Stamp, id, 0, n.stamp);
+    n.stamp = ++s_.clock;
+    s_.lru.emplace_back(n.stamp, id);
+    if (!journaling_ && s_.lru.size() - s_.lru_head > 4 * s_.cached + 65536) compact_lru();
 }
 
-void ExactPrefixCache::lru_append(int id) noexcept {
+void ExactPrefixCache::unstamp(int id) noexcept {
     Node& n = s_.nodes[std::size_t(id)];
-    n.older = s_.newest;
-    n.newer = -1;
-    if (s_.newest >= 0) s_.nodes[std::size_t(s_.newest)].newer = id;
-    else s_.oldest = id;
-    s_.newest = id;
+    log(Op::Stamp, id, 0, n.stamp);
+    n.stamp = 0;
 }
 
-void ExactPrefixCache::touch(int id) noexcept {
-    lru_unlink(id);
-    lru_append(id);
+int ExactPrefixCache::lru_front() noexcept {
+    while (s_.lru_head < s_.lru.size()) {
+        const auto [stamp, id] = s_.lru[s_.lru_head];
+        const Node& n = s_.nodes[std::size_t(id)];
+        if (n.stamp == stamp && n.block >= 0) return id;
+        ++s_.lru_head;
+    }
+    return -1;
+}
+
+// Keeps only the current entries (in order). Never inside an undo window: a
+// rollback returns to a prefix of the list as it was when the window opened.
+void ExactPrefixCache::compact_lru() {
+    std::size_t out = 0;
+    for (std::size_t i = s_.lru_head; i < s_.lru.size(); ++i) {
+        const auto& e = s_.lru[i];
+        const Node& n = s_.nodes[std::size_t(e.second)];
+        if (n.stamp == e.first && n.block >= 0) s_.lru[out++] = e;
+    }
+    s_.lru.resize(out);
+    s_.lru_head = 0;
 }
 
 // Erase empty structural leaves from `id` upward, never the root or `keep`.
@@ -69,6 +93,10 @@ void ExactPrefixCache::prune(int id, int keep) noexcept {
         const int parent = n.parent;
         s_.key_tokens -= n.edge.size();
         s_.nodes[std::size_t(parent)].children.erase(n.edge);
+        if (journaling_) {
+            log(Op::Prune, id, parent);
+            pruned_edges_.push_back(std::move(n.edge));
+        }
         n.edge.clear();
         n.parent = -1;
         --s_.live_nodes;
@@ -80,19 +108,21 @@ void ExactPrefixCache::prune(int id, int keep) noexcept {
 void ExactPrefixCache::drop(int id, int keep) noexcept {
     Node& n = s_.nodes[std::size_t(id)];
     s_.nodes[std::size_t(n.parent)].leased.erase(n.edge);
+    log(Op::LeasedDrop, n.parent, id);
     const int block = n.block;
-    auto lease = s_.leases.find(block);
-    if (--lease->second == 0) s_.leases.erase(lease);
-    lru_unlink(id);
+    lease_add(block, -1);
+    unstamp(id);
     pool_.unref(block);
+    log(Op::Block, id, block);
     n.block = -1;
     --s_.cached;
     prune(id, keep);
 }
 
 bool ExactPrefixCache::evict_one() {
-    if (s_.oldest < 0) return false;
-    drop(s_.oldest, -1);
+    const int victim = lru_front();
+    if (victim < 0) return false;
+    drop(victim, -1);
     ++s_.evictions;
     return true;
 }
@@ -165,11 +195,23 @@ void ExactPrefixCache::publish(const PagedSequence& sequence) {
     const std::size_t used = std::size_t(sequence.used);
     const std::size_t capacity = std::size_t(pool_.config().prefix_cache_blocks);
     const std::size_t count = std::min(sequence.blocks.size(), std::min((used + bt - 1) / bt, capacity));
+    auto& path = sequence.prefix_path;
+    if (path.size() > count) path.resize(count);
     int parent = 0;
     for (std::size_t i = 0; i < count; ++i) {
         const View key{sequence.tokens.data() + i * bt, std::min(bt, used - i * bt)};
-        int id;
-        {
+        int id = -1;
+        if (i < path.size()) {
+            // the hinted node is the child of `parent` under `key` iff it is live
+            // under that parent with that edge (edges are unique among siblings)
+            const int h = path[i];
+            if (h > 0 && std::size_t(h) < s_.nodes.size()) {
+                const Node& n = s_.nodes[std::size_t(h)];
+                if (n.parent == parent && n.edge.size() == key.n && std::equal(key.p, key.p + key.n, n.edge.begin()))
+                    id = h;
+            }
+        }
+        if (id < 0) {
             const auto& ch = s_.nodes[std::size_t(parent)].children;
             const auto it = ch.find(key);
             id = it != ch.end() ? it->second : new_node(parent, key);
@@ -179,28 +221,101 @@ void ExactPrefixCache::publish(const PagedSequence& sequence) {
         } else {
             const int page = sequence.blocks[i];
             s_.nodes[std::size_t(parent)].leased.emplace(s_.nodes[std::size_t(id)].edge, id);
+            log(Op::LeasedAdd, parent, id);
             try {
                 pool_.retain(page);
             } catch (...) {
                 s_.nodes[std::size_t(parent)].leased.erase(s_.nodes[std::size_t(id)].edge);
+                log(Op::LeasedDrop, parent, id);
                 prune(id, -1);
                 throw;
             }
             if (s_.cached == capacity) {
-                drop(s_.oldest, id);
+                drop(lru_front(), id);
                 ++s_.evictions;
             }
-            ++s_.leases[page];
+            lease_add(page, +1);
+            log(Op::Block, id, s_.nodes[std::size_t(id)].block);
             s_.nodes[std::size_t(id)].block = page;
-            lru_append(id);
+            touch(id);
             ++s_.cached;
         }
+        if (i < path.size()) path[i] = id;
+        else path.push_back(id);
         parent = id;
     }
 }
 
-ExactPrefixCache::Snapshot ExactPrefixCache::snapshot() const { return s_; }
+void ExactPrefixCache::begin_journal() {
+    if (s_.lru.size() - s_.lru_head > 4 * s_.cached + 65536) compact_lru();
+    journal_.clear();
+    pruned_edges_.clear();
+    saved_.counters = s_;
+    saved_.lru_size = s_.lru.size();
+    saved_.lru_head = s_.lru_head;
+    saved_.clock = s_.clock;
+    journaling_ = true;
+}
 
-void ExactPrefixCache::restore(const Snapshot& snapshot) { s_ = snapshot; }
+void ExactPrefixCache::end_journal() noexcept {
+    journaling_ = false;
+    journal_.clear();
+    pruned_edges_.clear();
+}
+
+void ExactPrefixCache::rollback_journal() noexcept {
+    journaling_ = false;
+    for (auto e = journal_.rbegin(); e != journal_.rend(); ++e) {
+        switch (e->op) {
+        case Op::NewNode: {
+            Node& n = s_.nodes[std::size_t(e->a)];
+            s_.nodes[std::size_t(e->b)].children.erase(n.edge);
+            n.edge.clear();
+            n.parent = -1;
+            n.block = -1;
+            n.stamp = 0;
+            n.children.clear();
+            n.leased.clear();
+            if (e->v) s_.spare.push_back(e->a);
+            else s_.nodes.pop_back();
+            break;
+        }
+        case Op::Prune: {
+            s_.spare.pop_back();
+            Node& n = s_.nodes[std::size_t(e->a)];
+            n.edge = std::move(pruned_edges_.back());
+            pruned_edges_.pop_back();
+            n.parent = e->b;
+            s_.nodes[std::size_t(e->b)].children.emplace(n.edge, e->a);
+            break;
+        }
+        case Op::LeasedAdd:
+            s_.nodes[std::size_t(e->a)].leased.erase(s_.nodes[std::size_t(e->b)].edge);
+            break;
+        case Op::LeasedDrop:
+            s_.nodes[std::size_t(e->a)].leased.emplace(s_.nodes[std::size_t(e->b)].edge, e->b);
+            break;
+        case Op::Stamp:
+            s_.nodes[std::size_t(e->a)].stamp = e->v;
+            break;
+        case Op::Block:
+            s_.nodes[std::size_t(e->a)].block = e->b;
+            break;
+        case Op::Lease: {
+            auto lease = s_.leases.find(e->a);
+            if (lease == s_.leases.end()) lease = s_.leases.emplace(e->a, 0u).first;
+            lease->second = std::uint32_t(int(lease->second) - e->b);
+            if (lease->second == 0) s_.leases.erase(lease);
+            break;
+        }
+        }
+    }
+    static_cast<Counters&>(s_) = saved_.counters;
+    s_.lru.resize(saved_.lru_size);
+    s_.lru_head = saved_.lru_head;
+    s_.clock = saved_.clock;
+    journal_.clear();
+    pruned_edges_.clear();
+}
 
 }  // namespace miniprefix_b200

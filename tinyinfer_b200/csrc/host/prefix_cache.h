@@ -17,11 +17,13 @@
 //  * clear(): drop every lease in lexicographic pre-order (:104-110), which fixes
 //    the order pages return to the pool's free list.
 // Internals differ: nodes live in an arena addressed by index, keys are owned
-// token vectors, and the whole index is a value, so it can be snapshotted and
-// restored (used to roll back a failed batched step exactly).
+// token vectors, every mutation can be recorded in an undo journal (used to roll
+// back a failed batched step exactly, at a cost proportional to the step's own
+// changes), and publish() first tries the node path the same sequence reached at
+// its previous publish (each hinted node is checked against its parent and edge
+// before use, so a stale hint only costs the ordinary lookup).
 #pragma once
 #include <cstdint>
-#include <deque>
 #include <map>
 #include <unordered_map>
 #include <vector>
@@ -51,10 +53,12 @@ public:
     void publish(const PagedSequence& sequence);
     bool evict_one();
 
-    // Opaque copy of the whole index (pool state is journaled separately).
-    struct Snapshot;
-    Snapshot snapshot() const;
-    void restore(const Snapshot& snapshot);
+    // Undo journal of the index (pool state is journaled separately): between
+    // begin_journal() and end_journal(), rollback_journal() returns the index to
+    // its state at begin_journal().
+    void begin_journal();
+    void rollback_journal() noexcept;
+    void end_journal() noexcept;
 
 private:
     struct EdgeLess {
@@ -77,31 +81,66 @@ private:
         int parent = -1;
         std::vector<std::int32_t> edge;
         int block = -1;
-        int older = -1, newer = -1;  // LRU links among leased nodes
-        Children children;           // every child
-        Children leased;             // children holding a lease (lookup set of reuse)
+        std::uint64_t stamp = 0;  // LRU time of the last touch; 0 while not leased
+        Children children;        // every child
+        Children leased;          // children holding a lease (lookup set of reuse)
     };
 
-public:
-    struct Snapshot {
-        std::deque<Node> nodes;
-        std::vector<int> spare;
-        int oldest = -1, newest = -1;
+    struct Counters {
         std::size_t cached = 0, live_nodes = 0, key_tokens = 0;
-        std::unordered_map<int, std::uint32_t> leases;
         std::size_t hits = 0, misses = 0, reused = 0, evictions = 0;
     };
+    // LRU order is the order of the nodes' stamps. `lru` lists (stamp, node) in
+    // increasing stamp order; an entry is current while the node still holds a
+    // lease with that stamp, and the least recently used lease is the first
+    // current entry at or after `lru_head`. Stale entries are skipped there and
+    // dropped by compaction (outside undo windows only).
+    struct State : Counters {
+        std::vector<Node> nodes;
+        std::vector<int> spare;
+        std::unordered_map<int, std::uint32_t> leases;
+        std::vector<std::pair<std::uint64_t, int>> lru;
+        std::size_t lru_head = 0;
+        std::uint64_t clock = 0;
+    };
+    // Journal entries: each records what its inverse needs.
+    enum class Op : std::uint8_t {
+        NewNode,     // a = node, b = parent, v = 1 when taken from the spare list
+        Prune,       // a = node, b = parent; the edge moves to pruned_edges_
+        LeasedAdd,   // a = parent, b = node
+        LeasedDrop,  // a = parent, b = node
+        Stamp,       // a = node, v = previous stamp
+        Block,       // a = node, b = previous block
+        Lease,       // a = page, b = +1 / -1
+    };
+    struct Entry {
+        Op op;
+        int a, b;
+        std::uint64_t v;
+    };
+    void log(Op op, int a, int b = 0, std::uint64_t v = 0) {
+        if (journaling_) journal_.push_back({op, a, b, v});
+    }
+    void lease_add(int page, int delta);
 
-private:
     int new_node(int parent, View edge);
-    void lru_unlink(int n) noexcept;
-    void lru_append(int n) noexcept;
-    void touch(int n) noexcept;
+    void touch(int n);            // becomes the most recently used lease
+    void unstamp(int n) noexcept; // leaves the LRU order
+    int lru_front() noexcept;     // least recently used lease, -1 when none
+    void compact_lru();
     void prune(int n, int keep) noexcept;
     void drop(int n, int keep) noexcept;
 
     KvBlockPool& pool_;
-    Snapshot s_;  // the live index (nodes[0] is the root)
+    State s_;  // the live index (nodes[0] is the root)
+    bool journaling_ = false;
+    std::vector<Entry> journal_;
+    std::vector<std::vector<std::int32_t>> pruned_edges_;
+    struct Window {
+        Counters counters;
+        std::size_t lru_size = 0, lru_head = 0;
+        std::uint64_t clock = 0;
+    } saved_;
 };
 
 }  // namespace miniprefix_b200

@@ -58,6 +58,9 @@ struct PagedSequence {
     int used = 0;
     std::vector<int> blocks;
     std::vector<std::int32_t> tokens;
+    // Lookup hint of the prefix cache: the index node of page i at this
+    // sequence's last publish (validated before each use; never changes results).
+    mutable std::vector<int> prefix_path;
 };
 
 struct ModelConfig {

@@ -46,7 +46,8 @@ class SequenceDescC(C.Structure):
 class CountersC(C.Structure):
     _fields_ = [("forwards", C.c_uint64), ("forward_ms", C.c_double), ("kernel_launches", C.c_uint64),
                 ("h2d_bytes", C.c_uint64), ("d2h_bytes", C.c_uint64), ("shared_prefix_rows", C.c_uint64),
-                ("shared_prefix_tokens", C.c_uint64)]
+                ("shared_prefix_tokens", C.c_uint64), ("host_prepare_ms", C.c_double), ("host_launch_ms", C.c_double),
+                ("host_wait_ms", C.c_double)]
 
 
 class TableEntryC(C.Structure):

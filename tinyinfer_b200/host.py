@@ -139,6 +139,10 @@ class PrefixCache(_Base):
     def evict_one(self):
         return bool(self.check(self.lib.mph_cache_evict_one(self.h)))
 
+    def journal(self, op):
+        """Undo window: 'begin', 'rollback' (to the state at begin) or 'end'."""
+        self.check(self.lib.mph_cache_journal(self.h, {"begin": 0, "rollback": 1, "end": 2}[op]))
+
     def clear(self):
         self.lib.mph_cache_clear(self.h)
 
