@@ -43,8 +43,16 @@
 namespace mpb {
 namespace {
 
-constexpr int kStageTokens = 16;
-constexpr int kStages = 3;
+#ifndef MPB_ATTN_STAGE_TOKENS
+#define MPB_ATTN_STAGE_TOKENS 16
+#endif
+#ifndef MPB_ATTN_STAGES
+#define MPB_ATTN_STAGES 3
+#endif
+constexpr int kStageTokens = MPB_ATTN_STAGE_TOKENS;  // a multiple of 8
+constexpr int kStages = MPB_ATTN_STAGES;
+constexpr int kPasses = kStageTokens / 8;            // 8 tokens per consumer pass
+static_assert(kStageTokens % 8 == 0 && kPasses >= 1, "stage = whole consumer passes");
 constexpr int kConsumers = kKvHeads;                   // 3 consumer warps
 constexpr int kThreads = (kConsumers + 1) * 32;        // + producer warp
 constexpr int kStageFloats = kStageTokens * kKvWidth;  // per pool
@@ -220,11 +228,11 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
         const float* kst = stages + 2 * buf * kStageFloats + kh * kHeadDim + c * 16;
         const float* vst = stages + (2 * buf + 1) * kStageFloats + kh * kHeadDim + lane;
         const bool full_stage = d.n_valid == kStageTokens;
-        // scores of tokens t and t + 8 for the 3 heads, in base-2 units
+        // scores of tokens t + 8 ps for the 3 heads, in base-2 units
         // (dot / 8 * log2 e); even / odd dims in the two halves of a packed FMA
-        float s[2][kGroup];
+        float s[kPasses][kGroup];
 #pragma unroll
-        for (int ps = 0; ps < 2; ++ps) {
+        for (int ps = 0; ps < kPasses; ++ps) {
             const float* krow = kst + (t + 8 * ps) * kKvWidth;
             float pe[kGroup] = {0.f, 0.f, 0.f}, po[kGroup] = {0.f, 0.f, 0.f};
 #pragma unroll
@@ -245,18 +253,25 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
                 s[ps][hh] = valid ? part * (0.125f * kLog2e) : -INFINITY;
             }
         }
-        // online softmax over the stage's 16 tokens (lanes differ in t across bits 2..4)
+        // online softmax over the stage's tokens (lanes differ in t across bits 2..4)
 #pragma unroll
         for (int hh = 0; hh < kGroup; ++hh) {
-            float mx = fmaxf(s[0][hh], s[1][hh]);
+            float mx = s[0][hh];
+#pragma unroll
+            for (int ps = 1; ps < kPasses; ++ps) mx = fmaxf(mx, s[ps][hh]);
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
             const float m_new = fmaxf(m_run[hh], mx);
             const float ms = m_new == -INFINITY ? 0.f : m_new;  // no valid token yet: all terms stay 0
             const float alpha = exp2f(m_run[hh] - ms);
-            const float p0 = exp2f(s[0][hh] - ms), p1 = exp2f(s[1][hh] - ms);
-            float sum = p0 + p1;
+            float pw[kPasses];
+            float sum = 0.f;
+#pragma unroll
+            for (int ps = 0; ps < kPasses; ++ps) {
+                pw[ps] = exp2f(s[ps][hh] - ms);
+                sum += pw[ps];
+            }
             sum += __shfl_xor_sync(0xffffffffu, sum, 4);
             sum += __shfl_xor_sync(0xffffffffu, sum, 8);
             sum += __shfl_xor_sync(0xffffffffu, sum, 16);
@@ -265,8 +280,8 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
             acc[hh][0] *= alpha;
             acc[hh][1] *= alpha;
             if (c == 0) {
-                probs[hh * kStageTokens + t] = p0;
-                probs[hh * kStageTokens + t + 8] = p1;
+#pragma unroll
+                for (int ps = 0; ps < kPasses; ++ps) probs[hh * kStageTokens + t + 8 * ps] = pw[ps];
             }
         }
         __syncwarp();
