@@ -122,12 +122,15 @@ void B200Runner::clear_prefix_cache() {
     kv_.clear_prefix_cache();
 }
 
-// Entries of `sequence.blocks` that differ from what the device already holds.
-void B200Runner::table_entries(int slot, const PagedSequence& sequence, std::vector<mp_table_entry>& out) {
+// Entries of `sequence.blocks` that differ from what the device already holds,
+// looking from index `from` on (entries before it are known to be in sync).
+void B200Runner::table_entries(int slot, const PagedSequence& sequence, std::vector<mp_table_entry>& out,
+                               std::size_t from) {
     auto& m = mirror_[std::size_t(slot)];
     const auto& b = sequence.blocks;
+    if (m.size() < from) from = 0;  // the mirror was dropped: compare everything
     if (m.size() < b.size()) m.resize(b.size(), -1);
-    for (std::size_t i = 0; i < b.size(); ++i)
+    for (std::size_t i = from; i < b.size(); ++i)
         if (m[i] != b[i]) {
             out.push_back({slot, int32_t(i), b[i]});
             m[i] = b[i];
@@ -230,7 +233,9 @@ std::size_t B200Runner::stage_append(const RequestId& id, const std::vector<Toke
         tx.commit();
         return ticket;
     }
-    table_entries(slot, sequence, entries_);
+    // an append changes at most its last original page (copy on write) and the
+    // pages after it; the mirror is dropped whenever anything else may change
+    table_entries(slot, sequence, entries_, tx.original_blocks() ? tx.original_blocks() - 1 : 0);
     const int bt = kv_.config().block_tokens;
     for (int p = sequence.used / bt; p <= (sequence.used + int(tokens.size()) - 1) / bt; ++p)
         written_epoch_[std::size_t(sequence.blocks[std::size_t(p)])] = epoch_;

@@ -7,10 +7,12 @@
 // -> logits download, throws "nonfinite CUDA logits" and rolls back on a
 // nonfinite result, and commits otherwise; release/clear drop pages and tables.
 // Beyond that, stage_append()/flush() let the Engine run all appends of a step as
-// ONE device forward (see model_runner.h). A staged append's device work is
-// flushed early when a later append of the same step would otherwise touch a
-// page that the pending work still reads or writes: a page freed and handed out
-// again, or a shared tail page written in the pending work and now copied.
+// ONE device forward (see model_runner.h). The forward copies every COW source
+// before writing any destination, then runs the layers; pending work is flushed
+// early only where that order differs from sequential appends: a later append
+// writes a page that a pending append's attention still reads (freed this step
+// by that sequence and handed out again), copies a tail page that pending work
+// writes, or belongs to a sequence that already has a pending append.
 #pragma once
 #include <map>
 #include <memory>
@@ -75,7 +77,8 @@ public:
 
 private:
     int slot_of(const RequestId& id) const;
-    void table_entries(int slot, const PagedSequence& sequence, std::vector<mp_table_entry>& out);
+    void table_entries(int slot, const PagedSequence& sequence, std::vector<mp_table_entry>& out,
+                       std::size_t from = 0);
     void free_slot(const RequestId& id);
     void mark_pending_reads(const RequestId& id);  // before a pending sequence drops its pages
     void drain() noexcept;  // best-effort completion of queued device work

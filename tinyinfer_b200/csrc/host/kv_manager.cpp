@@ -52,17 +52,21 @@ void KVManager::touch_sequence(const RequestId& id, bool dropping) {
         SavedSequence saved;
         auto it = sequences_.find(id);
         if (it != sequences_.end()) {
+            const auto& s = it->second.sequence;
             saved.existed = true;
-            saved.used = it->second.sequence.used;
-            saved.blocks = it->second.sequence.blocks;
-            saved.token_count = it->second.sequence.tokens.size();
+            saved.used = s.used;
+            saved.block_count = s.blocks.size();
+            saved.last_block = s.blocks.empty() ? -1 : s.blocks.back();
+            saved.token_count = s.tokens.size();
         }
         found = checkpoint_->sequences.emplace(id, std::move(saved)).first;
     }
     auto& saved = found->second;
     if (dropping && saved.existed && !saved.tokens) {
-        const auto& t = sequences_.at(id).sequence.tokens;
-        saved.tokens.emplace(t.begin(), t.begin() + std::ptrdiff_t(std::min(saved.token_count, t.size())));
+        const auto& s = sequences_.at(id).sequence;
+        saved.tokens.emplace(s.tokens.begin(), s.tokens.begin() + std::ptrdiff_t(std::min(saved.token_count, s.tokens.size())));
+        saved.blocks.emplace(s.blocks.begin(), s.blocks.begin() + std::ptrdiff_t(saved.block_count));
+        if (saved.block_count) saved.blocks->back() = saved.last_block;
     }
 }
 
@@ -191,7 +195,10 @@ KVManager::Append::Append(KVManager& owner, const RequestId& id, const std::vect
         throw std::invalid_argument("context overflow/empty input");
     owner.validate_tokens(tokens);
     owner.touch_sequence(id);
-    sequence.tokens.reserve(std::size_t(sequence.used) + tokens.size());
+    // room for the commit up front (commit must not allocate); grow geometrically,
+    // an exact reserve would copy the whole history on every decode append
+    const std::size_t need = std::size_t(sequence.used) + tokens.size();
+    if (sequence.tokens.capacity() < need) sequence.tokens.reserve(std::max(need, 2 * sequence.tokens.capacity()));
     const int valid = sequence.used % owner.config().block_tokens;
     bool cow = valid && owner.pool_.references(sequence.blocks.back()) > 1;
     owner.reserve_pages(id, sequence, sequence.used + int(tokens.size()), cow);
@@ -339,7 +346,12 @@ void KVManager::restore_checkpoint() {
         auto& state = sequences_[id];
         state.appending = false;
         state.sequence.used = saved.used;
-        state.sequence.blocks = std::move(saved.blocks);
+        if (saved.blocks) {
+            state.sequence.blocks = std::move(*saved.blocks);
+        } else {
+            state.sequence.blocks.resize(saved.block_count);
+            if (saved.block_count) state.sequence.blocks.back() = saved.last_block;
+        }
         if (saved.tokens) state.sequence.tokens = std::move(*saved.tokens);
         else state.sequence.tokens.resize(saved.token_count);
     }

@@ -18,6 +18,7 @@
 #pragma once
 #include <functional>
 #include <map>
+#include <unordered_map>
 #include <memory>
 #include <optional>
 
@@ -127,17 +128,22 @@ private:
 
     // A sequence as it was at the checkpoint. Tokens only grow inside a window
     // unless the sequence is released, so only their count is kept until then.
+    // A sequence's state at the checkpoint. Until it is dropped, an append can
+    // only replace its last page (copy on write) and add pages after it, so the
+    // page count and the last page restore it; a drop saves the full lists.
     struct SavedSequence {
         bool existed = false;
         int used = 0;
-        std::vector<int> blocks;
+        std::size_t block_count = 0;
+        int last_block = -1;
+        std::optional<std::vector<int>> blocks;
         std::size_t token_count = 0;
         std::optional<std::vector<std::int32_t>> tokens;
     };
     struct Checkpoint {
         std::vector<KvBlockPool::JournalEntry> pool_journal;
         std::size_t live = 0, peak = 0;
-        std::map<RequestId, SavedSequence> sequences;
+        std::unordered_map<RequestId, SavedSequence> sequences;
         std::map<RequestId, std::optional<std::size_t>> reservations;  // nullopt: did not exist
         std::size_t reserved_pages = 0, forward_tokens = 0;
         CostStats costs;

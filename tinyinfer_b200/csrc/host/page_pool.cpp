@@ -59,7 +59,7 @@ void KvBlockPool::reserve(PagedSequence& sequence, int end) {
     const std::size_t needed = std::size_t(end / bt + (end % bt != 0));
     if (needed <= sequence.blocks.size()) return;
     if (needed - sequence.blocks.size() > free_.size()) throw KvCapacityError("paged KV block pool exhausted");
-    sequence.blocks.reserve(needed);
+    if (sequence.blocks.capacity() < needed) sequence.blocks.reserve(std::max(needed, 2 * sequence.blocks.capacity()));
     while (sequence.blocks.size() < needed) {
         const int block = free_.back();
         free_.pop_back();

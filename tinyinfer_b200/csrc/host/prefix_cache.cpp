@@ -42,7 +42,7 @@ int ExactPrefixCache::new_node(int parent, View edge) {
     n.stamp = 0;
     n.children.clear();
     n.leased.clear();
-    s_.nodes[std::size_t(parent)].children.emplace(n.edge, id);
+    s_.nodes[std::size_t(parent)].children.insert(view(n.edge), id);
     ++s_.live_nodes;
     s_.key_tokens += edge.n;
     return id;
@@ -92,7 +92,7 @@ void ExactPrefixCache::prune(int id, int keep) noexcept {
         if (n.block >= 0 || !n.children.empty()) break;
         const int parent = n.parent;
         s_.key_tokens -= n.edge.size();
-        s_.nodes[std::size_t(parent)].children.erase(n.edge);
+        s_.nodes[std::size_t(parent)].children.erase(view(n.edge));
         if (journaling_) {
             log(Op::Prune, id, parent);
             pruned_edges_.push_back(std::move(n.edge));
@@ -107,7 +107,7 @@ void ExactPrefixCache::prune(int id, int keep) noexcept {
 
 void ExactPrefixCache::drop(int id, int keep) noexcept {
     Node& n = s_.nodes[std::size_t(id)];
-    s_.nodes[std::size_t(n.parent)].leased.erase(n.edge);
+    s_.nodes[std::size_t(n.parent)].leased.erase(view(n.edge));
     log(Op::LeasedDrop, n.parent, id);
     const int block = n.block;
     lease_add(block, -1);
@@ -135,8 +135,8 @@ void ExactPrefixCache::clear() noexcept {
         const int id = stack.back();
         stack.pop_back();
         if (id > 0 && s_.nodes[std::size_t(id)].block >= 0) order.push_back(id);
-        const auto& ch = s_.nodes[std::size_t(id)].children;
-        for (auto it = ch.rbegin(); it != ch.rend(); ++it) stack.push_back(it->second);
+        const auto& ch = s_.nodes[std::size_t(id)].children.items();
+        for (auto it = ch.rbegin(); it != ch.rend(); ++it) stack.push_back(it->id);
     }
     for (int id : order) drop(id, -1);
 }
@@ -153,8 +153,8 @@ int ExactPrefixCache::reuse(PagedSequence& sequence, const std::vector<std::int3
     while (count < limit) {
         const std::size_t length = std::min(bt, limit - count);
         const std::int32_t* q = prompt.data() + count;
-        const Children& leased = s_.nodes[std::size_t(parent)].leased;
-        const auto next = leased.lower_bound(View{q, length});
+        const auto& leased = s_.nodes[std::size_t(parent)].leased.items();
+        const std::size_t next = s_.nodes[std::size_t(parent)].leased.lower_bound(View{q, length});
         int best = -1;
         std::size_t matched = 0;
         auto consider = [&](int id) {
@@ -166,8 +166,8 @@ int ExactPrefixCache::reuse(PagedSequence& sequence, const std::vector<std::int3
                 best = id;
             }
         };
-        if (next != leased.end()) consider(next->second);
-        if (next != leased.begin()) consider(std::prev(next)->second);
+        if (next < leased.size()) consider(leased[next].id);
+        if (next > 0) consider(leased[next - 1].id);
         if (!matched) break;
         pages.push_back(s_.nodes[std::size_t(best)].block);
         touch(best);
@@ -212,20 +212,19 @@ void ExactPrefixCache::publish(const PagedSequence& sequence) {
             }
         }
         if (id < 0) {
-            const auto& ch = s_.nodes[std::size_t(parent)].children;
-            const auto it = ch.find(key);
-            id = it != ch.end() ? it->second : new_node(parent, key);
+            id = s_.nodes[std::size_t(parent)].children.find(key);
+            if (id < 0) id = new_node(parent, key);
         }
         if (s_.nodes[std::size_t(id)].block >= 0) {
             touch(id);
         } else {
             const int page = sequence.blocks[i];
-            s_.nodes[std::size_t(parent)].leased.emplace(s_.nodes[std::size_t(id)].edge, id);
+            s_.nodes[std::size_t(parent)].leased.insert(view(s_.nodes[std::size_t(id)].edge), id);
             log(Op::LeasedAdd, parent, id);
             try {
                 pool_.retain(page);
             } catch (...) {
-                s_.nodes[std::size_t(parent)].leased.erase(s_.nodes[std::size_t(id)].edge);
+                s_.nodes[std::size_t(parent)].leased.erase(view(s_.nodes[std::size_t(id)].edge));
                 log(Op::LeasedDrop, parent, id);
                 prune(id, -1);
                 throw;
@@ -269,7 +268,7 @@ void ExactPrefixCache::rollback_journal() noexcept {
         switch (e->op) {
         case Op::NewNode: {
             Node& n = s_.nodes[std::size_t(e->a)];
-            s_.nodes[std::size_t(e->b)].children.erase(n.edge);
+            s_.nodes[std::size_t(e->b)].children.erase(view(n.edge));
             n.edge.clear();
             n.parent = -1;
             n.block = -1;
@@ -286,14 +285,14 @@ void ExactPrefixCache::rollback_journal() noexcept {
             n.edge = std::move(pruned_edges_.back());
             pruned_edges_.pop_back();
             n.parent = e->b;
-            s_.nodes[std::size_t(e->b)].children.emplace(n.edge, e->a);
+            s_.nodes[std::size_t(e->b)].children.insert(view(n.edge), e->a);
             break;
         }
         case Op::LeasedAdd:
-            s_.nodes[std::size_t(e->a)].leased.erase(s_.nodes[std::size_t(e->b)].edge);
+            s_.nodes[std::size_t(e->a)].leased.erase(view(s_.nodes[std::size_t(e->b)].edge));
             break;
         case Op::LeasedDrop:
-            s_.nodes[std::size_t(e->a)].leased.emplace(s_.nodes[std::size_t(e->b)].edge, e->b);
+            s_.nodes[std::size_t(e->a)].leased.insert(view(s_.nodes[std::size_t(e->b)].edge), e->b);
             break;
         case Op::Stamp:
             s_.nodes[std::size_t(e->a)].stamp = e->v;

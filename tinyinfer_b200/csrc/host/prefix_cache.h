@@ -23,8 +23,9 @@
 // its previous publish (each hinted node is checked against its parent and edge
 // before use, so a stale hint only costs the ordinary lookup).
 #pragma once
+#include <algorithm>
 #include <cstdint>
-#include <map>
+#include <type_traits>
 #include <unordered_map>
 #include <vector>
 
@@ -61,22 +62,43 @@ public:
     void end_journal() noexcept;
 
 private:
-    struct EdgeLess {
-        using is_transparent = void;
-        struct View {
-            const std::int32_t* p;
-            std::size_t n;
-        };
-        static View view(const std::vector<std::int32_t>& v) { return {v.data(), v.size()}; }
-        static View view(const View& v) { return v; }
-        template <class A, class B>
-        bool operator()(const A& a, const B& b) const {
-            const View x = view(a), y = view(b);
-            return std::lexicographical_compare(x.p, x.p + x.n, y.p, y.p + y.n);
-        }
+    struct View {
+        const std::int32_t* p;
+        std::size_t n;
     };
-    using View = EdgeLess::View;
-    using Children = std::map<std::vector<std::int32_t>, int, EdgeLess>;
+    static View view(const std::vector<std::int32_t>& v) { return {v.data(), v.size()}; }
+    static bool less(View a, View b) { return std::lexicographical_compare(a.p, a.p + a.n, b.p, b.p + b.n); }
+    // Children of a node in lexicographic order of their edges: a sorted vector of
+    // (edge view, node). A view points into the child's own edge buffer, which
+    // stays put while the child is listed (moving a Node moves the buffer as a
+    // whole); nodes have few children, so lookups and inserts stay cheap.
+    class Children {
+    public:
+        struct Item {
+            View key;
+            int id;
+        };
+        bool empty() const { return items_.empty(); }
+        void clear() { items_.clear(); }
+        const std::vector<Item>& items() const { return items_; }
+        std::size_t lower_bound(View k) const {
+            return std::size_t(std::lower_bound(items_.begin(), items_.end(), k,
+                                                [](const Item& a, View b) { return less(a.key, b); }) -
+                               items_.begin());
+        }
+        int find(View k) const {
+            const std::size_t i = lower_bound(k);
+            return i < items_.size() && !less(k, items_[i].key) ? items_[i].id : -1;
+        }
+        void insert(View k, int id) { items_.insert(items_.begin() + std::ptrdiff_t(lower_bound(k)), Item{k, id}); }
+        void erase(View k) {
+            const std::size_t i = lower_bound(k);
+            if (i < items_.size() && !less(k, items_[i].key)) items_.erase(items_.begin() + std::ptrdiff_t(i));
+        }
+
+    private:
+        std::vector<Item> items_;
+    };
     struct Node {
         int parent = -1;
         std::vector<std::int32_t> edge;
@@ -85,6 +107,9 @@ private:
         Children children;        // every child
         Children leased;          // children holding a lease (lookup set of reuse)
     };
+    // Children views stay valid across reallocation of the node arena only if
+    // nodes move (never copy) their edge buffers.
+    static_assert(std::is_nothrow_move_constructible<Node>::value, "nodes must move their edges");
 
     struct Counters {
         std::size_t cached = 0, live_nodes = 0, key_tokens = 0;
