@@ -175,7 +175,9 @@ int mp_gemm_f32(const float* a, const float* b, float* c, int32_t m, int32_t n, 
  * caller device buffers: q [count][9*64] roped queries, pools in the reference
  * layout with `layers` layers, tables [count][table_stride] (device), out
  * [count][9*64]. `lengths` is a HOST array (tokens to attend per sequence);
- * pages_per_split 0 picks a split for the 148 SMs. Runs on `stream`
+ * pages_per_split 0 cuts the sequences' pages, concatenated, into one equal run
+ * per CTA of a single wave (3 per SM); > 0 cuts each sequence into slices of
+ * that many pages, pulled longest first by the wave. Runs on `stream`
  * (cudaStream_t, NULL = legacy default) and does not synchronise. Uses an
  * internal scratch buffer that grows on demand. */
 int mp_paged_attention_decode(const float* q, const float* keys, const float* values, int32_t layers, int32_t layer,
@@ -187,7 +189,7 @@ int mp_paged_attention_decode(const float* q, const float* keys, const float* va
  * cudaMalloc/cudaFree must not run because they synchronise the device. It calls
  * no allocator: its scratch is one file-scope __device__ array of about 5 MB held
  * by every GPU that loads the library. At most 512 sequences and 2048 slices per
- * call (pages_per_split 0 picks a slice length that fits); larger requests return
+ * call (pages_per_split 0: equal runs per CTA, which always fit); larger requests return
  * MP_ERR_INVALID. All calls on a device share that array: calls whose device work
  * overlaps race. The first call on a device, with that device current, looks up
  * the array's address; make it before any stream capture. `device_error`

@@ -77,7 +77,8 @@ def test_config2_matches_oracle(built):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("block_tokens,pps", [(16, 1), (16, 3), (4, 5), (12, 2), (32, 0), (1, 40)])
+@pytest.mark.parametrize("block_tokens,pps", [(16, 1), (16, 3), (4, 5), (12, 2), (32, 0), (1, 40), (16, 0), (4, 0),
+                                               (1, 0)])
 def test_edge_lengths_and_splits(built, block_tokens, pps):
     lengths = [1, 2, 15, 16, 17, 31, 32, 33, 63, 64, 65, 100, 255, 256, 257, 1000]
     pool = sum(-(-L // block_tokens) for L in lengths) + 7
@@ -94,6 +95,23 @@ def test_repeated_launches_reuse_counters(built):
     q, k, v, tables, lengths = make_case(9, 16, 700, 16, 2048)
     a, _ = run_gpu(q, k, v, tables, lengths, 16, 2048, 2)
     b, _ = run_gpu(q, k, v, tables, lengths, 16, 2048, 2)
+    assert np.array_equal(a, b)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("count,max_len", [(300, 40), (3, 5000), (444, 16), (7, 1)])
+def test_static_runs_match_oracle(built, count, max_len):
+    """pages_per_split 0: the pages of all sequences, concatenated, cut into one
+    equal run per CTA (fewer runs than CTAs when there are fewer pages; a run
+    spanning several sequences; a sequence spanning many runs); two launches give
+    identical results."""
+    pool = count * (-(-max_len // 16)) + 5
+    q, k, v, tables, lengths = make_case(13 + count, count, max_len, 16, pool)
+    ref = Oracle.decode_attention(q, lengths, tables, k, v, HEADS, KVH, DIM, 16)
+    a, status = run_gpu(q, k, v, tables, lengths, 16, pool, 0)
+    assert status == 0
+    check_close(a, ref)
+    b, _ = run_gpu(q, k, v, tables, lengths, 16, pool, 0)
     assert np.array_equal(a, b)
 
 

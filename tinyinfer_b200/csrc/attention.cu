@@ -13,7 +13,8 @@
 // final output.
 //
 // CTA = 4 warps, warp-specialised, no block-wide barrier in the steady state:
-//  * warp 3 (producer) walks its work items -- one, or with a schedule, items
+//  * warp 3 (producer) walks its work items -- one; or a fixed run of items (a
+//    static schedule that gives every CTA an equal share of the pages); or items
 //    pulled from a shared counter in the given order (persistent, one wave) --
 //    and for every 16-token stage writes a stage descriptor (item, row, first
 //    token, valid tokens, first/last flags) and moves the stage's K and V runs
@@ -114,14 +115,16 @@ __device__ __forceinline__ void issue_stage(const AttnParams& p, const int32_t* 
 __device__ void producer(const AttnParams& p, float* stages, StageDesc* desc, uint64_t* full, uint64_t* empty,
                          bool persistent, unsigned* failed, int lane) {
     uint32_t g = 0;  // stages issued so far
-    int item = blockIdx.x;
+    const bool fixed = p.cta_items != nullptr;
+    int item = fixed ? p.cta_items[blockIdx.x] : int(blockIdx.x);
+    const int item_end = fixed ? p.cta_items[blockIdx.x + 1] : p.work_count;
     // a stage's previous use must have been released by the 3 consumers
     auto acquire = [&](int buf) -> bool {
         if (g < uint32_t(kStages)) return true;
         return mbar_wait_bounded(&empty[buf], ((g / kStages) - 1) & 1);
     };
     while (true) {
-        if (item >= p.work_count) {
+        if (item >= item_end) {
             // no more work: a descriptor without copies releases the consumers
             const int buf = g % kStages;
             if (!acquire(buf)) {
@@ -134,9 +137,10 @@ __device__ void producer(const AttnParams& p, float* stages, StageDesc* desc, ui
             }
             return;
         }
-        const int wi = p.order ? p.order[item] : item;
+        const int wi = !fixed && p.order ? p.order[item] : item;
         int next = 0;
-        if (lane == 0) next = persistent ? int(gridDim.x + atomicAdd(&p.sched[0], 1u)) : p.work_count;
+        if (fixed) next = item + 1;
+        else if (lane == 0) next = persistent ? int(gridDim.x + atomicAdd(&p.sched[0], 1u)) : p.work_count;
         next = __shfl_sync(0xffffffffu, next, 0);
         const AttnWork w = p.work[wi];
         const int row = w.row;
@@ -389,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 3) paged_attention_kernel(const Attn
         fence_barrier_init();
     }
     __syncthreads();
-    const bool persistent = p.sched != nullptr;
+    const bool persistent = p.sched != nullptr && p.cta_items == nullptr;
     if (warp == kConsumers)
         producer(p, stages, desc, full, empty, persistent, failed, lane);
     else
@@ -411,8 +415,10 @@ cudaError_t configure_attention() {
 
 cudaError_t launch_paged_attention(const AttnParams& p, cudaStream_t stream) {
     if (p.work_count <= 0) return cudaSuccess;
-    // persistent: one wave of 3 CTAs per SM pulls the work items
-    const int grid = p.sched ? std::min(p.work_count, kAttnPersistentCtas) : p.work_count;
+    // static schedule: one CTA per segment; persistent: one wave of 3 CTAs per SM
+    // pulls the work items; else one CTA per item
+    const int grid = p.cta_items ? p.cta_count : (p.sched ? std::min(p.work_count, kAttnPersistentCtas) : p.work_count);
+    if (grid <= 0) return cudaSuccess;
     return launch_pdl(paged_attention_kernel, dim3(grid), dim3(kThreads), kAttnSmem, stream, p);
 }
 

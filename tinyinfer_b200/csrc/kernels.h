@@ -1,6 +1,7 @@
 // Host-visible launch interfaces of the sm_100a kernels (internal to the library;
 // the public boundary is include/miniprefix_b200.h).
 #pragma once
+#include <algorithm>
 #include <cstddef>
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -50,6 +51,10 @@ struct AttnParams {
     int work_count;
     const int32_t* order;  // optional processing order of the work items (longest first)
     unsigned* sched;       // optional [2] zeroed counters: persistent CTAs pull work items
+    // optional static schedule ([cta_count + 1]): CTA c processes work items
+    // [cta_items[c], cta_items[c + 1]) in order (order and sched unused)
+    const int32_t* cta_items;
+    int cta_count;
     float* partial;      // [slots][9][66] slice results: work items first, then shared-prefix slots
     unsigned* counters;  // [rows][3 kv heads] zero between launches
     float* out;          // [rows][out_stride]; the TF32 hi half when out_lo is set
@@ -141,10 +146,45 @@ inline int auto_pages_per_split(long long total_tokens, int block_tokens) {
     return int(pages < 1 ? 1 : pages);
 }
 
+constexpr int kAttnPersistentCtas = 148 * 3;  // one wave of the decode kernel
+// Static decode schedule for the operator entry points: the rows' pages,
+// concatenated in row order, cut into one equal run per CTA (min(persistent
+// CTAs, total pages) runs; a run may end one row and start the next). A row's
+// part of a run is one work item. Calls emit(row, page_begin, page_end, k) per
+// item in order (k = the item's index within its row) and cta_start(c, items)
+// when run c begins at item index `items` (c = 1 .. runs, the last one being
+// the total). Returns the number of runs (CTAs).
+template <class PagesOf, class Emit, class CtaStart>
+inline int plan_static_runs(int rows, PagesOf pages_of, Emit emit, CtaStart cta_start) {
+    long long total = 0;
+    for (int r = 0; r < rows; ++r) total += pages_of(r);
+    const long long runs = total < kAttnPersistentCtas ? (total > 0 ? total : 1) : kAttnPersistentCtas;
+    auto run_end = [&](long long c) { return (c + 1) * total / runs; };
+    long long pos = 0;
+    int run = 0, items = 0;
+    for (int r = 0; r < rows; ++r) {
+        const int pages = pages_of(r);
+        int k = 0;
+        if (pages <= 0) {
+            emit(r, 0, 0, k++);
+            ++items;
+        }
+        for (int pg = 0; pg < pages;) {
+            while (pos >= run_end(run)) cta_start(++run, items);
+            const int n = int(std::min<long long>(pages - pg, run_end(run) - pos));
+            emit(r, pg, pg + n, k++);
+            ++items;
+            pg += n;
+            pos += n;
+        }
+    }
+    while (run < runs) cta_start(++run, items);
+    return int(runs);
+}
+
 cudaError_t configure_attention();
 // Message returned by mp_last_error() on this thread.
 void set_last_error(const char* message);
-constexpr int kAttnPersistentCtas = 148 * 3;  // one wave of the decode kernel
 cudaError_t launch_paged_attention(const AttnParams& p, cudaStream_t stream);
 
 // ---------------------------------------------------------------- GEMM

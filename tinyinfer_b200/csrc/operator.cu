@@ -66,32 +66,45 @@ extern "C" int mp_paged_attention_decode(const float* q, const float* keys, cons
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return MP_ERR_CUDA;
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
     Scratch& s = g_scratch[device];
-    // Work list: slices of `pps` pages (0: mpb::auto_pages_per_split).
-    int pps = pages_per_split;
-    if (pps <= 0) {
-        long long total = 0;
-        for (int i = 0; i < count; ++i) total += lengths[i];
-        pps = mpb::auto_pages_per_split(total, block_tokens);
-    }
+    // Work list. pages_per_split 0: the rows' pages cut into one equal run per CTA
+    // (mpb::plan_static_runs; `order` then holds the runs' first items); else
+    // slices of that many pages pulled longest first by a persistent wave.
     std::vector<int32_t> host(size_t(count) * 4);
     std::vector<mpb::AttnWork> work;
+    std::vector<int32_t> order;
+    int runs = 0;
+    auto pages_of = [&](int r) { return (lengths[r] + block_tokens - 1) / block_tokens; };
     for (int r = 0; r < count; ++r) {
-        const int pages = (lengths[r] + block_tokens - 1) / block_tokens;
-        const int n = std::max(1, (pages + pps - 1) / pps);
-        host[r] = r;                              // slot
-        host[count + r] = lengths[r];             // length
-        host[2 * count + r] = n;                  // splits
-        host[3 * count + r] = int(work.size());   // first work item
-        for (int k = 0; k < n; ++k) work.push_back({r, k * pps, std::min(pages, (k + 1) * pps), k});
+        host[r] = r;              // slot
+        host[count + r] = lengths[r];  // length
     }
-    // processing order of the persistent kernel: longest slices first
-    std::vector<int32_t> order(work.size());
-    for (size_t i = 0; i < order.size(); ++i) order[i] = int32_t(i);
-    auto tokens = [&](int32_t i) {
-        const auto& w = work[i];
-        return std::min(w.page_end * block_tokens, int(lengths[w.row])) - w.page_begin * block_tokens;
-    };
-    std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return tokens(a) > tokens(b); });
+    if (pages_per_split <= 0) {
+        order.push_back(0);
+        runs = mpb::plan_static_runs(
+            count, pages_of,
+            [&](int r, int b, int e, int k) {
+                if (k == 0) host[3 * count + r] = int(work.size());  // first work item
+                host[2 * count + r] = k + 1;                         // splits
+                work.push_back({r, b, e, k});
+            },
+            [&](int, int items) { order.push_back(items); });
+    } else {
+        const int pps = pages_per_split;
+        for (int r = 0; r < count; ++r) {
+            const int n = std::max(1, (pages_of(r) + pps - 1) / pps);
+            host[2 * count + r] = n;                 // splits
+            host[3 * count + r] = int(work.size());  // first work item
+            for (int k = 0; k < n; ++k) work.push_back({r, k * pps, std::min(pages_of(r), (k + 1) * pps), k});
+        }
+        // processing order of the persistent kernel: longest slices first
+        order.resize(work.size());
+        for (size_t i = 0; i < order.size(); ++i) order[i] = int32_t(i);
+        auto tokens = [&](int32_t i) {
+            const auto& w = work[i];
+            return std::min(w.page_end * block_tokens, int(lengths[w.row])) - w.page_begin * block_tokens;
+        };
+        std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return tokens(a) > tokens(b); });
+    }
     const size_t words = host.size() + 4 * work.size() + order.size();
     cudaError_t e = grow(s.meta, s.meta_capacity, words, stream, false);
     if (e == cudaSuccess) e = grow(s.partial, s.partial_capacity, work.size() * mpb::kHeads * (mpb::kHeadDim + 2),
@@ -137,7 +150,10 @@ extern "C" int mp_paged_attention_decode(const float* q, const float* keys, cons
     p.row_work0 = s.meta + 3 * count;
     p.work = reinterpret_cast<const mpb::AttnWork*>(s.meta + 4 * count);
     p.work_count = int(work.size());
-    p.order = s.meta + 4 * count + 4 * work.size();
+    const int32_t* tail = s.meta + 4 * count + 4 * work.size();  // order, or the runs' first items
+    p.order = runs ? nullptr : tail;
+    p.cta_items = runs ? tail : nullptr;
+    p.cta_count = runs;
     p.partial = s.partial;
     p.counters = s.counters;
     p.sched = s.sched;

@@ -85,20 +85,17 @@ extern "C" int mp_paged_attention_decode_noalloc(const float* q, const float* ke
         }
         total_pages += (lengths[i] + block_tokens - 1) / block_tokens;
     }
-    // Slices: the decode operator's own choice when it fits, else the shortest
-    // slice length (in pages) whose slice count fits kMaxWork.
+    // Slices. pages_per_split 0: one equal run of pages per CTA
+    // (mpb::plan_static_runs: at most kMaxRows + kAttnPersistentCtas items, which
+    // fits kMaxWork); else slices of that many pages, pulled longest first.
     auto slices = [&](int pps) {
         long long n = 0;
         for (int i = 0; i < count; ++i) n += std::max(1, ((lengths[i] + block_tokens - 1) / block_tokens + pps - 1) / pps);
         return n;
     };
-    int pps = pages_per_split;
-    if (pps == 0) {
-        long long total_tokens = 0;
-        for (int i = 0; i < count; ++i) total_tokens += lengths[i];
-        pps = mpb::auto_pages_per_split(total_tokens, block_tokens);
-        while (slices(pps) > kMaxWork) pps *= 2;
-    } else if (slices(pps) > kMaxWork) {
+    static_assert(kMaxRows + mpb::kAttnPersistentCtas <= kMaxWork, "static runs fit the work list");
+    const int pps = pages_per_split;
+    if (pps != 0 && slices(pps) > kMaxWork) {
         mpb::set_last_error("mp_paged_attention_decode_noalloc: more than 2048 slices; raise pages_per_split");
         return MP_ERR_INVALID;
     }
@@ -130,24 +127,41 @@ extern "C" int mp_paged_attention_decode_noalloc(const float* q, const float* ke
     int work = 0;
     int32_t* rows = g_host_meta;
     int32_t* items = g_host_meta + 4 * count;
+    auto pages_of = [&](int r) { return (lengths[r] + block_tokens - 1) / block_tokens; };
+    auto emit = [&](int r, int b, int e, int k) {
+        if (k == 0) rows[3 * count + r] = work;
+        rows[2 * count + r] = k + 1;
+        items[4 * work] = r;
+        items[4 * work + 1] = b;
+        items[4 * work + 2] = e;
+        items[4 * work + 3] = k;
+        ++work;
+    };
     for (int r = 0; r < count; ++r) {
-        const int pages = (lengths[r] + block_tokens - 1) / block_tokens;
-        const int n = std::max(1, (pages + pps - 1) / pps);
         rows[r] = r;
         rows[count + r] = lengths[r];
-        rows[2 * count + r] = n;
-        rows[3 * count + r] = work;
-        for (int k = 0; k < n; ++k, ++work) {
-            items[4 * work] = r;
-            items[4 * work + 1] = k * pps;
-            items[4 * work + 2] = std::min(pages, (k + 1) * pps);
-            items[4 * work + 3] = k;
+    }
+    int runs = 0;
+    int32_t* order = nullptr;  // after the work list: the longest-first order, or the runs' first items
+    if (pps == 0) {
+        // the runs' first items follow the work list, whose final length is only
+        // known at the end: collect them at the top of the order region's maximum
+        // extent, then move them down
+        int32_t* starts = g_host_meta + 4 * count + 4 * kMaxWork;
+        starts[0] = 0;
+        runs = mpb::plan_static_runs(count, pages_of, emit, [&](int c, int it) { starts[c] = it; });
+        order = items + 4 * work;
+        std::memmove(order, starts, size_t(runs + 1) * sizeof(int32_t));
+    } else {
+        for (int r = 0; r < count; ++r) {
+            const int n = std::max(1, (pages_of(r) + pps - 1) / pps);
+            for (int k = 0; k < n; ++k) emit(r, k * pps, std::min(pages_of(r), (k + 1) * pps), k);
         }
+        order = items + 4 * work;
     }
     // processing order of the persistent kernel: longest slices first (insertion
     // sort into the fixed array; at most kMaxWork items)
-    int32_t* order = items + 4 * work;
-    for (int i = 0; i < work; ++i) {
+    for (int i = 0; i < (runs ? 0 : work); ++i) {
         auto tokens = [&](int k) {
             return std::min(items[4 * k + 2] * block_tokens, int(lengths[items[4 * k]])) - items[4 * k + 1] * block_tokens;
         };
@@ -160,7 +174,8 @@ extern "C" int mp_paged_attention_decode_noalloc(const float* q, const float* ke
         order[j] = i;
     }
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-    cudaError_t e = cudaMemcpyAsync(meta, g_host_meta, size_t(4 * count + 5 * work) * sizeof(int32_t),
+    const size_t tail = runs ? size_t(runs) + 1 : size_t(work);
+    cudaError_t e = cudaMemcpyAsync(meta, g_host_meta, (size_t(4 * count + 4 * work) + tail) * sizeof(int32_t),
                                     cudaMemcpyHostToDevice, stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(counters, 0, size_t(count) * mpb::kKvHeads * sizeof(unsigned), stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(sched, 0, 2 * sizeof(unsigned), stream);
@@ -187,7 +202,9 @@ extern "C" int mp_paged_attention_decode_noalloc(const float* q, const float* ke
     p.row_work0 = meta + 3 * count;
     p.work = reinterpret_cast<const mpb::AttnWork*>(meta + 4 * count);
     p.work_count = work;
-    p.order = meta + 4 * count + 4 * work;
+    p.order = runs ? nullptr : meta + 4 * count + 4 * work;
+    p.cta_items = runs ? meta + 4 * count + 4 * work : nullptr;
+    p.cta_count = runs;
     p.partial = partial;
     p.counters = counters;
     p.sched = sched;

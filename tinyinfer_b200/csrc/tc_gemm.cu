@@ -97,20 +97,23 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 
 // Fused epilogue over rows [r0, r1) of the tile, columns in parallel (coalesced).
 // Each output float4 is the sum over the cluster's slices, in slice order, of the
-// staged tiles at the same offset; a thread takes kUnroll outputs per round and
-// issues all their loads of one slice before adding, so loads overlap.
+// staged tiles at the same offset. A thread takes kUnroll outputs per round and
+// issues the loads of every slice (and the residual it adds to) before the first
+// add, so the cluster-shared-memory round trips overlap instead of queueing.
 //  Store  : c[row][n0 + j] = acc
 //  AddTo  : c[row][n0 + j] += acc                        (residual add)
 //  SwiGLU : per 64-column group g of the tile, columns 0..31 are gate and 32..63 up
 //           of output columns (n0 + 64 g) / 2 + 0..31; writes h = silu(gate) * up as
 //           TF32 hi/lo halves (the down projection's input).
-constexpr int kUnroll = 4;
+template <Epilogue E>
+__host__ __device__ constexpr int epilogue_unroll() { return E == Epilogue::SwiGLU ? 2 : 4; }
 
 template <int BN, Epilogue E>
 __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float* tile, int m0, int n0, int r0,
                                               int r1, int slices) {
     using Cfg = TcConfig<BN>;
     constexpr bool kSwiGLU = E == Epilogue::SwiGLU;
+    constexpr int kUnroll = epilogue_unroll<E>();
     // items per row: float4 of the tile (Store/AddTo) or of the gate halves (SwiGLU)
     constexpr int kItems = kSwiGLU ? (BN / 64) * 8 : BN / 4;
     constexpr int kLoads = kSwiGLU ? 2 : 1;  // gate and up
@@ -118,43 +121,51 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
     for (int base = threadIdx.x; base < total; base += kThreads * kUnroll) {
         int off[kUnroll];
         bool live[kUnroll];
+        float4* dst[kUnroll];
+        float4 resid[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             const int i = base + u * kThreads;
-            live[u] = i < total;
-            const int row = r0 + (live[u] ? i / kItems : 0), it = i % kItems;
+            const int row = r0 + (i < total ? i / kItems : 0), it = i % kItems;
+            live[u] = i < total && m0 + row < p.m;
             off[u] = row * Cfg::kTileStride + (kSwiGLU ? 64 * (it / 8) + 4 * (it % 8) : 4 * it);
+            dst[u] = nullptr;
+            if (!kSwiGLU) {
+                dst[u] = reinterpret_cast<float4*>(p.c + size_t(m0 + row) * p.ldc + n0 + 4 * it);
+                if (E == Epilogue::AddTo && live[u]) resid[u] = *dst[u];
+            }
         }
-        float4 acc[kUnroll][kLoads];
-        for (int k = 0; k < slices; ++k) {
-            float4 v[kUnroll][kLoads];
+        float4 v[kMaxSlices][kUnroll][kLoads];
+#pragma unroll
+        for (int k = 0; k < kMaxSlices; ++k)
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u)
 #pragma unroll
                 for (int h = 0; h < kLoads; ++h) {
                     const float* at = tile + off[u] + 32 * h;
-                    v[u][h] = slices == 1 ? *reinterpret_cast<const float4*>(at) : ld_cluster(at, uint32_t(k));
+                    if (k < slices)
+                        v[k][u][h] = slices == 1 ? *reinterpret_cast<const float4*>(at) : ld_cluster(at, uint32_t(k));
                 }
+        float4 acc[kUnroll][kLoads];
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u)
+        for (int u = 0; u < kUnroll; ++u)
 #pragma unroll
-                for (int h = 0; h < kLoads; ++h) {
-                    if (k == 0) {
-                        acc[u][h] = v[u][h];
-                    } else {
-                        acc[u][h].x += v[u][h].x;
-                        acc[u][h].y += v[u][h].y;
-                        acc[u][h].z += v[u][h].z;
-                        acc[u][h].w += v[u][h].w;
+            for (int h = 0; h < kLoads; ++h) {
+                acc[u][h] = v[0][u][h];
+#pragma unroll
+                for (int k = 1; k < kMaxSlices; ++k)
+                    if (k < slices) {
+                        acc[u][h].x += v[k][u][h].x;
+                        acc[u][h].y += v[k][u][h].y;
+                        acc[u][h].z += v[k][u][h].z;
+                        acc[u][h].w += v[k][u][h].w;
                     }
-                }
-        }
+            }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             if (!live[u]) continue;
             const int i = base + u * kThreads;
             const int row = r0 + i / kItems, it = i % kItems;
-            if (m0 + row >= p.m) continue;
             if (kSwiGLU) {
                 const float4 gt = acc[u][0], up = acc[u][kLoads - 1];
                 const float o[4] = {silu_mul(gt.x, up.x), silu_mul(gt.y, up.y), silu_mul(gt.z, up.z),
@@ -162,18 +173,17 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
                 float hv[4], lv[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) split_tf32(o[e], hv[e], lv[e]);
-                const size_t dst = size_t(m0 + row) * p.ld_out + (n0 + 64 * (it / 8)) / 2 + 4 * (it % 8);
-                *reinterpret_cast<float4*>(p.out_hi + dst) = make_float4(hv[0], hv[1], hv[2], hv[3]);
-                *reinterpret_cast<float4*>(p.out_lo + dst) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+                const size_t at = size_t(m0 + row) * p.ld_out + (n0 + 64 * (it / 8)) / 2 + 4 * (it % 8);
+                *reinterpret_cast<float4*>(p.out_hi + at) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+                *reinterpret_cast<float4*>(p.out_lo + at) = make_float4(lv[0], lv[1], lv[2], lv[3]);
             } else {
-                const float4 v = acc[u][0];
-                float4* dst = reinterpret_cast<float4*>(p.c + size_t(m0 + row) * p.ldc + n0 + 4 * it);
+                const float4 a = acc[u][0];
                 if (E == Epilogue::Store) {
-                    *dst = v;
+                    *dst[u] = a;
                 } else {
-                    const float4 x = *dst;
-                    *dst = make_float4(__fadd_rn(x.x, v.x), __fadd_rn(x.y, v.y), __fadd_rn(x.z, v.z),
-                                       __fadd_rn(x.w, v.w));
+                    const float4 x = resid[u];
+                    *dst[u] = make_float4(__fadd_rn(x.x, a.x), __fadd_rn(x.y, a.y), __fadd_rn(x.z, a.z),
+                                          __fadd_rn(x.w, a.w));
                 }
             }
         }
