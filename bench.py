@@ -62,6 +62,8 @@ def parse():
                    help="config3: the headline decode benchmark; config4 / config5: the serving workloads "
                         "of bench_serving.py")
     p.add_argument("--serve-requests", type=int, default=2048, help="config 5 request count")
+    p.add_argument("--shared-prefix-kernel", action="store_true",
+                   help="serve shared prefix pages with the tensor-core shared-prefix kernel (off by default)")
     return p.parse_args()
 
 
@@ -253,6 +255,8 @@ def run_b200(args, rank, world, local_rank):
     del weights
     engine = Engine(runner, n, args.prefill_budget, args.prompt, cfg.context)
     dev = engine.device()
+    if args.shared_prefix_kernel:
+        dev.shared_prefix(8, 128)
     # this GPU's shard of the world's requests (round-robin, no collective)
     mine = router.round_robin(n * world, world, rank)
     ps = prompts(args, mine)
@@ -332,10 +336,12 @@ def run_b200(args, rank, world, local_rank):
 
     hbm, peak_kind = peaks()
     launch_ms = attn_ms / max(attn_launches, 1)
-    bytes_per_launch = attn_bytes / max(attn_launches, 1)
-    unique_per_launch = uniq
+    # DRAM-level algorithmic bytes of one layer's decode attention: every distinct
+    # K/V row once (the shared prefix pages are read by all rows but come from
+    # DRAM once, then L2), plus each row's query and output
+    bytes_per_launch = uniq + n * 2 * 576 * 4
     achieved = bytes_per_launch / (launch_ms * 1e-3) / 1e9 if launch_ms > 0 else None
-    traffic = None
+    traffic, traffic_source = None, None
     # DRAM bytes per launch from the committed ncu capture of the same kernel on the
     # same rows, scaled to this run's algorithmic bytes per launch
     tpath = os.path.join(ROOT, "profiles", "paged_attention_decode_config3_traffic.json")
@@ -344,6 +350,7 @@ def run_b200(args, rank, world, local_rank):
             with open(tpath) as f:
                 t = json.load(f)
             traffic = t["dram_bytes_per_launch"] * bytes_per_launch / t["algorithmic_bytes_per_launch"]
+            traffic_source = t.get("source")
         except Exception:
             traffic = None
     line = {
@@ -363,6 +370,8 @@ def run_b200(args, rank, world, local_rank):
                                "prefix reused with COW of its partial page",
                    "model": "SmolLM2-135M shape, 30 layers, FP32, tied head", "requests_per_gpu": args.requests,
                    "prompt_tokens": args.prompt, "shared_prefix_tokens": args.shared, "block_tokens": bt,
+                   "shared_prefix_path": "tensor-core shared-prefix kernel" if args.shared_prefix_kernel else
+                                         "every row reads its whole context (shared pages from L2)",
                    "prefix_cache_blocks": args.prefix_blocks, "parallelism": f"request-sharded replicas x{world}",
                    "routing": "round-robin by global request index; each GPU its own weights, KV pool, "
                               "prefix cache and engine; no collective in a step",
@@ -377,15 +386,15 @@ def run_b200(args, rank, world, local_rank):
                 "host_ms_per_step": {k: counters[f"host_{k}_ms"] / args.steps for k in ("prepare", "launch", "wait")}},
         "gpu_launches": int(counters["kernel_launches"]),
         "roofline": {"bound": "hbm",
-                     "kernel": "decode attention: prefix_attention_kernel (shared pages, tcgen05) + "
-                               "paged_attention_kernel (rows' own pages, split-K), timed together per layer",
+                     "kernel": "paged_attention_kernel: split-K decode attention of every row over its whole "
+                               "context; the shared prefix pages are read by all rows, from DRAM once and then L2",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm if achieved else None, "traffic": traffic,
+                     "traffic_source": traffic_source,
                      "peak_kind": peak_kind, "launch_ms": launch_ms, "launches": attn_launches,
                      "algorithmic_bytes_per_launch": bytes_per_launch,
-                     "unique_bytes_per_launch": unique_per_launch,
                      "logical_bytes_per_launch": logical,
-                     "unique_achieved": unique_per_launch / (launch_ms * 1e-3) / 1e9 if launch_ms > 0 else None,
+                     "logical_achieved": logical / (launch_ms * 1e-3) / 1e9 if launch_ms > 0 else None,
                      "attention_share_of_forward": attn_ms / device_ms if device_ms else None},
         "clocks": clocks.summary(),
     }

@@ -6,7 +6,9 @@ with the same physical pages and the forward serves those tokens once for the
 whole group. Every follower's greedy stream must equal the C oracle's, which
 recomputes each history from an empty pool; the device counters must show that
 the shared-prefix path ran. Cases cover token chunks that end inside a 32-token
-tile, query blocks past 64 vectors, and page sizes 8 and 16.
+tile, query blocks past 64 vectors, and page sizes 8 and 16. The path is opt-in
+(mp_set_shared_prefix); by default every row reads the shared pages itself, and
+the last case checks that the default leaves it unused with the same streams.
 """
 import numpy as np
 import pytest
@@ -16,8 +18,9 @@ from tinyinfer_b200.synthetic import ModelConfig, random_weights
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("shared,followers,bt", [(300, 24, 16), (136, 8, 16), (523, 12, 8)])
-def test_shared_prefix_streams_match_oracle(built, shared, followers, bt):
+@pytest.mark.parametrize("shared,followers,bt,enabled", [(300, 24, 16, True), (136, 8, 16, True), (523, 12, 8, True),
+                                                         (300, 24, 16, False)])
+def test_shared_prefix_streams_match_oracle(built, shared, followers, bt, enabled):
     from tinyinfer_b200.host import Engine, Runner
 
     context = 640
@@ -47,6 +50,8 @@ def test_shared_prefix_streams_match_oracle(built, shared, followers, bt):
         prompts[f"f{i}"] = prefix + [int(t) for t in rng.integers(0, 64, int(rng.integers(1, 20)))]
         engine.submit(f"f{i}", prompts[f"f{i}"], 6)
     dev = engine.device()
+    if enabled:
+        dev.shared_prefix(8, 128)
     dev.counters(reset=True)
     outputs = {}
     while not engine.idle():
@@ -56,8 +61,11 @@ def test_shared_prefix_streams_match_oracle(built, shared, followers, bt):
             if tok is not None:
                 outputs.setdefault(rid, []).append(tok)
     counters = dev.counters(reset=True)
-    assert counters["shared_prefix_rows"] > 0, counters
-    assert counters["shared_prefix_tokens"] >= (shared // bt) * bt * followers
+    if enabled:
+        assert counters["shared_prefix_rows"] > 0, counters
+        assert counters["shared_prefix_tokens"] >= (shared // bt) * bt * followers
+    else:
+        assert counters["shared_prefix_rows"] == 0 and counters["shared_prefix_tokens"] == 0, counters
     for rid, p in prompts.items():
         seq = list(p)
         assert len(outputs[rid]) == 6

@@ -70,13 +70,15 @@ T* host_alloc(size_t count, const char* what) {
 //  * Decode rows (sequences appending fewer than kPrefillMinRows rows): each
 //    row's context pages are cut into slices of `pages_per_split` pages
 //    (0: mpb::auto_pages_per_split over all decode rows' tokens).
-//  * Shared prefixes: decode rows whose block tables begin with the same physical
-//    pages (prefix reuse, forks) form a group when at least kGroupMinRows rows
-//    share at least kGroupMinTokens tokens of full pages. The group's shared
-//    tokens become prefix work (attention_shared.cu, one CTA per kv head x 64
-//    query vectors x chunk) and each row's slices start after them. A page that
-//    holds a row's newest token is never shared (it was just written), so only
-//    pages before it count.
+//  * Shared prefixes (only when enabled with mp_set_shared_prefix): decode rows
+//    whose block tables begin with the same physical pages (prefix reuse, forks)
+//    form a group when at least `group_min_rows` rows share at least
+//    `group_min_tokens` tokens of full pages. The group's shared tokens become
+//    prefix work (attention_shared.cu, one CTA per kv head x 128 query vectors x
+//    chunk) and each row's slices start after them. A page that holds a row's
+//    newest token is never shared (it was just written), so only pages before it
+//    count. Off by default: every row reading the shared pages itself, which
+//    then stay in L2, measured faster on B200.
 //  * Prefill sequences: one work item per (64-row tile, kv head).
 struct AttnPlan {
     std::vector<int32_t> splits, work0, x0, nx;
@@ -90,15 +92,16 @@ struct AttnPlan {
     double logical_bytes = 0;  // the same with every row reading its whole context
 };
 
-constexpr int kGroupMinRows = 8;
-constexpr int kGroupMinTokens = 128;
+constexpr int kGroupMinTokensFloor = 16;  // smallest shared span worth a group
 constexpr int kPrefixMaxChunks = 64;
 constexpr double kPrefixTargetCtas = 148.0;  // one wave (one CTA per SM)
 
 // tables: host mirror of the device block tables ([slots][table_stride]).
+// group_min_rows 0: no shared-prefix groups.
 void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, int table_stride,
                     const std::vector<int32_t>& tables, int pages_per_split, size_t extra_capacity,
-                    size_t prefix_capacity, AttnPlan& plan) {
+                    size_t prefix_capacity, int group_min_rows, int group_min_tokens, AttnPlan& plan) {
+    group_min_tokens = std::max(group_min_tokens, kGroupMinTokensFloor);
     int rows = 0;
     for (int i = 0; i < count; ++i) rows += seqs[i].count;
     plan.splits.assign(rows, 0);
@@ -137,7 +140,7 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
         std::vector<std::pair<int32_t, int>> keyed;  // (first page, index into decode)
         for (int i = 0; i < int(decode.size()); ++i) {
             const int full = (decode[i].len - 1) / block_tokens;
-            if (full * block_tokens >= kGroupMinTokens)
+            if (group_min_rows > 0 && full * block_tokens >= group_min_tokens)
                 keyed.push_back({tables[size_t(decode[i].slot) * table_stride], i});
         }
         std::stable_sort(keyed.begin(), keyed.end(),
@@ -151,7 +154,7 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
         for (size_t b = 0; b < keyed.size();) {
             size_t e = b;
             while (e < keyed.size() && keyed[e].first == keyed[b].first) ++e;
-            if (int(e - b) >= kGroupMinRows && keyed[b].first >= 0) {
+            if (int(e - b) >= group_min_rows && keyed[b].first >= 0) {
                 const DecodeRow& ref = decode[keyed[b].second];
                 const int32_t* rt = tables.data() + size_t(ref.slot) * table_stride;
                 int lcp = (ref.len - 1) / block_tokens;
@@ -165,7 +168,7 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
                             break;
                         }
                 }
-                if (lcp * block_tokens >= kGroupMinTokens) candidates.push_back({b, e, lcp});
+                if (lcp * block_tokens >= group_min_tokens) candidates.push_back({b, e, lcp});
             }
             b = e;
         }
@@ -354,6 +357,7 @@ struct mp_context {
     AttnPlan plan;
     // attention profiling
     bool profile = false;
+    int group_min_rows = 0, group_min_tokens = 128;  // shared-prefix path (mp_set_shared_prefix)
     std::vector<cudaEvent_t> prof_events;
     int prof_used = 0;
     float prof_ms = 0.f;
@@ -935,7 +939,7 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
             }
         } mirror_guard{c->h_tables, mirror_undo};
         plan_attention(seqs, count, r.block_tokens, r.table_stride, c->h_tables, 0, c->extra_capacity,
-                       c->prefix_capacity, c->plan);
+                       c->prefix_capacity, c->group_min_rows, c->group_min_tokens, c->plan);
         const size_t W = c->plan.work.size(), P = c->plan.prefill.size(), X = c->plan.prefix.size();
         const size_t G = c->plan.group_slot.size();
         if (W > c->work_capacity) fail(MP_ERR_INVALID, "attention work list exceeds capacity");
@@ -1371,6 +1375,13 @@ int mp_cow_elapsed(mp_context* c, float* ms) {
     if (!c || !ms) return MP_ERR_INVALID;
     *ms = c->cow_ms;
     c->cow_ms = 0.f;
+    return MP_OK;
+}
+
+int mp_set_shared_prefix(mp_context* c, int32_t min_rows, int32_t min_tokens) {
+    if (!c || min_rows < 0 || min_tokens < 0) return MP_ERR_INVALID;
+    c->group_min_rows = min_rows;
+    c->group_min_tokens = min_tokens;
     return MP_OK;
 }
 

@@ -94,6 +94,7 @@ def library() -> C.CDLL:
         lib.mp_timer_mark.argtypes = [C.c_void_p]
         lib.mp_timer_elapsed.argtypes = [C.c_void_p, C.POINTER(C.c_float)]
         lib.mp_profile_enable.argtypes = [C.c_void_p, C.c_int32]
+        lib.mp_set_shared_prefix.argtypes = [C.c_void_p, C.c_int32, C.c_int32]
         lib.mp_profile_read.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_int32),
                                         C.POINTER(C.c_double)]
         lib.mp_paged_attention_decode.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
@@ -242,6 +243,10 @@ class DeviceContext:
         check(self.lib.mp_profile_read(self.h, C.byref(ms), C.byref(n), C.byref(b)))
         return ms.value, n.value, b.value
 
+    def shared_prefix(self, min_rows: int, min_tokens: int = 128) -> None:
+        """Shared-prefix attention for groups of >= min_rows rows (0: off, the default)."""
+        check(self.lib.mp_set_shared_prefix(self.h, min_rows, min_tokens))
+
 
 class ContextView:
     """Timing and counters of a device context owned elsewhere (e.g. by an engine)."""
@@ -270,6 +275,10 @@ class ContextView:
         out = CountersC()
         check(self.lib.mp_read_counters(self.h, C.byref(out), int(reset)))
         return {k: getattr(out, k) for k, _ in CountersC._fields_}
+
+    def shared_prefix(self, min_rows: int, min_tokens: int = 128) -> None:
+        """Shared-prefix attention for groups of >= min_rows rows (0: off, the default)."""
+        check(self.lib.mp_set_shared_prefix(self.h, min_rows, min_tokens))
 
     def sync(self, timeout_ms: int = 600000) -> None:
         check(self.lib.mp_sync(self.h, timeout_ms))
