@@ -199,11 +199,10 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
                          uint64_t* empty, float* probs, unsigned* failed, int kh, int lane) {
     const int t = lane >> 2, c = lane & 3;
     float4 qr[kGroup][4];
-    float m_run[kGroup], l_run[kGroup], acc[kGroup][2];
+    // softmax state of head c (lanes with c == 3 carry an unused copy)
+    float m_run = -INFINITY, l_run = 0.f, acc[kGroup][2];
 #pragma unroll
     for (int hh = 0; hh < kGroup; ++hh) {
-        m_run[hh] = -INFINITY;
-        l_run[hh] = 0.f;
         acc[hh][0] = acc[hh][1] = 0.f;
 #pragma unroll
         for (int j = 0; j < 4; ++j) qr[hh][j] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -224,17 +223,17 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                     qr[hh][j] = *reinterpret_cast<const float4*>(qrow + hh * kHeadDim + c * 16 + 4 * ((j + t) & 3));
-                m_run[hh] = -INFINITY;
-                l_run[hh] = 0.f;
                 acc[hh][0] = acc[hh][1] = 0.f;
             }
+            m_run = -INFINITY;
+            l_run = 0.f;
         }
         const float* kst = stages + 2 * buf * kStageFloats + kh * kHeadDim + c * 16;
         const float* vst = stages + (2 * buf + 1) * kStageFloats + kh * kHeadDim + lane;
         const bool full_stage = d.n_valid == kStageTokens;
-        // scores of tokens t + 8 ps for the 3 heads, in base-2 units
-        // (dot / 8 * log2 e); even / odd dims in the two halves of a packed FMA
-        float s[kPasses][kGroup];
+        // Q.K partial sums of tokens t + 8 ps over this lane's quarter of the dims,
+        // for the 3 heads (even / odd dims in the two halves of a packed FMA)
+        float x[kPasses][4];
 #pragma unroll
         for (int ps = 0; ps < kPasses; ++ps) {
             const float* krow = kst + (t + 8 * ps) * kKvWidth;
@@ -248,45 +247,63 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
                     fma2(pe[hh], po[hh], qr[hh][j].z, qr[hh][j].w, kv.z, kv.w);
                 }
             }
-            const bool valid = full_stage || t + 8 * ps < d.n_valid;
 #pragma unroll
-            for (int hh = 0; hh < kGroup; ++hh) {
-                float part = pe[hh] + po[hh];
-                part += __shfl_xor_sync(0xffffffffu, part, 1);
-                part += __shfl_xor_sync(0xffffffffu, part, 2);
-                s[ps][hh] = valid ? part * (0.125f * kLog2e) : -INFINITY;
-            }
+            for (int hh = 0; hh < kGroup; ++hh) x[ps][hh] = pe[hh] + po[hh];
+            x[ps][3] = 0.f;
         }
-        // online softmax over the stage's tokens (lanes differ in t across bits 2..4)
+        // Reduce-scatter over the 4 quarter lanes of a token: lane c ends with the
+        // full score of head c (c = 3: an unused fourth slot). Pairs xor 1 first,
+        // then xor 2, so each sum is ((q0 + q1) + (q2 + q3)) in quarter order.
+        const bool odd = c & 1, high = c & 2;
+        float s[kPasses];
 #pragma unroll
-        for (int hh = 0; hh < kGroup; ++hh) {
-            float mx = s[0][hh];
+        for (int ps = 0; ps < kPasses; ++ps) {
+            // lanes with even c keep heads {0, 2}, odd c heads {1, 3}
+            const float k0 = odd ? x[ps][1] : x[ps][0], k1 = odd ? x[ps][3] : x[ps][2];
+            const float g0 = odd ? x[ps][0] : x[ps][1], g1 = odd ? x[ps][2] : x[ps][3];
+            const float y0 = k0 + __shfl_xor_sync(0xffffffffu, g0, 1);
+            const float y1 = k1 + __shfl_xor_sync(0xffffffffu, g1, 1);
+            // c < 2 keep the first of the pair (head 0 or 1), c >= 2 the second (head 2 or 3)
+            const float keep = high ? y1 : y0, give = high ? y0 : y1;
+            const float part = keep + __shfl_xor_sync(0xffffffffu, give, 2);
+            const bool valid = full_stage || t + 8 * ps < d.n_valid;
+            s[ps] = valid ? part * (0.125f * kLog2e) : -INFINITY;  // base-2 units
+        }
+        // online softmax of head c over the stage's tokens (lanes differ in t across bits 2..4)
+        float alpha;
+        {
+            float mx = s[0];
 #pragma unroll
-            for (int ps = 1; ps < kPasses; ++ps) mx = fmaxf(mx, s[ps][hh]);
+            for (int ps = 1; ps < kPasses; ++ps) mx = fmaxf(mx, s[ps]);
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-            const float m_new = fmaxf(m_run[hh], mx);
+            const float m_new = fmaxf(m_run, mx);
             const float ms = m_new == -INFINITY ? 0.f : m_new;  // no valid token yet: all terms stay 0
-            const float alpha = exp2f(m_run[hh] - ms);
+            alpha = exp2f(m_run - ms);
             float pw[kPasses];
             float sum = 0.f;
 #pragma unroll
             for (int ps = 0; ps < kPasses; ++ps) {
-                pw[ps] = exp2f(s[ps][hh] - ms);
+                pw[ps] = exp2f(s[ps] - ms);
                 sum += pw[ps];
             }
             sum += __shfl_xor_sync(0xffffffffu, sum, 4);
             sum += __shfl_xor_sync(0xffffffffu, sum, 8);
             sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-            l_run[hh] = l_run[hh] * alpha + sum;
-            m_run[hh] = m_new;
-            acc[hh][0] *= alpha;
-            acc[hh][1] *= alpha;
-            if (c == 0) {
+            l_run = l_run * alpha + sum;
+            m_run = m_new;
+            if (c < kGroup) {
 #pragma unroll
-                for (int ps = 0; ps < kPasses; ++ps) probs[hh * kStageTokens + t + 8 * ps] = pw[ps];
+                for (int ps = 0; ps < kPasses; ++ps) probs[c * kStageTokens + t + 8 * ps] = pw[ps];
             }
+        }
+        // every lane rescales its dims of all 3 heads: head hh's factor from lane hh
+#pragma unroll
+        for (int hh = 0; hh < kGroup; ++hh) {
+            const float a = __shfl_sync(0xffffffffu, alpha, hh);
+            acc[hh][0] *= a;
+            acc[hh][1] *= a;
         }
         __syncwarp();
         // P.V: dims (lane, lane + 32) of this kv head, one packed FMA per head and token
@@ -320,9 +337,10 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
         if (splits == 1 && nx == 0) {
 #pragma unroll
             for (int hh = 0; hh < kGroup; ++hh) {
+                const float l = __shfl_sync(0xffffffffu, l_run, hh);
                 const size_t o = size_t(row) * p.out_stride + (kh * kGroup + hh) * kHeadDim;
-                write_out(p, o + lane, acc[hh][0] / l_run[hh]);
-                write_out(p, o + lane + 32, acc[hh][1] / l_run[hh]);
+                write_out(p, o + lane, acc[hh][0] / l);
+                write_out(p, o + lane + 32, acc[hh][1] / l);
             }
             continue;
         }
@@ -331,10 +349,11 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
             float* part = p.partial + (size_t(d.work) * kHeads + kh * kGroup + hh) * (kHeadDim + 2);
             part[2 + lane] = acc[hh][0];
             part[2 + lane + 32] = acc[hh][1];
-            if (lane == 0) {
-                part[0] = m_run[hh];
-                part[1] = l_run[hh];
-            }
+        }
+        if (lane < kGroup) {  // lane hh (t = 0, c = hh) holds head hh's max and sum
+            float* part = p.partial + (size_t(d.work) * kHeads + kh * kGroup + lane) * (kHeadDim + 2);
+            part[0] = m_run;
+            part[1] = l_run;
         }
         __threadfence();
         __syncwarp();
