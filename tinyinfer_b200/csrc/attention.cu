@@ -27,12 +27,12 @@
 //    keeps its 3 heads' 16 query values (rotated by t so a 128-bit phase spans all
 //    banks) in registers. Scores are reduced over the quarters by shuffles, the
 //    online softmax over the 16 tokens by shuffles, probabilities go through a
-//    per-warp scratch row, and P.V accumulates dims (lane, lane + 32) of 3 heads.
+//    per-warp scratch row, and P.V accumulates dims (2 lane, 2 lane + 1) of 3 heads.
 //  * Each consumer finishes a slice on its own: direct output for a single-slice
 //    row, else its partial (max, sum, unnormalised output) and the merge when it
 //    is the last arrival for (row, its kv head).
 //  * Arithmetic: packed FP32 FMAs (fma.rn.f32x2) for Q.K (even / odd dims) and
-//    P.V (dims lane / lane + 32); softmax weights as exp2 of scores scaled by
+//    P.V (dims 2 lane / 2 lane + 1); softmax weights as exp2 of scores scaled by
 //    log2(e) / 8, so maxima in partials are base-2 quantities.
 // Every wait is bounded (common.cuh); a timeout sets the error word and the warp
 // stops. Tokens past the row length are masked by select (never by multiplying).
@@ -229,7 +229,7 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
             l_run = 0.f;
         }
         const float* kst = stages + 2 * buf * kStageFloats + kh * kHeadDim + c * 16;
-        const float* vst = stages + (2 * buf + 1) * kStageFloats + kh * kHeadDim + lane;
+        const float* vst = stages + (2 * buf + 1) * kStageFloats + kh * kHeadDim + 2 * lane;
         const bool full_stage = d.n_valid == kStageTokens;
         // Q.K partial sums of tokens t + 8 ps over this lane's quarter of the dims,
         // for the 3 heads (even / odd dims in the two halves of a packed FMA)
@@ -306,7 +306,7 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
             acc[hh][1] *= a;
         }
         __syncwarp();
-        // P.V: dims (lane, lane + 32) of this kv head, one packed FMA per head and token
+        // P.V: dims (2 lane, 2 lane + 1) of this kv head, one packed FMA per head and token
 #pragma unroll
         for (int q4 = 0; q4 < kStageTokens / 4; ++q4) {
             float4 pr[kGroup];
@@ -316,7 +316,8 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const int tt = 4 * q4 + u;
-                float v0 = vst[tt * kKvWidth], v1 = vst[tt * kKvWidth + 32];
+                const float2 vv = *reinterpret_cast<const float2*>(vst + tt * kKvWidth);
+                float v0 = vv.x, v1 = vv.y;
                 if (!full_stage && tt >= d.n_valid) v0 = v1 = 0.f;
 #pragma unroll
                 for (int hh = 0; hh < kGroup; ++hh) {
@@ -339,16 +340,16 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
             for (int hh = 0; hh < kGroup; ++hh) {
                 const float l = __shfl_sync(0xffffffffu, l_run, hh);
                 const size_t o = size_t(row) * p.out_stride + (kh * kGroup + hh) * kHeadDim;
-                write_out(p, o + lane, acc[hh][0] / l);
-                write_out(p, o + lane + 32, acc[hh][1] / l);
+                write_out(p, o + 2 * lane, acc[hh][0] / l);
+                write_out(p, o + 2 * lane + 1, acc[hh][1] / l);
             }
             continue;
         }
 #pragma unroll
         for (int hh = 0; hh < kGroup; ++hh) {
             float* part = p.partial + (size_t(d.work) * kHeads + kh * kGroup + hh) * (kHeadDim + 2);
-            part[2 + lane] = acc[hh][0];
-            part[2 + lane + 32] = acc[hh][1];
+            part[2 + 2 * lane] = acc[hh][0];
+            part[3 + 2 * lane] = acc[hh][1];
         }
         if (lane < kGroup) {  // lane hh (t = 0, c = hh) holds head hh's max and sum
             float* part = p.partial + (size_t(d.work) * kHeads + kh * kGroup + lane) * (kHeadDim + 2);
@@ -364,29 +365,60 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
         if (prev != unsigned(splits - 1)) continue;
         __threadfence();
         // last slice of (row, kv head): merge the shared-prefix slots, then all
-        // slices, in that fixed order
+        // slices, in that fixed order. The loads of a batch of slots are issued
+        // together (the sums still run slot by slot, in order), so the merge costs a
+        // few round trips to L2 rather than one per slot, head and value.
         const int w0 = p.row_work0[row];
         const int x0 = nx ? p.row_x0[row] : 0;
+        const int ns = nx + splits;
+        auto slot_part = [&](int k, int hh) {
+            const int sl = k < nx ? x0 + k : w0 + (k - nx);
+            return p.partial + (size_t(sl) * kHeads + kh * kGroup + hh) * (kHeadDim + 2);
+        };
+        float mx[kGroup] = {-INFINITY, -INFINITY, -INFINITY};
+        for (int k0 = 0; k0 < ns; k0 += 8) {
+            float mv[8][kGroup];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+#pragma unroll
+                for (int hh = 0; hh < kGroup; ++hh) mv[u][hh] = k0 + u < ns ? __ldcg(slot_part(k0 + u, hh)) : -INFINITY;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+#pragma unroll
+                for (int hh = 0; hh < kGroup; ++hh) mx[hh] = fmaxf(mx[hh], mv[u][hh]);
+        }
+        float n0[kGroup] = {0.f, 0.f, 0.f}, n1[kGroup] = {0.f, 0.f, 0.f}, den[kGroup] = {0.f, 0.f, 0.f};
+        for (int k0 = 0; k0 < ns; k0 += 4) {
+            float mv[4][kGroup], lv[4][kGroup], d0[4][kGroup], d1[4][kGroup];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int hh = 0; hh < kGroup; ++hh) {
+                    if (k0 + u < ns) {
+                        const float* part = slot_part(k0 + u, hh);
+                        mv[u][hh] = __ldcg(part);
+                        lv[u][hh] = __ldcg(part + 1);
+                        d0[u][hh] = __ldcg(part + 2 + lane);
+                        d1[u][hh] = __ldcg(part + 2 + lane + 32);
+                    }
+                }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (k0 + u < ns) {
+#pragma unroll
+                    for (int hh = 0; hh < kGroup; ++hh) {
+                        const float sc = exp2f(mv[u][hh] - mx[hh]);  // maxima are in base-2 units
+                        den[hh] = fmaf(lv[u][hh], sc, den[hh]);
+                        n0[hh] = fmaf(d0[u][hh], sc, n0[hh]);
+                        n1[hh] = fmaf(d1[u][hh], sc, n1[hh]);
+                    }
+                }
+        }
 #pragma unroll
         for (int hh = 0; hh < kGroup; ++hh) {
-            const int h = kh * kGroup + hh;
-            float mx = -INFINITY;
-            for (int k = 0; k < nx + splits; ++k) {
-                const int sl = k < nx ? x0 + k : w0 + (k - nx);
-                mx = fmaxf(mx, __ldcg(p.partial + (size_t(sl) * kHeads + h) * (kHeadDim + 2)));
-            }
-            float n0 = 0.f, n1 = 0.f, den = 0.f;
-            for (int k = 0; k < nx + splits; ++k) {
-                const int sl = k < nx ? x0 + k : w0 + (k - nx);
-                const float* part = p.partial + (size_t(sl) * kHeads + h) * (kHeadDim + 2);
-                const float sc = exp2f(__ldcg(part) - mx);  // maxima are in base-2 units
-                den = fmaf(__ldcg(part + 1), sc, den);
-                n0 = fmaf(__ldcg(part + 2 + lane), sc, n0);
-                n1 = fmaf(__ldcg(part + 2 + lane + 32), sc, n1);
-            }
-            const size_t o = size_t(row) * p.out_stride + h * kHeadDim;
-            write_out(p, o + lane, n0 / den);
-            write_out(p, o + lane + 32, n1 / den);
+            const size_t o = size_t(row) * p.out_stride + (kh * kGroup + hh) * kHeadDim;
+            write_out(p, o + lane, n0[hh] / den[hh]);
+            write_out(p, o + lane + 32, n1[hh] / den[hh]);
         }
         if (lane == 0) *counter = 0u;  // ready for the next launch
     }
