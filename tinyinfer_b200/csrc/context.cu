@@ -67,9 +67,11 @@ T* host_alloc(size_t count, const char* what) {
 }
 
 // Work decomposition of paged attention.
-//  * Decode rows (sequences appending fewer than kPrefillMinRows rows): each
-//    row's context pages are cut into slices of `pages_per_split` pages
-//    (0: mpb::auto_pages_per_split over all decode rows' tokens).
+//  * Decode rows (sequences appending fewer than kPrefillMinRows rows): with
+//    pages_per_split 0 the rows' pages, concatenated, are cut into one equal run
+//    per CTA of the decode kernel's single wave (mpb::plan_static_runs); else each
+//    row's pages are cut into slices of `pages_per_split` pages, pulled longest
+//    first.
 //  * Shared prefixes (only when enabled with mp_set_shared_prefix): decode rows
 //    whose block tables begin with the same physical pages (prefix reuse, forks)
 //    form a group when at least `group_min_rows` rows share at least
@@ -84,6 +86,7 @@ struct AttnPlan {
     std::vector<int32_t> splits, work0, x0, nx;
     std::vector<mpb::AttnWork> work;
     std::vector<int32_t> order;  // decode work items, longest first (persistent schedule)
+    std::vector<int32_t> cta_items;  // static schedule: CTA c runs items [cta_items[c], cta_items[c + 1])
     std::vector<mpb::PrefillWork> prefill;
     std::vector<mpb::PrefixWork> prefix;
     std::vector<int32_t> group_rows, group_row0, group_slot;
@@ -218,6 +221,12 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
     long long decode_tokens = 0;
     for (const auto& d : decode) decode_tokens += d.len - shared_pages[d.row] * block_tokens;
     const int pps = pages_per_split > 0 ? pages_per_split : mpb::auto_pages_per_split(decode_tokens, block_tokens);
+    const bool runs = pages_per_split <= 0;
+    struct OwnPages {
+        int row, first, pages;
+    };
+    std::vector<OwnPages> own;  // decode rows of a static schedule, in row order
+    plan.cta_items.clear();
     int row = 0;
     for (int i = 0; i < count; ++i) {
         const auto& s = seqs[i];
@@ -245,16 +254,32 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
             const int len = s.start + j + 1;
             const int pages = (len + block_tokens - 1) / block_tokens;
             const int first = shared_pages[row];
-            const int n = std::max(1, (pages - first + pps - 1) / pps);
-            plan.splits[row] = n;
-            plan.work0[row] = int(plan.work.size());
-            for (int k = 0; k < n; ++k)
-                plan.work.push_back({row, first + k * pps, std::min(pages, first + (k + 1) * pps), k});
+            if (runs) {
+                own.push_back({row, first, pages});
+            } else {
+                const int n = std::max(1, (pages - first + pps - 1) / pps);
+                plan.splits[row] = n;
+                plan.work0[row] = int(plan.work.size());
+                for (int k = 0; k < n; ++k)
+                    plan.work.push_back({row, first + k * pps, std::min(pages, first + (k + 1) * pps), k});
+            }
             // K and V rows, the query row and output row, the table entries.
             const double own = 2.0 * mpb::kQWidth * sizeof(float) + double(pages) * sizeof(int32_t);
             plan.bytes += double(len - first * block_tokens) * kv_token_bytes + own;
             plan.logical_bytes += double(len) * kv_token_bytes + own;
         }
+    }
+    if (runs && !own.empty()) {
+        plan.cta_items.push_back(0);
+        mpb::plan_static_runs(
+            int(own.size()), [&](int i) { return own[i].pages - own[i].first; },
+            [&](int i, int b, int e, int k) {
+                const int row = own[i].row;
+                if (k == 0) plan.work0[row] = int(plan.work.size());
+                plan.splits[row] = k + 1;
+                plan.work.push_back({row, own[i].first + b, own[i].first + e, k});
+            },
+            [&](int, int items) { plan.cta_items.push_back(items); });
     }
     // shared-prefix slots follow the decode work items in the partial array
     for (int r = 0; r < rows; ++r)
@@ -273,6 +298,7 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
     }
     plan.order.resize(plan.work.size());
     for (size_t w = 0; w < plan.order.size(); ++w) plan.order[w] = int32_t(w);
+    if (!plan.cta_items.empty()) return;  // static schedule: no pull order
     std::stable_sort(plan.order.begin(), plan.order.end(),
                      [&](int32_t a, int32_t b) { return tokens[a] > tokens[b]; });
 }
@@ -351,7 +377,8 @@ struct mp_context {
     float cow_ms = 0.f;
     size_t off_tokens = 0, off_pos = 0, off_slot = 0, off_len = 0, off_splits = 0, off_work0 = 0, off_last = 0,
            off_work = 0, off_prefill = 0, off_x0 = 0, off_nx = 0, off_group_rows = 0, off_group_row0 = 0,
-           off_group_slot = 0, off_prefix = 0, off_order = 0;
+           off_group_slot = 0, off_prefix = 0, off_order = 0, off_cta = 0;
+    int cta_count = 0;  // static decode-attention schedule of the step (0: none)
     size_t prefill_capacity = 0;
     bool prepared = false;
     AttnPlan plan;
@@ -721,7 +748,8 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         c->entry_capacity = S * size_t(r.table_stride);
         c->region_capacity = S;
         c->meta_capacity = 6 * T + S + 4 * c->work_capacity + 8 * c->prefill_capacity + 2 * c->entry_capacity +
-                           12 * c->region_capacity + 2 + 4 * T + 2 + 8 * c->prefix_capacity + c->work_capacity;
+                           12 * c->region_capacity + 2 + 4 * T + 2 + 8 * c->prefix_capacity + c->work_capacity +
+                           mpb::kAttnPersistentCtas + 1;
         for (auto& e : c->cow_events) cuda_check(cudaEventCreate(&e), "create cow timing event");
         for (auto& e : c->fwd_events) cuda_check(cudaEventCreate(&e), "create forward timing event");
         c->meta = device_alloc<int32_t>(c->meta_capacity, "step metadata");
@@ -964,7 +992,8 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         c->off_group_slot = c->off_group_row0 + G + 1;
         c->off_prefix = c->off_group_slot + G;
         c->off_order = c->off_prefix + 8 * X;
-        c->off_entries = c->off_order + W;
+        c->off_cta = c->off_order + W;
+        c->off_entries = c->off_cta + c->plan.cta_items.size();
         c->off_regions = (c->off_entries + 2 * size_t(entry_count) + 1) & ~size_t(1);  // 8-byte aligned
         c->off_scratch = c->off_regions + 10 * size_t(region_count);                   // uint64 per region
         std::memcpy(h + c->off_tokens, tokens, size_t(T) * 4);
@@ -988,6 +1017,7 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         std::memcpy(h + c->off_group_slot, c->plan.group_slot.data(), G * 4);
         std::memcpy(h + c->off_prefix, c->plan.prefix.data(), X * sizeof(mpb::PrefixWork));
         std::memcpy(h + c->off_order, c->plan.order.data(), W * 4);
+        std::memcpy(h + c->off_cta, c->plan.cta_items.data(), c->plan.cta_items.size() * 4);
         for (int i = 0; i < entry_count; ++i) {
             h[c->off_entries + 2 * i] = entries[i].slot * c->rt.table_stride + entries[i].index;
             h[c->off_entries + 2 * i + 1] = entries[i].block;
@@ -1014,6 +1044,7 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         c->rows = T;
         c->seqs = count;
         c->work_count = int(W);
+        c->cta_count = c->plan.cta_items.empty() ? 0 : int(c->plan.cta_items.size()) - 1;
         c->prefill_count = int(P);
         c->prefix_count = int(X);
         c->step_prefix_rows = c->plan.group_rows.size();
@@ -1118,6 +1149,8 @@ int mp_forward_launch(mp_context* c) {
         ap.row_nx = meta + c->off_nx;
         ap.order = meta + c->off_order;
         ap.sched = c->attn_sched;
+        ap.cta_items = c->cta_count ? meta + c->off_cta : nullptr;
+        ap.cta_count = c->cta_count;
         ap.work = reinterpret_cast<const mpb::AttnWork*>(meta + c->off_work);
         ap.work_count = c->work_count;
         ap.partial = c->partial;
