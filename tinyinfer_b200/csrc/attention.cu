@@ -424,7 +424,7 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 3) paged_attention_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(kThreads, kAttnCtasPerSm) paged_attention_kernel(const AttnParams p) {
     pdl_enter();  // before any global memory access
     extern __shared__ __align__(128) unsigned char smem_raw[];
     float* stages = reinterpret_cast<float*>(smem_raw);

@@ -146,7 +146,11 @@ inline int auto_pages_per_split(long long total_tokens, int block_tokens) {
     return int(pages < 1 ? 1 : pages);
 }
 
-constexpr int kAttnPersistentCtas = 148 * 3;  // one wave of the decode kernel
+#ifndef MPB_ATTN_CTAS_PER_SM
+#define MPB_ATTN_CTAS_PER_SM 3
+#endif
+constexpr int kAttnCtasPerSm = MPB_ATTN_CTAS_PER_SM;  // resident decode-attention CTAs per SM
+constexpr int kAttnPersistentCtas = 148 * kAttnCtasPerSm;  // one wave of the decode kernel
 // Static decode schedule for the operator entry points: the rows' pages,
 // concatenated in row order, cut into one equal run per CTA (min(persistent
 // CTAs, total pages) runs; a run may end one row and start the next). A row's
