@@ -338,7 +338,7 @@ struct mp_context {
     std::vector<int32_t> h_tables;
     float *rope_cos = nullptr, *rope_sin = nullptr;
     // workspace (GEMM inputs as hi/lo halves)
-    float *x = nullptr, *qkv = nullptr, *q = nullptr, *logits = nullptr, *partial = nullptr;
+    float *x = nullptr, *q = nullptr, *logits = nullptr, *partial = nullptr;
     Split xn, attn, h, xl;
     // TMA tensor maps of every GEMM operand
     struct alignas(64) Maps {
@@ -452,7 +452,7 @@ void free_context(mp_context* c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     for (void* p : {(void*)c->embed, (void*)c->final_norm, (void*)c->in_norm, (void*)c->post_norm, (void*)c->keys,
                     (void*)c->values, (void*)c->tables, (void*)c->rope_cos, (void*)c->rope_sin, (void*)c->x,
-                    (void*)c->qkv, (void*)c->q, (void*)c->logits,
+                    (void*)c->q, (void*)c->logits,
                     (void*)c->partial,
                     (void*)c->counters, (void*)c->attn_sched, (void*)c->error, (void*)c->meta, (void*)c->out_tokens, (void*)c->out_finite,
                     (void*)c->cow, (void*)c->patch, (void*)c->cow_scratch})
@@ -703,7 +703,6 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         const size_t S = (size_t(r.max_step_sequences) + 127) / 128 * 128;
         c->x = device_alloc<float>(T * H, "residual stream");
         split(c->xn, T * H, "normed activations");
-        c->qkv = device_alloc<float>(T * c->qkvw, "qkv activations");
         c->q = device_alloc<float>(T * H, "roped queries");
         split(c->attn, T * H, "attention output");
         split(c->h, T * I, "mlp activations");
@@ -1080,12 +1079,12 @@ int mp_forward_launch(mp_context* c) {
         const int32_t* meta = c->meta;
         cuda_check(cudaMemsetAsync(c->error, 0, sizeof(unsigned), st), "reset error word");
         cuda_check(cudaEventRecord(c->fwd_events[0], st), "forward timing");
-        // kernels of this forward: embed; per layer qkv, rope/append, o, norm, gate/up,
-        // down (+1 input norm after layer 0, +1 per attention kind present); final
+        // kernels of this forward: embed; per layer qkv (with rope/append), o, norm,
+        // gate/up, down (+1 input norm after layer 0, +1 per attention kind present); final
         // norm, head, argmax; table patch / COW if any
         c->step_launches = uint64_t(c->entry_count > 0) +
                            uint64_t(c->region_count > 0 && c->region_rows > 0) * (c->cow_two_phase ? 2 : 1) + 1 +
-                           uint64_t(m.layers) * (6 + uint64_t(c->prefill_count > 0) + uint64_t(c->work_count > 0) +
+                           uint64_t(m.layers) * (5 + uint64_t(c->prefill_count > 0) + uint64_t(c->work_count > 0) +
                                                  uint64_t(c->prefix_count > 0)) +
                            uint64_t(m.layers - 1) + 3;
         cuda_check(mpb::launch_table_patch(meta + c->off_entries, c->entry_count, c->tables,
@@ -1114,6 +1113,22 @@ int mp_forward_launch(mp_context* c) {
                                              c->x, c->xn.hi, c->xn.lo, T, H, c->error, st),
                    "embed launch");
         const auto& mp = c->maps;
+        // the QKV projection's epilogue applies RoPE and appends K/V to the pages
+        mpb::RopeEpilogue rope{};
+        rope.row_pos = meta + c->off_pos;
+        rope.row_slot = meta + c->off_slot;
+        rope.cos = c->rope_cos;
+        rope.sin = c->rope_sin;
+        rope.max_position = m.context;
+        rope.q = c->q;
+        rope.q_stride = H;
+        rope.keys = c->keys;
+        rope.values = c->values;
+        rope.tables = c->tables;
+        rope.table_stride = r.table_stride;
+        rope.layers = m.layers;
+        rope.block_tokens = r.block_tokens;
+        rope.max_blocks = r.max_blocks;
         auto gemm = [&](const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
                         const CUtensorMap& b_lo, int rows, int n, int k, int b_row0, float* out, int ldc,
                         mpb::Epilogue e, const char* what, int bn = mpb::kTcBN) {
@@ -1125,6 +1140,7 @@ int mp_forward_launch(mp_context* c) {
             g.b_row0 = b_row0;
             g.c = out;
             g.ldc = ldc;
+            g.rope = rope;
             g.out_hi = c->h.hi;
             g.out_lo = c->h.lo;
             g.ld_out = I;
@@ -1193,35 +1209,15 @@ int mp_forward_launch(mp_context* c) {
         pp.out_lo = c->attn.lo;
         pp.out_stride = H;
         pp.error = c->error;
-        mpb::RopeAppendArgs ra{};
-        ra.qkv = c->qkv;
-        ra.qkv_stride = c->qkvw;
-        ra.row_pos = meta + c->off_pos;
-        ra.row_slot = meta + c->off_slot;
-        ra.rope_cos = c->rope_cos;
-        ra.rope_sin = c->rope_sin;
-        ra.max_position = m.context;
-        ra.q_out = c->q;
-        ra.q_stride = H;
-        ra.keys = c->keys;
-        ra.values = c->values;
-        ra.tables = c->tables;
-        ra.table_stride = r.table_stride;
-        ra.layers = m.layers;
-        ra.block_tokens = r.block_tokens;
-        ra.max_blocks = r.max_blocks;
-        ra.rows = T;
-        ra.error = c->error;
         for (int l = 0; l < m.layers; ++l) {
             const size_t L = size_t(l);
             if (l > 0)
                 cuda_check(mpb::launch_rmsnorm(c->x, nullptr, c->in_norm + L * H, m.rms_epsilon, c->xn.hi, c->xn.lo,
                                                T, H, st),
                            "rmsnorm launch");
-            gemm(mp.xn_hi, mp.xn_lo, mp.wqkv_hi, mp.wqkv_lo, T, c->qkvw, H, l * c->qkvw, c->qkv, c->qkvw,
-                 mpb::Epilogue::Store, "qkv gemm");
-            ra.layer = l;
-            cuda_check(mpb::launch_rope_append(ra, st), "rope/append launch");
+            rope.layer = l;
+            gemm(mp.xn_hi, mp.xn_lo, mp.wqkv_hi, mp.wqkv_lo, T, c->qkvw, H, l * c->qkvw, nullptr, 0,
+                 mpb::Epilogue::Rope, "qkv gemm");
             ap.layer = l;
             pp.layer = l;
             xp.layer = l;

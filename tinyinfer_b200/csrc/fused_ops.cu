@@ -3,7 +3,7 @@
 //  embed_rmsnorm : reference embedding_kernel + first rms_kernel
 //                  (miniprefix/src/backend/cuda/llama_runner.cu:15-22, launches :146,148)
 //  rmsnorm       : rms_kernel (:17-22); final norm only on each sequence's last row (:166)
-//  rope_append   : rope_kernel x2 + append_kernel (:23-32, launches :151-155)
+//  (rope_kernel x2 + append_kernel, :23-32, run in the QKV GEMM's epilogue: tc_gemm.cu)
 //  argmax        : greedy sampling of Engine::step (miniprefix/src/engine/engine.cpp:99)
 //                  + the nonfinite check (:94-95; runner :173), on device
 //  cow_copy      : the 2 cudaMemcpy2DAsync of a COW tail region (:130-137)
@@ -75,49 +75,6 @@ __global__ void rmsnorm_kernel(const float* x, const int32_t* rows, const float*
 // a' = a*cos - b*sin, b' = b*cos + a*sin with separately rounded products, as
 // the CPU runner (llama_runner.cpp:17-22) computes it; cos/sin come from tables
 // the host filled with the same libm calls as the CPU runner.
-__global__ void __launch_bounds__(384) rope_append_kernel(const RopeAppendArgs a) {
-    pdl_enter();  // before any global memory access
-    const int row = blockIdx.x, t = threadIdx.x;
-    const int pos = a.row_pos[row];
-    const float* src = a.qkv + size_t(row) * a.qkv_stride;
-    __shared__ size_t dst_off;
-    if (t == 0) {
-        const int page = pos / a.block_tokens;
-        int block = -1;
-        if (page < a.table_stride && pos < a.max_position)
-            block = a.tables[size_t(a.row_slot[row]) * a.table_stride + page];
-        if (block < 0 || block >= a.max_blocks) {
-            raise_error(a.error, kErrBounds);
-            dst_off = ~size_t(0);
-        } else {
-            dst_off = ((size_t(block) * a.layers + a.layer) * a.block_tokens + pos % a.block_tokens) * kKvWidth;
-        }
-    }
-    __syncthreads();
-    const size_t off = dst_off;
-    const int p = min(pos, a.max_position - 1);
-    if (t < 288 + 96) {
-        const bool is_q = t < 288;
-        const int idx = is_q ? t : t - 288;
-        const int head = idx / 32, d = idx % 32;
-        const float cs = a.rope_cos[size_t(p) * 32 + d], sn = a.rope_sin[size_t(p) * 32 + d];
-        const float* base = src + (is_q ? 0 : kQWidth) + head * kHeadDim;
-        const float x0 = base[d], x1 = base[d + 32];
-        const float r0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-        const float r1 = __fadd_rn(__fmul_rn(x1, cs), __fmul_rn(x0, sn));
-        if (is_q) {
-            float* q = a.q_out + size_t(row) * a.q_stride + head * kHeadDim;
-            q[d] = r0;
-            q[d + 32] = r1;
-        } else if (off != ~size_t(0)) {
-            float* k = a.keys + off + head * kHeadDim;
-            k[d] = r0;
-            k[d + 32] = r1;
-        }
-    }
-    if (t < kKvWidth && off != ~size_t(0)) a.values[off + t] = src[kQWidth + kKvWidth + t];
-}
-
 // One CTA of 1024 threads per logits row. First maximum wins (std::max_element):
 // candidates compare by value, then by lower index.
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int vocabulary, int32_t* tokens,
@@ -247,11 +204,6 @@ cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* nor
     if (count <= 0) return cudaSuccess;
     return launch_pdl(rmsnorm_kernel, dim3((count + 7) / 8), dim3(256), 0, stream, x, rows, norm_w, eps, out_hi, out_lo,
                       count, hidden);
-}
-
-cudaError_t launch_rope_append(const RopeAppendArgs& a, cudaStream_t stream) {
-    if (a.rows <= 0) return cudaSuccess;
-    return launch_pdl(rope_append_kernel, dim3(a.rows), dim3(384), 0, stream, a);
 }
 
 cudaError_t launch_argmax(const float* logits, int rows, int vocabulary, int32_t* tokens, int32_t* finite,

@@ -197,6 +197,28 @@ enum class Epilogue : int {
     Store = 0,   // C = acc
     AddTo = 1,   // C = C + acc  (residual add)
     SwiGLU = 2,  // gate/up column pairs -> silu(gate) * up as TF32 hi/lo halves
+    Rope = 3,    // QKV projection (64-wide tiles = heads): RoPE on q and k, q to the
+                 // attention input, k and v into the rows' page slots (TcGemmParams::rope)
+};
+
+// Epilogue::Rope: the rope_append step of the forward done by the QKV GEMM. Output
+// columns are 9 q heads, 3 k heads, 3 v heads of 64; tile n0 / 64 is one head. Row
+// r's position is row_pos[r]; its K/V slot is page tables[row_slot[r]][pos / bt],
+// slot pos % bt of layer `layer`. Rotation x0' = x0 cos - x1 sin, x1' = x1 cos + x0
+// sin of dims (d, d + 32) with host tables cos/sin[pos][d], each product rounded.
+struct RopeEpilogue {
+    const int32_t* row_pos;
+    const int32_t* row_slot;
+    const float* cos;
+    const float* sin;
+    int max_position;
+    float* q;
+    int q_stride;
+    float* keys;
+    float* values;
+    const int32_t* tables;
+    int table_stride;
+    int layers, layer, block_tokens, max_blocks;
 };
 
 // Tensor-core 3xTF32 GEMM (tc_gemm.cu). A and B come as TF32 hi/lo halves through
@@ -225,6 +247,7 @@ struct TcGemmParams {
     float* out_lo;
     int ld_out;
     unsigned* error;
+    RopeEpilogue rope;  // Epilogue::Rope only
 };
 cudaError_t configure_tc_gemm();
 cudaError_t launch_tc_gemm(const TcGemmMaps& maps, const TcGemmParams& p, Epilogue e, cudaStream_t stream);
@@ -239,27 +262,6 @@ cudaError_t launch_embed_rmsnorm(const int32_t* tokens, const float* embed, int 
 // rmsnorm(x[rows ? rows[i] : i]) * w as hi/lo halves into out_hi/out_lo[i] for i < count.
 cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, float* out_hi,
                            float* out_lo, int count, int hidden, cudaStream_t stream);
-// Split-half RoPE of q and k from qkv[r][960] with host-computed cos/sin tables
-// [position][32]; writes roped q to q_out[r][576] and k, v rows into the pools.
-struct RopeAppendArgs {
-    const float* qkv;
-    int qkv_stride;
-    const int32_t* row_pos;
-    const int32_t* row_slot;
-    const float* rope_cos;
-    const float* rope_sin;
-    int max_position;
-    float* q_out;
-    int q_stride;
-    float* keys;
-    float* values;
-    const int32_t* tables;
-    int table_stride;
-    int layers, layer, block_tokens, max_blocks;
-    int rows;
-    unsigned* error;
-};
-cudaError_t launch_rope_append(const RopeAppendArgs& a, cudaStream_t stream);
 // Greedy token (first index of the maximum) and finiteness of each logits row.
 cudaError_t launch_argmax(const float* logits, int rows, int vocabulary, int32_t* tokens, int32_t* finite,
                           cudaStream_t stream);

@@ -105,32 +105,68 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 //  SwiGLU : per 64-column group g of the tile, columns 0..31 are gate and 32..63 up
 //           of output columns (n0 + 64 g) / 2 + 0..31; writes h = silu(gate) * up as
 //           TF32 hi/lo halves (the down projection's input).
+//  Rope   : the tile is one head of the QKV projection; dims (d, d + 32) rotate
+//           together (q and k heads) and go to the attention input (q) or the row's
+//           page slot (k, v), see RopeEpilogue.
 template <Epilogue E>
-__host__ __device__ constexpr int epilogue_unroll() { return E == Epilogue::SwiGLU ? 2 : 4; }
+__host__ __device__ constexpr int epilogue_unroll() { return E == Epilogue::SwiGLU || E == Epilogue::Rope ? 2 : 4; }
+
+// Destination of head `head` (0..14) of batch row `grow` for the Rope epilogue:
+// the q row, or the K/V page slot (nullptr and an error bit when the row's page
+// is outside its table or the pool).
+__device__ __forceinline__ float* rope_destination(const TcGemmParams& p, int head, int grow) {
+    const RopeEpilogue& r = p.rope;
+    if (head < kHeads) return r.q + size_t(grow) * r.q_stride + head * kHeadDim;
+    const int pos = r.row_pos[grow];
+    const int page = pos / r.block_tokens;
+    int block = -1;
+    if (page < r.table_stride && pos < r.max_position) block = r.tables[size_t(r.row_slot[grow]) * r.table_stride + page];
+    if (block < 0 || block >= r.max_blocks) {
+        raise_error(p.error, kErrBounds);
+        return nullptr;
+    }
+    const size_t off = ((size_t(block) * r.layers + r.layer) * r.block_tokens + pos % r.block_tokens) * kKvWidth;
+    const int kvh = (head - kHeads) % kKvHeads;
+    return (head < kHeads + kKvHeads ? r.keys : r.values) + off + kvh * kHeadDim;
+}
 
 template <int BN, Epilogue E>
 __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float* tile, int m0, int n0, int r0,
                                               int r1, int slices) {
     using Cfg = TcConfig<BN>;
     constexpr bool kSwiGLU = E == Epilogue::SwiGLU;
+    constexpr bool kRope = E == Epilogue::Rope;
+    constexpr bool kPairs = kSwiGLU || kRope;  // columns (c, c + 32) of each 64-column group together
     constexpr int kUnroll = epilogue_unroll<E>();
-    // items per row: float4 of the tile (Store/AddTo) or of the gate halves (SwiGLU)
-    constexpr int kItems = kSwiGLU ? (BN / 64) * 8 : BN / 4;
-    constexpr int kLoads = kSwiGLU ? 2 : 1;  // gate and up
+    // items per row: float4 of the tile (Store/AddTo) or of the first halves (SwiGLU gate, Rope dims 0..31)
+    constexpr int kItems = kPairs ? (BN / 64) * 8 : BN / 4;
+    constexpr int kLoads = kPairs ? 2 : 1;
+    const int head = n0 / 64;  // Rope: the tile's head
     const int total = (r1 - r0) * kItems;
     for (int base = threadIdx.x; base < total; base += kThreads * kUnroll) {
         int off[kUnroll];
         bool live[kUnroll];
         float4* dst[kUnroll];
         float4 resid[kUnroll];
+        float4 rc[kUnroll], rs[kUnroll];  // Rope: cos / sin of the item's dims
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             const int i = base + u * kThreads;
             const int row = r0 + (i < total ? i / kItems : 0), it = i % kItems;
             live[u] = i < total && m0 + row < p.m;
-            off[u] = row * Cfg::kTileStride + (kSwiGLU ? 64 * (it / 8) + 4 * (it % 8) : 4 * it);
+            off[u] = row * Cfg::kTileStride + (kPairs ? 64 * (it / 8) + 4 * (it % 8) : 4 * it);
             dst[u] = nullptr;
-            if (!kSwiGLU) {
+            if (kRope) {
+                if (live[u]) {
+                    float* d = rope_destination(p, head, m0 + row);
+                    dst[u] = d ? reinterpret_cast<float4*>(d + 4 * it) : nullptr;
+                    if (head < kHeads + kKvHeads) {
+                        const int pc = min(p.rope.row_pos[m0 + row], p.rope.max_position - 1);
+                        rc[u] = *reinterpret_cast<const float4*>(p.rope.cos + size_t(pc) * 32 + 4 * it);
+                        rs[u] = *reinterpret_cast<const float4*>(p.rope.sin + size_t(pc) * 32 + 4 * it);
+                    }
+                }
+            } else if (!kSwiGLU) {
                 dst[u] = reinterpret_cast<float4*>(p.c + size_t(m0 + row) * p.ldc + n0 + 4 * it);
                 if (E == Epilogue::AddTo && live[u]) resid[u] = *dst[u];
             }
@@ -166,7 +202,24 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
             if (!live[u]) continue;
             const int i = base + u * kThreads;
             const int row = r0 + i / kItems, it = i % kItems;
-            if (kSwiGLU) {
+            if (kRope) {
+                if (!dst[u]) continue;
+                float4 a = acc[u][0], b = acc[u][kLoads - 1];
+                if (head < kHeads + kKvHeads) {
+                    const float4 cs = rc[u], sn = rs[u];
+                    const float4 x0 = a, x1 = b;
+                    a = make_float4(__fsub_rn(__fmul_rn(x0.x, cs.x), __fmul_rn(x1.x, sn.x)),
+                                    __fsub_rn(__fmul_rn(x0.y, cs.y), __fmul_rn(x1.y, sn.y)),
+                                    __fsub_rn(__fmul_rn(x0.z, cs.z), __fmul_rn(x1.z, sn.z)),
+                                    __fsub_rn(__fmul_rn(x0.w, cs.w), __fmul_rn(x1.w, sn.w)));
+                    b = make_float4(__fadd_rn(__fmul_rn(x1.x, cs.x), __fmul_rn(x0.x, sn.x)),
+                                    __fadd_rn(__fmul_rn(x1.y, cs.y), __fmul_rn(x0.y, sn.y)),
+                                    __fadd_rn(__fmul_rn(x1.z, cs.z), __fmul_rn(x0.z, sn.z)),
+                                    __fadd_rn(__fmul_rn(x1.w, cs.w), __fmul_rn(x0.w, sn.w)));
+                }
+                dst[u][0] = a;
+                dst[u][8] = b;  // dims + 32
+            } else if (kSwiGLU) {
                 const float4 gt = acc[u][0], up = acc[u][kLoads - 1];
                 const float o[4] = {silu_mul(gt.x, up.x), silu_mul(gt.y, up.y), silu_mul(gt.z, up.z),
                                     silu_mul(gt.w, up.w)};
@@ -375,6 +428,10 @@ cudaError_t configure_bn() {
         e = cudaFuncSetAttribute(tc_gemm_kernel<BN, Epilogue::AddTo>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(tc_gemm_kernel<BN, Epilogue::SwiGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    if constexpr (BN == 64)
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(tc_gemm_kernel<BN, Epilogue::Rope>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cfg::kSmem);
     // resident clusters of 1..8 CTAs (same resources for every epilogue)
     for (int s = 1; s <= kMaxSlices && e == cudaSuccess; ++s) {
         cudaLaunchConfig_t cfg{};
@@ -417,6 +474,12 @@ cudaError_t launch_e(const TcGemmMaps& maps, const TcGemmParams& p, Epilogue e, 
         case Epilogue::Store: return launch_bn<BN, Epilogue::Store>(maps, p, stream);
         case Epilogue::AddTo: return launch_bn<BN, Epilogue::AddTo>(maps, p, stream);
         case Epilogue::SwiGLU: return launch_bn<BN, Epilogue::SwiGLU>(maps, p, stream);
+        case Epilogue::Rope:
+            if constexpr (BN == 64) {
+                if (p.n != (kHeads + 2 * kKvHeads) * kHeadDim) return cudaErrorInvalidValue;
+                return launch_bn<BN, Epilogue::Rope>(maps, p, stream);
+            }
+            return cudaErrorInvalidValue;
     }
     return cudaErrorInvalidValue;
 }
