@@ -70,11 +70,6 @@ __global__ void rmsnorm_kernel(const float* x, const int32_t* rows, const float*
     rms_row(x + size_t(r) * hidden, w, eps, out_hi + size_t(i) * hidden, out_lo + size_t(i) * hidden, hidden, lane);
 }
 
-// One CTA of 384 threads per row: threads 0..287 rotate the 9 q heads' 32 pairs,
-// 288..383 the 3 k heads'; threads 0..191 also move the v row. The rotation is
-// a' = a*cos - b*sin, b' = b*cos + a*sin with separately rounded products, as
-// the CPU runner (llama_runner.cpp:17-22) computes it; cos/sin come from tables
-// the host filled with the same libm calls as the CPU runner.
 // One CTA of 1024 threads per logits row. First maximum wins (std::max_element):
 // candidates compare by value, then by lower index.
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int vocabulary, int32_t* tokens,

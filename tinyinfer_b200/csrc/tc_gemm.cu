@@ -106,8 +106,11 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 //           of output columns (n0 + 64 g) / 2 + 0..31; writes h = silu(gate) * up as
 //           TF32 hi/lo halves (the down projection's input).
 //  Rope   : the tile is one head of the QKV projection; dims (d, d + 32) rotate
-//           together (q and k heads) and go to the attention input (q) or the row's
-//           page slot (k, v), see RopeEpilogue.
+//           together (q and k heads) as the CPU runner does (a' = a cos - b sin,
+//           b' = b cos + a sin, products rounded separately; miniprefix/src/backend/
+//           cpu/llama_runner.cpp:17-22, cos/sin from host tables filled with its libm
+//           calls) and go to the attention input (q) or the row's page slot (k, v,
+//           paged_kv.cpp:53-56 offsets), see RopeEpilogue.
 template <Epilogue E>
 __host__ __device__ constexpr int epilogue_unroll() { return E == Epilogue::SwiGLU || E == Epilogue::Rope ? 2 : 4; }
 
