@@ -339,6 +339,7 @@ struct mp_context {
     float *rope_cos = nullptr, *rope_sin = nullptr;
     // workspace (GEMM inputs as hi/lo halves)
     float *x = nullptr, *q = nullptr, *logits = nullptr, *partial = nullptr;
+    float* ssq = nullptr;  // [rows][hidden / 64] sums of squares of x (folded RMSNorm)
     Split xn, attn, h, xl;
     // TMA tensor maps of every GEMM operand
     struct alignas(64) Maps {
@@ -452,7 +453,7 @@ void free_context(mp_context* c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     for (void* p : {(void*)c->embed, (void*)c->final_norm, (void*)c->in_norm, (void*)c->post_norm, (void*)c->keys,
                     (void*)c->values, (void*)c->tables, (void*)c->rope_cos, (void*)c->rope_sin, (void*)c->x,
-                    (void*)c->q, (void*)c->logits,
+                    (void*)c->q, (void*)c->logits, (void*)c->ssq,
                     (void*)c->partial,
                     (void*)c->counters, (void*)c->attn_sched, (void*)c->error, (void*)c->meta, (void*)c->out_tokens, (void*)c->out_finite,
                     (void*)c->cow, (void*)c->patch, (void*)c->cow_scratch})
@@ -703,6 +704,7 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         const size_t S = (size_t(r.max_step_sequences) + 127) / 128 * 128;
         c->x = device_alloc<float>(T * H, "residual stream");
         split(c->xn, T * H, "normed activations");
+        c->ssq = device_alloc<float>(T * (H / mpb::kSsqGroup), "row sums of squares");
         c->q = device_alloc<float>(T * H, "roped queries");
         split(c->attn, T * H, "attention output");
         split(c->h, T * I, "mlp activations");
@@ -1079,14 +1081,14 @@ int mp_forward_launch(mp_context* c) {
         const int32_t* meta = c->meta;
         cuda_check(cudaMemsetAsync(c->error, 0, sizeof(unsigned), st), "reset error word");
         cuda_check(cudaEventRecord(c->fwd_events[0], st), "forward timing");
-        // kernels of this forward: embed; per layer qkv (with rope/append), o, norm,
-        // gate/up, down (+1 input norm after layer 0, +1 per attention kind present); final
-        // norm, head, argmax; table patch / COW if any
+        // kernels of this forward: embed; per layer qkv (with rope/append), o, gate/up,
+        // down (+1 per attention kind present); final norm, head, argmax; table
+        // patch / COW if any
         c->step_launches = uint64_t(c->entry_count > 0) +
                            uint64_t(c->region_count > 0 && c->region_rows > 0) * (c->cow_two_phase ? 2 : 1) + 1 +
-                           uint64_t(m.layers) * (5 + uint64_t(c->prefill_count > 0) + uint64_t(c->work_count > 0) +
+                           uint64_t(m.layers) * (4 + uint64_t(c->prefill_count > 0) + uint64_t(c->work_count > 0) +
                                                  uint64_t(c->prefix_count > 0)) +
-                           uint64_t(m.layers - 1) + 3;
+                           3;
         cuda_check(mpb::launch_table_patch(meta + c->off_entries, c->entry_count, c->tables,
                                            int64_t(r.max_sequences) * r.table_stride, c->error, st),
                    "table patch launch");
@@ -1109,8 +1111,11 @@ int mp_forward_launch(mp_context* c) {
                        "cow launch");
         }
         if (c->cow_timed) cuda_check(cudaEventRecord(c->cow_events[1], st), "cow timing");
+        // RMSNorm before the QKV and gate/up projections is folded into the GEMMs: the
+        // producer of x (embedding, O and down epilogues) writes x * w as the next
+        // A operand and per-64-column sums of squares; the consumer scales its rows
         cuda_check(mpb::launch_embed_rmsnorm(meta + c->off_tokens, c->embed, m.vocabulary, c->in_norm, m.rms_epsilon,
-                                             c->x, c->xn.hi, c->xn.lo, T, H, c->error, st),
+                                             c->x, c->xn.hi, c->xn.lo, T, H, c->ssq, c->error, st),
                    "embed launch");
         const auto& mp = c->maps;
         // the QKV projection's epilogue applies RoPE and appends K/V to the pages
@@ -1131,7 +1136,8 @@ int mp_forward_launch(mp_context* c) {
         rope.max_blocks = r.max_blocks;
         auto gemm = [&](const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
                         const CUtensorMap& b_lo, int rows, int n, int k, int b_row0, float* out, int ldc,
-                        mpb::Epilogue e, const char* what, int bn = mpb::kTcBN) {
+                        mpb::Epilogue e, const char* what, int bn = mpb::kTcBN, const float* norm_next = nullptr,
+                        bool scale_rows = false) {
             mpb::TcGemmParams g{};
             g.m = rows;
             g.n = n;
@@ -1145,6 +1151,17 @@ int mp_forward_launch(mp_context* c) {
             g.out_lo = c->h.lo;
             g.ld_out = I;
             g.error = c->error;
+            if (norm_next) {  // producer of the next GEMM's normalised input
+                g.norm_w = norm_next;
+                g.out_hi = c->xn.hi;
+                g.out_lo = c->xn.lo;
+                g.ld_out = H;
+                g.ssq_out = c->ssq;
+            }
+            if (scale_rows) {  // consumer: rows scaled by 1 / rms
+                g.ssq_in = c->ssq;
+                g.eps = m.rms_epsilon;
+            }
             cuda_check(mpb::launch_tc_gemm({&a_hi, &a_lo, &b_hi, &b_lo}, g, e, st), what);
         };
         mpb::AttnParams ap{};
@@ -1211,13 +1228,9 @@ int mp_forward_launch(mp_context* c) {
         pp.error = c->error;
         for (int l = 0; l < m.layers; ++l) {
             const size_t L = size_t(l);
-            if (l > 0)
-                cuda_check(mpb::launch_rmsnorm(c->x, nullptr, c->in_norm + L * H, m.rms_epsilon, c->xn.hi, c->xn.lo,
-                                               T, H, st),
-                           "rmsnorm launch");
             rope.layer = l;
             gemm(mp.xn_hi, mp.xn_lo, mp.wqkv_hi, mp.wqkv_lo, T, c->qkvw, H, l * c->qkvw, nullptr, 0,
-                 mpb::Epilogue::Rope, "qkv gemm");
+                 mpb::Epilogue::Rope, "qkv gemm", mpb::kTcBN, nullptr, true);
             ap.layer = l;
             pp.layer = l;
             xp.layer = l;
@@ -1226,14 +1239,12 @@ int mp_forward_launch(mp_context* c) {
             cuda_check(mpb::launch_prefix_attention(xp, st), "shared-prefix attention launch");
             cuda_check(mpb::launch_paged_attention(ap, st), "attention launch");
             if (c->profile) record_attention_event(c);
-            gemm(mp.attn_hi, mp.attn_lo, mp.wo_hi, mp.wo_lo, T, H, H, l * H, c->x, H, mpb::Epilogue::AddTo, "o gemm");
-            cuda_check(mpb::launch_rmsnorm(c->x, nullptr, c->post_norm + L * H, m.rms_epsilon, c->xn.hi, c->xn.lo, T,
-                                           H, st),
-                       "rmsnorm launch");
+            gemm(mp.attn_hi, mp.attn_lo, mp.wo_hi, mp.wo_lo, T, H, H, l * H, c->x, H, mpb::Epilogue::AddTo, "o gemm",
+                 mpb::kTcBN, c->post_norm + L * H);
             gemm(mp.xn_hi, mp.xn_lo, mp.wgu_hi, mp.wgu_lo, T, 2 * I, H, l * 2 * I, nullptr, I, mpb::Epilogue::SwiGLU,
-                 "gate/up gemm", kGateUpBN);
+                 "gate/up gemm", kGateUpBN, nullptr, true);
             gemm(mp.h_hi, mp.h_lo, mp.wdown_hi, mp.wdown_lo, T, H, I, l * H, c->x, H, mpb::Epilogue::AddTo,
-                 "down gemm");
+                 "down gemm", mpb::kTcBN, l + 1 < m.layers ? c->in_norm + (L + 1) * H : nullptr);
         }
         cuda_check(mpb::launch_rmsnorm(c->x, meta + c->off_last, c->final_norm, m.rms_epsilon, c->xl.hi, c->xl.lo, S,
                                        H, st),

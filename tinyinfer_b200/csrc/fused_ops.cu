@@ -42,9 +42,13 @@ __device__ __forceinline__ void rms_row(const float* x, const float* w, float ep
     }
 }
 
+// With ssq (the first layer's norm folded into its QKV GEMM): writes x * w as
+// TF32 halves and the sum of squares of each 64-column group of x, reduced the
+// way the GEMM epilogue reduces it (4 values per lane, then a half-warp tree);
+// hidden a multiple of 64. Without: the normalised row, as rms_row.
 __global__ void embed_rmsnorm_kernel(const int32_t* tokens, const float* embed, int vocabulary, const float* w,
                                      float eps, float* x, float* normed_hi, float* normed_lo, int rows, int hidden,
-                                     unsigned* error) {
+                                     float* ssq, unsigned* error) {
     pdl_enter();  // before any global memory access
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -55,6 +59,34 @@ __global__ void embed_rmsnorm_kernel(const int32_t* tokens, const float* embed, 
     }
     const float* src = embed + size_t(tok) * hidden;
     float* xr = x + size_t(row) * hidden;
+    if (ssq) {
+        for (int d0 = 0; d0 < hidden; d0 += 128) {
+            const int d = d0 + lane * 4;
+            float q = 0.f;
+            if (d < hidden) {
+                const float4 v = *reinterpret_cast<const float4*>(src + d);
+                const float4 g = *reinterpret_cast<const float4*>(w + d);
+                *reinterpret_cast<float4*>(xr + d) = v;
+                float4 h, l;
+                split_tf32(__fmul_rn(v.x, g.x), h.x, l.x);
+                split_tf32(__fmul_rn(v.y, g.y), h.y, l.y);
+                split_tf32(__fmul_rn(v.z, g.z), h.z, l.z);
+                split_tf32(__fmul_rn(v.w, g.w), h.w, l.w);
+                *reinterpret_cast<float4*>(normed_hi + size_t(row) * hidden + d) = h;
+                *reinterpret_cast<float4*>(normed_lo + size_t(row) * hidden + d) = l;
+                q = __fmul_rn(v.x, v.x);
+                q = fmaf(v.y, v.y, q);
+                q = fmaf(v.z, v.z, q);
+                q = fmaf(v.w, v.w, q);
+            }
+            q += __shfl_xor_sync(0xffffffffu, q, 1);
+            q += __shfl_xor_sync(0xffffffffu, q, 2);
+            q += __shfl_xor_sync(0xffffffffu, q, 4);
+            q += __shfl_xor_sync(0xffffffffu, q, 8);
+            if ((lane & 15) == 0 && d < hidden) ssq[size_t(row) * (hidden / 64) + d / 64] = q;
+        }
+        return;
+    }
     for (int d = lane * 4; d < hidden; d += 128)
         *reinterpret_cast<float4*>(xr + d) = *reinterpret_cast<const float4*>(src + d);
     __syncwarp();
@@ -188,10 +220,11 @@ __global__ void table_patch_kernel(const int32_t* pairs, int count, int32_t* tab
 
 cudaError_t launch_embed_rmsnorm(const int32_t* tokens, const float* embed, int vocabulary, const float* norm_w,
                                  float eps, float* x, float* normed_hi, float* normed_lo, int rows, int hidden,
-                                 unsigned* error, cudaStream_t stream) {
+                                 float* ssq, unsigned* error, cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
+    if (ssq && hidden % 64) return cudaErrorInvalidValue;
     return launch_pdl(embed_rmsnorm_kernel, dim3((rows + 7) / 8), dim3(256), 0, stream, tokens, embed, vocabulary,
-                      norm_w, eps, x, normed_hi, normed_lo, rows, hidden, error);
+                      norm_w, eps, x, normed_hi, normed_lo, rows, hidden, ssq, error);
 }
 
 cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, float* out_hi,

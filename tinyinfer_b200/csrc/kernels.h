@@ -248,17 +248,31 @@ struct TcGemmParams {
     int ld_out;
     unsigned* error;
     RopeEpilogue rope;  // Epilogue::Rope only
+    // RMSNorm folded into the GEMMs around it (hidden = N of the producer = K of the
+    // consumer, a multiple of 64):
+    //  * AddTo with norm_w: besides c, writes the TF32 halves of c[row] * norm_w
+    //    (the next GEMM's A operand) into out_hi / out_lo (ld_out) and the sum of
+    //    squares of each 64-column group of c[row] into ssq_out[row][n0 / 64];
+    //  * Rope / SwiGLU with ssq_in: scales row r of the product by
+    //    1 / sqrt(sum_g ssq_in[r][g] / k + eps) (groups in order) before the epilogue.
+    const float* norm_w;
+    float* ssq_out;
+    const float* ssq_in;
+    float eps;
 };
+constexpr int kSsqGroup = 64;  // columns per partial sum of squares
 cudaError_t configure_tc_gemm();
 cudaError_t launch_tc_gemm(const TcGemmMaps& maps, const TcGemmParams& p, Epilogue e, cudaStream_t stream);
 // hi = x with the 13 low mantissa bits cleared, lo = x - hi, elementwise.
 cudaError_t launch_split(const float* x, float* hi, float* lo, size_t n, cudaStream_t stream);
 
 // ---------------------------------------------------------------- fused small ops
-// x[r][:] = embed[tokens[r]][:]; rmsnorm(x[r]) * w written as TF32 hi/lo halves.
+// x[r][:] = embed[tokens[r]][:]; rmsnorm(x[r]) * w written as TF32 hi/lo halves, or
+// with ssq (norm folded into the next GEMM): x[r] * w as halves and the sums of
+// squares of x[r]'s 64-column groups into ssq[r][hidden / 64].
 cudaError_t launch_embed_rmsnorm(const int32_t* tokens, const float* embed, int vocabulary, const float* norm_w,
                                  float eps, float* x, float* normed_hi, float* normed_lo, int rows, int hidden,
-                                 unsigned* error, cudaStream_t stream);
+                                 float* ssq, unsigned* error, cudaStream_t stream);
 // rmsnorm(x[rows ? rows[i] : i]) * w as hi/lo halves into out_hi/out_lo[i] for i < count.
 cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, float* out_hi,
                            float* out_lo, int count, int hidden, cudaStream_t stream);

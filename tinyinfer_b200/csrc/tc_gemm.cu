@@ -146,7 +146,23 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
     constexpr int kLoads = kPairs ? 2 : 1;
     const int head = n0 / 64;  // Rope: the tile's head
     const int total = (r1 - r0) * kItems;
-    for (int base = threadIdx.x; base < total; base += kThreads * kUnroll) {
+    // RMSNorm folded in (consumer side): this CTA's rows' 1 / rms from the producer's
+    // per-64-column sums of squares, summed in group order
+    __shared__ float row_scale[kBM];
+    const bool scaled = kPairs && p.ssq_in != nullptr;
+    if (scaled) {
+        const int groups = p.k / kSsqGroup;
+        for (int r = r0 + int(threadIdx.x); r < r1; r += kThreads) {
+            float ss = 0.f;
+            if (m0 + r < p.m)
+                for (int g = 0; g < groups; ++g) ss = __fadd_rn(ss, p.ssq_in[size_t(m0 + r) * groups + g]);
+            row_scale[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(p.k)), p.eps)));
+        }
+        __syncthreads();
+    }
+    const bool produce = E == Epilogue::AddTo && p.norm_w != nullptr;
+    // warp-uniform trip count (the producer's half-warp shuffles need every lane)
+    for (int base = threadIdx.x; base - int(threadIdx.x & 31) < total; base += kThreads * kUnroll) {
         int off[kUnroll];
         bool live[kUnroll];
         float4* dst[kUnroll];
@@ -200,8 +216,21 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
                         acc[u][h].w += v[k][u][h].w;
                     }
             }
+        if (scaled) {
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int i = base + u * kThreads;
+                const float sc = row_scale[r0 + (i < total ? i / kItems : 0)];
+#pragma unroll
+                for (int h = 0; h < kLoads; ++h)
+                    acc[u][h] = make_float4(__fmul_rn(acc[u][h].x, sc), __fmul_rn(acc[u][h].y, sc),
+                                            __fmul_rn(acc[u][h].z, sc), __fmul_rn(acc[u][h].w, sc));
+            }
+        }
+        float sq[kUnroll];  // producer: sum of squares of the item's 4 new values
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
+            sq[u] = 0.f;
             if (!live[u]) continue;
             const int i = base + u * kThreads;
             const int row = r0 + i / kItems, it = i % kItems;
@@ -238,9 +267,42 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
                     *dst[u] = a;
                 } else {
                     const float4 x = resid[u];
-                    *dst[u] = make_float4(__fadd_rn(x.x, a.x), __fadd_rn(x.y, a.y), __fadd_rn(x.z, a.z),
-                                          __fadd_rn(x.w, a.w));
+                    const float4 y = make_float4(__fadd_rn(x.x, a.x), __fadd_rn(x.y, a.y), __fadd_rn(x.z, a.z),
+                                                 __fadd_rn(x.w, a.w));
+                    *dst[u] = y;
+                    if (produce) {
+                        // the next GEMM's A operand: y * norm weight as TF32 halves
+                        const int col = n0 + 4 * it;
+                        const float4 w = *reinterpret_cast<const float4*>(p.norm_w + col);
+                        float4 hv, lv;
+                        split_tf32(__fmul_rn(y.x, w.x), hv.x, lv.x);
+                        split_tf32(__fmul_rn(y.y, w.y), hv.y, lv.y);
+                        split_tf32(__fmul_rn(y.z, w.z), hv.z, lv.z);
+                        split_tf32(__fmul_rn(y.w, w.w), hv.w, lv.w);
+                        const size_t at = size_t(m0 + row) * p.ld_out + col;
+                        *reinterpret_cast<float4*>(p.out_hi + at) = hv;
+                        *reinterpret_cast<float4*>(p.out_lo + at) = lv;
+                        float q = __fmul_rn(y.x, y.x);
+                        q = fmaf(y.y, y.y, q);
+                        q = fmaf(y.z, y.z, q);
+                        sq[u] = fmaf(y.w, y.w, q);
+                    }
                 }
+            }
+        }
+        if (produce) {
+            // 16 consecutive items (lanes) of a row cover one 64-column group: reduce
+            // over the half warp (a fixed tree) and let its first lane write the sum
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                float q = sq[u];
+                q += __shfl_xor_sync(0xffffffffu, q, 1);
+                q += __shfl_xor_sync(0xffffffffu, q, 2);
+                q += __shfl_xor_sync(0xffffffffu, q, 4);
+                q += __shfl_xor_sync(0xffffffffu, q, 8);
+                const int i = base + u * kThreads;
+                const int row = r0 + i / kItems, it = i % kItems;
+                if (live[u] && it % 16 == 0) p.ssq_out[size_t(m0 + row) * (p.n / kSsqGroup) + (n0 + 4 * it) / kSsqGroup] = q;
             }
         }
     }
