@@ -93,6 +93,20 @@ mph_runner* mph_runner_new_b200(int32_t device, const mp_model_config* model, in
                                 int32_t max_step_tokens, int32_t max_step_sequences);
 int mph_runner_set_weight(mph_runner* r, const char* name, const float* data, size_t elements);
 int mph_runner_finalize(mph_runner* r);
+/* The B200 runner built from an MPFX0001 model file: what make_cuda_runner(
+ * ModelWeights::load(path), context, kv) does in the reference (model.h:59-62,
+ * model.cpp:20-56). The file's config and every tensor are checked as the
+ * reference loader checks them (same messages); tensors stream to the device one
+ * at a time and the weights are finalized. NULL on failure (mph_last_error). */
+mph_runner* mph_runner_new_b200_file(int32_t device, const char* path, int32_t context, int32_t block_tokens,
+                                     int32_t max_blocks, int32_t prefix_blocks, int32_t max_sequences,
+                                     int32_t max_step_tokens, int32_t max_step_sequences);
+/* MPFX0001 reading without a device: the config alone, or the config and every
+ * tensor (in file order) through `sink`, which returns 0 to continue. Errors as
+ * the reference loader's (mph_last_error), -1 invalid argument, -4 format. */
+typedef int (*mph_tensor_sink)(const char* name, const float* data, uint64_t elements, void* user);
+int mph_mpfx_config(const char* path, mp_model_config* out);
+int mph_mpfx_read(const char* path, mp_model_config* out, mph_tensor_sink sink, void* user);
 /* Device-free runner with the real KV manager and scripted one-hot logits. */
 mph_runner* mph_runner_new_scripted(int32_t vocabulary, int32_t context, int32_t layers, int32_t width,
                                     int32_t block_tokens, int32_t max_blocks, int32_t prefix_blocks);

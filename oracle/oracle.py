@@ -129,6 +129,14 @@ class RefLib:
                      "ref_engine_new"):
             getattr(lib, name).restype = C.c_void_p
         lib.ref_weights_new.argtypes = [C.c_int] * 8 + [C.c_float, C.c_float, C.c_int]
+        lib.ref_weights_load.restype = C.c_void_p
+        lib.ref_weights_load.argtypes = [C.c_char_p]
+        lib.ref_weights_config.argtypes = [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_float)]
+        lib.ref_weights_tensor.restype = C.c_long
+        lib.ref_weights_tensor.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_long]
+        lib.ref_weights_count.restype = C.c_long
+        lib.ref_weights_count.argtypes = [C.c_void_p]
+        lib.ref_weights_free.argtypes = [C.c_void_p]
         lib.ref_weights_put.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_int, C.c_void_p]
         lib.ref_cpu_runner_new.argtypes = [C.c_void_p] + [C.c_int] * 4
         lib.ref_scripted_runner_new.argtypes = [C.c_int] * 7
@@ -161,6 +169,31 @@ class RefLib:
             self.check(self.lib.ref_weights_put(C.c_void_p(h), name.encode(), a.ctypes.data_as(C.c_void_p),
                                                 a.ndim, dims))
         return h
+
+    def load_mpfx(self, path: str):
+        """The reference loader on an MPFX0001 file: (config ints, (eps, theta),
+        {name: flat float32 array}); RefError with its message on failure."""
+        h = self.lib.ref_weights_load(path.encode())
+        if not h:
+            raise RefError(-4, self.error())
+        try:
+            ints = (C.c_int * 9)()
+            floats = (C.c_float * 2)()
+            self.lib.ref_weights_config(C.c_void_p(h), ints, floats)
+            from tinyinfer_b200 import mpfx
+            from tinyinfer_b200.synthetic import ModelConfig
+
+            cfg = ModelConfig(*list(ints)[:8], rms_epsilon=floats[0], rope_theta=floats[1], tied=bool(ints[8]))
+            out = {}
+            for name in mpfx.tensor_names(cfg):
+                n = self.lib.ref_weights_tensor(C.c_void_p(h), name.encode(), None, 0)
+                a = np.empty(n, dtype=np.float32)
+                self.lib.ref_weights_tensor(C.c_void_p(h), name.encode(), a.ctypes.data_as(C.c_void_p), n)
+                out[name] = a
+            assert self.lib.ref_weights_count(C.c_void_p(h)) == len(out)
+            return cfg, out
+        finally:
+            self.lib.ref_weights_free(C.c_void_p(h))
 
 
 RUNNER_STATS_FIELDS = (

@@ -14,6 +14,7 @@
 // Error convention shared with the product host library (include/miniprefix_b200_host.h):
 //   >= 0 success; -1 std::invalid_argument; -2 std::logic_error; -3 KvCapacityError;
 //   -4 other std::runtime_error; -5 std::out_of_range; -6 anything else.
+#include <algorithm>
 #include "miniprefix/engine.h"
 #include "miniprefix/kv_manager.h"
 #include "miniprefix/model.h"
@@ -172,6 +173,34 @@ int ref_weights_put(void* handle, const char* name, const float* data, int rank,
     });
 }
 void ref_weights_free(void* handle) { delete static_cast<std::shared_ptr<ModelWeights>*>(handle); }
+// The reference's own MPFX0001 loader (ModelWeights::load, model.cpp:20-56): NULL
+// and ref_last_error() on failure.
+void* ref_weights_load(const char* path) {
+    std::shared_ptr<ModelWeights> loaded;
+    if (guarded([&] { loaded = ModelWeights::load(path); return 0; }) < 0) return nullptr;
+    return new std::shared_ptr<ModelWeights>(std::move(loaded));
+}
+// layers, hidden, intermediate, heads, kv_heads, vocabulary, context, eos, tied;
+// eps and theta through `f`.
+int ref_weights_config(void* handle, int* out, float* f) {
+    const auto& c = (*static_cast<std::shared_ptr<ModelWeights>*>(handle))->config;
+    const int v[9] = {c.layers, c.hidden, c.intermediate, c.heads, c.kv_heads, c.vocabulary, c.context, c.eos,
+                      c.tied ? 1 : 0};
+    std::memcpy(out, v, sizeof(v));
+    f[0] = c.rms_epsilon;
+    f[1] = c.rope_theta;
+    return 0;
+}
+// Copies tensor `name` (count floats); returns its element count, -1 if absent.
+long ref_weights_tensor(void* handle, const char* name, float* out, long count) {
+    const auto& w = *static_cast<std::shared_ptr<ModelWeights>*>(handle);
+    const auto it = w->tensors.find(name);
+    if (it == w->tensors.end()) return -1;
+    const long n = static_cast<long>(it->second.numel());
+    std::memcpy(out, it->second.data<float>(), std::size_t(std::min(n, count)) * sizeof(float));
+    return n;
+}
+long ref_weights_count(void* handle) { return long((*static_cast<std::shared_ptr<ModelWeights>*>(handle))->tensors.size()); }
 
 // ---------------------------------------------------------------- runners
 void* ref_cpu_runner_new(void* weights, int context, int block_tokens, int max_blocks, int prefix_blocks) {

@@ -271,3 +271,30 @@ def test_decode_steps_run_as_one_forward(built):
             assert t == token(seq), rid
             seq.append(t)
     engine.shutdown()
+
+
+@pytest.mark.gpu
+def test_runner_from_mpfx_file_equals_uploaded_weights(built, tmp_path):
+    """Runner.b200_from_file (make_cuda_runner(ModelWeights::load(path), ...)) gives
+    the same logits, bit for bit, as the same weights uploaded tensor by tensor."""
+    from tinyinfer_b200 import mpfx
+    from tinyinfer_b200.host import Runner
+
+    cfg = ModelConfig(layers=2, intermediate=128, vocabulary=64, context=64, tied=False)
+    w = random_weights(cfg, seed=29)
+    path = str(tmp_path / "model.mpfx")
+    mpfx.write(path, cfg, w)
+    kw = dict(context=64, block_tokens=4, max_blocks=64, prefix_blocks=0, max_sequences=4, max_step_tokens=64,
+              max_step_sequences=4)
+    a = Runner.b200(cfg, w, **kw)
+    b = Runner.b200_from_file(path, **kw)
+    assert b.config.layers == 2 and not b.config.tied
+    prompt = [int(t) for t in np.random.default_rng(5).integers(0, 64, 11)]
+    outs = []
+    for r in (a, b):
+        r.create("s")
+        first = r.append("s", prompt)
+        second = r.append("s", [int(np.argmax(first))])
+        outs.append((first, second))
+        r.close()
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])

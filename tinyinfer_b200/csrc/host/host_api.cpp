@@ -7,6 +7,7 @@
 #include "b200_runner.h"
 #include "engine.h"
 #include "miniprefix_b200_host.h"
+#include "mpfx.h"
 #include "scripted_runner.h"
 
 using namespace miniprefix_b200;
@@ -351,6 +352,69 @@ mph_runner* mph_runner_new_b200(int32_t device, const mp_model_config* model, in
     }
     return h;
 }
+namespace {
+mp_model_config to_c(const ModelConfig& c) {
+    mp_model_config m{};
+    m.layers = c.layers;
+    m.hidden = c.hidden;
+    m.intermediate = c.intermediate;
+    m.heads = c.heads;
+    m.kv_heads = c.kv_heads;
+    m.vocabulary = c.vocabulary;
+    m.context = c.context;
+    m.eos = c.eos;
+    m.rms_epsilon = c.rms_epsilon;
+    m.rope_theta = c.rope_theta;
+    m.tied = c.tied ? 1 : 0;
+    return m;
+}
+}  // namespace
+
+mph_runner* mph_runner_new_b200_file(int32_t device, const char* path, int32_t context, int32_t block_tokens,
+                                     int32_t max_blocks, int32_t prefix_blocks, int32_t max_sequences,
+                                     int32_t max_step_tokens, int32_t max_step_sequences) {
+    auto* h = new mph_runner;
+    if (guarded([&] {
+            if (!path) throw std::invalid_argument("null model path");
+            const ModelConfig c = read_mpfx_config(path);
+            B200Options o;
+            o.device = device;
+            o.max_sequences = max_sequences;
+            o.max_step_tokens = max_step_tokens;
+            o.max_step_sequences = max_step_sequences;
+            auto r = std::make_unique<B200Runner>(c, context, KvCacheConfig{block_tokens, max_blocks, prefix_blocks}, o);
+            read_mpfx(path, [&](const MpfxTensor& t) { r->set_weight(t.name, t.data, t.elements); });
+            r->finalize_weights();
+            h->b200 = r.get();
+            h->runner = r.get();
+            h->owned = std::move(r);
+            return 0L;
+        }) < 0) {
+        delete h;
+        return nullptr;
+    }
+    return h;
+}
+
+int mph_mpfx_config(const char* path, mp_model_config* out) {
+    return int(guarded([&] {
+        if (!path || !out) throw std::invalid_argument("null argument");
+        *out = to_c(read_mpfx_config(path));
+        return 0L;
+    }));
+}
+
+int mph_mpfx_read(const char* path, mp_model_config* out, mph_tensor_sink sink, void* user) {
+    return int(guarded([&] {
+        if (!path || !out || !sink) throw std::invalid_argument("null argument");
+        *out = to_c(read_mpfx(path, [&](const MpfxTensor& t) {
+            if (sink(t.name.c_str(), t.data, uint64_t(t.elements), user) != 0)
+                throw std::runtime_error("tensor sink stopped the read");
+        }));
+        return 0L;
+    }));
+}
+
 int mph_runner_set_weight(mph_runner* r, const char* name, const float* data, size_t elements) {
     return int(guarded([&] {
         if (!r->b200) throw std::logic_error("not a B200 runner");

@@ -5,23 +5,25 @@
 
 namespace miniprefix_b200 {
 
-ExactPrefixCache::ExactPrefixCache(KvBlockPool& pool) : pool_(pool) { s_.nodes.emplace_back(); }
+ExactPrefixCache::ExactPrefixCache(KvBlockPool& pool) : pool_(pool) {
+    s_.nodes.emplace_back();
+    s_.leases.assign(std::size_t(std::max(pool.config().max_blocks, 0)), 0u);
+}
 
 ExactPrefixCache::~ExactPrefixCache() { clear(); }
 
 std::size_t ExactPrefixCache::cache_only_blocks() const {
     std::size_t count = 0;
-    for (const auto& [block, leases] : s_.leases)
-        if (leases && pool_.references(block) == leases) ++count;
+    for (std::size_t block = 0; block < s_.leases.size(); ++block) {
+        const std::uint32_t leases = s_.leases[block];
+        if (leases && pool_.references(int(block)) == leases) ++count;
+    }
     return count;
 }
 
 void ExactPrefixCache::lease_add(int page, int delta) {
     log(Op::Lease, page, delta);
-    auto lease = s_.leases.find(page);
-    if (lease == s_.leases.end()) lease = s_.leases.emplace(page, 0u).first;
-    lease->second = std::uint32_t(int(lease->second) + delta);
-    if (lease->second == 0) s_.leases.erase(lease);
+    s_.leases[std::size_t(page)] = std::uint32_t(int(s_.leases[std::size_t(page)]) + delta);
 }
 
 int ExactPrefixCache::new_node(int parent, View edge) {
@@ -301,10 +303,7 @@ void ExactPrefixCache::rollback_journal() noexcept {
             s_.nodes[std::size_t(e->a)].block = e->b;
             break;
         case Op::Lease: {
-            auto lease = s_.leases.find(e->a);
-            if (lease == s_.leases.end()) lease = s_.leases.emplace(e->a, 0u).first;
-            lease->second = std::uint32_t(int(lease->second) - e->b);
-            if (lease->second == 0) s_.leases.erase(lease);
+            s_.leases[std::size_t(e->a)] = std::uint32_t(int(s_.leases[std::size_t(e->a)]) - e->b);
             break;
         }
         }

@@ -123,7 +123,7 @@ private:
     struct State : Counters {
         std::vector<Node> nodes;
         std::vector<int> spare;
-        std::unordered_map<int, std::uint32_t> leases;
+        std::vector<std::uint32_t> leases;  // per pool page: index nodes leasing it
         std::vector<std::pair<std::uint64_t, int>> lru;
         std::size_t lru_head = 0;
         std::uint64_t clock = 0;

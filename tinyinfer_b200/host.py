@@ -60,8 +60,9 @@ def library() -> C.CDLL:
         lib = C.CDLL(HOST_LIB)
         lib.mph_last_error.restype = C.c_char_p
         for name in ("mph_cache_new", "mph_kv_new", "mph_runner_new_b200", "mph_runner_new_scripted",
-                     "mph_engine_new"):
+                     "mph_engine_new", "mph_runner_new_b200_file"):
             getattr(lib, name).restype = C.c_void_p
+        lib.mph_runner_new_b200_file.argtypes = [C.c_int32, C.c_char_p] + [C.c_int32] * 7
         lib.mph_cache_new.argtypes = [C.c_int32] * 5
         lib.mph_kv_new.argtypes = [C.c_int32] * 7
         lib.mph_runner_new_b200.argtypes = [C.c_int32, C.POINTER(_device.ModelConfigC)] + [C.c_int32] * 7
@@ -254,6 +255,23 @@ class Runner(_Base):
         r = cls(h, config.vocabulary, "b200")
         if weights is not None:
             r.load_weights(weights)
+        return r
+
+    @classmethod
+    def b200_from_file(cls, path: str, *, context: int, block_tokens=16, max_blocks=128, prefix_blocks=0, device=0,
+                       max_sequences=256, max_step_tokens=4096, max_step_sequences=256):
+        """A B200 runner built from an MPFX0001 model file (the reference's
+        make_cuda_runner(ModelWeights::load(path), context, kv))."""
+        from . import mpfx
+
+        cfg = mpfx.read_config(path)
+        lib = library()
+        h = lib.mph_runner_new_b200_file(device, path.encode(), context, block_tokens, max_blocks, prefix_blocks,
+                                         max_sequences, max_step_tokens, max_step_sequences)
+        if not h:
+            raise HostError(-1, lib.mph_last_error().decode())
+        r = cls(h, cfg.vocabulary, "b200")
+        r.config = cfg
         return r
 
     @classmethod
