@@ -414,6 +414,16 @@ class RefEngine:
     def step(self) -> bool:
         return bool(self.ref.check(self.ref.lib.ref_engine_step(self.h)))
 
+    def serve(self, text: str, capacity: int = 1 << 24) -> str:
+        """The reference worker protocol (apps/protocol/session.cpp) over this engine."""
+        lib = self.ref.lib
+        lib.ref_protocol_serve.restype = C.c_long
+        lib.ref_protocol_serve.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_long]
+        buf = C.create_string_buffer(capacity)
+        n = lib.ref_protocol_serve(self.h, text.encode(), buf, capacity)
+        assert n < capacity, "protocol response exceeds the buffer"
+        return buf.raw[:n].decode()
+
     def poll_events(self):
         # ref_engine_poll drains on every call; call once with room for all text.
         return _parse_events(None, lambda buf, cap: self.ref.lib.ref_engine_poll(self.h, buf, cap))

@@ -15,6 +15,9 @@
 //   >= 0 success; -1 std::invalid_argument; -2 std::logic_error; -3 KvCapacityError;
 //   -4 other std::runtime_error; -5 std::out_of_range; -6 anything else.
 #include <algorithm>
+#include <sstream>
+
+#include "protocol/session.h"
 #include "miniprefix/engine.h"
 #include "miniprefix/kv_manager.h"
 #include "miniprefix/model.h"
@@ -437,6 +440,21 @@ long ref_kv_offset(void* m, const char* id, int layer, int token) {
 
 // ---------------------------------------------------------------- Engine
 // Takes ownership of the runner handle's runner.
+// The reference's worker protocol (apps/protocol/session.cpp) over an engine.
+long ref_protocol_serve(void* engine, const char* input, char* out, long capacity) {
+    auto* h = static_cast<EngineHandle*>(engine);
+    std::istringstream in(input);
+    std::ostringstream os;
+    miniprefix::protocol::serve(*h->engine, in, os);
+    const std::string s = os.str();
+    if (out && capacity > 0) {
+        const std::size_t n = std::min(s.size(), std::size_t(capacity - 1));
+        std::memcpy(out, s.data(), n);
+        out[n] = '\0';
+    }
+    return long(s.size());
+}
+
 void* ref_engine_new(void* runner, int max_batch, int budget, int chunk, int context) {
     auto* rh = static_cast<RunnerHandle*>(runner);
     auto* h = new EngineHandle;

@@ -79,9 +79,30 @@ def build_host(force: bool = False) -> str | None:
     return HOST_LIB
 
 
+WORKER_DIR = os.path.join(CSRC, "worker")
+EXECUTABLES = {"mpb200_worker": "worker_main.cpp", "mpb200_stress": "stress_main.cpp"}
+
+
+def build_executables(force: bool = False) -> list[str]:
+    """The protocol worker and the lifecycle stress harness, linked against the
+    host library (in-tree, next to it)."""
+    out = []
+    for exe, src in EXECUTABLES.items():
+        path, source = os.path.join(HERE, exe), os.path.join(WORKER_DIR, src)
+        if not os.path.exists(source):
+            continue
+        headers = [os.path.join(CSRC, "host", f) for f in os.listdir(os.path.join(CSRC, "host")) if f.endswith(".h")]
+        if force or _stale(path, [source, HOST_LIB] + headers):
+            _run(["g++", "-O2", "-std=c++17", "-Wall", "-Wextra", f"-I{INCLUDE}", f"-I{os.path.join(CSRC, 'host')}",
+                  source, "-o", path, f"-L{HERE}", "-lmpb200_host", "-lmpb200", "-Wl,-rpath,$ORIGIN"])
+        out.append(path)
+    return out
+
+
 def build(force: bool = False) -> None:
     build_device(force)
     build_host(force)
+    build_executables(force)
 
 
 if __name__ == "__main__":

@@ -150,20 +150,32 @@ std::vector<float> B200Runner::append(const RequestId& id, const std::vector<Tok
     });
     std::vector<mp_table_entry> entries;
     table_entries(slot, sequence, entries);
-    const mp_sequence_desc desc{slot, sequence.used, int32_t(tokens.size())};
     std::vector<float> logits(std::size_t(config_.vocabulary));
     int32_t token = 0, finite = 0;
     mp_cow_timing(ctx_, cost_timing_ && !regions.empty());
-    const int rc = mp_forward(ctx_, &desc, 1, tokens.data(), entries.data(), int32_t(entries.size()), regions.data(),
-                              int32_t(regions.size()), &token, &finite, logits.data(), options_.timeout_ms);
+    // A forward carries at most max_step_tokens tokens: longer appends run as
+    // consecutive forwards of the same sequence (the table entries and the copy
+    // with the first); only the last returns logits, as only the last row's are
+    // the append's result.
+    const int n = int(tokens.size()), step = std::max(options_.max_step_tokens, 1);
+    int rc = MP_OK;
+    for (int off = 0; off < n && (rc == MP_OK || rc == MP_ERR_NONFINITE); off += step) {
+        const bool first = off == 0, last = off + step >= n;
+        const mp_sequence_desc desc{slot, sequence.used + off, std::min(step, n - off)};
+        rc = mp_forward(ctx_, &desc, 1, tokens.data() + off, first ? entries.data() : nullptr,
+                        first ? int32_t(entries.size()) : 0, first ? regions.data() : nullptr,
+                        first ? int32_t(regions.size()) : 0, &token, &finite, last ? logits.data() : nullptr,
+                        options_.timeout_ms);
+        if (!last && rc == MP_ERR_NONFINITE) rc = MP_OK;  // only the final row's logits count
+        if (first && cost_timing_ && !regions.empty() && rc != MP_ERR_CUDA && rc != MP_ERR_TIMEOUT) {
+            float ms = 0.f;
+            mp_cow_elapsed(ctx_, &ms);
+            costs_.cow_copy_ns += std::uint64_t(double(ms) * 1e6);
+            ++costs_.cow_timed_copies;
+        }
+    }
     stats_.token_uploaded_bytes += tokens.size() * sizeof(TokenId);
     stats_.block_table_uploaded_bytes += entries.size() * sizeof(int32_t);
-    if (cost_timing_ && !regions.empty() && rc != MP_ERR_CUDA && rc != MP_ERR_TIMEOUT) {
-        float ms = 0.f;
-        mp_cow_elapsed(ctx_, &ms);
-        costs_.cow_copy_ns += std::uint64_t(double(ms) * 1e6);
-        ++costs_.cow_timed_copies;
-    }
     if (rc != MP_OK) {
         mirror_[std::size_t(slot)].clear();  // re-upload the whole table next time
         if (rc == MP_ERR_NONFINITE) throw std::runtime_error("nonfinite CUDA logits");

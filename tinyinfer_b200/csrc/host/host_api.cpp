@@ -8,6 +8,9 @@
 #include "engine.h"
 #include "miniprefix_b200_host.h"
 #include "mpfx.h"
+#include "protocol.h"
+
+#include <sstream>
 #include "scripted_runner.h"
 
 using namespace miniprefix_b200;
@@ -394,6 +397,22 @@ mph_runner* mph_runner_new_b200_file(int32_t device, const char* path, int32_t c
         return nullptr;
     }
     return h;
+}
+
+long mph_engine_serve(mph_engine* e, const char* input, char* out, long capacity) {
+    return guarded([&] {
+        if (!e || !input) throw std::invalid_argument("null argument");
+        std::istringstream in(input);
+        std::ostringstream os;
+        protocol::serve(*e->engine, in, os);
+        const std::string s = os.str();
+        if (out && capacity > 0) {
+            const std::size_t n = std::min(s.size(), std::size_t(capacity - 1));
+            std::memcpy(out, s.data(), n);
+            out[n] = '\0';
+        }
+        return long(s.size());
+    });
 }
 
 int mph_mpfx_config(const char* path, mp_model_config* out) {

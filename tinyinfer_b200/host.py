@@ -385,6 +385,17 @@ class Engine(_Base):
         a, p, n = _toks(prompt)
         self.check(self.lib.mph_engine_submit(self.h, _ids(id), p, n, max_new_tokens, -1 if eos is None else int(eos)))
 
+    def serve(self, text: str, capacity: int = 1 << 24) -> str:
+        """Worker protocol v3 over this engine: the response lines to `text`'s
+        commands (served once; a response longer than `capacity` raises)."""
+        self.lib.mph_engine_serve.restype = C.c_long
+        self.lib.mph_engine_serve.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_long]
+        buf = C.create_string_buffer(capacity)
+        n = self.check(self.lib.mph_engine_serve(self.h, text.encode(), buf, capacity))
+        if n >= capacity:
+            raise HostError(-6, f"protocol response of {n} bytes exceeds the {capacity}-byte buffer")
+        return buf.raw[:n].decode()
+
     def step(self) -> bool:
         return bool(self.check(self.lib.mph_engine_step(self.h)))
 
