@@ -105,7 +105,7 @@ mph_runner* mph_runner_new_b200_file(int32_t device, const char* path, int32_t c
  * tensor (in file order) through `sink`, which returns 0 to continue. Errors as
  * the reference loader's (mph_last_error), -1 invalid argument, -4 format. */
 typedef int (*mph_tensor_sink)(const char* name, const float* data, uint64_t elements, void* user);
-/* Worker protocol v3 (miniprefix/apps/protocol/*) over the engine: serves the
+/* Worker protocol v3 (miniprefix/apps/protocol/session.cpp) over the engine: serves the
  * newline-separated commands of `input` until QUIT or their end and writes the
  * response lines into `out` (NUL-terminated, at most capacity - 1 bytes).
  * Returns the full response length. The mpb200_worker executable serves the same

@@ -42,6 +42,7 @@ int ExactPrefixCache::new_node(int parent, View edge) {
     n.edge.assign(edge.p, edge.p + edge.n);
     n.block = -1;
     n.stamp = 0;
+    n.prev = n.next = -1;
     n.children.clear();
     n.leased.clear();
     s_.nodes[std::size_t(parent)].children.insert(view(n.edge), id);
@@ -50,41 +51,63 @@ int ExactPrefixCache::new_node(int parent, View edge) {
     return id;
 }
 
+// The stamp a node had when the undo window opened is all a rollback needs, so
+// it is journaled at the node's first stamp change in the window only.
+void ExactPrefixCache::log_stamp(Node& n, int id) {
+    if (journaling_ && n.logged != window_) {
+        log(Op::Stamp, id, 0, n.stamp);
+        n.logged = window_;
+    }
+}
+
 void ExactPrefixCache::touch(int id) {
     Node& n = s_.nodes[std::size_t(id)];
-    log(Op::Stamp, id, 0, n.stamp);
+    log_stamp(n, id);
+    if (s_.lru_last != id) {
+        if (n.stamp) {  // unlink; a listed node that is not the tail has a successor
+            if (n.prev >= 0) s_.nodes[std::size_t(n.prev)].next = n.next;
+            else s_.lru_first = n.next;
+            s_.nodes[std::size_t(n.next)].prev = n.prev;
+        }
+        n.prev = s_.lru_last;
+        n.next = -1;
+        if (s_.lru_last >= 0) s_.nodes[std::size_t(s_.lru_last)].next = id;
+        else s_.lru_first = id;
+        s_.lru_last = id;
+    }
     n.stamp = ++s_.clock;
-    s_.lru.emplace_back(n.stamp, id);
-    if (!journaling_ && s_.lru.size() - s_.lru_head > 4 * s_.cached + 65536) compact_lru();
 }
 
 void ExactPrefixCache::unstamp(int id) noexcept {
     Node& n = s_.nodes[std::size_t(id)];
-    log(Op::Stamp, id, 0, n.stamp);
+    log_stamp(n, id);
+    if (n.stamp) {
+        if (n.prev >= 0) s_.nodes[std::size_t(n.prev)].next = n.next;
+        else s_.lru_first = n.next;
+        if (n.next >= 0) s_.nodes[std::size_t(n.next)].prev = n.prev;
+        else s_.lru_last = n.prev;
+    }
+    n.prev = n.next = -1;
     n.stamp = 0;
 }
 
-int ExactPrefixCache::lru_front() noexcept {
-    while (s_.lru_head < s_.lru.size()) {
-        const auto [stamp, id] = s_.lru[s_.lru_head];
-        const Node& n = s_.nodes[std::size_t(id)];
-        if (n.stamp == stamp && n.block >= 0) return id;
-        ++s_.lru_head;
+// Links every leased node (stamp != 0) in stamp order. Used after a rollback has
+// restored the stamps; `relink_` was reserved for all nodes when the window opened
+// and a rollback never leaves more nodes than that.
+void ExactPrefixCache::relink_lru() noexcept {
+    relink_.clear();
+    for (std::size_t id = 1; id < s_.nodes.size(); ++id)
+        if (s_.nodes[id].stamp) relink_.emplace_back(s_.nodes[id].stamp, int(id));
+    std::sort(relink_.begin(), relink_.end());
+    s_.lru_first = s_.lru_last = -1;
+    for (const auto& [stamp, id] : relink_) {
+        Node& n = s_.nodes[std::size_t(id)];
+        n.prev = s_.lru_last;
+        n.next = -1;
+        if (s_.lru_last >= 0) s_.nodes[std::size_t(s_.lru_last)].next = id;
+        else s_.lru_first = id;
+        s_.lru_last = id;
     }
-    return -1;
-}
-
-// Keeps only the current entries (in order). Never inside an undo window: a
-// rollback returns to a prefix of the list as it was when the window opened.
-void ExactPrefixCache::compact_lru() {
-    std::size_t out = 0;
-    for (std::size_t i = s_.lru_head; i < s_.lru.size(); ++i) {
-        const auto& e = s_.lru[i];
-        const Node& n = s_.nodes[std::size_t(e.second)];
-        if (n.stamp == e.first && n.block >= 0) s_.lru[out++] = e;
-    }
-    s_.lru.resize(out);
-    s_.lru_head = 0;
 }
 
 // Erase empty structural leaves from `id` upward, never the root or `keep`.
@@ -248,13 +271,12 @@ void ExactPrefixCache::publish(const PagedSequence& sequence) {
 }
 
 void ExactPrefixCache::begin_journal() {
-    if (s_.lru.size() - s_.lru_head > 4 * s_.cached + 65536) compact_lru();
     journal_.clear();
     pruned_edges_.clear();
+    relink_.reserve(s_.nodes.size());
     saved_.counters = s_;
-    saved_.lru_size = s_.lru.size();
-    saved_.lru_head = s_.lru_head;
     saved_.clock = s_.clock;
+    ++window_;
     journaling_ = true;
 }
 
@@ -309,9 +331,8 @@ void ExactPrefixCache::rollback_journal() noexcept {
         }
     }
     static_cast<Counters&>(s_) = saved_.counters;
-    s_.lru.resize(saved_.lru_size);
-    s_.lru_head = saved_.lru_head;
     s_.clock = saved_.clock;
+    relink_lru();
     journal_.clear();
     pruned_edges_.clear();
 }

@@ -19,9 +19,11 @@
 // Internals differ: nodes live in an arena addressed by index, keys are owned
 // token vectors, every mutation can be recorded in an undo journal (used to roll
 // back a failed batched step exactly, at a cost proportional to the step's own
-// changes), and publish() first tries the node path the same sequence reached at
-// its previous publish (each hinted node is checked against its parent and edge
-// before use, so a stale hint only costs the ordinary lookup).
+// changes), leases are kept in LRU order on an intrusive doubly-linked list
+// (touch = move to the tail, eviction = the head), and publish() first tries the
+// node path the same sequence reached at its previous publish (each hinted node
+// is checked against its parent and edge before use, so a stale hint only costs
+// the ordinary lookup).
 #pragma once
 #include <algorithm>
 #include <cstdint>
@@ -104,6 +106,8 @@ private:
         std::vector<std::int32_t> edge;
         int block = -1;
         std::uint64_t stamp = 0;  // LRU time of the last touch; 0 while not leased
+        std::uint64_t logged = 0; // undo window that already journaled the stamp
+        int prev = -1, next = -1; // LRU list neighbours while leased
         Children children;        // every child
         Children leased;          // children holding a lease (lookup set of reuse)
     };
@@ -115,17 +119,15 @@ private:
         std::size_t cached = 0, live_nodes = 0, key_tokens = 0;
         std::size_t hits = 0, misses = 0, reused = 0, evictions = 0;
     };
-    // LRU order is the order of the nodes' stamps. `lru` lists (stamp, node) in
-    // increasing stamp order; an entry is current while the node still holds a
-    // lease with that stamp, and the least recently used lease is the first
-    // current entry at or after `lru_head`. Stale entries are skipped there and
-    // dropped by compaction (outside undo windows only).
+    // LRU order is the order of the nodes' stamps: every leased node is on the
+    // list from `lru_first` (least recently used) to `lru_last`, and a touch takes
+    // the next clock value and moves the node to the tail, so list order and stamp
+    // order agree.
     struct State : Counters {
         std::vector<Node> nodes;
         std::vector<int> spare;
         std::vector<std::uint32_t> leases;  // per pool page: index nodes leasing it
-        std::vector<std::pair<std::uint64_t, int>> lru;
-        std::size_t lru_head = 0;
+        int lru_first = -1, lru_last = -1;
         std::uint64_t clock = 0;
     };
     // Journal entries: each records what its inverse needs.
@@ -134,7 +136,7 @@ private:
         Prune,       // a = node, b = parent; the edge moves to pruned_edges_
         LeasedAdd,   // a = parent, b = node
         LeasedDrop,  // a = parent, b = node
-        Stamp,       // a = node, v = previous stamp
+        Stamp,       // a = node, v = stamp before the window (logged once per window)
         Block,       // a = node, b = previous block
         Lease,       // a = page, b = +1 / -1
     };
@@ -149,21 +151,23 @@ private:
     void lease_add(int page, int delta);
 
     int new_node(int parent, View edge);
+    void log_stamp(Node& n, int id);
     void touch(int n);            // becomes the most recently used lease
     void unstamp(int n) noexcept; // leaves the LRU order
-    int lru_front() noexcept;     // least recently used lease, -1 when none
-    void compact_lru();
+    int lru_front() const noexcept { return s_.lru_first; }
+    void relink_lru() noexcept;   // rebuilds the list from the stamps
     void prune(int n, int keep) noexcept;
     void drop(int n, int keep) noexcept;
 
     KvBlockPool& pool_;
     State s_;  // the live index (nodes[0] is the root)
     bool journaling_ = false;
+    std::uint64_t window_ = 0;  // id of the current undo window (ids never repeat)
     std::vector<Entry> journal_;
     std::vector<std::vector<std::int32_t>> pruned_edges_;
+    std::vector<std::pair<std::uint64_t, int>> relink_;  // rollback scratch, reserved per window
     struct Window {
         Counters counters;
-        std::size_t lru_size = 0, lru_head = 0;
         std::uint64_t clock = 0;
     } saved_;
 };
