@@ -20,15 +20,18 @@
 //    (kind::tf32, M=128, N=BN, K=8) into one TMEM accumulator; tcgen05.commit
 //    releases the stage to the producer, and after the last block signals the
 //    accumulator barrier;
-//  * all 4 warps: each thread moves its TMEM lane (= tile row) with
-//    tcgen05.ld.32x32b into a row of a shared-memory tile (the stage ring is idle
-//    by then). The K slices of one output tile form a thread-block cluster
-//    (cluster dims 1 x 1 x slices): after a cluster barrier every CTA sums its
-//    share of the rows over all slices' tiles in slice order, reading the peers'
-//    shared memory directly (deterministic split-K for the small-M decode GEMMs,
-//    with no global round trip), and applies the fused epilogue with coalesced
-//    row-contiguous stores. A second cluster barrier keeps each tile alive until
-//    the peers have read it.
+//  * warps 2-3, meanwhile: gather the epilogue's per-row inputs that need global
+//    reads (RMSNorm row scales, RoPE destinations) into shared memory;
+//  * all 4 warps: the K slices of one output tile form a thread-block cluster
+//    (cluster dims 1 x 1 x slices) and each CTA owns a contiguous share of the
+//    tile's rows. After a cluster barrier (every slice past its MMAs, so every
+//    stage ring is idle) each thread moves its TMEM lane (= tile row) with
+//    tcgen05.ld.32x32b and stores it straight into the ring of the row's owner
+//    (st.shared::cluster, this slice's block there). After a second cluster
+//    barrier every CTA sums its rows over the slices' blocks in slice order from
+//    its own shared memory (deterministic split-K for the small-M decode GEMMs,
+//    no global round trip and no remote loads) and applies the fused epilogue
+//    with coalesced row-contiguous stores.
 // Every mbarrier wait is bounded; a timeout sets the error word, and the CTA still
 // passes both cluster barriers and releases its tensor memory.
 #include <cuda.h>
@@ -45,6 +48,7 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 32;  // fp32 elements per K block = one 128-byte swizzle row
 constexpr int kThreads = 128;
+constexpr int kMaxSlices = 8;  // portable cluster size
 
 template <int BN>
 struct TcConfig {
@@ -52,13 +56,18 @@ struct TcConfig {
     static constexpr int kATile = kBM * kBK * 4;  // bytes
     static constexpr int kBTile = BN * kBK * 4;
     static constexpr int kStage = 2 * kATile + 2 * kBTile;
-    static constexpr int kTileStride = BN + 4;  // floats per staged accumulator row (bank spread)
-    static constexpr int kTileBytes = kBM * kTileStride * 4;
-    static constexpr int kRing = kStages * kStage > kTileBytes ? kStages * kStage : kTileBytes;
+    static constexpr int kTileStride = BN + 4;  // floats per received accumulator row (bank spread)
+    // receive area: `slices` partial row blocks of ceil(128 / slices) rows each
+    static constexpr int kRecvBytes = (kBM + kMaxSlices) * kTileStride * 4;
+    static constexpr int kRing = kStages * kStage > kRecvBytes ? kStages * kStage : kRecvBytes;
     static constexpr int kSmem = kRing + 1024 /*align*/ + 256 /*barriers*/;
     static constexpr int kTmemCols = BN < 32 ? 32 : BN;
 };
-constexpr int kMaxSlices = 8;  // portable cluster size
+
+// Rows [slice_row0(r), slice_row0(r + 1)) of a tile are reduced and stored by
+// cluster rank r; row_owner is the inverse.
+__host__ __device__ constexpr int slice_row0(int rank, int slices) { return rank * kBM / slices; }
+__host__ __device__ constexpr int row_owner(int row, int slices) { return ((row + 1) * slices - 1) / kBM; }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -78,16 +87,17 @@ __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// float4 at the same shared-memory offset in cluster CTA `rank` (its own included).
-__device__ __forceinline__ float4 ld_cluster(const float* local, uint32_t rank) {
+// Address of the same shared-memory offset in cluster CTA `rank` (its own included).
+__device__ __forceinline__ uint32_t map_cluster(const void* local, uint32_t rank) {
     uint32_t remote;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(remote)
+    return remote;
+}
+
+__device__ __forceinline__ void st_cluster(uint32_t addr, float4 v) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+                 "f"(v.w)
                  : "memory");
-    return v;
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) {
@@ -97,9 +107,10 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 
 // Fused epilogue over rows [r0, r1) of the tile, columns in parallel (coalesced).
 // Each output float4 is the sum over the cluster's slices, in slice order, of the
-// staged tiles at the same offset. A thread takes kUnroll outputs per round and
-// issues the loads of every slice (and the residual it adds to) before the first
-// add, so the cluster-shared-memory round trips overlap instead of queueing.
+// partial tiles the slices pushed into this CTA's receive area (`recv`, one block
+// of `slice_floats` per slice, local row = row - r0). Per-row inputs that need
+// global reads (RMSNorm row scales, RoPE destinations and positions) were
+// gathered into shared memory by epilogue_rows_prepare while the MMAs ran.
 //  Store  : c[row][n0 + j] = acc
 //  AddTo  : c[row][n0 + j] += acc                        (residual add)
 //  SwiGLU : per 64-column group g of the tile, columns 0..31 are gate and 32..63 up
@@ -133,9 +144,44 @@ __device__ __forceinline__ float* rope_destination(const TcGemmParams& p, int he
     return (head < kHeads + kKvHeads ? r.keys : r.values) + off + kvh * kHeadDim;
 }
 
+// Per-row epilogue inputs of rows [r0, r1), indexed by row - r0.
+struct RowInputs {
+    float* scale;  // RMSNorm 1 / rms (SwiGLU, Rope with ssq_in)
+    float** dst;   // Rope: destination of the tile's head
+    int* pos;      // Rope: cos / sin table row
+};
+
+// Gathers RowInputs with `threads` threads (thread index t); runs beside the MMAs.
 template <int BN, Epilogue E>
-__device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float* tile, int m0, int n0, int r0,
-                                              int r1, int slices) {
+__device__ __forceinline__ void epilogue_rows_prepare(const TcGemmParams& p, const RowInputs& in, int m0, int n0,
+                                                      int r0, int r1, int t, int threads) {
+    constexpr bool kPairs = E == Epilogue::SwiGLU || E == Epilogue::Rope;
+    if (kPairs && p.ssq_in != nullptr) {
+        // this CTA's rows' 1 / rms from the producer's per-64-column sums of
+        // squares, summed in group order
+        const int groups = p.k / kSsqGroup;
+        for (int r = r0 + t; r < r1; r += threads) {
+            float ss = 0.f;
+            if (m0 + r < p.m)
+                for (int g = 0; g < groups; ++g) ss = __fadd_rn(ss, p.ssq_in[size_t(m0 + r) * groups + g]);
+            in.scale[r - r0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(p.k)), p.eps)));
+        }
+    }
+    if constexpr (E == Epilogue::Rope) {
+        const int head = n0 / 64;
+        for (int r = r0 + t; r < r1; r += threads) {
+            in.dst[r - r0] = nullptr;
+            in.pos[r - r0] = 0;
+            if (m0 + r >= p.m) continue;
+            in.dst[r - r0] = rope_destination(p, head, m0 + r);
+            if (head < kHeads + kKvHeads) in.pos[r - r0] = min(p.rope.row_pos[m0 + r], p.rope.max_position - 1);
+        }
+    }
+}
+
+template <int BN, Epilogue E>
+__device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float* recv, int slice_floats,
+                                              const RowInputs& in, int m0, int n0, int r0, int r1, int slices) {
     using Cfg = TcConfig<BN>;
     constexpr bool kSwiGLU = E == Epilogue::SwiGLU;
     constexpr bool kRope = E == Epilogue::Rope;
@@ -146,81 +192,61 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
     constexpr int kLoads = kPairs ? 2 : 1;
     const int head = n0 / 64;  // Rope: the tile's head
     const int total = (r1 - r0) * kItems;
-    // RMSNorm folded in (consumer side): this CTA's rows' 1 / rms from the producer's
-    // per-64-column sums of squares, summed in group order
-    __shared__ float row_scale[kBM];
     const bool scaled = kPairs && p.ssq_in != nullptr;
-    if (scaled) {
-        const int groups = p.k / kSsqGroup;
-        for (int r = r0 + int(threadIdx.x); r < r1; r += kThreads) {
-            float ss = 0.f;
-            if (m0 + r < p.m)
-                for (int g = 0; g < groups; ++g) ss = __fadd_rn(ss, p.ssq_in[size_t(m0 + r) * groups + g]);
-            row_scale[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(p.k)), p.eps)));
-        }
-        __syncthreads();
-    }
     const bool produce = E == Epilogue::AddTo && p.norm_w != nullptr;
     // warp-uniform trip count (the producer's half-warp shuffles need every lane)
     for (int base = threadIdx.x; base - int(threadIdx.x & 31) < total; base += kThreads * kUnroll) {
         int off[kUnroll];
         bool live[kUnroll];
         float4* dst[kUnroll];
-        float4 resid[kUnroll];
+        float4 resid[kUnroll], wn[kUnroll];
         float4 rc[kUnroll], rs[kUnroll];  // Rope: cos / sin of the item's dims
+        // global loads of the round first, so that their latencies overlap
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             const int i = base + u * kThreads;
-            const int row = r0 + (i < total ? i / kItems : 0), it = i % kItems;
-            live[u] = i < total && m0 + row < p.m;
-            off[u] = row * Cfg::kTileStride + (kPairs ? 64 * (it / 8) + 4 * (it % 8) : 4 * it);
+            const int lr = i < total ? i / kItems : 0, it = i % kItems;
+            live[u] = i < total && m0 + r0 + lr < p.m;
+            off[u] = lr * Cfg::kTileStride + (kPairs ? 64 * (it / 8) + 4 * (it % 8) : 4 * it);
             dst[u] = nullptr;
             if (kRope) {
                 if (live[u]) {
-                    float* d = rope_destination(p, head, m0 + row);
+                    float* d = in.dst[lr];
                     dst[u] = d ? reinterpret_cast<float4*>(d + 4 * it) : nullptr;
                     if (head < kHeads + kKvHeads) {
-                        const int pc = min(p.rope.row_pos[m0 + row], p.rope.max_position - 1);
+                        const int pc = in.pos[lr];
                         rc[u] = *reinterpret_cast<const float4*>(p.rope.cos + size_t(pc) * 32 + 4 * it);
                         rs[u] = *reinterpret_cast<const float4*>(p.rope.sin + size_t(pc) * 32 + 4 * it);
                     }
                 }
             } else if (!kSwiGLU) {
-                dst[u] = reinterpret_cast<float4*>(p.c + size_t(m0 + row) * p.ldc + n0 + 4 * it);
-                if (E == Epilogue::AddTo && live[u]) resid[u] = *dst[u];
+                dst[u] = reinterpret_cast<float4*>(p.c + size_t(m0 + r0 + lr) * p.ldc + n0 + 4 * it);
+                if (E == Epilogue::AddTo && live[u]) {
+                    resid[u] = *dst[u];
+                    if (produce) wn[u] = *reinterpret_cast<const float4*>(p.norm_w + n0 + 4 * it);
+                }
             }
         }
-        float4 v[kMaxSlices][kUnroll][kLoads];
-#pragma unroll
-        for (int k = 0; k < kMaxSlices; ++k)
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u)
-#pragma unroll
-                for (int h = 0; h < kLoads; ++h) {
-                    const float* at = tile + off[u] + 32 * h;
-                    if (k < slices)
-                        v[k][u][h] = slices == 1 ? *reinterpret_cast<const float4*>(at) : ld_cluster(at, uint32_t(k));
-                }
         float4 acc[kUnroll][kLoads];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u)
 #pragma unroll
             for (int h = 0; h < kLoads; ++h) {
-                acc[u][h] = v[0][u][h];
-#pragma unroll
-                for (int k = 1; k < kMaxSlices; ++k)
-                    if (k < slices) {
-                        acc[u][h].x += v[k][u][h].x;
-                        acc[u][h].y += v[k][u][h].y;
-                        acc[u][h].z += v[k][u][h].z;
-                        acc[u][h].w += v[k][u][h].w;
-                    }
+                const float* at = recv + off[u] + 32 * h;
+                acc[u][h] = *reinterpret_cast<const float4*>(at);
+                for (int k = 1; k < slices; ++k) {
+                    const float4 v = *reinterpret_cast<const float4*>(at + k * slice_floats);
+                    acc[u][h].x += v.x;
+                    acc[u][h].y += v.y;
+                    acc[u][h].z += v.z;
+                    acc[u][h].w += v.w;
+                }
             }
         if (scaled) {
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u) {
                 const int i = base + u * kThreads;
-                const float sc = row_scale[r0 + (i < total ? i / kItems : 0)];
+                const float sc = in.scale[i < total ? i / kItems : 0];
 #pragma unroll
                 for (int h = 0; h < kLoads; ++h)
                     acc[u][h] = make_float4(__fmul_rn(acc[u][h].x, sc), __fmul_rn(acc[u][h].y, sc),
@@ -273,7 +299,7 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
                     if (produce) {
                         // the next GEMM's A operand: y * norm weight as TF32 halves
                         const int col = n0 + 4 * it;
-                        const float4 w = *reinterpret_cast<const float4*>(p.norm_w + col);
+                        const float4 w = wn[u];
                         float4 hv, lv;
                         split_tf32(__fmul_rn(y.x, w.x), hv.x, lv.x);
                         split_tf32(__fmul_rn(y.y, w.y), hv.y, lv.y);
@@ -330,6 +356,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int kb_per = (kb_total + splits - 1) / splits;
     const int kb_begin = blockIdx.z * kb_per, kb_end = min(kb_total, kb_begin + kb_per);
     const int kblocks = kb_end - kb_begin;
+    // this CTA reduces and stores tile rows [r0, r1)
+    const int rank = splits > 1 ? int(cluster_rank()) : 0;
+    const int r0 = slice_row0(rank, splits), r1 = slice_row0(rank + 1, splits);
+    __shared__ float row_scale[kBM];
+    __shared__ float* row_dst[kBM];
+    __shared__ int row_pos[kBM];
+    const RowInputs rows{row_scale, row_dst, row_pos};
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
@@ -408,47 +441,57 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(&empty[s]);
         }
         if (ok) mma_commit(accum);
+    } else if (warp >= 2) {
+        // idle until the accumulator is ready: gather the epilogue's row inputs
+        epilogue_rows_prepare<BN, E>(p, rows, m0, n0, r0, r1, int(threadIdx.x) - 64, kThreads - 64);
     }
     __syncwarp();
     // Epilogue. The outcome is made CTA-uniform before anything that holds a barrier.
     if (!mbar_wait_bounded(accum, 0)) *failed = 1;
     __syncthreads();
     const bool ok = *failed == 0;
-    // Stage this slice's accumulator in shared memory: thread = tile row.
-    float* tile = reinterpret_cast<float*>(smem);
+    // Once every CTA of the cluster is past its MMAs, every stage ring is idle and
+    // becomes a receive area: each thread pushes its TMEM lane (= tile row) into
+    // the owner CTA of that row, as this slice's block there.
+    if (splits > 1) cluster_sync();
+    const int rows_max = (kBM + splits - 1) / splits;
+    const int slice_floats = rows_max * Cfg::kTileStride;
+    float* recv = reinterpret_cast<float*>(smem);
     if (ok) {
         tmem_fence_after();
         const int row = warp * 32 + lane;
+        const int owner = row_owner(row, splits);
+        float* slot = recv + rank * slice_floats + (row - slice_row0(owner, splits)) * Cfg::kTileStride;
+        const uint32_t remote = splits > 1 ? map_cluster(slot, uint32_t(owner)) : 0u;
 #pragma unroll
         for (int c0 = 0; c0 < BN; c0 += 32) {
             uint32_t r[32];
             tmem_load32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c0), r);
-            float4* dst = reinterpret_cast<float4*>(tile + row * Cfg::kTileStride + c0);
 #pragma unroll
-            for (int v = 0; v < 8; ++v)
-                dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                     __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+            for (int v = 0; v < 8; ++v) {
+                const float4 x = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                             __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+                if (splits > 1)
+                    st_cluster(remote + uint32_t((c0 + 4 * v) * 4), x);
+                else
+                    *reinterpret_cast<float4*>(slot + c0 + 4 * v) = x;
+            }
         }
     } else if (threadIdx.x == 0) {
         raise_error(p.error, kErrTimeout);
     }
     tmem_fence_before();
+    // every slice's block has arrived (and the row inputs are visible)
     if (splits > 1)
-        cluster_sync();  // every slice's tile is staged
+        cluster_sync();
     else
         __syncthreads();
-    if (ok) {
-        const int rank = splits > 1 ? int(cluster_rank()) : 0;
-        const int r0 = rank * kBM / splits, r1 = (rank + 1) * kBM / splits;
-        epilogue_rows<BN, E>(p, tile, m0, n0, r0, r1, splits);
-    }
-    if (splits > 1) cluster_sync();  // the peers have read this CTA's tile
-    __syncthreads();
     if (warp == 0) {
         tmem_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(uint32_t(Cfg::kTmemCols))
                      : "memory");
     }
+    if (ok) epilogue_rows<BN, E>(p, recv, slice_floats, rows, m0, n0, r0, r1, splits);
 }
 
 // Clusters of each size (index = slices) that the device holds at once, per tile
