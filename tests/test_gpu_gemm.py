@@ -45,7 +45,7 @@ def test_tc_gemm_matches_float64(built, m, n, k):
 @pytest.mark.gpu
 @pytest.mark.parametrize("m,n,k", [(7, 576, 1536), (64, 3072, 576)])
 def test_tc_gemm_split_k_is_deterministic(built, m, n, k):
-    """Split-K partials are summed in slice order by whichever CTA finishes last:
+    """Split-K partials are summed in slice order by the CTA that owns the row:
     repeated launches give bit-identical results, and a row's result does not
     depend on the other rows of the batch (the first rows of a larger M match
     the same rows computed alone)."""

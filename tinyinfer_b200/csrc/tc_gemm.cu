@@ -100,9 +100,18 @@ __device__ __forceinline__ void st_cluster(uint32_t addr, float4 v) {
                  : "memory");
 }
 
+// g / (1 + exp(-g)) * u (miniprefix/src/backend/cpu/llama_runner.cpp:97). The
+// reciprocal of d = 1 + exp(-g) >= 1 is the hardware approximation refined by one
+// Newton step, r' = r + r (1 - d r), within about 1 ulp of 1 / d; it has no
+// per-element branch (unlike the IEEE-rounded division and reciprocal), so the
+// compiler interleaves a round's independent outputs. d = inf (g < -88) gives 0.
 __device__ __forceinline__ float silu_mul(float g, float u) {
-    // g / (1 + exp(-g)) * u with an IEEE-rounded reciprocal
-    return __fmul_rn(__fmul_rn(g, __frcp_rn(__fadd_rn(1.0f, expf(-g)))), u);
+    const float d = __fadd_rn(1.0f, expf(-g));
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+    r = fmaf(r, fmaf(-d, r, 1.0f), r);
+    r = isinf(d) ? 0.0f : r;
+    return __fmul_rn(__fmul_rn(g, r), u);
 }
 
 // Fused epilogue over rows [r0, r1) of the tile, columns in parallel (coalesced).
