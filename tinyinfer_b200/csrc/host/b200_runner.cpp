@@ -2,6 +2,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <exception>
 
 namespace miniprefix_b200 {
 namespace {
@@ -261,6 +262,7 @@ std::size_t B200Runner::stage_append(const RequestId& id, const std::vector<Toke
 
 void B200Runner::flush() {
     if (descs_.empty()) {
+        kv_.settle_publishes();
         kv_.next_epoch();
         ++epoch_;
         return;
@@ -270,20 +272,41 @@ void B200Runner::flush() {
     out_finite_.assign(std::size_t(n), 0);
     const bool timed = cost_timing_ && !regions_.empty();
     mp_cow_timing(ctx_, timed);
-    const int rc = mp_forward(ctx_, descs_.data(), n, tokens_.data(), entries_.data(), int32_t(entries_.size()),
-                              regions_.data(), int32_t(regions_.size()), out_tokens_.data(), out_finite_.data(),
-                              nullptr, options_.timeout_ms);
+    // mp_forward in three parts: the step's queued prefix-cache publishes run on
+    // the host between the launch and the wait for the device.
+    int rc = mp_forward_prepare(ctx_, descs_.data(), n, tokens_.data(), entries_.data(), int32_t(entries_.size()),
+                                regions_.data(), int32_t(regions_.size()));
+    std::string error;
+    std::exception_ptr publish_error;
+    if (rc == MP_OK) {
+        rc = mp_forward_launch(ctx_);
+        if (rc == MP_OK) {
+            try {
+                kv_.settle_publishes();
+            } catch (...) {
+                publish_error = std::current_exception();
+            }
+        } else {
+            error = mp_last_error();
+        }
+        // after a failed launch this still waits for what was enqueued and ends the step
+        const int collected = mp_forward_collect(ctx_, out_tokens_.data(), out_finite_.data(), nullptr,
+                                                 options_.timeout_ms);
+        if (rc == MP_OK) rc = collected;
+    }
+    if (rc != MP_OK && error.empty()) error = mp_last_error();
     ++flushes_;
     stats_.token_uploaded_bytes += tokens_.size() * sizeof(TokenId);
     stats_.block_table_uploaded_bytes += entries_.size() * sizeof(int32_t);
-    if (rc != MP_OK && rc != MP_ERR_NONFINITE) {
+    if ((rc != MP_OK && rc != MP_ERR_NONFINITE) || publish_error) {
         for (auto& m : mirror_) m.clear();
         descs_.clear();
         tokens_.clear();
         entries_.clear();
         regions_.clear();
         tickets_.clear();
-        throw std::runtime_error(std::string("B200 forward: ") + mp_last_error());
+        if (publish_error) std::rethrow_exception(publish_error);
+        throw std::runtime_error(std::string("B200 forward: ") + error);
     }
     if (timed) {
         float ms = 0.f;

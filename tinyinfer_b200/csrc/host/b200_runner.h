@@ -50,7 +50,8 @@ public:
     void create(const RequestId& id) override;
     void fork_sequence(const RequestId& source, const RequestId& target) override;
     std::size_t reuse_prefix(const RequestId& id, const std::vector<TokenId>& prompt) override;
-    void cache_prefix(const RequestId& id) override { kv_.cache_prefix(id); }
+    // inside a batch the publish runs while the batch's forward computes
+    void cache_prefix(const RequestId& id) override { kv_.cache_prefix_deferred(id); }
     void clear_prefix_cache() override;
     std::vector<float> append(const RequestId& id, const std::vector<TokenId>& tokens) override;
     void release(const RequestId& id) override;

@@ -1,5 +1,7 @@
 #include "kv_manager.h"
 
+#include <algorithm>
+
 namespace miniprefix_b200 {
 
 KVManager::KVManager(KvCacheConfig config, int layers, int width, int context, int vocabulary)
@@ -78,6 +80,7 @@ void KVManager::touch_reservation(const RequestId& id) {
 }
 
 KvAdmission KVManager::reserve_request(const RequestId& id, std::size_t max_tokens) {
+    settle_publishes();
     require_idle();
     if (contains(id) || reservations_.count(id)) throw std::invalid_argument("duplicate KV reservation");
     if (!max_tokens || max_tokens > std::size_t(context_)) throw std::invalid_argument("invalid KV reservation context");
@@ -104,6 +107,7 @@ void KVManager::release_reservation(const RequestId& id) noexcept {
 }
 
 void KVManager::create(const RequestId& id) {
+    settle_publishes();
     require_idle();
     if (sequences_.count(id)) throw std::invalid_argument("sequence already exists");
     touch_sequence(id);
@@ -111,6 +115,7 @@ void KVManager::create(const RequestId& id) {
 }
 
 void KVManager::fork_sequence(const RequestId& source, const RequestId& target) {
+    settle_publishes();
     require_idle();
     const auto& original = sequences_.at(source).sequence;
     auto& destination = idle_state(target).sequence;
@@ -131,6 +136,7 @@ void KVManager::fork_sequence(const RequestId& source, const RequestId& target) 
 }
 
 std::size_t KVManager::reuse_prefix(const RequestId& id, const std::vector<TokenId>& prompt) {
+    settle_publishes();
     if (prompt.empty() || prompt.size() > std::size_t(context_)) throw std::invalid_argument("invalid prefix context");
     for (auto t : prompt)
         if (t < 0 || t >= vocabulary_) throw std::invalid_argument("invalid prefix token");
@@ -151,14 +157,52 @@ std::size_t KVManager::reuse_prefix(const RequestId& id, const std::vector<Token
     return count;
 }
 
-void KVManager::cache_prefix(const RequestId& id) {
-    auto& sequence = idle_state(id).sequence;
+void KVManager::publish(State& state) {
     ++costs_.publish_calls;
     CostTimer timer(cost_timing_, costs_.publish_ns);
-    prefix_.publish(sequence);
+    prefix_.publish(state.sequence);
+}
+
+void KVManager::cache_prefix(const RequestId& id) {
+    settle_publishes();
+    publish(idle_state(id));
+}
+
+void KVManager::cache_prefix_deferred(const RequestId& id) {
+    if (!checkpoint_) return cache_prefix(id);
+    auto& state = idle_state(id);
+    // a publish that would fail fails here, where the caller made it
+    if (state.publish_queued || state.sequence.tokens.size() != std::size_t(state.sequence.used))
+        return cache_prefix(id);
+    state.publish_queued = true;
+    pending_publishes_.push_back(&state);
+}
+
+void KVManager::settle_publishes() {
+    // (not inside an append transaction: the queue waits for its end)
+    if (pending_publishes_.empty() || append_active_) return;
+    std::vector<State*> queue;
+    queue.swap(pending_publishes_);
+    for (State* s : queue) s->publish_queued = false;
+    for (State* s : queue) publish(*s);  // a failure drops the rest, as it would end the step
+}
+
+bool KVManager::commutes_with_publishes(const State& state, std::size_t tokens) const {
+    const auto& sequence = state.sequence;
+    const std::size_t bt = std::size_t(config().block_tokens);
+    const std::size_t end = std::size_t(sequence.used) + tokens;
+    if (state.publish_queued) return false;
+    if ((end + bt - 1) / bt > sequence.blocks.size()) return false;  // takes pages from the free list
+    return sequence.used % int(bt) == 0 || pool_.references(sequence.blocks.back()) == 1;  // no copy on write
+}
+
+CostStats KVManager::cost_stats() const {
+    settle_for_read();
+    return costs_;
 }
 
 void KVManager::clear_prefix_cache() {
+    settle_publishes();
     require_idle();
     for (const auto& item : sequences_)
         if (item.second.appending) throw std::logic_error("cannot clear prefix cache during KV append");
@@ -191,6 +235,8 @@ KVManager::Append::Append(KVManager& owner, const RequestId& id, const std::vect
     : owner_(&owner), id_(id), state_(&owner.idle_state(id)), tokens_(tokens),
       original_blocks_(state_->sequence.blocks.size()) {
     auto& sequence = state_->sequence;
+    if (!owner.pending_publishes_.empty() && !owner.commutes_with_publishes(*state_, tokens.size()))
+        owner.settle_publishes();
     if (tokens.empty() || tokens.size() > std::size_t(owner.context_ - sequence.used))
         throw std::invalid_argument("context overflow/empty input");
     owner.validate_tokens(tokens);
@@ -263,12 +309,14 @@ void KVManager::Append::rollback() noexcept {
 }
 
 void KVManager::reset_sequence(const RequestId& id) {
+    settle_publishes();
     auto& state = idle_state(id);
     touch_sequence(id, true);
     pool_.release(state.sequence);
 }
 
 void KVManager::release(const RequestId& id) {
+    settle_publishes();
     require_idle();
     auto it = sequences_.find(id);
     if (it == sequences_.end()) throw std::invalid_argument("unknown sequence");
@@ -285,6 +333,7 @@ void KVManager::release(const RequestId& id) {
 }
 
 void KVManager::clear() {
+    settle_publishes();
     require_idle();
     for (const auto& item : sequences_)
         if (item.second.appending) throw std::logic_error("cannot clear sequences during KV append");
@@ -300,6 +349,7 @@ void KVManager::clear() {
 }
 
 KvStats KVManager::stats() const {
+    settle_for_read();
     KvStats r;
     r.live_sequences = sequences_.size();
     r.forward_tokens = forward_tokens_;
@@ -321,6 +371,7 @@ KvStats KVManager::stats() const {
 }
 
 void KVManager::begin_checkpoint() {
+    settle_publishes();
     require_idle();
     checkpoint_ = std::make_unique<Checkpoint>();
     checkpoint_->live = pool_.live_blocks();
@@ -334,6 +385,8 @@ void KVManager::begin_checkpoint() {
 
 void KVManager::restore_checkpoint() {
     if (!checkpoint_) throw std::logic_error("no KV checkpoint");
+    for (State* s : pending_publishes_) s->publish_queued = false;
+    pending_publishes_.clear();  // never applied: nothing of them to undo
     auto& cp = *checkpoint_;
     pool_.attach_journal(nullptr);
     pool_.undo(cp.pool_journal, 0, cp.live, cp.peak);
@@ -367,6 +420,7 @@ void KVManager::restore_checkpoint() {
 }
 
 void KVManager::end_checkpoint() {
+    settle_publishes();
     pool_.attach_journal(nullptr);
     prefix_.end_journal();
     checkpoint_.reset();

@@ -15,6 +15,16 @@
 // which every mutation is recorded so that the exact state at the checkpoint can
 // be restored (pages, references, free-list order, sequences, reservations,
 // prefix index and counters).
+//
+// Inside a window a publish may wait (cache_prefix_deferred): queued publishes
+// run in call order at settle_publishes(), and before any operation whose
+// outcome they could change -- every public operation except an append that
+// commutes with them. A publish changes only the prefix index, page references
+// and (evicting a cache-only page) the free list; an append that needs no new
+// page and writes only pages nobody else references (no copy on write), of a
+// sequence without a queued publish, reads none of that, so every page,
+// reference, free-list and index state matches the un-deferred order. A
+// runner publishes the queue while its device forward runs.
 #pragma once
 #include <functional>
 #include <map>
@@ -30,6 +40,7 @@ class KVManager {
     struct State {
         PagedSequence sequence;
         bool appending = false;
+        bool publish_queued = false;  // in pending_publishes_
     };
 
 public:
@@ -87,6 +98,8 @@ public:
     void fork_sequence(const RequestId& source, const RequestId& target);
     std::size_t reuse_prefix(const RequestId& id, const std::vector<TokenId>& prompt);
     void cache_prefix(const RequestId& id);
+    void cache_prefix_deferred(const RequestId& id);  // cache_prefix, queued inside a checkpoint window
+    void settle_publishes();
     void clear_prefix_cache();
     Append prepare_append(const RequestId& id, const std::vector<TokenId>& tokens) {
         return Append(*this, id, tokens);
@@ -96,7 +109,7 @@ public:
     void clear();
     KvStats stats() const;
     void set_cost_timing(bool enabled) { cost_timing_ = enabled; }
-    CostStats cost_stats() const { return costs_; }
+    CostStats cost_stats() const;
     const KvBlockPool& pool() const { return pool_; }
     bool freed_this_epoch(int block) const { return pool_.freed_this_epoch(block); }
     void next_epoch() { pool_.next_epoch(); }
@@ -114,6 +127,11 @@ private:
     void reserve_pages(const RequestId& id, PagedSequence& sequence, int end, bool& cow);
     void touch_sequence(const RequestId& id, bool dropping = false);  // journal a sequence mutation
     void touch_reservation(const RequestId& id);
+    void publish(State& state);
+    bool commutes_with_publishes(const State& state, std::size_t tokens) const;
+    // Readers see the state after every queued publish (the queue is an
+    // evaluation-order detail, not part of the observable state).
+    void settle_for_read() const { const_cast<KVManager*>(this)->settle_publishes(); }
 
     int layers_, width_, context_, vocabulary_;
     KvBlockPool pool_;
@@ -125,6 +143,9 @@ private:
     bool append_active_ = false;
     bool cost_timing_ = false;
     CostStats costs_;
+    // Queued publishes, in call order. A queued sequence is never erased: every
+    // operation that can erase one settles or (restore) drops the queue first.
+    std::vector<State*> pending_publishes_;
 
     // A sequence as it was at the checkpoint. Tokens only grow inside a window
     // unless the sequence is released, so only their count is kept until then.

@@ -30,7 +30,7 @@ public:
     std::size_t reuse_prefix(const RequestId& id, const std::vector<TokenId>& p) override {
         return kv_.reuse_prefix(id, p);
     }
-    void cache_prefix(const RequestId& id) override { kv_.cache_prefix(id); }
+    void cache_prefix(const RequestId& id) override { kv_.cache_prefix_deferred(id); }
     void clear_prefix_cache() override { kv_.clear_prefix_cache(); }
     std::vector<float> append(const RequestId& id, const std::vector<TokenId>& tokens) override;
     void release(const RequestId& id) override { kv_.release(id); }
@@ -42,6 +42,7 @@ public:
     bool batched() const override { return true; }
     void begin_batch() override;
     std::size_t stage_append(const RequestId& id, const std::vector<TokenId>& tokens) override;
+    void flush() override { kv_.settle_publishes(); }
     void restore_batch() override;
     void fail_append(const RequestId& id, const std::vector<TokenId>& tokens) override;
     void end_batch() override;
