@@ -187,13 +187,20 @@ void KVManager::settle_publishes() {
     for (State* s : queue) publish(*s);  // a failure drops the rest, as it would end the step
 }
 
+// A queued publish changes the prefix index, leases (page references) and LRU
+// order, and frees a page only by evicting the last lease of a cache-only page.
+// So an append commutes with the queue when it copies no page (its partial last
+// page has no other holder), and any pages it takes from the free list come
+// without an eviction while no page is cache-only (the queue then frees none).
 bool KVManager::commutes_with_publishes(const State& state, std::size_t tokens) const {
     const auto& sequence = state.sequence;
     const std::size_t bt = std::size_t(config().block_tokens);
     const std::size_t end = std::size_t(sequence.used) + tokens;
     if (state.publish_queued) return false;
-    if ((end + bt - 1) / bt > sequence.blocks.size()) return false;  // takes pages from the free list
-    return sequence.used % int(bt) == 0 || pool_.references(sequence.blocks.back()) == 1;  // no copy on write
+    if (sequence.used % int(bt) && pool_.references(sequence.blocks.back()) != 1) return false;  // may copy
+    const std::size_t count = (end + bt - 1) / bt;
+    if (count <= sequence.blocks.size()) return true;
+    return pool_.cache_only_blocks() == 0 && pool_.free_blocks() >= count - sequence.blocks.size();
 }
 
 CostStats KVManager::cost_stats() const {

@@ -19,12 +19,9 @@
 // Inside a window a publish may wait (cache_prefix_deferred): queued publishes
 // run in call order at settle_publishes(), and before any operation whose
 // outcome they could change -- every public operation except an append that
-// commutes with them. A publish changes only the prefix index, page references
-// and (evicting a cache-only page) the free list; an append that needs no new
-// page and writes only pages nobody else references (no copy on write), of a
-// sequence without a queued publish, reads none of that, so every page,
-// reference, free-list and index state matches the un-deferred order. A
-// runner publishes the queue while its device forward runs.
+// commutes with them (commutes_with_publishes), so every page, reference,
+// free-list and index state matches the un-deferred order. A runner publishes
+// the queue while its device forward runs.
 #pragma once
 #include <functional>
 #include <map>

@@ -18,17 +18,31 @@ KvBlockPool::KvBlockPool(KvCacheConfig config, int layers, int width) : config_(
     }
     block_elements_ = total / std::size_t(config.max_blocks);
     refs_.assign(std::size_t(config.max_blocks), 0);
+    leases_.assign(std::size_t(config.max_blocks), 0);
     freed_epoch_.assign(std::size_t(config.max_blocks), 0);
     free_.resize(std::size_t(config.max_blocks));
     // Descending, so that pages 0, 1, 2, ... are handed out first.
     for (int i = 0; i < config.max_blocks; ++i) free_[std::size_t(i)] = config.max_blocks - 1 - i;
 }
 
+void KvBlockPool::set_refs(std::size_t block, std::uint32_t refs) noexcept {
+    const bool before = cache_only(block);
+    refs_[block] = refs;
+    cache_only_ = cache_only_ + std::size_t(cache_only(block)) - std::size_t(before);
+}
+
+void KvBlockPool::add_lease(int block, int delta) noexcept {
+    const std::size_t b = std::size_t(block);
+    const bool before = cache_only(b);
+    leases_[b] = std::uint32_t(int(leases_[b]) + delta);
+    cache_only_ = cache_only_ + std::size_t(cache_only(b)) - std::size_t(before);
+}
+
 int KvBlockPool::allocate() {
     if (free_.empty()) throw KvCapacityError("paged KV block pool exhausted");
     const int block = free_.back();
     free_.pop_back();
-    refs_[std::size_t(block)] = 1;
+    set_refs(std::size_t(block), 1);
     ++live_;
     peak_ = std::max(peak_, live_);
     record(JournalEntry::Popped, block);
@@ -36,14 +50,13 @@ int KvBlockPool::allocate() {
 }
 
 void KvBlockPool::retain(int block) {
-    ++refs_.at(std::size_t(block));
+    set_refs(std::size_t(block), refs_.at(std::size_t(block)) + 1);
     record(JournalEntry::RefUp, block);
 }
 
 void KvBlockPool::unref(int block) noexcept {
-    auto& r = refs_[std::size_t(block)];
-    --r;
-    if (r == 0) {
+    set_refs(std::size_t(block), refs_[std::size_t(block)] - 1);
+    if (refs_[std::size_t(block)] == 0) {
         free_.push_back(block);
         --live_;
         freed_epoch_[std::size_t(block)] = epoch_;
@@ -63,7 +76,7 @@ void KvBlockPool::reserve(PagedSequence& sequence, int end) {
     while (sequence.blocks.size() < needed) {
         const int block = free_.back();
         free_.pop_back();
-        refs_[std::size_t(block)] = 1;
+        set_refs(std::size_t(block), 1);
         ++live_;
         sequence.blocks.push_back(block);
         record(JournalEntry::Popped, block);
@@ -95,18 +108,18 @@ void KvBlockPool::undo(const std::vector<JournalEntry>& journal, std::size_t mar
                        std::size_t peak) noexcept {
     for (std::size_t i = journal.size(); i-- > mark;) {
         const auto& e = journal[i];
-        auto& r = refs_[std::size_t(e.block)];
+        const std::size_t b = std::size_t(e.block);
         switch (e.kind) {
             case JournalEntry::Popped:  // was free with 0 references, at the back
-                r = 0;
+                set_refs(b, 0);
                 free_.push_back(e.block);
                 break;
             case JournalEntry::Pushed:  // was live with 1 reference
                 free_.pop_back();
-                r = 1;
+                set_refs(b, 1);
                 break;
-            case JournalEntry::RefUp: --r; break;
-            case JournalEntry::RefDown: ++r; break;
+            case JournalEntry::RefUp: set_refs(b, refs_[b] - 1); break;
+            case JournalEntry::RefDown: set_refs(b, refs_[b] + 1); break;
         }
     }
     live_ = live;

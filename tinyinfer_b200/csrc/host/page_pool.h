@@ -28,6 +28,12 @@ public:
     std::size_t free_blocks() const { return free_.size(); }
     // Throws std::out_of_range for a page outside the pool.
     std::size_t references(int block) const { return refs_.at(std::size_t(block)); }
+    // Prefix-cache leases per page (index nodes holding it; each is also one of the
+    // page's references), kept beside the references so that the number of
+    // cache-only pages -- leased, and every reference a lease -- is exact at all times.
+    std::size_t leases(int block) const { return leases_[std::size_t(block)]; }
+    void add_lease(int block, int delta) noexcept;
+    std::size_t cache_only_blocks() const { return cache_only_; }
 
     int allocate();
     void retain(int block);
@@ -56,10 +62,14 @@ private:
     void record(JournalEntry::Kind kind, int block) {
         if (journal_) journal_->push_back({kind, block});
     }
+    bool cache_only(std::size_t block) const { return leases_[block] && refs_[block] == leases_[block]; }
+    void set_refs(std::size_t block, std::uint32_t refs) noexcept;  // every reference count write
     KvCacheConfig config_;
     std::size_t block_elements_ = 0;
     std::vector<int> free_;  // back() is handed out next
     std::vector<std::uint32_t> refs_;
+    std::vector<std::uint32_t> leases_;
+    std::size_t cache_only_ = 0;
     std::size_t live_ = 0, peak_ = 0;
     std::vector<JournalEntry>* journal_ = nullptr;
     std::vector<std::uint32_t> freed_epoch_;

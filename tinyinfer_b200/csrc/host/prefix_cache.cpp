@@ -7,23 +7,15 @@ namespace miniprefix_b200 {
 
 ExactPrefixCache::ExactPrefixCache(KvBlockPool& pool) : pool_(pool) {
     s_.nodes.emplace_back();
-    s_.leases.assign(std::size_t(std::max(pool.config().max_blocks, 0)), 0u);
 }
 
 ExactPrefixCache::~ExactPrefixCache() { clear(); }
 
-std::size_t ExactPrefixCache::cache_only_blocks() const {
-    std::size_t count = 0;
-    for (std::size_t block = 0; block < s_.leases.size(); ++block) {
-        const std::uint32_t leases = s_.leases[block];
-        if (leases && pool_.references(int(block)) == leases) ++count;
-    }
-    return count;
-}
+std::size_t ExactPrefixCache::cache_only_blocks() const { return pool_.cache_only_blocks(); }
 
 void ExactPrefixCache::lease_add(int page, int delta) {
     log(Op::Lease, page, delta);
-    s_.leases[std::size_t(page)] = std::uint32_t(int(s_.leases[std::size_t(page)]) + delta);
+    pool_.add_lease(page, delta);
 }
 
 int ExactPrefixCache::new_node(int parent, View edge) {
@@ -325,7 +317,7 @@ void ExactPrefixCache::rollback_journal() noexcept {
             s_.nodes[std::size_t(e->a)].block = e->b;
             break;
         case Op::Lease: {
-            s_.leases[std::size_t(e->a)] = std::uint32_t(int(s_.leases[std::size_t(e->a)]) - e->b);
+            pool_.add_lease(e->a, -e->b);
             break;
         }
         }

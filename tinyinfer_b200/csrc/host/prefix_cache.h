@@ -126,7 +126,6 @@ private:
     struct State : Counters {
         std::vector<Node> nodes;
         std::vector<int> spare;
-        std::vector<std::uint32_t> leases;  // per pool page: index nodes leasing it
         int lru_first = -1, lru_last = -1;
         std::uint64_t clock = 0;
     };
