@@ -203,14 +203,18 @@ int mp_paged_attention_decode(const float* q, const float* keys, const float* va
  * overlaps race. The first call on a device, with that device current, looks up
  * the array's address; make it before any stream capture. `device_error`
  * (optional, caller-owned device word, zeroed by the caller) receives the kernel's
- * error bits (1 = page id out of range, 2 = copy wait expired). */
+ * error bits (1 = page id out of range, 2 = copy wait expired); when it is NULL the
+ * bits go to a word inside the fixed array, which mp_paged_attention_status reads
+ * and clears (before the next call on the device, which clears it again). */
 int mp_paged_attention_decode_noalloc(const float* q, const float* keys, const float* values, int32_t layers,
                                       int32_t layer, int32_t block_tokens, int32_t max_blocks, const int32_t* tables,
                                       int32_t table_stride, const int32_t* lengths, int32_t count, float* out,
                                       int32_t pages_per_split, void* stream, uint32_t* device_error);
-/* Synchronises `stream`, then reads and clears the operator's device error word on
- * the current device: MP_OK, MP_ERR_BOUNDS (a page id outside [0, max_blocks)) or
- * MP_ERR_TIMEOUT (an in-kernel copy wait expired). */
+/* Synchronises `stream`, then reads and clears the decode operators' device error
+ * words on the current device (mp_paged_attention_decode's, and the word that
+ * mp_paged_attention_decode_noalloc fills when given no device_error): MP_OK,
+ * MP_ERR_BOUNDS (a page id outside [0, max_blocks)) or MP_ERR_TIMEOUT (an in-kernel
+ * copy wait expired; the allocating operator's arrival counters are reset). */
 int mp_paged_attention_status(void* stream);
 
 #ifdef __cplusplus

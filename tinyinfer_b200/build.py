@@ -29,15 +29,11 @@ DEVICE_SOURCES = ["attention.cu", "attention_shared.cu", "attention_prefill.cu",
 HOST_SOURCES = []  # filled in by host/ when present
 
 
-def _stale(target: str, sources: list[str]) -> bool:
+def _stale(target: str, deps: list[str]) -> bool:
     if not os.path.exists(target):
         return True
     t = os.path.getmtime(target)
-    deps = list(sources)
-    for d in (CSRC, os.path.join(CSRC, "host"), INCLUDE):
-        if os.path.isdir(d):
-            deps += [os.path.join(d, f) for f in os.listdir(d) if f.endswith((".h", ".cuh", ".hpp"))]
-    return any(os.path.getmtime(s) > t for s in deps)
+    return any(os.path.getmtime(d) > t for d in deps)
 
 
 def _run(cmd: list[str]) -> None:
@@ -45,18 +41,30 @@ def _run(cmd: list[str]) -> None:
     subprocess.run(cmd, check=True)
 
 
+def _headers() -> list[str]:
+    out = []
+    for d in (CSRC, os.path.join(CSRC, "host"), INCLUDE):
+        if os.path.isdir(d):
+            out += [os.path.join(d, f) for f in os.listdir(d) if f.endswith((".h", ".cuh", ".hpp"))]
+    return out
+
+
 def build_device(force: bool = False) -> str:
+    """Compile each stale .cu (newer than its object, or any header newer) in
+    parallel, then link the shared library if any object changed."""
+    from concurrent.futures import ThreadPoolExecutor
+
     sources = [os.path.join(CSRC, s) for s in DEVICE_SOURCES]
-    if not force and not _stale(DEVICE_LIB, sources):
-        return DEVICE_LIB
     objdir = os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
-    objects = []
-    for s in sources:
-        o = os.path.join(objdir, os.path.basename(s) + ".o")
-        _run([NVCC, *ARCH, *COMMON, "-c", s, "-o", o])
-        objects.append(o)
-    _run([NVCC, *ARCH, "-shared", "-o", DEVICE_LIB, *objects])
+    headers = _headers()
+    objects = [os.path.join(objdir, os.path.basename(s) + ".o") for s in sources]
+    todo = [(s, o) for s, o in zip(sources, objects) if force or _stale(o, [s] + headers)]
+    if todo:
+        with ThreadPoolExecutor(max_workers=min(len(todo), os.cpu_count() or 4)) as pool:
+            list(pool.map(lambda so: _run([NVCC, *ARCH, *COMMON, "-c", so[0], "-o", so[1]]), todo))
+    if todo or _stale(DEVICE_LIB, objects):
+        _run([NVCC, *ARCH, "-shared", "-o", DEVICE_LIB, *objects])
     return DEVICE_LIB
 
 
@@ -71,7 +79,7 @@ def build_host(force: bool = False) -> str | None:
     sources = host_sources()
     if not sources:
         return None
-    if not force and not _stale(HOST_LIB, sources + [DEVICE_LIB]):
+    if not force and not _stale(HOST_LIB, sources + [DEVICE_LIB] + _headers()):
         return HOST_LIB
     _run(["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-Wextra", f"-I{INCLUDE}",
           f"-I{os.path.join(CSRC, 'host')}", *sources, "-o", HOST_LIB, f"-L{HERE}", "-lmpb200",

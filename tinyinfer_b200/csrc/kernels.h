@@ -190,6 +190,10 @@ cudaError_t configure_attention();
 // Message returned by mp_last_error() on this thread.
 void set_last_error(const char* message);
 cudaError_t launch_paged_attention(const AttnParams& p, cudaStream_t stream);
+// Reads and clears (on `stream`, synchronising it) the error word that
+// mp_paged_attention_decode_noalloc writes for callers that pass no device_error;
+// *bits = 0 when no such call has run on the current device. Allocates nothing.
+cudaError_t noalloc_take_error(cudaStream_t stream, unsigned* bits);
 
 // ---------------------------------------------------------------- GEMM
 // C[M][N] (op) A[M][K] * B[N][K]^T, B stored K-contiguous ("nn.Linear" layout).

@@ -168,20 +168,36 @@ extern "C" int mp_paged_attention_decode(const float* q, const float* keys, cons
     return MP_OK;
 }
 
-// Reads and clears the operator's device error word for the current device
-// (synchronises `stream`). Returns MP_OK, MP_ERR_BOUNDS or MP_ERR_TIMEOUT.
+// Reads and clears the operators' device error words on the current device
+// (synchronises `stream`): the allocating operator's, and the word that
+// mp_paged_attention_decode_noalloc writes when its caller passes no
+// device_error. Returns MP_OK, MP_ERR_BOUNDS or MP_ERR_TIMEOUT. After a timeout
+// the arrival counters and the schedule of the allocating operator are cleared:
+// a CTA that gave up never counted its slice, and leftover counts would make the
+// next call merge at the wrong slice.
 extern "C" int mp_paged_attention_status(void* stream_ptr) {
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return MP_ERR_CUDA;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    unsigned err = 0;
+    if (mpb::noalloc_take_error(stream, &err) != cudaSuccess) return MP_ERR_CUDA;
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
     Scratch& s = g_scratch[device];
-    if (!s.error) return MP_OK;
-    unsigned err = 0;
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-    if (cudaMemcpyAsync(&err, s.error, sizeof(unsigned), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
-        cudaStreamSynchronize(stream) != cudaSuccess)
-        return MP_ERR_CUDA;
+    if (s.error) {
+        unsigned own = 0;
+        if (cudaMemcpyAsync(&own, s.error, sizeof(unsigned), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+            cudaStreamSynchronize(stream) != cudaSuccess)
+            return MP_ERR_CUDA;
+        if (own) {
+            if (cudaMemsetAsync(s.error, 0, sizeof(unsigned), stream) != cudaSuccess) return MP_ERR_CUDA;
+            if (own & mpb::kErrTimeout) {
+                if (cudaMemsetAsync(s.counters, 0, s.counter_capacity * sizeof(unsigned), stream) != cudaSuccess ||
+                    cudaMemsetAsync(s.sched, 0, 2 * sizeof(unsigned), stream) != cudaSuccess)
+                    return MP_ERR_CUDA;
+            }
+        }
+        err |= own;
+    }
     if (!err) return MP_OK;
-    cudaMemsetAsync(s.error, 0, sizeof(unsigned), stream);
     return (err & mpb::kErrTimeout) ? MP_ERR_TIMEOUT : MP_ERR_BOUNDS;
 }

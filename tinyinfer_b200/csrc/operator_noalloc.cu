@@ -24,6 +24,11 @@
 // streams, or from different host threads without ordering -- race on the
 // array and give wrong results.
 //
+// Errors: bounds and timeout bits go to the caller's device_error word when one
+// is given. With device_error NULL they go to an error word inside the array,
+// which mp_paged_attention_status reads and clears; each call clears it before
+// its kernel, so read it before the next call on the same device.
+//
 // Set-up: the first call on a device, with that device current, looks up the
 // array's device address with cudaGetSymbolAddress (in host code the array's
 // name is only a host-side stand-in, not a device address) and keeps it for
@@ -217,4 +222,25 @@ extern "C" int mp_paged_attention_decode_noalloc(const float* q, const float* ke
         return MP_ERR_CUDA;
     }
     return MP_OK;
+}
+
+cudaError_t mpb::noalloc_take_error(cudaStream_t stream, unsigned* bits) {
+    *bits = 0;
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return e;
+    if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+    unsigned char* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_setup_mutex);
+        base = g_scratch_address[device];
+    }
+    if (!base) return cudaSuccess;  // no call on this device yet
+    unsigned* error = reinterpret_cast<unsigned*>(base + kErrorOffset);
+    unsigned word = 0;
+    e = cudaMemcpyAsync(&word, error, sizeof(unsigned), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e == cudaSuccess && word) e = cudaMemsetAsync(error, 0, sizeof(unsigned), stream);
+    if (e == cudaSuccess) *bits = word;
+    return e;
 }
