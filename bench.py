@@ -54,8 +54,6 @@ def parse():
     p.add_argument("--prefill-budget", type=int, default=8192)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-workers", type=int, default=0)
-    p.add_argument("--cpu-context", type=int, default=512)
-    p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--operator", action="store_true",
                    help="time the paged-attention decode operator alone on BASELINE config 2")
     p.add_argument("--workload", choices=["config3", "config4", "config5"], default="config3",
@@ -74,6 +72,38 @@ def peaks():
         return float(d["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def tf32_peak(device_index):
+    """Dense TF32 tensor-core throughput of this GPU, measured here: torch.matmul
+    (cuBLAS) on 8192^3 FP32 operands with TF32 enabled, best of 10 launches timed
+    with CUDA events (2 N^3 FLOP each). The denominator of the GEMM roofline."""
+    import torch
+
+    dev = torch.device("cuda", device_index)
+    n = 8192
+    g = torch.Generator(device=dev).manual_seed(1)
+    a = torch.randn(n, n, device=dev, generator=g)
+    b = torch.randn(n, n, device=dev, generator=g)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        for _ in range(3):
+            c = torch.matmul(a, b)
+        best = None
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            c = torch.matmul(a, b)
+            e1.record()
+            e1.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b, c
+    torch.cuda.empty_cache()
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12
 
 
 # ----------------------------------------------------------------------------- workload
@@ -181,48 +211,137 @@ def unique_decode_bytes(engine, ids, block_tokens):
 
 
 # ----------------------------------------------------------------------------- CPU baseline
-def _cpu_worker(args_tuple):
-    """One reference CPU runner: build a context of `context` tokens (untimed), then
-    decode greedily for `seconds`. Returns (steps, elapsed)."""
-    context, seconds, layers, worker = args_tuple
+def _cpu_worker(index, layers, prompt, shared, decode_steps, go, results):
+    """One single-threaded reference CpuRunner (oracle/_ref) on config 3's request
+    `index`: its 2048-token prompt (the shared 1032-token prefix + its own suffix)
+    prefilled untimed, then, once `go` is set, `decode_steps` greedy decode tokens
+    timed at context 2048+."""
     sys.path.insert(0, ROOT)
     from oracle.oracle import RefLib, RefRunner
-    from tinyinfer_b200.synthetic import ModelConfig, random_tokens, random_weights
+    from tinyinfer_b200.synthetic import ModelConfig, random_weights
 
-    c = ModelConfig(layers=layers, context=context + 4096)
-    w = random_weights(c, seed=0)
-    ref = RefLib()
-    r = RefRunner.cpu(ref, c, w, c.context, 16, (c.context + 15) // 16 + 1, 0)
-    r.create("s")
-    logits = r.append("s", random_tokens(context, c.vocabulary, 100 + worker))
-    steps, start = 0, time.perf_counter()
-    while time.perf_counter() - start < seconds:
-        logits = r.append("s", [int(np.argmax(logits))])
-        steps += 1
-    return steps, time.perf_counter() - start
+    try:
+        c = ModelConfig(layers=layers, context=len(prompt) + decode_steps + 16)
+        w = random_weights(c, seed=0)
+        ref = RefLib()
+        r = RefRunner.cpu(ref, c, w, c.context, 16, (c.context + 15) // 16 + 1, 0)
+        del w
+        r.create("s")
+        t0 = time.perf_counter()
+        logits = r.append("s", prompt)
+        prefill_s = time.perf_counter() - t0
+        go.wait()
+        start = time.perf_counter()
+        for _ in range(decode_steps):
+            logits = r.append("s", [int(np.argmax(logits))])
+        results.put((index, decode_steps, time.perf_counter() - start, prefill_s, None))
+    except Exception as e:  # reported, never silently dropped
+        results.put((index, 0, 0.0, 0.0, f"{type(e).__name__}: {e}"))
 
 
-def cpu_baseline(args, workers=None, seconds=None):
-    from oracle import oracle as orc
+class CpuBaseline:
+    """The reference CPU engine at BASELINE config 3's context, on the host cores:
+    P single-threaded reference CpuRunner processes (spawned), one per core, each
+    holding one of config 3's requests (2048-token prompt: 1032 shared + 1016 own
+    tokens). The prefills (minutes of CPU) run untimed and may overlap the GPU arm;
+    start() launches them, measure() releases the timed decode steps and returns
+    the aggregate decode tok/s at context 2048."""
 
-    kind = "reference" if os.path.exists(orc.REF_SO) else None
-    if kind is None:
-        return {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
-                "sample": "oracle/_ref/libmpref.so not present on this host"}
-    n = workers or args.cpu_workers or min(os.cpu_count() or 1, 16)
-    seconds = seconds or args.cpu_seconds
-    ctx = mp.get_context("spawn")
+    def __init__(self, args, workers=None, decode_steps=16):
+        self.args = args
+        self.n = workers or args.cpu_workers or max(1, min((os.cpu_count() or 1) - 2, 16))
+        self.decode_steps = decode_steps
+        self.procs = []
+
+    def start(self):
+        from oracle import oracle as orc
+
+        self.available = os.path.exists(orc.REF_SO)
+        if not self.available:
+            return self
+        ctx = mp.get_context("spawn")
+        self.go = ctx.Event()
+        self.results = ctx.Queue()
+        self.t0 = time.perf_counter()
+        for i, p in enumerate(prompts(self.args, range(self.n))):
+            proc = ctx.Process(target=_cpu_worker, args=(i, self.args.layers, [int(t) for t in p], self.args.shared,
+                                                          self.decode_steps, self.go, self.results), daemon=True)
+            proc.start()
+            self.procs.append(proc)
+        return self
+
+    def measure(self):
+        if not self.available:
+            return {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "same_config": True,
+                    "sample": "oracle/_ref/libmpref.so not present on this host"}
+        self.go.set()
+        got = [self.results.get(timeout=3600) for _ in self.procs]
+        for proc in self.procs:
+            proc.join(timeout=60)
+        errors = [g[4] for g in got if g[4]]
+        if errors:
+            return {"value": None, "unit": "tok/s", "cores": self.n, "kind": "reference", "same_config": True,
+                    "sample": f"reference CPU workers failed: {errors[0]}"}
+        steps = sum(g[1] for g in got)
+        elapsed = max(g[2] for g in got)
+        prefill = max(g[3] for g in got)
+        cpu = "unknown CPU"
+        try:
+            with open("/proc/cpuinfo") as f:
+                cpu = next(l.split(":", 1)[1].strip() for l in f if l.startswith("model name"))
+        except Exception:
+            pass
+        return {"value": steps / elapsed, "unit": "tok/s", "cores": self.n, "kind": "reference",
+                "same_config": True, "cpu_model": cpu, "host_cpus": os.cpu_count(),
+                "per_core_tok_s": steps / elapsed / self.n,
+                "sample": (f"{self.n} single-threaded reference CpuRunner processes (oracle/_ref, AVX2+FMA) on "
+                           f"{cpu}, each holding one config-3 request (2048-token prompt = the 1032-token shared "
+                           f"prefix + 1016 own tokens, prefilled untimed in {prefill:.0f} s) and greedy-decoding "
+                           f"{self.decode_steps} tokens at context 2048-{2048 + self.decode_steps} "
+                           f"({steps} tokens in {elapsed:.1f} s)")}
+
+
+def replay_parity(record):
+    """CPU-baseline leg, after the timed steps: the run's emitted tokens replayed
+    through the UNMODIFIED reference engine over its scripted runner
+    (oracle/replay.py). Every step's events (request, token, finish reason) must be
+    identical; so must the step stats, KV stats and copy-on-write / reuse counters
+    after every untimed step and at the end, and the final page table of every
+    request (bit-exact page ids). The token values themselves are checked against
+    the C oracle's logits by tests/test_gpu_config3.py at this geometry."""
+    from oracle.replay import COUNT_FIELDS, KV_FIELDS, Mismatch, Step, Trace, replay
+
     t0 = time.perf_counter()
-    with ctx.Pool(n) as pool:
-        res = pool.map(_cpu_worker, [(args.cpu_context, seconds, args.layers, i) for i in range(n)])
-    steps = sum(r[0] for r in res)
-    elapsed = max(r[1] for r in res)
-    return {"value": steps / elapsed, "unit": "tok/s", "cores": n, "kind": kind,
-            "sample": (f"{n} single-threaded reference CpuRunner processes (oracle/_ref, AVX2+FMA), each "
-                       f"greedy-decoding one sequence at context {args.cpu_context} for ~{seconds:.0f} s after an "
-                       f"untimed {args.cpu_context}-token prefill ({steps} tokens, {time.perf_counter() - t0:.0f} s "
-                       f"wall); a 2048-token context takes minutes per core to build, and the CPU cost per token "
-                       f"grows with context, so this overstates the CPU rate at ctx 2k")}
+    trace = Trace()
+    trace.ids = list(record["ids"])
+    for op in record["ops"]:
+        if op[0] == "submit":
+            trace.ops.append(("submit", op[1], [int(x) for x in op[2]], int(op[3]), None))
+        elif op[0] == "step":
+            _, evs, ss, rs, cs = op
+            trace.ops.append(("step", Step(list(evs), ss, {k: rs[k] for k in KV_FIELDS},
+                                           {k: cs[k] for k in COUNT_FIELDS})))
+        else:
+            req, tok, rea = op[1]
+            trace.ops.append(("step", Step([(trace.ids[int(r)], None if int(x) < 0 else int(x),
+                                             None if int(y) < 0 else int(y)) for r, x, y in zip(req, tok, rea)])))
+    final, last = record["final"], trace.ops[-1][1]
+    last.step_stats = final["step_stats"]
+    last.kv = {k: final["runner_stats"][k] for k in KV_FIELDS}
+    last.costs = {k: final["costs"][k] for k in COUNT_FIELDS}
+    last.sequences = {rid: seq for rid, seq in final["sequences"].items() if seq is not None}
+    out = {"checked_by": "reference Engine + scripted runner (oracle/_ref) fed this run's emitted tokens"}
+    try:
+        out["compared"] = replay(trace, **record["geometry"])
+        out["bookkeeping"] = "identical"
+    except Mismatch as e:
+        out["bookkeeping"] = "MISMATCH"
+        out["detail"] = str(e)
+    except Exception as e:  # reference library missing or failing: say so, do not guess
+        out["bookkeeping"] = None
+        out["detail"] = f"replay not run: {type(e).__name__}: {e}"
+    out["seconds"] = round(time.perf_counter() - t0, 1)
+    return out
 
 
 # ----------------------------------------------------------------------------- B200 arm
@@ -262,17 +381,32 @@ def run_b200(args, rank, world, local_rank):
     ps = prompts(args, mine)
     ids = [f"r{i}" for i in mine]
 
+    # The run is recorded (submits, every step's events; stats and page tables
+    # outside the timed steps) so that the CPU-baseline leg can replay it through
+    # the reference engine: plain lists here, nothing from oracle/.
+    record = {"ops": [], "ids": ids}
+
+    def setup_step():
+        engine.step()
+        evs = engine.poll_events()
+        rs, cs = engine.runner_stats(), engine.cost_stats()
+        record["ops"].append(("step", [(e[0], e[1], e[2]) for e in evs], engine.last_step_stats(), rs, cs))
+        return evs
+
+    def submit(i):
+        engine.submit(ids[i], ps[i], max_new)
+        record["ops"].append(("submit", ids[i], ps[i], max_new))
+
     # Seed: prefill to completion so the shared prefix is published.
     t_setup = time.perf_counter()
-    engine.submit(ids[0], ps[0], max_new)
-    while not any(e[1] is not None for e in engine.poll_events()):
-        engine.step()
+    submit(0)
+    while not any(e[1] is not None for e in setup_step()):
+        pass
     for i in range(1, n):
-        engine.submit(ids[i], ps[i], max_new)
+        submit(i)
     started = {ids[0]}
     while len(started) < n:
-        engine.step()
-        for rid, tok, reason, err in engine.poll_events():
+        for rid, tok, reason, err in setup_step():
             if reason == 3:
                 raise RuntimeError(f"request {rid} failed: {err}")
             if tok is not None:
@@ -284,16 +418,19 @@ def run_b200(args, rank, world, local_rank):
     def decode_step():
         engine.step()
         evs = engine.poll_compact()
+        record["ops"].append(("compact", evs))
         return len(evs[0])
 
     for _ in range(args.warmup):
         decode_step()
     uniq = unique_decode_bytes(engine, ids, bt)
     logical = logical_decode_bytes(engine, ids)
+    tf32 = tf32_peak(local_rank)
     before = dev.counters(reset=True)
     # kernels launched before the timed steps (for `ncu -s` on this command)
     print(f"launches_before_timed={before['kernel_launches']}", file=sys.stderr, flush=True)
     dev.profile_read()
+    dev.profile_read_gemm()
     dev.profile(True)
     if dist:
         dist.barrier()
@@ -316,6 +453,12 @@ def run_b200(args, rank, world, local_rank):
     dev.profile(False)
     counters = dev.counters(reset=True)
     attn_ms, attn_launches, attn_bytes = dev.profile_read()
+    gemm_ms, gemm_intervals, head_ms, heads = dev.profile_read_gemm()
+    record["final"] = {"step_stats": engine.last_step_stats(), "runner_stats": engine.runner_stats(),
+                       "costs": engine.cost_stats(), "sequences": {rid: engine.sequence(rid) for rid in ids}}
+    record["geometry"] = dict(vocabulary=cfg.vocabulary, context=cfg.context, layers=cfg.layers, width=cfg.kv_width,
+                              block_tokens=bt, max_blocks=max_blocks, prefix_blocks=args.prefix_blocks, max_batch=n,
+                              token_budget=args.prefill_budget, prefill_chunk=args.prompt)
     if dist:
         dist.barrier()
 
@@ -396,13 +539,42 @@ def run_b200(args, rank, world, local_rank):
                      "logical_bytes_per_launch": logical,
                      "logical_achieved": logical / (launch_ms * 1e-3) / 1e9 if launch_ms > 0 else None,
                      "attention_share_of_forward": attn_ms / device_ms if device_ms else None},
+        "gemm_roofline": gemm_roofline(cfg, n, gemm_ms, gemm_intervals, head_ms, heads, tf32),
         "clocks": clocks.summary(),
+        "_record": record,
     }
     engine.shutdown()
     engine.close()
     if dist:
         dist.destroy_process_group()
     return line
+
+
+def gemm_roofline(cfg, rows, gemm_ms, intervals, head_ms, heads, tf32_tflops):
+    """The projection GEMMs of one decode step at M = rows, against the measured
+    TF32 peak. Useful FLOP (2 M N K; the kernels issue 3x that as 3xTF32 MMAs):
+    per layer QKV 576x960, O 576x576, gate/up 576x3072, down 1536x576; the tied LM
+    head 576x49152. Times from CUDA events on the context stream: each interval
+    between two layers' attention launches holds one layer's four GEMMs."""
+    H, I, V = cfg.hidden, cfg.intermediate, cfg.vocabulary
+    kvw = cfg.kv_width
+    layer_flop = 2.0 * rows * (H * (H + 2 * kvw) + H * H + H * 2 * I + I * H)
+    head_flop = 2.0 * rows * H * V
+    out = {"bound": "tensor", "unit": "TFLOP/s", "peak": tf32_tflops,
+           "peak_kind": "measured here: cuBLAS TF32 8192^3, best of 10 (MEASURED_PEAKS.json has bf16 only)",
+           "useful_flop_per_layer": layer_flop, "issued_flop_per_layer": 3 * layer_flop,
+           "useful_flop_head": head_flop}
+    if intervals:
+        us = 1000.0 * gemm_ms / intervals
+        ach = layer_flop / (us * 1e-6) / 1e12
+        out.update({"layer_gemm_us": us, "achieved": ach, "frac": ach / tf32_tflops,
+                    "issued_frac": 3 * ach / tf32_tflops})
+    if heads:
+        us = 1000.0 * head_ms / heads
+        ach = head_flop / (us * 1e-6) / 1e12
+        out.update({"head_us": us, "head_achieved": ach, "head_frac": ach / tf32_tflops,
+                    "head_issued_frac": 3 * ach / tf32_tflops})
+    return out
 
 
 # ----------------------------------------------------------------------------- operator (config 2)
@@ -476,22 +648,23 @@ def run_operator(args, local_rank):
 
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args, rank, world):
+    """The reference arm: the reference's own CPU engine (oracle/_ref, compiled from
+    the reference sources) at config 3's context on this host's cores; rank 0 only."""
     if rank != 0:
         return None
     from oracle import oracle as orc
 
     if not os.path.exists(orc.REF_SO):
         return {"impl": "reference", "unavailable": "oracle/_ref/libmpref.so (reference CPU engine) not built on this host"}
-    n = args.cpu_workers or min(os.cpu_count() or 1, 16)
-    per_step = max(2.0, args.cpu_seconds / max(args.steps, 1))
-    res = cpu_baseline(args, n, per_step * (args.steps + args.warmup))
+    res = CpuBaseline(args, decode_steps=max(4, min(args.steps, 16))).start().measure()
     value = res["value"]
     return {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": None if not value else 1000.0 * n / value,
+            "warmup": args.warmup, "ms_per_step": None if not value else 1000.0 * res["cores"] / value,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": "config3 decode on the reference CPU engine (see cpu_baseline.sample)",
-                       "model": "SmolLM2-135M shape, 30 layers, FP32"},
+            "config": {"workload": "config3 decode at context 2048 on the reference CPU engine (see "
+                                   "cpu_baseline.sample)",
+                       "model": f"SmolLM2-135M shape, {args.layers} layers, FP32, tied head", "same_config": True},
             "cpu_baseline": res,
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
@@ -511,9 +684,14 @@ def main():
         run = bench_serving.run_config4 if args.workload == "config4" else bench_serving.run_config5
         line = run(args, rank, world, local_rank)
     else:
+        # the CPU baseline's untimed prefills start first (spawned processes, no
+        # CUDA) and overlap the GPU arm; their timed decode runs after it
+        baseline = CpuBaseline(args).start() if world == 1 and not args.no_cpu_baseline else None
         line = run_b200(args, rank, world, local_rank)
-        if line is not None and world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(args)
+        record = line.pop("_record", None) if line is not None else None
+        if line is not None and baseline is not None:
+            line["parity"] = replay_parity(record)
+            line["cpu_baseline"] = baseline.measure()
     if line is not None:
         print(json.dumps(line), flush=True)
 

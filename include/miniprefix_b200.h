@@ -119,6 +119,13 @@ int mp_forward_launch(mp_context* ctx);
 int mp_forward_collect(mp_context* ctx, int32_t* out_tokens, int32_t* out_finite, float* out_logits,
                        int32_t timeout_ms);
 
+/* Failure-path tests (no counterpart in the reference, whose kernels have no
+ * bounded waits): the next forward's first GEMM launch gets a producer that issues
+ * no copies and waits bounded at `wait_us` microseconds (1 us .. 1 s). Its waits run
+ * out, the kernel records the timeout bit, releases its tensor memory and returns,
+ * and that forward reports MP_ERR_TIMEOUT (its outputs and the K/V rows it should
+ * have written are garbage). The context stays usable: later forwards are normal. */
+int mp_inject_wait_timeout(mp_context* ctx, int32_t wait_us);
 /* Waits for all queued work with a bounded host wait (event polling). */
 int mp_sync(mp_context* ctx, int32_t timeout_ms);
 
@@ -149,6 +156,11 @@ int mp_profile_enable(mp_context* ctx, int32_t enabled);
  * prefix-tree serving). */
 int mp_set_shared_prefix(mp_context* ctx, int32_t min_rows, int32_t min_tokens);
 int mp_profile_read(mp_context* ctx, float* attention_ms, int32_t* attention_launches, double* attention_bytes);
+/* The same profiling (no counterpart in the reference) for the projection GEMMs:
+ * the summed milliseconds and count of the intervals between one layer's attention
+ * and the next layer's (each: O, gate/up and down of a layer plus the next layer's
+ * QKV), and of the LM head GEMM; reset on read. */
+int mp_profile_read_gemm(mp_context* ctx, float* layer_gemm_ms, int32_t* intervals, float* head_ms, int32_t* heads);
 /* Cumulative counters of collected forwards: device time from the first to the
  * last kernel of each forward (CUDA events on the context stream), kernels
  * launched, and bytes moved host->device / device->host by the forwards;

@@ -166,6 +166,14 @@ int mph_engine_flushes(mph_engine* e, size_t* flushes, size_t* hazard_flushes);
 /* The device context of the engine's B200 runner (NULL for other runners), for
  * timing and counters through include/miniprefix_b200.h. */
 mp_context* mph_engine_device(mph_engine* e);
+/* Parity checks of batched runs (no counterpart in the reference, whose append()
+ * returns every request's logits): while capture is on, each device forward of
+ * the engine's B200 runner also downloads the logits of its appends, and
+ * mph_engine_logits copies the latest ones of request `id` (at most `capacity`
+ * floats) and returns the vocabulary size, or -1 when none were captured, -2
+ * when the runner is not a B200 runner. Switching capture off drops them. */
+int mph_engine_capture_logits(mph_engine* e, int32_t on);
+long mph_engine_logits(mph_engine* e, const char* id, float* out, long capacity);
 
 #ifdef __cplusplus
 }

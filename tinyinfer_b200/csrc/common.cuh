@@ -59,13 +59,15 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 
 // Bounded wait. Returns false (and the caller must record kErrTimeout) when the
-// phase did not complete within the bounds above.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+// phase did not complete within `limit_ns` of wall time (default
+// kWaitNanoseconds) or kWaitLimit polls.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint64_t limit_ns = kWaitNanoseconds) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t start = global_ns();
     for (uint32_t i = 0; i < kWaitLimit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255) == 255 && global_ns() - start > kWaitNanoseconds) return false;
+        if ((i & 255) == 255 && global_ns() - start > limit_ns) return false;
     }
     return false;
 }

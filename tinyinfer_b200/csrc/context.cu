@@ -315,7 +315,7 @@ struct mp_context {
     mp_runtime_config rt{};
     int dim = 64, kvw = 192, qkvw = 960;
     cudaStream_t stream = nullptr;
-    cudaEvent_t done = nullptr, mark[2] = {nullptr, nullptr};
+    cudaEvent_t done = nullptr, idle = nullptr, mark[2] = {nullptr, nullptr};
     int mark_count = 0;
     // weights: the embedding in FP32 (row gather), every GEMM operand packed [N][K]
     // (K contiguous) as TF32 hi/lo halves; per-layer matrices stacked by layer
@@ -382,6 +382,11 @@ struct mp_context {
     int cta_count = 0;  // static decode-attention schedule of the step (0: none)
     size_t prefill_capacity = 0;
     bool prepared = false;
+    // host waits of staging reuse and pool copies (bounded, MP_ERR_TIMEOUT)
+    int host_wait_ms = 600000;
+    // failure-path tests (mp_inject_wait_timeout): the next forward's first GEMM
+    // issues no copies and bounds its waits at this many microseconds
+    int stall_next_us = 0;
     AttnPlan plan;
     // attention profiling
     bool profile = false;
@@ -391,6 +396,12 @@ struct mp_context {
     float prof_ms = 0.f;
     int prof_launches = 0;
     double prof_bytes = 0;
+    // projection GEMMs: the interval from one layer's attention end to the next
+    // layer's attention start is that layer's O, gate/up and down GEMMs plus the
+    // next layer's QKV GEMM; the LM head is bracketed by its own pair of events
+    float prof_gemm_ms = 0.f, prof_head_ms = 0.f;
+    int prof_gemm_intervals = 0, prof_heads = 0;
+    cudaEvent_t head_events[2] = {nullptr, nullptr};
 };
 
 namespace {
@@ -450,7 +461,13 @@ void split_host(const float* x, float* hi, float* lo, size_t n) {
 void free_context(mp_context* c) {
     if (!c) return;
     cudaSetDevice(c->device);
-    if (c->stream) cudaStreamSynchronize(c->stream);
+    // queued work must end before its buffers are freed: poll, bounded by the
+    // context's host wait limit (after that the buffers are freed regardless)
+    if (c->stream) {
+        const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(c->host_wait_ms);
+        while (cudaStreamQuery(c->stream) == cudaErrorNotReady && std::chrono::steady_clock::now() < deadline)
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
     for (void* p : {(void*)c->embed, (void*)c->final_norm, (void*)c->in_norm, (void*)c->post_norm, (void*)c->keys,
                     (void*)c->values, (void*)c->tables, (void*)c->rope_cos, (void*)c->rope_sin, (void*)c->x,
                     (void*)c->q, (void*)c->logits, (void*)c->ssq,
@@ -466,11 +483,14 @@ void free_context(mp_context* c) {
                     (void*)c->h_cow})
         if (p) cudaFreeHost(p);
     for (auto e : c->prof_events) cudaEventDestroy(e);
+    for (auto e : c->head_events)
+        if (e) cudaEventDestroy(e);
     for (auto e : c->cow_events)
         if (e) cudaEventDestroy(e);
     for (auto e : c->fwd_events)
         if (e) cudaEventDestroy(e);
     if (c->done) cudaEventDestroy(c->done);
+    if (c->idle) cudaEventDestroy(c->idle);
     for (auto e : c->mark)
         if (e) cudaEventDestroy(e);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -501,6 +521,13 @@ void wait_event(cudaEvent_t e, int timeout_ms) {
         if (waited < std::chrono::milliseconds(2)) std::this_thread::yield();
         else std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
+}
+
+// Bounded wait until everything queued on the context's stream has completed
+// (staging buffers about to be refilled, pool copies ordered after the forward).
+void wait_stream(mp_context* c, const char* what) {
+    cuda_check(cudaEventRecord(c->idle, c->stream), what);
+    wait_event(c->idle, c->host_wait_ms);
 }
 
 void validate_geometry(const mp_model_config& m, const mp_runtime_config& r) {
@@ -597,7 +624,7 @@ size_t expected_tensors(const mp_model_config& m) { return size_t(m.layers) * 9 
 
 void ensure_patch(mp_context* c, size_t pairs) {
     if (pairs <= c->patch_capacity) return;
-    cuda_check(cudaStreamSynchronize(c->stream), "patch staging reuse");
+    wait_stream(c, "patch staging reuse");
     if (c->h_patch) cudaFreeHost(c->h_patch);
     if (c->patch) cudaFree(c->patch);
     c->h_patch = nullptr;
@@ -623,8 +650,19 @@ void harvest_profile(mp_context* c) {
         cuda_check(cudaEventElapsedTime(&ms, c->prof_events[i], c->prof_events[i + 1]), "profile elapsed");
         c->prof_ms += ms;
         c->prof_launches += 1;
+        if (i + 2 < c->prof_used) {
+            cuda_check(cudaEventElapsedTime(&ms, c->prof_events[i + 1], c->prof_events[i + 2]), "profile elapsed");
+            c->prof_gemm_ms += ms;
+            c->prof_gemm_intervals += 1;
+        }
     }
     c->prof_used = 0;
+    if (c->head_events[0]) {
+        float ms = 0.f;
+        cuda_check(cudaEventElapsedTime(&ms, c->head_events[0], c->head_events[1]), "profile elapsed");
+        c->prof_head_ms += ms;
+        c->prof_heads += 1;
+    }
 }
 
 }  // namespace
@@ -654,6 +692,7 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         cuda_check(cudaSetDevice(device), "select device");
         cuda_check(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "create stream");
         cuda_check(cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming), "create event");
+        cuda_check(cudaEventCreateWithFlags(&c->idle, cudaEventDisableTiming), "create event");
         for (auto& e : c->mark) cuda_check(cudaEventCreate(&e), "create timer event");
         cuda_check(mpb::configure_attention(), "configure attention kernel");
         cuda_check(mpb::configure_prefix_attention(), "configure shared-prefix attention kernel");
@@ -760,7 +799,7 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         c->h_tokens = host_alloc<int32_t>(S, "token staging");
         c->h_finite = host_alloc<int32_t>(S, "finite staging");
         c->h_error = host_alloc<unsigned>(1, "error staging");
-        cuda_check(cudaStreamSynchronize(c->stream), "context initialisation");
+        wait_stream(c, "context initialisation");
     });
     if (rc != MP_OK) {
         free_context(c);
@@ -833,7 +872,7 @@ int mp_table_write(mp_context* c, int32_t slot, int32_t first, const int32_t* bl
         cuda_check(cudaSetDevice(c->device), "select device");
         ensure_patch(c, size_t(count));
         // The staging buffer may still feed the previous patch: wait for it.
-        cuda_check(cudaStreamSynchronize(c->stream), "table staging reuse");
+        wait_stream(c, "table staging reuse");
         for (int i = 0; i < count; ++i) {
             c->h_patch[2 * i] = slot * c->rt.table_stride + first + i;
             c->h_patch[2 * i + 1] = blocks[i];
@@ -862,7 +901,7 @@ int mp_cow_copy(mp_context* c, const mp_tail_copy_region* regions, int32_t count
         }
         cuda_check(cudaSetDevice(c->device), "select device");
         if (size_t(count) > c->cow_capacity) {
-            cuda_check(cudaStreamSynchronize(c->stream), "cow staging reuse");
+            wait_stream(c, "cow staging reuse");
             if (c->h_cow) cudaFreeHost(c->h_cow);
             if (c->cow) cudaFree(c->cow);
             c->h_cow = nullptr;
@@ -872,7 +911,7 @@ int mp_cow_copy(mp_context* c, const mp_tail_copy_region* regions, int32_t count
             c->cow = device_alloc<int32_t>(size_t(count) * 10, "cow regions");
             c->cow_capacity = count;
         }
-        cuda_check(cudaStreamSynchronize(c->stream), "cow staging reuse");
+        wait_stream(c, "cow staging reuse");
         std::memcpy(c->h_cow, regions, size_t(count) * sizeof(mp_tail_copy_region));
         cuda_check(cudaMemcpyAsync(c->cow, c->h_cow, size_t(count) * sizeof(mp_tail_copy_region),
                                    cudaMemcpyHostToDevice, c->stream),
@@ -975,7 +1014,7 @@ int mp_forward_prepare(mp_context* c, const mp_sequence_desc* seqs, int32_t coun
         if (P > c->prefill_capacity) fail(MP_ERR_INVALID, "prefill work list exceeds capacity");
         // layout: tokens | pos | slot | len | splits | work0 | last | work
         cuda_check(cudaSetDevice(c->device), "select device");
-        cuda_check(cudaStreamSynchronize(c->stream), "metadata staging reuse");
+        wait_stream(c, "metadata staging reuse");
         int32_t* h = c->h_meta;
         c->off_tokens = 0;
         c->off_pos = c->off_tokens + T;
@@ -1162,6 +1201,11 @@ int mp_forward_launch(mp_context* c) {
                 g.ssq_in = c->ssq;
                 g.eps = m.rms_epsilon;
             }
+            if (c->stall_next_us > 0) {  // mp_inject_wait_timeout: this launch's waits run out
+                g.stall = 1;
+                g.wait_ns = uint64_t(c->stall_next_us) * 1000u;
+                c->stall_next_us = 0;
+            }
             cuda_check(mpb::launch_tc_gemm({&a_hi, &a_lo, &b_hi, &b_lo}, g, e, st), what);
         };
         mpb::AttnParams ap{};
@@ -1249,8 +1293,14 @@ int mp_forward_launch(mp_context* c) {
         cuda_check(mpb::launch_rmsnorm(c->x, meta + c->off_last, c->final_norm, m.rms_epsilon, c->xl.hi, c->xl.lo, S,
                                        H, st),
                    "final norm launch");
+        if (c->profile) {
+            for (auto& e : c->head_events)
+                if (!e) cuda_check(cudaEventCreate(&e), "profile event");
+            cuda_check(cudaEventRecord(c->head_events[0], st), "profile event record");
+        }
         gemm(mp.xl_hi, mp.xl_lo, mp.head_hi, mp.head_lo, S, m.vocabulary, H, 0, c->logits, m.vocabulary,
              mpb::Epilogue::Store, "lm head gemm", head_tile_n(m.vocabulary));
+        if (c->profile) cuda_check(cudaEventRecord(c->head_events[1], st), "profile event record");
         cuda_check(mpb::launch_argmax(c->logits, S, m.vocabulary, c->out_tokens, c->out_finite, st), "argmax launch");
         cuda_check(cudaEventRecord(c->fwd_events[1], st), "forward timing");
         if (c->profile) c->prof_bytes += c->plan.bytes * m.layers;
@@ -1327,11 +1377,22 @@ int mp_forward(mp_context* c, const mp_sequence_desc* seqs, int32_t count, const
     if (rc != MP_OK) return rc;
     rc = mp_forward_launch(c);
     if (rc != MP_OK) {
-        if (c && c->stream) cudaStreamSynchronize(c->stream);
+        if (c && c->stream) {
+            const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(c->host_wait_ms);
+            while (cudaStreamQuery(c->stream) == cudaErrorNotReady && std::chrono::steady_clock::now() < deadline)
+                std::this_thread::sleep_for(std::chrono::microseconds(50));
+        }
         if (c) c->prepared = false;
         return rc;
     }
     return mp_forward_collect(c, out_tokens, out_finite, out_logits, timeout_ms);
+}
+
+int mp_inject_wait_timeout(mp_context* c, int32_t wait_us) {
+    return guarded([&] {
+        if (!c || wait_us < 1 || wait_us > 1000000) fail(MP_ERR_INVALID, "wait limit must be 1 us .. 1 s");
+        c->stall_next_us = wait_us;
+    });
 }
 
 int mp_sync(mp_context* c, int32_t timeout_ms) {
@@ -1363,7 +1424,7 @@ static int kv_copy(mp_context* c, int32_t pool, uint64_t offset, uint64_t count,
         if (!c || !host || (pool != 0 && pool != 1)) fail(MP_ERR_INVALID, "invalid argument");
         if (offset > c->pool_elements || count > c->pool_elements - offset) fail(MP_ERR_INVALID, "range outside the pool");
         cuda_check(cudaSetDevice(c->device), "select device");
-        cuda_check(cudaStreamSynchronize(c->stream), "pool copy ordering");
+        wait_stream(c, "pool copy ordering");
         float* base = (pool == 0 ? c->keys : c->values) + offset;
         cuda_check(to_device ? cudaMemcpy(base, host, count * 4, cudaMemcpyHostToDevice)
                              : cudaMemcpy(host, base, count * 4, cudaMemcpyDeviceToHost),
@@ -1442,6 +1503,17 @@ int mp_profile_read(mp_context* c, float* attention_ms, int32_t* launches, doubl
     return MP_OK;
 }
 
+int mp_profile_read_gemm(mp_context* c, float* layer_gemm_ms, int32_t* intervals, float* head_ms, int32_t* heads) {
+    if (!c) return MP_ERR_INVALID;
+    if (layer_gemm_ms) *layer_gemm_ms = c->prof_gemm_ms;
+    if (intervals) *intervals = c->prof_gemm_intervals;
+    if (head_ms) *head_ms = c->prof_head_ms;
+    if (heads) *heads = c->prof_heads;
+    c->prof_gemm_ms = c->prof_head_ms = 0.f;
+    c->prof_gemm_intervals = c->prof_heads = 0;
+    return MP_OK;
+}
+
 // C = A . B^T through the 3xTF32 tensor-core GEMM on caller device buffers (a [m][k],
 // b [n][k], c [m][n], row-major). Allocates and frees its own hi/lo scratch and
 // synchronises `stream`; meant for tests and tools, not for the hot path.
@@ -1487,7 +1559,17 @@ int mp_gemm_f32(const float* a, const float* b, float* out, int32_t m, int32_t n
                    "gemm launch");
         unsigned herr = 0;
         cuda_check(cudaMemcpyAsync(&herr, err, 4, cudaMemcpyDeviceToHost, st), "read error word");
-        cuda_check(cudaStreamSynchronize(st), "gemm completion");
+        cudaEvent_t done = nullptr;
+        cuda_check(cudaEventCreateWithFlags(&done, cudaEventDisableTiming), "create event");
+        const cudaError_t recorded = cudaEventRecord(done, st);
+        try {
+            cuda_check(recorded, "gemm completion");
+            wait_event(done, 600000);
+        } catch (...) {
+            cudaEventDestroy(done);
+            throw;
+        }
+        cudaEventDestroy(done);
         if (herr) fail(MP_ERR_TIMEOUT, "tensor-core GEMM wait expired");
     });
     for (float* p : scratch) cudaFree(p);

@@ -256,8 +256,23 @@ std::size_t B200Runner::stage_append(const RequestId& id, const std::vector<Toke
     descs_.push_back({slot, sequence.used, int32_t(tokens.size())});
     tokens_.insert(tokens_.end(), tokens.begin(), tokens.end());
     tickets_.push_back(ticket);
+    if (capture_) pending_ids_.push_back(id);
     tx.commit();
     return ticket;
+}
+
+void B200Runner::set_logits_capture(bool on) {
+    if (!descs_.empty()) flush();
+    capture_ = on;
+    pending_ids_.clear();
+    if (!on) captured_.clear();
+}
+
+bool B200Runner::captured_logits(const RequestId& id, std::vector<float>& out) const {
+    const auto it = captured_.find(id);
+    if (it == captured_.end()) return false;
+    out = it->second;
+    return true;
 }
 
 void B200Runner::flush() {
@@ -290,8 +305,16 @@ void B200Runner::flush() {
             error = mp_last_error();
         }
         // after a failed launch this still waits for what was enqueued and ends the step
-        const int collected = mp_forward_collect(ctx_, out_tokens_.data(), out_finite_.data(), nullptr,
-                                                 options_.timeout_ms);
+        const std::size_t vocabulary = std::size_t(config_.vocabulary);
+        if (capture_) out_logits_.assign(std::size_t(n) * vocabulary, 0.f);
+        const int collected = mp_forward_collect(ctx_, out_tokens_.data(), out_finite_.data(),
+                                                 capture_ ? out_logits_.data() : nullptr, options_.timeout_ms);
+        if (capture_ && collected == MP_OK && pending_ids_.size() == std::size_t(n)) {
+            for (int i = 0; i < n; ++i)
+                captured_[pending_ids_[std::size_t(i)]].assign(out_logits_.begin() + std::ptrdiff_t(i * vocabulary),
+                                                               out_logits_.begin() + std::ptrdiff_t((i + 1) * vocabulary));
+            stats_.logits_downloaded_bytes += out_logits_.size() * sizeof(float);
+        }
         if (rc == MP_OK) rc = collected;
     }
     if (rc != MP_OK && error.empty()) error = mp_last_error();
@@ -305,6 +328,7 @@ void B200Runner::flush() {
         entries_.clear();
         regions_.clear();
         tickets_.clear();
+    pending_ids_.clear();
         if (publish_error) std::rethrow_exception(publish_error);
         throw std::runtime_error(std::string("B200 forward: ") + error);
     }
@@ -324,6 +348,7 @@ void B200Runner::flush() {
     entries_.clear();
     regions_.clear();
     tickets_.clear();
+    pending_ids_.clear();
     for (int s : quarantine_) free_slots_.push_back(s);
     quarantine_.clear();
     kv_.next_epoch();
@@ -337,6 +362,7 @@ void B200Runner::restore_batch() {
     entries_.clear();
     regions_.clear();
     tickets_.clear();
+    pending_ids_.clear();
     kv_.restore_checkpoint();
     // Undo slot moves newest first, then forget every device-table mirror.
     auto& cp = *checkpoint_;
@@ -387,6 +413,7 @@ void B200Runner::clear() {
     entries_.clear();
     regions_.clear();
     tickets_.clear();
+    pending_ids_.clear();
     const int rc = ctx_ ? mp_sync(ctx_, options_.timeout_ms) : MP_OK;
     kv_.end_checkpoint();
     checkpoint_.reset();

@@ -70,6 +70,15 @@ public:
     void end_batch() override;
     void set_replay(bool replay) override { replay_ = replay; }
 
+    // Logits capture for parity checks of batched runs: while on, every flush also
+    // downloads the logits of its staged appends (vocabulary floats each) and keeps
+    // the latest ones per request (kept after the request is released, until
+    // capture is switched off). Off by default; the hot path downloads greedy
+    // tokens only.
+    void set_logits_capture(bool on);
+    // Copies the latest captured logits of `id` into `out`; false if there are none.
+    bool captured_logits(const RequestId& id, std::vector<float>& out) const;
+
     // Introspection for tests and tools.
     const KVManager& kv() const { return kv_; }
     mp_context* device() const { return ctx_; }
@@ -110,6 +119,10 @@ private:
     std::vector<mp_tail_copy_region> regions_;
     std::vector<std::size_t> tickets_;
     std::vector<int32_t> out_tokens_, out_finite_;
+    bool capture_ = false;
+    std::vector<RequestId> pending_ids_;  // id of each pending append (capture only)
+    std::vector<float> out_logits_;
+    std::map<RequestId, std::vector<float>> captured_;
     std::uint32_t epoch_ = 1;
     bool replay_ = false;
     std::size_t flushes_ = 0, hazard_flushes_ = 0;

@@ -670,4 +670,21 @@ int mph_engine_flushes(mph_engine* e, size_t* flushes, size_t* hazard_flushes) {
 
 mp_context* mph_engine_device(mph_engine* e) { return e->b200 ? e->b200->device() : nullptr; }
 
+int mph_engine_capture_logits(mph_engine* e, int32_t on) {
+    return int(guarded([&]() -> long {
+        if (!e->b200) throw std::logic_error("logits capture needs a B200 runner");
+        e->b200->set_logits_capture(on != 0);
+        return 0;
+    }));
+}
+
+long mph_engine_logits(mph_engine* e, const char* id, float* out, long capacity) {
+    if (!e->b200) return -2;
+    std::vector<float> logits;
+    if (!e->b200->captured_logits(id, logits)) return -1;
+    const long n = long(logits.size());
+    if (out) std::copy(logits.begin(), logits.begin() + std::min(n, capacity), out);
+    return n;
+}
+
 }  // extern "C"

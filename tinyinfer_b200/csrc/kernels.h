@@ -263,6 +263,12 @@ struct TcGemmParams {
     float* ssq_out;
     const float* ssq_in;
     float eps;
+    // Bound of each mbarrier wait in ns (0: kWaitNanoseconds), and the failure-path
+    // test switch: with `stall` set the producer issues no copies, so every wait
+    // runs out after wait_ns, the kernel records kErrTimeout and returns (no copy
+    // is in flight, the tensor memory is released).
+    uint64_t wait_ns;
+    int stall;
 };
 constexpr int kSsqGroup = 64;  // columns per partial sum of squares
 cudaError_t configure_tc_gemm();

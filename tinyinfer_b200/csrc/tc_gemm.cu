@@ -396,7 +396,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The weights (B) never depend on an earlier kernel: the first stages' weight
     // tiles are requested before waiting for the predecessor (programmatic
     // dependent launch), the activations (A) only after.
-    const int pre = min(S, kblocks);
+    const uint64_t wait_ns = p.wait_ns ? p.wait_ns : kWaitNanoseconds;
+    const int pre = p.stall ? 0 : min(S, kblocks);
     if (warp == 0 && lane == 0) {
         for (int kb = 0; kb < pre; ++kb) {
             unsigned char* st = smem + kb * Cfg::kStage;
@@ -409,9 +410,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_enter();
     if (warp == 0 && lane == 0) {
         // TMA producer
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = 0; kb < (p.stall ? 0 : kblocks); ++kb) {
             const int s = kb % S;
-            if (kb >= S && !mbar_wait_bounded(&empty[s], ((kb / S) - 1) & 1)) {
+            if (kb >= S && !mbar_wait_bounded(&empty[s], ((kb / S) - 1) & 1, wait_ns)) {
                 *failed = 1;
                 break;
             }
@@ -431,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
             const int s = kb % S;
-            if (!mbar_wait_bounded(&full[s], (kb / S) & 1)) {
+            if (!mbar_wait_bounded(&full[s], (kb / S) & 1, wait_ns)) {
                 *failed = 1;
                 ok = false;
                 break;
@@ -456,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
     // Epilogue. The outcome is made CTA-uniform before anything that holds a barrier.
-    if (!mbar_wait_bounded(accum, 0)) *failed = 1;
+    if (!mbar_wait_bounded(accum, 0, wait_ns)) *failed = 1;
     __syncthreads();
     const bool ok = *failed == 0;
     // Once every CTA of the cluster is past its MMAs, every stage ring is idle and

@@ -87,6 +87,7 @@ def library() -> C.CDLL:
         lib.mp_forward_launch.argtypes = [C.c_void_p]
         lib.mp_forward_collect.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32]
         lib.mp_sync.argtypes = [C.c_void_p, C.c_int32]
+        lib.mp_inject_wait_timeout.argtypes = [C.c_void_p, C.c_int32]
         lib.mp_kv_pools.argtypes = [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
                                     C.POINTER(C.c_uint64)]
         lib.mp_kv_read.argtypes = [C.c_void_p, C.c_int32, C.c_uint64, C.c_uint64, C.c_void_p]
@@ -95,6 +96,8 @@ def library() -> C.CDLL:
         lib.mp_timer_elapsed.argtypes = [C.c_void_p, C.POINTER(C.c_float)]
         lib.mp_profile_enable.argtypes = [C.c_void_p, C.c_int32]
         lib.mp_set_shared_prefix.argtypes = [C.c_void_p, C.c_int32, C.c_int32]
+        lib.mp_profile_read_gemm.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_int32),
+                                             C.POINTER(C.c_float), C.POINTER(C.c_int32)]
         lib.mp_profile_read.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_int32),
                                         C.POINTER(C.c_double)]
         lib.mp_paged_attention_decode.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
@@ -210,6 +213,11 @@ class DeviceContext:
     def sync(self, timeout_ms: int = 60000) -> None:
         check(self.lib.mp_sync(self.h, timeout_ms))
 
+    def inject_wait_timeout(self, wait_us: int) -> None:
+        """Failure-path tests: the next forward's first GEMM issues no copies and its
+        bounded waits run out after wait_us microseconds (mp_inject_wait_timeout)."""
+        check(self.lib.mp_inject_wait_timeout(self.h, wait_us))
+
     def pools(self):
         k, v, n = C.c_void_p(), C.c_void_p(), C.c_uint64()
         check(self.lib.mp_kv_pools(self.h, C.byref(k), C.byref(v), C.byref(n)))
@@ -270,6 +278,12 @@ class ContextView:
         ms, n, b = C.c_float(), C.c_int32(), C.c_double()
         check(self.lib.mp_profile_read(self.h, C.byref(ms), C.byref(n), C.byref(b)))
         return ms.value, n.value, b.value
+
+    def profile_read_gemm(self):
+        """(layer GEMM ms, intervals, LM head ms, head launches) since the last read."""
+        g, n, h, k = C.c_float(), C.c_int32(), C.c_float(), C.c_int32()
+        check(self.lib.mp_profile_read_gemm(self.h, C.byref(g), C.byref(n), C.byref(h), C.byref(k)))
+        return g.value, n.value, h.value, k.value
 
     def counters(self, reset: bool = False) -> dict:
         out = CountersC()

@@ -466,6 +466,23 @@ class Engine(_Base):
     def script(self, id, tokens):
         self.runner.script(id, tokens)
 
+    def capture_logits(self, on: bool) -> None:
+        """While on, every device forward also keeps the logits of its appends
+        (parity checks of batched runs; see logits())."""
+        self.lib.mph_engine_capture_logits.argtypes = [C.c_void_p, C.c_int32]
+        self.check(self.lib.mph_engine_capture_logits(self.h, int(bool(on))))
+
+    def logits(self, id):
+        """The latest captured logits of request `id`, or None."""
+        self.lib.mph_engine_logits.restype = C.c_long
+        self.lib.mph_engine_logits.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_long]
+        n = self.lib.mph_engine_logits(self.h, _ids(id), None, 0)
+        if n < 0:
+            return None
+        out = np.empty(n, dtype=np.float32)
+        self.lib.mph_engine_logits(self.h, _ids(id), out.ctypes.data_as(C.c_void_p), n)
+        return out
+
     def device(self):
         """A device.ContextView of the engine's B200 context (None for other runners)."""
         h = self.lib.mph_engine_device(self.h)
