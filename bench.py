@@ -301,7 +301,7 @@ class CpuBaseline:
                            f"({steps} tokens in {elapsed:.1f} s)")}
 
 
-def replay_parity(record):
+def replay_parity(record, cow=True):
     """CPU-baseline leg, after the timed steps: the run's emitted tokens replayed
     through the UNMODIFIED reference engine over its scripted runner
     (oracle/replay.py). Every step's events (request, token, finish reason) must be
@@ -332,7 +332,7 @@ def replay_parity(record):
     last.sequences = {rid: seq for rid, seq in final["sequences"].items() if seq is not None}
     out = {"checked_by": "reference Engine + scripted runner (oracle/_ref) fed this run's emitted tokens"}
     try:
-        out["compared"] = replay(trace, **record["geometry"])
+        out["compared"] = replay(trace, cow=cow, **record["geometry"])
         out["bookkeeping"] = "identical"
     except Mismatch as e:
         out["bookkeeping"] = "MISMATCH"

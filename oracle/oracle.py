@@ -17,6 +17,11 @@ import subprocess
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+# The reference checkout whose sources build _ref/: MINIPREFIX_REFERENCE when set,
+# else a directory named `reference` beside this repository (oracle/Makefile uses
+# the same rule).
+REFERENCE = os.environ.get("MINIPREFIX_REFERENCE",
+                           os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 ORACLE_SO = os.path.join(HERE, "libmporacle.so")
 REF_SO = os.path.join(HERE, "_ref", "libmpref.so")
 
@@ -31,9 +36,9 @@ def build_oracle() -> None:
 
 def build_ref() -> bool:
     """Compile _ref/libmpref.so when the reference sources are present."""
-    if not os.path.isdir(os.environ.get("REF", "/root/reference")):
+    if not os.path.isdir(REFERENCE):
         return os.path.exists(REF_SO)
-    subprocess.run(["make", "-s", "-j8", "-C", HERE, "ref"], check=True)
+    subprocess.run(["make", "-s", "-j8", "-C", HERE, "ref", f"MINIPREFIX_REFERENCE={REFERENCE}"], check=True)
     return True
 
 

@@ -23,8 +23,12 @@ from .oracle import KV_STATS_FIELDS, RefEngine, RefLib, RefRunner
 # RunnerStats fields a scripted reference runner fills (its KV manager's); the
 # rest count device traffic, which a scripted runner has none of.
 KV_FIELDS = KV_STATS_FIELDS
-# CostStats fields that count events rather than time.
+# CostStats fields recorded from the product run: the prefix-cache lookups and
+# publishes (counted by both KV managers) and the copy-on-write pages and bytes
+# (counted by the product runner; the reference's scripted runner counts none,
+# so they are compared against the copy-on-write regions it recorded instead).
 COUNT_FIELDS = ("lookup_calls", "publish_calls", "cow_pages", "cow_bytes")
+KV_COUNT_FIELDS = ("lookup_calls", "publish_calls")
 
 
 @dataclass
@@ -85,9 +89,12 @@ class Mismatch(AssertionError):
 
 
 def replay(trace: Trace, *, vocabulary, context, layers, width, block_tokens, max_blocks, prefix_blocks, max_batch,
-           token_budget, prefill_chunk, ref: RefLib | None = None) -> dict:
+           token_budget, prefill_chunk, ref: RefLib | None = None, cow: bool = True) -> dict:
     """Replays ``trace`` through the reference engine; raises Mismatch at the first
-    difference, else returns a summary of what was compared."""
+    difference, else returns a summary of what was compared. ``cow``: the product
+    runner counts its copy-on-write pages and bytes (a device runner does; a
+    scripted one does not), and they must equal the number of copy-on-write
+    regions the reference engine produced and their bytes (both pools)."""
     ref = ref or RefLib()
     runner = RefRunner.scripted_runner(ref, vocabulary, context, layers, width, block_tokens, max_blocks,
                                        prefix_blocks)
@@ -127,9 +134,16 @@ def replay(trace: Trace, *, vocabulary, context, layers, width, block_tokens, ma
                     diff = {k: (kv[k], s.kv[k]) for k in KV_FIELDS if kv[k] != s.kv[k]}
                     raise Mismatch(f"op {n}: KV stats differ (reference, product): {diff}")
                 cs = engine.cost_stats()
-                costs = {k: cs[k] for k in COUNT_FIELDS}
-                if costs != s.costs:
-                    raise Mismatch(f"op {n}: cost counters {costs} vs {s.costs}")
+                for k in KV_COUNT_FIELDS:
+                    if cs[k] != s.costs[k]:
+                        raise Mismatch(f"op {n}: {k} {cs[k]} (reference) vs {s.costs[k]} (product)")
+                if cow:
+                    regions = engine.regions()
+                    cow_bytes = sum(2 * r[3] * r[4] * 4 for r in regions)  # K and V pools, width x rows floats
+                    if (len(regions), cow_bytes) != (s.costs["cow_pages"], s.costs["cow_bytes"]):
+                        raise Mismatch(f"op {n}: copy-on-write pages / bytes {len(regions)} / {cow_bytes} (reference "
+                                       f"regions) vs {s.costs['cow_pages']} / {s.costs['cow_bytes']} (product)")
+                    counted["cow_pages"] = len(regions)
                 counted["stats_checks"] += 1
             if s.sequences is not None:
                 for rid, seq in s.sequences.items():

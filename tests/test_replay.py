@@ -45,7 +45,7 @@ def record(seed):
 @pytest.mark.parametrize("seed", range(4))
 def test_replay_of_a_product_run_matches(built, ref, seed):
     trace = record(seed)
-    counted = replay(trace, ref=ref, **GEOM)
+    counted = replay(trace, ref=ref, cow=False, **GEOM)
     assert counted["steps"] > 5 and counted["tables"] > 0 and counted["stats_checks"] == counted["steps"]
 
 
@@ -59,27 +59,27 @@ def test_replay_reports_a_changed_event_page_or_stat(built, ref):
     s = next(op[1] for op in t.ops if op[0] == "step" and len(op[1].events) > 1)
     del s.events[-1]
     with pytest.raises(Mismatch, match="events differ"):
-        replay(t, ref=ref, **GEOM)
+        replay(t, ref=ref, cow=False, **GEOM)
     # a finish reason
     t = copy.deepcopy(trace)
     s = next(op[1] for op in t.ops if op[0] == "step" and any(e[2] is not None for e in op[1].events))
     i = next(i for i, e in enumerate(s.events) if e[2] is not None)
     s.events[i] = (s.events[i][0], s.events[i][1], 2)
     with pytest.raises(Mismatch, match="events differ"):
-        replay(t, ref=ref, **GEOM)
+        replay(t, ref=ref, cow=False, **GEOM)
     # a page id
     t = copy.deepcopy(trace)
     s = next(op[1] for op in t.ops if op[0] == "step" and op[1].sequences)
     rid, (used, blocks) = next(iter(s.sequences.items()))
     s.sequences[rid] = (used, [blocks[0] + 1] + blocks[1:])
     with pytest.raises(Mismatch, match="page table"):
-        replay(t, ref=ref, **GEOM)
+        replay(t, ref=ref, cow=False, **GEOM)
     # a KV stat
     t = copy.deepcopy(trace)
     s = [op[1] for op in t.ops if op[0] == "step"][-1]
     s.kv["prefix_hits"] += 1
     with pytest.raises(Mismatch, match="KV stats"):
-        replay(t, ref=ref, **GEOM)
+        replay(t, ref=ref, cow=False, **GEOM)
     assert len(steps) > 5
 
 
@@ -115,10 +115,49 @@ def test_bench_record_format_replays(built, ref):
     record["final"] = {"step_stats": engine.last_step_stats(), "runner_stats": engine.runner_stats(),
                        "costs": engine.cost_stats(), "sequences": {rid: engine.sequence(rid) for rid in ids}}
     record["geometry"] = g
-    out = bench.replay_parity(record)
+    out = bench.replay_parity(record, cow=False)
     assert out["bookkeeping"] == "identical", out
     assert out["compared"]["tables"] == 8
     record["final"]["sequences"]["r3"] = (record["final"]["sequences"]["r3"][0] + 1,
                                           record["final"]["sequences"]["r3"][1])
-    assert bench.replay_parity(record)["bookkeeping"] == "MISMATCH"
+    assert bench.replay_parity(record, cow=False)["bookkeeping"] == "MISMATCH"
     engine.close()
+
+
+def test_copy_on_write_counts_compare_with_reference_regions(built, ref):
+    """A device runner counts its copy-on-write pages and bytes; the replay compares
+    them with the regions the reference engine produced. Here the product scripted
+    runner's own regions stand in for a device runner's counters."""
+    import copy
+
+    g = GEOM
+    rng = np.random.default_rng(11)
+    runner = Runner.scripted(g["vocabulary"], g["context"], g["layers"], g["width"], g["block_tokens"],
+                             g["max_blocks"], g["prefix_blocks"])
+    engine = Engine(runner, g["max_batch"], g["token_budget"], g["prefill_chunk"], g["context"])
+    trace = Trace()
+    shared = [int(t) for t in rng.integers(0, 16, 9)]  # a partial shared page at 4 tokens per page
+    def step():
+        engine.step()
+        trace.step(engine, events=engine.poll_events())
+        regions = runner.regions()
+        trace.ops[-1][1].costs.update(cow_pages=len(regions), cow_bytes=sum(2 * r[3] * r[4] * 4 for r in regions))
+
+    for i in range(6):
+        rid = f"c{i}"
+        runner.script(rid, [int(t) for t in rng.integers(1, 16, 8)])
+        prompt = shared + [int(t) for t in rng.integers(0, 16, 2)]
+        engine.submit(rid, prompt, 4)
+        trace.submit(rid, prompt, 4)
+        if i == 0:  # the seed runs first and publishes the shared pages
+            for _ in range(4):
+                step()
+    while not engine.idle():
+        step()
+    engine.close()
+    counted = replay(trace, ref=ref, **GEOM)
+    assert counted["cow_pages"] >= 1
+    t = copy.deepcopy(trace)
+    t.ops[-1][1].costs["cow_pages"] += 1
+    with pytest.raises(Mismatch, match="copy-on-write"):
+        replay(t, ref=ref, **GEOM)

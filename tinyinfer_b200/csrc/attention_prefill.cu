@@ -1,231 +1,246 @@
-// Chunked-prefill paged attention (sm_100a): many query rows of one sequence.
+// Chunked-prefill paged attention on the tensor cores (sm_100a): many query rows
+// of one sequence against its paged context.
 //
-// Computes the same causal GQA attention as the CPU runner
-// (miniprefix/src/backend/cpu/llama_runner.cpp:85-93) for a chunk of `count` rows
-// appended at positions start..start+count-1, but shares every K/V tile among
-// 64 query rows x 3 heads of one KV group instead of re-reading the context per
-// row and head as the reference kernel does (miniprefix/src/backend/cuda/
-// llama_runner.cu:33-48).
+// Computes the causal GQA attention of the CPU runner
+// (miniprefix/src/backend/cpu/llama_runner.cpp:85-93: scores q.k / sqrt(64) over
+// the tokens at or before the row's position, softmax, weighted sum of V; kv head
+// = head / 3) for a chunk of rows appended at positions start .. start + count - 1,
+// sharing every K/V sub-chunk among the 42 rows x 3 heads of one kv group instead
+// of re-reading the context per row and head as the reference kernel does
+// (miniprefix/src/backend/cuda/llama_runner.cu:33-48).
 //
-// CTA = (64-row query tile, kv head). Per 32-token context tile:
-//   S[192][32] = Q K^T (each thread a 6 x 4 block), masked causally and by length;
-//   online softmax per query vector (one thread per vector, running max / sum);
-//   O[192][64] = O * alpha + P V (each thread a 6 x 8 block).
-// K/V rows are gathered through the block table with 16-byte cp.async into a
-// double-buffered tile; rows past the sequence end are zero-filled so stale
-// shared memory cannot reach the result.
-#include "common.cuh"
-#include "kernels.h"
+// CTA = (tile of up to 42 query rows, kv head), 4 warps. Query vector v (UMMA row,
+// TMEM lane, and the thread that owns it) is row v / 3, head kh * 3 + v % 3;
+// vectors 126, 127 and those of rows past the tile are padding. The query block is
+// split once into TF32 hi / lo halves as a K-major 128-byte-swizzled UMMA tile.
+// Per 64-token sub-chunk of the context [0, start_of_tile + rows):
+//  * its raw K and V rows were gathered through the block table by 16-byte
+//    cp.async while the previous sub-chunk computed; all threads split them into
+//    hi / lo K and V^T tiles, then start the next sub-chunk's gathers;
+//  * one thread issues S = Q K^T as 3xTF32 tcgen05.mma (M=128, N=64) into tensor
+//    memory: Q_lo K_hi + Q_hi K_lo + Q_hi K_hi per 8-dim step (FP32-level products
+//    from TF32 tensor cores; the dropped lo.lo term is below 2^-20 relative);
+//  * thread = query vector: tcgen05.ld of its 64 scores, the causal mask (token <=
+//    the row's position), exact softmax over the sub-chunk in registers (base 2,
+//    log2(e) folded into the 1/8 scale), probabilities written as hi / lo A tiles;
+//  * one thread issues O = P V the same way (K = the 64 tokens);
+//  * thread = query vector: tcgen05.ld of its 64 outputs, folded into a running
+//    (max, sum, output) in registers -- online softmax across sub-chunks; a
+//    sub-chunk that masks all of a vector's tokens leaves its state unchanged.
+// The output (running output / sum) goes out as TF32 hi / lo halves, the O
+// projection's A operand. All MMA waits are bounded mbarrier waits; a timeout sets
+// the error word and the CTA still releases its tensor memory.
+#include "attn_tc.cuh"
 
 namespace mpb {
 namespace {
 
-constexpr int kQRows = kPrefillTileRows;   // query rows per CTA
-constexpr int kQVec = kQRows * kGroup;     // 192 query vectors (row, head of the group)
-constexpr int kKT = 32;                    // context tokens per tile
-constexpr int kThreads = 256;
-constexpr int kQStride = kHeadDim + 1;     // 65: conflict-free column reads
-constexpr int kKVStride = kHeadDim + 4;    // 68: 16-byte aligned rows for cp.async
-constexpr int kSStride = kKT + 1;          // 33
-constexpr size_t kPrefillSmem =
-    (size_t(kQVec) * kQStride + 2 * 2 * kKT * kKVStride + size_t(kQVec) * kSStride + kQVec) * sizeof(float);
+using namespace attn_tc;
+constexpr int kThreads = 128;
+constexpr int kRows = kPrefillTileRows;  // query rows per CTA
+static_assert(kRows * kGroup <= kQ, "a tile's query vectors fit the UMMA M of 128");
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
-// Stage context tokens [t0, t0 + 32) of kv head kh into K/V tile buffers.
-__device__ __forceinline__ void load_tile(const PrefillParams& p, const int32_t* table, int len, int kh, int t0,
-                                          float* kt, float* vt, int tid) {
-    // 32 tokens x 16 float4 per pool; 256 threads -> 2 float4 of K and 2 of V each.
-#pragma unroll
-    for (int it = 0; it < 2; ++it) {
-        const int idx = tid + it * kThreads;  // 0..511
-        const int tok = idx >> 4, c4 = idx & 15;
-        const int t = t0 + tok;
-        float* kd = kt + tok * kKVStride + c4 * 4;
-        float* vd = vt + tok * kKVStride + c4 * 4;
-        if (t < len) {
-            const int page = t / p.block_tokens;
-            int block = page < p.table_stride ? table[page] : -1;
-            if (block < 0 || block >= p.max_blocks) {
-                raise_error(p.error, kErrBounds);
-                block = 0;
-            }
-            const size_t off = ((size_t(block) * p.layers + p.layer) * p.block_tokens + (t - page * p.block_tokens)) *
-                                   kKvWidth + kh * kHeadDim + c4 * 4;
-            cp_async16(kd, p.keys + off);
-            cp_async16(vd, p.values + off);
-        } else {
-            *reinterpret_cast<float4*>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
-            *reinterpret_cast<float4*>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-    }
-    cp_async_commit();
-}
-
-__global__ void __launch_bounds__(kThreads, 2) prefill_attention_kernel(const PrefillParams p) {
+__global__ void __launch_bounds__(kThreads, 1) prefill_attention_kernel(const PrefillParams p) {
     pdl_enter();  // before any global memory access
-    extern __shared__ __align__(16) float sm[];
-    float* Qs = sm;                                  // [192][65]
-    float* Ks = Qs + kQVec * kQStride;               // [2][32][68]
-    float* Vs = Ks + 2 * kKT * kKVStride;            // [2][32][68]
-    float* Ss = Vs + 2 * kKT * kKVStride;            // [192][33]
-    float* alpha_s = Ss + kQVec * kSStride;          // [192]
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* sm =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char *qhi = sm + kOffQhi, *qlo = sm + kOffQlo, *phi = sm + kOffPhi, *plo = sm + kOffPlo;
+    unsigned char *khi = sm + kOffKhi, *klo = sm + kOffKlo;
+    unsigned char *vhi = sm + kOffVhi, *vlo = sm + kOffVlo;
+    float* raw_k = reinterpret_cast<float*>(sm + kOffRawK);
+    float* raw_v = reinterpret_cast<float*>(sm + kOffRawV);
+    int* blk = reinterpret_cast<int*>(sm + kOffBlk);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffBar);
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 1);
+    int* failed = reinterpret_cast<int*>(tmem_holder + 1);
 
+    const int tid = threadIdx.x, warp = tid >> 5;
     const PrefillWork w = p.work[blockIdx.x];
     const int kh = w.kv_head;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int rows = w.rows;                     // valid query rows in this tile (<= 64)
-    const int pos0 = w.position;                 // position of the first query row
-    const int len = pos0 + rows;                 // context needed by the last row
+    const int rows = w.rows;          // valid query rows of the tile (1..42)
+    const int pos0 = w.position;      // position of the tile's first row
+    const int len = pos0 + rows;      // context of the tile's last row
     const int32_t* table = p.tables + size_t(w.slot) * p.table_stride;
+    auto block_of = [&](int token) {
+        return attn_tc::token_block(table, p.table_stride, p.block_tokens, p.max_blocks, token, p.error);
+    };
 
-    // Q tile: vector v = r * 3 + hh holds row (row0 + r), head kh*3 + hh.
-    for (int i = tid; i < kQVec * kHeadDim; i += kThreads) {
-        const int v = i / kHeadDim, d = i % kHeadDim;
-        const int r = v / kGroup, hh = v % kGroup;
-        Qs[v * kQStride + d] =
-            r < rows ? p.q[size_t(w.row0 + r) * p.q_stride + (kh * kGroup + hh) * kHeadDim + d] : 0.f;
+    if (warp == 0) tmem_alloc(tmem_holder, kTmemCols);
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        *failed = 0;
+        fence_barrier_init();
     }
-    const int n_tiles = (len + kKT - 1) / kKT;
-    load_tile(p, table, len, kh, 0, Ks, Vs, tid);
-
-    // identities
-    const int sq = lane, sk = warp;          // scores: vectors sq + 32 i (i < 6), keys sk + 8 j (j < 4)
-    const int oq = lane, od = warp * 8;      // output: vectors oq + 32 i, dims od .. od + 7
-    float m_run = -INFINITY, l_run = 0.f;    // softmax state of vector `tid` (tid < 192)
-    float acc[6][8];
+    // sub-chunk 0's gathers first, then the query block while they fly
+    if (tid < kT) blk[tid] = tid < len ? block_of(tid) : 0;
+    __syncthreads();
+    gather_raw(p.keys, p.values, p.layers, p.layer, p.block_tokens, blk, 0, min(kT, len), kh, raw_k, raw_v, tid,
+               kThreads);
+    int next_blk = 0;  // physical block of this thread's token in the next sub-chunk
+    if (tid < kT && kT + tid < len) next_blk = block_of(kT + tid);
+    {
+        // query vector v -> tile row v: 16 float4 per vector; all loads first
+        constexpr int kPer = kQ * 16 / kThreads;
+        float4 v[kPer];
 #pragma unroll
-    for (int i = 0; i < 6; ++i)
+        for (int u = 0; u < kPer; ++u) {
+            const int i = tid + u * kThreads;
+            const int qv = i >> 4, c4 = i & 15;
+            v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (qv < rows * kGroup) {
+                const int head = kh * kGroup + qv % kGroup;
+                v[u] = *reinterpret_cast<const float4*>(p.q + size_t(w.row0 + qv / kGroup) * p.q_stride +
+                                                        head * kHeadDim + c4 * 4);
+            }
+        }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+        for (int u = 0; u < kPer; ++u) {
+            const int i = tid + u * kThreads;
+            const int qv = i >> 4, c4 = i & 15;
+            store_split4(qhi + (c4 >> 3) * kQTile, qlo + (c4 >> 3) * kQTile, sw128_offset(qv, c4 & 7), v[u]);
+        }
+    }
+    tmem_fence_before();
+    __syncthreads();
+    tmem_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    const uint32_t tmem_s = tmem, tmem_o = tmem + kT;
+    constexpr uint32_t idesc = umma_idesc_tf32<kQ, kT>();
 
-    for (int tile = 0; tile < n_tiles; ++tile) {
-        const int buf = tile & 1;
+    const int qv = warp * 32 + (tid & 31);  // this thread's query vector = TMEM lane
+    const bool live = qv < rows * kGroup;
+    const int my_pos = pos0 + qv / kGroup;  // keys at positions <= my_pos are visible
+    const uint32_t lane_base = uint32_t(warp * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f, o_run[kHeadDim];
+#pragma unroll
+    for (int d = 0; d < kHeadDim; ++d) o_run[d] = 0.f;
+    uint32_t phase = 0;
+    bool ok = true;
+
+    for (int t0 = 0; t0 < len; t0 += kT) {
+        const int n_valid = min(kT, len - t0);
         cp_async_wait_all();
-        __syncthreads();  // tile `tile` landed; previous tile fully consumed
-        if (tile + 1 < n_tiles)
-            load_tile(p, table, len, kh, (tile + 1) * kKT, Ks + (buf ^ 1) * kKT * kKVStride,
-                      Vs + (buf ^ 1) * kKT * kKVStride, tid);
-        const float* K = Ks + buf * kKT * kKVStride;
-        const float* V = Vs + buf * kKT * kKVStride;
-        const int t0 = tile * kKT;
-        // S = Q K^T / 8 with causal mask
-        {
-            float s[6][4];
-#pragma unroll
-            for (int i = 0; i < 6; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
-#pragma unroll 8
-            for (int d = 0; d < kHeadDim; ++d) {
-                float qv[6], kv[4];
-#pragma unroll
-                for (int i = 0; i < 6; ++i) qv[i] = Qs[(sq + 32 * i) * kQStride + d];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) kv[j] = K[(sk + 8 * j) * kKVStride + d];
-#pragma unroll
-                for (int i = 0; i < 6; ++i)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) s[i][j] = fmaf(qv[i], kv[j], s[i][j]);
-            }
-#pragma unroll
-            for (int i = 0; i < 6; ++i) {
-                const int v = sq + 32 * i;
-                const int qpos = pos0 + v / kGroup;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int key = sk + 8 * j;
-                    Ss[v * kSStride + key] = (t0 + key <= qpos) ? s[i][j] * 0.125f : -INFINITY;
-                }
-            }
+        __syncthreads();  // this sub-chunk's raw rows are in shared memory
+        split_kv(raw_k, raw_v, n_valid, khi, klo, vhi, vlo, tid, kThreads);
+        fence_proxy_async_shared();  // generic-proxy tile writes -> tensor-core reads
+        tmem_fence_before();
+        __syncthreads();  // tiles complete; the staging buffer is free
+        tmem_fence_after();
+        if (tid == 0) {
+            issue_3xtf32(tmem_s, qhi, qlo, kQTile, khi, klo, kKTile, idesc);
+            mma_commit(bar);
         }
+        // the next sub-chunk's gathers overlap this one's products
+        const int t1 = t0 + kT;
+        if (t1 < len) {
+            if (tid < kT) blk[tid] = next_blk;
+            __syncthreads();
+            gather_raw(p.keys, p.values, p.layers, p.layer, p.block_tokens, blk, t1, min(kT, len - t1), kh, raw_k,
+                       raw_v, tid, kThreads);
+            next_blk = 0;
+            if (tid < kT && t1 + kT + tid < len) next_blk = block_of(t1 + kT + tid);
+        }
+        if (!mbar_wait_bounded(bar, phase)) *failed = 1;
+        phase ^= 1;
         __syncthreads();
-        // online softmax, one thread per query vector
-        if (tid < kQVec) {
-            float* srow = Ss + tid * kSStride;
-            float mx = m_run;
+        if (*failed) {
+            ok = false;
+            break;
+        }
+        tmem_fence_after();
+        // scores in base-2 units; the causal mask keeps tokens t0 + j <= my_pos
+        float s[kT];
+        tmem_row64(tmem_s + lane_base, s);
+        const int visible = live ? min(n_valid, my_pos - t0 + 1) : 0;  // tokens j < visible
+        float mx = -INFINITY;
 #pragma unroll
-            for (int k = 0; k < kKT; ++k) mx = fmaxf(mx, srow[k]);
-            // Rows past `rows` see only masked keys beyond their position; keep them finite.
-            const float m_new = mx;
-            const float alpha = m_new == -INFINITY ? 1.f : expf(m_run - m_new);
-            float sum = 0.f;
+        for (int j = 0; j < kT; ++j) {
+            s[j] = j < visible ? s[j] * (0.125f * kLog2e) : -INFINITY;
+            mx = fmaxf(mx, s[j]);
+        }
+        float sum = 0.f;
+        const float base = visible > 0 ? mx : 0.f;  // all masked: every weight 0
 #pragma unroll
-            for (int k = 0; k < kKT; ++k) {
-                const float e = m_new == -INFINITY ? 0.f : expf(srow[k] - m_new);
-                srow[k] = e;
-                sum += e;
-            }
-            l_run = l_run * alpha + sum;
+        for (int j = 0; j < kT; ++j) {
+            s[j] = j < visible ? exp2f(s[j] - base) : 0.f;
+            sum += s[j];
+        }
+        // P as the A operand (rows = query vectors, K = tokens)
+#pragma unroll
+        for (int c4 = 0; c4 < kT / 4; ++c4)
+            store_split4(phi + (c4 >> 3) * kQTile, plo + (c4 >> 3) * kQTile, sw128_offset(qv, c4 & 7),
+                         make_float4(s[4 * c4], s[4 * c4 + 1], s[4 * c4 + 2], s[4 * c4 + 3]));
+        fence_proxy_async_shared();
+        tmem_fence_before();
+        __syncthreads();
+        tmem_fence_after();
+        if (tid == 0) {
+            issue_3xtf32(tmem_o, phi, plo, kQTile, vhi, vlo, kKTile, idesc);
+            mma_commit(bar);
+        }
+        if (!mbar_wait_bounded(bar, phase)) *failed = 1;
+        phase ^= 1;
+        __syncthreads();
+        if (*failed) {
+            ok = false;
+            break;
+        }
+        tmem_fence_after();
+        if (visible > 0) {
+            // fold this sub-chunk into the running (max, sum, output)
+            const float m_new = fmaxf(m_run, mx);
+            const float a_old = exp2f(m_run - m_new), a_new = exp2f(mx - m_new);  // m_run = -inf: a_old = 0
+            l_run = l_run * a_old + sum * a_new;
             m_run = m_new;
-            alpha_s[tid] = alpha;
+            float o[kT];
+            tmem_row64(tmem_o + lane_base, o);
+#pragma unroll
+            for (int d = 0; d < kHeadDim; ++d) o_run[d] = fmaf(o_run[d], a_old, o[d] * a_new);
         }
-        __syncthreads();
-        // O = O * alpha + P V
-        {
-            float al[6];
+        tmem_fence_before();
+    }
+    cp_async_wait_all();  // nothing may still land in shared memory after the CTA ends
+
+    if (ok && live) {
+        const int r = qv / kGroup, head = kh * kGroup + qv % kGroup;
+        const size_t at = size_t(w.row0 + r) * p.out_stride + head * kHeadDim;
+        const float inv = 1.0f / l_run;
 #pragma unroll
-            for (int i = 0; i < 6; ++i) al[i] = alpha_s[oq + 32 * i];
-#pragma unroll
-            for (int i = 0; i < 6; ++i)
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] *= al[i];
-#pragma unroll 4
-            for (int k = 0; k < kKT; ++k) {
-                const float4 v0 = *reinterpret_cast<const float4*>(V + k * kKVStride + od);
-                const float4 v1 = *reinterpret_cast<const float4*>(V + k * kKVStride + od + 4);
-                const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-                for (int i = 0; i < 6; ++i) {
-                    const float pr = Ss[(oq + 32 * i) * kSStride + k];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(pr, vv[j], acc[i][j]);
-                }
+        for (int c4 = 0; c4 < kHeadDim / 4; ++c4) {
+            const float4 val = make_float4(o_run[4 * c4] * inv, o_run[4 * c4 + 1] * inv, o_run[4 * c4 + 2] * inv,
+                                           o_run[4 * c4 + 3] * inv);
+            if (p.out_lo) {
+                float4 h, l;
+                split_tf32(val.x, h.x, l.x);
+                split_tf32(val.y, h.y, l.y);
+                split_tf32(val.z, h.z, l.z);
+                split_tf32(val.w, h.w, l.w);
+                *reinterpret_cast<float4*>(p.out + at + 4 * c4) = h;
+                *reinterpret_cast<float4*>(p.out_lo + at + 4 * c4) = l;
+            } else {
+                *reinterpret_cast<float4*>(p.out + at + 4 * c4) = val;
             }
         }
     }
+    if (!ok && tid == 0) raise_error(p.error, kErrTimeout);
+    tmem_fence_before();
     __syncthreads();
-    if (tid < kQVec) alpha_s[tid] = l_run;  // reuse as the final denominators
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < 6; ++i) {
-        const int v = oq + 32 * i;
-        const int r = v / kGroup, hh = v % kGroup;
-        if (r >= rows) continue;
-        const float den = alpha_s[v];
-        const size_t at = size_t(w.row0 + r) * p.out_stride + (kh * kGroup + hh) * kHeadDim + od;
-        float val[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) val[j] = acc[i][j] / den;
-        if (p.out_lo) {
-            float hi[8], lo[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) split_tf32(val[j], hi[j], lo[j]);
-            *reinterpret_cast<float4*>(p.out + at) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-            *reinterpret_cast<float4*>(p.out + at + 4) = make_float4(hi[4], hi[5], hi[6], hi[7]);
-            *reinterpret_cast<float4*>(p.out_lo + at) = make_float4(lo[0], lo[1], lo[2], lo[3]);
-            *reinterpret_cast<float4*>(p.out_lo + at + 4) = make_float4(lo[4], lo[5], lo[6], lo[7]);
-        } else {
-            *reinterpret_cast<float4*>(p.out + at) = make_float4(val[0], val[1], val[2], val[3]);
-            *reinterpret_cast<float4*>(p.out + at + 4) = make_float4(val[4], val[5], val[6], val[7]);
-        }
+    if (warp == 0) {
+        tmem_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
     }
 }
 
 }  // namespace
 
 cudaError_t configure_prefill_attention() {
-    return cudaFuncSetAttribute(prefill_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(kPrefillSmem));
+    return cudaFuncSetAttribute(prefill_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem));
 }
 
 cudaError_t launch_prefill_attention(const PrefillParams& p, cudaStream_t stream) {
     if (p.work_count <= 0) return cudaSuccess;
-    return launch_pdl(prefill_attention_kernel, dim3(p.work_count), dim3(kThreads), kPrefillSmem, stream, p);
+    return launch_pdl(prefill_attention_kernel, dim3(p.work_count), dim3(kThreads), kSmem, stream, p);
 }
 
 }  // namespace mpb

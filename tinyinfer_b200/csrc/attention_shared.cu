@@ -29,50 +29,17 @@
 //  * thread = query row: tcgen05.ld of its 64 outputs, folded into a running
 //    (max, sum, output) in registers -- online softmax across sub-chunks.
 // All MMA waits are bounded mbarrier waits; a timeout sets the error word.
-#include "common.cuh"
-#include "kernels.h"
-#include "umma.cuh"
+#include "attn_tc.cuh"
 
 namespace mpb {
 namespace {
 
+using namespace attn_tc;
 constexpr int kPQ = kPrefixQueries;  // 128 query vectors = UMMA M
-constexpr int kPT = 64;              // tokens per sub-chunk = UMMA N of S, K of P.V
+static_assert(kPQ == attn_tc::kQ, "query block of the tensor-core attention tiles");
+constexpr int kPT = attn_tc::kT;     // tokens per sub-chunk
 constexpr int kPThreads = 128;
-constexpr int kQTile = kPQ * 32 * 4;   // one 32-element K block of a 128-row tile (16 KB)
-constexpr int kKTile = kPT * 32 * 4;   // one K block of a 64-row tile (8 KB)
-// shared memory (1024-aligned tiles): Q hi / lo and P hi / lo (2 K blocks each),
-// K hi / lo and V^T hi / lo (2 K blocks each), the raw K and V staging rows
-// ([64 tokens][64 floats]; V's 16-byte chunks XOR-swizzled by token so the
-// transposing reads spread over the banks), the physical blocks of the staged
-// tokens, then the barrier and the TMEM address
-constexpr int kOffQhi = 0, kOffQlo = 2 * kQTile;
-constexpr int kOffPhi = 4 * kQTile, kOffPlo = 6 * kQTile;
-constexpr int kOffKhi = 8 * kQTile, kOffKlo = kOffKhi + 2 * kKTile;
-constexpr int kOffVhi = kOffKlo + 2 * kKTile, kOffVlo = kOffVhi + 2 * kKTile;
-constexpr int kOffRawK = kOffVlo + 2 * kKTile, kOffRawV = kOffRawK + kPT * kHeadDim * 4;
-constexpr int kOffBlk = kOffRawV + kPT * kHeadDim * 4;
-constexpr int kOffBar = kOffBlk + kPT * 4;
-constexpr size_t kPrefixSmem = size_t(kOffBar) + 64 + 1024 /*alignment slack*/;
-static_assert(kPrefixSmem <= 232448, "shared memory of the prefix kernel");
-constexpr uint32_t kTmemCols = 128;  // S: columns 0..63, O: 64..127
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
-__device__ __forceinline__ void store_split4(unsigned char* hi_tile, unsigned char* lo_tile, uint32_t off,
-                                             float4 v) {
-    float4 h, l;
-    split_tf32(v.x, h.x, l.x);
-    split_tf32(v.y, h.y, l.y);
-    split_tf32(v.z, h.z, l.z);
-    split_tf32(v.w, h.w, l.w);
-    *reinterpret_cast<float4*>(hi_tile + off) = h;
-    *reinterpret_cast<float4*>(lo_tile + off) = l;
-}
+constexpr size_t kPrefixSmem = attn_tc::kSmem;
 
 // Query block: qv = row_in_group * 3 + head_in_group -> tile row, hi/lo halves.
 // All 16 loads of a thread are issued before any is split and stored.
@@ -100,55 +67,9 @@ __device__ __forceinline__ void load_queries(const PrefixParams& p, const Prefix
     }
 }
 
-// Float offset of the K/V row of token t0 + t (kv head kh) in either pool, from the
-// sub-chunk's staged physical block ids (blk[t]).
-__device__ __forceinline__ size_t kv_offset(const PrefixParams& p, const int* blk, int t0, int t, int kh) {
-    const int token = t0 + t;
-    return ((size_t(blk[t]) * p.layers + p.layer) * p.block_tokens + token % p.block_tokens) * kKvWidth +
-           kh * kHeadDim;
-}
-
-// 3xTF32 product over 2 K blocks of 32: D = A_lo B_hi + A_hi B_lo + A_hi B_hi.
-__device__ __forceinline__ void issue_3xtf32(uint32_t tmem_d, const unsigned char* a_hi, const unsigned char* a_lo,
-                                             int a_block_bytes, const unsigned char* b_hi, const unsigned char* b_lo,
-                                             int b_block_bytes, uint32_t idesc) {
-#pragma unroll
-    for (int kb = 0; kb < 2; ++kb) {
-        const uint64_t ah = smem_desc(a_hi + kb * a_block_bytes), al = smem_desc(a_lo + kb * a_block_bytes);
-        const uint64_t bh = smem_desc(b_hi + kb * b_block_bytes), bl = smem_desc(b_lo + kb * b_block_bytes);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint64_t step = uint64_t(j * 32) >> 4;  // 8 tf32 = 32 bytes along the swizzled row
-            mma_tf32(tmem_d, al + step, bh + step, idesc, (kb | j) != 0);
-            mma_tf32(tmem_d, ah + step, bl + step, idesc, 1);
-            mma_tf32(tmem_d, ah + step, bh + step, idesc, 1);
-        }
-    }
-}
-
 // Physical block of shared token `token`, bounds-checked.
 __device__ __forceinline__ int token_block(const PrefixParams& p, const int32_t* table, int token) {
-    const int page = token / p.block_tokens;
-    int block = page < p.table_stride ? table[page] : -1;
-    if (block < 0 || block >= p.max_blocks) {
-        raise_error(p.error, kErrBounds);
-        block = 0;  // stay in bounds; the error word fails the step
-    }
-    return block;
-}
-
-// Start the gathers of the raw K / V rows of tokens [t0, t0 + n) into staging
-// (blk holds their physical blocks); rows past n are not fetched.
-__device__ __forceinline__ void gather_raw(const PrefixParams& p, const int* blk, int t0, int n, int kh, float* raw_k,
-                                           float* raw_v, int tid) {
-    for (int i = tid; i < kPT * 16; i += kPThreads) {
-        const int t = i >> 4, c4 = i & 15;
-        if (t >= n) continue;
-        const size_t off = kv_offset(p, blk, t0, t, kh) + c4 * 4;
-        cp_async16(raw_k + t * kHeadDim + c4 * 4, p.keys + off);
-        cp_async16(raw_v + t * kHeadDim + ((c4 ^ (t & 15)) * 4), p.values + off);
-    }
-    cp_async_commit();
+    return attn_tc::token_block(table, p.table_stride, p.block_tokens, p.max_blocks, token, p.error);
 }
 
 __global__ void __launch_bounds__(kPThreads, 1) prefix_attention_kernel(const PrefixParams p) {
@@ -181,7 +102,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefix_attention_kernel(const Pr
     // sub-chunk 0's gathers first, then the query block while they fly
     if (tid < kPT) blk[tid] = w.tok_begin + tid < w.tok_end ? token_block(p, table, w.tok_begin + tid) : 0;
     __syncthreads();
-    gather_raw(p, blk, w.tok_begin, min(kPT, w.tok_end - w.tok_begin), kh, raw_k, raw_v, tid);
+    gather_raw(p.keys, p.values, p.layers, p.layer, p.block_tokens, blk, w.tok_begin,
+               min(kPT, w.tok_end - w.tok_begin), kh, raw_k, raw_v, tid, kPThreads);
     // physical block of this thread's token in the next sub-chunk, fetched early
     int next_blk = 0;
     if (tid < kPT && w.tok_begin + kPT + tid < w.tok_end) next_blk = token_block(p, table, w.tok_begin + kPT + tid);
@@ -207,27 +129,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefix_attention_kernel(const Pr
         __syncthreads();  // this sub-chunk's raw rows are in shared memory
         // split into hi / lo K rows (token-major) and V^T (dim-major); tokens past
         // the sub-chunk are zero
-        for (int i = tid; i < kPT * 16; i += kPThreads) {
-            const int t = i >> 4, c4 = i & 15;
-            const float4 kv = t < n_valid ? *reinterpret_cast<const float4*>(raw_k + t * kHeadDim + c4 * 4)
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-            store_split4(khi + (c4 >> 3) * kKTile, klo + (c4 >> 3) * kKTile, sw128_offset(t, c4 & 7), kv);
-        }
-        for (int i = tid; i < kPT * 16; i += kPThreads) {
-            const int t = i & (kPT - 1), c4 = i / kPT;  // consecutive threads: consecutive tokens
-            const float4 vv = t < n_valid ? *reinterpret_cast<const float4*>(raw_v + t * kHeadDim + ((c4 ^ (t & 15)) * 4))
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float ve[4] = {vv.x, vv.y, vv.z, vv.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int d = 4 * c4 + e;  // V^T row; column = token t (K block t / 32)
-                const uint32_t off = sw128_offset(d, (t & 31) >> 2) + uint32_t(t & 3) * 4;
-                float h, l;
-                split_tf32(ve[e], h, l);
-                *reinterpret_cast<float*>(vhi + (t >> 5) * kKTile + off) = h;
-                *reinterpret_cast<float*>(vlo + (t >> 5) * kKTile + off) = l;
-            }
-        }
+        split_kv(raw_k, raw_v, n_valid, khi, klo, vhi, vlo, tid, kPThreads);
         fence_proxy_async_shared();  // generic-proxy tile writes -> tensor-core reads
         tmem_fence_before();
         __syncthreads();  // split tiles complete; the staging buffer is free
@@ -241,7 +143,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefix_attention_kernel(const Pr
         if (t1 < w.tok_end) {
             if (tid < kPT) blk[tid] = next_blk;
             __syncthreads();
-            gather_raw(p, blk, t1, min(kPT, w.tok_end - t1), kh, raw_k, raw_v, tid);
+            gather_raw(p.keys, p.values, p.layers, p.layer, p.block_tokens, blk, t1, min(kPT, w.tok_end - t1), kh,
+                       raw_k, raw_v, tid, kPThreads);
             next_blk = 0;
             if (tid < kPT && t1 + kPT + tid < w.tok_end) next_blk = token_block(p, table, t1 + kPT + tid);
         }

@@ -237,7 +237,7 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
                     plan.prefill.push_back({row + t * mpb::kPrefillTileRows, rows_in,
                                             s.start + t * mpb::kPrefillTileRows, s.slot, kh, {0, 0, 0}});
             }
-            // The context of the whole chunk is read once per 64-row tile.
+            // The context of the whole chunk is read once per row tile.
             const int tiles = (s.count + mpb::kPrefillTileRows - 1) / mpb::kPrefillTileRows;
             double b = 0;
             for (int t = 0; t < tiles; ++t) {
@@ -281,6 +281,11 @@ void plan_attention(const mp_sequence_desc* seqs, int count, int block_tokens, i
             },
             [&](int, int items) { plan.cta_items.push_back(items); });
     }
+    // prefill tiles with the longest context first: the CTAs with the most work
+    // start in the first wave
+    std::stable_sort(plan.prefill.begin(), plan.prefill.end(), [](const mpb::PrefillWork& a, const mpb::PrefillWork& b) {
+        return a.position + a.rows > b.position + b.rows;
+    });
     // shared-prefix slots follow the decode work items in the partial array
     for (int r = 0; r < rows; ++r)
         if (plan.nx[r]) plan.x0[r] += int(plan.work.size());

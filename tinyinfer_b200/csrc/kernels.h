@@ -104,7 +104,7 @@ cudaError_t configure_prefix_attention();
 // Chunked prefill: one CTA per (64-row query tile of one sequence, kv head).
 struct PrefillWork {
     int32_t row0;      // batch row of the tile's first query
-    int32_t rows;      // valid rows in the tile (1..64)
+    int32_t rows;      // valid rows in the tile (1..kPrefillTileRows)
     int32_t position;  // sequence position of the first row
     int32_t slot;      // block-table slot of the sequence
     int32_t kv_head;
@@ -130,7 +130,9 @@ struct PrefillParams {
 // Sequences appending at least this many rows in one forward take the tiled
 // prefill kernel; shorter appends (decode) take the split-K decode kernel per row.
 constexpr int kPrefillMinRows = 8;
-constexpr int kPrefillTileRows = 64;
+// query rows per prefill CTA: rows x 3 heads of a kv group fill the 128 rows of
+// the tensor-core tile
+constexpr int kPrefillTileRows = 42;
 
 cudaError_t configure_prefill_attention();
 cudaError_t launch_prefill_attention(const PrefillParams& p, cudaStream_t stream);
