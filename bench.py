@@ -54,8 +54,9 @@ def parse():
     p.add_argument("--prefill-budget", type=int, default=8192)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-workers", type=int, default=0)
-    p.add_argument("--operator", action="store_true",
-                   help="time the paged-attention decode operator alone on BASELINE config 2")
+    p.add_argument("--operator", nargs="?", const="decode", choices=["decode", "prefill"], default=None,
+                   help="time an attention operator alone: decode on BASELINE config 2, or prefill on config 4's "
+                        "last chunk (16 sequences x 512 rows at position 3584)")
     p.add_argument("--workload", choices=["config3", "config4", "config5"], default="config3",
                    help="config3: the headline decode benchmark; config4 / config5: the serving workloads "
                         "of bench_serving.py")
@@ -646,6 +647,71 @@ def run_operator(args, local_rank):
             "clocks": clocks.summary()}
 
 
+def run_operator_prefill(args, local_rank):
+    """The tensor-core prefill attention operator on BASELINE config 4's geometry:
+    16 sequences each appending its last 512-token chunk at positions 3584..4095 of
+    a 4096-token prompt (one-layer pool, random-permutation tables, Q/K/V ~ N(0,1)).
+    Useful FLOP = 4 x 64 per (row, head, visible key); the kernel issues 3x that
+    as 3xTF32 MMAs plus the masked part of each 64-token sub-chunk."""
+    import torch
+
+    from tinyinfer_b200 import device
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    seqs, start, count, bt = 16, 3584, 512, 16
+    pages = (start + count) // bt
+    pool = seqs * pages
+    rng = np.random.default_rng(4)
+    tables = rng.permutation(pool).astype(np.int32).reshape(seqs, pages)
+    gen = torch.Generator(device=dev).manual_seed(4)
+    keys = torch.randn(pool * bt * 192, device=dev, generator=gen)
+    values = torch.randn(pool * bt * 192, device=dev, generator=gen)
+    q = torch.randn(seqs * count, 576, device=dev, generator=gen)
+    out = torch.empty_like(q)
+    tt = torch.from_numpy(tables).to(dev)
+    stream = torch.cuda.current_stream()
+    starts, counts = [start] * seqs, [count] * seqs
+    visible = seqs * sum(start + r + 1 for r in range(count))  # (row, key) pairs per head
+    useful = 4.0 * 64 * 9 * visible
+
+    def launch():
+        device.paged_attention_prefill(q.data_ptr(), keys.data_ptr(), values.data_ptr(), 1, 0, bt, pool,
+                                       tt.data_ptr(), pages, starts, counts, out.data_ptr(), stream.cuda_stream)
+
+    peak = tf32_peak(local_rank)
+    for _ in range(max(args.warmup, 1)):
+        launch()
+    torch.cuda.synchronize()
+    times = []
+    with ClockSampler(local_rank) as clocks:
+        torch.cuda.cudart().cudaProfilerStart()
+        for _ in range(args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            launch()
+            b.record(stream)
+            times.append((a, b))
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+    assert device.paged_attention_status(stream.cuda_stream) == 0
+    ms = [a.elapsed_time(b) for a, b in times]
+    avg = sum(ms) / len(ms)
+    tflops = useful / (avg * 1e-3) / 1e12
+    return {"metric": "prefill attention useful TFLOP/s (BASELINE config 4, last 512-token chunk)", "value": tflops,
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": avg,
+            "higher_is_better": True, "dtype": "f32 (3xTF32 tensor-core products)",
+            "data": "synthetic (seeded N(0,1) Q/K/V)",
+            "config": {"workload": "config4 prefill attention operator: 16 sequences x 512 rows at positions "
+                                   "3584..4095, 9q/3kv heads, d 64, page 16, random-permutation tables",
+                       "useful_flop": useful, "prompt_tokens_per_step": seqs * count},
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tflops / peak, "issued_frac": 3 * tflops / peak,
+                         "peak_kind": "measured here: cuBLAS TF32 8192^3, best of 10",
+                         "min_ms": min(ms), "max_ms": max(ms)},
+            "clocks": clocks.summary()}
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args, rank, world):
     """The reference arm: the reference's own CPU engine (oracle/_ref, compiled from
@@ -677,7 +743,8 @@ def main():
     if args.impl == "reference":
         line = run_reference(args, rank, world)
     elif args.operator:
-        line = run_operator(args, local_rank) if rank == 0 else None
+        run = run_operator_prefill if args.operator == "prefill" else run_operator
+        line = run(args, local_rank) if rank == 0 else None
     elif args.workload != "config3":
         import bench_serving
 

@@ -227,6 +227,20 @@ int mp_paged_attention_decode_noalloc(const float* q, const float* keys, const f
  * mp_paged_attention_decode_noalloc fills when given no device_error): MP_OK,
  * MP_ERR_BOUNDS (a page id outside [0, max_blocks)) or MP_ERR_TIMEOUT (an in-kernel
  * copy wait expired; the allocating operator's arrival counters are reset). */
+/* The paged-attention PREFILL operator alone: causal attention of chunks of
+ * query rows (miniprefix/src/backend/cuda/llama_runner.cu:33-48 for rows past the
+ * first; the CPU runner's loop miniprefix/src/backend/cpu/llama_runner.cpp:85-93).
+ * Sequence i appends seq_counts[i] rows at positions seq_starts[i] ..
+ * seq_starts[i] + seq_counts[i] - 1; its rows are consecutive in q and out
+ * ([rows][9*64], sequences in order) and its K/V rows up to the last position are
+ * already in the pools. Row r attends to the sequence's tokens 0 .. its position.
+ * seq_starts / seq_counts are HOST arrays; tables [count][table_stride] (device).
+ * Runs the tensor-core prefill kernel on `stream` without synchronising; shares
+ * the decode operator's internal scratch (errors: mp_paged_attention_status). */
+int mp_paged_attention_prefill(const float* q, const float* keys, const float* values, int32_t layers,
+                               int32_t layer, int32_t block_tokens, int32_t max_blocks, const int32_t* tables,
+                               int32_t table_stride, const int32_t* seq_starts, const int32_t* seq_counts,
+                               int32_t count, float* out, void* stream);
 int mp_paged_attention_status(void* stream);
 
 #ifdef __cplusplus

@@ -64,3 +64,45 @@ def test_chunked_prefill_two_sequences_against_oracle(built):
         last = step([(0, [last[0]]), (1, [last[1]])])
     ctx.close()
     print(f"chunked prefill: worst abs err {worst:.3g}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("seed", [3, 4])
+def test_prefill_operator_against_oracle(built, seed):
+    """mp_paged_attention_prefill on random N(0,1) Q/K/V: chunks at positions 0 and
+    deep into a context, tiles that end mid-chunk, single-row chunks, page tables
+    that are a random permutation of the pool. Each row equals the oracle's decode
+    attention of that row over the tokens up to its position, within the attention
+    tests' tolerance |gpu - oracle| <= 1e-5 + 1e-4 |oracle|."""
+    import torch
+    from tinyinfer_b200 import device
+
+    rng = np.random.default_rng(seed)
+    bt, pool = 16, 2048
+    chunks = [(0, 50), (100, 42), (1000, 300), (3584, 512), (7, 1), (64, 43)]
+    stride = max(-(-(s + c) // bt) for s, c in chunks)
+    perm = rng.permutation(pool).astype(np.int32)
+    tables = np.zeros((len(chunks), stride), dtype=np.int32)
+    at = 0
+    for i, (s, c) in enumerate(chunks):
+        n = -(-(s + c) // bt)
+        tables[i, :n] = perm[at:at + n]
+        at += n
+    keys = rng.standard_normal(pool * bt * 192, dtype=np.float32)
+    values = rng.standard_normal(pool * bt * 192, dtype=np.float32)
+    rows = sum(c for _, c in chunks)
+    q = rng.standard_normal((rows, 576), dtype=np.float32)
+    dev = torch.device("cuda:0")
+    tq, tk, tv, tt = (torch.from_numpy(a).to(dev) for a in (q, keys, values, tables))
+    out = torch.full_like(tq, float("nan"))
+    stream = torch.cuda.current_stream().cuda_stream
+    device.paged_attention_prefill(tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), 1, 0, bt, pool, tt.data_ptr(), stride,
+                                   [s for s, _ in chunks], [c for _, c in chunks], out.data_ptr(), stream)
+    assert device.paged_attention_status(stream) == 0
+    got = out.cpu().numpy()
+    lengths = np.concatenate([np.arange(s + 1, s + c + 1) for s, c in chunks]).astype(np.int32)
+    row_tables = np.concatenate([np.repeat(tables[i:i + 1], c, axis=0) for i, (_, c) in enumerate(chunks)])
+    expect = Oracle.decode_attention(q, lengths, row_tables, keys, values, 9, 3, 64, bt)
+    assert np.isfinite(got).all()
+    err = np.abs(got - expect)
+    assert (err <= 1e-5 + 1e-4 * np.abs(expect)).all(), float(err.max())

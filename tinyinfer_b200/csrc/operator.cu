@@ -168,6 +168,77 @@ extern "C" int mp_paged_attention_decode(const float* q, const float* keys, cons
     return MP_OK;
 }
 
+extern "C" int mp_paged_attention_prefill(const float* q, const float* keys, const float* values, int32_t layers,
+                                          int32_t layer, int32_t block_tokens, int32_t max_blocks,
+                                          const int32_t* tables, int32_t table_stride, const int32_t* seq_starts,
+                                          const int32_t* seq_counts, int32_t count, float* out, void* stream_ptr) {
+    if (!q || !keys || !values || !tables || !seq_starts || !seq_counts || !out || count < 1 || layers < 1 ||
+        layer < 0 || layer >= layers || block_tokens < 1 || max_blocks < 1 || table_stride < 1) {
+        mpb::set_last_error("invalid argument");
+        return MP_ERR_INVALID;
+    }
+    // Tiles of up to kPrefillTileRows rows per (sequence, kv head), the longest
+    // context first (the planner of the forward does the same).
+    std::vector<mpb::PrefillWork> work;
+    int row = 0;
+    for (int i = 0; i < count; ++i) {
+        if (seq_starts[i] < 0 || seq_counts[i] < 1 ||
+            int64_t(seq_starts[i]) + seq_counts[i] > int64_t(table_stride) * block_tokens) {
+            mpb::set_last_error("sequence rows outside its block table");
+            return MP_ERR_INVALID;
+        }
+        for (int t = 0; t * mpb::kPrefillTileRows < seq_counts[i]; ++t)
+            for (int kh = 0; kh < mpb::kKvHeads; ++kh)
+                work.push_back({row + t * mpb::kPrefillTileRows,
+                                std::min(mpb::kPrefillTileRows, seq_counts[i] - t * mpb::kPrefillTileRows),
+                                seq_starts[i] + t * mpb::kPrefillTileRows, i, kh, {0, 0, 0}});
+        row += seq_counts[i];
+    }
+    std::stable_sort(work.begin(), work.end(), [](const mpb::PrefillWork& a, const mpb::PrefillWork& b) {
+        return a.position + a.rows > b.position + b.rows;
+    });
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return MP_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    Scratch& s = g_scratch[device];
+    const size_t words = work.size() * sizeof(mpb::PrefillWork) / sizeof(int32_t);
+    cudaError_t e = grow(s.meta, s.meta_capacity, words, stream, false);
+    if (e == cudaSuccess && !s.error) {
+        e = cudaMalloc(reinterpret_cast<void**>(&s.error), sizeof(unsigned));
+        if (e == cudaSuccess) e = cudaMemsetAsync(s.error, 0, sizeof(unsigned), stream);
+    }
+    if (e == cudaSuccess) e = mpb::configure_prefill_attention();
+    // pageable source: staged before cudaMemcpyAsync returns
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s.meta, work.data(), words * 4, cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) {
+        mpb::set_last_error(cudaGetErrorString(e));
+        return e == cudaErrorMemoryAllocation ? MP_ERR_NOMEM : MP_ERR_CUDA;
+    }
+    mpb::PrefillParams p{};
+    p.q = q;
+    p.q_stride = mpb::kQWidth;
+    p.keys = keys;
+    p.values = values;
+    p.layers = layers;
+    p.layer = layer;
+    p.block_tokens = block_tokens;
+    p.max_blocks = max_blocks;
+    p.tables = tables;
+    p.table_stride = table_stride;
+    p.work = reinterpret_cast<const mpb::PrefillWork*>(s.meta);
+    p.work_count = int(work.size());
+    p.out = out;
+    p.out_stride = mpb::kQWidth;
+    p.error = s.error;
+    e = mpb::launch_prefill_attention(p, stream);
+    if (e != cudaSuccess) {
+        mpb::set_last_error(cudaGetErrorString(e));
+        return MP_ERR_CUDA;
+    }
+    return MP_OK;
+}
+
 // Reads and clears the operators' device error words on the current device
 // (synchronises `stream`): the allocating operator's, and the word that
 // mp_paged_attention_decode_noalloc writes when its caller passes no

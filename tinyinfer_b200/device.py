@@ -104,6 +104,9 @@ def library() -> C.CDLL:
                                                   C.c_int32, C.c_void_p, C.c_int32, C.c_void_p, C.c_int32,
                                                   C.c_void_p, C.c_int32, C.c_void_p]
         lib.mp_paged_attention_status.argtypes = [C.c_void_p]
+        lib.mp_paged_attention_prefill.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32,
+                                                   C.c_int32, C.c_int32, C.c_void_p, C.c_int32, C.c_void_p,
+                                                   C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]
         lib.mp_gemm_f32.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p]
         _lib = lib
     return _lib
@@ -307,6 +310,17 @@ def paged_attention_decode(q_ptr: int, keys_ptr: int, values_ptr: int, layers: i
     check(lib.mp_paged_attention_decode(q_ptr, keys_ptr, values_ptr, layers, layer, block_tokens, max_blocks,
                                         tables_ptr, table_stride, _ptr(lens), len(lens), out_ptr, pages_per_split,
                                         stream))
+
+
+def paged_attention_prefill(q_ptr: int, keys_ptr: int, values_ptr: int, layers: int, layer: int, block_tokens: int,
+                            max_blocks: int, tables_ptr: int, table_stride: int, starts, counts, out_ptr: int,
+                            stream: int | None = None) -> None:
+    """The prefill operator on caller device pointers (see mp_paged_attention_prefill)."""
+    lib = library()
+    st = np.ascontiguousarray(starts, dtype=np.int32)
+    ct = np.ascontiguousarray(counts, dtype=np.int32)
+    check(lib.mp_paged_attention_prefill(q_ptr, keys_ptr, values_ptr, layers, layer, block_tokens, max_blocks,
+                                         tables_ptr, table_stride, _ptr(st), _ptr(ct), len(st), out_ptr, stream))
 
 
 def gemm_f32(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, stream: int | None = None) -> None:
