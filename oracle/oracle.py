@@ -34,11 +34,19 @@ def build_oracle() -> None:
     subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
 
 
+DROPIN_TEST = os.path.join(HERE, "_ref", "cow_test_b200")
+
+
 def build_ref() -> bool:
-    """Compile _ref/libmpref.so when the reference sources are present."""
+    """Compile _ref/libmpref.so (the reference CPU engine) and, once the product
+    libraries exist, _ref/cow_test_b200 (the reference's cow_test.cpp on the B200
+    drop-in runner) when the reference sources are present."""
     if not os.path.isdir(REFERENCE):
         return os.path.exists(REF_SO)
-    subprocess.run(["make", "-s", "-j8", "-C", HERE, "ref", f"MINIPREFIX_REFERENCE={REFERENCE}"], check=True)
+    targets = ["ref"]
+    if os.path.exists(os.path.join(os.path.dirname(HERE), "tinyinfer_b200", "libmpb200_host.so")):
+        targets.append("dropin")
+    subprocess.run(["make", "-s", "-j8", "-C", HERE, *targets, f"MINIPREFIX_REFERENCE={REFERENCE}"], check=True)
     return True
 
 

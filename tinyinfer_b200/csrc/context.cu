@@ -512,8 +512,10 @@ struct HostTimer {
     }
 };
 
-// Polls `e` (yielding for the first 2 ms, then sleeping 20 us between polls)
-// until it completes or `timeout_ms` elapses.
+// Polls `e` until it completes or `timeout_ms` elapses. For the first 50 ms the
+// thread only yields between polls, so a forward's completion (a few ms) is seen
+// within microseconds; a sleep would stretch each poll to the kernel's timer
+// slack (tens of microseconds). Longer waits sleep 100 us between polls.
 void wait_event(cudaEvent_t e, int timeout_ms) {
     const auto start = std::chrono::steady_clock::now();
     for (;;) {
@@ -523,8 +525,8 @@ void wait_event(cudaEvent_t e, int timeout_ms) {
         const auto waited = std::chrono::steady_clock::now() - start;
         if (timeout_ms >= 0 && waited > std::chrono::milliseconds(timeout_ms))
             fail(MP_ERR_TIMEOUT, "device work did not complete within the timeout");
-        if (waited < std::chrono::milliseconds(2)) std::this_thread::yield();
-        else std::this_thread::sleep_for(std::chrono::microseconds(20));
+        if (waited < std::chrono::milliseconds(50)) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::microseconds(100));
     }
 }
 
