@@ -174,11 +174,13 @@ def greedy_stream(h, prompt, steps):
 
 
 @pytest.mark.gpu
-def test_batched_engine_streams_match_oracle(built):
+def test_batched_engine_streams_match_oracle(built, ref):
     """Requests sharing a prefix (reuse + COW of the partial shared page), chunked
     prefill and batched decode in one engine: every greedy stream equals the
-    oracle's, and the step's bookkeeping equals the reference engine replayed with
-    the GPU's tokens (when the reference library is present)."""
+    oracle's, and the run's bookkeeping equals the reference engine replayed with
+    the GPU's tokens (oracle/replay.py: events, step stats, KV stats, copy-on-write
+    counts and every live page table after each step)."""
+    from oracle.replay import Trace, replay
     from tinyinfer_b200.host import Engine, Runner
 
     cfg = ModelConfig(layers=2, intermediate=128, vocabulary=64, context=64, tied=True)
@@ -190,28 +192,39 @@ def test_batched_engine_streams_match_oracle(built):
         out, _ = o.append(keys, values, list(range(32)), 0, list(seq))
         return out
 
+    geom = dict(vocabulary=64, context=64, layers=cfg.layers, width=cfg.kv_width, block_tokens=4, max_blocks=256,
+                prefix_blocks=32, max_batch=6, token_budget=24, prefill_chunk=8)
     runner = Runner.b200(cfg, w, context=64, block_tokens=4, max_blocks=256, prefix_blocks=32, max_sequences=16,
                          max_step_tokens=128, max_step_sequences=16)
     engine = Engine(runner, 6, 24, 8, 64)
+    trace = Trace()
     rng = np.random.default_rng(4)
     shared = [int(t) for t in rng.integers(0, 64, 9)]  # 9 tokens: a partial shared page at block_tokens 4
     prompts = {"seed": shared + [1]}
     for i in range(5):
         prompts[f"f{i}"] = shared + [int(t) for t in rng.integers(0, 64, int(rng.integers(1, 6)))]
-    engine.submit("seed", prompts["seed"], 4)
-    while not engine.idle():
+    outputs = {}
+
+    def step():
         engine.step()
-    outputs = {"seed": [e[1] for e in engine.poll_events() if e[1] is not None]}
+        events = engine.poll_events()
+        live = [r for r in trace.ids if engine.sequence(r) is not None]
+        trace.step(engine, events=events, sequences=live)
+        for rid, tok, reason, err in events:
+            assert reason in (None, 1), err
+            if tok is not None:
+                outputs.setdefault(rid, []).append(tok)
+
+    engine.submit("seed", prompts["seed"], 4)
+    trace.submit("seed", prompts["seed"], 4)
+    while not engine.idle():
+        step()
     for k, p in prompts.items():
         if k != "seed":
             engine.submit(k, p, 5)
-    events = []
+            trace.submit(k, p, 5)
     while not engine.idle():
-        engine.step()
-        events += engine.poll_events()
-    for rid, tok, reason, err in events:
-        assert reason in (None, 1), err
-        outputs.setdefault(rid, []).append(tok)
+        step()
     for rid, p in prompts.items():
         seq = list(p)
         for t in outputs[rid]:
@@ -221,6 +234,8 @@ def test_batched_engine_streams_match_oracle(built):
     assert st["prefix_hits"] >= 5 and engine.cost_stats()["cow_pages"] >= 1
     engine.shutdown()
     assert engine.runner_stats()["kv_live_blocks"] == 0
+    counted = replay(trace, ref=ref, **geom)
+    assert counted["cow_pages"] >= 1 and counted["tables"] > 0
 
 
 @pytest.mark.gpu
