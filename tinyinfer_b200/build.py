@@ -24,6 +24,9 @@ HOST_LIB = os.path.join(HERE, "libmpb200_host.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", f"-I{CSRC}"]
+# Extra nvcc flags for tuning builds, e.g. MPB_NVCC_FLAGS="-DMPB_GEMM_CTAS_PER_SM=2" (the
+# compile-time switches are documented where they are defined); empty by default.
+COMMON += os.environ.get("MPB_NVCC_FLAGS", "").split()
 
 DEVICE_SOURCES = ["attention.cu", "attention_shared.cu", "attention_prefill.cu", "tc_gemm.cu", "fused_ops.cu", "context.cu", "operator.cu", "operator_noalloc.cu"]
 HOST_SOURCES = []  # filled in by host/ when present

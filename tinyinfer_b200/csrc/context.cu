@@ -415,7 +415,10 @@ size_t max_work(const mp_runtime_config& rt) { return size_t(rt.max_step_tokens)
 
 // Tile widths (B rows per CTA tile) of the wide projections: fewer re-reads of the
 // activations per output column block.
-constexpr int kGateUpBN = 128;  // 2 x intermediate is a multiple of 128 (intermediate % 64 == 0)
+#ifndef MPB_GATE_UP_BN
+#define MPB_GATE_UP_BN 128
+#endif
+constexpr int kGateUpBN = MPB_GATE_UP_BN;  // 2 x intermediate is a multiple of 128 (intermediate % 64 == 0)
 int head_tile_n(int vocabulary) { return vocabulary % 256 == 0 ? 256 : (vocabulary % 128 == 0 ? 128 : 64); }
 int gemm_tile_n(int n) {
     if (n >= 8192) return head_tile_n(n);

@@ -50,9 +50,16 @@ constexpr int kBK = 32;  // fp32 elements per K block = one 128-byte swizzle row
 constexpr int kThreads = 128;
 constexpr int kMaxSlices = 8;  // portable cluster size
 
+// Resident CTAs per SM the kernel is built for: 1 (deep stage rings) or 2 (two
+// 2-stage CTAs share an SM, so small-M GEMMs can spread over more K slices).
+#ifndef MPB_GEMM_CTAS_PER_SM
+#define MPB_GEMM_CTAS_PER_SM 1
+#endif
+constexpr int kCtasPerSm = MPB_GEMM_CTAS_PER_SM;
+
 template <int BN>
 struct TcConfig {
-    static constexpr int kStages = BN <= 64 ? 4 : (BN <= 128 ? 3 : 2);
+    static constexpr int kStages = kCtasPerSm == 2 ? 2 : (BN <= 64 ? 4 : (BN <= 128 ? 3 : 2));
     static constexpr int kATile = kBM * kBK * 4;  // bytes
     static constexpr int kBTile = BN * kBK * 4;
     static constexpr int kStage = 2 * kATile + 2 * kBTile;
@@ -66,8 +73,8 @@ struct TcConfig {
     // owner's rows of the residual (at most 64 rows when the K slices are 2 or
     // more) and the tile's RMSNorm weights, prefetched into shared memory by the
     // idle warps while the MMAs run (no room beside the wider tiles' rings)
-    static constexpr int kResidRows = BN == 64 ? kBM / 2 : 0;
-    static constexpr int kResidBytes = BN == 64 ? (kResidRows + 1) * BN * 4 : 0;
+    static constexpr int kResidRows = BN == 64 && kCtasPerSm == 1 ? kBM / 2 : 0;
+    static constexpr int kResidBytes = kResidRows ? (kResidRows + 1) * BN * 4 : 0;
 };
 template <int BN, Epilogue E>
 constexpr int dynamic_smem() { return TcConfig<BN>::kSmem + (E == Epilogue::AddTo ? TcConfig<BN>::kResidBytes : 0); }
@@ -358,7 +365,7 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
 }
 
 template <int BN, Epilogue E>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                    const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                    const TcGemmParams p) {
