@@ -187,14 +187,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_kernel(const Pr
             break;
         }
         tmem_fence_after();
+        // the TMEM load is warp-collective (.sync.aligned): every lane executes it,
+        // whatever its mask; only the fold below depends on the lane
+        float o[kT];
+        tmem_row64(tmem_o + lane_base, o);
         if (visible > 0) {
             // fold this sub-chunk into the running (max, sum, output)
             const float m_new = fmaxf(m_run, mx);
             const float a_old = exp2f(m_run - m_new), a_new = exp2f(mx - m_new);  // m_run = -inf: a_old = 0
             l_run = l_run * a_old + sum * a_new;
             m_run = m_new;
-            float o[kT];
-            tmem_row64(tmem_o + lane_base, o);
 #pragma unroll
             for (int d = 0; d < kHeadDim; ++d) o_run[d] = fmaf(o_run[d], a_old, o[d] * a_new);
         }

@@ -72,6 +72,8 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t tmem, uint32_t cols) {
 }
 
 // 32 consecutive columns of this warp's 32 TMEM lanes: thread = lane, r = columns.
+// Warp-collective (.sync.aligned): all 32 lanes must execute it convergently, never
+// under a lane-dependent condition.
 __device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
