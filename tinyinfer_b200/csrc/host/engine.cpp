@@ -3,6 +3,7 @@
 #include <algorithm>
 #include <cmath>
 #include <map>
+#include <set>
 
 namespace miniprefix_b200 {
 namespace {
@@ -17,9 +18,10 @@ SchedulerConfig scheduler_config(const EngineConfig& config) {
 
 Engine::Engine(std::unique_ptr<ModelRunner> runner, EngineConfig config)
     : runner_(std::move(runner)), config_(config), scheduler_(scheduler_config(config)) {
-    if (!runner_ || config.context < 1 || config.context > runner_->config().context ||
-        config.context > runner_->context_limit())
-        throw std::invalid_argument("invalid engine configuration");
+    // the engine's context may not exceed the model's or the runner's limit
+    const bool within = runner_ && config.context >= 1 && config.context <= runner_->config().context &&
+                        config.context <= runner_->context_limit();
+    if (!within) throw std::invalid_argument("invalid engine configuration");
 }
 
 Engine::~Engine() {
@@ -29,22 +31,36 @@ Engine::~Engine() {
     }
 }
 
+namespace {
+
+// The submit checks, in the order the reference applies them (engine.cpp:19-26).
+void validate_request(const Request& r, const std::set<RequestId>& seen, int context, int vocabulary) {
+    const auto& g = r.generation;
+    const std::uint64_t total = r.prompt_token_ids.size() + std::uint64_t(g.max_new_tokens);
+    const bool shape_ok = !r.id.empty() && !seen.count(r.id) && !r.prompt_token_ids.empty() &&
+                          g.max_new_tokens >= 1 && total <= std::uint64_t(context);
+    if (!shape_ok) throw std::invalid_argument("invalid request, duplicate ID or context overflow");
+    const auto outside = [vocabulary](TokenId t) { return t < 0 || t >= vocabulary; };
+    if (std::any_of(r.prompt_token_ids.begin(), r.prompt_token_ids.end(), outside))
+        throw std::invalid_argument("invalid prompt token");
+    if (g.eos_token_id && outside(*g.eos_token_id)) throw std::invalid_argument("invalid EOS");
+}
+
+template <class Container>
+void drop_finished(Container& states) {
+    states.erase(std::remove_if(states.begin(), states.end(), [](const auto& s) { return s.finished; }),
+                 states.end());
+}
+
+}  // namespace
+
 void Engine::submit(Request request) {
     if (failed_) throw std::runtime_error("engine failed; create a new engine");
-    if (request.id.empty() || seen_.count(request.id) || request.prompt_token_ids.empty() ||
-        request.generation.max_new_tokens < 1 ||
-        request.prompt_token_ids.size() + std::uint64_t(request.generation.max_new_tokens) >
-            std::uint64_t(config_.context))
-        throw std::invalid_argument("invalid request, duplicate ID or context overflow");
-    for (auto t : request.prompt_token_ids)
-        if (t < 0 || t >= runner_->config().vocabulary) throw std::invalid_argument("invalid prompt token");
-    if (request.generation.eos_token_id &&
-        (*request.generation.eos_token_id < 0 || *request.generation.eos_token_id >= runner_->config().vocabulary))
-        throw std::invalid_argument("invalid EOS");
+    validate_request(request, seen_, config_.context, runner_->config().vocabulary);
+    seen_.insert(request.id);
     State state;
     state.request = std::move(request);
     waiting_.push_back(std::move(state));
-    seen_.insert(waiting_.back().request.id);
 }
 
 void Engine::finish_host(State& state, TerminalCleanup cleanup) {
@@ -57,33 +73,32 @@ void Engine::finish_host(State& state, TerminalCleanup cleanup) {
 void Engine::terminal(State& state, FinishReason reason, std::optional<TokenId> token, const std::string& error,
                       TerminalCleanup cleanup) {
     if (state.finished) return;
-    // Completion and cancellation release the lease first; a fatal failure leaves
-    // cleanup to the runner (engine.cpp:63-70).
-    if (state.resident && cleanup == TerminalCleanup::ReleaseSequence) runner_->release(state.request.id);
-    runner_->release_reservation(state.request.id);
-    state.resident = false;
+    // Completion and cancellation give the pages back before the event; a fatal
+    // failure leaves the cleanup to the runner (the reference's order,
+    // engine.cpp:63-70).
+    finish_host(state, cleanup);
     events_.push_back({state.request.id, token, reason, error});
-    state.finished = true;
 }
 
 void Engine::remove_finished(bool include_waiting) {
-    const auto finished = [](const State& s) { return s.finished; };
-    active_.erase(std::remove_if(active_.begin(), active_.end(), finished), active_.end());
-    if (include_waiting) waiting_.erase(std::remove_if(waiting_.begin(), waiting_.end(), finished), waiting_.end());
+    drop_finished(active_);
+    if (include_waiting) drop_finished(waiting_);
 }
 
 void Engine::restore_prefix(State& state) {
-    auto& request = state.request;
-    runner_->create(request.id);
+    const auto& id = state.request.id;
+    const auto& prompt = state.request.prompt_token_ids;
+    runner_->create(id);
     state.resident = true;
-    const auto reused = runner_->reuse_prefix(request.id, request.prompt_token_ids);
-    // At least one prompt token must remain for the logits (engine.cpp:44-55).
-    const auto block_tokens = runner_->kv_block_tokens();
-    if (reused >= request.prompt_token_ids.size() || (reused && !block_tokens))
-        throw std::runtime_error("invalid reusable prefix range");
-    state.kv_block_tokens = block_tokens;
-    state.prefilled = reused;
-    step_stats_.prefix_reused_tokens += reused;
+    const std::size_t cached = runner_->reuse_prefix(id, prompt);
+    // A reused prefix must leave at least one prompt token to compute logits from,
+    // and needs a paged runner (engine.cpp:44-55).
+    const std::size_t page = runner_->kv_block_tokens();
+    const bool usable = cached < prompt.size() && (cached == 0 || page != 0);
+    if (!usable) throw std::runtime_error("invalid reusable prefix range");
+    state.kv_block_tokens = page;
+    state.prefilled = cached;
+    step_stats_.prefix_reused_tokens += cached;
 }
 
 void Engine::resolve(std::vector<Outcome>& outcomes, std::size_t& resolved, const std::vector<SchedulePhase>& phases,

@@ -4,10 +4,20 @@
 
 namespace miniprefix_b200 {
 
+namespace {
+// Pages a request of `tokens` tokens may hold: its last token's page index + 1.
+std::size_t pages_for(std::size_t tokens, int block_tokens) { return (tokens - 1) / std::size_t(block_tokens) + 1; }
+// Whether `pages` more fit beside `committed` of `total` (never underflows).
+bool fits(std::size_t committed, std::size_t pages, std::size_t total) {
+    return committed <= total && pages <= total - committed;
+}
+}  // namespace
+
 KVManager::KVManager(KvCacheConfig config, int layers, int width, int context, int vocabulary)
     : layers_(layers), width_(width), context_(context), vocabulary_(vocabulary), pool_(config, layers, width),
       prefix_(pool_) {
-    if (context < 1 || vocabulary < 1) throw std::invalid_argument("invalid KV manager context/vocabulary");
+    const bool usable = context >= 1 && vocabulary >= 1;
+    if (!usable) throw std::invalid_argument("invalid KV manager context/vocabulary");
 }
 
 KVManager::~KVManager() {
@@ -34,8 +44,8 @@ KVManager::State& KVManager::idle_state(const RequestId& id) {
 }
 
 void KVManager::validate_tokens(const std::vector<TokenId>& tokens) const {
-    for (auto t : tokens)
-        if (t < 0 || t >= vocabulary_) throw std::invalid_argument("invalid token");
+    const auto outside = [this](TokenId t) { return t < 0 || t >= vocabulary_; };
+    if (std::any_of(tokens.begin(), tokens.end(), outside)) throw std::invalid_argument("invalid token");
 }
 
 // Pages held logically: every reservation, plus the pages of sequences that
@@ -82,16 +92,18 @@ void KVManager::touch_reservation(const RequestId& id) {
 KvAdmission KVManager::reserve_request(const RequestId& id, std::size_t max_tokens) {
     settle_publishes();
     require_idle();
-    if (contains(id) || reservations_.count(id)) throw std::invalid_argument("duplicate KV reservation");
-    if (!max_tokens || max_tokens > std::size_t(context_)) throw std::invalid_argument("invalid KV reservation context");
-    const std::size_t pages = 1 + (max_tokens - 1) / std::size_t(config().block_tokens);
-    const std::size_t total = std::size_t(config().max_blocks);
-    if (pages > total) return KvAdmission::Impossible;
-    const std::size_t committed = committed_blocks();
-    if (committed > total || pages > total - committed) return KvAdmission::Wait;
+    const bool known = contains(id) || reservations_.count(id) != 0;
+    if (known) throw std::invalid_argument("duplicate KV reservation");
+    const bool in_context = max_tokens >= 1 && max_tokens <= std::size_t(context_);
+    if (!in_context) throw std::invalid_argument("invalid KV reservation context");
+    // no discount for pages another sequence already shares (kv_manager.cpp:46-51)
+    const std::size_t need = pages_for(max_tokens, config().block_tokens);
+    const std::size_t pool = std::size_t(config().max_blocks);
+    if (need > pool) return KvAdmission::Impossible;
+    if (!fits(committed_blocks(), need, pool)) return KvAdmission::Wait;
     touch_reservation(id);
-    reservations_.emplace(id, pages);
-    reserved_pages_ += pages;
+    reservations_[id] = need;
+    reserved_pages_ += need;
     return KvAdmission::Ready;
 }
 
@@ -117,22 +129,22 @@ void KVManager::create(const RequestId& id) {
 void KVManager::fork_sequence(const RequestId& source, const RequestId& target) {
     settle_publishes();
     require_idle();
-    const auto& original = sequences_.at(source).sequence;
-    auto& destination = idle_state(target).sequence;
-    if (source == target || destination.used || !destination.blocks.empty() || !destination.tokens.empty())
-        throw std::invalid_argument("fork requires a distinct empty target");
-    const auto reservation = reservations_.find(target);
-    if (reservation != reservations_.end()) {
-        if (original.blocks.size() > reservation->second) throw KvCapacityError("fork exceeds KV reservation");
-    } else {
-        const std::size_t used = committed_blocks(), total = std::size_t(config().max_blocks);
-        if (used > total || original.blocks.size() > total - used)
-            throw KvCapacityError("fork exceeds unreserved KV capacity");
+    const PagedSequence& from = sequences_.at(source).sequence;
+    PagedSequence& into = idle_state(target).sequence;
+    const bool empty_target = into.used == 0 && into.blocks.empty() && into.tokens.empty();
+    if (source == target || !empty_target) throw std::invalid_argument("fork requires a distinct empty target");
+    // The target takes every page of the source: within its reservation if it has
+    // one, else within the pool's unreserved capacity.
+    const std::size_t pages = from.blocks.size();
+    if (const auto r = reservations_.find(target); r != reservations_.end()) {
+        if (pages > r->second) throw KvCapacityError("fork exceeds KV reservation");
+    } else if (!fits(committed_blocks(), pages, std::size_t(config().max_blocks))) {
+        throw KvCapacityError("fork exceeds unreserved KV capacity");
     }
-    PagedSequence copy = original;  // host metadata first, then leases
+    PagedSequence shared = from;  // the host metadata is copied before any lease is taken
     touch_sequence(target);
-    for (int block : copy.blocks) pool_.retain(block);
-    destination = std::move(copy);
+    for (const int block : shared.blocks) pool_.retain(block);
+    into = std::move(shared);
 }
 
 std::size_t KVManager::reuse_prefix(const RequestId& id, const std::vector<TokenId>& prompt) {
