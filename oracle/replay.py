@@ -100,6 +100,7 @@ def replay(trace: Trace, *, vocabulary, context, layers, width, block_tokens, ma
                                        prefix_blocks)
     engine = RefEngine(runner, max_batch, token_budget, prefill_chunk, context)
     counted = {"steps": 0, "events": 0, "stats_checks": 0, "tables": 0}
+    ref_cow = [0, 0]  # copy-on-write regions and bytes so far (each read of the regions drains them)
     try:
         for n, op in enumerate(trace.ops):
             if op[0] == "submit":
@@ -139,11 +140,12 @@ def replay(trace: Trace, *, vocabulary, context, layers, width, block_tokens, ma
                         raise Mismatch(f"op {n}: {k} {cs[k]} (reference) vs {s.costs[k]} (product)")
                 if cow:
                     regions = engine.regions()
-                    cow_bytes = sum(2 * r[3] * r[4] * 4 for r in regions)  # K and V pools, width x rows floats
-                    if (len(regions), cow_bytes) != (s.costs["cow_pages"], s.costs["cow_bytes"]):
-                        raise Mismatch(f"op {n}: copy-on-write pages / bytes {len(regions)} / {cow_bytes} (reference "
+                    ref_cow[0] += len(regions)
+                    ref_cow[1] += sum(2 * r[3] * r[4] * 4 for r in regions)  # K and V pools, width x rows floats
+                    if tuple(ref_cow) != (s.costs["cow_pages"], s.costs["cow_bytes"]):
+                        raise Mismatch(f"op {n}: copy-on-write pages / bytes {ref_cow[0]} / {ref_cow[1]} (reference "
                                        f"regions) vs {s.costs['cow_pages']} / {s.costs['cow_bytes']} (product)")
-                    counted["cow_pages"] = len(regions)
+                    counted["cow_pages"] = ref_cow[0]
                 counted["stats_checks"] += 1
             if s.sequences is not None:
                 for rid, seq in s.sequences.items():

@@ -137,11 +137,15 @@ def test_copy_on_write_counts_compare_with_reference_regions(built, ref):
     engine = Engine(runner, g["max_batch"], g["token_budget"], g["prefill_chunk"], g["context"])
     trace = Trace()
     shared = [int(t) for t in rng.integers(0, 16, 9)]  # a partial shared page at 4 tokens per page
+    cow = [0, 0]  # the product runner's regions so far (each read drains them)
+
     def step():
         engine.step()
         trace.step(engine, events=engine.poll_events())
         regions = runner.regions()
-        trace.ops[-1][1].costs.update(cow_pages=len(regions), cow_bytes=sum(2 * r[3] * r[4] * 4 for r in regions))
+        cow[0] += len(regions)
+        cow[1] += sum(2 * r[3] * r[4] * 4 for r in regions)
+        trace.ops[-1][1].costs.update(cow_pages=cow[0], cow_bytes=cow[1])
 
     for i in range(6):
         rid = f"c{i}"
