@@ -69,15 +69,9 @@ struct TcConfig {
     static constexpr int kRing = kStages * kStage > kRecvBytes ? kStages * kStage : kRecvBytes;
     static constexpr int kSmem = kRing + 1024 /*align*/ + 256 /*barriers*/;
     static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-    // AddTo under split-K with 64-wide tiles (the forward's O and down GEMMs): the
-    // owner's rows of the residual (at most 64 rows when the K slices are 2 or
-    // more) and the tile's RMSNorm weights, prefetched into shared memory by the
-    // idle warps while the MMAs run (no room beside the wider tiles' rings)
-    static constexpr int kResidRows = BN == 64 && kCtasPerSm == 1 ? kBM / 2 : 0;
-    static constexpr int kResidBytes = kResidRows ? (kResidRows + 1) * BN * 4 : 0;
 };
 template <int BN, Epilogue E>
-constexpr int dynamic_smem() { return TcConfig<BN>::kSmem + (E == Epilogue::AddTo ? TcConfig<BN>::kResidBytes : 0); }
+constexpr int dynamic_smem() { return TcConfig<BN>::kSmem; }
 
 // Rows [slice_row0(r), slice_row0(r + 1)) of a tile are reduced and stored by
 // cluster rank r; row_owner is the inverse.
@@ -205,8 +199,7 @@ __device__ __forceinline__ void epilogue_rows_prepare(const TcGemmParams& p, con
 
 template <int BN, Epilogue E>
 __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float* recv, int slice_floats,
-                                              const RowInputs& in, int m0, int n0, int r0, int r1, int slices,
-                                              const float* resid_s) {
+                                              const RowInputs& in, int m0, int n0, int r0, int r1, int slices) {
     using Cfg = TcConfig<BN>;
     constexpr bool kSwiGLU = E == Epilogue::SwiGLU;
     constexpr bool kRope = E == Epilogue::Rope;
@@ -247,13 +240,8 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
             } else if (!kSwiGLU) {
                 dst[u] = reinterpret_cast<float4*>(p.c + size_t(m0 + r0 + lr) * p.ldc + n0 + 4 * it);
                 if (E == Epilogue::AddTo && live[u]) {
-                    if (resid_s) {  // prefetched while the MMAs ran
-                        resid[u] = reinterpret_cast<const float4*>(resid_s)[lr * (BN / 4) + it];
-                        if (produce) wn[u] = reinterpret_cast<const float4*>(resid_s + Cfg::kResidRows * BN)[it];
-                    } else {
-                        resid[u] = *dst[u];
-                        if (produce) wn[u] = *reinterpret_cast<const float4*>(p.norm_w + n0 + 4 * it);
-                    }
+                    resid[u] = *dst[u];
+                    if (produce) wn[u] = *reinterpret_cast<const float4*>(p.norm_w + n0 + 4 * it);
                 }
             }
         }
@@ -393,10 +381,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     __shared__ float* row_dst[kBM];
     __shared__ int row_pos[kBM];
     const RowInputs rows{row_scale, row_dst, row_pos};
-    // AddTo under split-K: residual rows prefetched here (see TcConfig::kResidBytes)
-    float* resid_s = E == Epilogue::AddTo && splits > 1 && r1 - r0 <= Cfg::kResidRows
-                         ? reinterpret_cast<float*>(smem + Cfg::kRing + 256)
-                         : nullptr;
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
@@ -479,20 +463,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     } else if (warp >= 2) {
         // idle until the accumulator is ready: gather the epilogue's row inputs
         epilogue_rows_prepare<BN, E>(p, rows, m0, n0, r0, r1, int(threadIdx.x) - 64, kThreads - 64);
-        if (resid_s) {
-            // the owner's residual rows and the norm weights (written by earlier
-            // kernels: readable after the programmatic-launch wait above)
-            const int t = int(threadIdx.x) - 64;
-            float4* rs = reinterpret_cast<float4*>(resid_s);
-            for (int i = t; i < (r1 - r0) * (BN / 4); i += kThreads - 64) {
-                const int lr = i / (BN / 4), it = i % (BN / 4);
-                if (m0 + r0 + lr < p.m)
-                    rs[i] = *reinterpret_cast<const float4*>(p.c + size_t(m0 + r0 + lr) * p.ldc + n0 + 4 * it);
-            }
-            if (p.norm_w)
-                for (int i = t; i < BN / 4; i += kThreads - 64)
-                    rs[Cfg::kResidRows * (BN / 4) + i] = *reinterpret_cast<const float4*>(p.norm_w + n0 + 4 * i);
-        }
     }
     __syncwarp();
     // Epilogue. The outcome is made CTA-uniform before anything that holds a barrier.
@@ -540,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(uint32_t(Cfg::kTmemCols))
                      : "memory");
     }
-    if (ok) epilogue_rows<BN, E>(p, recv, slice_floats, rows, m0, n0, r0, r1, splits, resid_s);
+    if (ok) epilogue_rows<BN, E>(p, recv, slice_floats, rows, m0, n0, r0, r1, splits);
 }
 
 // Clusters of each size (index = slices) that the device holds at once, per tile
