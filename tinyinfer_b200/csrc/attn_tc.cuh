@@ -23,7 +23,7 @@ constexpr int kKTile = kT * 32 * 4;     // one K block of a 64-row tile (8 KB)
 // shared memory layout (1024-aligned tiles): Q hi / lo and P hi / lo (2 K blocks
 // each), K hi / lo and V^T hi / lo (2 K blocks each), the raw K and V staging
 // rows ([64 tokens][64 floats]), the physical blocks of the staged tokens, then
-// the MMA barrier, the TMEM address and a failure flag
+// the MMA barriers, the TMEM address and a failure flag
 constexpr int kOffQhi = 0, kOffQlo = 2 * kQTile;
 constexpr int kOffPhi = 4 * kQTile, kOffPlo = 6 * kQTile;
 constexpr int kOffKhi = 8 * kQTile, kOffKlo = kOffKhi + 2 * kKTile;
@@ -31,7 +31,7 @@ constexpr int kOffVhi = kOffKlo + 2 * kKTile, kOffVlo = kOffVhi + 2 * kKTile;
 constexpr int kOffRawK = kOffVlo + 2 * kKTile, kOffRawV = kOffRawK + kT * kHeadDim * 4;
 constexpr int kOffBlk = kOffRawV + kT * kHeadDim * 4;
 constexpr int kOffBar = kOffBlk + kT * 4;
-constexpr size_t kSmem = size_t(kOffBar) + 64 + 1024 /*alignment slack*/;
+constexpr size_t kSmem = size_t(kOffBar) + 64 + 1024 /*alignment slack*/;  // barriers etc. in the 64 bytes
 static_assert(kSmem <= 232448, "shared memory of a tensor-core attention CTA");
 constexpr uint32_t kTmemCols = 128;  // S: columns 0..63, O: 64..127
 
@@ -102,17 +102,22 @@ __device__ __forceinline__ void gather_raw(const float* keys, const float* value
     cp_async_commit();
 }
 
-// Splits the staged rows into the hi / lo K tiles (token-major) and V^T tiles
-// (dim-major); tokens at or past n_valid become zero.
-__device__ __forceinline__ void split_kv(const float* raw_k, const float* raw_v, int n_valid, unsigned char* khi,
-                                         unsigned char* klo, unsigned char* vhi, unsigned char* vlo, int tid,
-                                         int threads) {
+// Splits the staged K rows into the hi / lo K tiles (token-major); tokens at or
+// past n_valid become zero.
+__device__ __forceinline__ void split_k(const float* raw_k, int n_valid, unsigned char* khi, unsigned char* klo,
+                                        int tid, int threads) {
     for (int i = tid; i < kT * 16; i += threads) {
         const int t = i >> 4, c4 = i & 15;
         const float4 kv = t < n_valid ? *reinterpret_cast<const float4*>(raw_k + t * kHeadDim + c4 * 4)
                                       : make_float4(0.f, 0.f, 0.f, 0.f);
         store_split4(khi + (c4 >> 3) * kKTile, klo + (c4 >> 3) * kKTile, sw128_offset(t, c4 & 7), kv);
     }
+}
+
+// Splits the staged V rows into the hi / lo V^T tiles (dim-major); tokens at or
+// past n_valid become zero.
+__device__ __forceinline__ void split_v(const float* raw_v, int n_valid, unsigned char* vhi, unsigned char* vlo,
+                                        int tid, int threads) {
     for (int i = tid; i < kT * 16; i += threads) {
         const int t = i & (kT - 1), c4 = i / kT;  // consecutive threads: consecutive tokens
         const float4 vv = t < n_valid ? *reinterpret_cast<const float4*>(raw_v + t * kHeadDim + ((c4 ^ (t & 15)) * 4))
@@ -128,6 +133,13 @@ __device__ __forceinline__ void split_kv(const float* raw_k, const float* raw_v,
             *reinterpret_cast<float*>(vlo + (t >> 5) * kKTile + off) = l;
         }
     }
+}
+
+__device__ __forceinline__ void split_kv(const float* raw_k, const float* raw_v, int n_valid, unsigned char* khi,
+                                         unsigned char* klo, unsigned char* vhi, unsigned char* vlo, int tid,
+                                         int threads) {
+    split_k(raw_k, n_valid, khi, klo, tid, threads);
+    split_v(raw_v, n_valid, vhi, vlo, tid, threads);
 }
 
 // The 64 fp32 columns [col, col + 64) of this thread's TMEM lane.
