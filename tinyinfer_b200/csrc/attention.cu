@@ -54,6 +54,13 @@ constexpr int kStageTokens = MPB_ATTN_STAGE_TOKENS;  // a multiple of 8
 constexpr int kStages = MPB_ATTN_STAGES;
 constexpr int kPasses = kStageTokens / 8;            // 8 tokens per consumer pass
 static_assert(kStageTokens % 8 == 0 && kPasses >= 1, "stage = whole consumer passes");
+// Query of a consumer's current row: in registers (48 per lane), or, with
+// MPB_ATTN_Q_SMEM, in a per-warp shared-memory slot read once per pass (frees the
+// registers for more resident CTAs per SM).
+#ifndef MPB_ATTN_Q_SMEM
+#define MPB_ATTN_Q_SMEM 0
+#endif
+constexpr bool kQInSmem = MPB_ATTN_Q_SMEM != 0;
 constexpr int kConsumers = kKvHeads;                   // 3 consumer warps
 constexpr int kThreads = (kConsumers + 1) * 32;        // + producer warp
 constexpr int kStageFloats = kStageTokens * kKvWidth;  // per pool
@@ -70,6 +77,7 @@ constexpr int kFirst = 1, kLast = 2;
 
 constexpr size_t kAttnSmem = size_t(kStages) * 2 * kStageFloats * sizeof(float) +         // K/V stages
                              size_t(kConsumers) * kGroup * kStageTokens * sizeof(float) +  // probabilities
+                             size_t(kConsumers) * kGroup * kHeadDim * sizeof(float) +      // queries
                              kStages * sizeof(StageDesc) + 2 * kStages * sizeof(uint64_t) + 16;
 
 // Output element: plain FP32, or TF32 hi/lo halves when the caller asked for them.
@@ -196,7 +204,7 @@ __device__ void producer(const AttnParams& p, float* stages, StageDesc* desc, ui
 }
 
 __device__ void consumer(const AttnParams& p, const float* stages, const StageDesc* desc, uint64_t* full,
-                         uint64_t* empty, float* probs, unsigned* failed, int kh, int lane) {
+                         uint64_t* empty, float* probs, float* qs, unsigned* failed, int kh, int lane) {
     const int t = lane >> 2, c = lane & 3;
     float4 qr[kGroup][4];
     // softmax state of head c (lanes with c == 3 carry an unused copy)
@@ -218,11 +226,19 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
         if (d.work < 0) return;
         if (d.flags & kFirst) {
             const float* qrow = p.q + size_t(d.row) * p.q_stride + kh * kGroup * kHeadDim;
+            if constexpr (kQInSmem) {
+                // the row's 3 x 64 query values into this warp's slot (48 float4)
+                for (int i = lane; i < kGroup * kHeadDim / 4; i += 32)
+                    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(qrow)[i];
+                __syncwarp();
+            }
 #pragma unroll
             for (int hh = 0; hh < kGroup; ++hh) {
+                if constexpr (!kQInSmem) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    qr[hh][j] = *reinterpret_cast<const float4*>(qrow + hh * kHeadDim + c * 16 + 4 * ((j + t) & 3));
+                    for (int j = 0; j < 4; ++j)
+                        qr[hh][j] = *reinterpret_cast<const float4*>(qrow + hh * kHeadDim + c * 16 + 4 * ((j + t) & 3));
+                }
                 acc[hh][0] = acc[hh][1] = 0.f;
             }
             m_run = -INFINITY;
@@ -243,8 +259,11 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
                 const float4 kv = *reinterpret_cast<const float4*>(krow + 4 * ((j + t) & 3));
 #pragma unroll
                 for (int hh = 0; hh < kGroup; ++hh) {
-                    fma2(pe[hh], po[hh], qr[hh][j].x, qr[hh][j].y, kv.x, kv.y);
-                    fma2(pe[hh], po[hh], qr[hh][j].z, qr[hh][j].w, kv.z, kv.w);
+                    const float4 qv = kQInSmem ? *reinterpret_cast<const float4*>(qs + hh * kHeadDim + c * 16 +
+                                                                                  4 * ((j + t) & 3))
+                                               : qr[hh][j];
+                    fma2(pe[hh], po[hh], qv.x, qv.y, kv.x, kv.y);
+                    fma2(pe[hh], po[hh], qv.z, qv.w, kv.z, kv.w);
                 }
             }
 #pragma unroll
@@ -429,7 +448,8 @@ __global__ void __launch_bounds__(kThreads, kAttnCtasPerSm) paged_attention_kern
     extern __shared__ __align__(128) unsigned char smem_raw[];
     float* stages = reinterpret_cast<float*>(smem_raw);
     float* probs = stages + 2 * kStages * kStageFloats;  // [3 consumers][3][16]
-    StageDesc* desc = reinterpret_cast<StageDesc*>(probs + kConsumers * kGroup * kStageTokens);
+    float* qsm = probs + kConsumers * kGroup * kStageTokens;  // [3 consumers][3][64] (kQInSmem)
+    StageDesc* desc = reinterpret_cast<StageDesc*>(qsm + kConsumers * kGroup * kHeadDim);
     uint64_t* full = reinterpret_cast<uint64_t*>(desc + kStages);
     uint64_t* empty = full + kStages;
     unsigned* failed = reinterpret_cast<unsigned*>(empty + kStages);
@@ -448,7 +468,8 @@ __global__ void __launch_bounds__(kThreads, kAttnCtasPerSm) paged_attention_kern
     if (warp == kConsumers)
         producer(p, stages, desc, full, empty, persistent, failed, lane);
     else
-        consumer(p, stages, desc, full, empty, probs + warp * kGroup * kStageTokens, failed, warp, lane);
+        consumer(p, stages, desc, full, empty, probs + warp * kGroup * kStageTokens, qsm + warp * kGroup * kHeadDim,
+                 failed, warp, lane);
     __syncthreads();
     if (tid == 0 && *failed) raise_error(p.error, kErrTimeout);
     if (persistent && tid == 0 && atomicAdd(&p.sched[1], 1u) == gridDim.x - 1) {
