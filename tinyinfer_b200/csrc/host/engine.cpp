@@ -248,8 +248,9 @@ bool Engine::step() {
                 if (!s.resident) restore_prefix(s);
                 const bool prefilling = work.phase == SchedulePhase::Prefill;
                 const auto count = plan.take_input(work.phase, r.prompt_token_ids.size() - s.prefilled);
-                std::vector<TokenId> input;
-                if (!prefilling) input = {s.output.back()};
+                // one reused buffer: a decode append allocates nothing here
+                std::vector<TokenId>& input = input_;
+                if (!prefilling) input.assign(1, s.output.back());
                 else
                     input.assign(r.prompt_token_ids.begin() + std::ptrdiff_t(s.prefilled),
                                  r.prompt_token_ids.begin() + std::ptrdiff_t(s.prefilled + count));

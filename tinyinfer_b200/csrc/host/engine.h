@@ -79,6 +79,7 @@ private:
     std::vector<State> active_;
     std::set<RequestId> seen_;
     std::vector<GenerationEvent> events_;
+    std::vector<TokenId> input_;  // the input tokens of the append being staged
     bool failed_ = false;
     bool step_failed_ = false;  // a failed append of this step was replayed and rethrown
     EngineStepStats step_stats_;

@@ -257,7 +257,8 @@ int mph_kv_append(mph_kv* m, const char* id, const int32_t* tokens, int32_t coun
                   size_t* region) {
     return int(guarded([&] {
         tail[0] = tail[1] = tail[2] = -1;
-        auto tx = m->kv.prepare_append(id, tokens_of(tokens, count));
+        const auto input = tokens_of(tokens, count);  // outlives the transaction
+        auto tx = m->kv.prepare_append(id, input);
         if (tx.tail_copy()) {
             tail[0] = tx.tail_copy()->source;
             tail[1] = tx.tail_copy()->destination;

@@ -59,26 +59,42 @@ std::size_t KVManager::committed_blocks() const {
 
 void KVManager::touch_sequence(const RequestId& id, bool dropping) {
     if (!checkpoint_) return;
-    auto found = checkpoint_->sequences.find(id);
-    if (found == checkpoint_->sequences.end()) {
+    auto& cp = *checkpoint_;
+    auto it = sequences_.find(id);
+    State* state = it != sequences_.end() ? &it->second : nullptr;
+    std::size_t slot;
+    if (state && state->saved_window == cp.window) {
+        slot = state->saved_slot;
+    } else if (const auto known = cp.stateless.find(id); known != cp.stateless.end()) {
+        slot = known->second;
+    } else {
         SavedSequence saved;
-        auto it = sequences_.find(id);
-        if (it != sequences_.end()) {
-            const auto& s = it->second.sequence;
+        if (state) {
+            const auto& s = state->sequence;
             saved.existed = true;
             saved.used = s.used;
             saved.block_count = s.blocks.size();
             saved.last_block = s.blocks.empty() ? -1 : s.blocks.back();
             saved.token_count = s.tokens.size();
         }
-        found = checkpoint_->sequences.emplace(id, std::move(saved)).first;
+        slot = cp.sequences.size();
+        cp.sequences.emplace_back(id, std::move(saved));
+        if (!state) cp.stateless.emplace(id, slot);
     }
-    auto& saved = found->second;
-    if (dropping && saved.existed && !saved.tokens) {
-        const auto& s = sequences_.at(id).sequence;
-        saved.tokens.emplace(s.tokens.begin(), s.tokens.begin() + std::ptrdiff_t(std::min(saved.token_count, s.tokens.size())));
-        saved.blocks.emplace(s.blocks.begin(), s.blocks.begin() + std::ptrdiff_t(saved.block_count));
-        if (saved.block_count) saved.blocks->back() = saved.last_block;
+    if (state) {
+        state->saved_window = cp.window;
+        state->saved_slot = slot;
+    }
+    auto& saved = cp.sequences[slot].second;
+    if (dropping) {
+        // the State may be erased next: keep the entry reachable by id
+        cp.stateless.emplace(id, slot);
+        if (saved.existed && !saved.tokens) {
+            const auto& s = sequences_.at(id).sequence;
+            saved.tokens.emplace(s.tokens.begin(), s.tokens.begin() + std::ptrdiff_t(std::min(saved.token_count, s.tokens.size())));
+            saved.blocks.emplace(s.blocks.begin(), s.blocks.begin() + std::ptrdiff_t(saved.block_count));
+            if (saved.block_count) saved.blocks->back() = saved.last_block;
+        }
     }
 }
 
@@ -251,7 +267,7 @@ void KVManager::reserve_pages(const RequestId& id, PagedSequence& sequence, int 
 }
 
 KVManager::Append::Append(KVManager& owner, const RequestId& id, const std::vector<TokenId>& tokens)
-    : owner_(&owner), id_(id), state_(&owner.idle_state(id)), tokens_(tokens),
+    : owner_(&owner), id_(id), state_(&owner.idle_state(id)), tokens_(&tokens),
       original_blocks_(state_->sequence.blocks.size()) {
     auto& sequence = state_->sequence;
     if (!owner.pending_publishes_.empty() && !owner.commutes_with_publishes(*state_, tokens.size()))
@@ -306,9 +322,9 @@ void KVManager::Append::commit() {
     if (!owner_) throw std::logic_error("KV append already finished");
     if (copy_ && !copied_) throw std::logic_error("shared tail payload was not copied");
     auto& sequence = state_->sequence;
-    sequence.tokens.insert(sequence.tokens.end(), tokens_.begin(), tokens_.end());
-    sequence.used += int(tokens_.size());
-    owner_->forward_tokens_ += tokens_.size();
+    sequence.tokens.insert(sequence.tokens.end(), tokens_->begin(), tokens_->end());
+    sequence.used += int(tokens_->size());
+    owner_->forward_tokens_ += tokens_->size();
     if (copy_) owner_->pool_.unref(copy_->source);
     state_->appending = false;
     owner_->append_active_ = false;
@@ -393,6 +409,7 @@ void KVManager::begin_checkpoint() {
     settle_publishes();
     require_idle();
     checkpoint_ = std::make_unique<Checkpoint>();
+    checkpoint_->window = ++windows_;
     checkpoint_->live = pool_.live_blocks();
     checkpoint_->peak = pool_.peak_blocks();
     prefix_.begin_journal();

@@ -38,6 +38,10 @@ class KVManager {
         PagedSequence sequence;
         bool appending = false;
         bool publish_queued = false;  // in pending_publishes_
+        // journal entry of this sequence in the open checkpoint window (valid while
+        // saved_window equals the window's number)
+        std::uint64_t saved_window = 0;
+        std::size_t saved_slot = 0;
     };
 
 public:
@@ -54,7 +58,7 @@ public:
         KVManager* owner_;
         RequestId id_;
         State* state_;
-        std::vector<TokenId> tokens_;
+        const std::vector<TokenId>* tokens_;  // the caller's tokens; they outlive the transaction
         std::size_t original_blocks_;
         std::optional<TailCopy> copy_;
         bool copied_ = false;
@@ -159,14 +163,20 @@ private:
         std::optional<std::vector<std::int32_t>> tokens;
     };
     struct Checkpoint {
+        std::uint64_t window = 0;  // number of this checkpoint window
         std::vector<KvBlockPool::JournalEntry> pool_journal;
         std::size_t live = 0, peak = 0;
-        std::unordered_map<RequestId, SavedSequence> sequences;
+        // every sequence touched in the window, once, in first-touch order; a
+        // sequence's entry is found through its State (saved_window / saved_slot)
+        // or, while it has no State (created or dropped in the window), by id
+        std::vector<std::pair<RequestId, SavedSequence>> sequences;
+        std::unordered_map<RequestId, std::size_t> stateless;
         std::map<RequestId, std::optional<std::size_t>> reservations;  // nullopt: did not exist
         std::size_t reserved_pages = 0, forward_tokens = 0;
         CostStats costs;
     };
     std::unique_ptr<Checkpoint> checkpoint_;
+    std::uint64_t windows_ = 0;  // checkpoint windows opened so far
 };
 
 }  // namespace miniprefix_b200
