@@ -75,10 +75,23 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def fp16_peak():
+    """Dense 16-bit tensor-core throughput of this pool's B200s (the GEMMs' MMA kind,
+    kind::f16; FP16 runs at the BF16 rate): MEASURED_PEAKS.json's bf16 burst figure
+    (cuBLAS 8192^3, best of 10), the denominator of the GEMM roofline."""
+    try:
+        with open(PEAKS) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def tf32_peak(device_index):
     """Dense TF32 tensor-core throughput of this GPU, measured here: torch.matmul
     (cuBLAS) on 8192^3 FP32 operands with TF32 enabled, best of 10 launches timed
-    with CUDA events (2 N^3 FLOP each). The denominator of the GEMM roofline."""
+    with CUDA events (2 N^3 FLOP each). The denominator of the tensor-core prefill
+    attention roofline (its MMAs are kind::tf32)."""
     import torch
 
     dev = torch.device("cuda", device_index)
@@ -426,7 +439,6 @@ def run_b200(args, rank, world, local_rank):
         decode_step()
     uniq = unique_decode_bytes(engine, ids, bt)
     logical = logical_decode_bytes(engine, ids)
-    tf32 = tf32_peak(local_rank)
     before = dev.counters(reset=True)
     # kernels launched before the timed steps (for `ncu -s` on this command)
     print(f"launches_before_timed={before['kernel_launches']}", file=sys.stderr, flush=True)
@@ -540,7 +552,7 @@ def run_b200(args, rank, world, local_rank):
                      "logical_bytes_per_launch": logical,
                      "logical_achieved": logical / (launch_ms * 1e-3) / 1e9 if launch_ms > 0 else None,
                      "attention_share_of_forward": attn_ms / device_ms if device_ms else None},
-        "gemm_roofline": gemm_roofline(cfg, n, gemm_ms, gemm_intervals, head_ms, heads, tf32),
+        "gemm_roofline": gemm_roofline(cfg, n, gemm_ms, gemm_intervals, head_ms, heads),
         "clocks": clocks.summary(),
         "_record": record,
     }
@@ -551,30 +563,29 @@ def run_b200(args, rank, world, local_rank):
     return line
 
 
-def gemm_roofline(cfg, rows, gemm_ms, intervals, head_ms, heads, tf32_tflops):
+def gemm_roofline(cfg, rows, gemm_ms, intervals, head_ms, heads):
     """The projection GEMMs of one decode step at M = rows, against the measured
-    TF32 peak. Useful FLOP (2 M N K; the kernels issue 3x that as 3xTF32 MMAs):
-    per layer QKV 576x960, O 576x576, gate/up 576x3072, down 1536x576; the tied LM
-    head 576x49152. Times from CUDA events on the context stream: each interval
-    between two layers' attention launches holds one layer's four GEMMs."""
+    16-bit tensor peak. Useful FLOP 2 M N K (the kernels issue 3x that: the split
+    FP16 products A_hi.B_hi, A_hi.B_lo, A_lo.B_hi): per layer QKV 576x960, O
+    576x576, gate/up 576x3072, down 1536x576; the tied LM head 576x49152. Times
+    from CUDA events on the context stream: each interval between two layers'
+    attention launches holds one layer's four GEMMs."""
     H, I, V = cfg.hidden, cfg.intermediate, cfg.vocabulary
     kvw = cfg.kv_width
     layer_flop = 2.0 * rows * (H * (H + 2 * kvw) + H * H + H * 2 * I + I * H)
     head_flop = 2.0 * rows * H * V
-    out = {"bound": "tensor", "unit": "TFLOP/s", "peak": tf32_tflops,
-           "peak_kind": "measured here: cuBLAS TF32 8192^3, best of 10 (MEASURED_PEAKS.json has bf16 only)",
+    peak, kind = fp16_peak()
+    out = {"bound": "tensor", "unit": "TFLOP/s", "peak": peak, "peak_kind": kind, "mma_kind": "f16 (split FP32)",
            "useful_flop_per_layer": layer_flop, "issued_flop_per_layer": 3 * layer_flop,
            "useful_flop_head": head_flop}
     if intervals:
         us = 1000.0 * gemm_ms / intervals
         ach = layer_flop / (us * 1e-6) / 1e12
-        out.update({"layer_gemm_us": us, "achieved": ach, "frac": ach / tf32_tflops,
-                    "issued_frac": 3 * ach / tf32_tflops})
+        out.update({"layer_gemm_us": us, "achieved": ach, "frac": ach / peak, "issued_frac": 3 * ach / peak})
     if heads:
         us = 1000.0 * head_ms / heads
         ach = head_flop / (us * 1e-6) / 1e12
-        out.update({"head_us": us, "head_achieved": ach, "head_frac": ach / tf32_tflops,
-                    "head_issued_frac": 3 * ach / tf32_tflops})
+        out.update({"head_us": us, "head_achieved": ach, "head_frac": ach / peak, "head_issued_frac": 3 * ach / peak})
     return out
 
 

@@ -1,11 +1,14 @@
-"""The 3xTF32 tcgen05 GEMM alone vs float64 numpy: C = A . B^T.
+"""The split-precision tcgen05 GEMM alone vs float64 numpy: C = A . B^T.
 
-Two checks per shape, on the worst element's |gpu - exact| / sum_k |a_k b_k|:
+Every operand value x goes to the tensor cores as two FP16 halves, hi = fp16(x) and
+lo = fp16((x - hi) * 2^11), and the GEMM forms A_hi.B_hi + 2^-11 (A_hi.B_lo +
+A_lo.B_hi). Two checks per shape, on the worst element's
+|gpu - exact| / sum_k |a_k b_k|:
   * absolute: at most 2^-18 (about 4e-6);
-  * against plain TF32 (both operands truncated to TF32, computed in float64
-    here): the 3xTF32 error must be at least 8x smaller -- the split must buy
-    back the precision TF32 drops. (The remaining error is dominated by the
-    tensor core's FP32 accumulation, and grows slowly with K.)
+  * against a single FP16 product (both operands rounded to FP16, computed in
+    float64 here): the split's error must be at least 8x smaller -- the split must
+    buy back the precision one FP16 pass drops. (The remaining error is dominated
+    by the tensor core's FP32 accumulation, and grows slowly with K.)
 """
 import numpy as np
 import pytest
@@ -33,11 +36,11 @@ def test_tc_gemm_matches_float64(built, m, n, k):
     assert np.isfinite(got).all()
     worst = float((err / scale).max())
 
-    def tf32(x):
-        return (x.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32).astype(np.float64)
+    def f16(x):
+        return x.astype(np.float16).astype(np.float64)
 
-    plain = float((np.abs(tf32(a) @ tf32(b).T - exact) / scale).max())
-    print(f"m={m} n={n} k={k}: 3xTF32 {worst:.3e}  plain TF32 {plain:.3e}")
+    plain = float((np.abs(f16(a) @ f16(b).T - exact) / scale).max())
+    print(f"m={m} n={n} k={k}: split FP16 {worst:.3e}  single FP16 {plain:.3e}")
     assert worst <= 2.0 ** -18, worst
     assert worst * 8 <= plain, (worst, plain)
 

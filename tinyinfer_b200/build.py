@@ -24,7 +24,7 @@ HOST_LIB = os.path.join(HERE, "libmpb200_host.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", f"-I{CSRC}"]
-# Extra nvcc flags for tuning builds, e.g. MPB_NVCC_FLAGS="-DMPB_GEMM_CTAS_PER_SM=2" (the
+# Extra nvcc flags for tuning builds, e.g. MPB_NVCC_FLAGS="-DMPB_GATE_UP_BN=128" (the
 # compile-time switches are documented where they are defined); empty by default.
 COMMON += os.environ.get("MPB_NVCC_FLAGS", "").split()
 

@@ -80,15 +80,24 @@ constexpr size_t kAttnSmem = size_t(kStages) * 2 * kStageFloats * sizeof(float) 
                              size_t(kConsumers) * kGroup * kHeadDim * sizeof(float) +      // queries
                              kStages * sizeof(StageDesc) + 2 * kStages * sizeof(uint64_t) + 16;
 
-// Output element: plain FP32, or TF32 hi/lo halves when the caller asked for them.
+// Output elements: plain FP32, or the O projection's FP16 hi/lo halves when the
+// caller asked for them. write_out2 writes elements i and i + 1 (i even).
 __device__ __forceinline__ void write_out(const AttnParams& p, size_t i, float v) {
-    if (p.out_lo) {
-        float h, l;
-        split_tf32(v, h, l);
-        p.out[i] = h;
+    if (p.out_hi) {
+        __half h, l;
+        split_f16(v, h, l);
+        p.out_hi[i] = h;
         p.out_lo[i] = l;
     } else {
         p.out[i] = v;
+    }
+}
+__device__ __forceinline__ void write_out2(const AttnParams& p, size_t i, float v0, float v1) {
+    if (p.out_hi) {
+        store_split2(p.out_hi + i, p.out_lo + i, v0, v1);
+    } else {  // caller buffers of the operator entry points: 4-byte alignment only
+        p.out[i] = v0;
+        p.out[i + 1] = v1;
     }
 }
 
@@ -359,8 +368,7 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
             for (int hh = 0; hh < kGroup; ++hh) {
                 const float l = __shfl_sync(0xffffffffu, l_run, hh);
                 const size_t o = size_t(row) * p.out_stride + (kh * kGroup + hh) * kHeadDim;
-                write_out(p, o + 2 * lane, acc[hh][0] / l);
-                write_out(p, o + 2 * lane + 1, acc[hh][1] / l);
+                write_out2(p, o + 2 * lane, acc[hh][0] / l, acc[hh][1] / l);
             }
             continue;
         }

@@ -232,14 +232,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_kernel(const Pr
         for (int c4 = 0; c4 < kHeadDim / 4; ++c4) {
             const float4 val = make_float4(o_run[4 * c4] * inv, o_run[4 * c4 + 1] * inv, o_run[4 * c4 + 2] * inv,
                                            o_run[4 * c4 + 3] * inv);
-            if (p.out_lo) {
-                float4 h, l;
-                split_tf32(val.x, h.x, l.x);
-                split_tf32(val.y, h.y, l.y);
-                split_tf32(val.z, h.z, l.z);
-                split_tf32(val.w, h.w, l.w);
-                *reinterpret_cast<float4*>(p.out + at + 4 * c4) = h;
-                *reinterpret_cast<float4*>(p.out_lo + at + 4 * c4) = l;
+            if (p.out_hi) {
+                store_split4(p.out_hi + at + 4 * c4, p.out_lo + at + 4 * c4, val);
             } else {
                 *reinterpret_cast<float4*>(p.out + at + 4 * c4) = val;
             }

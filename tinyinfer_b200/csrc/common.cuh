@@ -2,6 +2,7 @@
 // through mbarriers with bounded waits, warp reductions, and the device error word.
 #pragma once
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "kernels.h"
@@ -104,6 +105,38 @@ constexpr float kLog2e = 1.4426950408889634f;
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
     lo = __fsub_rn(x, hi);
+}
+
+// FP16 operand halves of the tensor-core GEMMs: hi = x rounded to FP16, lo = the
+// remainder x - hi (exact in FP32) scaled by 2^11 and rounded to FP16, so that
+// x = hi + lo * 2^-11 within about 2^-23 |x| (kernels.h, kSplitLoScale).
+__device__ __forceinline__ void split_f16(float x, __half& hi, __half& lo) {
+    hi = __float2half_rn(x);
+    lo = __float2half_rn(__fmul_rn(__fsub_rn(x, __half2float(hi)), kSplitLoScale));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(__half a, __half b) {
+    return uint32_t(__half_as_ushort(a)) | (uint32_t(__half_as_ushort(b)) << 16);
+}
+
+// Halves of 4 consecutive values at hi[0..3] / lo[0..3] (8-byte aligned).
+__device__ __forceinline__ void store_split4(__half* hi, __half* lo, float4 v) {
+    __half h[4], l[4];
+    split_f16(v.x, h[0], l[0]);
+    split_f16(v.y, h[1], l[1]);
+    split_f16(v.z, h[2], l[2]);
+    split_f16(v.w, h[3], l[3]);
+    *reinterpret_cast<uint2*>(hi) = make_uint2(pack_half2(h[0], h[1]), pack_half2(h[2], h[3]));
+    *reinterpret_cast<uint2*>(lo) = make_uint2(pack_half2(l[0], l[1]), pack_half2(l[2], l[3]));
+}
+
+// Halves of 2 consecutive values (4-byte aligned).
+__device__ __forceinline__ void store_split2(__half* hi, __half* lo, float a, float b) {
+    __half h0, l0, h1, l1;
+    split_f16(a, h0, l0);
+    split_f16(b, h1, l1);
+    *reinterpret_cast<uint32_t*>(hi) = pack_half2(h0, h1);
+    *reinterpret_cast<uint32_t*>(lo) = pack_half2(l0, l1);
 }
 
 __device__ __forceinline__ float warp_max(float v) {

@@ -323,11 +323,11 @@ struct mp_context {
     cudaEvent_t done = nullptr, idle = nullptr, mark[2] = {nullptr, nullptr};
     int mark_count = 0;
     // weights: the embedding in FP32 (row gather), every GEMM operand packed [N][K]
-    // (K contiguous) as TF32 hi/lo halves; per-layer matrices stacked by layer
+    // (K contiguous) as FP16 hi/lo halves (split_f16); per-layer matrices stacked by layer
     float *embed = nullptr, *final_norm = nullptr, *in_norm = nullptr, *post_norm = nullptr;
     struct Split {
-        float* hi = nullptr;
-        float* lo = nullptr;
+        __half* hi = nullptr;
+        __half* lo = nullptr;
     };
     // gate and up are fused: rows 64b..64b+31 of wgu hold gate rows 32b..32b+31 and
     // rows 64b+32..64b+63 the matching up rows, so a 64-row GEMM tile carries both
@@ -413,10 +413,11 @@ namespace {
 
 size_t max_work(const mp_runtime_config& rt) { return size_t(rt.max_step_tokens) + 2048; }
 
-// Tile widths (B rows per CTA tile) of the wide projections: fewer re-reads of the
-// activations per output column block.
+// Tile width (B rows per CTA tile) of the fused gate/up projection: 64 (more tiles,
+// three stages, usually no K split at decode sizes) or 128 (half the activation
+// re-reads, two stages, split K).
 #ifndef MPB_GATE_UP_BN
-#define MPB_GATE_UP_BN 128
+#define MPB_GATE_UP_BN 64
 #endif
 constexpr int kGateUpBN = MPB_GATE_UP_BN;  // 2 x intermediate is a multiple of 128 (intermediate % 64 == 0)
 int head_tile_n(int vocabulary) { return vocabulary % 256 == 0 ? 256 : (vocabulary % 128 == 0 ? 128 : 64); }
@@ -439,30 +440,27 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// 2-D fp32 map over a row-major [rows][cols] buffer, boxes of 32 columns (one
-// 128-byte swizzled row) x box_rows rows.
-void encode_map(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+// 2-D fp16 map over a row-major [rows][cols] buffer (cols a multiple of 8), boxes of
+// 64 columns (one 128-byte swizzled row) x box_rows rows; columns past `cols` read
+// as zeros.
+void encode_map(CUtensorMap* map, const __half* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
     const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols * sizeof(float)};
-    const cuuint32_t box[2] = {32, box_rows};
+    const cuuint64_t strides[1] = {cols * sizeof(__half)};
+    const cuuint32_t box[2] = {64, box_rows};
     const cuuint32_t element_strides[2] = {1, 1};
-    const CUresult r = tensor_map_encoder()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+    const CUresult r = tensor_map_encoder()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims,
                                             strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) fail(MP_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
 }
 
-// TF32 hi/lo halves on the host (same rule as the device split_tf32).
-void split_host(const float* x, float* hi, float* lo, size_t n) {
+// FP16 hi/lo halves on the host, the rule of the device split_f16: hi = x rounded
+// to FP16, lo = (x - hi) * 2^11 rounded to FP16.
+void split_host(const float* x, __half* hi, __half* lo, size_t n) {
     for (size_t i = 0; i < n; ++i) {
-        uint32_t b;
-        std::memcpy(&b, &x[i], 4);
-        b &= 0xFFFFE000u;
-        float h;
-        std::memcpy(&h, &b, 4);
-        hi[i] = h;
-        lo[i] = x[i] - h;
+        hi[i] = __float2half_rn(x[i]);
+        lo[i] = __float2half_rn((x[i] - __half2float(hi[i])) * mpb::kSplitLoScale);
     }
 }
 
@@ -560,8 +558,8 @@ void validate_geometry(const mp_model_config& m, const mp_runtime_config& r) {
 
 struct WeightSlot {
     float* base;     // fp32 destination (embedding, norms) or nullptr
-    float* hi;       // TF32 halves destination of a GEMM operand slice, or nullptr
-    float* lo;
+    __half* hi;      // FP16 halves destination of a GEMM operand slice, or nullptr
+    __half* lo;
     int rows_n;      // N of the packed [N][K] matrix slice
     int k;           // K
     bool transpose;  // MPFX [K][N] -> packed [N][K]
@@ -596,7 +594,9 @@ WeightSlot resolve(mp_context* c, const std::string& name) {
     if (s == "input_layernorm.weight") return {c->in_norm + L * H, nullptr, nullptr, 1, H, false, size_t(H), 0};
     if (s == "post_attention_layernorm.weight")
         return {c->post_norm + L * H, nullptr, nullptr, 1, H, false, size_t(H), 0};
-    auto slice = [](const mp_context::Split& s, size_t offset) { return std::pair<float*, float*>(s.hi + offset, s.lo + offset); };
+    auto slice = [](const mp_context::Split& s, size_t offset) {
+        return std::pair<__half*, __half*>(s.hi + offset, s.lo + offset);
+    };
     const size_t qkv = L * size_t(c->qkvw) * H;
     if (s == "self_attn.q_proj.weight") {
         auto p = slice(c->wqkv, qkv);
@@ -710,8 +710,8 @@ int mp_create(int device, const mp_model_config* model, const mp_runtime_config*
         const size_t H = m.hidden, I = m.intermediate, L = m.layers, V = m.vocabulary;
         cuda_check(mpb::configure_tc_gemm(), "configure tensor-core GEMM");
         auto split = [](mp_context::Split& s, size_t n, const char* what) {
-            s.hi = device_alloc<float>(n, what);
-            s.lo = device_alloc<float>(n, what);
+            s.hi = device_alloc<__half>(n, what);
+            s.lo = device_alloc<__half>(n, what);
         };
         c->embed = device_alloc<float>(V * H, "embedding");
         c->final_norm = device_alloc<float>(H, "final norm");
@@ -829,7 +829,7 @@ int mp_set_weight(mp_context* c, const char* name, const float* host, size_t ele
         if (elements != slot.elements) fail(MP_ERR_INVALID, std::string("tensor shape mismatch: ") + name);
         if (slot.base) cuda_check(cudaMemcpy(slot.base, host, elements * 4, cudaMemcpyHostToDevice), "upload weight");
         if (slot.hi) {
-            // MPFX stores [K][N] ([in][out]); the GEMM reads [N][K] as TF32 halves.
+            // MPFX stores [K][N] ([in][out]); the GEMM reads [N][K] as FP16 halves.
             std::vector<float> t;
             const float* packed = host;
             if (slot.transpose) {
@@ -839,20 +839,20 @@ int mp_set_weight(mp_context* c, const char* name, const float* host, size_t ele
                     for (int n = 0; n < N; ++n) t[size_t(n) * K + k] = host[size_t(k) * N + n];
                 packed = t.data();
             }
-            std::vector<float> hi(elements), lo(elements);
+            std::vector<__half> hi(elements), lo(elements);
             split_host(packed, hi.data(), lo.data(), elements);
             if (!slot.interleave) {
-                cuda_check(cudaMemcpy(slot.hi, hi.data(), elements * 4, cudaMemcpyHostToDevice), "upload weight");
-                cuda_check(cudaMemcpy(slot.lo, lo.data(), elements * 4, cudaMemcpyHostToDevice), "upload weight");
+                cuda_check(cudaMemcpy(slot.hi, hi.data(), elements * 2, cudaMemcpyHostToDevice), "upload weight");
+                cuda_check(cudaMemcpy(slot.lo, lo.data(), elements * 2, cudaMemcpyHostToDevice), "upload weight");
             } else {
                 // gate/up rows go to alternating 32-row blocks of the fused matrix
                 const size_t K = size_t(slot.k), block = 32 * K;
                 const size_t half = size_t(slot.interleave - 1) * block;
                 for (int b = 0; b < slot.rows_n / 32; ++b) {
                     const size_t dst = size_t(b) * 2 * block + half, src = size_t(b) * block;
-                    cuda_check(cudaMemcpy(slot.hi + dst, hi.data() + src, block * 4, cudaMemcpyHostToDevice),
+                    cuda_check(cudaMemcpy(slot.hi + dst, hi.data() + src, block * 2, cudaMemcpyHostToDevice),
                                "upload weight");
-                    cuda_check(cudaMemcpy(slot.lo + dst, lo.data() + src, block * 4, cudaMemcpyHostToDevice),
+                    cuda_check(cudaMemcpy(slot.lo + dst, lo.data() + src, block * 2, cudaMemcpyHostToDevice),
                                "upload weight");
                 }
             }
@@ -1242,7 +1242,8 @@ int mp_forward_launch(mp_context* c) {
         ap.work_count = c->work_count;
         ap.partial = c->partial;
         ap.counters = c->counters;
-        ap.out = c->attn.hi;
+        ap.out = nullptr;
+        ap.out_hi = c->attn.hi;
         ap.out_lo = c->attn.lo;
         ap.out_stride = H;
         ap.error = c->error;
@@ -1276,7 +1277,8 @@ int mp_forward_launch(mp_context* c) {
         pp.table_stride = r.table_stride;
         pp.work = reinterpret_cast<const mpb::PrefillWork*>(meta + c->off_prefill);
         pp.work_count = c->prefill_count;
-        pp.out = c->attn.hi;
+        pp.out = nullptr;
+        pp.out_hi = c->attn.hi;
         pp.out_lo = c->attn.lo;
         pp.out_stride = H;
         pp.error = c->error;
@@ -1524,11 +1526,11 @@ int mp_profile_read_gemm(mp_context* c, float* layer_gemm_ms, int32_t* intervals
     return MP_OK;
 }
 
-// C = A . B^T through the 3xTF32 tensor-core GEMM on caller device buffers (a [m][k],
-// b [n][k], c [m][n], row-major). Allocates and frees its own hi/lo scratch and
-// synchronises `stream`; meant for tests and tools, not for the hot path.
+// C = A . B^T through the split-precision tensor-core GEMM on caller device buffers
+// (a [m][k], b [n][k], c [m][n], row-major). Allocates and frees its own hi/lo
+// scratch and synchronises `stream`; meant for tests and tools, not for the hot path.
 int mp_gemm_f32(const float* a, const float* b, float* out, int32_t m, int32_t n, int32_t k, void* stream_ptr) {
-    std::vector<float*> scratch;
+    std::vector<void*> scratch;
     cudaStream_t st = static_cast<cudaStream_t>(stream_ptr);
     const int rc = guarded([&] {
         if (!a || !b || !out || m < 1 || n < 1 || k < 1) fail(MP_ERR_INVALID, "invalid argument");
@@ -1536,12 +1538,12 @@ int mp_gemm_f32(const float* a, const float* b, float* out, int32_t m, int32_t n
         cuda_check(mpb::configure_tc_gemm(), "configure tensor-core GEMM");
         const size_t rows_a = (size_t(m) + 127) / 128 * 128, rows_b = size_t(n);
         auto alloc = [&](size_t count) {
-            float* p = device_alloc<float>(count, "gemm scratch");
+            __half* p = device_alloc<__half>(count, "gemm scratch");
             scratch.push_back(p);
-            cuda_check(cudaMemsetAsync(p, 0, count * 4, st), "clear gemm scratch");
+            cuda_check(cudaMemsetAsync(p, 0, count * sizeof(__half), st), "clear gemm scratch");
             return p;
         };
-        float *ah = alloc(rows_a * k), *al = alloc(rows_a * k), *bh = alloc(rows_b * k), *bl = alloc(rows_b * k);
+        __half *ah = alloc(rows_a * k), *al = alloc(rows_a * k), *bh = alloc(rows_b * k), *bl = alloc(rows_b * k);
         cuda_check(mpb::launch_split(a, ah, al, size_t(m) * k, st), "split a");
         cuda_check(mpb::launch_split(b, bh, bl, size_t(n) * k, st), "split b");
         struct alignas(64) M4 {
@@ -1555,7 +1557,7 @@ int mp_gemm_f32(const float* a, const float* b, float* out, int32_t m, int32_t n
         encode_map(&maps->bh, bh, rows_b, k, uint32_t(bn));
         encode_map(&maps->bl, bl, rows_b, k, uint32_t(bn));
         unsigned* err = device_alloc<unsigned>(1, "gemm error word");
-        scratch.push_back(reinterpret_cast<float*>(err));
+        scratch.push_back(err);
         cuda_check(cudaMemsetAsync(err, 0, 4, st), "clear error word");
         mpb::TcGemmParams g{};
         g.m = m;
@@ -1582,7 +1584,7 @@ int mp_gemm_f32(const float* a, const float* b, float* out, int32_t m, int32_t n
         cudaEventDestroy(done);
         if (herr) fail(MP_ERR_TIMEOUT, "tensor-core GEMM wait expired");
     });
-    for (float* p : scratch) cudaFree(p);
+    for (void* p : scratch) cudaFree(p);
     return rc;
 }
 

@@ -17,7 +17,7 @@ namespace {
 // One warp per row. Sum of squares by per-lane partials and a butterfly; the
 // normalisation order matches the CPU runner: (x * scale) * w
 // (miniprefix/src/backend/cpu/llama_runner.cpp:10-16).
-__device__ __forceinline__ void rms_row(const float* x, const float* w, float eps, float* out_hi, float* out_lo,
+__device__ __forceinline__ void rms_row(const float* x, const float* w, float eps, __half* out_hi, __half* out_lo,
                                         int hidden, int lane) {
     float sum = 0.f;
     for (int d = lane * 4; d < hidden; d += 128) {
@@ -32,23 +32,19 @@ __device__ __forceinline__ void rms_row(const float* x, const float* w, float ep
     for (int d = lane * 4; d < hidden; d += 128) {
         const float4 v = *reinterpret_cast<const float4*>(x + d);
         const float4 g = *reinterpret_cast<const float4*>(w + d);
-        float4 h, l;
-        split_tf32(__fmul_rn(__fmul_rn(v.x, scale), g.x), h.x, l.x);
-        split_tf32(__fmul_rn(__fmul_rn(v.y, scale), g.y), h.y, l.y);
-        split_tf32(__fmul_rn(__fmul_rn(v.z, scale), g.z), h.z, l.z);
-        split_tf32(__fmul_rn(__fmul_rn(v.w, scale), g.w), h.w, l.w);
-        *reinterpret_cast<float4*>(out_hi + d) = h;
-        *reinterpret_cast<float4*>(out_lo + d) = l;
+        store_split4(out_hi + d, out_lo + d,
+                     make_float4(__fmul_rn(__fmul_rn(v.x, scale), g.x), __fmul_rn(__fmul_rn(v.y, scale), g.y),
+                                 __fmul_rn(__fmul_rn(v.z, scale), g.z), __fmul_rn(__fmul_rn(v.w, scale), g.w)));
     }
 }
 
 // With ssq (the first layer's norm folded into its QKV GEMM): writes x * w as
-// TF32 halves and the sum of squares of each 64-column group of x, reduced the
+// FP16 halves and the sum of squares of each 64-column group of x, reduced the
 // way the GEMM epilogue reduces it (4 values per lane, then a half-warp tree);
 // hidden a multiple of 64. Without: the normalised row, as rms_row.
 __global__ void embed_rmsnorm_kernel(const int32_t* tokens, const float* embed, int vocabulary, const float* w,
-                                     float eps, float* x, float* normed_hi, float* normed_lo, int rows, int hidden,
-                                     float* ssq, unsigned* error) {
+                                     float eps, float* x, __half* normed_hi, __half* normed_lo, int rows,
+                                     int hidden, float* ssq, unsigned* error) {
     pdl_enter();  // before any global memory access
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -67,13 +63,9 @@ __global__ void embed_rmsnorm_kernel(const int32_t* tokens, const float* embed, 
                 const float4 v = *reinterpret_cast<const float4*>(src + d);
                 const float4 g = *reinterpret_cast<const float4*>(w + d);
                 *reinterpret_cast<float4*>(xr + d) = v;
-                float4 h, l;
-                split_tf32(__fmul_rn(v.x, g.x), h.x, l.x);
-                split_tf32(__fmul_rn(v.y, g.y), h.y, l.y);
-                split_tf32(__fmul_rn(v.z, g.z), h.z, l.z);
-                split_tf32(__fmul_rn(v.w, g.w), h.w, l.w);
-                *reinterpret_cast<float4*>(normed_hi + size_t(row) * hidden + d) = h;
-                *reinterpret_cast<float4*>(normed_lo + size_t(row) * hidden + d) = l;
+                store_split4(normed_hi + size_t(row) * hidden + d, normed_lo + size_t(row) * hidden + d,
+                             make_float4(__fmul_rn(v.x, g.x), __fmul_rn(v.y, g.y), __fmul_rn(v.z, g.z),
+                                         __fmul_rn(v.w, g.w)));
                 q = __fmul_rn(v.x, v.x);
                 q = fmaf(v.y, v.y, q);
                 q = fmaf(v.z, v.z, q);
@@ -93,8 +85,8 @@ __global__ void embed_rmsnorm_kernel(const int32_t* tokens, const float* embed, 
     rms_row(xr, w, eps, normed_hi + size_t(row) * hidden, normed_lo + size_t(row) * hidden, hidden, lane);
 }
 
-__global__ void rmsnorm_kernel(const float* x, const int32_t* rows, const float* w, float eps, float* out_hi,
-                               float* out_lo, int count, int hidden) {
+__global__ void rmsnorm_kernel(const float* x, const int32_t* rows, const float* w, float eps, __half* out_hi,
+                               __half* out_lo, int count, int hidden) {
     pdl_enter();  // before any global memory access
     const int i = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
     if (i >= count) return;
@@ -219,7 +211,7 @@ __global__ void table_patch_kernel(const int32_t* pairs, int count, int32_t* tab
 }  // namespace
 
 cudaError_t launch_embed_rmsnorm(const int32_t* tokens, const float* embed, int vocabulary, const float* norm_w,
-                                 float eps, float* x, float* normed_hi, float* normed_lo, int rows, int hidden,
+                                 float eps, float* x, __half* normed_hi, __half* normed_lo, int rows, int hidden,
                                  float* ssq, unsigned* error, cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
     if (ssq && hidden % 64) return cudaErrorInvalidValue;
@@ -227,8 +219,8 @@ cudaError_t launch_embed_rmsnorm(const int32_t* tokens, const float* embed, int 
                       norm_w, eps, x, normed_hi, normed_lo, rows, hidden, ssq, error);
 }
 
-cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, float* out_hi,
-                           float* out_lo, int count, int hidden, cudaStream_t stream) {
+cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, __half* out_hi,
+                           __half* out_lo, int count, int hidden, cudaStream_t stream) {
     if (count <= 0) return cudaSuccess;
     return launch_pdl(rmsnorm_kernel, dim3((count + 7) / 8), dim3(256), 0, stream, x, rows, norm_w, eps, out_hi, out_lo,
                       count, hidden);

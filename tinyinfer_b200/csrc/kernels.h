@@ -4,6 +4,7 @@
 #include <algorithm>
 #include <cstddef>
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace mpb {
@@ -57,8 +58,9 @@ struct AttnParams {
     int cta_count;
     float* partial;      // [slots][9][66] slice results: work items first, then shared-prefix slots
     unsigned* counters;  // [rows][3 kv heads] zero between launches
-    float* out;          // [rows][out_stride]; the TF32 hi half when out_lo is set
-    float* out_lo;       // optional: lo halves (GEMM input), same layout
+    float* out;          // [rows][out_stride] FP32 output (when out_hi is null)
+    __half* out_hi;      // optional: the output as the O projection's FP16 operand
+    __half* out_lo;      // halves (split_f16), same layout; `out` is then unused
     int out_stride;
     unsigned* error;
 };
@@ -122,7 +124,8 @@ struct PrefillParams {
     const PrefillWork* work;
     int work_count;
     float* out;
-    float* out_lo;  // optional lo halves, as in AttnParams
+    __half* out_hi;  // optional FP16 operand halves, as in AttnParams
+    __half* out_lo;
     int out_stride;
     unsigned* error;
 };
@@ -202,7 +205,7 @@ cudaError_t noalloc_take_error(cudaStream_t stream, unsigned* bits);
 enum class Epilogue : int {
     Store = 0,   // C = acc
     AddTo = 1,   // C = C + acc  (residual add)
-    SwiGLU = 2,  // gate/up column pairs -> silu(gate) * up as TF32 hi/lo halves
+    SwiGLU = 2,  // gate/up column pairs -> silu(gate) * up as FP16 hi/lo halves
     Rope = 3,    // QKV projection (64-wide tiles = heads): RoPE on q and k, q to the
                  // attention input, k and v into the rows' page slots (TcGemmParams::rope)
 };
@@ -227,9 +230,19 @@ struct RopeEpilogue {
     int layers, layer, block_tokens, max_blocks;
 };
 
-// Tensor-core 3xTF32 GEMM (tc_gemm.cu). A and B come as TF32 hi/lo halves through
-// 2-D TMA tensor maps (fp32, rows x K, 128-byte swizzle, boxes of 32 x 128 rows
-// for A and 32 x bn rows for B, bn = 64, 128 or 256); B's rows start at b_row0
+// GEMM operands in split precision. Every FP32 operand value x travels as two FP16
+// halves (split_f16, common.cuh): hi = fp16(x) rounded to nearest and
+// lo = fp16((x - hi) * 2^11), so x = hi + lo * 2^-11 within about 2^-23 |x|. The
+// tensor-core GEMM forms the three products A_hi.B_hi + 2^-11 (A_hi.B_lo + A_lo.B_hi)
+// (the dropped A_lo.B_lo term is below 2^-22 relative). |x| must stay below 65504,
+// the FP16 range; a larger operand becomes infinite and the forward's logits then
+// come out nonfinite, which the step reports as an error.
+constexpr float kSplitLoScale = 2048.0f;
+constexpr float kSplitLoUnscale = 1.0f / 2048.0f;
+
+// Tensor-core split-precision GEMM (tc_gemm.cu). A and B come as FP16 hi/lo halves
+// through 2-D TMA tensor maps (fp16, rows x K, 128-byte swizzle, boxes of 64 x 128
+// rows for A and 64 x bn rows for B, bn = 64, 128 or 256); B's rows start at b_row0
 // (stacked per-layer weights). Epilogues: Store / AddTo into c; SwiGLU expects B's
 // rows in 32-row gate/up blocks (rows 64b..64b+31 gate, 64b+32..64b+63 up) and
 // writes silu(gate) * up for output columns 32b..32b+31 as hi/lo halves (out_hi,
@@ -249,14 +262,14 @@ struct TcGemmParams {
     int b_row0;
     float* c;
     int ldc;
-    float* out_hi;
-    float* out_lo;
+    __half* out_hi;
+    __half* out_lo;
     int ld_out;
     unsigned* error;
     RopeEpilogue rope;  // Epilogue::Rope only
     // RMSNorm folded into the GEMMs around it (hidden = N of the producer = K of the
     // consumer, a multiple of 64):
-    //  * AddTo with norm_w: besides c, writes the TF32 halves of c[row] * norm_w
+    //  * AddTo with norm_w: besides c, writes the FP16 halves of c[row] * norm_w
     //    (the next GEMM's A operand) into out_hi / out_lo (ld_out) and the sum of
     //    squares of each 64-column group of c[row] into ssq_out[row][n0 / 64];
     //  * Rope / SwiGLU with ssq_in: scales row r of the product by
@@ -274,20 +287,22 @@ struct TcGemmParams {
 };
 constexpr int kSsqGroup = 64;  // columns per partial sum of squares
 cudaError_t configure_tc_gemm();
+// K must be a multiple of 8 (16-byte rows for the tensor maps); a partial last
+// 64-wide K block is zero-filled by the TMA engine.
 cudaError_t launch_tc_gemm(const TcGemmMaps& maps, const TcGemmParams& p, Epilogue e, cudaStream_t stream);
-// hi = x with the 13 low mantissa bits cleared, lo = x - hi, elementwise.
-cudaError_t launch_split(const float* x, float* hi, float* lo, size_t n, cudaStream_t stream);
+// FP16 hi/lo operand halves of x (split_f16), elementwise.
+cudaError_t launch_split(const float* x, __half* hi, __half* lo, size_t n, cudaStream_t stream);
 
 // ---------------------------------------------------------------- fused small ops
-// x[r][:] = embed[tokens[r]][:]; rmsnorm(x[r]) * w written as TF32 hi/lo halves, or
+// x[r][:] = embed[tokens[r]][:]; rmsnorm(x[r]) * w written as FP16 hi/lo halves, or
 // with ssq (norm folded into the next GEMM): x[r] * w as halves and the sums of
 // squares of x[r]'s 64-column groups into ssq[r][hidden / 64].
 cudaError_t launch_embed_rmsnorm(const int32_t* tokens, const float* embed, int vocabulary, const float* norm_w,
-                                 float eps, float* x, float* normed_hi, float* normed_lo, int rows, int hidden,
+                                 float eps, float* x, __half* normed_hi, __half* normed_lo, int rows, int hidden,
                                  float* ssq, unsigned* error, cudaStream_t stream);
-// rmsnorm(x[rows ? rows[i] : i]) * w as hi/lo halves into out_hi/out_lo[i] for i < count.
-cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, float* out_hi,
-                           float* out_lo, int count, int hidden, cudaStream_t stream);
+// rmsnorm(x[rows ? rows[i] : i]) * w as FP16 hi/lo halves into out_hi/out_lo[i] for i < count.
+cudaError_t launch_rmsnorm(const float* x, const int32_t* rows, const float* norm_w, float eps, __half* out_hi,
+                           __half* out_lo, int count, int hidden, cudaStream_t stream);
 // Greedy token (first index of the maximum) and finiteness of each logits row.
 cudaError_t launch_argmax(const float* logits, int rows, int vocabulary, int32_t* tokens, int32_t* finite,
                           cudaStream_t stream);

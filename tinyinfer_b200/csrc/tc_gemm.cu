@@ -1,37 +1,47 @@
-// Tensor-core FP32 GEMM for sm_100a: 3xTF32 on tcgen05 with TMEM accumulators.
+// Tensor-core FP32 GEMM for sm_100a: split-precision FP16 products on tcgen05 with
+// TMEM accumulators.
 //
 // C[M][N] (op)= A[M][K] . B[N][K]^T for the projections of the forward (fused QKV,
 // O, gate, up, down, LM head) -- the reference runs them as pedantic FP32 cuBLAS
 // SGEMMs (miniprefix/src/backend/cuda/llama_runner.cu:69-71).
 //
-// FP32 accuracy from TF32 tensor cores (the published split-precision method,
-// e.g. Ootomo & Yokota 2022): every operand x is stored as hi + lo with
-// hi = x with its 13 low mantissa bits cleared (exact in TF32) and lo = x - hi
-// (exact in FP32); C = A_lo.B_hi + A_hi.B_lo + A_hi.B_hi, accumulated in FP32 in
-// tensor memory. The dropped A_lo.B_lo term and TF32 truncation of lo are below
-// 2^-20 relative per product. Weights are split once at upload; the kernels that
-// produce GEMM inputs (RMSNorm, attention, SwiGLU) write hi/lo pairs directly.
+// FP32 accuracy from 16-bit tensor cores (the published split-precision method,
+// Ootomo & Yokota 2022, in its FP16 form): every operand x is stored as two FP16
+// halves, hi = fp16(x) and lo = fp16((x - hi) * 2^11) (kernels.h), and
+// C = A_hi.B_hi + 2^-11 (A_hi.B_lo + A_lo.B_hi). The FP16 products are exact in the
+// tensor core's FP32 accumulation; the two sums are kept in separate TMEM
+// accumulators (the main product and the scaled cross terms) and combined as
+// main + 2^-11 cross with one fused multiply-add. The dropped A_lo.B_lo term and
+// the rounding of lo are below 2^-22 relative per product. The kind::f16 pipe runs
+// at twice the TF32 rate and the halves take 4 bytes per value instead of 8, so a
+// K block moves half the operand bytes of the same product in TF32 halves.
+// Weights are split once at upload; the kernels that produce GEMM inputs
+// (RMSNorm, attention, SwiGLU, the residual epilogues) write the halves directly.
 //
 // A CTA computes the K-slice blockIdx.z (of gridDim.z) of a 128 x BN tile with 4 warps:
-//  * warp 0 / one lane: TMA producer. Per 32-element K block it loads the four
+//  * warp 0 / one lane: TMA producer. Per 64-element K block it loads the four
 //    operand tiles (A_hi, A_lo, B_hi, B_lo; 128-byte swizzled rows, one CTA per load)
 //    into a stage and signals the stage's full mbarrier by transaction count;
 //  * warp 1 / one lane: MMA issuer. Per K block 4 K-steps x 3 tcgen05.mma
-//    (kind::tf32, M=128, N=BN, K=8) into one TMEM accumulator; tcgen05.commit
+//    (kind::f16, M=128, N=BN, K=16) into the two TMEM accumulators; tcgen05.commit
 //    releases the stage to the producer, and after the last block signals the
 //    accumulator barrier;
 //  * warps 2-3, meanwhile: gather the epilogue's per-row inputs that need global
 //    reads (RMSNorm row scales, RoPE destinations) into shared memory;
 //  * all 4 warps: the K slices of one output tile form a thread-block cluster
 //    (cluster dims 1 x 1 x slices) and each CTA owns a contiguous share of the
-//    tile's rows. After a cluster barrier (every slice past its MMAs, so every
-//    stage ring is idle) each thread moves its TMEM lane (= tile row) with
-//    tcgen05.ld.32x32b and stores it straight into the ring of the row's owner
-//    (st.shared::cluster, this slice's block there). After a second cluster
-//    barrier every CTA sums its rows over the slices' blocks in slice order from
-//    its own shared memory (deterministic split-K for the small-M decode GEMMs,
-//    no global round trip and no remote loads) and applies the fused epilogue
-//    with coalesced row-contiguous stores.
+//    tile's rows. As soon as its own accumulators are final, each thread reads its
+//    TMEM lane (= tile row) with tcgen05.ld.32x32b, combines the two sums, and
+//    stores the row into the receive area of the row's owner CTA with st.async
+//    (this slice's block there), completing bytes on the owner's receive
+//    mbarrier. The owner waits on that barrier alone -- no cluster-wide barrier
+//    separates the MMAs from the push -- then sums its rows over the slices'
+//    blocks in slice order (deterministic split-K for the small-M decode GEMMs, no
+//    global round trip and no remote loads) and applies the fused epilogue with
+//    coalesced row-contiguous stores. Two split cluster barriers remain off the
+//    critical path: one whose arrival follows the barrier set-up at the start and
+//    whose wait precedes the first push, and one whose arrival follows the pushes
+//    and whose wait precedes the exit.
 // Every mbarrier wait is bounded; a timeout sets the error word, and the CTA still
 // passes both cluster barriers and releases its tensor memory.
 #include <cuda.h>
@@ -46,29 +56,29 @@ namespace mpb {
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kBK = 32;  // fp32 elements per K block = one 128-byte swizzle row
+constexpr int kBK = 64;  // fp16 elements per K block = one 128-byte swizzle row
 constexpr int kThreads = 128;
 constexpr int kMaxSlices = 8;  // portable cluster size
 
-// Resident CTAs per SM the kernel is built for: 1 (deep stage rings) or 2 (two
-// 2-stage CTAs share an SM, so small-M GEMMs can spread over more K slices).
-#ifndef MPB_GEMM_CTAS_PER_SM
-#define MPB_GEMM_CTAS_PER_SM 1
-#endif
-constexpr int kCtasPerSm = MPB_GEMM_CTAS_PER_SM;
-
 template <int BN>
 struct TcConfig {
-    static constexpr int kStages = kCtasPerSm == 2 ? 2 : (BN <= 64 ? 4 : (BN <= 128 ? 3 : 2));
-    static constexpr int kATile = kBM * kBK * 4;  // bytes
-    static constexpr int kBTile = BN * kBK * 4;
+    // Tiles up to 128 wide may split K: their slices push partial rows into a
+    // receive area of its own, so a slice can push while its owner still runs MMAs
+    // out of the stage ring. The 256-wide LM-head tiles never split K and reuse the
+    // idle ring for their rows.
+    static constexpr bool kOwnRecv = BN <= 128;
+    static constexpr int kStages = BN <= 64 ? 3 : 2;
+    static constexpr int kATile = kBM * kBK * 2;  // bytes
+    static constexpr int kBTile = BN * kBK * 2;
     static constexpr int kStage = 2 * kATile + 2 * kBTile;
     static constexpr int kTileStride = BN + 4;  // floats per received accumulator row (bank spread)
     // receive area: `slices` partial row blocks of ceil(128 / slices) rows each
     static constexpr int kRecvBytes = (kBM + kMaxSlices) * kTileStride * 4;
-    static constexpr int kRing = kStages * kStage > kRecvBytes ? kStages * kStage : kRecvBytes;
-    static constexpr int kSmem = kRing + 1024 /*align*/ + 256 /*barriers*/;
-    static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+    static constexpr int kRing = kStages * kStage;
+    static constexpr int kData = kOwnRecv ? kRing + kRecvBytes : (kRing > kRecvBytes ? kRing : kRecvBytes);
+    static constexpr int kSmem = kData + 1024 /*align*/ + 256 /*barriers*/;
+    // two accumulators of BN columns: A_hi.B_hi, then the cross terms
+    static constexpr int kTmemCols = 2 * BN;
 };
 template <int BN, Epilogue E>
 constexpr int dynamic_smem() { return TcConfig<BN>::kSmem; }
@@ -92,9 +102,10 @@ __device__ __forceinline__ uint32_t cluster_rank() {
     return r;
 }
 
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
+// Split cluster barrier: every thread of every CTA of the cluster arrives, then
+// waits for all arrivals of that phase.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 // Address of the same shared-memory offset in cluster CTA `rank` (its own included).
 __device__ __forceinline__ uint32_t map_cluster(const void* local, uint32_t rank) {
@@ -103,9 +114,13 @@ __device__ __forceinline__ uint32_t map_cluster(const void* local, uint32_t rank
     return remote;
 }
 
-__device__ __forceinline__ void st_cluster(uint32_t addr, float4 v) {
-    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
-                 "f"(v.w)
+// 16 bytes into a cluster CTA's shared memory at `addr`, completing their
+// transaction bytes on that CTA's mbarrier at `bar` (both shared::cluster
+// addresses of the same CTA).
+__device__ __forceinline__ void st_async(uint32_t addr, float4 v, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                     addr),
+                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar)
                  : "memory");
 }
 
@@ -133,7 +148,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 //  AddTo  : c[row][n0 + j] += acc                        (residual add)
 //  SwiGLU : per 64-column group g of the tile, columns 0..31 are gate and 32..63 up
 //           of output columns (n0 + 64 g) / 2 + 0..31; writes h = silu(gate) * up as
-//           TF32 hi/lo halves (the down projection's input).
+//           FP16 hi/lo halves (the down projection's input).
 //  Rope   : the tile is one head of the QKV projection; dims (d, d + 32) rotate
 //           together (q and k heads) as the CPU runner does (a' = a cos - b sin,
 //           b' = b cos + a sin, products rounded separately; miniprefix/src/backend/
@@ -299,12 +314,8 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
                 const float4 gt = acc[u][0], up = acc[u][kLoads - 1];
                 const float o[4] = {silu_mul(gt.x, up.x), silu_mul(gt.y, up.y), silu_mul(gt.z, up.z),
                                     silu_mul(gt.w, up.w)};
-                float hv[4], lv[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) split_tf32(o[e], hv[e], lv[e]);
                 const size_t at = size_t(m0 + row) * p.ld_out + (n0 + 64 * (it / 8)) / 2 + 4 * (it % 8);
-                *reinterpret_cast<float4*>(p.out_hi + at) = make_float4(hv[0], hv[1], hv[2], hv[3]);
-                *reinterpret_cast<float4*>(p.out_lo + at) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+                store_split4(p.out_hi + at, p.out_lo + at, make_float4(o[0], o[1], o[2], o[3]));
             } else {
                 const float4 a = acc[u][0];
                 if (E == Epilogue::Store) {
@@ -315,17 +326,13 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
                                                  __fadd_rn(x.w, a.w));
                     *dst[u] = y;
                     if (produce) {
-                        // the next GEMM's A operand: y * norm weight as TF32 halves
+                        // the next GEMM's A operand: y * norm weight as FP16 halves
                         const int col = n0 + 4 * it;
                         const float4 w = wn[u];
-                        float4 hv, lv;
-                        split_tf32(__fmul_rn(y.x, w.x), hv.x, lv.x);
-                        split_tf32(__fmul_rn(y.y, w.y), hv.y, lv.y);
-                        split_tf32(__fmul_rn(y.z, w.z), hv.z, lv.z);
-                        split_tf32(__fmul_rn(y.w, w.w), hv.w, lv.w);
                         const size_t at = size_t(m0 + row) * p.ld_out + col;
-                        *reinterpret_cast<float4*>(p.out_hi + at) = hv;
-                        *reinterpret_cast<float4*>(p.out_lo + at) = lv;
+                        store_split4(p.out_hi + at, p.out_lo + at,
+                                     make_float4(__fmul_rn(y.x, w.x), __fmul_rn(y.y, w.y), __fmul_rn(y.z, w.z),
+                                                 __fmul_rn(y.w, w.w)));
                         float q = __fmul_rn(y.x, y.x);
                         q = fmaf(y.y, y.y, q);
                         q = fmaf(y.z, y.z, q);
@@ -353,7 +360,7 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
 }
 
 template <int BN, Epilogue E>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+__global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                    const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
                    const TcGemmParams p) {
@@ -361,16 +368,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     constexpr int S = Cfg::kStages;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStage);
+    float* recv = reinterpret_cast<float*>(smem + (Cfg::kOwnRecv ? Cfg::kRing : 0));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kData);
     uint64_t* empty = full + S;
     uint64_t* accum = empty + S;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accum + 1);
+    uint64_t* recv_bar = accum + 1;  // the slices' partial rows of this CTA's share have landed
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(recv_bar + 1);
     int* failed = reinterpret_cast<int*>(tmem_holder + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
     // K blocks of this CTA's split: [kb_begin, kb_end)
-    const int kb_total = p.k / kBK, splits = gridDim.z;
+    const int kb_total = (p.k + kBK - 1) / kBK, splits = gridDim.z;
     const int kb_per = (kb_total + splits - 1) / splits;
     const int kb_begin = blockIdx.z * kb_per, kb_end = min(kb_total, kb_begin + kb_per);
     const int kblocks = kb_end - kb_begin;
@@ -382,24 +391,24 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     __shared__ int row_pos[kBM];
     const RowInputs rows{row_scale, row_dst, row_pos};
 
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
-                     "r"(uint32_t(Cfg::kTmemCols))
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
+    if (warp == 0) tmem_alloc(tmem_holder, uint32_t(Cfg::kTmemCols));
     if (threadIdx.x == 32) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
         mbar_init(accum, 1);
+        mbar_init(recv_bar, 1);
+        // every slice (this one included) sends (r1 - r0) rows of BN floats
+        if (splits > 1) mbar_arrive_expect_tx(recv_bar, uint32_t(splits * (r1 - r0) * BN) * 4u);
         *failed = 0;
         fence_barrier_init();
     }
     tmem_fence_before();
     __syncthreads();
     tmem_fence_after();
+    // phase 1: this CTA's barriers are initialised (waited before the first push)
+    if (splits > 1) cluster_arrive();
     const uint32_t tmem = *tmem_holder;
 
     // The weights (B) never depend on an earlier kernel: the first stages' weight
@@ -436,8 +445,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             tma_load_2d(st + Cfg::kATile, &a_lo, kx, m0, &full[s]);
         }
     } else if (warp == 1 && lane == 0) {
-        // MMA issuer
-        constexpr uint32_t idesc = umma_idesc_tf32<kBM, BN>();
+        // MMA issuer: main = A_hi.B_hi in columns [0, BN), cross = A_lo.B_hi +
+        // A_hi.B_lo in columns [BN, 2 BN)
+        constexpr uint32_t idesc = umma_idesc_f16<kBM, BN>();
+        const uint32_t d_main = tmem, d_cross = tmem + uint32_t(BN);
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
             const int s = kb % S;
@@ -451,11 +462,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             const uint64_t dah = smem_desc(st), dal = smem_desc(st + Cfg::kATile);
             const uint64_t dbh = smem_desc(st + 2 * Cfg::kATile), dbl = smem_desc(st + 2 * Cfg::kATile + Cfg::kBTile);
 #pragma unroll
-            for (int j = 0; j < kBK / 8; ++j) {
-                const uint64_t step = uint64_t(j * 32) >> 4;  // 8 tf32 = 32 bytes along the swizzled row
-                mma_tf32(tmem, dal + step, dbh + step, idesc, (kb | j) != 0);
-                mma_tf32(tmem, dah + step, dbl + step, idesc, 1);
-                mma_tf32(tmem, dah + step, dbh + step, idesc, 1);
+            for (int j = 0; j < kBK / 16; ++j) {
+                const uint64_t step = uint64_t(j * 32) >> 4;  // 16 fp16 = 32 bytes along the swizzled row
+                const uint32_t acc = (kb | j) != 0;
+                mma_f16(d_cross, dal + step, dbh + step, idesc, acc);
+                mma_f16(d_cross, dah + step, dbl + step, idesc, 1);
+                mma_f16(d_main, dah + step, dbh + step, idesc, acc);
             }
             mma_commit(&empty[s]);
         }
@@ -468,30 +480,35 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     // Epilogue. The outcome is made CTA-uniform before anything that holds a barrier.
     if (!mbar_wait_bounded(accum, 0, wait_ns)) *failed = 1;
     __syncthreads();
-    const bool ok = *failed == 0;
-    // Once every CTA of the cluster is past its MMAs, every stage ring is idle and
-    // becomes a receive area: each thread pushes its TMEM lane (= tile row) into
-    // the owner CTA of that row, as this slice's block there.
-    if (splits > 1) cluster_sync();
+    bool ok = *failed == 0;
     const int rows_max = (kBM + splits - 1) / splits;
     const int slice_floats = rows_max * Cfg::kTileStride;
-    float* recv = reinterpret_cast<float*>(smem);
+    // phase 1: every CTA of the cluster can receive
+    if (splits > 1) cluster_wait();
     if (ok) {
+        // each thread moves its TMEM lane (= tile row), main + 2^-11 cross, into the
+        // row's owner as this slice's block there
         tmem_fence_after();
         const int row = warp * 32 + lane;
         const int owner = row_owner(row, splits);
         float* slot = recv + rank * slice_floats + (row - slice_row0(owner, splits)) * Cfg::kTileStride;
         const uint32_t remote = splits > 1 ? map_cluster(slot, uint32_t(owner)) : 0u;
+        const uint32_t remote_bar = splits > 1 ? map_cluster(recv_bar, uint32_t(owner)) : 0u;
+        const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
 #pragma unroll
         for (int c0 = 0; c0 < BN; c0 += 32) {
-            uint32_t r[32];
-            tmem_load32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c0), r);
+            uint32_t hm[32], hc[32];
+            tmem_load32(lane_base + uint32_t(c0), hm);
+            tmem_load32(lane_base + uint32_t(BN + c0), hc);
 #pragma unroll
             for (int v = 0; v < 8; ++v) {
-                const float4 x = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                             __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+                float f[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    f[e] = fmaf(__uint_as_float(hc[4 * v + e]), kSplitLoUnscale, __uint_as_float(hm[4 * v + e]));
+                const float4 x = make_float4(f[0], f[1], f[2], f[3]);
                 if (splits > 1)
-                    st_cluster(remote + uint32_t((c0 + 4 * v) * 4), x);
+                    st_async(remote + uint32_t((c0 + 4 * v) * 4), x, remote_bar);
                 else
                     *reinterpret_cast<float4*>(slot + c0 + 4 * v) = x;
             }
@@ -500,17 +517,26 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         raise_error(p.error, kErrTimeout);
     }
     tmem_fence_before();
-    // every slice's block has arrived (and the row inputs are visible)
-    if (splits > 1)
-        cluster_sync();
-    else
-        __syncthreads();
+    // tensor memory reads are done (and, unsplit, the tile rows and row inputs are visible)
+    __syncthreads();
     if (warp == 0) {
         tmem_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(uint32_t(Cfg::kTmemCols))
-                     : "memory");
+        tmem_dealloc(tmem, uint32_t(Cfg::kTmemCols));
+    }
+    if (splits > 1) {
+        // phase 2: this CTA's pushes are issued (waited before the exit, so no CTA
+        // leaves while a slice may still push into it)
+        cluster_arrive();
+        // every slice's block of this CTA's rows has landed
+        const bool got = mbar_wait_bounded(recv_bar, 0, wait_ns);
+        const bool all = __syncthreads_and(got) != 0;
+        if (ok && !all) {
+            if (threadIdx.x == 0) raise_error(p.error, kErrTimeout);
+            ok = false;
+        }
     }
     if (ok) epilogue_rows<BN, E>(p, recv, slice_floats, rows, m0, n0, r0, r1, splits);
+    if (splits > 1) cluster_wait();
 }
 
 // Clusters of each size (index = slices) that the device holds at once, per tile
@@ -524,10 +550,11 @@ cudaError_t launch_bn(const TcGemmMaps& maps, const TcGemmParams& p, cudaStream_
     using Cfg = TcConfig<BN>;
     static_assert(dynamic_smem<BN, E>() + 2048 /*static*/ <= 232448, "stage buffers exceed shared memory");
     const int tiles = (p.n / BN) * ((p.m + kBM - 1) / kBM);
-    const int kb = p.k / kBK;
-    // K slices: as many as keep every tile's cluster resident in one wave, at
-    // least 2 K blocks per slice, at most one portable cluster, no empty slice
-    int splits = std::max(1, std::min(kMaxSlices, kb / 2));
+    const int kb = (p.k + kBK - 1) / kBK;
+    // K slices (tiles with their own receive area only): as many as keep every
+    // tile's cluster resident in one wave, at most one portable cluster, no empty
+    // slice
+    int splits = Cfg::kOwnRecv ? std::max(1, std::min(kMaxSlices, kb)) : 1;
     while (splits > 1 && tiles > g_active_clusters[bn_index(BN)][splits]) --splits;
     while (splits > 1 && (splits - 1) * ((kb + splits - 1) / splits) >= kb) --splits;
     cudaLaunchConfig_t cfg{};
@@ -580,10 +607,10 @@ cudaError_t configure_bn() {
     return e;
 }
 
-// hi/lo split of a whole buffer (weights at upload, test inputs).
-__global__ void split_kernel(const float* x, float* hi, float* lo, size_t n) {
+// hi/lo split of a whole buffer (test inputs).
+__global__ void split_kernel(const float* x, __half* hi, __half* lo, size_t n) {
     for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
-        split_tf32(x[i], hi[i], lo[i]);
+        split_f16(x[i], hi[i], lo[i]);
 }
 
 }  // namespace
@@ -614,7 +641,7 @@ cudaError_t launch_e(const TcGemmMaps& maps, const TcGemmParams& p, Epilogue e, 
 
 cudaError_t launch_tc_gemm(const TcGemmMaps& maps, const TcGemmParams& p, Epilogue e, cudaStream_t stream) {
     if (p.m <= 0) return cudaSuccess;
-    if (p.k % kBK) return cudaErrorInvalidValue;
+    if (p.k <= 0 || p.k % 8) return cudaErrorInvalidValue;
     switch (p.bn == 0 ? 64 : p.bn) {
         case 64: return launch_e<64>(maps, p, e, stream);
         case 128: return launch_e<128>(maps, p, e, stream);
@@ -623,7 +650,7 @@ cudaError_t launch_tc_gemm(const TcGemmMaps& maps, const TcGemmParams& p, Epilog
     return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_split(const float* x, float* hi, float* lo, size_t n, cudaStream_t stream) {
+cudaError_t launch_split(const float* x, __half* hi, __half* lo, size_t n, cudaStream_t stream) {
     if (!n) return cudaSuccess;
     split_kernel<<<1184, 256, 0, stream>>>(x, hi, lo, n);
     return cudaGetLastError();

@@ -1,10 +1,10 @@
 // tcgen05 (5th-generation tensor core) building blocks shared by the kernels that
-// run TF32 matrix products on sm_100a: shared-memory operand descriptors for
-// K-major tiles in the 128-byte swizzled layout, the instruction descriptor of
-// kind::tf32 with an FP32 accumulator, MMA issue and commit, and tensor-memory
+// run matrix products on sm_100a: shared-memory operand descriptors for K-major
+// tiles in the 128-byte swizzled layout, the instruction descriptors of kind::tf32
+// and kind::f16 with an FP32 accumulator, MMA issue and commit, and tensor-memory
 // (TMEM) allocation and loads.
 //
-// Operand tiles: rows of 32 fp32 elements (128 bytes, one K block), 8-row groups
+// Operand tiles: rows of 128 bytes (32 fp32 or 64 fp16 elements, one K block), 8-row groups
 // of 1024 bytes; inside a group the 16-byte chunk c of row r sits at chunk
 // position c ^ (r % 8) (the layout the TMA engine writes for SWIZZLE_128B). A tile
 // starts on a 1024-byte boundary.
@@ -38,6 +38,23 @@ __device__ __forceinline__ uint32_t sw128_offset(int row, int chunk) {
 template <int M, int N>
 __host__ __device__ constexpr uint32_t umma_idesc_tf32() {
     return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+
+// Instruction descriptor of kind::f16 with FP16 A and B (format 0 @ bits 7, 10)
+// and an FP32 accumulator (1 @ bit 4), both K-major.
+template <int M, int N>
+__host__ __device__ constexpr uint32_t umma_idesc_f16() {
+    return (1u << 4) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+
+// D (TMEM) (+)= A . B^T, one K step of 16 fp16 elements (32 bytes of each operand
+// row); `accumulate` 0 overwrites.
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
 }
 
 // D (TMEM) (+)= A . B^T, one K step of 8 tf32 elements; `accumulate` 0 overwrites.
