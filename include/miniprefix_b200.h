@@ -186,7 +186,8 @@ int mp_cow_timing(mp_context* ctx, int32_t enabled);
 int mp_cow_elapsed(mp_context* ctx, float* milliseconds);
 
 /* C = A . B^T (a [m][k], b [n][k], c [m][n] row-major, device buffers) through the
- * 3xTF32 tcgen05 GEMM of the forward (Store epilogue, with the forward's split-K
+ * split-precision FP16 tcgen05 GEMM of the forward (each operand as FP16 halves,
+ * three products per useful one; Store epilogue, with the forward's split-K
  * choice: shapes with few output tiles run as K slices summed in slice order);
  * n a multiple of 64, k of 32. Allocates its own scratch and synchronises
  * `stream`: a test/tool entry, not the hot path. */

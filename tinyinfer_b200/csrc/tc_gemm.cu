@@ -80,8 +80,25 @@ struct TcConfig {
     // two accumulators of BN columns: A_hi.B_hi, then the cross terms
     static constexpr int kTmemCols = 2 * BN;
 };
+// AddTo at 64-wide tiles (the O and down projections) fetches its rows of the
+// residual and the norm weights into shared memory while the MMAs run: a residual
+// read issued only in the epilogue waited several microseconds for the data.
 template <int BN, Epilogue E>
-constexpr int dynamic_smem() { return TcConfig<BN>::kSmem; }
+__host__ __device__ constexpr bool prefetch_residual() { return E == Epilogue::AddTo && BN == 64; }
+template <int BN>
+constexpr int kResidStride = BN + 4;  // floats per prefetched residual row (bank spread)
+template <int BN, Epilogue E>
+__host__ __device__ constexpr int resid_bytes() { return prefetch_residual<BN, E>() ? (kBM * kResidStride<BN> + BN) * 4 : 0; }
+template <int BN, Epilogue E>
+constexpr int dynamic_smem() { return TcConfig<BN>::kSmem + resid_bytes<BN, E>(); }
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 
 // Rows [slice_row0(r), slice_row0(r + 1)) of a tile are reduced and stored by
 // cluster rank r; row_owner is the inverse.
@@ -105,6 +122,11 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 // Split cluster barrier: every thread of every CTA of the cluster arrives, then
 // waits for all arrivals of that phase.
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+// Arrival that orders no memory: the exit barrier only keeps a CTA alive while a
+// slice may still push into it (the pushed bytes are tracked by its mbarrier).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 // Address of the same shared-memory offset in cluster CTA `rank` (its own included).
@@ -182,6 +204,8 @@ struct RowInputs {
     float* scale;  // RMSNorm 1 / rms (SwiGLU, Rope with ssq_in)
     float** dst;   // Rope: destination of the tile's head
     int* pos;      // Rope: cos / sin table row
+    float* resid;  // AddTo (prefetch_residual): rows [r0, r1) of c's tile, kResidStride apart
+    float* norm;   // AddTo (prefetch_residual): the tile's BN norm weights
 };
 
 // Gathers RowInputs with `threads` threads (thread index t); runs beside the MMAs.
@@ -189,6 +213,19 @@ template <int BN, Epilogue E>
 __device__ __forceinline__ void epilogue_rows_prepare(const TcGemmParams& p, const RowInputs& in, int m0, int n0,
                                                       int r0, int r1, int t, int threads) {
     constexpr bool kPairs = E == Epilogue::SwiGLU || E == Epilogue::Rope;
+    if constexpr (prefetch_residual<BN, E>()) {
+        // 16-byte copies, not waited for here: the threads wait just before the epilogue
+        constexpr int kChunks = BN / 4;
+        for (int i = t; i < (r1 - r0) * kChunks; i += threads) {
+            const int lr = i / kChunks, c = i % kChunks;
+            if (m0 + r0 + lr < p.m)
+                cp_async16(in.resid + lr * kResidStride<BN> + 4 * c,
+                           p.c + size_t(m0 + r0 + lr) * p.ldc + n0 + 4 * c);
+        }
+        if (p.norm_w != nullptr)
+            for (int c = t; c < kChunks; c += threads) cp_async16(in.norm + 4 * c, p.norm_w + n0 + 4 * c);
+        cp_async_commit();
+    }
     if (kPairs && p.ssq_in != nullptr) {
         // this CTA's rows' 1 / rms from the producer's per-64-column sums of
         // squares, summed in group order
@@ -255,8 +292,13 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
             } else if (!kSwiGLU) {
                 dst[u] = reinterpret_cast<float4*>(p.c + size_t(m0 + r0 + lr) * p.ldc + n0 + 4 * it);
                 if (E == Epilogue::AddTo && live[u]) {
-                    resid[u] = *dst[u];
-                    if (produce) wn[u] = *reinterpret_cast<const float4*>(p.norm_w + n0 + 4 * it);
+                    if constexpr (prefetch_residual<BN, E>()) {
+                        resid[u] = *reinterpret_cast<const float4*>(in.resid + lr * kResidStride<BN> + 4 * it);
+                        if (produce) wn[u] = *reinterpret_cast<const float4*>(in.norm + 4 * it);
+                    } else {
+                        resid[u] = *dst[u];
+                        if (produce) wn[u] = *reinterpret_cast<const float4*>(p.norm_w + n0 + 4 * it);
+                    }
                 }
             }
         }
@@ -286,7 +328,8 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
                                             __fmul_rn(acc[u][h].z, sc), __fmul_rn(acc[u][h].w, sc));
             }
         }
-        float sq[kUnroll];  // producer: sum of squares of the item's 4 new values
+        float sq[kUnroll];     // producer: sum of squares of the item's 4 new values
+        float4 sum[kUnroll];   // AddTo: residual + product
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             sq[u] = 0.f;
@@ -324,15 +367,8 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
                     const float4 x = resid[u];
                     const float4 y = make_float4(__fadd_rn(x.x, a.x), __fadd_rn(x.y, a.y), __fadd_rn(x.z, a.z),
                                                  __fadd_rn(x.w, a.w));
-                    *dst[u] = y;
+                    sum[u] = y;
                     if (produce) {
-                        // the next GEMM's A operand: y * norm weight as FP16 halves
-                        const int col = n0 + 4 * it;
-                        const float4 w = wn[u];
-                        const size_t at = size_t(m0 + row) * p.ld_out + col;
-                        store_split4(p.out_hi + at, p.out_lo + at,
-                                     make_float4(__fmul_rn(y.x, w.x), __fmul_rn(y.y, w.y), __fmul_rn(y.z, w.z),
-                                                 __fmul_rn(y.w, w.w)));
                         float q = __fmul_rn(y.x, y.x);
                         q = fmaf(y.y, y.y, q);
                         q = fmaf(y.z, y.z, q);
@@ -356,6 +392,25 @@ __device__ __forceinline__ void epilogue_rows(const TcGemmParams& p, const float
                 if (live[u] && it % 16 == 0) p.ssq_out[size_t(m0 + row) * (p.n / kSsqGroup) + (n0 + 4 * it) / kSsqGroup] = q;
             }
         }
+        // AddTo: the residual sums (and, producing, the next GEMM's A operand y * norm
+        // weight as FP16 halves) are stored after the row sums of squares are reduced
+        if (E == Epilogue::AddTo) {
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                if (!live[u]) continue;
+                const float4 y = sum[u];
+                *dst[u] = y;
+                if (produce) {
+                    const int i = base + u * kThreads;
+                    const int row = r0 + i / kItems, it = i % kItems;
+                    const float4 w = wn[u];
+                    const size_t at = size_t(m0 + row) * p.ld_out + n0 + 4 * it;
+                    store_split4(p.out_hi + at, p.out_lo + at,
+                                 make_float4(__fmul_rn(y.x, w.x), __fmul_rn(y.y, w.y), __fmul_rn(y.z, w.z),
+                                             __fmul_rn(y.w, w.w)));
+                }
+            }
+        }
     }
 }
 
@@ -375,6 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* recv_bar = accum + 1;  // the slices' partial rows of this CTA's share have landed
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(recv_bar + 1);
     int* failed = reinterpret_cast<int*>(tmem_holder + 1);
+    float* resid_rows = reinterpret_cast<float*>(smem + Cfg::kData + 256);  // resid_bytes<BN, E>()
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
@@ -389,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ float row_scale[kBM];
     __shared__ float* row_dst[kBM];
     __shared__ int row_pos[kBM];
-    const RowInputs rows{row_scale, row_dst, row_pos};
+    const RowInputs rows{row_scale, row_dst, row_pos, resid_rows, resid_rows + kBM * kResidStride<BN>};
 
     if (warp == 0) tmem_alloc(tmem_holder, uint32_t(Cfg::kTmemCols));
     if (threadIdx.x == 32) {
@@ -526,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (splits > 1) {
         // phase 2: this CTA's pushes are issued (waited before the exit, so no CTA
         // leaves while a slice may still push into it)
-        cluster_arrive();
+        cluster_arrive_relaxed();
         // every slice's block of this CTA's rows has landed
         const bool got = mbar_wait_bounded(recv_bar, 0, wait_ns);
         const bool all = __syncthreads_and(got) != 0;
@@ -534,6 +590,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (threadIdx.x == 0) raise_error(p.error, kErrTimeout);
             ok = false;
         }
+    }
+    if constexpr (prefetch_residual<BN, E>()) {
+        // the residual rows that warps 2-3 requested are in shared memory
+        if (warp >= 2) cp_async_commit_wait_all();
+        __syncthreads();
     }
     if (ok) epilogue_rows<BN, E>(p, recv, slice_floats, rows, m0, n0, r0, r1, splits);
     if (splits > 1) cluster_wait();
