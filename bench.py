@@ -121,11 +121,18 @@ def tf32_peak(device_index):
 
 
 # ----------------------------------------------------------------------------- workload
+# Decode steps run after the timed ones with CUDA events around every attention
+# launch and the LM head: the per-kernel breakdown of the roofline lines. They are
+# not timed into `value`: an event recorded between two kernels ends programmatic
+# dependent launch at that boundary (about 6% of a config-3 step with 61 of them).
+PROFILED_STEPS = 3
+
+
 def max_new_tokens(args):
-    """Enough new tokens that no request finishes before the timed steps end: the
+    """Enough new tokens that no request finishes before the profiled steps end: the
     followers that start decoding first run ahead by up to the prefill steps."""
     prefill_steps = -(-args.requests * (args.prompt - args.shared) // args.prefill_budget)
-    return args.warmup + args.steps + prefill_steps + 8
+    return args.warmup + args.steps + PROFILED_STEPS + prefill_steps + 8
 
 
 def model_config(args):
@@ -442,9 +449,6 @@ def run_b200(args, rank, world, local_rank):
     before = dev.counters(reset=True)
     # kernels launched before the timed steps (for `ncu -s` on this command)
     print(f"launches_before_timed={before['kernel_launches']}", file=sys.stderr, flush=True)
-    dev.profile_read()
-    dev.profile_read_gemm()
-    dev.profile(True)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
@@ -463,8 +467,15 @@ def run_b200(args, rank, world, local_rank):
         torch.cuda.cudart().cudaProfilerStop()
     dev.sync()
     torch.cuda.synchronize()
-    dev.profile(False)
     counters = dev.counters(reset=True)
+    # per-kernel breakdown: a few more decode steps with events around the kernels
+    dev.profile_read()
+    dev.profile_read_gemm()
+    dev.profile(True)
+    for _ in range(PROFILED_STEPS):
+        decode_step()
+    dev.sync()
+    dev.profile(False)
     attn_ms, attn_launches, attn_bytes = dev.profile_read()
     gemm_ms, gemm_intervals, head_ms, heads = dev.profile_read_gemm()
     record["final"] = {"step_stats": engine.last_step_stats(), "runner_stats": engine.runner_stats(),
@@ -544,6 +555,10 @@ def run_b200(args, rank, world, local_rank):
         "roofline": {"bound": "hbm",
                      "kernel": "paged_attention_kernel: split-K decode attention of every row over its whole "
                                "context; the shared prefix pages are read by all rows, from DRAM once and then L2",
+                     "timing": f"CUDA events around each attention launch on the context stream, over "
+                               f"{PROFILED_STEPS} decode steps run right after the timed ones (events between "
+                               f"kernels end programmatic dependent launch there, so these durations are upper "
+                               f"bounds of the timed steps' launches)",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm if achieved else None, "traffic": traffic,
                      "traffic_source": traffic_source,
@@ -551,7 +566,8 @@ def run_b200(args, rank, world, local_rank):
                      "algorithmic_bytes_per_launch": bytes_per_launch,
                      "logical_bytes_per_launch": logical,
                      "logical_achieved": logical / (launch_ms * 1e-3) / 1e9 if launch_ms > 0 else None,
-                     "attention_share_of_forward": attn_ms / device_ms if device_ms else None},
+                     "attention_share_of_forward": (attn_ms / PROFILED_STEPS) / (device_ms / args.steps)
+                     if device_ms else None},
         "gemm_roofline": gemm_roofline(cfg, n, gemm_ms, gemm_intervals, head_ms, heads),
         "clocks": clocks.summary(),
         "_record": record,

@@ -180,16 +180,21 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 template <Epilogue E>
 __host__ __device__ constexpr int epilogue_unroll() { return E == Epilogue::SwiGLU || E == Epilogue::Rope ? 2 : 4; }
 
-// Destination of head `head` (0..14) of batch row `grow` for the Rope epilogue:
-// the q row, or the K/V page slot (nullptr and an error bit when the row's page
-// is outside its table or the pool).
-__device__ __forceinline__ float* rope_destination(const TcGemmParams& p, int head, int grow) {
+// Physical page of position `pos` of table slot `slot` (-1 past the table or the
+// context).
+__device__ __forceinline__ int rope_block(const TcGemmParams& p, int slot, int pos) {
+    const RopeEpilogue& r = p.rope;
+    const int page = pos / r.block_tokens;
+    if (page < r.table_stride && pos < r.max_position) return r.tables[size_t(slot) * r.table_stride + page];
+    return -1;
+}
+
+// Destination of head `head` (0..14) of batch row `grow` at position `pos` in page
+// `block` for the Rope epilogue: the q row, or the K/V page slot (nullptr and an
+// error bit when the row's page is outside its table or the pool).
+__device__ __forceinline__ float* rope_destination(const TcGemmParams& p, int head, int grow, int pos, int block) {
     const RopeEpilogue& r = p.rope;
     if (head < kHeads) return r.q + size_t(grow) * r.q_stride + head * kHeadDim;
-    const int pos = r.row_pos[grow];
-    const int page = pos / r.block_tokens;
-    int block = -1;
-    if (page < r.table_stride && pos < r.max_position) block = r.tables[size_t(r.row_slot[grow]) * r.table_stride + page];
     if (block < 0 || block >= r.max_blocks) {
         raise_error(p.error, kErrBounds);
         return nullptr;
@@ -226,25 +231,70 @@ __device__ __forceinline__ void epilogue_rows_prepare(const TcGemmParams& p, con
             for (int c = t; c < kChunks; c += threads) cp_async16(in.norm + 4 * c, p.norm_w + n0 + 4 * c);
         cp_async_commit();
     }
+    // Two rows per thread and pass; every global load of a pass is requested before
+    // any of them is used, so a pass costs one round trip (two for Rope's table
+    // entries) instead of one per value -- these gathers run beside the MMAs and
+    // must not outlast them.
     if (kPairs && p.ssq_in != nullptr) {
         // this CTA's rows' 1 / rms from the producer's per-64-column sums of
         // squares, summed in group order
         const int groups = p.k / kSsqGroup;
-        for (int r = r0 + t; r < r1; r += threads) {
-            float ss = 0.f;
-            if (m0 + r < p.m)
-                for (int g = 0; g < groups; ++g) ss = __fadd_rn(ss, p.ssq_in[size_t(m0 + r) * groups + g]);
-            in.scale[r - r0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(p.k)), p.eps)));
+        constexpr int kMaxGroups = 16;
+        for (int base = r0 + t; base < r1; base += 2 * threads) {
+            if (groups <= kMaxGroups) {
+                float v[2][kMaxGroups];
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    const int r = base + b * threads;
+                    const bool live = r < r1 && m0 + r < p.m;
+#pragma unroll
+                    for (int g = 0; g < kMaxGroups; ++g)
+                        v[b][g] = live && g < groups ? p.ssq_in[size_t(m0 + r) * groups + g] : 0.f;
+                }
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    const int r = base + b * threads;
+                    if (r >= r1) continue;
+                    float ss = 0.f;
+#pragma unroll
+                    for (int g = 0; g < kMaxGroups; ++g)
+                        if (g < groups) ss = __fadd_rn(ss, v[b][g]);
+                    in.scale[r - r0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(p.k)), p.eps)));
+                }
+            } else {
+                for (int b = 0; b < 2; ++b) {
+                    const int r = base + b * threads;
+                    if (r >= r1) continue;
+                    float ss = 0.f;
+                    if (m0 + r < p.m)
+                        for (int g = 0; g < groups; ++g) ss = __fadd_rn(ss, p.ssq_in[size_t(m0 + r) * groups + g]);
+                    in.scale[r - r0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(p.k)), p.eps)));
+                }
+            }
         }
     }
     if constexpr (E == Epilogue::Rope) {
         const int head = n0 / 64;
-        for (int r = r0 + t; r < r1; r += threads) {
-            in.dst[r - r0] = nullptr;
-            in.pos[r - r0] = 0;
-            if (m0 + r >= p.m) continue;
-            in.dst[r - r0] = rope_destination(p, head, m0 + r);
-            if (head < kHeads + kKvHeads) in.pos[r - r0] = min(p.rope.row_pos[m0 + r], p.rope.max_position - 1);
+        const bool kv = head >= kHeads;
+        for (int base = r0 + t; base < r1; base += 2 * threads) {
+            bool live[2];
+            int pos[2], slot[2], block[2];
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+                const int r = base + b * threads;
+                live[b] = r < r1 && m0 + r < p.m;
+                pos[b] = live[b] ? p.rope.row_pos[m0 + r] : 0;
+                slot[b] = live[b] && kv ? p.rope.row_slot[m0 + r] : 0;
+            }
+#pragma unroll
+            for (int b = 0; b < 2; ++b) block[b] = live[b] && kv ? rope_block(p, slot[b], pos[b]) : -1;
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+                const int r = base + b * threads;
+                if (r >= r1) continue;
+                in.dst[r - r0] = live[b] ? rope_destination(p, head, m0 + r, pos[b], block[b]) : nullptr;
+                in.pos[r - r0] = live[b] && head < kHeads + kKvHeads ? min(pos[b], p.rope.max_position - 1) : 0;
+            }
         }
     }
 }
