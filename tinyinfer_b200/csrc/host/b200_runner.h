@@ -15,6 +15,7 @@
 // writes, or belongs to a sequence that already has a pending append.
 #pragma once
 #include <map>
+#include <unordered_map>
 #include <memory>
 #include <string>
 #include <vector>
@@ -102,7 +103,7 @@ private:
     bool cost_timing_ = false;
     int table_stride_ = 0;
 
-    std::map<RequestId, int> slots_;
+    std::unordered_map<RequestId, int> slots_;
     std::vector<int> free_slots_;
     std::vector<int> quarantine_;              // freed while device work may still read them
     std::vector<std::vector<int>> mirror_;     // device-known table of each slot

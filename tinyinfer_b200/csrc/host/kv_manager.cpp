@@ -57,11 +57,14 @@ std::size_t KVManager::committed_blocks() const {
     return count;
 }
 
-void KVManager::touch_sequence(const RequestId& id, bool dropping) {
+void KVManager::touch_sequence(const RequestId& id, bool dropping, State* known) {
     if (!checkpoint_) return;
     auto& cp = *checkpoint_;
-    auto it = sequences_.find(id);
-    State* state = it != sequences_.end() ? &it->second : nullptr;
+    State* state = known;
+    if (!state) {
+        auto it = sequences_.find(id);
+        state = it != sequences_.end() ? &it->second : nullptr;
+    }
     std::size_t slot;
     if (state && state->saved_window == cp.window) {
         slot = state->saved_slot;
@@ -198,7 +201,8 @@ void KVManager::cache_prefix(const RequestId& id) {
 
 void KVManager::cache_prefix_deferred(const RequestId& id) {
     if (!checkpoint_) return cache_prefix(id);
-    auto& state = idle_state(id);
+    require_idle();
+    State& state = last_append_ && last_append_id_ == id ? *last_append_ : idle_state(id);
     // a publish that would fail fails here, where the caller made it
     if (state.publish_queued || state.sequence.tokens.size() != std::size_t(state.sequence.used))
         return cache_prefix(id);
@@ -209,10 +213,13 @@ void KVManager::cache_prefix_deferred(const RequestId& id) {
 void KVManager::settle_publishes() {
     // (not inside an append transaction: the queue waits for its end)
     if (pending_publishes_.empty() || append_active_) return;
-    std::vector<State*> queue;
-    queue.swap(pending_publishes_);
-    for (State* s : queue) s->publish_queued = false;
-    for (State* s : queue) publish(*s);  // a failure drops the rest, as it would end the step
+    settling_.swap(pending_publishes_);
+    struct Drop {  // a failure drops the rest, as it would end the step
+        std::vector<State*>& v;
+        ~Drop() { v.clear(); }
+    } drop{settling_};
+    for (State* s : settling_) s->publish_queued = false;
+    for (State* s : settling_) publish(*s);
 }
 
 // A queued publish changes the prefix index, leases (page references) and LRU
@@ -275,7 +282,7 @@ KVManager::Append::Append(KVManager& owner, const RequestId& id, const std::vect
     if (tokens.empty() || tokens.size() > std::size_t(owner.context_ - sequence.used))
         throw std::invalid_argument("context overflow/empty input");
     owner.validate_tokens(tokens);
-    owner.touch_sequence(id);
+    owner.touch_sequence(id, false, state_);
     // room for the commit up front (commit must not allocate); grow geometrically,
     // an exact reserve would copy the whole history on every decode append
     const std::size_t need = std::size_t(sequence.used) + tokens.size();
@@ -328,6 +335,8 @@ void KVManager::Append::commit() {
     if (copy_) owner_->pool_.unref(copy_->source);
     state_->appending = false;
     owner_->append_active_ = false;
+    owner_->last_append_ = state_;
+    owner_->last_append_id_ = id_;
     owner_ = nullptr;
 }
 
@@ -359,6 +368,7 @@ void KVManager::release(const RequestId& id) {
     touch_sequence(id, true);
     touch_reservation(id);
     pool_.release(it->second.sequence);
+    last_append_ = nullptr;
     sequences_.erase(it);
     auto r = reservations_.find(id);
     if (r != reservations_.end()) {
@@ -376,6 +386,7 @@ void KVManager::clear() {
         touch_sequence(item.first, true);
         pool_.release(item.second.sequence);
     }
+    last_append_ = nullptr;
     sequences_.clear();
     prefix_.clear();
     for (const auto& r : reservations_) touch_reservation(r.first);
@@ -408,7 +419,7 @@ KvStats KVManager::stats() const {
 void KVManager::begin_checkpoint() {
     settle_publishes();
     require_idle();
-    checkpoint_ = std::make_unique<Checkpoint>();
+    checkpoint_ = spare_checkpoint_ ? std::move(spare_checkpoint_) : std::make_unique<Checkpoint>();
     checkpoint_->window = ++windows_;
     checkpoint_->live = pool_.live_blocks();
     checkpoint_->peak = pool_.peak_blocks();
@@ -424,6 +435,7 @@ void KVManager::restore_checkpoint() {
     for (State* s : pending_publishes_) s->publish_queued = false;
     pending_publishes_.clear();  // never applied: nothing of them to undo
     auto& cp = *checkpoint_;
+    last_append_ = nullptr;
     pool_.attach_journal(nullptr);
     pool_.undo(cp.pool_journal, 0, cp.live, cp.peak);
     prefix_.rollback_journal();
@@ -452,14 +464,20 @@ void KVManager::restore_checkpoint() {
     forward_tokens_ = cp.forward_tokens;
     costs_ = cp.costs;
     append_active_ = false;
-    checkpoint_.reset();
+    close_checkpoint();
+}
+
+void KVManager::close_checkpoint() {
+    if (!checkpoint_) return;
+    checkpoint_->recycle();
+    spare_checkpoint_ = std::move(checkpoint_);
 }
 
 void KVManager::end_checkpoint() {
     settle_publishes();
     pool_.attach_journal(nullptr);
     prefix_.end_journal();
-    checkpoint_.reset();
+    close_checkpoint();
 }
 
 }  // namespace miniprefix_b200

@@ -126,7 +126,8 @@ private:
     void validate_tokens(const std::vector<TokenId>& tokens) const;
     std::size_t committed_blocks() const;
     void reserve_pages(const RequestId& id, PagedSequence& sequence, int end, bool& cow);
-    void touch_sequence(const RequestId& id, bool dropping = false);  // journal a sequence mutation
+    // journal a sequence mutation; `known` is id's State when the caller has it
+    void touch_sequence(const RequestId& id, bool dropping = false, State* known = nullptr);
     void touch_reservation(const RequestId& id);
     void publish(State& state);
     bool commutes_with_publishes(const State& state, std::size_t tokens) const;
@@ -138,7 +139,7 @@ private:
     KvBlockPool pool_;
     ExactPrefixCache prefix_;
     std::map<RequestId, State> sequences_;
-    std::map<RequestId, std::size_t> reservations_;
+    std::unordered_map<RequestId, std::size_t> reservations_;
     std::size_t reserved_pages_ = 0;  // sum of reservations_
     std::size_t forward_tokens_ = 0;
     bool append_active_ = false;
@@ -147,6 +148,12 @@ private:
     // Queued publishes, in call order. A queued sequence is never erased: every
     // operation that can erase one settles or (restore) drops the queue first.
     std::vector<State*> pending_publishes_;
+    std::vector<State*> settling_;  // the queue being applied (keeps its capacity)
+    // the sequence of the last committed append (its id is the map key), so that
+    // the publish that follows an append finds it without a lookup; cleared when
+    // any sequence is erased
+    State* last_append_ = nullptr;
+    RequestId last_append_id_;
 
     // A sequence as it was at the checkpoint. Tokens only grow inside a window
     // unless the sequence is released, so only their count is kept until then.
@@ -174,8 +181,17 @@ private:
         std::map<RequestId, std::optional<std::size_t>> reservations;  // nullopt: did not exist
         std::size_t reserved_pages = 0, forward_tokens = 0;
         CostStats costs;
+        // empties the journals, keeping their storage for the next window
+        void recycle() {
+            pool_journal.clear();
+            sequences.clear();
+            stateless.clear();
+            reservations.clear();
+        }
     };
     std::unique_ptr<Checkpoint> checkpoint_;
+    std::unique_ptr<Checkpoint> spare_checkpoint_;  // a closed window's storage, reused by the next
+    void close_checkpoint();
     std::uint64_t windows_ = 0;  // checkpoint windows opened so far
 };
 

@@ -414,14 +414,18 @@ class Engine(_Base):
         return events
 
     def poll_compact(self, capacity=1 << 16):
-        req = np.empty(capacity, dtype=np.int32)
-        tok = np.empty(capacity, dtype=np.int32)
-        rea = np.empty(capacity, dtype=np.int32)
-        n = self.lib.mph_engine_poll_compact(self.h, req.ctypes.data_as(C.c_void_p), tok.ctypes.data_as(C.c_void_p),
-                                             rea.ctypes.data_as(C.c_void_p), capacity)
+        """The pending events as three int32 arrays (request index, token or -1,
+        finish reason or -1). The receive buffers are allocated once per engine and
+        capacity; the returned arrays are copies."""
+        bufs = getattr(self, "_poll_bufs", None)
+        if bufs is None or bufs[0] != capacity:
+            arrays = [np.empty(capacity, dtype=np.int32) for _ in range(3)]
+            bufs = self._poll_bufs = (capacity, arrays, [C.c_void_p(a.ctypes.data) for a in arrays])
+        _, (req, tok, rea), ptrs = bufs
+        n = self.lib.mph_engine_poll_compact(self.h, ptrs[0], ptrs[1], ptrs[2], capacity)
         if n > capacity:
             raise RuntimeError("more events than capacity")
-        return req[:n], tok[:n], rea[:n]
+        return req[:n].copy(), tok[:n].copy(), rea[:n].copy()
 
     def cancel(self, id):
         self.check(self.lib.mph_engine_cancel(self.h, _ids(id)))
