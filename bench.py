@@ -467,6 +467,8 @@ def run_b200(args, rank, world, local_rank):
         torch.cuda.cudart().cudaProfilerStop()
     dev.sync()
     torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
     counters = dev.counters(reset=True)
     # per-kernel breakdown: a few more decode steps with events around the kernels
     dev.profile_read()
