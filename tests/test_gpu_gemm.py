@@ -71,3 +71,28 @@ def test_tc_gemm_split_k_is_deterministic(built, m, n, k):
     one = torch.empty((1, n), device=dev)
     device.gemm_f32(ta[:1].contiguous().data_ptr(), tb.data_ptr(), one.data_ptr(), 1, n, k, stream)
     assert np.array_equal(one.cpu().numpy()[0].view(np.uint32), runs[0][0].view(np.uint32))
+
+
+@pytest.mark.gpu
+def test_tc_gemm_operand_beyond_fp16_range_is_loud(built):
+    """The split stores every operand as FP16 halves; a value beyond FP16's range
+    (65504) becomes infinite instead of losing accuracy silently, so the products
+    of its row come out nonfinite (in the forward, nonfinite logits fail the step).
+    Rows without such a value are unaffected."""
+    import torch
+    from tinyinfer_b200 import device
+
+    m, n, k = 4, 64, 64
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    b = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float32)
+    a[1, 7] = 1.0e5
+    dev = torch.device("cuda:0")
+    ta, tb = torch.from_numpy(a).to(dev), torch.from_numpy(b).to(dev)
+    tc = torch.zeros((m, n), device=dev)
+    device.gemm_f32(ta.data_ptr(), tb.data_ptr(), tc.data_ptr(), m, n, k, torch.cuda.current_stream().cuda_stream)
+    got = tc.cpu().numpy()
+    assert not np.isfinite(got[1]).any()
+    exact = a.astype(np.float64) @ b.astype(np.float64).T
+    for r in (0, 2, 3):
+        assert np.allclose(got[r], exact[r], rtol=1e-5, atol=1e-5)

@@ -32,16 +32,18 @@
 //    (cluster dims 1 x 1 x slices) and each CTA owns a contiguous share of the
 //    tile's rows. As soon as its own accumulators are final, each thread reads its
 //    TMEM lane (= tile row) with tcgen05.ld.32x32b, combines the two sums, and
-//    stores the row into the receive area of the row's owner CTA with st.async
-//    (this slice's block there), completing bytes on the owner's receive
-//    mbarrier. The owner waits on that barrier alone -- no cluster-wide barrier
-//    separates the MMAs from the push -- then sums its rows over the slices'
-//    blocks in slice order (deterministic split-K for the small-M decode GEMMs, no
-//    global round trip and no remote loads) and applies the fused epilogue with
-//    coalesced row-contiguous stores. Two split cluster barriers remain off the
-//    critical path: one whose arrival follows the barrier set-up at the start and
-//    whose wait precedes the first push, and one whose arrival follows the pushes
-//    and whose wait precedes the exit.
+//    writes the row into a staging copy of the tile in the (now idle) stage ring;
+//    one thread then sends each owner CTA its rows with one bulk shared-to-shared
+//    copy (cp.async.bulk.shared::cluster, this slice's block in the owner's
+//    receive area), completing bytes on the owner's receive mbarrier. The owner
+//    waits on that barrier alone -- no cluster-wide barrier separates the MMAs
+//    from the push -- then sums its rows over the slices' blocks in slice order
+//    (deterministic split-K for the small-M decode GEMMs, no global round trip and
+//    no remote loads) and applies the fused epilogue with coalesced row-contiguous
+//    stores. Two split cluster barriers remain off the critical path: one whose
+//    arrival follows the barrier set-up at the start and whose wait precedes the
+//    first copy, and one whose arrival follows the copies and whose wait precedes
+//    the exit.
 // Every mbarrier wait is bounded; a timeout sets the error word, and the CTA still
 // passes both cluster barriers and releases its tensor memory.
 #include <cuda.h>
@@ -136,15 +138,18 @@ __device__ __forceinline__ uint32_t map_cluster(const void* local, uint32_t rank
     return remote;
 }
 
-// 16 bytes into a cluster CTA's shared memory at `addr`, completing their
-// transaction bytes on that CTA's mbarrier at `bar` (both shared::cluster
-// addresses of the same CTA).
-__device__ __forceinline__ void st_async(uint32_t addr, float4 v, uint32_t bar) {
-    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
-                     addr),
-                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar)
+// Bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory to a
+// cluster CTA's shared memory at `dst`, completing its bytes on that CTA's
+// mbarrier at `bar` (dst and bar: shared::cluster addresses of the same CTA).
+__device__ __forceinline__ void bulk_copy_s2c(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst),
+                 "r"(smem_u32(src)), "r"(bytes), "r"(bar)
                  : "memory");
 }
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk copy of this thread has read its source.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
 // g / (1 + exp(-g)) * u (miniprefix/src/backend/cpu/llama_runner.cpp:97). The
 // reciprocal of d = 1 + exp(-g) >= 1 is the hardware approximation refined by one
@@ -474,6 +479,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* recv = reinterpret_cast<float*>(smem + (Cfg::kOwnRecv ? Cfg::kRing : 0));
+    // split K: the tile's combined rows are staged in the stage ring (idle once the
+    // accumulators are final) for the bulk copies to their owners
+    float* stage_rows = reinterpret_cast<float*>(smem);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kData);
     uint64_t* empty = full + S;
     uint64_t* accum = empty + S;
@@ -505,8 +513,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(accum, 1);
         mbar_init(recv_bar, 1);
-        // every slice (this one included) sends (r1 - r0) rows of BN floats
-        if (splits > 1) mbar_arrive_expect_tx(recv_bar, uint32_t(splits * (r1 - r0) * BN) * 4u);
+        // every slice (this one included) sends (r1 - r0) rows of kTileStride floats
+        if (splits > 1) mbar_arrive_expect_tx(recv_bar, uint32_t(splits * (r1 - r0) * Cfg::kTileStride) * 4u);
         *failed = 0;
         fence_barrier_init();
     }
@@ -592,14 +600,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // phase 1: every CTA of the cluster can receive
     if (splits > 1) cluster_wait();
     if (ok) {
-        // each thread moves its TMEM lane (= tile row), main + 2^-11 cross, into the
-        // row's owner as this slice's block there
+        // each thread moves its TMEM lane (= tile row), main + 2^-11 cross: unsplit
+        // straight into the receive area; split, into a staging copy of the tile in
+        // the idle stage ring, from which one bulk copy per owner CTA sends that
+        // owner's rows as this slice's block there
         tmem_fence_after();
         const int row = warp * 32 + lane;
-        const int owner = row_owner(row, splits);
-        float* slot = recv + rank * slice_floats + (row - slice_row0(owner, splits)) * Cfg::kTileStride;
-        const uint32_t remote = splits > 1 ? map_cluster(slot, uint32_t(owner)) : 0u;
-        const uint32_t remote_bar = splits > 1 ? map_cluster(recv_bar, uint32_t(owner)) : 0u;
+        float* slot = (splits > 1 ? stage_rows : recv) + row * Cfg::kTileStride;
         const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
 #pragma unroll
         for (int c0 = 0; c0 < BN; c0 += 32) {
@@ -612,13 +619,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
                     f[e] = fmaf(__uint_as_float(hc[4 * v + e]), kSplitLoUnscale, __uint_as_float(hm[4 * v + e]));
-                const float4 x = make_float4(f[0], f[1], f[2], f[3]);
-                if (splits > 1)
-                    st_async(remote + uint32_t((c0 + 4 * v) * 4), x, remote_bar);
-                else
-                    *reinterpret_cast<float4*>(slot + c0 + 4 * v) = x;
+                *reinterpret_cast<float4*>(slot + c0 + 4 * v) = make_float4(f[0], f[1], f[2], f[3]);
             }
         }
+        // the staged rows are read by the bulk-copy engine (async proxy)
+        if (splits > 1) fence_proxy_async_shared();
     } else if (threadIdx.x == 0) {
         raise_error(p.error, kErrTimeout);
     }
@@ -630,8 +635,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_dealloc(tmem, uint32_t(Cfg::kTmemCols));
     }
     if (splits > 1) {
-        // phase 2: this CTA's pushes are issued (waited before the exit, so no CTA
-        // leaves while a slice may still push into it)
+        if (ok && threadIdx.x == 0) {
+            // owner j's rows [slice_row0(j), slice_row0(j + 1)) are contiguous in the
+            // staging copy, at the stride of the receive area
+            for (int j = 0; j < splits; ++j) {
+                const int a = slice_row0(j, splits), b = slice_row0(j + 1, splits);
+                bulk_copy_s2c(map_cluster(recv + rank * slice_floats, uint32_t(j)), stage_rows + a * Cfg::kTileStride,
+                              uint32_t((b - a) * Cfg::kTileStride) * 4u, map_cluster(recv_bar, uint32_t(j)));
+            }
+            bulk_commit();
+        }
+        // phase 2: this CTA's copies are issued (waited before the exit, so no CTA
+        // leaves while a slice may still copy into it)
         cluster_arrive_relaxed();
         // every slice's block of this CTA's rows has landed
         const bool got = mbar_wait_bounded(recv_bar, 0, wait_ns);
@@ -647,7 +662,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncthreads();
     }
     if (ok) epilogue_rows<BN, E>(p, recv, slice_floats, rows, m0, n0, r0, r1, splits);
-    if (splits > 1) cluster_wait();
+    if (splits > 1) {
+        if (threadIdx.x == 0) bulk_wait_read_all();  // the staging copy is read before the CTA ends
+        cluster_wait();
+    }
 }
 
 // Clusters of each size (index = slices) that the device holds at once, per tile
@@ -660,6 +678,7 @@ template <int BN, Epilogue E>
 cudaError_t launch_bn(const TcGemmMaps& maps, const TcGemmParams& p, cudaStream_t stream) {
     using Cfg = TcConfig<BN>;
     static_assert(dynamic_smem<BN, E>() + 2048 /*static*/ <= 232448, "stage buffers exceed shared memory");
+    static_assert(!Cfg::kOwnRecv || Cfg::kRing >= kBM * Cfg::kTileStride * 4, "split-K staging exceeds the ring");
     const int tiles = (p.n / BN) * ((p.m + kBM - 1) / kBM);
     const int kb = (p.k + kBK - 1) / kBK;
     // K slices (tiles with their own receive area only): as many as keep every
