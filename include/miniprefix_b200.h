@@ -42,8 +42,11 @@ typedef struct {
 
 /* Paged KV pool and step capacities. block_tokens / max_blocks are
  * KvCacheConfig's (miniprefix/include/miniprefix/paged_kv.h:13-17); each of the K
- * and V pools holds max_blocks * layers * block_tokens * kv_width floats in the
- * reference layout [block][layer][slot][kv_width] (paged_kv.h:25-27). */
+ * and V pools holds max_blocks * layers * block_tokens * kv_width floats. On the
+ * device a pool is layer-major, [layer][block][slot][kv_width], so that one layer's
+ * pages share a compact address range; every pool offset this API takes (COW
+ * regions, mp_kv_read / mp_kv_write) is an offset in the reference layout
+ * [block][layer][slot][kv_width] (paged_kv.h:25-27) and is translated. */
 typedef struct {
     int32_t block_tokens;
     int32_t max_blocks;
@@ -129,10 +132,11 @@ int mp_inject_wait_timeout(mp_context* ctx, int32_t wait_us);
 /* Waits for all queued work with a bounded host wait (event polling). */
 int mp_sync(mp_context* ctx, int32_t timeout_ms);
 
-/* Device pointers of the K and V pools and their element count (tests, tools). */
+/* Device pointers of the K and V pools (layer-major, see mp_runtime_config) and
+ * their element count (tests, tools). */
 int mp_kv_pools(mp_context* ctx, float** keys, float** values, uint64_t* elements);
 /* Synchronous host copies of pool payload (0 = K pool, 1 = V pool), element
- * offsets; for tests and tools that inspect or seed pages. */
+ * offsets in the reference layout; for tests and tools that inspect or seed pages. */
 int mp_kv_read(mp_context* ctx, int32_t pool, uint64_t offset, uint64_t count, float* host);
 int mp_kv_write(mp_context* ctx, int32_t pool, uint64_t offset, uint64_t count, const float* host);
 /* The context stream as a cudaStream_t (void* here to keep the ABI CUDA-free). */

@@ -129,6 +129,65 @@ def test_cow_region_copies_both_pools(built):
     ctx.close()
 
 
+def apply_regions(pool, regions):
+    """Reference-layout effect of tail-copy regions applied as one step: every
+    source read, then every destination written (in region order)."""
+    out = pool.copy()
+    rows = [[pool[s + r * p:s + r * p + w].copy() for r in range(n)] for d, s, p, w, n in regions]
+    for (d, s, p, w, n), data in zip(regions, rows):
+        for r in range(n):
+            out[d + r * p:d + r * p + w] = data[r]
+    return out
+
+
+@pytest.mark.gpu
+def test_pool_offsets_are_reference_layout(built):
+    """The context's pools are layer-major on the device while mp_kv_read /
+    mp_kv_write and COW regions take reference-layout element offsets
+    ([block][layer][slot][192], miniprefix/include/miniprefix/paged_kv.h:25-27):
+    ranges that start and end inside pages round-trip, and regions whose rows
+    cross page boundaries (direct, and two-phase through a forward) copy exactly
+    the elements they name."""
+    ctx = device_for(MINI, random_weights(MINI, seed=3), 4, 8, max_sequences=2, max_step_tokens=8,
+                     max_step_sequences=2)
+    kvw, layers, bt = MINI.kv_width, MINI.layers, 4
+    _, _, n = ctx.pools()
+    page = bt * kvw
+    block = layers * page
+    assert n == 8 * block
+    rng = np.random.default_rng(5)
+    keys = rng.standard_normal(n).astype(np.float32)
+    ctx.kv_write(0, 0, keys)
+    ctx.kv_write(1, 0, -keys)
+    for off, cnt in [(0, n), (4, 100), (page - 8, 24), (block - 4, block + 8), (3 * page + 12, n - 3 * page - 12),
+                     (2 * block, 3 * block), (n - 4, 4)]:
+        assert np.array_equal(ctx.kv_read(0, off, cnt), keys[off:off + cnt]), (off, cnt)
+        assert np.array_equal(ctx.kv_read(1, off, cnt), -keys[off:off + cnt]), (off, cnt)
+    patch = rng.standard_normal(2 * page + 40).astype(np.float32)
+    at = page + 20
+    ctx.kv_write(0, at, patch)
+    ctx.kv_write(1, at, -patch)
+    keys[at:at + patch.size] = patch
+    assert np.array_equal(ctx.kv_read(0, 0, n), keys)
+    assert np.array_equal(ctx.kv_read(1, 0, n), -keys)
+    # direct copy: rows of 800 floats starting 16 floats before a page end
+    direct = [(5 * block + 8, block + page - 16, 2 * page, page + 32, 2)]
+    ctx.cow_copy(direct)
+    ctx.sync()
+    keys = apply_regions(keys, direct)
+    assert np.array_equal(ctx.kv_read(0, 0, n), keys)
+    assert np.array_equal(ctx.kv_read(1, 0, n), -keys)
+    # two-phase: the second region's source overlaps the first one's destination
+    chained = [(4 * block + 40, 2 * block + 700, block, 200, 2), (6 * block + 4, 4 * block + 100, block, 900, 2)]
+    ctx.table_write(0, 0, [0])
+    ctx.forward([(0, 0, 1)], [3], regions=chained, logits=False)
+    keys = apply_regions(keys, chained)
+    # block 0 holds the step's own K/V row
+    assert np.array_equal(ctx.kv_read(0, block, n - block), keys[block:])
+    assert np.array_equal(ctx.kv_read(1, block, n - block), -keys[block:])
+    ctx.close()
+
+
 @pytest.mark.gpu
 def test_forward_cow_chain_reads_sources_first(built):
     """The COW regions of one batched step apply as if every source were read

@@ -122,7 +122,7 @@ __device__ __forceinline__ void issue_stage(const AttnParams& p, const int32_t* 
             raise_error(p.error, kErrBounds);
             block = 0;  // stay in bounds; the error word fails the step
         }
-        const size_t src = ((size_t(block) * p.layers + p.layer) * bt + (run_begin - page * bt)) * kKvWidth;
+        const size_t src = (pool_page(block, p.page_stride, p.layer_offset) * bt + (run_begin - page * bt)) * kKvWidth;
         const uint32_t bytes = uint32_t(run_end - run_begin) * kKvWidth * sizeof(float);
         bulk_copy_g2s(kdst + (run_begin - a) * kKvWidth, p.keys + src, bytes, bar);
         bulk_copy_g2s(vdst + (run_begin - a) * kKvWidth, p.values + src, bytes, bar);
@@ -133,6 +133,16 @@ __device__ void producer(const AttnParams& p, float* stages, StageDesc* desc, ui
                          bool persistent, unsigned* failed, int lane) {
     uint32_t g = 0;  // stages issued so far
     const bool fixed = p.cta_items != nullptr;
+    // With early copies the schedule is read, and the first ring fill of stages
+    // below row_len - kPrefillMinRows is issued, before the programmatic wait.
+    bool waited = false;
+    auto enter = [&] {
+        if (!waited) {
+            pdl_enter();
+            waited = true;
+        }
+    };
+    if (!(fixed && p.early_copies)) enter();
     int item = fixed ? p.cta_items[blockIdx.x] : int(blockIdx.x);
     const int item_end = fixed ? p.cta_items[blockIdx.x + 1] : p.work_count;
     // a stage's previous use must have been released by the 3 consumers
@@ -142,6 +152,7 @@ __device__ void producer(const AttnParams& p, float* stages, StageDesc* desc, ui
     };
     while (true) {
         if (item >= item_end) {
+            enter();
             // no more work: a descriptor without copies releases the consumers
             const int buf = g % kStages;
             if (!acquire(buf)) {
@@ -183,12 +194,13 @@ __device__ void producer(const AttnParams& p, float* stages, StageDesc* desc, ui
                     window = load_window(win0);
                 }
             }
+            const int a = tok_begin + i * kStageTokens;
+            const int e = min(a + kStageTokens, tok_end);
+            if (g >= uint32_t(kStages) || e + kPrefillMinRows > len) enter();
             if (!acquire(b)) {
                 if (lane == 0) atomicOr(failed, 1u);
                 return;
             }
-            const int a = tok_begin + i * kStageTokens;
-            const int e = min(a + kStageTokens, tok_end);
             if (lane == 0) {
                 desc[b].work = wi;
                 desc[b].row = row;
@@ -452,7 +464,6 @@ __device__ void consumer(const AttnParams& p, const float* stages, const StageDe
 }
 
 __global__ void __launch_bounds__(kThreads, kAttnCtasPerSm) paged_attention_kernel(const AttnParams p) {
-    pdl_enter();  // before any global memory access
     extern __shared__ __align__(128) unsigned char smem_raw[];
     float* stages = reinterpret_cast<float*>(smem_raw);
     float* probs = stages + 2 * kStages * kStageFloats;  // [3 consumers][3][16]
@@ -473,11 +484,16 @@ __global__ void __launch_bounds__(kThreads, kAttnCtasPerSm) paged_attention_kern
     }
     __syncthreads();
     const bool persistent = p.sched != nullptr && p.cta_items == nullptr;
-    if (warp == kConsumers)
+    // Only shared memory is touched above. The consumers read the queries (the
+    // preceding QKV epilogue's output) and so wait for the previous kernel first;
+    // the producer waits before its first copy that may not be read early.
+    if (warp == kConsumers) {
         producer(p, stages, desc, full, empty, persistent, failed, lane);
-    else
+    } else {
+        pdl_enter();
         consumer(p, stages, desc, full, empty, probs + warp * kGroup * kStageTokens, qsm + warp * kGroup * kHeadDim,
                  failed, warp, lane);
+    }
     __syncthreads();
     if (tid == 0 && *failed) raise_error(p.error, kErrTimeout);
     if (persistent && tid == 0 && atomicAdd(&p.sched[1], 1u) == gridDim.x - 1) {

@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_kernel(const Pr
     };
     auto valid_in = [&](int sub) { return min(kT, len - sub * kT); };  // tokens of sub-chunk `sub`
     auto gather = [&](int sub) {
-        gather_raw(p.keys, p.values, p.layers, p.layer, p.block_tokens, blk, sub * kT, valid_in(sub), kh, raw_k,
+        gather_raw(p.keys, p.values, p.page_stride, p.layer_offset, p.block_tokens, blk, sub * kT, valid_in(sub), kh, raw_k,
                    raw_v, tid, kThreads);
     };
 

@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefix_attention_kernel(const Pr
     // sub-chunk 0's gathers first, then the query block while they fly
     if (tid < kPT) blk[tid] = w.tok_begin + tid < w.tok_end ? token_block(p, table, w.tok_begin + tid) : 0;
     __syncthreads();
-    gather_raw(p.keys, p.values, p.layers, p.layer, p.block_tokens, blk, w.tok_begin,
+    gather_raw(p.keys, p.values, p.page_stride, p.layer_offset, p.block_tokens, blk, w.tok_begin,
                min(kPT, w.tok_end - w.tok_begin), kh, raw_k, raw_v, tid, kPThreads);
     // physical block of this thread's token in the next sub-chunk, fetched early
     int next_blk = 0;
@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefix_attention_kernel(const Pr
         if (t1 < w.tok_end) {
             if (tid < kPT) blk[tid] = next_blk;
             __syncthreads();
-            gather_raw(p.keys, p.values, p.layers, p.layer, p.block_tokens, blk, t1, min(kPT, w.tok_end - t1), kh,
+            gather_raw(p.keys, p.values, p.page_stride, p.layer_offset, p.block_tokens, blk, t1, min(kPT, w.tok_end - t1), kh,
                        raw_k, raw_v, tid, kPThreads);
             next_blk = 0;
             if (tid < kPT && t1 + kPT + tid < w.tok_end) next_blk = token_block(p, table, t1 + kPT + tid);

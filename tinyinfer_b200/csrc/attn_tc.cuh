@@ -84,17 +84,18 @@ __device__ __forceinline__ int token_block(const int32_t* table, int table_strid
     return block;
 }
 
-// Starts the gathers of the raw K / V rows (kv head kh, `layer` of a
-// [block][layer][slot][192] pool) of tokens t0 .. t0 + n - 1 into staging; blk[t]
-// holds token t0 + t's physical block. Rows past n are not fetched.
-__device__ __forceinline__ void gather_raw(const float* keys, const float* values, int layers, int layer,
+// Starts the gathers of the raw K / V rows (kv head kh; pages addressed by
+// pool_page(block, page_stride, layer_offset)) of tokens t0 .. t0 + n - 1 into
+// staging; blk[t] holds token t0 + t's physical block. Rows past n are not fetched.
+__device__ __forceinline__ void gather_raw(const float* keys, const float* values, int page_stride,
+                                           int64_t layer_offset,
                                            int block_tokens, const int* blk, int t0, int n, int kh, float* raw_k,
                                            float* raw_v, int tid, int threads) {
     for (int i = tid; i < kT * 16; i += threads) {
         const int t = i >> 4, c4 = i & 15;
         if (t >= n) continue;
         const int token = t0 + t;
-        const size_t off = ((size_t(blk[t]) * layers + layer) * block_tokens + token % block_tokens) * kKvWidth +
+        const size_t off = (pool_page(blk[t], page_stride, layer_offset) * block_tokens + token % block_tokens) * kKvWidth +
                            kh * kHeadDim + c4 * 4;
         cp_async16(raw_k + t * kHeadDim + c4 * 4, keys + off);
         cp_async16(raw_v + t * kHeadDim + ((c4 ^ (t & 15)) * 4), values + off);

@@ -335,7 +335,11 @@ struct mp_context {
     Split wqkv, wo, wgu, wdown, head;
     std::set<std::string> received;
     bool finalized = false;
-    // pools and tables
+    // pools and tables. Each pool is layer-major, [layer][block][slot][192]: the pages
+    // one layer's attention reads share a compact address range (a [block][layer]
+    // pool spreads them at a stride of `layers` pages, which measured ~10% slower
+    // streaming). The API speaks reference-layout offsets ([block][layer][slot][192]:
+    // COW regions, mp_kv_read / mp_kv_write), translated by layer_major_offset().
     float *keys = nullptr, *values = nullptr;
     uint64_t pool_elements = 0;
     int32_t* tables = nullptr;
@@ -536,6 +540,11 @@ void wait_event(cudaEvent_t e, int timeout_ms) {
 void wait_stream(mp_context* c, const char* what) {
     cuda_check(cudaEventRecord(c->idle, c->stream), what);
     wait_event(c->idle, c->host_wait_ms);
+}
+
+// The layer-major pools as seen from reference-layout offsets.
+mpb::PoolGeometry pool_geometry(const mp_context* c) {
+    return {uint64_t(c->rt.block_tokens) * uint64_t(c->kvw), uint64_t(c->model.layers), uint64_t(c->rt.max_blocks)};
 }
 
 void validate_geometry(const mp_model_config& m, const mp_runtime_config& r) {
@@ -927,7 +936,7 @@ int mp_cow_copy(mp_context* c, const mp_tail_copy_region* regions, int32_t count
                                    cudaMemcpyHostToDevice, c->stream),
                    "upload cow regions");
         cuda_check(mpb::launch_cow_copy(reinterpret_cast<const mpb::CowRegion*>(c->cow), count, int(max_rows), c->keys,
-                                        c->values, c->pool_elements, c->error, c->stream),
+                                        c->values, c->pool_elements, pool_geometry(c), c->error, c->stream),
                    "cow launch");
     });
 }
@@ -1147,16 +1156,16 @@ int mp_forward_launch(mp_context* c) {
         if (c->cow_two_phase) {
             const auto* at = reinterpret_cast<const uint64_t*>(meta + c->off_scratch);
             cuda_check(mpb::launch_cow_copy(regions, c->region_count, c->region_rows, c->keys, c->values,
-                                            c->pool_elements, c->error, st, mpb::kCowGather, at, c->cow_scratch,
+                                            c->pool_elements, pool_geometry(c), c->error, st, mpb::kCowGather, at, c->cow_scratch,
                                             c->cow_scratch_elements),
                        "cow gather launch");
             cuda_check(mpb::launch_cow_copy(regions, c->region_count, c->region_rows, c->keys, c->values,
-                                            c->pool_elements, c->error, st, mpb::kCowScatter, at, c->cow_scratch,
+                                            c->pool_elements, pool_geometry(c), c->error, st, mpb::kCowScatter, at, c->cow_scratch,
                                             c->cow_scratch_elements),
                        "cow scatter launch");
         } else {
             cuda_check(mpb::launch_cow_copy(regions, c->region_count, c->region_rows, c->keys, c->values,
-                                            c->pool_elements, c->error, st),
+                                            c->pool_elements, pool_geometry(c), c->error, st),
                        "cow launch");
         }
         if (c->cow_timed) cuda_check(cudaEventRecord(c->cow_events[1], st), "cow timing");
@@ -1180,7 +1189,7 @@ int mp_forward_launch(mp_context* c) {
         rope.values = c->values;
         rope.tables = c->tables;
         rope.table_stride = r.table_stride;
-        rope.layers = m.layers;
+        rope.page_stride = 1;  // layer-major pools
         rope.block_tokens = r.block_tokens;
         rope.max_blocks = r.max_blocks;
         auto gemm = [&](const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
@@ -1223,7 +1232,7 @@ int mp_forward_launch(mp_context* c) {
         ap.q_stride = H;
         ap.keys = c->keys;
         ap.values = c->values;
-        ap.layers = m.layers;
+        ap.page_stride = 1;  // layer-major pools
         ap.block_tokens = r.block_tokens;
         ap.max_blocks = r.max_blocks;
         ap.tables = c->tables;
@@ -1247,12 +1256,13 @@ int mp_forward_launch(mp_context* c) {
         ap.out_lo = c->attn.lo;
         ap.out_stride = H;
         ap.error = c->error;
+        ap.early_copies = 1;  // the step's uploads and COW copies precede every layer
         mpb::PrefixParams xp{};
         xp.q = c->q;
         xp.q_stride = H;
         xp.keys = c->keys;
         xp.values = c->values;
-        xp.layers = m.layers;
+        xp.page_stride = 1;  // layer-major pools
         xp.block_tokens = r.block_tokens;
         xp.max_blocks = r.max_blocks;
         xp.tables = c->tables;
@@ -1270,7 +1280,7 @@ int mp_forward_launch(mp_context* c) {
         pp.q_stride = H;
         pp.keys = c->keys;
         pp.values = c->values;
-        pp.layers = m.layers;
+        pp.page_stride = 1;  // layer-major pools
         pp.block_tokens = r.block_tokens;
         pp.max_blocks = r.max_blocks;
         pp.tables = c->tables;
@@ -1284,12 +1294,13 @@ int mp_forward_launch(mp_context* c) {
         pp.error = c->error;
         for (int l = 0; l < m.layers; ++l) {
             const size_t L = size_t(l);
-            rope.layer = l;
+            const int64_t layer_offset = int64_t(l) * r.max_blocks;  // pool_page(): layer-major pools
+            rope.layer_offset = layer_offset;
             gemm(mp.xn_hi, mp.xn_lo, mp.wqkv_hi, mp.wqkv_lo, T, c->qkvw, H, l * c->qkvw, nullptr, 0,
                  mpb::Epilogue::Rope, "qkv gemm", mpb::kTcBN, nullptr, true);
-            ap.layer = l;
-            pp.layer = l;
-            xp.layer = l;
+            ap.layer_offset = layer_offset;
+            pp.layer_offset = layer_offset;
+            xp.layer_offset = layer_offset;
             if (c->profile) record_attention_event(c);
             cuda_check(mpb::launch_prefill_attention(pp, st), "prefill attention launch");
             cuda_check(mpb::launch_prefix_attention(xp, st), "shared-prefix attention launch");
@@ -1431,16 +1442,51 @@ int mp_kv_pools(mp_context* c, float** keys, float** values, uint64_t* elements)
     return MP_OK;
 }
 
+// Host copies of the reference-layout element range [offset, offset + count): the
+// range is cut at page boundaries of the reference layout, and each run of whole
+// blocks moves as one strided copy per layer.
 static int kv_copy(mp_context* c, int32_t pool, uint64_t offset, uint64_t count, void* host, bool to_device) {
     return guarded([&] {
         if (!c || !host || (pool != 0 && pool != 1)) fail(MP_ERR_INVALID, "invalid argument");
         if (offset > c->pool_elements || count > c->pool_elements - offset) fail(MP_ERR_INVALID, "range outside the pool");
         cuda_check(cudaSetDevice(c->device), "select device");
         wait_stream(c, "pool copy ordering");
-        float* base = (pool == 0 ? c->keys : c->values) + offset;
-        cuda_check(to_device ? cudaMemcpy(base, host, count * 4, cudaMemcpyHostToDevice)
-                             : cudaMemcpy(host, base, count * 4, cudaMemcpyDeviceToHost),
-                   "pool copy");
+        float* base = pool == 0 ? c->keys : c->values;
+        float* h = static_cast<float*>(host);
+        const mpb::PoolGeometry g = pool_geometry(c);
+        const uint64_t page = g.page_elements, block = page * g.layers;
+        auto piece = [&](uint64_t e, uint64_t n) {  // n floats inside one reference page
+            float* d = base + mpb::layer_major_offset(g, e);
+            float* hp = h + (e - offset);
+            cuda_check(to_device ? cudaMemcpy(d, hp, n * 4, cudaMemcpyHostToDevice)
+                                 : cudaMemcpy(hp, d, n * 4, cudaMemcpyDeviceToHost),
+                       "pool copy");
+        };
+        uint64_t e = offset;
+        const uint64_t end = offset + count;
+        while (e < end && (e % block != 0 || end - e < block)) {  // head: pieces up to a block boundary
+            const uint64_t n = std::min(end - e, page - e % page);
+            piece(e, n);
+            e += n;
+        }
+        if (e < end) {  // whole blocks [b0, b1): one 2D copy per layer
+            const uint64_t b0 = e / block, b1 = b0 + (end - e) / block;
+            for (uint64_t l = 0; l < g.layers; ++l) {
+                float* d = base + (l * g.max_blocks + b0) * page;
+                float* hp = h + (b0 * block + l * page - offset);
+                cuda_check(to_device ? cudaMemcpy2D(d, page * 4, hp, block * 4, page * 4, b1 - b0,
+                                                    cudaMemcpyHostToDevice)
+                                     : cudaMemcpy2D(hp, block * 4, d, page * 4, page * 4, b1 - b0,
+                                                    cudaMemcpyDeviceToHost),
+                           "pool copy");
+            }
+            e = b1 * block;
+            while (e < end) {  // tail
+                const uint64_t n = std::min(end - e, page - e % page);
+                piece(e, n);
+                e += n;
+            }
+        }
     });
 }
 

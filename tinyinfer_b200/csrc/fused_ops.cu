@@ -155,17 +155,19 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int v
 
 // grid (count, max_rows): one CTA per (region, layer row), float4 copies of
 // `width` floats in both pools (or between the pools and the gather scratch).
-// Offsets are validated against the pool and scratch sizes.
+// Offsets are validated against the pool and scratch sizes. With a layer-major
+// pool a row is copied in pieces that stay inside one page of the reference
+// layout, each piece's pool offsets translated (a tail-copy row is one piece).
 __global__ void cow_copy_kernel(const CowRegion* regions, float* keys, float* values, uint64_t pool_elements,
-                                unsigned* error, int mode, const uint64_t* scratch_offset, float* scratch,
-                                uint64_t scratch_elements) {
+                                PoolGeometry g, unsigned* error, int mode, const uint64_t* scratch_offset,
+                                float* scratch, uint64_t scratch_elements) {
     pdl_enter();  // before any global memory access
     const CowRegion r = regions[blockIdx.x];
     const uint64_t row = blockIdx.y;
     if (row >= r.rows) return;
     const uint64_t dst = r.destination + row * r.pitch, src = r.source + row * r.pitch;
     const uint64_t at = mode == kCowDirect ? 0 : scratch_offset[blockIdx.x] + row * r.width;
-    bool ok = !((r.width | dst | src | at) & 3);
+    bool ok = !((r.width | dst | src | at) & 3) && !(g.page_elements & 3) && g.page_elements > 0;
     if (mode != kCowScatter) ok = ok && src + r.width <= pool_elements;
     if (mode != kCowGather) ok = ok && dst + r.width <= pool_elements;
     if (mode != kCowDirect) ok = ok && at + r.width <= scratch_elements && !(scratch_elements & 3);
@@ -173,25 +175,37 @@ __global__ void cow_copy_kernel(const CowRegion* regions, float* keys, float* va
         if (threadIdx.x == 0) raise_error(error, kErrBounds);
         return;
     }
-    const float4 *ks, *vs;
-    float4 *kd, *vd;
-    if (mode == kCowScatter) {
-        ks = reinterpret_cast<const float4*>(scratch + at);
-        vs = reinterpret_cast<const float4*>(scratch + scratch_elements + at);
-    } else {
-        ks = reinterpret_cast<const float4*>(keys + src);
-        vs = reinterpret_cast<const float4*>(values + src);
-    }
-    if (mode == kCowGather) {
-        kd = reinterpret_cast<float4*>(scratch + at);
-        vd = reinterpret_cast<float4*>(scratch + scratch_elements + at);
-    } else {
-        kd = reinterpret_cast<float4*>(keys + dst);
-        vd = reinterpret_cast<float4*>(values + dst);
-    }
-    for (uint64_t i = threadIdx.x; i < r.width / 4; i += blockDim.x) {
-        kd[i] = ks[i];
-        vd[i] = vs[i];
+    const bool pool_src = mode != kCowScatter, pool_dst = mode != kCowGather;
+    auto place = [&](uint64_t e) { return g.layers ? layer_major_offset(g, e) : e; };
+    for (uint64_t pos = 0; pos < r.width;) {
+        uint64_t n = r.width - pos;  // floats in this piece (a multiple of 4)
+        if (g.layers) {
+            if (pool_src) n = min(n, g.page_elements - (src + pos) % g.page_elements);
+            if (pool_dst) n = min(n, g.page_elements - (dst + pos) % g.page_elements);
+        }
+        const float4 *ks, *vs;
+        float4 *kd, *vd;
+        if (pool_src) {
+            const uint64_t o = place(src + pos);
+            ks = reinterpret_cast<const float4*>(keys + o);
+            vs = reinterpret_cast<const float4*>(values + o);
+        } else {
+            ks = reinterpret_cast<const float4*>(scratch + at + pos);
+            vs = reinterpret_cast<const float4*>(scratch + scratch_elements + at + pos);
+        }
+        if (pool_dst) {
+            const uint64_t o = place(dst + pos);
+            kd = reinterpret_cast<float4*>(keys + o);
+            vd = reinterpret_cast<float4*>(values + o);
+        } else {
+            kd = reinterpret_cast<float4*>(scratch + at + pos);
+            vd = reinterpret_cast<float4*>(scratch + scratch_elements + at + pos);
+        }
+        for (uint64_t i = threadIdx.x; i < n / 4; i += blockDim.x) {
+            kd[i] = ks[i];
+            vd[i] = vs[i];
+        }
+        pos += n;
     }
 }
 
@@ -233,12 +247,16 @@ cudaError_t launch_argmax(const float* logits, int rows, int vocabulary, int32_t
 }
 
 cudaError_t launch_cow_copy(const CowRegion* regions, int count, int max_rows, float* keys, float* values,
-                            uint64_t pool_elements, unsigned* error, cudaStream_t stream, CowMode mode,
-                            const uint64_t* scratch_offset, float* scratch, uint64_t scratch_elements) {
+                            uint64_t pool_elements, const PoolGeometry& geometry, unsigned* error,
+                            cudaStream_t stream, CowMode mode, const uint64_t* scratch_offset, float* scratch,
+                            uint64_t scratch_elements) {
     if (count <= 0 || max_rows <= 0) return cudaSuccess;
     if (mode != kCowDirect && (!scratch_offset || !scratch)) return cudaErrorInvalidValue;
+    if (geometry.layers && (geometry.page_elements == 0 || geometry.max_blocks == 0 ||
+                            geometry.page_elements * geometry.layers * geometry.max_blocks != pool_elements))
+        return cudaErrorInvalidValue;
     return launch_pdl(cow_copy_kernel, dim3(count, max_rows), dim3(256), 0, stream, regions, keys, values,
-                      pool_elements, error, int(mode), scratch_offset, scratch, scratch_elements);
+                      pool_elements, geometry, error, int(mode), scratch_offset, scratch, scratch_elements);
 }
 
 cudaError_t launch_table_patch(const int32_t* pairs, int count, int32_t* tables, int64_t table_elements,

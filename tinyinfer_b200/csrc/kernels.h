@@ -18,6 +18,19 @@ constexpr int kGroup = kHeads / kKvHeads;
 constexpr int kKvWidth = kKvHeads * kHeadDim;  // 192 floats per token per pool
 constexpr int kQWidth = kHeads * kHeadDim;     // 576
 
+// Page addressing in a K or V pool of `block_tokens`-slot pages (kKvWidth floats
+// per slot). The page of (block, layer) starts at
+//   pool_page(block, page_stride, layer_offset) * block_tokens * kKvWidth
+// floats. Two layouts use it:
+//  * the reference's [block][layer][slot][192] (caller pools of the operator entry
+//    points): page_stride = layers, layer_offset = layer;
+//  * layer-major [layer][block][slot][192] (the forward context's own pools, so one
+//    layer's pages share a compact address range): page_stride = 1,
+//    layer_offset = layer * max_blocks.
+__host__ __device__ __forceinline__ size_t pool_page(int block, int page_stride, int64_t layer_offset) {
+    return size_t(block) * size_t(page_stride) + size_t(layer_offset);
+}
+
 // Device error word bits (read back by the host after each step).
 enum : unsigned {
     kErrBounds = 1u,    // a block-table entry or index fell outside its buffer
@@ -37,9 +50,10 @@ struct AttnWork {
 struct AttnParams {
     const float* q;  // roped queries, [rows][q_stride], 9 heads x 64 per row
     int q_stride;
-    const float* keys;    // K pool [block][layers][block_tokens][192]
+    const float* keys;    // K pool, pages addressed by pool_page(block, page_stride, layer_offset)
     const float* values;  // V pool, same layout
-    int layers, layer, block_tokens, max_blocks;
+    int page_stride, block_tokens, max_blocks;
+    int64_t layer_offset;
     const int32_t* tables;  // [slots][table_stride] physical page ids
     int table_stride;
     const int32_t* row_slot;    // table slot of each query row
@@ -63,6 +77,13 @@ struct AttnParams {
     __half* out_lo;      // halves (split_f16), same layout; `out` is then unused
     int out_stride;
     unsigned* error;
+    // Static schedule only: the schedule arrays, the tables and every page token
+    // below row_len - kPrefillMinRows were written before the previous kernel
+    // started (host upload, table patch, COW copies, earlier layers), so the
+    // producer may read them, and fill its ring, before the programmatic wait.
+    // Tokens at or past that bound may be the rows' appends by the preceding
+    // QKV epilogue (a decode row's sequence appends fewer than kPrefillMinRows).
+    int early_copies;
 };
 
 // Shared-prefix decode attention (attention_shared.cu). Decode rows whose block
@@ -88,7 +109,8 @@ struct PrefixParams {
     int q_stride;
     const float* keys;
     const float* values;
-    int layers, layer, block_tokens, max_blocks;
+    int page_stride, block_tokens, max_blocks;
+    int64_t layer_offset;  // pool_page()
     const int32_t* tables;
     int table_stride;
     const int32_t* group_rows;  // batch rows of every group, concatenated
@@ -118,7 +140,8 @@ struct PrefillParams {
     int q_stride;
     const float* keys;
     const float* values;
-    int layers, layer, block_tokens, max_blocks;
+    int page_stride, block_tokens, max_blocks;
+    int64_t layer_offset;  // pool_page()
     const int32_t* tables;
     int table_stride;
     const PrefillWork* work;
@@ -227,7 +250,8 @@ struct RopeEpilogue {
     float* values;
     const int32_t* tables;
     int table_stride;
-    int layers, layer, block_tokens, max_blocks;
+    int page_stride, block_tokens, max_blocks;
+    int64_t layer_offset;  // pool_page()
 };
 
 // GEMM operands in split precision. Every FP32 operand value x travels as two FP16
@@ -316,10 +340,24 @@ struct CowRegion {
 // scratch_elements floats, values in the next) and then scatters it
 // (kCowScatter), so that every source is read before any destination is written.
 enum CowMode : int { kCowDirect = 0, kCowGather = 1, kCowScatter = 2 };
+// Region offsets are reference-layout element offsets ([block][layer][slot][192],
+// as KVManager's tail-copy regions carry them). A pool in that layout is addressed
+// directly (layers = 0); a layer-major pool ([layer][block][slot][192]) through
+// layer_major_offset().
+struct PoolGeometry {
+    uint64_t page_elements;  // block_tokens * kKvWidth
+    uint64_t layers;         // 0: the pool is in the reference layout
+    uint64_t max_blocks;
+};
+__host__ __device__ __forceinline__ uint64_t layer_major_offset(const PoolGeometry& g, uint64_t e) {
+    const uint64_t page = e / g.page_elements, within = e - page * g.page_elements;
+    const uint64_t block = page / g.layers, layer = page - block * g.layers;
+    return (layer * g.max_blocks + block) * g.page_elements + within;
+}
 cudaError_t launch_cow_copy(const CowRegion* regions, int count, int max_rows, float* keys, float* values,
-                            uint64_t pool_elements, unsigned* error, cudaStream_t stream, CowMode mode = kCowDirect,
-                            const uint64_t* scratch_offset = nullptr, float* scratch = nullptr,
-                            uint64_t scratch_elements = 0);
+                            uint64_t pool_elements, const PoolGeometry& geometry, unsigned* error,
+                            cudaStream_t stream, CowMode mode = kCowDirect, const uint64_t* scratch_offset = nullptr,
+                            float* scratch = nullptr, uint64_t scratch_elements = 0);
 // tables[index[i]] = value[i]
 cudaError_t launch_table_patch(const int32_t* pairs, int count, int32_t* tables, int64_t table_elements,
                                unsigned* error, cudaStream_t stream);

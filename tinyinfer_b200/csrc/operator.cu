@@ -138,8 +138,8 @@ extern "C" int mp_paged_attention_decode(const float* q, const float* keys, cons
     p.q_stride = mpb::kQWidth;
     p.keys = keys;
     p.values = values;
-    p.layers = layers;
-    p.layer = layer;
+    p.page_stride = layers;  // caller pools: the reference layout [block][layer][slot][192]
+    p.layer_offset = layer;
     p.block_tokens = block_tokens;
     p.max_blocks = max_blocks;
     p.tables = tables;
@@ -220,8 +220,8 @@ extern "C" int mp_paged_attention_prefill(const float* q, const float* keys, con
     p.q_stride = mpb::kQWidth;
     p.keys = keys;
     p.values = values;
-    p.layers = layers;
-    p.layer = layer;
+    p.page_stride = layers;  // caller pools: the reference layout [block][layer][slot][192]
+    p.layer_offset = layer;
     p.block_tokens = block_tokens;
     p.max_blocks = max_blocks;
     p.tables = tables;

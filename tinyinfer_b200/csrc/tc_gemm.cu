@@ -103,9 +103,8 @@ __device__ __forceinline__ void cp_async_commit_wait_all() {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 
 // Rows [slice_row0(r), slice_row0(r + 1)) of a tile are reduced and stored by
-// cluster rank r; row_owner is the inverse.
+// cluster rank r.
 __host__ __device__ constexpr int slice_row0(int rank, int slices) { return rank * kBM / slices; }
-__host__ __device__ constexpr int row_owner(int row, int slices) { return ((row + 1) * slices - 1) / kBM; }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -204,7 +203,7 @@ __device__ __forceinline__ float* rope_destination(const TcGemmParams& p, int he
         raise_error(p.error, kErrBounds);
         return nullptr;
     }
-    const size_t off = ((size_t(block) * r.layers + r.layer) * r.block_tokens + pos % r.block_tokens) * kKvWidth;
+    const size_t off = (pool_page(block, r.page_stride, r.layer_offset) * r.block_tokens + pos % r.block_tokens) * kKvWidth;
     const int kvh = (head - kHeads) % kKvHeads;
     return (head < kHeads + kKvHeads ? r.keys : r.values) + off + kvh * kHeadDim;
 }
