@@ -1209,6 +1209,10 @@ int mp_forward_launch(mp_context* c) {
             g.out_lo = c->h.lo;
             g.ld_out = I;
             g.error = c->error;
+            // x (the residual) is written only by the embedding, O and down launches,
+            // each at least two launches before its next reader; the Rope metadata and
+            // tables by the step's upload and table patch
+            g.early_rows = 1;
             if (norm_next) {  // producer of the next GEMM's normalised input
                 g.norm_w = norm_next;
                 g.out_hi = c->xn.hi;

@@ -308,6 +308,10 @@ struct TcGemmParams {
     // is in flight, the tensor memory is released).
     uint64_t wait_ns;
     int stall;
+    // The residual rows (AddTo) and the Rope destinations' metadata and block
+    // tables were written at least two kernels earlier, so they may be gathered
+    // before the programmatic wait (the forward's layer sequence guarantees it).
+    int early_rows;
 };
 constexpr int kSsqGroup = 64;  // columns per partial sum of squares
 cudaError_t configure_tc_gemm();

@@ -218,11 +218,15 @@ struct RowInputs {
 };
 
 // Gathers RowInputs with `threads` threads (thread index t); runs beside the MMAs.
+// `parts`: kRowsSettled gathers what was written at least two kernels earlier (the
+// residual rows and norm weights, the Rope destinations), kRowsFresh what the
+// preceding kernel writes (the row scales' sums of squares).
+constexpr int kRowsSettled = 1, kRowsFresh = 2;
 template <int BN, Epilogue E>
 __device__ __forceinline__ void epilogue_rows_prepare(const TcGemmParams& p, const RowInputs& in, int m0, int n0,
-                                                      int r0, int r1, int t, int threads) {
+                                                      int r0, int r1, int t, int threads, int parts) {
     constexpr bool kPairs = E == Epilogue::SwiGLU || E == Epilogue::Rope;
-    if constexpr (prefetch_residual<BN, E>()) {
+    if (prefetch_residual<BN, E>() && (parts & kRowsSettled)) {
         // 16-byte copies, not waited for here: the threads wait just before the epilogue
         constexpr int kChunks = BN / 4;
         for (int i = t; i < (r1 - r0) * kChunks; i += threads) {
@@ -239,7 +243,7 @@ __device__ __forceinline__ void epilogue_rows_prepare(const TcGemmParams& p, con
     // any of them is used, so a pass costs one round trip (two for Rope's table
     // entries) instead of one per value -- these gathers run beside the MMAs and
     // must not outlast them.
-    if (kPairs && p.ssq_in != nullptr) {
+    if (kPairs && p.ssq_in != nullptr && (parts & kRowsFresh)) {
         // this CTA's rows' 1 / rms from the producer's per-64-column sums of
         // squares, summed in group order
         const int groups = p.k / kSsqGroup;
@@ -278,26 +282,28 @@ __device__ __forceinline__ void epilogue_rows_prepare(const TcGemmParams& p, con
         }
     }
     if constexpr (E == Epilogue::Rope) {
-        const int head = n0 / 64;
-        const bool kv = head >= kHeads;
-        for (int base = r0 + t; base < r1; base += 2 * threads) {
-            bool live[2];
-            int pos[2], slot[2], block[2];
+        if (parts & kRowsSettled) {
+            const int head = n0 / 64;
+            const bool kv = head >= kHeads;
+            for (int base = r0 + t; base < r1; base += 2 * threads) {
+                bool live[2];
+                int pos[2], slot[2], block[2];
 #pragma unroll
-            for (int b = 0; b < 2; ++b) {
-                const int r = base + b * threads;
-                live[b] = r < r1 && m0 + r < p.m;
-                pos[b] = live[b] ? p.rope.row_pos[m0 + r] : 0;
-                slot[b] = live[b] && kv ? p.rope.row_slot[m0 + r] : 0;
-            }
+                for (int b = 0; b < 2; ++b) {
+                    const int r = base + b * threads;
+                    live[b] = r < r1 && m0 + r < p.m;
+                    pos[b] = live[b] ? p.rope.row_pos[m0 + r] : 0;
+                    slot[b] = live[b] && kv ? p.rope.row_slot[m0 + r] : 0;
+                }
 #pragma unroll
-            for (int b = 0; b < 2; ++b) block[b] = live[b] && kv ? rope_block(p, slot[b], pos[b]) : -1;
+                for (int b = 0; b < 2; ++b) block[b] = live[b] && kv ? rope_block(p, slot[b], pos[b]) : -1;
 #pragma unroll
-            for (int b = 0; b < 2; ++b) {
-                const int r = base + b * threads;
-                if (r >= r1) continue;
-                in.dst[r - r0] = live[b] ? rope_destination(p, head, m0 + r, pos[b], block[b]) : nullptr;
-                in.pos[r - r0] = live[b] && head < kHeads + kKvHeads ? min(pos[b], p.rope.max_position - 1) : 0;
+                for (int b = 0; b < 2; ++b) {
+                    const int r = base + b * threads;
+                    if (r >= r1) continue;
+                    in.dst[r - r0] = live[b] ? rope_destination(p, head, m0 + r, pos[b], block[b]) : nullptr;
+                    in.pos[r - r0] = live[b] && head < kHeads + kKvHeads ? min(pos[b], p.rope.max_position - 1) : 0;
+                }
             }
         }
     }
@@ -537,6 +543,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(st + 2 * Cfg::kATile, &b_hi, kx, p.b_row0 + n0, &full[kb]);
             tma_load_2d(st + 2 * Cfg::kATile + Cfg::kBTile, &b_lo, kx, p.b_row0 + n0, &full[kb]);
         }
+    } else if (warp >= 2 && p.early_rows) {
+        epilogue_rows_prepare<BN, E>(p, rows, m0, n0, r0, r1, int(threadIdx.x) - 64, kThreads - 64, kRowsSettled);
     }
     pdl_enter();
     if (warp == 0 && lane == 0) {
@@ -587,7 +595,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) mma_commit(accum);
     } else if (warp >= 2) {
         // idle until the accumulator is ready: gather the epilogue's row inputs
-        epilogue_rows_prepare<BN, E>(p, rows, m0, n0, r0, r1, int(threadIdx.x) - 64, kThreads - 64);
+        epilogue_rows_prepare<BN, E>(p, rows, m0, n0, r0, r1, int(threadIdx.x) - 64, kThreads - 64,
+                                     p.early_rows ? kRowsFresh : kRowsSettled | kRowsFresh);
     }
     __syncwarp();
     // Epilogue. The outcome is made CTA-uniform before anything that holds a barrier.
